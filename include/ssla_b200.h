@@ -1,0 +1,156 @@
+/* ssla_b200.h -- C ABI of the B200-native SSLA-S per-event hot path.
+ *
+ * libssla_b200.so (ssla_rt_b200/) exports everything declared here: plain
+ * C types, pointers and sizes, no torch or C++ types.  Each entry point
+ * names the reference interface it replaces (paths relative to the
+ * haohq19/ssla-rt checkout).  Device pointers are CUDA global-memory
+ * pointers of the engine's device; `stream` is a cudaStream_t (NULL = the
+ * legacy default stream).  Every function returns SSLA_OK (0) or an
+ * SSLA_ERR_* code and never aborts; ssla_last_error() gives the message.
+ */
+#ifndef SSLA_B200_H
+#define SSLA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "ssla_abi_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SSLA_OK = 0,
+    SSLA_ERR_ARG = 1,        /* bad argument / shape / layout              */
+    SSLA_ERR_CUDA = 2,       /* a CUDA call failed                         */
+    SSLA_ERR_LOAD = 3,       /* weights.npz / meta.json missing or invalid */
+    SSLA_ERR_CAPACITY = 4,   /* more events than the engine was sized for  */
+    SSLA_ERR_NO_DEVICE = 5   /* no CUDA device / kernels not loadable      */
+};
+
+/* Temporal-dropout gate layouts.
+ * DECOMP: the single-thread reference chain, src/legacy/schemes/
+ *   s2_decomp_st.cpp:138-176 (gates after s0, s1, s2 on the s1, s2, s3
+ *   grids; head for every event finishing s3).
+ * HYBRID: the production chain, src/lib_stage01_to_gpu.cpp:228-311 followed
+ *   by orin/kernels/ssla_s2_s3_head_celled.cuh:1679-1755 (gates on the s1,
+ *   s2, s2 and s3 grids; the fourth gates the head). */
+enum { SSLA_LAYOUT_DECOMP = 0, SSLA_LAYOUT_HYBRID = 1 };
+
+/* Per-event flag bits (ssla_engine_drain_* `flags`). */
+enum {
+    SSLA_F_VALID = 1,  /* in bounds, entered stage 0     */
+    SSLA_F_R1 = 2,     /* passed gate 0, entered stage 1 */
+    SSLA_F_R2 = 4,     /* entered stage 2                */
+    SSLA_F_R3 = 8,     /* entered stage 3                */
+    SSLA_F_R4 = 16     /* produced a head prediction     */
+};
+
+typedef struct SslaEngine SslaEngine;
+
+typedef struct {
+    int n_partitions;          /* independent event streams (ring partitions) */
+    int max_events;            /* capacity of one drain call, all partitions  */
+    int layout;                /* SSLA_LAYOUT_*                                */
+    int device;                /* CUDA device ordinal                          */
+    int record_stage_outputs;  /* 1: keep per-event stage outputs (tests)     */
+    int max_events_per_partition; /* 0: ceil(max_events / n_partitions)      */
+} SslaEngineConfig;
+
+typedef struct {
+    int H, W, ncls, tdrop_window, layout, n_partitions, max_events;
+    int device;
+    long long stage_events[5]; /* last drain: events entering s0..s3 / head   */
+} SslaEngineInfo;
+
+/* State buffers readable / writable per partition. `index` is the layer
+ * (HIDDEN), gate (COUNTER) or stage (STAGE_OUT). STAGE_OUT and FLAGS cover
+ * the events of the last drain call (all partitions; partition ignored). */
+enum {
+    SSLA_STATE_HIDDEN = 0,     /* float [Hs*Ws][C_s]                          */
+    SSLA_STATE_COUNTER = 1,    /* uint8 gate counters on the gate's grid      */
+    SSLA_STATE_LAST_T = 2,     /* double [H*W], -1 = never seen               */
+    SSLA_STATE_PREDS_DEC = 3,  /* float [H3*W3][5+ncls] cx,cy,w,h,obj,cls..   */
+    SSLA_STATE_PREDS_RAW = 4,  /* float [H3*W3][5+ncls] reg0..3,obj,cls..     */
+    SSLA_STATE_VERSION = 5,    /* uint32 [H3*W3] head writes per cell          */
+    SSLA_STATE_STAGE_OUT = 6,  /* float [max_events][C_s]                      */
+    SSLA_STATE_FLAGS = 7       /* uint8 [max_events]                           */
+};
+
+/* Loads <weights_dir>/meta.json + weights.npz (schema of
+ * tools/make_ssla_stub.py:29-144), reshapes the layers into per-position
+ * tensors and folds the head's BatchNorm, uploads everything to `device`
+ * and allocates per-partition state sized for cfg->max_events.
+ * Replaces deploy::SslaSPipeline::load + reset (src/ssla_kernels.cpp:161-286)
+ * and the weight half of s01g_init_full (src/lib_stage01_to_gpu.cpp:354-421). */
+int  ssla_engine_create(const char* weights_dir, const SslaEngineConfig* cfg,
+                        SslaEngine** out);
+void ssla_engine_destroy(SslaEngine* eng);
+
+/* Zero hidden state and counters, forget last timestamps, set every
+ * prediction row to head(0) (src/ssla_kernels.cpp:276-286, :969-989). */
+int  ssla_engine_reset(SslaEngine* eng, void* stream);
+
+/* Runs every event of every partition through s0..s3 and the head, in
+ * stream order per partition, with exactly the sequential semantics of the
+ * selected layout.  events_dev: float (t, x, y, p) rows (openeva::Event,
+ * vendor/openeva/event.h:8-13); partition p owns rows
+ * [part_offsets[p], part_offsets[p+1]) (host array, n_partitions+1 ints).
+ * flags_dev (may be NULL): uint8 per row, SSLA_F_* bits.  Asynchronous on
+ * `stream`.  Replaces the per-event loop of s2_decomp_st.cpp:138-176 and
+ * the shard_worker + persistent-kernel chain of the hybrid runtime. */
+int  ssla_engine_drain_device(SslaEngine* eng, const float* events_dev,
+                              const int* part_offsets, uint8_t* flags_dev,
+                              void* stream);
+
+/* Same, from and to host memory (pinned or pageable): copies the events in,
+ * drains, copies the flags out and synchronises `stream`.  The analogue of
+ * s01g_submit_batch (src/lib_stage01_to_gpu.cpp:501-538) for a batch. */
+int  ssla_engine_drain_host(SslaEngine* eng, const float* events_host,
+                            const int* part_offsets, uint8_t* flags_host,
+                            void* stream);
+
+int  ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes);
+int  ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index,
+                            void* host_dst, size_t bytes);
+int  ssla_engine_write_state(SslaEngine* eng, int kind, int partition, int index,
+                             const void* host_src, size_t bytes);
+/* Device address of a state buffer (for zero-copy consumers of predictions). */
+void* ssla_engine_state_ptr(SslaEngine* eng, int kind, int partition, int index);
+int  ssla_engine_info(SslaEngine* eng, SslaEngineInfo* info);
+
+/* drain_n contract of the reference's P1 kernels: each block processes its
+ * records in order and writes one HybridS2S3OutputSlot per record; weights,
+ * hidden state and tdrop counters are read from / written to the device
+ * buffers named in `cfg` (a HOST copy of the HybridS2S3Config the reference
+ * kernel receives).  rings / outs / batch_clks: host arrays of device
+ * pointers, ns: host array.  batch_clks (may be NULL): every 2-word batch
+ * slot of a block receives the %globaltimer ns at drain start and end.
+ * Replaces k_ssla_s2s3_celled_drain_n_multi
+ * (orin/kernels/ssla_s2_s3_head_celled.cuh:1108-1255). */
+int  ssla_s2s3_drain_n_multi(const HybridS2S3Config* cfg,
+                             const HybridInputRec* const* rings, const int* ns,
+                             HybridS2S3OutputSlot* const* outs,
+                             unsigned long long* const* batch_clks,
+                             void* stream);
+/* Two-ring form; replaces k_ssla_s2s3_celled_drain_n
+ * (orin/kernels/ssla_s2_s3_head_celled.cuh:914-1095). */
+int  ssla_s2s3_drain_n(const HybridS2S3Config* cfg,
+                       const HybridInputRec* ring0, const HybridInputRec* ring1,
+                       int n0, int n1,
+                       HybridS2S3OutputSlot* out0, HybridS2S3OutputSlot* out1,
+                       unsigned long long* batch_clk0,
+                       unsigned long long* batch_clk1, void* stream);
+
+/* Portable exp used by every sigmoid / SiLU / box decode of the engine
+ * (the device code's exact twin), for tests on hosts without a GPU. */
+float ssla_expf_host(float x);
+
+const char* ssla_last_error(void);
+const char* ssla_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,55 @@
+"""Builds libssla_b200.so in-tree (nvcc, sm_100a).
+
+The library is a plain C-ABI shared object (include/ssla_b200.h); the CUDA
+runtime is linked statically so the .so needs only the driver on the GPU box.
+Flags: -fmad=false keeps every floating-point contraction explicit (the
+kernels write fmaf where the reference's arithmetic is a fused
+multiply-add), which is what makes results bit-identical to the CPU oracle.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+LIB = os.path.join(HERE, "libssla_b200.so")
+SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp"]
+HEADERS = ["ssla_device.cuh", "ssla_kernels.cuh", "ssla_weights.h"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+              "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-shared",
+              "-cudart", "static"]
+
+
+def _nvcc() -> str:
+    for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
+        if c and (os.path.isabs(c) and os.path.exists(c) or not os.path.isabs(c)):
+            return c
+    return "nvcc"
+
+
+def _stale() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
+    deps += [os.path.join(REPO, "include", f) for f in ("ssla_b200.h", "ssla_abi_types.h")]
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not _stale():
+        return LIB
+    cmd = [_nvcc(), *NVCC_FLAGS, f"-I{os.path.join(REPO, 'include')}", f"-I{CSRC}",
+           *[os.path.join(CSRC, f) for f in SOURCES], "-o", LIB]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True)
+    print(LIB)

@@ -1,0 +1,132 @@
+// ssla_device.cuh -- device-side types and math shared by the engine kernels.
+//
+// Engine model (one drain call = one "chunk" of events for P independent
+// partitions):
+//   - gates are integer-only, so every temporal-dropout decision of the chunk
+//     is computed up front (k_gates) and the events entering each stage are
+//     compacted in stream order into E_s lists (k_compact_*);
+//   - every layer is then run layer-synchronously over the whole chunk:
+//       k_scan   -- one warp per grid cell walks, in stream order, the events
+//                   whose 3x3 patch covers the cell and applies the LRU update
+//                   h = sigmoid(g)*h + v (the cell-owner invariant of
+//                   ssla_s2_s3_head_celled.cuh:1-38 taken to its limit: one
+//                   owner per cell, no atomics, exact per-cell order);
+//       k_event  -- per event (batched 32 per CTA): the 9-owner gather
+//                   sum_delta goW[delta]*(q*h_new) in the reference patch
+//                   order, residual, fp64 LayerNorm, then the next layer's
+//                   fused qvg matvec for all patch positions (or the head).
+// Arithmetic follows the oracle contract exactly (fmaf chains in reference
+// loop order, no other contraction -- the build uses -fmad=false --,
+// sequential fp64 LayerNorm sums, ssla_expf below), so results are
+// bit-identical to oracle/ssla_oracle.c.
+#pragma once
+
+#include <cstdint>
+
+namespace ssla {
+
+constexpr int kNT = 256;            // threads per CTA (event / filter kernels)
+constexpr int kMB = 32;             // events per k_event batch
+constexpr int kEPT = 8;             // events per thread in k_event tiles
+constexpr int kGroups = kMB / kEPT; // event groups per batch
+constexpr int kTile = 8;            // tile side (cells) of tile lists
+constexpr int kMaxParts = 1024;
+constexpr uint32_t kInvalidXY = 0xFFFFFFFFu;
+constexpr int kCompactTile = 4096;  // events per compaction tile
+
+enum : uint8_t { F_VALID = 1, F_R1 = 2, F_R2 = 4, F_R3 = 8, F_R4 = 16 };
+enum { LAYOUT_DECOMP = 0, LAYOUT_HYBRID = 1 };
+
+__host__ __device__ constexpr int chans(int s) { return s == 0 ? 12 : s == 1 ? 24 : s == 2 ? 48 : 96; }
+
+struct DevLayer {
+    const float* qvgT;   // [A][IN][3*OUT]
+    const float* goWT;   // [A][OUT][OUT]  ([p][i][o])
+    const float* ipT;    // [IN][OUT] or null
+    const float* gamma;  // [OUT]
+    const float* beta;   // [OUT]
+};
+
+struct DevHead {
+    const float *cls_convT, *cls_conv_b, *reg_convT, *reg_conv_b;  // [96][96], [96]
+    const float *cls_predT, *cls_pred_b;                            // [96][ncls]
+    const float *reg_predT, *reg_pred_b;                            // [96][4]
+    const float *obj_predT, *obj_pred_b;                            // [96][1]
+};
+
+// Per-partition state pointers (device memory).
+struct PartState {
+    float* hidden[8];    // [Hs*Ws][C_s]
+    uint8_t* cnt[4];     // gate counters, grid of gate g per layout
+    double* last_t;      // [H*W]
+    float* preds_dec;    // [H3*W3][5+ncls]
+    float* preds_raw;    // [H3*W3][5+ncls]
+    uint32_t* version;   // [H3*W3]
+    int own_x0, own_x1, own_y0, own_y1;  // owned range, s2 coordinates
+};
+
+struct Geo {
+    int H[4], W[4];      // grid per stage
+    int P;               // partitions
+    int layout;
+    int window;
+    int ncls;
+    int stride_h, stride_w;
+    int tx[4], ty[4];    // tiles per stage (x, y)
+    int seg;             // tile-list segment length
+    int nseg[4];         // allocated segments per (partition, tile) per stage
+    int cap[5];          // allocated entries of each stage list (E_0 = events)
+};
+
+struct StageEntry {      // one event in a stage list E_s, stream order
+    int e;               // chunk-global event / record index
+    int kprev;           // index in E_{s-1} (E_0 index == e)
+    uint32_t xy0;        // pixel coords x | y << 16
+};
+
+__device__ __forceinline__ int gate_grid(int layout, int g) {
+    return g == 0 ? 1 : g == 1 ? 2 : g == 2 ? (layout == LAYOUT_HYBRID ? 2 : 3) : 3;
+}
+
+// Twin of or_expf (oracle/ssla_oracle.c): Cody-Waite reduction with ln2 split
+// into a 12-bit head and a float tail, degree-7 Taylor polynomial by Horner
+// with fmaf, exact power-of-two scaling.  IEEE basic operations only, so
+// host and device results are identical; accuracy is tested against
+// CUDA's expf and libm.
+__host__ __device__ __forceinline__ float ssla_pow2i(int e) {
+#ifdef __CUDA_ARCH__
+    return __int_as_float((e + 127) << 23);
+#else
+    union { uint32_t u; float f; } b;
+    b.u = static_cast<uint32_t>(e + 127) << 23;
+    return b.f;
+#endif
+}
+
+__host__ __device__ __forceinline__ float ssla_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return __builtin_huge_valf();
+    if (x < -104.0f) return 0.0f;
+    const float n = rintf(x * 1.44269502f);
+    float r = fmaf(-n, 0.693115234375f, x);
+    r = fmaf(-n, 3.19461833e-05f, r);
+    float p = 1.98412701e-04f;
+    p = fmaf(p, r, 1.38888892e-03f);
+    p = fmaf(p, r, 8.33333377e-03f);
+    p = fmaf(p, r, 4.16666679e-02f);
+    p = fmaf(p, r, 1.66666672e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = static_cast<int>(n);
+    const int n1 = ni / 2;
+    const int n2 = ni - n1;
+    return (p * ssla_pow2i(n1)) * ssla_pow2i(n2);
+}
+
+// vendor/openeva/prim/activation.h:17
+__host__ __device__ __forceinline__ float ssla_sigmoidf(float x) {
+    return 1.0f / (1.0f + ssla_expf(-x));
+}
+
+}  // namespace ssla

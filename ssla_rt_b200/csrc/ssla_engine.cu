@@ -1,0 +1,800 @@
+// ssla_engine.cu -- host side of the B200 engine and the C ABI of
+// include/ssla_b200.h.
+//
+// An SslaEngine owns the device copy of one model (weights reshaped at load
+// time), per-partition recurrent state and a workspace sized for one drain
+// call.  A drain enqueues the fixed kernel sequence of ssla_kernels.cu on the
+// caller's stream; every size the kernels need beyond the host-known event
+// counts lives on the device, so the sequence never synchronises.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "ssla_b200.h"
+#include "ssla_kernels.cuh"
+#include "ssla_weights.h"
+
+namespace ssla {
+namespace {
+
+thread_local std::string g_last_error;
+
+struct CudaError : std::runtime_error {
+    explicit CudaError(const std::string& m) : std::runtime_error(m) {}
+};
+
+#define SSLA_CK(call)                                                                   \
+    do {                                                                                \
+        const cudaError_t e_ = (call);                                                  \
+        if (e_ != cudaSuccess)                                                          \
+            throw ::ssla::CudaError(std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+void check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        SSLA_CK(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// Owning device allocation.
+struct DevBuf {
+    void* p = nullptr;
+    size_t n = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    void alloc(size_t bytes) {
+        release();
+        if (bytes == 0) bytes = 16;
+        SSLA_CK(cudaMalloc(&p, bytes));
+        n = bytes;
+    }
+    template <typename T> T* as() const { return static_cast<T*>(p); }
+};
+
+template <typename T>
+void upload(DevBuf& b, const std::vector<T>& v) {
+    b.alloc(v.size() * sizeof(T));
+    if (!v.empty()) SSLA_CK(cudaMemcpy(b.p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+}
+
+int cells(const Geo& g, int s) { return g.W[s] * g.H[s]; }
+
+int host_gate_grid(int layout, int gate) {
+    return gate == 0 ? 1 : gate == 1 ? 2 : gate == 2 ? (layout == LAYOUT_HYBRID ? 2 : 3) : 3;
+}
+
+// Upper bound of the events passing a gate with `cells_g` counters when `n`
+// events reach it: at one counter, passes among c consecutive arrivals are
+// at most ceil(c / w) when w divides 256 (the counter period), and at most
+// ceil(c / 256) * ceil(256 / w) otherwise.
+long long gate_bound(long long n, int cells_g, int window) {
+    if (window <= 1) return n;
+    long long b;
+    if (256 % window == 0) {
+        b = n / window + cells_g;
+    } else {
+        const long long per = (256 + window - 1) / window;
+        b = (n / 256 + cells_g) * per;
+    }
+    return std::min(n, b);
+}
+
+void make_geo(Geo& g, int H, int W, int P, int layout, int window, int ncls) {
+    std::memset(&g, 0, sizeof g);
+    for (int s = 0; s < 4; ++s) {
+        g.H[s] = H >> s;
+        g.W[s] = W >> s;
+        g.tx[s] = (g.W[s] + kTile - 1) / kTile;
+        g.ty[s] = (g.H[s] + kTile - 1) / kTile;
+    }
+    g.P = P;
+    g.layout = layout;
+    g.window = window;
+    g.ncls = ncls;
+    g.stride_h = H / g.H[3];
+    g.stride_w = W / g.W[3];
+}
+
+// Per-drain workspace: stage lists, tile lists, per-(entry, delta) layer
+// records and residuals, sized from proven upper bounds of the events that
+// can reach each stage.
+struct Workspace {
+    int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, n_active = 0;
+    long long cap_part[5] = {0}, cap[5] = {0};
+    DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
+    DevBuf tl[4], tl_cnt[4], S_A, S_B, R_A, R_B, head_dec, head_raw, feat, slot_feat, stamps;
+    DevBuf stage_out[4];
+
+    void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
+        P = P_; mpe = mpe_; n_max = n_max_; s_first = s_first_;
+        g.seg = std::min(4096, std::max(256, ((mpe + 255) / 256) * 256));
+        cap_part[s_first] = mpe;
+        cap[s_first] = n_max;
+        for (int s = s_first; s < 4; ++s) {
+            const int cg = cells(g, host_gate_grid(g.layout, s));
+            cap_part[s + 1] = gate_bound(cap_part[s], cg, g.window);
+            cap[s + 1] = std::min(cap[s], gate_bound(cap[s], cg * P, g.window));
+        }
+        for (int s = 0; s < 4; ++s)
+            g.nseg[s] = s < s_first ? 0 : static_cast<int>((cap_part[s] + g.seg - 1) / g.seg);
+        for (int s = 0; s < 5; ++s) g.cap[s] = static_cast<int>(s < s_first ? 0 : cap[s]);
+        tiles_per_part = static_cast<int>((mpe + kCompactTile - 1) / kCompactTile);
+        if (tiles_per_part < 1) tiles_per_part = 1;
+
+        ev.alloc(static_cast<size_t>(n_max) * sizeof(float4));
+        ev_off.alloc(sizeof(int) * (P + 1));
+        ev_xy.alloc(sizeof(uint32_t) * n_max);
+        rflags.alloc(n_max);
+        for (int s = 1; s <= 4; ++s) {
+            E[s].alloc(sizeof(StageEntry) * std::max<long long>(cap[s], 1));
+            off[s].alloc(sizeof(int) * (P + 1));
+        }
+        count.alloc(sizeof(int) * 5);
+        tilecnt.alloc(sizeof(int) * 4 * P * tiles_per_part);
+        tilebase.alloc(sizeof(int) * 4 * P * tiles_per_part);
+        for (int s = s_first; s < 4; ++s) {
+            const size_t slots = static_cast<size_t>(P) * g.tx[s] * g.ty[s] * g.nseg[s];
+            tl[s].alloc(slots * g.seg * sizeof(int2));
+            tl_cnt[s].alloc(slots * sizeof(int));
+        }
+        size_t sa = 0, sb = 0, ra = 0, rb = 0;
+        for (int s = s_first; s < 4; ++s) {
+            const size_t c = chans(s), k = static_cast<size_t>(std::max<long long>(cap[s], 1));
+            sa = std::max(sa, k * (s == 0 ? 1 : 9) * 3 * c);
+            sb = std::max(sb, k * 9 * 3 * c);
+            ra = std::max(ra, k * c);
+            rb = std::max(rb, k * c);
+        }
+        S_A.alloc(sa * 4); S_B.alloc(sb * 4); R_A.alloc(ra * 4); R_B.alloc(rb * 4);
+        const int cols = 5 + g.ncls;
+        head_dec.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
+        head_raw.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
+        stamps.alloc(sizeof(unsigned long long) * 2);
+        if (s_first == 2) {
+            feat.alloc(sizeof(float) * 24 * n_max);
+            slot_feat.alloc(sizeof(float) * 96 * n_max);
+        }
+        for (int s = 0; s < 4; ++s) {
+            if (record) stage_out[s].alloc(sizeof(float) * chans(s) * static_cast<size_t>(n_max));
+            else stage_out[s].release();
+        }
+    }
+};
+
+// Enqueues stages s_first..3 (layers 2*s_first..7) for a planned workspace.
+// rec_off / E_2 / feat must be prepared by the caller for s_first == 2.
+void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_parts,
+                const DevLayer* L, const DevHead* head, bool do_head, bool record) {
+    const int* d_count = w.count.as<int>();
+    for (int s = w.s_first; s < 4; ++s) {
+        const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
+        const int2* tl = w.tl[s].as<int2>();
+        const int* tl_cnt = w.tl_cnt[s].as<int>();
+        for (int half = 0; half < 2; ++half) {
+            const int l = 2 * s + half;
+            // S / R ping-pong: even layers read A, odd layers read B.
+            float* S_in = (half == 0) ? w.S_A.as<float>() : w.S_B.as<float>();
+            float* R_in = (half == 0) ? w.R_A.as<float>() : w.R_B.as<float>();
+            float* S_out = (half == 0) ? w.S_B.as<float>() : w.S_A.as<float>();
+            float* R_out = (half == 0) ? w.R_B.as<float>() : w.R_A.as<float>();
+            ScanArgs sa{};
+            sa.g = g; sa.stage = s; sa.layer = l; sa.tl = tl; sa.tl_cnt = tl_cnt; sa.range = range;
+            sa.S = S_in; sa.parts = d_parts; sa.rflags = w.rflags.as<uint8_t>(); sa.second = half;
+            launch_scan(st, l, sa);
+            check_launch("k_scan");
+
+            EventArgs ea{};
+            ea.g = g; ea.stage = s; ea.count = d_count;
+            ea.ev_xy = w.ev_xy.as<uint32_t>(); ea.rflags = w.rflags.as<uint8_t>();
+            ea.S_in = S_in; ea.R_in = R_in; ea.S_out = S_out; ea.R_out = R_out;
+            ea.L = L[l];
+            if (l < 7) ea.N = L[l + 1];
+            ea.head = *head;
+            ea.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
+            ea.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
+            ea.head_dec = w.head_dec.as<float>();
+            ea.head_raw = w.head_raw.as<float>();
+            long long n_cap;
+            int mode;
+            if (half == 0) {
+                mode = MODE_FIRST;
+                ea.needq_bit = static_cast<uint8_t>(F_R1 << s);
+                if (s == 0) { ea.list = 0; ea.n_static = w.n_active; n_cap = w.n_active; }
+                else { ea.list = s; ea.E = w.E[s].as<StageEntry>(); n_cap = w.cap[s]; }
+            } else {
+                mode = (s < 3) ? MODE_SECOND : (do_head ? MODE_HEAD : MODE_LAST);
+                ea.list = s + 1;
+                ea.E = w.E[s + 1].as<StageEntry>();
+                n_cap = w.cap[s + 1];
+            }
+            const int grid = static_cast<int>(std::min<long long>((n_cap + kMB - 1) / kMB, 148LL * 8));
+            launch_event(st, l, mode, ea, grid);
+            check_launch("k_event");
+        }
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Engine
+// ---------------------------------------------------------------------------
+struct Engine {
+    int device = 0;
+    Geo g{};
+    int layout = LAYOUT_HYBRID;
+    int max_events = 0, mpe = 0;
+    bool record = false;
+    HostModel model;
+    DevBuf wbuf[8][5];          // qvgT, goWT, ipT, gamma, beta per layer
+    DevBuf hbuf[10];
+    DevLayer L[8]{};
+    DevHead head{};
+    // state
+    DevBuf hidden[8], cnt[4], last_t, preds_dec, preds_raw, version, parts;
+    std::vector<PartState> h_parts;
+    Workspace ws;
+    int* pinned_off = nullptr;
+    long long last_counts[5] = {0};
+    int last_n = 0;
+
+    ~Engine() {
+        if (pinned_off) cudaFreeHost(pinned_off);
+    }
+
+    size_t state_elems(int kind, int index) const {
+        switch (kind) {
+            case SSLA_STATE_HIDDEN: return static_cast<size_t>(cells(g, index / 2)) * chans(index / 2);
+            case SSLA_STATE_COUNTER: return static_cast<size_t>(cells(g, host_gate_grid(layout, index)));
+            case SSLA_STATE_LAST_T: return static_cast<size_t>(cells(g, 0));
+            case SSLA_STATE_PREDS_DEC:
+            case SSLA_STATE_PREDS_RAW: return static_cast<size_t>(cells(g, 3)) * (5 + g.ncls);
+            case SSLA_STATE_VERSION: return static_cast<size_t>(cells(g, 3));
+            case SSLA_STATE_STAGE_OUT: return static_cast<size_t>(max_events) * chans(index);
+            case SSLA_STATE_FLAGS: return static_cast<size_t>(max_events);
+            default: return 0;
+        }
+    }
+    static size_t elem_size(int kind) {
+        switch (kind) {
+            case SSLA_STATE_COUNTER: case SSLA_STATE_FLAGS: return 1;
+            case SSLA_STATE_LAST_T: return 8;
+            case SSLA_STATE_VERSION: return 4;
+            default: return 4;
+        }
+    }
+    char* state_ptr(int kind, int p, int index) {
+        const size_t per = state_elems(kind, index) * elem_size(kind);
+        switch (kind) {
+            case SSLA_STATE_HIDDEN: return hidden[index].as<char>() + per * p;
+            case SSLA_STATE_COUNTER: return cnt[index].as<char>() + per * p;
+            case SSLA_STATE_LAST_T: return last_t.as<char>() + per * p;
+            case SSLA_STATE_PREDS_DEC: return preds_dec.as<char>() + per * p;
+            case SSLA_STATE_PREDS_RAW: return preds_raw.as<char>() + per * p;
+            case SSLA_STATE_VERSION: return version.as<char>() + per * p;
+            case SSLA_STATE_STAGE_OUT: return record ? ws.stage_out[index].as<char>() : nullptr;
+            case SSLA_STATE_FLAGS: return ws.rflags.as<char>();
+            default: return nullptr;
+        }
+    }
+
+    void create(const char* dir, const SslaEngineConfig& c) {
+        device = c.device;
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) throw CudaError("no CUDA device");
+        if (device < 0 || device >= ndev) throw std::invalid_argument("device ordinal out of range");
+        DeviceGuard dg(device);
+        model = load_model(dir);
+        layout = c.layout;
+        record = c.record_stage_outputs != 0;
+        max_events = c.max_events;
+        const int P = c.n_partitions;
+        mpe = c.max_events_per_partition > 0 ? c.max_events_per_partition : (max_events + P - 1) / P;
+        make_geo(g, model.meta.height, model.meta.width, P, layout, model.meta.tdrop_window,
+                 model.meta.num_classes);
+        for (int l = 0; l < 8; ++l) {
+            const HostLayer& hl = model.layers[l];
+            upload(wbuf[l][0], hl.qvgT);
+            upload(wbuf[l][1], hl.goWT);
+            if (!hl.ipT.empty()) upload(wbuf[l][2], hl.ipT);
+            upload(wbuf[l][3], hl.gamma);
+            upload(wbuf[l][4], hl.beta);
+            L[l].qvgT = wbuf[l][0].as<float>();
+            L[l].goWT = wbuf[l][1].as<float>();
+            L[l].ipT = hl.ipT.empty() ? nullptr : wbuf[l][2].as<float>();
+            L[l].gamma = wbuf[l][3].as<float>();
+            L[l].beta = wbuf[l][4].as<float>();
+        }
+        const HostHead& hh = model.head;
+        const std::vector<float>* hv[10] = {&hh.cls_convT, &hh.cls_conv_b, &hh.reg_convT, &hh.reg_conv_b,
+                                            &hh.cls_predT, &hh.cls_pred_b, &hh.reg_predT, &hh.reg_pred_b,
+                                            &hh.obj_predT, &hh.obj_pred_b};
+        for (int i = 0; i < 10; ++i) upload(hbuf[i], *hv[i]);
+        head = DevHead{hbuf[0].as<float>(), hbuf[1].as<float>(), hbuf[2].as<float>(), hbuf[3].as<float>(),
+                       hbuf[4].as<float>(), hbuf[5].as<float>(), hbuf[6].as<float>(), hbuf[7].as<float>(),
+                       hbuf[8].as<float>(), hbuf[9].as<float>()};
+        // state
+        for (int l = 0; l < 8; ++l) hidden[l].alloc(state_elems(SSLA_STATE_HIDDEN, l) * 4 * P);
+        for (int gi = 0; gi < 4; ++gi) cnt[gi].alloc(state_elems(SSLA_STATE_COUNTER, gi) * P);
+        last_t.alloc(state_elems(SSLA_STATE_LAST_T, 0) * 8 * P);
+        preds_dec.alloc(state_elems(SSLA_STATE_PREDS_DEC, 0) * 4 * P);
+        preds_raw.alloc(state_elems(SSLA_STATE_PREDS_RAW, 0) * 4 * P);
+        version.alloc(state_elems(SSLA_STATE_VERSION, 0) * 4 * P);
+        h_parts.assign(P, PartState{});
+        for (int p = 0; p < P; ++p) {
+            PartState& ps = h_parts[p];
+            for (int l = 0; l < 8; ++l) ps.hidden[l] = reinterpret_cast<float*>(state_ptr(SSLA_STATE_HIDDEN, p, l));
+            for (int gi = 0; gi < 4; ++gi) ps.cnt[gi] = reinterpret_cast<uint8_t*>(state_ptr(SSLA_STATE_COUNTER, p, gi));
+            ps.last_t = reinterpret_cast<double*>(state_ptr(SSLA_STATE_LAST_T, p, 0));
+            ps.preds_dec = reinterpret_cast<float*>(state_ptr(SSLA_STATE_PREDS_DEC, p, 0));
+            ps.preds_raw = reinterpret_cast<float*>(state_ptr(SSLA_STATE_PREDS_RAW, p, 0));
+            ps.version = reinterpret_cast<uint32_t*>(state_ptr(SSLA_STATE_VERSION, p, 0));
+            ps.own_x0 = 0; ps.own_x1 = g.W[2]; ps.own_y0 = 0; ps.own_y1 = g.H[2];
+        }
+        upload(parts, h_parts);
+        ws.plan(g, P, mpe, max_events, 0, record);
+        SSLA_CK(cudaMallocHost(&pinned_off, sizeof(int) * (P + 1)));
+        reset(nullptr);
+        SSLA_CK(cudaStreamSynchronize(nullptr));
+    }
+
+    void reset(cudaStream_t st) {
+        DeviceGuard dg(device);
+        for (int l = 0; l < 8; ++l) SSLA_CK(cudaMemsetAsync(hidden[l].p, 0, hidden[l].n, st));
+        for (int gi = 0; gi < 4; ++gi) SSLA_CK(cudaMemsetAsync(cnt[gi].p, 0, cnt[gi].n, st));
+        launch_fill_f64(st, last_t.as<double>(), last_t.n / 8, -1.0);
+        check_launch("fill last_t");
+        launch_reset_preds(st, g, parts.as<PartState>(), head);
+        check_launch("k_reset_preds");
+    }
+
+    void drain(const float* ev_dev, const int* off, uint8_t* flags_dev, cudaStream_t st) {
+        DeviceGuard dg(device);
+        const int P = g.P;
+        if (off[0] != 0) throw std::invalid_argument("part_offsets[0] must be 0");
+        for (int p = 0; p < P; ++p) {
+            const int n_p = off[p + 1] - off[p];
+            if (n_p < 0) throw std::invalid_argument("part_offsets must be non-decreasing");
+            if (n_p > mpe) throw std::length_error("partition holds more events than max_events_per_partition");
+        }
+        const int n = off[P];
+        if (n > max_events) throw std::length_error("more events than max_events");
+        ws.n_active = n;
+        last_n = n;
+        std::memcpy(pinned_off, off, sizeof(int) * (P + 1));
+        SSLA_CK(cudaMemcpyAsync(ws.ev_off.p, pinned_off, sizeof(int) * (P + 1), cudaMemcpyHostToDevice, st));
+        const float4* ev = reinterpret_cast<const float4*>(ev_dev);
+        launch_prep(st, ev, n, g.W[0], g.H[0], ws.ev_xy.as<uint32_t>(), ws.rflags.as<uint8_t>());
+        check_launch("k_prep");
+        // stage-0 tile lists
+        FilterArgs fa{};
+        fa.g = g; fa.stage = 0; fa.ev_xy = ws.ev_xy.as<uint32_t>(); fa.rflags = ws.rflags.as<uint8_t>();
+        fa.range = ws.ev_off.as<int>(); fa.tl = ws.tl[0].as<int2>(); fa.tl_cnt = ws.tl_cnt[0].as<int>();
+        launch_filter(st, fa, dim3(P, g.tx[0] * g.ty[0], g.nseg[0]));
+        check_launch("k_filter s0");
+        // gates + preprocess + layer-0 qvg
+        GateArgs ga{};
+        ga.g = g; ga.ev = ev; ga.ev_off = ws.ev_off.as<int>(); ga.tl0 = ws.tl[0].as<int2>();
+        ga.tl0_cnt = ws.tl_cnt[0].as<int>(); ga.parts = parts.as<PartState>();
+        ga.rflags = ws.rflags.as<uint8_t>(); ga.S0 = ws.S_A.as<float>(); ga.R0 = ws.R_A.as<float>();
+        ga.L0 = L[0];
+        launch_gates(st, ga);
+        check_launch("k_gates");
+        // stage lists
+        CompactArgs ca{};
+        ca.g = g; ca.s_first = 0; ca.tiles_per_part = ws.tiles_per_part; ca.ev_off = ws.ev_off.as<int>();
+        ca.rflags = ws.rflags.as<uint8_t>(); ca.ev_xy = ws.ev_xy.as<uint32_t>();
+        ca.tilecnt = ws.tilecnt.as<int>(); ca.tilebase = ws.tilebase.as<int>();
+        for (int s = 0; s <= 4; ++s) { ca.E[s] = ws.E[s].as<StageEntry>(); ca.off[s] = ws.off[s].as<int>(); }
+        ca.count = ws.count.as<int>();
+        launch_compact(st, ca);
+        check_launch("k_compact");
+        for (int s = 1; s < 4; ++s) {
+            FilterArgs f{};
+            f.g = g; f.stage = s; f.E = ws.E[s].as<StageEntry>(); f.rflags = ws.rflags.as<uint8_t>();
+            f.range = ws.off[s].as<int>(); f.tl = ws.tl[s].as<int2>(); f.tl_cnt = ws.tl_cnt[s].as<int>();
+            f.out_bit = static_cast<uint8_t>(F_R1 << s);
+            launch_filter(st, f, dim3(P, g.tx[s] * g.ty[s], g.nseg[s]));
+            check_launch("k_filter");
+        }
+        run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record);
+        CommitArgs cm{};
+        cm.g = g; cm.E4 = ws.E[4].as<StageEntry>(); cm.off4 = ws.off[4].as<int>();
+        cm.head_dec = ws.head_dec.as<float>(); cm.head_raw = ws.head_raw.as<float>();
+        cm.parts = parts.as<PartState>();
+        launch_commit(st, cm);
+        check_launch("k_commit");
+        if (flags_dev && n > 0)
+            SSLA_CK(cudaMemcpyAsync(flags_dev, ws.rflags.p, n, cudaMemcpyDeviceToDevice, st));
+    }
+};
+
+// ---------------------------------------------------------------------------
+// drain_n (stage-2 entry) on the reference's HybridS2S3Config buffers.
+// A process-wide workspace per device is grown on demand.
+// ---------------------------------------------------------------------------
+struct DrainN {
+    std::mutex mu;
+    struct PerDev {
+        Workspace ws;
+        Geo g{};
+        int P = 0, mpe = 0, n_max = 0, H2 = 0, W2 = 0, window = 0;
+        DevBuf parts, outs, clks, rec;
+        int* pinned = nullptr;
+    };
+    std::vector<std::unique_ptr<PerDev>> dev;
+
+    int run(const HybridS2S3Config* cfg, const HybridInputRec* const* rings, const int* ns,
+            HybridS2S3OutputSlot* const* outs, unsigned long long* const* clks, cudaStream_t st) {
+        std::lock_guard<std::mutex> lk(mu);
+        int device = 0;
+        SSLA_CK(cudaGetDevice(&device));
+        if (static_cast<int>(dev.size()) <= device) dev.resize(device + 1);
+        if (!dev[device]) dev[device].reset(new PerDev());
+        PerDev& d = *dev[device];
+        const int P = cfg->n_blocks;
+        if (P < 1 || P > SSLA_MAX_BLOCKS) throw std::invalid_argument("cfg->n_blocks must be 1..16");
+        if (cfg->H2 <= 0 || cfg->W2 <= 0 || cfg->H3 != cfg->H2 / 2 || cfg->W3 != cfg->W2 / 2)
+            throw std::invalid_argument("cfg grid sizes must satisfy H3 = H2/2, W3 = W2/2");
+        if ((cfg->H2 % 2) || (cfg->W2 % 2)) throw std::invalid_argument("H2 and W2 must be even");
+        for (int b = 1; b < P; ++b)
+            for (int li = 0; li < 4; ++li)
+                if (std::memcmp(&cfg->layers[b][li], &cfg->layers[0][li], sizeof(LayerWeightsS2S3)) != 0)
+                    throw std::invalid_argument("all blocks must share the same layer weights");
+        std::vector<int> off(P + 1, 0);
+        int mpe = 1;
+        for (int b = 0; b < P; ++b) {
+            if (ns[b] < 0) throw std::invalid_argument("negative record count");
+            off[b + 1] = off[b] + ns[b];
+            mpe = std::max(mpe, ns[b]);
+        }
+        const int n = off[P];
+        const int window = cfg->tdrop_window;
+        if (d.P != P || d.mpe < mpe || d.n_max < n || d.H2 != cfg->H2 || d.W2 != cfg->W2 ||
+            d.window != window) {
+            // full-resolution geometry whose stage-2 grid is H2 x W2
+            make_geo(d.g, cfg->H2 * 4, cfg->W2 * 4, P, LAYOUT_HYBRID, window, 2);
+            d.P = P; d.mpe = std::max(mpe, d.mpe); d.n_max = std::max(n, d.n_max);
+            d.H2 = cfg->H2; d.W2 = cfg->W2; d.window = window;
+            SSLA_CK(cudaStreamSynchronize(st));
+            d.ws.plan(d.g, P, d.mpe, d.n_max, 2, false);
+            d.parts.alloc(sizeof(PartState) * P);
+            d.outs.alloc(sizeof(void*) * P);
+            d.clks.alloc(sizeof(void*) * P);
+            d.rec.alloc(sizeof(HybridInputRec) * static_cast<size_t>(std::max(d.n_max, 1)));
+            if (d.pinned) cudaFreeHost(d.pinned);
+            d.pinned = nullptr;
+            SSLA_CK(cudaMallocHost(&d.pinned, sizeof(int) * (P + 1) + sizeof(PartState) * P +
+                                                  2 * sizeof(void*) * P));
+        }
+        Workspace& w = d.ws;
+        w.n_active = n;
+        // per-block state and parameters (pinned staging, async upload)
+        char* pin = reinterpret_cast<char*>(d.pinned);
+        int* p_off = reinterpret_cast<int*>(pin);
+        PartState* p_parts = reinterpret_cast<PartState*>(pin + sizeof(int) * (P + 1));
+        void** p_outs = reinterpret_cast<void**>(pin + sizeof(int) * (P + 1) + sizeof(PartState) * P);
+        void** p_clks = p_outs + P;
+        std::memcpy(p_off, off.data(), sizeof(int) * (P + 1));
+        for (int b = 0; b < P; ++b) {
+            PartState ps{};
+            for (int li = 0; li < 4; ++li) ps.hidden[4 + li] = cfg->hidden[b][li];
+            ps.cnt[2] = cfg->tdrop_s2[b];
+            ps.cnt[3] = cfg->tdrop_s3[b];
+            ps.own_x0 = cfg->strip[b].owned_lo; ps.own_x1 = cfg->strip[b].owned_hi;
+            ps.own_y0 = cfg->strip[b].owned_y_lo; ps.own_y1 = cfg->strip[b].owned_y_hi;
+            p_parts[b] = ps;
+            p_outs[b] = outs ? outs[b] : nullptr;
+            p_clks[b] = clks ? clks[b] : nullptr;
+        }
+        SSLA_CK(cudaMemcpyAsync(w.ev_off.p, p_off, sizeof(int) * (P + 1), cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaMemcpyAsync(w.off[2].p, p_off, sizeof(int) * (P + 1), cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaMemcpyAsync(d.parts.p, p_parts, sizeof(PartState) * P, cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaMemcpyAsync(d.outs.p, p_outs, sizeof(void*) * P, cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaMemcpyAsync(d.clks.p, p_clks, sizeof(void*) * P, cudaMemcpyHostToDevice, st));
+        launch_stamp(st, w.stamps.as<unsigned long long>());
+        check_launch("k_stamp");
+        for (int b = 0; b < P; ++b)
+            if (ns[b] > 0)
+                SSLA_CK(cudaMemcpyAsync(d.rec.as<HybridInputRec>() + off[b], rings[b],
+                                        sizeof(HybridInputRec) * ns[b], cudaMemcpyDeviceToDevice, st));
+        launch_prep_records(st, d.rec.p, n, w.E[2].as<StageEntry>(), w.ev_xy.as<uint32_t>(),
+                            w.rflags.as<uint8_t>(), w.feat.as<float>());
+        check_launch("k_prep_records");
+        const Geo& g = d.g;
+        FilterArgs f2{};
+        f2.g = g; f2.stage = 2; f2.E = w.E[2].as<StageEntry>(); f2.rflags = w.rflags.as<uint8_t>();
+        f2.range = w.off[2].as<int>(); f2.tl = w.tl[2].as<int2>(); f2.tl_cnt = w.tl_cnt[2].as<int>();
+        f2.out_bit = 0;   // gates not known yet; refiltered below
+        launch_filter(st, f2, dim3(P, g.tx[2] * g.ty[2], g.nseg[2]));
+        check_launch("k_filter s2");
+        Gate2Args ga{};
+        ga.g = g; ga.rec_off = w.ev_off.as<int>(); ga.tl2 = w.tl[2].as<int2>(); ga.tl2_cnt = w.tl_cnt[2].as<int>();
+        ga.parts = d.parts.as<PartState>(); ga.rflags = w.rflags.as<uint8_t>();
+        launch_gates_s2(st, ga);
+        check_launch("k_gates_s2");
+        CompactArgs ca{};
+        ca.g = g; ca.s_first = 2; ca.tiles_per_part = w.tiles_per_part; ca.ev_off = w.ev_off.as<int>();
+        ca.rflags = w.rflags.as<uint8_t>(); ca.ev_xy = w.ev_xy.as<uint32_t>();
+        ca.tilecnt = w.tilecnt.as<int>(); ca.tilebase = w.tilebase.as<int>();
+        for (int s = 0; s <= 4; ++s) { ca.E[s] = w.E[s].as<StageEntry>(); ca.off[s] = w.off[s].as<int>(); }
+        ca.count = w.count.as<int>();
+        launch_compact(st, ca);
+        check_launch("k_compact");
+        for (int s = 2; s < 4; ++s) {     // stage-2 lists again, now with the output bit
+            FilterArgs f{};
+            f.g = g; f.stage = s; f.E = w.E[s].as<StageEntry>(); f.rflags = w.rflags.as<uint8_t>();
+            f.range = w.off[s].as<int>(); f.tl = w.tl[s].as<int2>(); f.tl_cnt = w.tl_cnt[s].as<int>();
+            f.out_bit = static_cast<uint8_t>(F_R1 << s);
+            launch_filter(st, f, dim3(P, g.tx[s] * g.ty[s], g.nseg[s]));
+            check_launch("k_filter");
+        }
+        // count[2] = n for the entry kernel
+        SSLA_CK(cudaMemcpyAsync(w.count.as<int>() + 2, p_off + P, sizeof(int), cudaMemcpyHostToDevice, st));
+        DevLayer L[8]{};
+        for (int li = 0; li < 4; ++li) {
+            const LayerWeightsS2S3& lw = cfg->layers[0][li];
+            L[4 + li] = DevLayer{lw.qvgIn, lw.goW, lw.input_proj, lw.ln_gamma, lw.ln_beta};
+        }
+        // record features -> layer-4 qvg + residual
+        EventArgs ea{};
+        ea.g = g; ea.stage = 2; ea.mode = MODE_ENTRY; ea.count = w.count.as<int>(); ea.list = 2;
+        ea.E = w.E[2].as<StageEntry>(); ea.ev_xy = w.ev_xy.as<uint32_t>(); ea.rflags = w.rflags.as<uint8_t>();
+        ea.S_out = w.S_A.as<float>(); ea.R_out = w.R_A.as<float>(); ea.N = L[4];
+        ea.entry_feat = w.feat.as<float>();
+        launch_event(st, 4, MODE_ENTRY, ea, static_cast<int>(std::min<long long>((n + kMB - 1) / kMB, 148LL * 8)));
+        check_launch("k_event entry");
+        DevHead nohead{};
+        run_layers(st, g, w, d.parts.as<PartState>(), L, &nohead, false, false);
+        if (outs) {
+            launch_write_slots(st, n, P, w.ev_off.as<int>(), w.rflags.as<uint8_t>(), w.ev_xy.as<uint32_t>(),
+                               d.parts.as<PartState>(), w.slot_feat.as<float>(), d.outs.as<void*>());
+            check_launch("k_write_slots");
+        }
+        launch_stamp(st, w.stamps.as<unsigned long long>() + 1);
+        check_launch("k_stamp");
+        if (clks) {
+            launch_fill_clk(st, P, w.ev_off.as<int>(), w.stamps.as<unsigned long long>(),
+                            d.clks.as<unsigned long long*>());
+            check_launch("k_fill_clk");
+        }
+        // the pinned staging buffers are reused by the next call
+        SSLA_CK(cudaStreamSynchronize(st));
+        return SSLA_OK;
+    }
+};
+
+DrainN& drain_n_state() {
+    static DrainN* d = new DrainN();   // process lifetime
+    return *d;
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        return f();
+    } catch (const CudaError& e) {
+        g_last_error = e.what();
+        return SSLA_ERR_CUDA;
+    } catch (const std::length_error& e) {
+        g_last_error = e.what();
+        return SSLA_ERR_CAPACITY;
+    } catch (const std::invalid_argument& e) {
+        g_last_error = e.what();
+        return SSLA_ERR_ARG;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "host allocation failed";
+        return SSLA_ERR_CUDA;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return SSLA_ERR_LOAD;
+    }
+}
+
+}  // namespace ssla
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+struct SslaEngine {
+    ssla::Engine e;
+};
+
+extern "C" {
+
+const char* ssla_last_error(void) { return ssla::g_last_error.c_str(); }
+const char* ssla_version(void) { return "ssla_b200 0.1.0 (sm_100a)"; }
+float ssla_expf_host(float x) { return ssla::ssla_expf(x); }
+
+int ssla_engine_create(const char* weights_dir, const SslaEngineConfig* cfg, SslaEngine** out) {
+    if (!weights_dir || !cfg || !out) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    *out = nullptr;
+    if (cfg->n_partitions < 1 || cfg->n_partitions > ssla::kMaxParts || cfg->max_events < 1 ||
+        (cfg->layout != SSLA_LAYOUT_DECOMP && cfg->layout != SSLA_LAYOUT_HYBRID)) {
+        ssla::g_last_error = "invalid SslaEngineConfig";
+        return SSLA_ERR_ARG;
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        ssla::g_last_error = "no CUDA device";
+        return SSLA_ERR_NO_DEVICE;
+    }
+    auto* h = new (std::nothrow) SslaEngine();
+    if (!h) { ssla::g_last_error = "host allocation failed"; return SSLA_ERR_CUDA; }
+    const int rc = ssla::guarded([&] { h->e.create(weights_dir, *cfg); return SSLA_OK; });
+    if (rc != SSLA_OK) { delete h; return rc; }
+    *out = h;
+    return SSLA_OK;
+}
+
+void ssla_engine_destroy(SslaEngine* eng) {
+    if (!eng) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(eng->e.device);
+    cudaDeviceSynchronize();
+    delete eng;
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+int ssla_engine_reset(SslaEngine* eng, void* stream) {
+    if (!eng) { ssla::g_last_error = "null engine"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] { eng->e.reset(static_cast<cudaStream_t>(stream)); return SSLA_OK; });
+}
+
+int ssla_engine_drain_device(SslaEngine* eng, const float* events_dev, const int* part_offsets,
+                             uint8_t* flags_dev, void* stream) {
+    if (!eng || !part_offsets || (!events_dev && part_offsets[eng->e.g.P] > 0)) {
+        ssla::g_last_error = "null argument";
+        return SSLA_ERR_ARG;
+    }
+    return ssla::guarded([&] {
+        eng->e.drain(events_dev, part_offsets, flags_dev, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_drain_host(SslaEngine* eng, const float* events_host, const int* part_offsets,
+                           uint8_t* flags_host, void* stream) {
+    if (!eng || !part_offsets) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const int n = part_offsets[e.g.P];
+        if (n < 0 || n > e.max_events) throw std::length_error("more events than max_events");
+        if (n > 0) {
+            if (!events_host) throw std::invalid_argument("null events");
+            SSLA_CK(cudaMemcpyAsync(e.ws.ev.p, events_host, sizeof(float) * 4 * n, cudaMemcpyHostToDevice, st));
+        }
+        e.drain(e.ws.ev.as<float>(), part_offsets, nullptr, st);
+        if (flags_host && n > 0)
+            SSLA_CK(cudaMemcpyAsync(flags_host, e.ws.rflags.p, n, cudaMemcpyDeviceToHost, st));
+        SSLA_CK(cudaStreamSynchronize(st));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes) {
+    if (!eng || !bytes) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    *bytes = eng->e.state_elems(kind, index) * ssla::Engine::elem_size(kind);
+    return *bytes ? SSLA_OK : SSLA_ERR_ARG;
+}
+
+static int state_args_ok(SslaEngine* eng, int kind, int partition, int index) {
+    if (!eng) return 0;
+    if (partition < 0 || partition >= eng->e.g.P) return 0;
+    if (kind == SSLA_STATE_HIDDEN && (index < 0 || index > 7)) return 0;
+    if (kind == SSLA_STATE_COUNTER && (index < 0 || index > 3)) return 0;
+    if (kind == SSLA_STATE_STAGE_OUT && (index < 0 || index > 3 || !eng->e.record)) return 0;
+    if (kind < 0 || kind > SSLA_STATE_FLAGS) return 0;
+    return 1;
+}
+
+int ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index, void* host_dst, size_t bytes) {
+    if (!state_args_ok(eng, kind, partition, index) || !host_dst) {
+        ssla::g_last_error = "bad state selector";
+        return SSLA_ERR_ARG;
+    }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        const size_t full = e.state_elems(kind, index) * ssla::Engine::elem_size(kind);
+        if (bytes > full) throw std::invalid_argument("read larger than the state buffer");
+        SSLA_CK(cudaDeviceSynchronize());
+        SSLA_CK(cudaMemcpy(host_dst, e.state_ptr(kind, partition, index), bytes, cudaMemcpyDeviceToHost));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_write_state(SslaEngine* eng, int kind, int partition, int index, const void* host_src,
+                            size_t bytes) {
+    if (!state_args_ok(eng, kind, partition, index) || !host_src || kind >= SSLA_STATE_STAGE_OUT) {
+        ssla::g_last_error = "bad state selector";
+        return SSLA_ERR_ARG;
+    }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        const size_t full = e.state_elems(kind, index) * ssla::Engine::elem_size(kind);
+        if (bytes > full) throw std::invalid_argument("write larger than the state buffer");
+        SSLA_CK(cudaDeviceSynchronize());
+        SSLA_CK(cudaMemcpy(e.state_ptr(kind, partition, index), host_src, bytes, cudaMemcpyHostToDevice));
+        return SSLA_OK;
+    });
+}
+
+void* ssla_engine_state_ptr(SslaEngine* eng, int kind, int partition, int index) {
+    if (!state_args_ok(eng, kind, partition, index)) return nullptr;
+    return eng->e.state_ptr(kind, partition, index);
+}
+
+int ssla_engine_info(SslaEngine* eng, SslaEngineInfo* info) {
+    if (!eng || !info) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        std::memset(info, 0, sizeof *info);
+        info->H = e.g.H[0]; info->W = e.g.W[0]; info->ncls = e.g.ncls; info->tdrop_window = e.g.window;
+        info->layout = e.layout; info->n_partitions = e.g.P; info->max_events = e.max_events;
+        info->device = e.device;
+        ssla::DeviceGuard dg(e.device);
+        int cnt[5] = {0};
+        SSLA_CK(cudaDeviceSynchronize());
+        SSLA_CK(cudaMemcpy(cnt, e.ws.count.p, sizeof cnt, cudaMemcpyDeviceToHost));
+        info->stage_events[0] = e.last_n;
+        for (int s = 1; s < 5; ++s) info->stage_events[s] = cnt[s];
+        return SSLA_OK;
+    });
+}
+
+int ssla_s2s3_drain_n_multi(const HybridS2S3Config* cfg, const HybridInputRec* const* rings, const int* ns,
+                            HybridS2S3OutputSlot* const* outs, unsigned long long* const* batch_clks,
+                            void* stream) {
+    if (!cfg || !rings || !ns) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        return ssla::drain_n_state().run(cfg, rings, ns, outs, batch_clks, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int ssla_s2s3_drain_n(const HybridS2S3Config* cfg, const HybridInputRec* ring0, const HybridInputRec* ring1,
+                      int n0, int n1, HybridS2S3OutputSlot* out0, HybridS2S3OutputSlot* out1,
+                      unsigned long long* batch_clk0, unsigned long long* batch_clk1, void* stream) {
+    if (!cfg) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    // The reference kernel runs exactly two blocks (ssla_s2_s3_head_celled.cuh:927).
+    HybridS2S3Config two = *cfg;
+    two.n_blocks = 2;
+    const HybridInputRec* rings[2] = {ring0, ring1};
+    const int ns[2] = {n0, n1};
+    HybridS2S3OutputSlot* outs[2] = {out0, out1};
+    unsigned long long* clks[2] = {batch_clk0, batch_clk1};
+    const bool any_clk = batch_clk0 || batch_clk1;
+    return ssla_s2s3_drain_n_multi(&two, rings, ns, (out0 || out1) ? outs : nullptr,
+                                   any_clk ? clks : nullptr, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,1096 @@
+// ssla_kernels.cu -- sm_100a kernels of the SSLA-S per-event hot path.
+//
+// One drain call processes a chunk of events for P independent partitions
+// (ring partitions / camera streams).  Kernel sequence (ssla_engine.cu):
+//   k_prep        validity + packed pixel coords per event
+//   k_filter(s0)  ordered tile lists of the events around each 8x8 tile
+//   k_gates       preprocess (dt_norm) + all four temporal-dropout gates +
+//                 layer-0 qvg/residual, one warp per (partition, s3 block)
+//   k_compact_*   stream-ordered stage lists E_1..E_4
+//   k_filter(s1..s3)
+//   per layer l:  k_scan (cell-major LRU update) then k_event (event-major
+//                 gather / LayerNorm / next-layer qvg, or the head)
+//   k_commit      last head write per s3 cell -> predictions + version
+// Reference behaviour each kernel reproduces is cited inline.
+#include "ssla_kernels.cuh"
+
+#include <cuda_runtime.h>
+
+#include "ssla_abi_types.h"
+
+namespace ssla {
+
+namespace {
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+__device__ __forceinline__ int hi_lane(unsigned m) { return 31 - __clz(m); }
+
+// uint8 counter rule of tdrop_check_at (src/ssla_kernels.cpp:912-921) and
+// parallel_tdrop (ssla_s2_s3_head_celled.cuh:742-745): pass iff window <= 1
+// or the pre-increment count (mod 256) is a multiple of the window.
+__device__ __forceinline__ bool gate_pass(int pre_count, int window) {
+    if (window <= 1) return true;
+    return ((pre_count & 255) % window) == 0;
+}
+
+// Warp-cooperative ordered gate over the lanes in `active` (stream order ==
+// lane order).  `key` selects a counter in smem `cnt`; lanes not in `active`
+// must pass a key unique to themselves.  Returns this lane's pass bit and
+// advances the counters.
+__device__ __forceinline__ bool warp_gate(bool active, int key, int* cnt, int window) {
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    bool pass = false;
+    if (active) pass = gate_pass(cnt[key] + __popc(peers & lanemask_lt()), window);
+    __syncwarp();
+    if (active && (threadIdx.x & 31) == hi_lane(peers)) cnt[key] += __popc(peers);
+    __syncwarp();
+    return pass;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// k_prep: bounds rule of the drivers (s2_decomp_st.cpp:140-144,
+// lib_stage01_to_gpu.cpp:210-214): int truncation then range check; written
+// as float comparisons so NaN / huge values are rejected like on the host.
+// ---------------------------------------------------------------------------
+__global__ void k_prep(const float4* __restrict__ ev, int n, int W0, int H0,
+                       uint32_t* __restrict__ ev_xy, uint8_t* __restrict__ rflags) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float4 e = ev[i];
+        uint32_t xy = kInvalidXY;
+        if (e.y > -1.0f && e.y < static_cast<float>(W0) && e.z > -1.0f && e.z < static_cast<float>(H0)) {
+            const int x = static_cast<int>(e.y), y = static_cast<int>(e.z);
+            xy = static_cast<uint32_t>(x) | (static_cast<uint32_t>(y) << 16);
+        }
+        ev_xy[i] = xy;
+        rflags[i] = 0;
+    }
+}
+
+// Stage-2 entry (drain_n): records -> E_2 identity list + packed coords.
+__global__ void k_prep_records(const HybridInputRec* __restrict__ rec, int n,
+                               StageEntry* __restrict__ E2, uint32_t* __restrict__ ev_xy,
+                               uint8_t* __restrict__ rflags, float* __restrict__ feat) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const uint32_t x2 = rec[i].x, y2 = rec[i].y;
+        const uint32_t xy0 = (x2 << 2) | ((y2 << 2) << 16);
+        E2[i] = StageEntry{i, i, xy0};
+        ev_xy[i] = xy0;
+        rflags[i] = F_VALID | F_R1 | F_R2;
+        for (int c = 0; c < 24; ++c) feat[static_cast<size_t>(i) * 24 + c] = rec[i].feat1[c];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_filter: for (partition, tile, segment) compact, in stream order, the
+// stage entries whose stage cell lies in the tile grown by one cell (the
+// entries whose 3x3 patch touches the tile).  grid (P, tiles, segments).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
+    const int p = blockIdx.x, tile = blockIdx.y, seg = blockIdx.z;
+    const int s = a.stage;
+    const int ntiles = a.g.tx[s] * a.g.ty[s];
+    const int lo = a.range[p], hi = a.range[p + 1];
+    const int seg_lo = lo + seg * a.g.seg;
+    if (seg_lo >= hi || seg >= a.g.nseg[s]) return;
+    const int seg_hi = min(hi, seg_lo + a.g.seg);
+    const int tx0 = (tile % a.g.tx[s]) * kTile, ty0 = (tile / a.g.tx[s]) * kTile;
+    const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
+    int2* out = a.tl + slot * a.g.seg;
+    __shared__ int warp_tot[kNT / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int running = 0;
+    for (int j0 = seg_lo; j0 < seg_hi; j0 += kNT) {
+        const int j = j0 + threadIdx.x;
+        bool hit = false;
+        int2 ent = make_int2(0, 0);
+        if (j < seg_hi) {
+            uint32_t xy0;
+            uint32_t flag = 0;
+            if (s == 0) {
+                xy0 = a.ev_xy[j];
+            } else {
+                const StageEntry se = a.E[j];
+                xy0 = se.xy0;
+                flag = (a.rflags[se.e] & a.out_bit) ? 1u : 0u;
+            }
+            if (xy0 != kInvalidXY) {
+                const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s;
+                const int cy = static_cast<int>(xy0 >> 16) >> s;
+                hit = cx >= tx0 - 1 && cx <= tx0 + kTile && cy >= ty0 - 1 && cy <= ty0 + kTile;
+                ent = make_int2(j, static_cast<int>(static_cast<uint32_t>(cx) |
+                                                    (static_cast<uint32_t>(cy) << 16) | (flag << 31)));
+            }
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        if (lane == 0) warp_tot[warp] = __popc(m);
+        __syncthreads();
+        int woff = 0, tot = 0;
+#pragma unroll
+        for (int w = 0; w < kNT / 32; ++w) {
+            const int c = warp_tot[w];
+            woff += (w < warp) ? c : 0;
+            tot += c;
+        }
+        if (hit) out[running + woff + __popc(m & lanemask_lt())] = ent;
+        running += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) a.tl_cnt[slot] = running;
+}
+
+// ---------------------------------------------------------------------------
+// k_gates: one warp per (partition, s3 block).  Walks the block's own events
+// in stream order (from the stage-0 tile list of the block) and computes
+//   preprocess  dt_norm = clamp((t - last_t[pix]) / 1e5, 0, 1), 1 on a first
+//               hit (src/ssla_kernels.cpp:288-309)
+//   gate 0 / 1 / 2 / 3 on the layout's grids (all cells of an event's gates
+//               lie inside its s3 block, so the block owns every counter it
+//               touches)
+//   layer 0 qvg (q, v, sigmoid(g)) and residual input_proj * (dt, p).
+// Same-key ordering inside a 32-event window uses __match_any_sync ranks.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(32) k_gates(GateArgs a) {
+    const int p = blockIdx.x, blk = blockIdx.y;
+    const int W3 = a.g.W[3];
+    const int bx = blk % W3, by = blk / W3;
+    const int lane = threadIdx.x;
+    const PartState ps = a.parts[p];
+    const bool hyb = a.g.layout == LAYOUT_HYBRID;
+    const int window = a.g.window;
+    __shared__ double lt[64];
+    __shared__ int c0[16], c1[4], c2[4], c3[1];
+    const int W0 = a.g.W[0], W1 = a.g.W[1], W2 = a.g.W[2];
+    for (int i = lane; i < 64; i += 32)
+        lt[i] = ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)];
+    if (lane < 16) c0[lane] = ps.cnt[0][(by * 4 + lane / 4) * W1 + bx * 4 + (lane % 4)];
+    if (lane < 4) c1[lane] = ps.cnt[1][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)];
+    if (hyb) {
+        if (lane < 4) c2[lane] = ps.cnt[2][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)];
+        if (lane == 0) c3[0] = ps.cnt[3][by * W3 + bx];
+    } else if (lane == 0) {
+        c2[0] = ps.cnt[2][by * W3 + bx];
+    }
+    __syncwarp();
+
+    const int ntiles = a.g.tx[0] * a.g.ty[0];
+    const int tile = by * a.g.tx[0] + bx;     // s0 tiles are the s3 blocks
+    const int n_p = a.ev_off[p + 1] - a.ev_off[p];
+    const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[0]);
+    const float* qT = a.L0.qvgT;               // [1][2][36]
+    const float* ipT = a.L0.ipT;               // [2][12]
+    for (int seg = 0; seg < nseg; ++seg) {
+        const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0] + seg;
+        const int cnt = a.tl0_cnt[slot];
+        const int2* lst = a.tl0 + slot * a.g.seg;
+        for (int j0 = 0; j0 < cnt; j0 += 32) {
+            const int j = j0 + lane;
+            int2 ent = make_int2(0, 0);
+            if (j < cnt) ent = lst[j];
+            const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
+            const bool own = (j < cnt) && (x0 >> 3) == bx && (y0 >> 3) == by;
+            if (__ballot_sync(0xffffffffu, own) == 0u) continue;
+            const int k = ent.x;
+            float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (own) e = a.ev[k];
+            // preprocess
+            const int pix = own ? ((y0 & 7) * 8 + (x0 & 7)) : (64 + lane);
+            const unsigned peers = __match_any_sync(0xffffffffu, pix);
+            const unsigned prevm = peers & lanemask_lt();
+            const int src = prevm ? hi_lane(prevm) : lane;
+            const float t_prev_lane = __shfl_sync(0xffffffffu, e.x, src);
+            float dt = 0.0f;
+            if (own) {
+                const double prev = prevm ? static_cast<double>(t_prev_lane) : lt[pix];
+                if (prev < 0.0) {
+                    dt = 1.0f;
+                } else {
+                    double v = (static_cast<double>(e.x) - prev) / 1e5;
+                    if (v < 0.0) v = 0.0;
+                    if (v > 1.0) v = 1.0;
+                    dt = static_cast<float>(v);
+                }
+            }
+            __syncwarp();
+            if (own && lane == hi_lane(peers)) lt[pix] = static_cast<double>(e.x);
+            __syncwarp();
+            // gates
+            const int k0 = own ? (((y0 >> 1) & 3) * 4 + ((x0 >> 1) & 3)) : (100 + lane);
+            const bool pass0 = warp_gate(own, k0, c0, window);
+            const bool in1 = own && pass0;
+            const int sub2 = ((y0 >> 2) & 1) * 2 + ((x0 >> 2) & 1);
+            const bool pass1 = warp_gate(in1, in1 ? sub2 : 100 + lane, c1, window);
+            const bool in2 = in1 && pass1;
+            const bool pass2 = warp_gate(in2, in2 ? (hyb ? sub2 : 0) : 100 + lane, c2, window);
+            const bool in3 = in2 && pass2;
+            bool pass3 = true;
+            if (hyb) pass3 = warp_gate(in3, in3 ? 0 : 100 + lane, c3, window);
+            if (own) {
+                uint8_t f = F_VALID;
+                if (pass0) f |= F_R1;
+                if (in2) f |= F_R2;
+                if (in3) f |= F_R3;
+                if (in3 && pass3) f |= F_R4;
+                a.rflags[k] = f;
+                // layer 0: qvg = qvgIn[0] * (dt, p) (matvec_ct<2,36>), residual
+                // = input_proj * (dt, p) (matvec_ct<2,12>).
+                float* S = a.S0 + static_cast<size_t>(k) * 36;
+#pragma unroll 4
+                for (int jj = 0; jj < 36; ++jj) {
+                    float acc = fmaf(__ldg(qT + jj), dt, 0.0f);
+                    acc = fmaf(__ldg(qT + 36 + jj), e.w, acc);
+                    S[jj] = (jj >= 24) ? ssla_sigmoidf(acc) : acc;
+                }
+                float* R = a.R0 + static_cast<size_t>(k) * 12;
+#pragma unroll 4
+                for (int o = 0; o < 12; ++o) {
+                    float acc = fmaf(__ldg(ipT + o), dt, 0.0f);
+                    R[o] = fmaf(__ldg(ipT + 12 + o), e.w, acc);
+                }
+            }
+        }
+    }
+    __syncwarp();
+    for (int i = lane; i < 64; i += 32)
+        ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)] = lt[i];
+    if (lane < 16) ps.cnt[0][(by * 4 + lane / 4) * W1 + bx * 4 + (lane % 4)] = static_cast<uint8_t>(c0[lane]);
+    if (lane < 4) ps.cnt[1][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)] = static_cast<uint8_t>(c1[lane]);
+    if (hyb) {
+        if (lane < 4) ps.cnt[2][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)] = static_cast<uint8_t>(c2[lane]);
+        if (lane == 0) ps.cnt[3][by * W3 + bx] = static_cast<uint8_t>(c3[0]);
+    } else if (lane == 0) {
+        ps.cnt[2][by * W3 + bx] = static_cast<uint8_t>(c2[0]);
+    }
+}
+
+// drain_n records entering at stage 2: tdrop_s2 (s2 grid) then, for the
+// passing records, tdrop_s3 (s3 grid) -- ssla_s2_s3_head_celled.cuh:1020-1051.
+// One warp per (partition, s3 cell); walks the stage-2 tile list holding it.
+__global__ void __launch_bounds__(32) k_gates_s2(Gate2Args a) {
+    const int p = blockIdx.x, cell = blockIdx.y;
+    const int W3 = a.g.W[3], W2 = a.g.W[2];
+    const int gx = cell % W3, gy = cell / W3;
+    const int lane = threadIdx.x;
+    const PartState ps = a.parts[p];
+    const int window = a.g.window;
+    __shared__ int c2[4], c3[1];
+    if (lane < 4) c2[lane] = ps.cnt[2][(gy * 2 + lane / 2) * W2 + gx * 2 + (lane % 2)];
+    if (lane == 0) c3[0] = ps.cnt[3][gy * W3 + gx];
+    __syncwarp();
+    const int ntiles = a.g.tx[2] * a.g.ty[2];
+    const int tile = ((gy * 2) / kTile) * a.g.tx[2] + (gx * 2) / kTile;
+    const int n_p = a.rec_off[p + 1] - a.rec_off[p];
+    const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[2]);
+    for (int seg = 0; seg < nseg; ++seg) {
+        const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[2] + seg;
+        const int cnt = a.tl2_cnt[slot];
+        const int2* lst = a.tl2 + slot * a.g.seg;
+        for (int j0 = 0; j0 < cnt; j0 += 32) {
+            const int j = j0 + lane;
+            int2 ent = make_int2(0, 0);
+            if (j < cnt) ent = lst[j];
+            const int x2 = ent.y & 0xFFFF, y2 = (ent.y >> 16) & 0x7FFF;
+            const bool own = (j < cnt) && (x2 >> 1) == gx && (y2 >> 1) == gy;
+            if (__ballot_sync(0xffffffffu, own) == 0u) continue;
+            const int sub = (y2 & 1) * 2 + (x2 & 1);
+            const bool p2 = warp_gate(own, own ? sub : 100 + lane, c2, window);
+            const bool in3 = own && p2;
+            const bool p3 = warp_gate(in3, in3 ? 0 : 100 + lane, c3, window);
+            if (own) {
+                uint8_t f = F_VALID | F_R1 | F_R2;
+                if (p2) f |= F_R3;
+                if (in3 && p3) f |= F_R4;
+                a.rflags[ent.x] = f;
+            }
+        }
+    }
+    __syncwarp();
+    if (lane < 4) ps.cnt[2][(gy * 2 + lane / 2) * W2 + gx * 2 + (lane % 2)] = static_cast<uint8_t>(c2[lane]);
+    if (lane == 0) ps.cnt[3][gy * W3 + gx] = static_cast<uint8_t>(c3[0]);
+}
+
+// ---------------------------------------------------------------------------
+// Stage-list compaction (stream order) of the events whose reach bit R_s is
+// set, for lists s_first+1 .. 4.  Compaction tiles never straddle partitions.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kNT) k_compact_count(CompactArgs a) {
+    const int p = blockIdx.x, t = blockIdx.y;
+    const int lo = a.ev_off[p] + t * kCompactTile;
+    const int hi = min(a.ev_off[p + 1], lo + kCompactTile);
+    int c[4] = {0, 0, 0, 0};
+    for (int i = lo + static_cast<int>(threadIdx.x); i < hi; i += kNT) {
+        const uint8_t f = a.rflags[i];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) c[s] += (f >> (s + 1)) & 1;
+    }
+    __shared__ int red[kNT / 32][4];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        int v = c[s];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+        if (lane == 0) red[warp][s] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 4) {
+        int v = 0;
+        for (int w = 0; w < kNT / 32; ++w) v += red[w][threadIdx.x];
+        a.tilecnt[(static_cast<size_t>(p) * a.tiles_per_part + t) * 4 + threadIdx.x] = v;
+    }
+}
+
+__global__ void __launch_bounds__(kNT) k_compact_scan(CompactArgs a) {
+    const int n = a.g.P * a.tiles_per_part;
+    __shared__ int carry[4];
+    __shared__ int wsum[kNT / 32][4];
+    if (threadIdx.x < 4) carry[threadIdx.x] = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int b0 = 0; b0 < n; b0 += kNT) {
+        const int i = b0 + threadIdx.x;
+        int v[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) v[s] = (i < n) ? a.tilecnt[static_cast<size_t>(i) * 4 + s] : 0;
+        int incl[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            int x = v[s];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            incl[s] = x;
+            if (lane == 31) wsum[warp][s] = x;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            int wo = 0, tot = 0;
+            for (int w = 0; w < kNT / 32; ++w) {
+                wo += (w < warp) ? wsum[w][s] : 0;
+                tot += wsum[w][s];
+            }
+            if (i < n) a.tilebase[static_cast<size_t>(i) * 4 + s] = carry[s] + wo + incl[s] - v[s];
+            __syncthreads();
+            if (threadIdx.x == 0) carry[s] += tot;
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x < 4) {
+        const int s = threadIdx.x + 1;
+        if (s > a.s_first) {
+            for (int p = 0; p < a.g.P; ++p)
+                a.off[s][p] = min(a.tilebase[(static_cast<size_t>(p) * a.tiles_per_part) * 4 + threadIdx.x],
+                                  a.g.cap[s]);
+            a.off[s][a.g.P] = min(carry[threadIdx.x], a.g.cap[s]);
+            a.count[s] = min(carry[threadIdx.x], a.g.cap[s]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kNT) k_compact_scatter(CompactArgs a) {
+    const int p = blockIdx.x, t = blockIdx.y;
+    const int lo = a.ev_off[p] + t * kCompactTile;
+    const int hi = min(a.ev_off[p + 1], lo + kCompactTile);
+    if (lo >= hi) return;
+    __shared__ int wtot[kNT / 32][4];
+    __shared__ int run[4];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x < 4)
+        run[threadIdx.x] = a.tilebase[(static_cast<size_t>(p) * a.tiles_per_part + t) * 4 + threadIdx.x];
+    __syncthreads();
+    for (int j0 = lo; j0 < hi; j0 += kNT) {
+        const int i = j0 + threadIdx.x;
+        const uint8_t f = (i < hi) ? a.rflags[i] : 0;
+        unsigned m[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            m[s] = __ballot_sync(0xffffffffu, (f >> (s + 1)) & 1);
+            if (lane == 0) wtot[warp][s] = __popc(m[s]);
+        }
+        __syncthreads();
+        int pos[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            int wo = 0;
+            for (int w = 0; w < warp; ++w) wo += wtot[w][s];
+            pos[s] = run[s] + wo + __popc(m[s] & lanemask_lt());
+        }
+        if (i < hi) {
+            const uint32_t xy0 = a.ev_xy[i];
+            int prev = i;                           // E_0 index == event index
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int list = s + 1;
+                if ((f >> list) & 1) {
+                    if (list > a.s_first && pos[s] < a.g.cap[list])
+                        a.E[list][pos[s]] = StageEntry{i, prev, xy0};
+                    prev = (list > a.s_first) ? pos[s] : i;
+                }
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < 4) {
+            int tot = 0;
+            for (int w = 0; w < kNT / 32; ++w) tot += wtot[w][threadIdx.x];
+            run[threadIdx.x] += tot;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_scan: one warp per (partition, cell) of the layer's grid, 8 cells per CTA.
+// Walks, in stream order, the tile-list entries whose 3x3 patch covers the
+// cell (only the cell itself for the K=1 layer) and applies lru_step
+// (vendor/openeva/prim/rnn.h:80-91): h = sigmoid(g) * h + v (fmaf), and
+// q -> q * h for entries whose layer output is consumed.  Lanes own
+// channels; hidden state stays in registers for the whole chunk.
+// grid (P, tiles, 8), block 256.
+// ---------------------------------------------------------------------------
+template <int A, int OUT>
+__global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
+    constexpr int CPL = (OUT + 31) / 32;
+    const int p = blockIdx.x, tile = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int s = a.stage;
+    const int local = blockIdx.z * (kNT / 32) + warp;     // 0..63 in the tile
+    const int cx = (tile % a.g.tx[s]) * kTile + (local % kTile);
+    const int cy = (tile / a.g.tx[s]) * kTile + (local / kTile);
+    const int Wl = a.g.W[s], Hl = a.g.H[s];
+    if (cx >= Wl || cy >= Hl) return;
+    float* hp = a.parts[p].hidden[a.layer] + (static_cast<size_t>(cy) * Wl + cx) * OUT;
+    float h[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        const int o = lane + 32 * c;
+        h[c] = (o < OUT) ? hp[o] : 0.0f;
+    }
+    const int ntiles = a.g.tx[s] * a.g.ty[s];
+    const int n_p = a.range[p + 1] - a.range[p];
+    const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
+    float* __restrict__ S = a.S;
+    for (int seg = 0; seg < nseg; ++seg) {
+        const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
+        const int cnt = a.tl_cnt[slot];
+        const int2* lst = a.tl + slot * a.g.seg;
+        for (int j0 = 0; j0 < cnt; j0 += 32) {
+            const int j = j0 + lane;
+            int2 ent = make_int2(0, 0);
+            if (j < cnt) ent = lst[j];
+            const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
+            const int dx = cx - ex, dy = cy - ey;
+            bool hit;
+            if (A == 1) hit = (j < cnt) && dx == 0 && dy == 0;
+            else hit = (j < cnt) && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1;
+            const int delta = (A == 1) ? 0 : (1 - dy) * 3 + (1 - dx);    // ssla_kernels.cpp:375
+            int outf = 1;
+            if (a.second) {
+                if (s == 0) outf = (hit && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
+                else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
+            }
+            const int pk = ent.x * A + delta;                     // (entry, delta) row
+            const int pkf = (pk << 1) | outf;
+            unsigned m = __ballot_sync(0xffffffffu, hit);
+            while (m) {
+                int row[4], of[4];
+                int nh = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int src = m ? (__ffs(m) - 1) : 0;
+                    const int v = __shfl_sync(0xffffffffu, pkf, src);
+                    row[q] = v >> 1;
+                    of[q] = (m != 0u) ? (v & 1) : 0;
+                    nh += (m != 0u) ? 1 : 0;
+                    m &= (m - 1u);
+                }
+                float qv[4][CPL], vv[4][CPL], av[4][CPL];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
+#pragma unroll
+                    for (int c = 0; c < CPL; ++c) {
+                        const int o = lane + 32 * c;
+                        const bool ok = (q < nh) && (o < OUT);
+                        qv[q][c] = (ok && of[q]) ? r[o] : 0.0f;
+                        vv[q][c] = ok ? r[OUT + o] : 0.0f;
+                        av[q][c] = ok ? r[2 * OUT + o] : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (q < nh) {
+                        float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
+#pragma unroll
+                        for (int c = 0; c < CPL; ++c) {
+                            const int o = lane + 32 * c;
+                            if (o < OUT) {
+                                h[c] = fmaf(av[q][c], h[c], vv[q][c]);
+                                if (of[q]) r[o] = qv[q][c] * h[c];
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        const int o = lane + 32 * c;
+        if (o < OUT) hp[o] = h[c];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_event: event-major, 32 events per batch, 256 threads.
+//   x  = gather (modes 0-3): out = sum over delta = 8..0 of
+//        goW[delta] * qh[delta] (each delta an fmaf chain from 0, added in the
+//        reference's patch order, layer_forward_ct :340-380), + residual,
+//        fp64 LayerNorm (layernorm_ct, layernorm.h:41-62)
+//     or the record's stage-1 feature (mode 4);
+//   then the next layer's qvg for its patch positions (matvec_ct<IN,3*OUT>,
+//   q rows only where that layer's output is consumed) and residual
+//   (input_proj or copy), or the YOLOX head (mode 2,
+//   async_yolox.h:203-254).
+// Thread tiles: one output x 8 events; weights stream from L2 once per
+// 8 events, features come from shared memory.
+// ---------------------------------------------------------------------------
+template <int A, int OUT, int A2, int OUT2, int MODE>
+__global__ void __launch_bounds__(kNT) k_event(EventArgs a) {
+    constexpr int XD = (MODE == MODE_ENTRY) ? 24 : OUT;     // feature width
+    __shared__ __align__(16) float sm[3 * 96 * kMB];
+    float* qh_s = sm;                     // [OUT][kMB]
+    float* out_s = sm + 96 * kMB;         // [OUT][kMB]
+    float* x_s = sm + 2 * 96 * kMB;       // [XD][kMB]
+    float* act_s = sm;                    // head: [192][kMB] (qh_s + out_s)
+    __shared__ int kin_s[kMB], kout_s[kMB], e_s[kMB], valid_s[kMB], needq_s[kMB];
+    __shared__ int cx_s[kMB], cy_s[kMB], cx2_s[kMB], cy2_s[kMB];
+    __shared__ unsigned inb_s[kMB], inb2_s[kMB];
+    __shared__ double mean_s[kMB], inv_s[kMB];
+    __shared__ float res_s[kMB][24];
+    const int tid = threadIdx.x;
+    const int s = a.stage;
+    const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
+    const int Wl = a.g.W[s], Hl = a.g.H[s];
+    const int s2 = (MODE == MODE_FIRST || MODE == MODE_ENTRY) ? s : s + 1;   // next layer's stage
+    const int W2 = a.g.W[s2 < 4 ? s2 : 3], H2 = a.g.H[s2 < 4 ? s2 : 3];
+
+    for (int batch = blockIdx.x; batch * kMB < n_list; batch += gridDim.x) {
+        if (tid < kMB) {
+            const int idx = batch * kMB + tid;
+            int valid = 0, kin = 0, kout = 0, e = 0, needq = 1;
+            uint32_t xy0 = 0;
+            if (idx < n_list) {
+                if (a.list == 0) {                              // stage 0, all events
+                    e = idx; kin = idx; kout = idx;
+                    xy0 = a.ev_xy[idx];
+                    valid = (a.rflags[idx] & F_VALID) ? 1 : 0;
+                } else if (MODE == MODE_FIRST || MODE == MODE_ENTRY) {
+                    const StageEntry se = a.E[idx];
+                    e = se.e; kin = idx; kout = idx; xy0 = se.xy0; valid = 1;
+                } else {
+                    const StageEntry se = a.E[idx];
+                    e = se.e; kin = se.kprev; kout = idx; xy0 = se.xy0; valid = 1;
+                }
+                if (valid && MODE == MODE_FIRST) needq = (a.rflags[e] & a.needq_bit) ? 1 : 0;
+            }
+            const int x0 = static_cast<int>(xy0 & 0xFFFFu), y0 = static_cast<int>(xy0 >> 16);
+            const int cx = x0 >> s, cy = y0 >> s;
+            const int cx2 = x0 >> (s2 < 4 ? s2 : 3), cy2 = y0 >> (s2 < 4 ? s2 : 3);
+            unsigned m1 = 0, m2 = 0;
+            for (int d = 0; d < 9; ++d) {
+                const int dy = 1 - d / 3, dx = 1 - d % 3;
+                if (cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl) m1 |= 1u << d;
+                if (cx2 + dx >= 0 && cx2 + dx < W2 && cy2 + dy >= 0 && cy2 + dy < H2) m2 |= 1u << d;
+            }
+            valid_s[tid] = valid; kin_s[tid] = kin; kout_s[tid] = kout; e_s[tid] = e;
+            needq_s[tid] = needq; cx_s[tid] = cx; cy_s[tid] = cy; cx2_s[tid] = cx2; cy2_s[tid] = cy2;
+            inb_s[tid] = (A == 1) ? 1u : m1;
+            inb2_s[tid] = (A2 == 1) ? 1u : m2;
+        }
+        __syncthreads();
+
+        if (MODE == MODE_ENTRY) {
+            for (int t = tid; t < XD * kMB; t += kNT) {
+                const int i = t / kMB, b = t % kMB;
+                x_s[t] = valid_s[b] ? a.entry_feat[static_cast<size_t>(e_s[b]) * 24 + i] : 0.0f;
+            }
+        } else {
+            // ---- gather over patch positions in the reference order ----
+            for (int t = tid; t < OUT * kMB; t += kNT) out_s[t] = 0.0f;
+            for (int d = A - 1; d >= 0; --d) {
+                __syncthreads();
+                for (int t = tid; t < OUT * kMB; t += kNT) {
+                    const int i = t / kMB, b = t % kMB;
+                    float v = 0.0f;
+                    if (valid_s[b] && ((inb_s[b] >> d) & 1u))
+                        v = a.S_in[(static_cast<size_t>(kin_s[b]) * A + d) * (3 * OUT) + i];
+                    qh_s[t] = v;
+                }
+                __syncthreads();
+                for (int item = tid; item < OUT * kGroups; item += kNT) {
+                    const int o = item % OUT, g = item / OUT;
+                    float acc[kEPT];
+#pragma unroll
+                    for (int b = 0; b < kEPT; ++b) acc[b] = 0.0f;
+                    const float* w = a.L.goWT + static_cast<size_t>(d) * OUT * OUT + o;
+#pragma unroll 4
+                    for (int i = 0; i < OUT; ++i) {
+                        const float wv = __ldg(w + static_cast<size_t>(i) * OUT);
+                        const float4 x0 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT);
+                        const float4 x1 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT + 4);
+                        acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
+                        acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
+                        acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
+                        acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
+                    }
+#pragma unroll
+                    for (int b = 0; b < kEPT; ++b) out_s[o * kMB + g * kEPT + b] += acc[b];
+                }
+            }
+            __syncthreads();
+            // ---- residual + LayerNorm statistics (sequential fp64 per event) ----
+            if (tid < kMB && valid_s[tid]) {
+                const int b = tid;
+                const float* r = a.R_in + static_cast<size_t>(kin_s[b]) * OUT;
+                double sum = 0.0;
+                for (int o = 0; o < OUT; ++o) {
+                    const float v = out_s[o * kMB + b] + r[o];
+                    out_s[o * kMB + b] = v;
+                    sum += static_cast<double>(v);
+                }
+                const double mean = sum / static_cast<double>(OUT);
+                double var = 0.0;
+                for (int o = 0; o < OUT; ++o) {
+                    const double dd = static_cast<double>(out_s[o * kMB + b]) - mean;
+                    var += dd * dd;
+                }
+                var /= static_cast<double>(OUT);
+                mean_s[b] = mean;
+                inv_s[b] = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+            }
+            __syncthreads();
+            for (int t = tid; t < OUT * kMB; t += kNT) {
+                const int o = t / kMB, b = t % kMB;
+                float xv = 0.0f;
+                if (valid_s[b]) {
+                    const double v = (static_cast<double>(out_s[t]) - mean_s[b]) * inv_s[b];
+                    xv = static_cast<float>(v * static_cast<double>(__ldg(a.L.gamma + o)) +
+                                            static_cast<double>(__ldg(a.L.beta + o)));
+                }
+                x_s[t] = xv;
+            }
+        }
+        __syncthreads();
+        // ---- per-event feature outputs ----
+        if (MODE != MODE_ENTRY && (a.stage_out != nullptr || a.slot_feat != nullptr)) {
+            for (int t = tid; t < OUT * kMB; t += kNT) {
+                const int b = t % kMB, o = t / kMB;
+                if (!valid_s[b]) continue;
+                if (a.stage_out && MODE != MODE_FIRST)
+                    a.stage_out[static_cast<size_t>(e_s[b]) * OUT + o] = x_s[t];
+                if (a.slot_feat) {
+                    a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + o] = x_s[t];
+                    if (OUT == 48) a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + 48 + o] = 0.0f;
+                }
+            }
+        }
+
+        if (MODE == MODE_FIRST || MODE == MODE_SECOND || MODE == MODE_ENTRY) {
+            // ---- next layer: qvg for every patch position, then residual ----
+            constexpr int J2 = 3 * OUT2;
+            for (int item = tid; item < A2 * J2 * kGroups; item += kNT) {
+                const int j = item % (A2 * J2), g = item / (A2 * J2);
+                const int d2 = j / J2, jj = j % J2, part = jj / OUT2;
+                unsigned gm = 0;
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) {
+                    const int bb = g * kEPT + b;
+                    const bool need = valid_s[bb] && ((inb2_s[bb] >> d2) & 1u) &&
+                                      (part != 0 || needq_s[bb]);
+                    gm |= need ? (1u << b) : 0u;
+                }
+                if (!gm) continue;
+                float acc[kEPT];
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) acc[b] = 0.0f;
+                const float* w = a.N.qvgT + static_cast<size_t>(d2) * XD * J2 + jj;
+#pragma unroll 4
+                for (int i = 0; i < XD; ++i) {
+                    const float wv = __ldg(w + static_cast<size_t>(i) * J2);
+                    const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
+                    const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
+                    acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
+                    acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
+                    acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
+                    acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
+                }
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) {
+                    if ((gm >> b) & 1u) {
+                        const float v = (part == 2) ? ssla_sigmoidf(acc[b]) : acc[b];
+                        a.S_out[(static_cast<size_t>(kout_s[g * kEPT + b]) * A2 + d2) * J2 + jj] = v;
+                    }
+                }
+            }
+            for (int item = tid; item < OUT2 * kGroups; item += kNT) {
+                const int o2 = item % OUT2, g = item / OUT2;
+                float acc[kEPT];
+                if (a.N.ipT != nullptr) {
+#pragma unroll
+                    for (int b = 0; b < kEPT; ++b) acc[b] = 0.0f;
+                    for (int i = 0; i < XD; ++i) {
+                        const float wv = __ldg(a.N.ipT + static_cast<size_t>(i) * OUT2 + o2);
+#pragma unroll
+                        for (int b = 0; b < kEPT; ++b)
+                            acc[b] = fmaf(wv, x_s[i * kMB + g * kEPT + b], acc[b]);
+                    }
+                } else {
+#pragma unroll
+                    for (int b = 0; b < kEPT; ++b) acc[b] = x_s[o2 * kMB + g * kEPT + b];
+                }
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) {
+                    const int bb = g * kEPT + b;
+                    if (valid_s[bb] && needq_s[bb])
+                        a.R_out[static_cast<size_t>(kout_s[bb]) * OUT2 + o2] = acc[b];
+                }
+            }
+        } else if (MODE == MODE_HEAD) {
+            // ---- YOLOX head: cls / reg 1x1 convs (BN folded) + SiLU ----
+            for (int item = tid; item < 192 * kGroups; item += kNT) {
+                const int j = item % 192, g = item / 192;
+                const int jo = j % 96;
+                const float* W = (j < 96) ? a.head.cls_convT : a.head.reg_convT;
+                const float bias = __ldg(((j < 96) ? a.head.cls_conv_b : a.head.reg_conv_b) + jo);
+                float acc[kEPT];
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) acc[b] = bias;
+#pragma unroll 4
+                for (int i = 0; i < 96; ++i) {
+                    const float wv = __ldg(W + i * 96 + jo);
+                    const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
+                    const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
+                    acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
+                    acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
+                    acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
+                    acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
+                }
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b)
+                    act_s[j * kMB + g * kEPT + b] = acc[b] * ssla_sigmoidf(acc[b]);
+            }
+            __syncthreads();
+            const int ncls = a.g.ncls, cols = 5 + ncls;
+            for (int item = tid; item < kMB * cols; item += kNT) {
+                const int b = item % kMB, r = item / kMB;
+                if (!valid_s[b]) continue;
+                float acc;
+                if (r < 4) {
+                    acc = __ldg(a.head.reg_pred_b + r);
+                    for (int i = 0; i < 96; ++i)
+                        acc = fmaf(__ldg(a.head.reg_predT + i * 4 + r), act_s[(96 + i) * kMB + b], acc);
+                } else if (r == 4) {
+                    acc = __ldg(a.head.obj_pred_b);
+                    for (int i = 0; i < 96; ++i)
+                        acc = fmaf(__ldg(a.head.obj_predT + i), act_s[(96 + i) * kMB + b], acc);
+                } else {
+                    const int c = r - 5;
+                    acc = __ldg(a.head.cls_pred_b + c);
+                    for (int i = 0; i < 96; ++i)
+                        acc = fmaf(__ldg(a.head.cls_predT + i * ncls + c), act_s[i * kMB + b], acc);
+                }
+                res_s[b][r] = acc;
+            }
+            __syncthreads();
+            for (int item = tid; item < kMB * cols; item += kNT) {
+                const int b = item % kMB, r = item / kMB;
+                if (!valid_s[b]) continue;
+                const float v = res_s[b][r];
+                float d;
+                if (r == 0) d = (v + static_cast<float>(cx_s[b])) * static_cast<float>(a.g.stride_w);
+                else if (r == 1) d = (v + static_cast<float>(cy_s[b])) * static_cast<float>(a.g.stride_h);
+                else if (r == 2) d = ssla_expf(v) * static_cast<float>(a.g.stride_w);
+                else if (r == 3) d = ssla_expf(v) * static_cast<float>(a.g.stride_h);
+                else d = v;
+                a.head_dec[static_cast<size_t>(kout_s[b]) * cols + r] = d;
+                a.head_raw[static_cast<size_t>(kout_s[b]) * cols + r] = v;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_commit: one warp per (partition, s3 cell): the last head event of the
+// chunk at the cell (stream order) sets the cell's prediction rows, and the
+// version counter advances by the number of head writes
+// (ssla_kernels.cpp:927-967 last-writer semantics; ssla_s2_s3_head_celled.cuh:
+// 887-901 ownership + version).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kNT) k_commit(CommitArgs a) {
+    const int p = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int W3 = a.g.W[3], H3 = a.g.H[3];
+    const int cell = blockIdx.y * (kNT / 32) + warp;
+    if (cell >= W3 * H3) return;
+    const PartState ps = a.parts[p];
+    const int lo = a.off4[p], hi = min(a.off4[p + 1], a.g.cap[4]);
+    int count = 0, last = -1;
+    for (int j0 = lo; j0 < hi; j0 += 32) {
+        const int j = j0 + lane;
+        bool hit = false;
+        if (j < hi) {
+            const uint32_t xy0 = a.E4[j].xy0;
+            const int x0 = static_cast<int>(xy0 & 0xFFFFu), y0 = static_cast<int>(xy0 >> 16);
+            const int x2 = x0 >> 2, y2 = y0 >> 2;
+            hit = ((y0 >> 3) * W3 + (x0 >> 3)) == cell && x2 >= ps.own_x0 && x2 < ps.own_x1 &&
+                  y2 >= ps.own_y0 && y2 < ps.own_y1;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        count += __popc(m);
+        if (m) last = j0 + hi_lane(m);
+    }
+    if (count == 0) return;
+    const int cols = 5 + a.g.ncls;
+    if (lane < cols) {
+        ps.preds_dec[static_cast<size_t>(cell) * cols + lane] = a.head_dec[static_cast<size_t>(last) * cols + lane];
+        ps.preds_raw[static_cast<size_t>(cell) * cols + lane] = a.head_raw[static_cast<size_t>(last) * cols + lane];
+    }
+    if (lane == 0) ps.version[cell] += static_cast<uint32_t>(count);
+}
+
+// Reset: prediction rows = head(0 feature) for every cell
+// (prepopulate_head_zero, ssla_kernels.cpp:969-989); raw rows and versions 0.
+__global__ void k_reset_preds(Geo g, const PartState* parts, DevHead hd) {
+    const int p = blockIdx.x;
+    const int n3 = g.W[3] * g.H[3];
+    const int cols = 5 + g.ncls;
+    const PartState ps = parts[p];
+    for (int cell = threadIdx.x; cell < n3; cell += blockDim.x) {
+        float cls_f[96], reg_f[96];
+        for (int j = 0; j < 96; ++j) {
+            float acc = hd.cls_conv_b[j];
+            float acc2 = hd.reg_conv_b[j];
+            for (int i = 0; i < 96; ++i) {
+                acc = fmaf(hd.cls_convT[i * 96 + j], 0.0f, acc);
+                acc2 = fmaf(hd.reg_convT[i * 96 + j], 0.0f, acc2);
+            }
+            cls_f[j] = acc * ssla_sigmoidf(acc);
+            reg_f[j] = acc2 * ssla_sigmoidf(acc2);
+        }
+        float res[21];
+        for (int r = 0; r < cols; ++r) {
+            float acc;
+            if (r < 4) {
+                acc = hd.reg_pred_b[r];
+                for (int i = 0; i < 96; ++i) acc = fmaf(hd.reg_predT[i * 4 + r], reg_f[i], acc);
+            } else if (r == 4) {
+                acc = hd.obj_pred_b[0];
+                for (int i = 0; i < 96; ++i) acc = fmaf(hd.obj_predT[i], reg_f[i], acc);
+            } else {
+                acc = hd.cls_pred_b[r - 5];
+                for (int i = 0; i < 96; ++i) acc = fmaf(hd.cls_predT[i * g.ncls + (r - 5)], cls_f[i], acc);
+            }
+            res[r] = acc;
+        }
+        const int gx = cell % g.W[3], gy = cell / g.W[3];
+        for (int r = 0; r < cols; ++r) {
+            float d;
+            if (r == 0) d = (res[0] + static_cast<float>(gx)) * static_cast<float>(g.stride_w);
+            else if (r == 1) d = (res[1] + static_cast<float>(gy)) * static_cast<float>(g.stride_h);
+            else if (r == 2) d = ssla_expf(res[2]) * static_cast<float>(g.stride_w);
+            else if (r == 3) d = ssla_expf(res[3]) * static_cast<float>(g.stride_h);
+            else d = res[r];
+            ps.preds_dec[static_cast<size_t>(cell) * cols + r] = d;
+            ps.preds_raw[static_cast<size_t>(cell) * cols + r] = 0.0f;
+        }
+        ps.version[cell] = 0u;
+    }
+}
+
+// drain_n output slots (ssla_s2_s3_head_celled.cuh:1066-1087): pass codes
+// 1 owner-passed / 0 owner-dropped / -1 halo, and the s3_feat slot as the
+// reference kernel leaves it.  outs: device array of per-block slot arrays.
+__global__ void k_write_slots(int n, int P, const int* __restrict__ rec_off,
+                              const uint8_t* __restrict__ rflags,
+                              const uint32_t* __restrict__ ev_xy,
+                              const PartState* __restrict__ parts,
+                              const float* __restrict__ slot_feat,
+                              HybridS2S3OutputSlot* const* outs) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        int p = 0;
+        while (p + 1 < P && i >= rec_off[p + 1]) ++p;
+        const PartState& ps = parts[p];
+        const uint32_t xy0 = ev_xy[i];
+        const int x2 = static_cast<int>(xy0 & 0xFFFFu) >> 2, y2 = static_cast<int>(xy0 >> 16) >> 2;
+        const bool owner = x2 >= ps.own_x0 && x2 < ps.own_x1 && y2 >= ps.own_y0 && y2 < ps.own_y1;
+        const uint8_t f = rflags[i];
+        const int p2 = (f & F_R3) ? 1 : 0;
+        const int p3 = (f & F_R4) ? 1 : 0;
+        if (outs[p] == nullptr) continue;
+        HybridS2S3OutputSlot* o = outs[p] + (i - rec_off[p]);
+        o->pass2 = owner ? p2 : -1;
+        o->pass3 = owner ? (p2 ? p3 : 0) : -1;
+        for (int c = 0; c < 96; ++c) o->s3_feat[c] = slot_feat[static_cast<size_t>(i) * 96 + c];
+    }
+}
+
+// drain_n timing words: every (t_pop, t_done) pair of a block's batch_clk
+// array gets the drain's start / end %globaltimer stamps.
+__global__ void k_fill_clk(int P, const int* __restrict__ rec_off,
+                           const unsigned long long* __restrict__ stamps,
+                           unsigned long long* const* clks) {
+    const int p = blockIdx.x;
+    if (clks[p] == nullptr) return;
+    const int nb = (rec_off[p + 1] - rec_off[p] + 7) / 8;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        clks[p][2 * b] = stamps[0];
+        clks[p][2 * b + 1] = stamps[1];
+    }
+}
+
+// Per-block timing words of the drain_n contract: global nanosecond timer.
+__global__ void k_stamp(unsigned long long* dst) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    *dst = t;
+}
+
+// ---------------------------------------------------------------------------
+// Explicit instantiations used by the engine.
+// ---------------------------------------------------------------------------
+template __global__ void k_scan<1, 12>(ScanArgs);
+template __global__ void k_scan<9, 12>(ScanArgs);
+template __global__ void k_scan<9, 24>(ScanArgs);
+template __global__ void k_scan<9, 48>(ScanArgs);
+template __global__ void k_scan<9, 96>(ScanArgs);
+
+template __global__ void k_event<1, 12, 9, 12, MODE_FIRST>(EventArgs);    // L0 -> L1
+template __global__ void k_event<9, 12, 9, 24, MODE_SECOND>(EventArgs);   // L1 -> L2
+template __global__ void k_event<9, 24, 9, 24, MODE_FIRST>(EventArgs);    // L2 -> L3
+template __global__ void k_event<9, 24, 9, 48, MODE_SECOND>(EventArgs);   // L3 -> L4
+template __global__ void k_event<9, 48, 9, 48, MODE_FIRST>(EventArgs);    // L4 -> L5
+template __global__ void k_event<9, 48, 9, 96, MODE_SECOND>(EventArgs);   // L5 -> L6
+template __global__ void k_event<9, 96, 9, 96, MODE_FIRST>(EventArgs);    // L6 -> L7
+template __global__ void k_event<9, 96, 1, 96, MODE_HEAD>(EventArgs);     // L7 -> head
+template __global__ void k_event<9, 96, 1, 96, MODE_LAST>(EventArgs);     // L7 (drain_n)
+template __global__ void k_event<1, 24, 9, 48, MODE_ENTRY>(EventArgs);    // record -> L4
+
+}  // namespace ssla
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+namespace ssla {
+
+namespace {
+__global__ void k_fill_f64(double* p, size_t n, double v) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        p[i] = v;
+}
+int grid_for(size_t n, int per_block, int cap = 148 * 16) {
+    const size_t g = (n + per_block - 1) / per_block;
+    return static_cast<int>(g < 1 ? 1 : (g > static_cast<size_t>(cap) ? cap : g));
+}
+}  // namespace
+
+void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
+                 uint32_t* ev_xy, uint8_t* rflags) {
+    if (n <= 0) return;
+    k_prep<<<grid_for(n, kNT), kNT, 0, st>>>(ev, n, W0, H0, ev_xy, rflags);
+}
+
+void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
+                         uint32_t* ev_xy, uint8_t* rflags, float* feat) {
+    if (n <= 0) return;
+    k_prep_records<<<grid_for(n, kNT), kNT, 0, st>>>(static_cast<const HybridInputRec*>(rec), n,
+                                                      E2, ev_xy, rflags, feat);
+}
+
+void launch_filter(cudaStream_t st, const FilterArgs& a, dim3 grid) {
+    k_filter<<<grid, kNT, 0, st>>>(a);
+}
+
+void launch_gates(cudaStream_t st, const GateArgs& a) {
+    k_gates<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), 32, 0, st>>>(a);
+}
+
+void launch_gates_s2(cudaStream_t st, const Gate2Args& a) {
+    k_gates_s2<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), 32, 0, st>>>(a);
+}
+
+void launch_compact(cudaStream_t st, const CompactArgs& a) {
+    const dim3 grid(a.g.P, a.tiles_per_part);
+    k_compact_count<<<grid, kNT, 0, st>>>(a);
+    k_compact_scan<<<1, kNT, 0, st>>>(a);
+    k_compact_scatter<<<grid, kNT, 0, st>>>(a);
+}
+
+void launch_scan(cudaStream_t st, int layer, const ScanArgs& a) {
+    const int s = layer / 2;
+    const dim3 grid(a.g.P, a.g.tx[s] * a.g.ty[s], (kTile * kTile) / (kNT / 32));
+    switch (layer) {
+        case 0: k_scan<1, 12><<<grid, kNT, 0, st>>>(a); break;
+        case 1: k_scan<9, 12><<<grid, kNT, 0, st>>>(a); break;
+        case 2: case 3: k_scan<9, 24><<<grid, kNT, 0, st>>>(a); break;
+        case 4: case 5: k_scan<9, 48><<<grid, kNT, 0, st>>>(a); break;
+        default: k_scan<9, 96><<<grid, kNT, 0, st>>>(a); break;
+    }
+}
+
+void launch_event(cudaStream_t st, int layer, int mode, const EventArgs& a, int grid) {
+    if (grid < 1) grid = 1;
+    if (mode == MODE_ENTRY) { k_event<1, 24, 9, 48, MODE_ENTRY><<<grid, kNT, 0, st>>>(a); return; }
+    switch (layer) {
+        case 0: k_event<1, 12, 9, 12, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
+        case 1: k_event<9, 12, 9, 24, MODE_SECOND><<<grid, kNT, 0, st>>>(a); break;
+        case 2: k_event<9, 24, 9, 24, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
+        case 3: k_event<9, 24, 9, 48, MODE_SECOND><<<grid, kNT, 0, st>>>(a); break;
+        case 4: k_event<9, 48, 9, 48, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
+        case 5: k_event<9, 48, 9, 96, MODE_SECOND><<<grid, kNT, 0, st>>>(a); break;
+        case 6: k_event<9, 96, 9, 96, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
+        default:
+            if (mode == MODE_HEAD) k_event<9, 96, 1, 96, MODE_HEAD><<<grid, kNT, 0, st>>>(a);
+            else k_event<9, 96, 1, 96, MODE_LAST><<<grid, kNT, 0, st>>>(a);
+            break;
+    }
+}
+
+void launch_commit(cudaStream_t st, const CommitArgs& a) {
+    const int n3 = a.g.W[3] * a.g.H[3];
+    k_commit<<<dim3(a.g.P, (n3 + 7) / 8), kNT, 0, st>>>(a);
+}
+
+void launch_reset_preds(cudaStream_t st, const Geo& g, const PartState* parts, const DevHead& hd) {
+    k_reset_preds<<<g.P, 128, 0, st>>>(g, parts, hd);
+}
+
+void launch_fill_f64(cudaStream_t st, double* p, size_t n, double v) {
+    if (n == 0) return;
+    k_fill_f64<<<grid_for(n, kNT), kNT, 0, st>>>(p, n, v);
+}
+
+void launch_write_slots(cudaStream_t st, int n, int P, const int* rec_off, const uint8_t* rflags,
+                        const uint32_t* ev_xy, const PartState* parts, const float* slot_feat,
+                        void* const* outs) {
+    if (n <= 0) return;
+    k_write_slots<<<grid_for(n, kNT), kNT, 0, st>>>(n, P, rec_off, rflags, ev_xy, parts, slot_feat,
+                                                     reinterpret_cast<HybridS2S3OutputSlot* const*>(outs));
+}
+
+void launch_fill_clk(cudaStream_t st, int P, const int* rec_off, const unsigned long long* stamps,
+                     unsigned long long* const* clks) {
+    k_fill_clk<<<P, kNT, 0, st>>>(P, rec_off, stamps, clks);
+}
+
+void launch_stamp(cudaStream_t st, unsigned long long* dst) { k_stamp<<<1, 1, 0, st>>>(dst); }
+
+}  // namespace ssla

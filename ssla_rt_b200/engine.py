@@ -1,0 +1,202 @@
+"""Python host mirror of the C ABI (include/ssla_b200.h).
+
+``SslaEngine`` plays the role of the reference's host objects for this path:
+``deploy::SslaSPipeline`` (load / reset / per-event step, single stream,
+src/ssla_kernels.cpp) and the ``s01g_*`` library (many shard streams,
+src/lib_stage01_to_gpu.cpp), with all the per-event math on the GPU.
+``drain_n_multi`` is the reference's P1 ``k_ssla_s2s3_celled_drain_n_multi``
+contract.  There is no CPU fallback: loading fails loudly without the built
+library or a CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import abi
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libssla_b200.so")
+_lib = None
+
+
+class SslaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ssla error {code}: {msg}")
+        self.code = code
+
+
+def load_library() -> C.CDLL:
+    """Load libssla_b200.so (built by ssla_rt_b200/build.py); raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} missing: build it with `python ssla_rt_b200/build.py`")
+    lib = C.CDLL(LIB_PATH)
+    vp, i, f = C.c_void_p, C.c_int, C.c_float
+    sig = {
+        "ssla_engine_create": (i, [C.c_char_p, C.POINTER(abi.SslaEngineConfig), C.POINTER(vp)]),
+        "ssla_engine_destroy": (None, [vp]),
+        "ssla_engine_reset": (i, [vp, vp]),
+        "ssla_engine_drain_device": (i, [vp, vp, vp, vp, vp]),
+        "ssla_engine_drain_host": (i, [vp, vp, vp, vp, vp]),
+        "ssla_engine_state_bytes": (i, [vp, i, i, C.POINTER(C.c_size_t)]),
+        "ssla_engine_read_state": (i, [vp, i, i, i, vp, C.c_size_t]),
+        "ssla_engine_write_state": (i, [vp, i, i, i, vp, C.c_size_t]),
+        "ssla_engine_state_ptr": (vp, [vp, i, i, i]),
+        "ssla_engine_info": (i, [vp, C.POINTER(abi.SslaEngineInfo)]),
+        "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
+        "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
+        "ssla_expf_host": (f, [f]),
+        "ssla_last_error": (C.c_char_p, []),
+        "ssla_version": (C.c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc != abi.SSLA_OK:
+        raise SslaError(rc, load_library().ssla_last_error().decode())
+
+
+def _ptr(x) -> Optional[int]:
+    """Address of a numpy array or a torch tensor (None passes through)."""
+    if x is None:
+        return None
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    return int(x)
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        return None
+    if hasattr(stream, "cuda_stream"):
+        return stream.cuda_stream
+    return int(stream)
+
+
+class SslaEngine:
+    """One model, ``n_partitions`` independent event streams on one GPU."""
+
+    CHANS = (12, 24, 48, 96)
+
+    def __init__(self, weights_dir: str, *, n_partitions: int = 1, max_events: int = 65536,
+                 layout: int = abi.LAYOUT_HYBRID, device: int = 0,
+                 record_stage_outputs: bool = False, max_events_per_partition: int = 0):
+        self.lib = load_library()
+        cfg = abi.SslaEngineConfig(n_partitions, max_events, layout, device,
+                                   1 if record_stage_outputs else 0, max_events_per_partition)
+        h = C.c_void_p()
+        _check(self.lib.ssla_engine_create(weights_dir.encode(), C.byref(cfg), C.byref(h)))
+        self.h = h
+        info = self.info()
+        self.H, self.W, self.ncls = info.H, info.W, info.ncls
+        self.n_partitions, self.max_events, self.layout = n_partitions, max_events, layout
+        self.device = device
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.ssla_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> abi.SslaEngineInfo:
+        inf = abi.SslaEngineInfo()
+        _check(self.lib.ssla_engine_info(self.h, C.byref(inf)))
+        return inf
+
+    def reset(self, stream=None) -> None:
+        _check(self.lib.ssla_engine_reset(self.h, _stream(stream)))
+
+    @staticmethod
+    def offsets(counts: Sequence[int]) -> np.ndarray:
+        return np.concatenate([[0], np.cumsum(np.asarray(counts, dtype=np.int64))]).astype(np.int32)
+
+    def drain(self, events, part_offsets, flags=None, stream=None) -> None:
+        """Device path: ``events`` a CUDA tensor (n, 4) float32, ``flags`` an
+        optional CUDA uint8 tensor (n,); asynchronous on ``stream``."""
+        off = np.ascontiguousarray(part_offsets, dtype=np.int32)
+        _check(self.lib.ssla_engine_drain_device(self.h, _ptr(events), off.ctypes.data,
+                                                 _ptr(flags), _stream(stream)))
+
+    def drain_host(self, events: np.ndarray, part_offsets, flags: Optional[np.ndarray] = None,
+                   stream=None) -> None:
+        """Host path: copies in, drains, copies flags out, synchronises."""
+        off = np.ascontiguousarray(part_offsets, dtype=np.int32)
+        _check(self.lib.ssla_engine_drain_host(self.h, _ptr(events), off.ctypes.data,
+                                               _ptr(flags), _stream(stream)))
+
+    def _read(self, kind: int, partition: int, index: int, dtype) -> np.ndarray:
+        nb = C.c_size_t()
+        _check(self.lib.ssla_engine_state_bytes(self.h, kind, index, C.byref(nb)))
+        out = np.empty(nb.value // np.dtype(dtype).itemsize, dtype=dtype)
+        _check(self.lib.ssla_engine_read_state(self.h, kind, partition, index, out.ctypes.data, nb.value))
+        return out
+
+    def _write(self, kind: int, partition: int, index: int, values: np.ndarray) -> None:
+        v = np.ascontiguousarray(values)
+        _check(self.lib.ssla_engine_write_state(self.h, kind, partition, index, v.ctypes.data, v.nbytes))
+
+    def hidden(self, layer: int, partition: int = 0) -> np.ndarray:
+        return self._read(abi.STATE_HIDDEN, partition, layer, np.float32)
+
+    def set_hidden(self, layer: int, values: np.ndarray, partition: int = 0) -> None:
+        self._write(abi.STATE_HIDDEN, partition, layer, np.asarray(values, np.float32))
+
+    def counters(self, gate: int, partition: int = 0) -> np.ndarray:
+        return self._read(abi.STATE_COUNTER, partition, gate, np.uint8)
+
+    def last_t(self, partition: int = 0) -> np.ndarray:
+        return self._read(abi.STATE_LAST_T, partition, 0, np.float64)
+
+    def preds_dec(self, partition: int = 0) -> np.ndarray:
+        return self._read(abi.STATE_PREDS_DEC, partition, 0, np.float32).reshape(-1, 5 + self.ncls)
+
+    def preds_raw(self, partition: int = 0) -> np.ndarray:
+        return self._read(abi.STATE_PREDS_RAW, partition, 0, np.float32).reshape(-1, 5 + self.ncls)
+
+    def version(self, partition: int = 0) -> np.ndarray:
+        return self._read(abi.STATE_VERSION, partition, 0, np.uint32)
+
+    def stage_out(self, stage: int, n: int) -> np.ndarray:
+        a = self._read(abi.STATE_STAGE_OUT, 0, stage, np.float32)
+        return a.reshape(-1, self.CHANS[stage])[:n]
+
+    def flags(self, n: int) -> np.ndarray:
+        return self._read(abi.STATE_FLAGS, 0, 0, np.uint8)[:n]
+
+    def state_ptr(self, kind: int, partition: int = 0, index: int = 0) -> int:
+        return self.lib.ssla_engine_state_ptr(self.h, kind, partition, index) or 0
+
+
+def drain_n_multi(cfg: abi.HybridS2S3Config, rings: Sequence[int], ns: Sequence[int],
+                  outs: Optional[Sequence[int]] = None, batch_clks: Optional[Sequence[int]] = None,
+                  stream=None) -> None:
+    """k_ssla_s2s3_celled_drain_n_multi contract; device pointers as ints."""
+    lib = load_library()
+    P = len(rings)
+    r = (C.c_void_p * P)(*rings)
+    n = (C.c_int * P)(*ns)
+    o = (C.c_void_p * P)(*outs) if outs is not None else None
+    k = (C.c_void_p * P)(*batch_clks) if batch_clks is not None else None
+    _check(lib.ssla_s2s3_drain_n_multi(C.byref(cfg), C.cast(r, C.c_void_p), C.cast(n, C.c_void_p),
+                                       C.cast(o, C.c_void_p) if o is not None else None,
+                                       C.cast(k, C.c_void_p) if k is not None else None,
+                                       _stream(stream)))
