@@ -1,0 +1,393 @@
+#!/usr/bin/env python
+"""Benchmark of the SSLA-S per-event hot path on B200 (one JSON line).
+
+Workload: 200,000 uniform synthetic events at 80x64
+(x ~ U{0..79}, y ~ U{0..63}, polarity +-1, Poisson 2 Mev/s timestamps, seed
+1), split into 8 ring partitions of 25,000 events -- each an independent
+event stream, as the reference's throughput harness splits its events over
+independent blocks (orin/perf_celled_multi.py:179-190).  Stub weights
+(tools/make_ssla_stub.py schema, seed 1, tdrop 4), production gate layout
+(CPU gates at s1/s2 + GPU tdrop_s2/tdrop_s3).  A step drains all 200,000
+events through s0..s3 and the head; the streams continue from step to step
+(timestamps advance, state persists).
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+value  = events drained / device time (CUDA events), max over ranks, L2
+         flushed between steps (untimed)
+e2e    = same metric through ssla_engine_drain_host (pinned host events in,
+         flags + predictions out, host<->device copies inside the timing)
+N > 1  = one rank per GPU (torchrun), each drains its own 200k-event set
+         (weak scaling, no collective on the data path).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "Mev/s drained (output events) at 1/2/4/8 B200; p50/p99 emit→prediction µs"
+N_EVENTS = 200_000
+N_PARTS = 8
+H, W = 64, 80
+CHANS = (12, 24, 48, 96)
+LAYER_DIMS = ((2, 12, 1), (12, 12, 9), (12, 24, 9), (24, 24, 9), (24, 48, 9), (48, 48, 9),
+              (48, 96, 9), (96, 96, 9))
+
+
+def workload(rank: int):
+    from ssla_rt_b200 import events
+    ev = events.config_events(1, seed=1 + 1000 * rank)
+    return events.split_partitions(ev, N_PARTS)
+
+
+# ---------------------------------------------------------------------------
+# Algorithmic work (exact, from the drain's gate flags and event coordinates)
+# ---------------------------------------------------------------------------
+def patches(coords_xy: np.ndarray, s: int) -> np.ndarray:
+    """In-bounds 3x3 patch positions per event at stage s."""
+    x = coords_xy[:, 0].astype(np.int64) >> s
+    y = coords_xy[:, 1].astype(np.int64) >> s
+    ws, hs = W >> s, H >> s
+    nx = 1 + (x > 0) + (x < ws - 1)
+    ny = 1 + (y > 0) + (y < hs - 1)
+    return nx * ny
+
+
+def algorithmic_macs(ev: np.ndarray, flags: np.ndarray) -> dict:
+    """MACs per layer split as qvg / gather / residual (survey 8(d) model
+    with exact in-bounds patch counts), plus the head."""
+    from ssla_rt_b200 import abi
+    xy = ev[:, 1:3]
+    valid = (flags & abi.F_VALID) != 0
+    reach = [valid] + [(flags & b) != 0 for b in (abi.F_R1, abi.F_R2, abi.F_R3, abi.F_R4)]
+    out = {}
+    for l, (IN, OUT, A) in enumerate(LAYER_DIMS):
+        s = l // 2
+        ent = reach[s]
+        np_ = patches(xy[ent], s) if A == 9 else np.ones(int(ent.sum()), np.int64)
+        outn = reach[s + 1][ent] if l % 2 == 1 else np.ones(int(ent.sum()), bool)
+        qvg = int((np_ * np.where(outn, 3, 2)).sum()) * OUT * IN
+        gather = int(np_[outn].sum()) * OUT * OUT
+        resid = int(outn.sum()) * IN * OUT if IN != OUT else 0
+        out[l] = {"qvg": qvg, "gather": gather, "resid": resid}
+    out["head"] = int(reach[4].sum()) * (2 * 96 * 96 + 7 * 96)
+    return out
+
+
+def phase_flops(macs: dict, name: str) -> float:
+    """Algorithmic FLOPs of one engine phase (2 per MAC)."""
+    if name.startswith("event_L"):
+        l = int(name[7])
+        m = macs[l]["gather"]
+        if l < 7:
+            m += macs[l + 1]["qvg"] + macs[l + 1]["resid"]
+        else:
+            m += macs["head"]
+        if l == 0:
+            m += 0
+        return 2.0 * m
+    return 0.0
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, device_index: int) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [c.strip() for c in line.split(",")]
+            if len(f) >= 9 and f[0].isdigit():
+                rows.append(f)
+        os.unlink(self.path)
+        mine = [r for r in rows if int(r[0]) == device_index] or rows
+        sm = [float(r[1]) for r in mine if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in mine for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(mine)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own SslaSPipeline (oracle/_ref), else the
+# C restatement (oracle/), same 8 independent streams, host threads.
+# ---------------------------------------------------------------------------
+def cpu_baseline(parts, weights_dir: str, reps: int = 3) -> dict:
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    threads = min(len(parts), os.cpu_count() or 1)
+    n = sum(len(p) for p in parts)
+    if os.path.exists(O.REF_SO):
+        ref = O.RefPipeline(weights_dir, O.LAYOUT_HYBRID)
+        best = min(ref.time_streams(parts, threads) for _ in range(reps))
+        kind = "reference"
+    else:
+        import concurrent.futures as cf
+        def one(p):
+            orc = O.Oracle(O.load_npz(weights_dir), H, W, 4, O.LAYOUT_HYBRID)
+            orc.run_events(p, want_stage_out=False)
+        t0 = time.perf_counter()
+        with cf.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(one, parts))
+        best = time.perf_counter() - t0
+        kind = "port"
+    return {"value": n / best / 1e6, "unit": "Mev/s", "cores": threads, "kind": kind,
+            "sample": f"the full step workload: {len(parts)} independent streams x "
+                      f"{len(parts[0])} events, one host thread per stream, best of {reps}"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    from ssla_rt_b200 import stub
+    with tempfile.TemporaryDirectory() as d:
+        stub.write_stub(d, h=H, w=W, seed=1, tdrop=4)
+        parts = workload(0)
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle as O
+        threads = min(len(parts), os.cpu_count() or 1)
+        kind = "reference" if os.path.exists(O.REF_SO) else "port"
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            if kind == "reference":
+                dt = O.RefPipeline(d, O.LAYOUT_HYBRID).time_streams(parts, threads)
+            else:
+                dt = cpu_baseline(parts, d, reps=1)["value"]
+                dt = N_EVENTS / (dt * 1e6)
+            if i >= args.warmup:
+                times.append(dt)
+        total = sum(times)
+        value = N_EVENTS * args.steps / total / 1e6
+        line = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "Mev/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(),
+            "cpu_baseline": {"value": value, "unit": "Mev/s", "cores": threads, "kind": kind,
+                             "sample": f"{N_PARTS} independent streams x {N_EVENTS // N_PARTS} events "
+                                       f"per step, one host thread per stream"},
+            "e2e": {"value": value, "unit": "Mev/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+
+
+def config_dict() -> dict:
+    return {"workload": "config1: 200,000 uniform events at 80x64 in 8 ring partitions of 25,000 "
+                        "(independent streams), full s0..s3 + YOLOX head",
+            "model": "SSLA-S stub (tools/make_ssla_stub.py schema, seed 1, tdrop 4)",
+            "events_per_step": N_EVENTS, "partitions": N_PARTS, "sensor": "80x64",
+            "gate_layout": "hybrid (lib_stage01_to_gpu + celled kernel)",
+            "l2": "flushed between steps (256 MiB write, untimed)",
+            "parallelism": "per-GPU independent partitions"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from ssla_rt_b200 import abi, stub
+    from ssla_rt_b200.engine import SslaEngine, measure_fp32_peak
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+    wdir = tempfile.mkdtemp(prefix="ssla_stub_")
+    stub.write_stub(wdir, h=H, w=W, seed=1, tdrop=4)
+    parts = workload(rank)
+    ev_np = np.ascontiguousarray(np.concatenate(parts))
+    counts = [len(p) for p in parts]
+    eng = SslaEngine(wdir, n_partitions=N_PARTS, max_events=N_EVENTS, layout=abi.LAYOUT_HYBRID,
+                     device=local, max_events_per_partition=max(counts))
+    off = eng.offsets(counts)
+    ev = torch.from_numpy(ev_np).to(dev)
+    span = float(ev_np[:, 0].max()) + 1.0
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)   # 256 MiB
+    stream = torch.cuda.current_stream(dev)
+    step_no = [0]
+
+    def advance():
+        # the streams continue: next batch of events later in time
+        step_no[0] += 1
+        ev[:, 0] += span
+
+    def flush_l2():
+        flush.fill_(float(step_no[0]))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- warm-up ----
+    for _ in range(args.warmup):
+        advance()
+        eng.drain(ev, off, stream=stream)
+    torch.cuda.synchronize(dev)
+
+    # ---- timed: K device-timed drains, per-phase events on ----
+    eng.set_profiling(True)
+    phase_acc = {}
+    step_ms = []
+    clocks = ClockSampler()
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    for _ in range(args.steps):
+        advance()
+        flush_l2()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        eng.drain(ev, off, stream=stream)
+        b.record(stream)
+        b.synchronize()
+        step_ms.append(a.elapsed_time(b))
+        for name, ms, nl in eng.phase_times():
+            acc = phase_acc.setdefault(name, [0.0, 0, 0])
+            acc[0] += ms
+            acc[1] += 1
+            acc[2] += nl
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop(local)
+    eng.set_profiling(False)
+    launches = eng.info().launches * args.steps
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * N_EVENTS * args.steps / (total_ms * 1e-3) / 1e6
+
+    # ---- e2e through the host C-ABI path (pinned host events) ----
+    pinned = ev.cpu().pin_memory()        # continue from the device stream's timestamps
+    host_ev = pinned.numpy()
+    host_flags = torch.empty(N_EVENTS, dtype=torch.uint8).pin_memory().numpy()
+    e2e_s = []
+    for i in range(args.warmup + args.steps):
+        host_ev[:, 0] += span
+        flush_l2()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        eng.drain_host(host_ev, off, host_flags, stream=stream)
+        preds = [eng.preds_dec(p) for p in range(N_PARTS)]
+        t1 = time.perf_counter()
+        if i >= args.warmup:
+            e2e_s.append(t1 - t0)
+    e2e_total = sum(e2e_s)
+    if world > 1:
+        t = torch.tensor([e2e_total], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e = world * N_EVENTS * args.steps / e2e_total / 1e6
+    d2h = N_EVENTS + sum(p.nbytes for p in preds)
+
+    # ---- roofline of the dominant phase (live CUDA-event durations) ----
+    flags_dev = torch.zeros(N_EVENTS, dtype=torch.uint8, device=dev)
+    eng.drain(ev, off, flags=flags_dev, stream=stream)
+    flags = flags_dev.cpu().numpy()
+    macs = algorithmic_macs(ev_np, flags)
+    total_macs = sum(v["qvg"] + v["gather"] + v["resid"] for k, v in macs.items() if k != "head") + macs["head"]
+    dom = max(phase_acc.items(), key=lambda kv: kv[1][0])
+    dom_name, (dom_ms_sum, dom_n, _) = dom
+    dom_ms = dom_ms_sum / dom_n
+    fp32_peak = measure_fp32_peak(local)
+    dflops = phase_flops(macs, dom_name)
+    achieved = dflops / (dom_ms * 1e-3) / 1e12 if dflops > 0 else None
+    roofline = {
+        "kernel": dom_name, "bound": "fp32",
+        "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+        "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
+        "traffic": None,
+        "peak_source": "measured FFMA peak (ssla_measure_fp32_peak, this run); the path is FP32 "
+                       "CUDA-core work, MEASURED_PEAKS.json holds only HBM and bf16 tensor peaks",
+        "avg_ms": dom_ms, "algorithmic_flops_per_launch": dflops,
+        "share_of_step": dom_ms_sum / total_ms if world == 1 else None,
+    }
+    phases = {k: round(v[0] / v[1], 4) for k, v in sorted(phase_acc.items(), key=lambda kv: -kv[1][0])}
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(parts, wdir)
+        line = {
+            "metric": METRIC, "value": value, "unit": "Mev/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": config_dict(), "clocks": clk,
+            "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(ev_np.nbytes),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
+            "algorithmic_mac_per_event": total_macs / N_EVENTS,
+            "stage_events": [int(x) for x in eng.info().stage_events],
+            "phase_ms": phases,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -62,7 +62,16 @@ typedef struct {
     int H, W, ncls, tdrop_window, layout, n_partitions, max_events;
     int device;
     long long stage_events[5]; /* last drain: events entering s0..s3 / head   */
+    int launches;              /* kernels the last drain launched              */
+    int _pad;
 } SslaEngineInfo;
+
+/* One timed phase of a profiled drain (a kernel or a short kernel group). */
+typedef struct {
+    char  name[40];
+    float ms;
+    int   launches;
+} SslaPhaseTime;
 
 /* State buffers readable / writable per partition. `index` is the layer
  * (HIDDEN), gate (COUNTER) or stage (STAGE_OUT). STAGE_OUT and FLAGS cover
@@ -142,6 +151,18 @@ int  ssla_s2s3_drain_n(const HybridS2S3Config* cfg,
                        HybridS2S3OutputSlot* out0, HybridS2S3OutputSlot* out1,
                        unsigned long long* batch_clk0,
                        unsigned long long* batch_clk1, void* stream);
+
+/* Per-phase timing (the analogue of the reference's clock64 phase stamps,
+ * orin/kernels/ssla_s2_s3_head_celled_profile.cuh:17-40): when enabled,
+ * every drain records a CUDA event after each phase on its stream;
+ * ssla_engine_phase_times synchronises and returns the elapsed times of the
+ * last drain's phases in launch order. */
+int  ssla_engine_set_profiling(SslaEngine* eng, int enable);
+int  ssla_engine_phase_times(SslaEngine* eng, SslaPhaseTime* out, int max_n, int* n_out);
+
+/* FP32 FMA-pipe peak of `device`, measured with a dependent-chain-free FFMA
+ * loop over every SM (the denominator of the engine's roofline). */
+int  ssla_measure_fp32_peak(int device, double* tflops_out);
 
 /* Portable exp used by every sigmoid / SiLU / box decode of the engine
  * (the device code's exact twin), for tests on hosts without a GPU. */

@@ -69,7 +69,12 @@ class SslaEngineConfig(C.Structure):
 class SslaEngineInfo(C.Structure):
     _fields_ = [("H", C.c_int), ("W", C.c_int), ("ncls", C.c_int), ("tdrop_window", C.c_int),
                 ("layout", C.c_int), ("n_partitions", C.c_int), ("max_events", C.c_int),
-                ("device", C.c_int), ("stage_events", C.c_longlong * 5)]
+                ("device", C.c_int), ("stage_events", C.c_longlong * 5),
+                ("launches", C.c_int), ("_pad", C.c_int)]
+
+
+class SslaPhaseTime(C.Structure):
+    _fields_ = [("name", C.c_char * 40), ("ms", C.c_float), ("launches", C.c_int)]
 
 
 SSLA_OK, SSLA_ERR_ARG, SSLA_ERR_CUDA, SSLA_ERR_LOAD, SSLA_ERR_CAPACITY, SSLA_ERR_NO_DEVICE = range(6)
@@ -84,5 +89,6 @@ EXPORTED = (
     "ssla_engine_drain_device", "ssla_engine_drain_host", "ssla_engine_state_bytes",
     "ssla_engine_read_state", "ssla_engine_write_state", "ssla_engine_state_ptr",
     "ssla_engine_info", "ssla_s2s3_drain_n_multi", "ssla_s2s3_drain_n",
+    "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak",
     "ssla_expf_host", "ssla_last_error", "ssla_version",
 )

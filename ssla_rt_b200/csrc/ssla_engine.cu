@@ -42,6 +42,42 @@ void check_launch(const char* what) {
     if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Optional per-phase timing: one CUDA event after each phase of a drain.
+struct Prof {
+    bool on = false;
+    std::vector<cudaEvent_t> ev;
+    std::vector<std::string> names;
+    std::vector<int> nl;
+    int used = 0;
+    int launches = 0;
+    ~Prof() {
+        for (auto e : ev) cudaEventDestroy(e);
+    }
+    void begin(cudaStream_t st) {
+        used = 0;
+        launches = 0;
+        names.clear();
+        nl.clear();
+        if (on) record(st);
+    }
+    void record(cudaStream_t st) {
+        if (used == static_cast<int>(ev.size())) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) throw std::runtime_error("cudaEventCreate failed");
+            ev.push_back(e);
+        }
+        if (cudaEventRecord(ev[used], st) != cudaSuccess) throw std::runtime_error("cudaEventRecord failed");
+        ++used;
+    }
+    void mark(const char* name, int n_launch, cudaStream_t st) {
+        launches += n_launch;
+        if (!on) return;
+        names.emplace_back(name);
+        nl.push_back(n_launch);
+        record(st);
+    }
+};
+
 struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int dev) {
@@ -135,6 +171,12 @@ struct Workspace {
         cap_part[s_first] = mpe;
         cap[s_first] = n_max;
         for (int s = s_first; s < 4; ++s) {
+            // DECOMP has no gate after stage 3: every stage-3 event reaches the head.
+            if (s == 3 && g.layout != LAYOUT_HYBRID) {
+                cap_part[4] = cap_part[3];
+                cap[4] = cap[3];
+                break;
+            }
             const int cg = cells(g, host_gate_grid(g.layout, s));
             cap_part[s + 1] = gate_bound(cap_part[s], cg, g.window);
             cap[s + 1] = std::min(cap[s], gate_bound(cap[s], cg * P, g.window));
@@ -188,7 +230,11 @@ struct Workspace {
 // Enqueues stages s_first..3 (layers 2*s_first..7) for a planned workspace.
 // rec_off / E_2 / feat must be prepared by the caller for s_first == 2.
 void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_parts,
-                const DevLayer* L, const DevHead* head, bool do_head, bool record) {
+                const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof) {
+    static const char* kScanNames[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
+                                        "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
+    static const char* kEventNames[8] = {"event_L0", "event_L1", "event_L2", "event_L3",
+                                         "event_L4", "event_L5", "event_L6", "event_L7_head"};
     const int* d_count = w.count.as<int>();
     for (int s = w.s_first; s < 4; ++s) {
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
@@ -206,6 +252,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             sa.S = S_in; sa.parts = d_parts; sa.rflags = w.rflags.as<uint8_t>(); sa.second = half;
             launch_scan(st, l, sa);
             check_launch("k_scan");
+            prof.mark(kScanNames[l], 1, st);
 
             EventArgs ea{};
             ea.g = g; ea.stage = s; ea.count = d_count;
@@ -234,6 +281,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             const int grid = static_cast<int>(std::min<long long>((n_cap + kMB - 1) / kMB, 148LL * 8));
             launch_event(st, l, mode, ea, grid);
             check_launch("k_event");
+            prof.mark(kEventNames[l], 1, st);
         }
     }
 }
@@ -258,6 +306,7 @@ struct Engine {
     DevBuf hidden[8], cnt[4], last_t, preds_dec, preds_raw, version, parts;
     std::vector<PartState> h_parts;
     Workspace ws;
+    Prof prof;
     int* pinned_off = nullptr;
     long long last_counts[5] = {0};
     int last_n = 0;
@@ -376,26 +425,29 @@ struct Engine {
         DeviceGuard dg(device);
         const int P = g.P;
         if (off[0] != 0) throw std::invalid_argument("part_offsets[0] must be 0");
-        for (int p = 0; p < P; ++p) {
-            const int n_p = off[p + 1] - off[p];
-            if (n_p < 0) throw std::invalid_argument("part_offsets must be non-decreasing");
-            if (n_p > mpe) throw std::length_error("partition holds more events than max_events_per_partition");
-        }
+        for (int p = 0; p < P; ++p)
+            if (off[p + 1] < off[p]) throw std::invalid_argument("part_offsets must be non-decreasing");
+        for (int p = 0; p < P; ++p)
+            if (off[p + 1] - off[p] > mpe)
+                throw std::length_error("partition holds more events than max_events_per_partition");
         const int n = off[P];
         if (n > max_events) throw std::length_error("more events than max_events");
         ws.n_active = n;
         last_n = n;
+        prof.begin(st);
         std::memcpy(pinned_off, off, sizeof(int) * (P + 1));
         SSLA_CK(cudaMemcpyAsync(ws.ev_off.p, pinned_off, sizeof(int) * (P + 1), cudaMemcpyHostToDevice, st));
         const float4* ev = reinterpret_cast<const float4*>(ev_dev);
         launch_prep(st, ev, n, g.W[0], g.H[0], ws.ev_xy.as<uint32_t>(), ws.rflags.as<uint8_t>());
         check_launch("k_prep");
+        prof.mark("prep", n > 0 ? 1 : 0, st);
         // stage-0 tile lists
         FilterArgs fa{};
         fa.g = g; fa.stage = 0; fa.ev_xy = ws.ev_xy.as<uint32_t>(); fa.rflags = ws.rflags.as<uint8_t>();
         fa.range = ws.ev_off.as<int>(); fa.tl = ws.tl[0].as<int2>(); fa.tl_cnt = ws.tl_cnt[0].as<int>();
         launch_filter(st, fa, dim3(P, g.tx[0] * g.ty[0], g.nseg[0]));
         check_launch("k_filter s0");
+        prof.mark("filter_s0", 1, st);
         // gates + preprocess + layer-0 qvg
         GateArgs ga{};
         ga.g = g; ga.ev = ev; ga.ev_off = ws.ev_off.as<int>(); ga.tl0 = ws.tl[0].as<int2>();
@@ -404,6 +456,7 @@ struct Engine {
         ga.L0 = L[0];
         launch_gates(st, ga);
         check_launch("k_gates");
+        prof.mark("gates", 1, st);
         // stage lists
         CompactArgs ca{};
         ca.g = g; ca.s_first = 0; ca.tiles_per_part = ws.tiles_per_part; ca.ev_off = ws.ev_off.as<int>();
@@ -413,6 +466,7 @@ struct Engine {
         ca.count = ws.count.as<int>();
         launch_compact(st, ca);
         check_launch("k_compact");
+        prof.mark("compact", 3, st);
         for (int s = 1; s < 4; ++s) {
             FilterArgs f{};
             f.g = g; f.stage = s; f.E = ws.E[s].as<StageEntry>(); f.rflags = ws.rflags.as<uint8_t>();
@@ -421,13 +475,15 @@ struct Engine {
             launch_filter(st, f, dim3(P, g.tx[s] * g.ty[s], g.nseg[s]));
             check_launch("k_filter");
         }
-        run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record);
+        prof.mark("filter_s123", 3, st);
+        run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record, prof);
         CommitArgs cm{};
         cm.g = g; cm.E4 = ws.E[4].as<StageEntry>(); cm.off4 = ws.off[4].as<int>();
         cm.head_dec = ws.head_dec.as<float>(); cm.head_raw = ws.head_raw.as<float>();
         cm.parts = parts.as<PartState>();
         launch_commit(st, cm);
         check_launch("k_commit");
+        prof.mark("commit", 1, st);
         if (flags_dev && n > 0)
             SSLA_CK(cudaMemcpyAsync(flags_dev, ws.rflags.p, n, cudaMemcpyDeviceToDevice, st));
     }
@@ -569,7 +625,8 @@ struct DrainN {
         launch_event(st, 4, MODE_ENTRY, ea, static_cast<int>(std::min<long long>((n + kMB - 1) / kMB, 148LL * 8)));
         check_launch("k_event entry");
         DevHead nohead{};
-        run_layers(st, g, w, d.parts.as<PartState>(), L, &nohead, false, false);
+        Prof noprof;
+        run_layers(st, g, w, d.parts.as<PartState>(), L, &nohead, false, false, noprof);
         if (outs) {
             launch_write_slots(st, n, P, w.ev_off.as<int>(), w.rflags.as<uint8_t>(), w.ev_xy.as<uint32_t>(),
                                d.parts.as<PartState>(), w.slot_feat.as<float>(), d.outs.as<void*>());
@@ -767,7 +824,46 @@ int ssla_engine_info(SslaEngine* eng, SslaEngineInfo* info) {
         SSLA_CK(cudaDeviceSynchronize());
         SSLA_CK(cudaMemcpy(cnt, e.ws.count.p, sizeof cnt, cudaMemcpyDeviceToHost));
         info->stage_events[0] = e.last_n;
+        info->launches = e.prof.launches;
         for (int s = 1; s < 5; ++s) info->stage_events[s] = cnt[s];
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_set_profiling(SslaEngine* eng, int enable) {
+    if (!eng) { ssla::g_last_error = "null engine"; return SSLA_ERR_ARG; }
+    eng->e.prof.on = enable != 0;
+    return SSLA_OK;
+}
+
+int ssla_engine_phase_times(SslaEngine* eng, SslaPhaseTime* out, int max_n, int* n_out) {
+    if (!eng || !out || !n_out) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        ssla::Prof& p = e.prof;
+        const int n = std::min<int>(static_cast<int>(p.names.size()), max_n);
+        *n_out = 0;
+        if (!p.on || p.used < 2) return SSLA_OK;
+        SSLA_CK(cudaEventSynchronize(p.ev[p.used - 1]));
+        for (int i = 0; i < n; ++i) {
+            float ms = 0.0f;
+            SSLA_CK(cudaEventElapsedTime(&ms, p.ev[i], p.ev[i + 1]));
+            std::memset(out[i].name, 0, sizeof out[i].name);
+            std::strncpy(out[i].name, p.names[i].c_str(), sizeof out[i].name - 1);
+            out[i].ms = ms;
+            out[i].launches = p.nl[i];
+        }
+        *n_out = n;
+        return SSLA_OK;
+    });
+}
+
+int ssla_measure_fp32_peak(int device, double* tflops_out) {
+    if (!tflops_out) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(device);
+        *tflops_out = ssla::measure_ffma_peak();
         return SSLA_OK;
     });
 }

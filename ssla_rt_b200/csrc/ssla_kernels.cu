@@ -16,6 +16,8 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "ssla_abi_types.h"
 
 namespace ssla {
@@ -1092,5 +1094,54 @@ void launch_fill_clk(cudaStream_t st, int P, const int* rec_off, const unsigned 
 }
 
 void launch_stamp(cudaStream_t st, unsigned long long* dst) { k_stamp<<<1, 1, 0, st>>>(dst); }
+
+namespace {
+// 8 independent FFMA chains per thread; a and b come from memory so nothing
+// folds, the result is stored only under a never-true runtime condition.
+__global__ void __launch_bounds__(512) k_ffma_peak(const float* __restrict__ ab, int iters, float* sink) {
+    const float a = ab[0], b = ab[1];
+    float r[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[k] = static_cast<float>(threadIdx.x + k);
+    for (int i = 0; i < iters; ++i) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r[k] = fmaf(r[k], a, b);
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += r[k];
+    if (s == 123456.789f) sink[threadIdx.x] = s;
+}
+}  // namespace
+
+double measure_ffma_peak() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 0.0;
+    float* buf = nullptr;
+    if (cudaMalloc(&buf, 4096) != cudaSuccess) return 0.0;
+    const float ab[2] = {0.999999f, 1e-7f};
+    cudaMemcpy(buf, ab, sizeof ab, cudaMemcpyHostToDevice);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    const int iters = 1 << 16, threads = 512, blocks = sms * 4;
+    double best = 0.0;
+    for (int rep = 0; rep < 3; ++rep) {
+        cudaEventRecord(e0);
+        k_ffma_peak<<<blocks, threads>>>(buf, iters, buf + 16);
+        cudaEventRecord(e1);
+        cudaEventSynchronize(e1);
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        const double flops = 2.0 * 8.0 * iters * static_cast<double>(threads) * blocks;
+        if (ms > 0.0f && rep > 0) best = std::max(best, flops / (ms * 1e-3) / 1e12);
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(buf);
+    return best;
+}
 
 }  // namespace ssla

@@ -138,5 +138,7 @@ void launch_write_slots(cudaStream_t st, int n, int P, const int* rec_off, const
 void launch_fill_clk(cudaStream_t st, int P, const int* rec_off, const unsigned long long* stamps,
                      unsigned long long* const* clks);
 void launch_stamp(cudaStream_t st, unsigned long long* dst);
+// Measured FP32 FMA throughput of the current device, TFLOP/s.
+double measure_ffma_peak();
 
 }  // namespace ssla

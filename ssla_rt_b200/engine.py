@@ -51,6 +51,9 @@ def load_library() -> C.CDLL:
         "ssla_engine_info": (i, [vp, C.POINTER(abi.SslaEngineInfo)]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
         "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
+        "ssla_engine_set_profiling": (i, [vp, i]),
+        "ssla_engine_phase_times": (i, [vp, vp, i, C.POINTER(C.c_int)]),
+        "ssla_measure_fp32_peak": (i, [i, C.POINTER(C.c_double)]),
         "ssla_expf_host": (f, [f]),
         "ssla_last_error": (C.c_char_p, []),
         "ssla_version": (C.c_char_p, []),
@@ -182,8 +185,25 @@ class SslaEngine:
     def flags(self, n: int) -> np.ndarray:
         return self._read(abi.STATE_FLAGS, 0, 0, np.uint8)[:n]
 
+    def set_profiling(self, on: bool) -> None:
+        _check(self.lib.ssla_engine_set_profiling(self.h, 1 if on else 0))
+
+    def phase_times(self):
+        """[(name, ms, launches)] of the last profiled drain, launch order."""
+        buf = (abi.SslaPhaseTime * 128)()
+        n = C.c_int()
+        _check(self.lib.ssla_engine_phase_times(self.h, C.cast(buf, C.c_void_p), 128, C.byref(n)))
+        return [(buf[i].name.decode(), buf[i].ms, buf[i].launches) for i in range(n.value)]
+
     def state_ptr(self, kind: int, partition: int = 0, index: int = 0) -> int:
         return self.lib.ssla_engine_state_ptr(self.h, kind, partition, index) or 0
+
+
+def measure_fp32_peak(device: int = 0) -> float:
+    """Measured FP32 FFMA peak of the device in TFLOP/s."""
+    v = C.c_double()
+    _check(load_library().ssla_measure_fp32_peak(device, C.byref(v)))
+    return v.value
 
 
 def drain_n_multi(cfg: abi.HybridS2S3Config, rings: Sequence[int], ns: Sequence[int],
