@@ -65,8 +65,9 @@ def patches(coords_xy: np.ndarray, s: int) -> np.ndarray:
 
 
 def algorithmic_macs(ev: np.ndarray, flags: np.ndarray) -> dict:
-    """MACs per layer split as qvg / gather / residual (survey 8(d) model
-    with exact in-bounds patch counts), plus the head."""
+    """MACs per layer (survey 8(d) model with exact in-bounds patch counts):
+    vg / q = the v,g and q rows of the fused qvg matvec, gather = the goW
+    contributions, resid = input_proj; plus the head."""
     from ssla_rt_b200 import abi
     xy = ev[:, 1:3]
     valid = (flags & abi.F_VALID) != 0
@@ -77,26 +78,29 @@ def algorithmic_macs(ev: np.ndarray, flags: np.ndarray) -> dict:
         ent = reach[s]
         np_ = patches(xy[ent], s) if A == 9 else np.ones(int(ent.sum()), np.int64)
         outn = reach[s + 1][ent] if l % 2 == 1 else np.ones(int(ent.sum()), bool)
-        qvg = int((np_ * np.where(outn, 3, 2)).sum()) * OUT * IN
-        gather = int(np_[outn].sum()) * OUT * OUT
-        resid = int(outn.sum()) * IN * OUT if IN != OUT else 0
-        out[l] = {"qvg": qvg, "gather": gather, "resid": resid}
+        out[l] = {"vg": int(np_.sum()) * 2 * OUT * IN,
+                  "q": int(np_[outn].sum()) * OUT * IN,
+                  "gather": int(np_[outn].sum()) * OUT * OUT,
+                  "resid": int(outn.sum()) * IN * OUT if IN != OUT else 0}
     out["head"] = int(reach[4].sum()) * (2 * 96 * 96 + 7 * 96)
     return out
 
 
+def total_macs(macs: dict) -> int:
+    return sum(v["vg"] + v["q"] + v["gather"] + v["resid"] for k, v in macs.items() if k != "head") + macs["head"]
+
+
 def phase_flops(macs: dict, name: str) -> float:
-    """Algorithmic FLOPs of one engine phase (2 per MAC)."""
-    if name.startswith("event_L"):
-        l = int(name[7])
-        m = macs[l]["gather"]
-        if l < 7:
-            m += macs[l + 1]["qvg"] + macs[l + 1]["resid"]
-        else:
-            m += macs["head"]
-        if l == 0:
-            m += 0
-        return 2.0 * m
+    """Algorithmic FLOPs of one engine phase (2 per MAC); 0 for integer or
+    scan phases."""
+    if name.startswith("gather_L"):
+        l = int(name[8])
+        return 2.0 * (macs[l]["gather"] + (macs["head"] if l == 7 else 0))
+    if name.startswith("gemm_L"):
+        l = int(name[6])
+        kind = name.split("_")[-1]
+        m = macs[l]
+        return 2.0 * {"vg": m["vg"], "q": m["q"], "all": m["vg"] + m["q"], "res": m["resid"]}[kind]
     return 0.0
 
 
@@ -345,7 +349,7 @@ def main() -> int:
     eng.drain(ev, off, flags=flags_dev, stream=stream)
     flags = flags_dev.cpu().numpy()
     macs = algorithmic_macs(ev_np, flags)
-    total_macs = sum(v["qvg"] + v["gather"] + v["resid"] for k, v in macs.items() if k != "head") + macs["head"]
+    tot_macs = total_macs(macs)
     dom = max(phase_acc.items(), key=lambda kv: kv[1][0])
     dom_name, (dom_ms_sum, dom_n, _) = dom
     dom_ms = dom_ms_sum / dom_n
@@ -377,7 +381,7 @@ def main() -> int:
             "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(ev_np.nbytes),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
-            "algorithmic_mac_per_event": total_macs / N_EVENTS,
+            "algorithmic_mac_per_event": tot_macs / N_EVENTS,
             "stage_events": [int(x) for x in eng.info().stage_events],
             "phase_ms": phases,
         }

@@ -162,7 +162,7 @@ struct Workspace {
     int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, n_active = 0;
     long long cap_part[5] = {0}, cap[5] = {0};
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
-    DevBuf tl[4], tl_cnt[4], S_A, S_B, R_A, R_B, head_dec, head_raw, feat, slot_feat, stamps;
+    DevBuf tl[4], tl_cnt[4], S_A, S_B, R_A, R_B, X, head_dec, head_raw, feat, slot_feat, stamps;
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -212,6 +212,7 @@ struct Workspace {
             rb = std::max(rb, k * c);
         }
         S_A.alloc(sa * 4); S_B.alloc(sb * 4); R_A.alloc(ra * 4); R_B.alloc(rb * 4);
+        X.alloc(ra * 4);                        // layer outputs, [rows][C_s]
         const int cols = 5 + g.ncls;
         head_dec.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
         head_raw.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
@@ -228,60 +229,103 @@ struct Workspace {
 };
 
 // Enqueues stages s_first..3 (layers 2*s_first..7) for a planned workspace.
-// rec_off / E_2 / feat must be prepared by the caller for s_first == 2.
+// On entry S_A / R_A hold the (q, v, sigmoid(g)) rows and residuals of the
+// first layer of stage s_first.  Per stage s (first layer 2s, second 2s+1):
+//   scan 2s on S_A | gather 2s -> X (E_s rows), R_B = X for events whose
+//   second-layer output is used | GEMM v,g cols of layer 2s+1 for all E_s
+//   rows and q cols for E_{s+1} rows -> S_B | scan 2s+1 on S_B |
+//   gather 2s+1 -> X (E_{s+1} rows) | GEMM layer 2s+2 all cols + input_proj
+//   -> S_A, R_A   (stage 3: gather 7 runs the head instead).
 void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_parts,
                 const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof) {
-    static const char* kScanNames[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
-                                        "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
-    static const char* kEventNames[8] = {"event_L0", "event_L1", "event_L2", "event_L3",
-                                         "event_L4", "event_L5", "event_L6", "event_L7_head"};
+    static const char* kScan[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
+                                   "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
+    static const char* kGather[8] = {"gather_L0", "gather_L1", "gather_L2", "gather_L3",
+                                     "gather_L4", "gather_L5", "gather_L6", "gather_L7_head"};
+    static const char* kVG[8] = {"", "gemm_L1_vg", "", "gemm_L3_vg", "", "gemm_L5_vg", "", "gemm_L7_vg"};
+    static const char* kQ[8] = {"", "gemm_L1_q", "", "gemm_L3_q", "", "gemm_L5_q", "", "gemm_L7_q"};
+    static const char* kAll[8] = {"", "", "gemm_L2_all", "", "gemm_L4_all", "", "gemm_L6_all", ""};
+    static const char* kRes[8] = {"", "", "gemm_L2_res", "", "gemm_L4_res", "", "gemm_L6_res", ""};
     const int* d_count = w.count.as<int>();
+    float* X = w.X.as<float>();
     for (int s = w.s_first; s < 4; ++s) {
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
         const int2* tl = w.tl[s].as<int2>();
         const int* tl_cnt = w.tl_cnt[s].as<int>();
+        const long long n_s = (s == 0) ? w.n_active : w.cap[s];
         for (int half = 0; half < 2; ++half) {
             const int l = 2 * s + half;
-            // S / R ping-pong: even layers read A, odd layers read B.
-            float* S_in = (half == 0) ? w.S_A.as<float>() : w.S_B.as<float>();
-            float* R_in = (half == 0) ? w.R_A.as<float>() : w.R_B.as<float>();
-            float* S_out = (half == 0) ? w.S_B.as<float>() : w.S_A.as<float>();
-            float* R_out = (half == 0) ? w.R_B.as<float>() : w.R_A.as<float>();
+            float* S_l = (half == 0) ? w.S_A.as<float>() : w.S_B.as<float>();
+            float* R_l = (half == 0) ? w.R_A.as<float>() : w.R_B.as<float>();
             ScanArgs sa{};
             sa.g = g; sa.stage = s; sa.layer = l; sa.tl = tl; sa.tl_cnt = tl_cnt; sa.range = range;
-            sa.S = S_in; sa.parts = d_parts; sa.rflags = w.rflags.as<uint8_t>(); sa.second = half;
+            sa.S = S_l; sa.parts = d_parts; sa.rflags = w.rflags.as<uint8_t>(); sa.second = half;
             launch_scan(st, l, sa);
             check_launch("k_scan");
-            prof.mark(kScanNames[l], 1, st);
+            prof.mark(kScan[l], 1, st);
 
-            EventArgs ea{};
-            ea.g = g; ea.stage = s; ea.count = d_count;
-            ea.ev_xy = w.ev_xy.as<uint32_t>(); ea.rflags = w.rflags.as<uint8_t>();
-            ea.S_in = S_in; ea.R_in = R_in; ea.S_out = S_out; ea.R_out = R_out;
-            ea.L = L[l];
-            if (l < 7) ea.N = L[l + 1];
-            ea.head = *head;
-            ea.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
-            ea.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
-            ea.head_dec = w.head_dec.as<float>();
-            ea.head_raw = w.head_raw.as<float>();
-            long long n_cap;
-            int mode;
+            GatherArgs ga{};
+            ga.g = g; ga.stage = s; ga.second = half; ga.count = d_count;
+            ga.ev_xy = w.ev_xy.as<uint32_t>(); ga.rflags = w.rflags.as<uint8_t>();
+            ga.S_in = S_l; ga.R_in = R_l; ga.L = L[l]; ga.head = *head;
+            ga.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
+            ga.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
+            ga.head_dec = w.head_dec.as<float>();
+            ga.head_raw = w.head_raw.as<float>();
+            const bool last = (l == 7);
+            ga.X_out = last ? nullptr : X;
+            long long n_rows;
             if (half == 0) {
-                mode = MODE_FIRST;
-                ea.needq_bit = static_cast<uint8_t>(F_R1 << s);
-                if (s == 0) { ea.list = 0; ea.n_static = w.n_active; n_cap = w.n_active; }
-                else { ea.list = s; ea.E = w.E[s].as<StageEntry>(); n_cap = w.cap[s]; }
+                if (s == 0) { ga.list = 0; ga.n_static = w.n_active; }
+                else { ga.list = s; ga.E = w.E[s].as<StageEntry>(); }
+                n_rows = n_s;
+                ga.copyres_bit = static_cast<uint8_t>(F_R1 << s);      // R_{s+1}
+                ga.R_next = w.R_B.as<float>();
             } else {
-                mode = (s < 3) ? MODE_SECOND : (do_head ? MODE_HEAD : MODE_LAST);
-                ea.list = s + 1;
-                ea.E = w.E[s + 1].as<StageEntry>();
-                n_cap = w.cap[s + 1];
+                ga.list = s + 1;
+                ga.E = w.E[s + 1].as<StageEntry>();
+                n_rows = w.cap[s + 1];
             }
-            const int grid = static_cast<int>(std::min<long long>((n_cap + kMB - 1) / kMB, 148LL * 8));
-            launch_event(st, l, mode, ea, grid);
-            check_launch("k_event");
-            prof.mark(kEventNames[l], 1, st);
+            const int grid = static_cast<int>(std::min<long long>((n_rows + kMB - 1) / kMB, 148LL * 8));
+            launch_gather(st, l, last && do_head, ga, grid);
+            check_launch("k_gather");
+            prof.mark(kGather[l], 1, st);
+            if (last) break;
+
+            GemmArgs gm{};
+            gm.count = d_count; gm.X = X; gm.A2 = 9;
+            if (half == 0) {
+                // layer l+1 (second layer of stage s): v,g for every E_s row
+                gm.W = L[l + 1].qvgT; gm.S = w.S_B.as<float>();
+                if (s == 0) { gm.list = 0; gm.n_static = w.n_active; gm.g_cap = w.n_active; }
+                else { gm.list = s; gm.g_cap = static_cast<int>(w.cap[s]); }
+                gm.colmode = COLS_VG; gm.n_cols = gemm_cols(l + 1, COLS_VG);
+                launch_gemm(st, l + 1, gm, n_s);
+                check_launch("k_gemm vg");
+                prof.mark(kVG[l + 1], 1, st);
+                // q columns only for events whose layer-(l+1) output is used
+                GemmArgs gq = gm;
+                gq.list = s + 1; gq.g_cap = static_cast<int>(w.cap[s + 1]);
+                gq.E = w.E[s + 1].as<StageEntry>();
+                gq.colmode = COLS_Q; gq.n_cols = gemm_cols(l + 1, COLS_Q);
+                launch_gemm(st, l + 1, gq, w.cap[s + 1]);
+                check_launch("k_gemm q");
+                prof.mark(kQ[l + 1], 1, st);
+            } else {
+                // layer l+1 = first layer of stage s+1: all columns + input_proj
+                gm.list = s + 1; gm.g_cap = static_cast<int>(w.cap[s + 1]);
+                gm.W = L[l + 1].qvgT; gm.S = w.S_A.as<float>();
+                gm.colmode = COLS_ALL; gm.n_cols = gemm_cols(l + 1, COLS_ALL);
+                launch_gemm(st, l + 1, gm, w.cap[s + 1]);
+                check_launch("k_gemm all");
+                prof.mark(kAll[l + 1], 1, st);
+                GemmArgs gr = gm;
+                gr.W = L[l + 1].ipT; gr.R = w.R_A.as<float>();
+                gr.colmode = COLS_RES; gr.n_cols = gemm_cols(l + 1, COLS_RES);
+                launch_gemm(st, l + 1, gr, w.cap[s + 1]);
+                check_launch("k_gemm res");
+                prof.mark(kRes[l + 1], 1, st);
+            }
         }
     }
 }
@@ -616,14 +660,16 @@ struct DrainN {
             const LayerWeightsS2S3& lw = cfg->layers[0][li];
             L[4 + li] = DevLayer{lw.qvgIn, lw.goW, lw.input_proj, lw.ln_gamma, lw.ln_beta};
         }
-        // record features -> layer-4 qvg + residual
-        EventArgs ea{};
-        ea.g = g; ea.stage = 2; ea.mode = MODE_ENTRY; ea.count = w.count.as<int>(); ea.list = 2;
-        ea.E = w.E[2].as<StageEntry>(); ea.ev_xy = w.ev_xy.as<uint32_t>(); ea.rflags = w.rflags.as<uint8_t>();
-        ea.S_out = w.S_A.as<float>(); ea.R_out = w.R_A.as<float>(); ea.N = L[4];
-        ea.entry_feat = w.feat.as<float>();
-        launch_event(st, 4, MODE_ENTRY, ea, static_cast<int>(std::min<long long>((n + kMB - 1) / kMB, 148LL * 8)));
-        check_launch("k_event entry");
+        // record features -> layer-4 qvg (all columns) + residual
+        GemmArgs ge{};
+        ge.list = 2; ge.count = w.count.as<int>(); ge.g_cap = n; ge.X = w.feat.as<float>(); ge.A2 = 9;
+        ge.W = L[4].qvgT; ge.S = w.S_A.as<float>(); ge.colmode = COLS_ALL; ge.n_cols = gemm_cols(4, COLS_ALL);
+        launch_gemm(st, 4, ge, n);
+        check_launch("k_gemm entry");
+        GemmArgs gr = ge;
+        gr.W = L[4].ipT; gr.R = w.R_A.as<float>(); gr.colmode = COLS_RES; gr.n_cols = gemm_cols(4, COLS_RES);
+        launch_gemm(st, 4, gr, n);
+        check_launch("k_gemm entry res");
         DevHead nohead{};
         Prof noprof;
         run_layers(st, g, w, d.parts.as<PartState>(), L, &nohead, false, false, noprof);

@@ -8,8 +8,9 @@
 //                 layer-0 qvg/residual, one warp per (partition, s3 block)
 //   k_compact_*   stream-ordered stage lists E_1..E_4
 //   k_filter(s1..s3)
-//   per layer l:  k_scan (cell-major LRU update) then k_event (event-major
-//                 gather / LayerNorm / next-layer qvg, or the head)
+//   per layer l:  k_scan (cell-major LRU update), k_gather (event-major
+//                 9-owner gather / residual / LayerNorm, or the head), then
+//                 k_gemm (the next layer's qvg as a tiled FP32 GEMM)
 //   k_commit      last head write per s3 cell -> predictions + version
 // Reference behaviour each kernel reproduces is cited inline.
 #include "ssla_kernels.cuh"
@@ -550,233 +551,157 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// k_event: event-major, 32 events per batch, 256 threads.
-//   x  = gather (modes 0-3): out = sum over delta = 8..0 of
-//        goW[delta] * qh[delta] (each delta an fmaf chain from 0, added in the
-//        reference's patch order, layer_forward_ct :340-380), + residual,
-//        fp64 LayerNorm (layernorm_ct, layernorm.h:41-62)
-//     or the record's stage-1 feature (mode 4);
-//   then the next layer's qvg for its patch positions (matvec_ct<IN,3*OUT>,
-//   q rows only where that layer's output is consumed) and residual
-//   (input_proj or copy), or the YOLOX head (mode 2,
-//   async_yolox.h:203-254).
-// Thread tiles: one output x 8 events; weights stream from L2 once per
-// 8 events, features come from shared memory.
+// k_gather: the 9-owner gather + residual + LayerNorm of one layer for a batch
+// of 32 output-producing events (layer_forward_ct, src/ssla_kernels.cpp:
+// 340-384):  out = sum over delta = 8..0 (reference patch order) of
+// goW[delta] * qh[delta], each delta an fmaf chain from 0 over the input
+// channels; + residual; LayerNorm with sequential fp64 sums
+// (layernorm.h:41-62).  goW[delta] and the batch's qh rows are staged in
+// shared memory per delta; a thread owns 2 outputs x 8 events.
+// HEAD additionally runs the YOLOX head (async_yolox.h:203-254) on the
+// stage-3 feature.
 // ---------------------------------------------------------------------------
-template <int A, int OUT, int A2, int OUT2, int MODE>
-__global__ void __launch_bounds__(kNT) k_event(EventArgs a) {
-    constexpr int XD = (MODE == MODE_ENTRY) ? 24 : OUT;     // feature width
-    __shared__ __align__(16) float sm[3 * 96 * kMB];
-    float* qh_s = sm;                     // [OUT][kMB]
-    float* out_s = sm + 96 * kMB;         // [OUT][kMB]
-    float* x_s = sm + 2 * 96 * kMB;       // [XD][kMB]
-    float* act_s = sm;                    // head: [192][kMB] (qh_s + out_s)
-    __shared__ int kin_s[kMB], kout_s[kMB], e_s[kMB], valid_s[kMB], needq_s[kMB];
-    __shared__ int cx_s[kMB], cy_s[kMB], cx2_s[kMB], cy2_s[kMB];
-    __shared__ unsigned inb_s[kMB], inb2_s[kMB];
+template <int A, int OUT, bool HEAD>
+__global__ void __launch_bounds__(kNT) k_gather(GatherArgs a) {
+    extern __shared__ __align__(16) float dsm[];
+    float* gw_s = dsm;                          // [OUT][OUT]  goWT[delta]
+    float* qh_s = gw_s + OUT * OUT;             // [OUT][kMB]
+    float* out_s = qh_s + OUT * kMB;            // [OUT][kMB]
+    float* x_s = out_s + OUT * kMB;             // [OUT][kMB]
+    float* act_s = x_s + OUT * kMB;             // HEAD: [192][kMB]
+    __shared__ int srow_s[kMB], row_s[kMB], e_s[kMB], valid_s[kMB], copy_s[kMB];
+    __shared__ int cx_s[kMB], cy_s[kMB];
+    __shared__ unsigned inb_s[kMB];
     __shared__ double mean_s[kMB], inv_s[kMB];
     __shared__ float res_s[kMB][24];
     const int tid = threadIdx.x;
     const int s = a.stage;
     const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    const int s2 = (MODE == MODE_FIRST || MODE == MODE_ENTRY) ? s : s + 1;   // next layer's stage
-    const int W2 = a.g.W[s2 < 4 ? s2 : 3], H2 = a.g.H[s2 < 4 ? s2 : 3];
+    constexpr int OP = OUT / 2;                 // output pairs
 
     for (int batch = blockIdx.x; batch * kMB < n_list; batch += gridDim.x) {
         if (tid < kMB) {
-            const int idx = batch * kMB + tid;
-            int valid = 0, kin = 0, kout = 0, e = 0, needq = 1;
+            const int r = batch * kMB + tid;
+            int valid = 0, srow = 0, e = 0, cp = 0;
             uint32_t xy0 = 0;
-            if (idx < n_list) {
-                if (a.list == 0) {                              // stage 0, all events
-                    e = idx; kin = idx; kout = idx;
-                    xy0 = a.ev_xy[idx];
-                    valid = (a.rflags[idx] & F_VALID) ? 1 : 0;
-                } else if (MODE == MODE_FIRST || MODE == MODE_ENTRY) {
-                    const StageEntry se = a.E[idx];
-                    e = se.e; kin = idx; kout = idx; xy0 = se.xy0; valid = 1;
+            if (r < n_list) {
+                if (a.list == 0) {
+                    e = r; srow = r; xy0 = a.ev_xy[r];
+                    valid = (a.rflags[r] & F_VALID) ? 1 : 0;
                 } else {
-                    const StageEntry se = a.E[idx];
-                    e = se.e; kin = se.kprev; kout = idx; xy0 = se.xy0; valid = 1;
+                    const StageEntry se = a.E[r];
+                    e = se.e; xy0 = se.xy0; valid = 1;
+                    srow = a.second ? se.kprev : r;
                 }
-                if (valid && MODE == MODE_FIRST) needq = (a.rflags[e] & a.needq_bit) ? 1 : 0;
+                if (valid && a.copyres_bit) cp = (a.rflags[e] & a.copyres_bit) ? 1 : 0;
             }
-            const int x0 = static_cast<int>(xy0 & 0xFFFFu), y0 = static_cast<int>(xy0 >> 16);
-            const int cx = x0 >> s, cy = y0 >> s;
-            const int cx2 = x0 >> (s2 < 4 ? s2 : 3), cy2 = y0 >> (s2 < 4 ? s2 : 3);
-            unsigned m1 = 0, m2 = 0;
+            const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
+            unsigned m1 = 0;
             for (int d = 0; d < 9; ++d) {
                 const int dy = 1 - d / 3, dx = 1 - d % 3;
                 if (cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl) m1 |= 1u << d;
-                if (cx2 + dx >= 0 && cx2 + dx < W2 && cy2 + dy >= 0 && cy2 + dy < H2) m2 |= 1u << d;
             }
-            valid_s[tid] = valid; kin_s[tid] = kin; kout_s[tid] = kout; e_s[tid] = e;
-            needq_s[tid] = needq; cx_s[tid] = cx; cy_s[tid] = cy; cx2_s[tid] = cx2; cy2_s[tid] = cy2;
-            inb_s[tid] = (A == 1) ? 1u : m1;
-            inb2_s[tid] = (A2 == 1) ? 1u : m2;
+            srow_s[tid] = srow; row_s[tid] = r; e_s[tid] = e; valid_s[tid] = valid; copy_s[tid] = cp;
+            cx_s[tid] = cx; cy_s[tid] = cy; inb_s[tid] = (A == 1) ? 1u : m1;
         }
-        __syncthreads();
-
-        if (MODE == MODE_ENTRY) {
-            for (int t = tid; t < XD * kMB; t += kNT) {
-                const int i = t / kMB, b = t % kMB;
-                x_s[t] = valid_s[b] ? a.entry_feat[static_cast<size_t>(e_s[b]) * 24 + i] : 0.0f;
-            }
-        } else {
-            // ---- gather over patch positions in the reference order ----
-            for (int t = tid; t < OUT * kMB; t += kNT) out_s[t] = 0.0f;
-            for (int d = A - 1; d >= 0; --d) {
-                __syncthreads();
-                for (int t = tid; t < OUT * kMB; t += kNT) {
-                    const int i = t / kMB, b = t % kMB;
-                    float v = 0.0f;
-                    if (valid_s[b] && ((inb_s[b] >> d) & 1u))
-                        v = a.S_in[(static_cast<size_t>(kin_s[b]) * A + d) * (3 * OUT) + i];
-                    qh_s[t] = v;
-                }
-                __syncthreads();
-                for (int item = tid; item < OUT * kGroups; item += kNT) {
-                    const int o = item % OUT, g = item / OUT;
-                    float acc[kEPT];
-#pragma unroll
-                    for (int b = 0; b < kEPT; ++b) acc[b] = 0.0f;
-                    const float* w = a.L.goWT + static_cast<size_t>(d) * OUT * OUT + o;
-#pragma unroll 4
-                    for (int i = 0; i < OUT; ++i) {
-                        const float wv = __ldg(w + static_cast<size_t>(i) * OUT);
-                        const float4 x0 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT);
-                        const float4 x1 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT + 4);
-                        acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
-                        acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
-                        acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
-                        acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
-                    }
-#pragma unroll
-                    for (int b = 0; b < kEPT; ++b) out_s[o * kMB + g * kEPT + b] += acc[b];
-                }
-            }
+        for (int t = tid; t < OUT * kMB; t += kNT) out_s[t] = 0.0f;
+        for (int d = A - 1; d >= 0; --d) {
             __syncthreads();
-            // ---- residual + LayerNorm statistics (sequential fp64 per event) ----
-            if (tid < kMB && valid_s[tid]) {
-                const int b = tid;
-                const float* r = a.R_in + static_cast<size_t>(kin_s[b]) * OUT;
-                double sum = 0.0;
-                for (int o = 0; o < OUT; ++o) {
-                    const float v = out_s[o * kMB + b] + r[o];
-                    out_s[o * kMB + b] = v;
-                    sum += static_cast<double>(v);
-                }
-                const double mean = sum / static_cast<double>(OUT);
-                double var = 0.0;
-                for (int o = 0; o < OUT; ++o) {
-                    const double dd = static_cast<double>(out_s[o * kMB + b]) - mean;
-                    var += dd * dd;
-                }
-                var /= static_cast<double>(OUT);
-                mean_s[b] = mean;
-                inv_s[b] = 1.0 / sqrt(var + static_cast<double>(1e-5f));
-            }
-            __syncthreads();
+            const float* gsrc = a.L.goWT + static_cast<size_t>(d) * OUT * OUT;
+            for (int t = tid; t < OUT * OUT / 4; t += kNT)
+                reinterpret_cast<float4*>(gw_s)[t] = __ldg(reinterpret_cast<const float4*>(gsrc) + t);
             for (int t = tid; t < OUT * kMB; t += kNT) {
-                const int o = t / kMB, b = t % kMB;
-                float xv = 0.0f;
-                if (valid_s[b]) {
-                    const double v = (static_cast<double>(out_s[t]) - mean_s[b]) * inv_s[b];
-                    xv = static_cast<float>(v * static_cast<double>(__ldg(a.L.gamma + o)) +
-                                            static_cast<double>(__ldg(a.L.beta + o)));
+                const int b = t % kMB, i = t / kMB;
+                float v = 0.0f;
+                if (valid_s[b] && ((inb_s[b] >> d) & 1u))
+                    v = a.S_in[(static_cast<size_t>(srow_s[b]) * A + d) * (3 * OUT) + i];
+                qh_s[i * kMB + b] = v;
+            }
+            __syncthreads();
+            for (int item = tid; item < OP * kGroups; item += kNT) {
+                const int op = item % OP, g = item / OP;
+                float acc0[kEPT], acc1[kEPT];
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
+#pragma unroll 4
+                for (int i = 0; i < OUT; ++i) {
+                    const float2 w = *reinterpret_cast<const float2*>(gw_s + i * OUT + 2 * op);
+                    const float4 x0 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT);
+                    const float4 x1 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT + 4);
+                    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                    for (int b = 0; b < kEPT; ++b) {
+                        acc0[b] = fmaf(w.x, xs[b], acc0[b]);
+                        acc1[b] = fmaf(w.y, xs[b], acc1[b]);
+                    }
                 }
-                x_s[t] = xv;
+#pragma unroll
+                for (int b = 0; b < kEPT; ++b) {
+                    out_s[(2 * op) * kMB + g * kEPT + b] += acc0[b];
+                    out_s[(2 * op + 1) * kMB + g * kEPT + b] += acc1[b];
+                }
             }
         }
         __syncthreads();
-        // ---- per-event feature outputs ----
-        if (MODE != MODE_ENTRY && (a.stage_out != nullptr || a.slot_feat != nullptr)) {
-            for (int t = tid; t < OUT * kMB; t += kNT) {
-                const int b = t % kMB, o = t / kMB;
-                if (!valid_s[b]) continue;
-                if (a.stage_out && MODE != MODE_FIRST)
-                    a.stage_out[static_cast<size_t>(e_s[b]) * OUT + o] = x_s[t];
-                if (a.slot_feat) {
-                    a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + o] = x_s[t];
-                    if (OUT == 48) a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + 48 + o] = 0.0f;
-                }
+        if (tid < kMB && valid_s[tid]) {
+            const int b = tid;
+            const float* r = a.R_in + static_cast<size_t>(srow_s[b]) * OUT;
+            double sum = 0.0;
+            for (int o = 0; o < OUT; ++o) {
+                const float v = out_s[o * kMB + b] + r[o];
+                out_s[o * kMB + b] = v;
+                sum += static_cast<double>(v);
+            }
+            const double mean = sum / static_cast<double>(OUT);
+            double var = 0.0;
+            for (int o = 0; o < OUT; ++o) {
+                const double dd = static_cast<double>(out_s[o * kMB + b]) - mean;
+                var += dd * dd;
+            }
+            var /= static_cast<double>(OUT);
+            mean_s[b] = mean;
+            inv_s[b] = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+        }
+        __syncthreads();
+        for (int t = tid; t < OUT * kMB; t += kNT) {
+            const int o = t / kMB, b = t % kMB;
+            float xv = 0.0f;
+            if (valid_s[b]) {
+                const double v = (static_cast<double>(out_s[t]) - mean_s[b]) * inv_s[b];
+                xv = static_cast<float>(v * static_cast<double>(__ldg(a.L.gamma + o)) +
+                                        static_cast<double>(__ldg(a.L.beta + o)));
+            }
+            x_s[t] = xv;
+        }
+        __syncthreads();
+        // ---- outputs: layer feature (row-major per event), copy residual of
+        //      the stage's second layer, stage outputs, drain_n slot ----
+        for (int t = tid; t < OUT * kMB; t += kNT) {
+            const int b = t / OUT, o = t % OUT;
+            if (!valid_s[b]) continue;
+            const float xv = x_s[o * kMB + b];
+            if (a.X_out) a.X_out[static_cast<size_t>(row_s[b]) * OUT + o] = xv;
+            if (copy_s[b]) a.R_next[static_cast<size_t>(row_s[b]) * OUT + o] = xv;
+            if (a.stage_out && a.second) a.stage_out[static_cast<size_t>(e_s[b]) * OUT + o] = xv;
+            if (a.slot_feat) {
+                a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + o] = xv;
+                if (OUT == 48) a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + 48 + o] = 0.0f;
             }
         }
-
-        if (MODE == MODE_FIRST || MODE == MODE_SECOND || MODE == MODE_ENTRY) {
-            // ---- next layer: qvg for every patch position, then residual ----
-            constexpr int J2 = 3 * OUT2;
-            for (int item = tid; item < A2 * J2 * kGroups; item += kNT) {
-                const int j = item % (A2 * J2), g = item / (A2 * J2);
-                const int d2 = j / J2, jj = j % J2, part = jj / OUT2;
-                unsigned gm = 0;
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b) {
-                    const int bb = g * kEPT + b;
-                    const bool need = valid_s[bb] && ((inb2_s[bb] >> d2) & 1u) &&
-                                      (part != 0 || needq_s[bb]);
-                    gm |= need ? (1u << b) : 0u;
-                }
-                if (!gm) continue;
-                float acc[kEPT];
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b) acc[b] = 0.0f;
-                const float* w = a.N.qvgT + static_cast<size_t>(d2) * XD * J2 + jj;
-#pragma unroll 4
-                for (int i = 0; i < XD; ++i) {
-                    const float wv = __ldg(w + static_cast<size_t>(i) * J2);
-                    const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
-                    const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
-                    acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
-                    acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
-                    acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
-                    acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
-                }
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b) {
-                    if ((gm >> b) & 1u) {
-                        const float v = (part == 2) ? ssla_sigmoidf(acc[b]) : acc[b];
-                        a.S_out[(static_cast<size_t>(kout_s[g * kEPT + b]) * A2 + d2) * J2 + jj] = v;
-                    }
-                }
-            }
-            for (int item = tid; item < OUT2 * kGroups; item += kNT) {
-                const int o2 = item % OUT2, g = item / OUT2;
-                float acc[kEPT];
-                if (a.N.ipT != nullptr) {
-#pragma unroll
-                    for (int b = 0; b < kEPT; ++b) acc[b] = 0.0f;
-                    for (int i = 0; i < XD; ++i) {
-                        const float wv = __ldg(a.N.ipT + static_cast<size_t>(i) * OUT2 + o2);
-#pragma unroll
-                        for (int b = 0; b < kEPT; ++b)
-                            acc[b] = fmaf(wv, x_s[i * kMB + g * kEPT + b], acc[b]);
-                    }
-                } else {
-#pragma unroll
-                    for (int b = 0; b < kEPT; ++b) acc[b] = x_s[o2 * kMB + g * kEPT + b];
-                }
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b) {
-                    const int bb = g * kEPT + b;
-                    if (valid_s[bb] && needq_s[bb])
-                        a.R_out[static_cast<size_t>(kout_s[bb]) * OUT2 + o2] = acc[b];
-                }
-            }
-        } else if (MODE == MODE_HEAD) {
-            // ---- YOLOX head: cls / reg 1x1 convs (BN folded) + SiLU ----
+        if (HEAD) {
+            // cls / reg 1x1 convs (BN folded, bias-first accumulation) + SiLU
             for (int item = tid; item < 192 * kGroups; item += kNT) {
                 const int j = item % 192, g = item / 192;
                 const int jo = j % 96;
-                const float* W = (j < 96) ? a.head.cls_convT : a.head.reg_convT;
+                const float* Wt = (j < 96) ? a.head.cls_convT : a.head.reg_convT;
                 const float bias = __ldg(((j < 96) ? a.head.cls_conv_b : a.head.reg_conv_b) + jo);
                 float acc[kEPT];
 #pragma unroll
                 for (int b = 0; b < kEPT; ++b) acc[b] = bias;
 #pragma unroll 4
                 for (int i = 0; i < 96; ++i) {
-                    const float wv = __ldg(W + i * 96 + jo);
+                    const float wv = __ldg(Wt + i * 96 + jo);
                     const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
                     const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
                     acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
@@ -821,11 +746,120 @@ __global__ void __launch_bounds__(kNT) k_event(EventArgs a) {
                 else if (r == 2) d = ssla_expf(v) * static_cast<float>(a.g.stride_w);
                 else if (r == 3) d = ssla_expf(v) * static_cast<float>(a.g.stride_h);
                 else d = v;
-                a.head_dec[static_cast<size_t>(kout_s[b]) * cols + r] = d;
-                a.head_raw[static_cast<size_t>(kout_s[b]) * cols + r] = v;
+                a.head_dec[static_cast<size_t>(row_s[b]) * cols + r] = d;
+                a.head_raw[static_cast<size_t>(row_s[b]) * cols + r] = v;
             }
         }
         __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_gemm: next-layer fused qvg (matvec_ct<IN,3*OUT>, linear.h:80-90) for a set
+// of events and a set of weight columns, as a register-tiled FP32 GEMM:
+//   Y[row][col] = sum_k X[row][k] * W[k][col]   (fmaf chain, k ascending)
+// Columns (per patch position delta of the next layer, J2 = 3*OUT2):
+//   COLS_ALL  every q, v, g column          (first layers: output always used)
+//   COLS_VG   the v and g columns           (second layers: every event)
+//   COLS_Q    the q columns                 (second layers: events whose
+//                                            output is consumed)
+//   COLS_RES  input_proj (the residual, matvec_ct<IN,OUT>)
+// g columns are stored as sigmoid(g).  A CTA computes a BM x BN tile with the
+// whole K extent of X and W staged in shared memory; a thread owns 8 rows x
+// 4 columns.  grid-stride over (row tile, column tile).
+// ---------------------------------------------------------------------------
+template <int K, int OUT2, int BM, int BN>
+__global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
+    constexpr int J2 = 3 * OUT2;
+    constexpr int TN = BN / 4;                  // column groups (threads per row group)
+    static_assert((BM / 8) * TN == kNT, "tile shape");
+    extern __shared__ __align__(16) float dsm[];
+    float* As = dsm;                            // [K][BM]
+    float* Bs = dsm + K * BM;                   // [K][BN]
+    __shared__ int xrow_s[BM];
+    const int tid = threadIdx.x;
+    const int tx = tid % TN, ty = tid / TN;
+    const int n_rows = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g_cap);
+    const int n_rt = (n_rows + BM - 1) / BM;
+    const int n_ct = (a.n_cols + BN - 1) / BN;
+    const size_t srow_stride = static_cast<size_t>(a.A2) * J2;
+    for (int unit = blockIdx.x; unit < n_rt * n_ct; unit += gridDim.x) {
+        const int rt = unit / n_ct, ct = unit % n_ct;
+        const int r0 = rt * BM, c0 = ct * BN;
+        __syncthreads();
+        if (tid < BM) {
+            const int r = r0 + tid;
+            xrow_s[tid] = (r < n_rows) ? (a.E ? a.E[r].kprev : r) : -1;
+        }
+        __syncthreads();
+        for (int t = tid; t < K * BM; t += kNT) {
+            const int r = t % BM, k = t / BM;
+            const int xr = xrow_s[r];
+            As[k * BM + r] = (xr >= 0) ? a.X[static_cast<size_t>(xr) * K + k] : 0.0f;
+        }
+        for (int t = tid; t < K * BN; t += kNT) {
+            const int c = t % BN, k = t / BN;
+            const int col = c0 + c;
+            float w = 0.0f;
+            if (col < a.n_cols) {
+                if (a.colmode == COLS_RES) {
+                    w = __ldg(a.W + static_cast<size_t>(k) * OUT2 + col);
+                } else {
+                    int d, jj;
+                    if (a.colmode == COLS_ALL) { d = col / J2; jj = col % J2; }
+                    else if (a.colmode == COLS_VG) { d = col / (2 * OUT2); jj = OUT2 + col % (2 * OUT2); }
+                    else { d = col / OUT2; jj = col % OUT2; }
+                    w = __ldg(a.W + (static_cast<size_t>(d) * K + k) * J2 + jj);
+                }
+            }
+            Bs[k * BN + c] = w;
+        }
+        __syncthreads();
+        float acc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+#pragma unroll 4
+        for (int k = 0; k < K; ++k) {
+            const float4 a0 = *reinterpret_cast<const float4*>(As + k * BM + ty * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(As + k * BM + ty * 8 + 4);
+            const float4 b = *reinterpret_cast<const float4*>(Bs + k * BN + tx * 4);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        // epilogue: 4 consecutive columns never straddle a delta block
+        const int col = c0 + tx * 4;
+        if (col < a.n_cols) {
+            int jcol = col, part = 0;
+            if (a.colmode == COLS_ALL) { jcol = col; part = (col % J2) / OUT2; }
+            else if (a.colmode == COLS_VG) {
+                const int d = col / (2 * OUT2), cc = col % (2 * OUT2);
+                jcol = d * J2 + OUT2 + cc; part = 1 + cc / OUT2;
+            } else if (a.colmode == COLS_Q) {
+                const int d = col / OUT2;
+                jcol = d * J2 + col % OUT2; part = 0;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int xr = xrow_s[ty * 8 + i];
+                if (xr < 0) continue;
+                float4 v = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+                if (a.colmode == COLS_RES) {
+                    *reinterpret_cast<float4*>(a.R + static_cast<size_t>(xr) * OUT2 + col) = v;
+                } else {
+                    if (part == 2) {
+                        v.x = ssla_sigmoidf(v.x); v.y = ssla_sigmoidf(v.y);
+                        v.z = ssla_sigmoidf(v.z); v.w = ssla_sigmoidf(v.w);
+                    }
+                    *reinterpret_cast<float4*>(a.S + static_cast<size_t>(xr) * srow_stride + jcol) = v;
+                }
+            }
+        }
     }
 }
 
@@ -974,16 +1008,6 @@ template __global__ void k_scan<9, 24>(ScanArgs);
 template __global__ void k_scan<9, 48>(ScanArgs);
 template __global__ void k_scan<9, 96>(ScanArgs);
 
-template __global__ void k_event<1, 12, 9, 12, MODE_FIRST>(EventArgs);    // L0 -> L1
-template __global__ void k_event<9, 12, 9, 24, MODE_SECOND>(EventArgs);   // L1 -> L2
-template __global__ void k_event<9, 24, 9, 24, MODE_FIRST>(EventArgs);    // L2 -> L3
-template __global__ void k_event<9, 24, 9, 48, MODE_SECOND>(EventArgs);   // L3 -> L4
-template __global__ void k_event<9, 48, 9, 48, MODE_FIRST>(EventArgs);    // L4 -> L5
-template __global__ void k_event<9, 48, 9, 96, MODE_SECOND>(EventArgs);   // L5 -> L6
-template __global__ void k_event<9, 96, 9, 96, MODE_FIRST>(EventArgs);    // L6 -> L7
-template __global__ void k_event<9, 96, 1, 96, MODE_HEAD>(EventArgs);     // L7 -> head
-template __global__ void k_event<9, 96, 1, 96, MODE_LAST>(EventArgs);     // L7 (drain_n)
-template __global__ void k_event<1, 24, 9, 48, MODE_ENTRY>(EventArgs);    // record -> L4
 
 }  // namespace ssla
 
@@ -1048,21 +1072,53 @@ void launch_scan(cudaStream_t st, int layer, const ScanArgs& a) {
     }
 }
 
-void launch_event(cudaStream_t st, int layer, int mode, const EventArgs& a, int grid) {
+void launch_gather(cudaStream_t st, int layer, bool head, const GatherArgs& a, int grid) {
     if (grid < 1) grid = 1;
-    if (mode == MODE_ENTRY) { k_event<1, 24, 9, 48, MODE_ENTRY><<<grid, kNT, 0, st>>>(a); return; }
+    auto go = [&](auto kern, int OUT, int extra) {
+        const size_t smem = sizeof(float) * (static_cast<size_t>(OUT) * OUT + 3 * OUT * kMB + extra);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        kern<<<grid, kNT, smem, st>>>(a);
+    };
     switch (layer) {
-        case 0: k_event<1, 12, 9, 12, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
-        case 1: k_event<9, 12, 9, 24, MODE_SECOND><<<grid, kNT, 0, st>>>(a); break;
-        case 2: k_event<9, 24, 9, 24, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
-        case 3: k_event<9, 24, 9, 48, MODE_SECOND><<<grid, kNT, 0, st>>>(a); break;
-        case 4: k_event<9, 48, 9, 48, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
-        case 5: k_event<9, 48, 9, 96, MODE_SECOND><<<grid, kNT, 0, st>>>(a); break;
-        case 6: k_event<9, 96, 9, 96, MODE_FIRST><<<grid, kNT, 0, st>>>(a); break;
+        case 0: go(k_gather<1, 12, false>, 12, 0); break;
+        case 1: go(k_gather<9, 12, false>, 12, 0); break;
+        case 2: case 3: go(k_gather<9, 24, false>, 24, 0); break;
+        case 4: case 5: go(k_gather<9, 48, false>, 48, 0); break;
+        case 6: go(k_gather<9, 96, false>, 96, 0); break;
         default:
-            if (mode == MODE_HEAD) k_event<9, 96, 1, 96, MODE_HEAD><<<grid, kNT, 0, st>>>(a);
-            else k_event<9, 96, 1, 96, MODE_LAST><<<grid, kNT, 0, st>>>(a);
+            if (head) go(k_gather<9, 96, true>, 96, 192 * kMB);
+            else go(k_gather<9, 96, false>, 96, 0);
             break;
+    }
+}
+
+int gemm_cols(int layer, int colmode) {
+    static const int kOut[8] = {12, 12, 24, 24, 48, 48, 96, 96};
+    const int out2 = kOut[layer], a2 = (layer == 0) ? 1 : 9;
+    switch (colmode) {
+        case COLS_ALL: return a2 * 3 * out2;
+        case COLS_VG: return a2 * 2 * out2;
+        case COLS_Q: return a2 * out2;
+        default: return out2;
+    }
+}
+
+void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_rows) {
+    auto go = [&](auto kern, int K, int BM, int BN) {
+        const long long units = ((max_rows + BM - 1) / BM) * ((a.n_cols + BN - 1) / BN);
+        const int grid = static_cast<int>(std::max(1LL, std::min(units, 148LL * 12)));
+        const size_t smem = sizeof(float) * static_cast<size_t>(K) * (BM + BN);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        kern<<<grid, kNT, smem, st>>>(a);
+    };
+    switch (layer) {                       // next layer: K = its IN, OUT2 = its OUT
+        case 1: go(k_gemm<12, 12, 128, 64>, 12, 128, 64); break;
+        case 2: go(k_gemm<12, 24, 128, 64>, 12, 128, 64); break;
+        case 3: go(k_gemm<24, 24, 128, 64>, 24, 128, 64); break;
+        case 4: go(k_gemm<24, 48, 64, 128>, 24, 64, 128); break;
+        case 5: go(k_gemm<48, 48, 64, 128>, 48, 64, 128); break;
+        case 6: go(k_gemm<48, 96, 64, 128>, 48, 64, 128); break;
+        default: go(k_gemm<96, 96, 64, 128>, 96, 64, 128); break;
     }
 }
 

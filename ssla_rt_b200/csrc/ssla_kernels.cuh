@@ -69,39 +69,46 @@ struct ScanArgs {
     int second;              // 1: second layer of the stage
 };
 
-// k_event modes: what produces x (the event's feature) and what follows.
-enum {
-    MODE_FIRST = 0,   // gather layer 2s -> qvg of layer 2s+1 (same events)
-    MODE_SECOND = 1,  // gather layer 2s+1 -> qvg of layer 2s+2 (next stage)
-    MODE_HEAD = 2,    // gather layer 7 -> YOLOX head
-    MODE_LAST = 3,    // gather layer 7 only (drain_n: no head)
-    MODE_ENTRY = 4    // x = stage-1 feature of a record -> qvg of layer 4
-};
-
-struct EventArgs {
+// Rows of a gather / GEMM launch: the first `count[list]` entries of a stage
+// list (list 1..4), or `n_static` chunk events (list 0).
+struct GatherArgs {
     Geo g;
     int stage;               // stage of the gathered layer
-    int mode;                // MODE_* below
-    int n_static;            // stage-0 first layer: list length (all events)
-    const int* count;        // device list lengths (index: list id)
-    int list;                // list id for count[] (1..4); 0 = all events
-    const StageEntry* E;     // iterated list (mode 1/2 and stage >= 1)
-    const uint32_t* ev_xy;
+    int second;              // 1: second layer of the stage (rows carry kprev)
+    int list;
+    int n_static;
+    const int* count;
+    const StageEntry* E;     // row entries (list > 0)
+    const uint32_t* ev_xy;   // list == 0
     const uint8_t* rflags;
-    uint8_t needq_bit;       // mode 0: reach bit of "next layer output needed"
-    const float* S_in;
-    const float* R_in;
-    float* S_out;
-    float* R_out;
-    DevLayer L;              // gathered layer (goWT, gamma, beta)
-    DevLayer N;              // next layer (qvgT, ipT)
+    uint8_t copyres_bit;     // first layer: R_next = x for events with this bit
+    const float* S_in;       // (qh, v, a) rows of the layer
+    const float* R_in;       // residual rows of the layer
+    float* X_out;            // [row][OUT] layer output (may be null)
+    float* R_next;           // copy residual of the stage's second layer
+    DevLayer L;
     DevHead head;
-    float* stage_out;        // optional [N][OUT] per chunk event
-    float* head_dec;         // mode 2: [cap4][5+ncls]
+    float* stage_out;        // optional [N][OUT] per chunk event (second layers)
+    float* slot_feat;        // drain_n: [N][96] the reference's s3_feat slot
+    float* head_dec;         // head: [cap4][5+ncls]
     float* head_raw;
-    // drain_n (stage-2 entry) path, optional
-    const float* entry_feat; // mode 4: [N][24] stage-1 features of the records
-    float* slot_feat;        // [N][96] the reference's s3_feat slot contents
+};
+
+enum { COLS_ALL = 0, COLS_VG = 1, COLS_Q = 2, COLS_RES = 3 };
+
+struct GemmArgs {
+    int list;
+    int n_static;
+    const int* count;
+    int g_cap;               // capacity of the row list
+    const StageEntry* E;     // non-null: row r reads / writes row E[r].kprev
+    const float* X;          // [*][K] input features
+    const float* W;          // qvgT [A2][K][3*OUT2] or ipT [K][OUT2]
+    int colmode;
+    int n_cols;
+    int A2;
+    float* S;                // [*][A2*3*OUT2]
+    float* R;                // [*][OUT2]
 };
 
 struct CommitArgs {
@@ -128,7 +135,10 @@ void launch_gates(cudaStream_t st, const GateArgs& a);
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a);
 void launch_compact(cudaStream_t st, const CompactArgs& a);
 void launch_scan(cudaStream_t st, int layer, const ScanArgs& a);
-void launch_event(cudaStream_t st, int layer, int mode, const EventArgs& a, int grid);
+void launch_gather(cudaStream_t st, int layer, bool head, const GatherArgs& a, int grid);
+// GEMM for next layer `layer` (its IN = K, OUT2, A2) with the given columns.
+void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_rows);
+int gemm_cols(int layer, int colmode);
 void launch_commit(cudaStream_t st, const CommitArgs& a);
 void launch_reset_preds(cudaStream_t st, const Geo& g, const PartState* parts, const DevHead& hd);
 void launch_fill_f64(cudaStream_t st, double* p, size_t n, double v);
