@@ -124,9 +124,14 @@ __host__ __device__ __forceinline__ float ssla_expf(float x) {
     return (p * ssla_pow2i(n1)) * ssla_pow2i(n2);
 }
 
-// vendor/openeva/prim/activation.h:17
+// vendor/openeva/prim/activation.h:17.  The reciprocal is IEEE round-to-
+// nearest on both sides (__frcp_rn on the device), i.e. exactly 1.0f / y.
 __host__ __device__ __forceinline__ float ssla_sigmoidf(float x) {
+#ifdef __CUDA_ARCH__
+    return __frcp_rn(1.0f + ssla_expf(-x));
+#else
     return 1.0f / (1.0f + ssla_expf(-x));
+#endif
 }
 
 }  // namespace ssla

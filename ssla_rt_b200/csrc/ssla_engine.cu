@@ -241,7 +241,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
     static const char* kScan[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
                                    "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
     static const char* kGather[8] = {"gather_L0", "gather_L1", "gather_L2", "gather_L3",
-                                     "gather_L4", "gather_L5", "gather_L6", "gather_L7_head"};
+                                     "gather_L4", "gather_L5", "gather_L6", "gather_L7"};
     static const char* kVG[8] = {"", "gemm_L1_vg", "", "gemm_L3_vg", "", "gemm_L5_vg", "", "gemm_L7_vg"};
     static const char* kQ[8] = {"", "gemm_L1_q", "", "gemm_L3_q", "", "gemm_L5_q", "", "gemm_L7_q"};
     static const char* kAll[8] = {"", "", "gemm_L2_all", "", "gemm_L4_all", "", "gemm_L6_all", ""};
@@ -267,13 +267,11 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             GatherArgs ga{};
             ga.g = g; ga.stage = s; ga.second = half; ga.count = d_count;
             ga.ev_xy = w.ev_xy.as<uint32_t>(); ga.rflags = w.rflags.as<uint8_t>();
-            ga.S_in = S_l; ga.R_in = R_l; ga.L = L[l]; ga.head = *head;
+            ga.S_in = S_l; ga.R_in = R_l; ga.L = L[l];
             ga.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
             ga.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
-            ga.head_dec = w.head_dec.as<float>();
-            ga.head_raw = w.head_raw.as<float>();
+            ga.X_out = X;
             const bool last = (l == 7);
-            ga.X_out = last ? nullptr : X;
             long long n_rows;
             if (half == 0) {
                 if (s == 0) { ga.list = 0; ga.n_static = w.n_active; }
@@ -286,11 +284,20 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
                 ga.E = w.E[s + 1].as<StageEntry>();
                 n_rows = w.cap[s + 1];
             }
-            const int grid = static_cast<int>(std::min<long long>((n_rows + kMB - 1) / kMB, 148LL * 8));
-            launch_gather(st, l, last && do_head, ga, grid);
+            launch_gather(st, l, ga, n_rows);
             check_launch("k_gather");
             prof.mark(kGather[l], 1, st);
-            if (last) break;
+            if (last) {
+                if (do_head) {
+                    HeadArgs ha{};
+                    ha.g = g; ha.count = d_count; ha.E4 = w.E[4].as<StageEntry>(); ha.X = X;
+                    ha.head = *head; ha.head_dec = w.head_dec.as<float>(); ha.head_raw = w.head_raw.as<float>();
+                    launch_head(st, ha, w.cap[4]);
+                    check_launch("k_head");
+                    prof.mark("head", 1, st);
+                }
+                break;
+            }
 
             GemmArgs gm{};
             gm.count = d_count; gm.X = X; gm.A2 = 9;

@@ -551,38 +551,43 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// k_gather: the 9-owner gather + residual + LayerNorm of one layer for a batch
-// of 32 output-producing events (layer_forward_ct, src/ssla_kernels.cpp:
-// 340-384):  out = sum over delta = 8..0 (reference patch order) of
-// goW[delta] * qh[delta], each delta an fmaf chain from 0 over the input
-// channels; + residual; LayerNorm with sequential fp64 sums
-// (layernorm.h:41-62).  goW[delta] and the batch's qh rows are staged in
-// shared memory per delta; a thread owns 2 outputs x 8 events.
-// HEAD additionally runs the YOLOX head (async_yolox.h:203-254) on the
-// stage-3 feature.
+// k_gather: the 9-owner gather + residual + LayerNorm of one layer as a
+// register-tiled FP32 GEMM over a tile of BM output-producing events
+// (layer_forward_ct, src/ssla_kernels.cpp:340-384):
+//   out[e][o] = sum over delta = 8..0 (reference patch order) of
+//               (fmaf chain over i of goW[delta][o][i] * qh[e][delta][i]),
+//   then + residual, then LayerNorm with sequential fp64 sums
+//   (layernorm.h:41-62).
+// Per delta the BM qh rows and goW[delta] are staged in shared memory; a
+// thread owns 8 events x 3 outputs (BM = 2048 * 3 / OUT: 512 / 256 / 128 /
+// 64 events for OUT = 12 / 24 / 48 / 96).  Out-of-bounds patch positions
+// contribute +0, which leaves every sum bit-identical to skipping them.
 // ---------------------------------------------------------------------------
-template <int A, int OUT, bool HEAD>
+template <int A, int OUT>
 __global__ void __launch_bounds__(kNT) k_gather(GatherArgs a) {
+    constexpr int CG = OUT / 3;                 // column groups
+    constexpr int RG = kNT / CG;                // row groups
+    constexpr int BM = RG * 8;
+    constexpr int AST = BM + 4;                 // padded stride of the transposed qh tile
     extern __shared__ __align__(16) float dsm[];
-    float* gw_s = dsm;                          // [OUT][OUT]  goWT[delta]
-    float* qh_s = gw_s + OUT * OUT;             // [OUT][kMB]
-    float* out_s = qh_s + OUT * kMB;            // [OUT][kMB]
-    float* x_s = out_s + OUT * kMB;             // [OUT][kMB]
-    float* act_s = x_s + OUT * kMB;             // HEAD: [192][kMB]
-    __shared__ int srow_s[kMB], row_s[kMB], e_s[kMB], valid_s[kMB], copy_s[kMB];
-    __shared__ int cx_s[kMB], cy_s[kMB];
-    __shared__ unsigned inb_s[kMB];
-    __shared__ double mean_s[kMB], inv_s[kMB];
-    __shared__ float res_s[kMB][24];
+    float* Bs = dsm;                            // [OUT][OUT]  goWT[delta] (i-major)
+    float* As = Bs + OUT * OUT;                 // [OUT][AST]  qh rows, transposed
+    float* Ys = As + OUT * AST;                 // [BM][OUT+1] pre-LN values
+    int* srow_s = reinterpret_cast<int*>(Ys + BM * (OUT + 1));
+    int* row_s = srow_s + BM;
+    int* e_s = row_s + BM;
+    int* flag_s = e_s + BM;                     // bit0 valid, bit1 copy residual
+    unsigned* inb_s = reinterpret_cast<unsigned*>(flag_s + BM);
     const int tid = threadIdx.x;
+    const int cgi = tid % CG, rgi = tid / CG;
     const int s = a.stage;
     const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    constexpr int OP = OUT / 2;                 // output pairs
 
-    for (int batch = blockIdx.x; batch * kMB < n_list; batch += gridDim.x) {
-        if (tid < kMB) {
-            const int r = batch * kMB + tid;
+    for (int tile = blockIdx.x; tile * BM < n_list; tile += gridDim.x) {
+        __syncthreads();
+        for (int t = tid; t < BM; t += kNT) {
+            const int r = tile * BM + t;
             int valid = 0, srow = 0, e = 0, cp = 0;
             uint32_t xy0 = 0;
             if (r < n_list) {
@@ -598,159 +603,202 @@ __global__ void __launch_bounds__(kNT) k_gather(GatherArgs a) {
             }
             const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
             unsigned m1 = 0;
+#pragma unroll
             for (int d = 0; d < 9; ++d) {
                 const int dy = 1 - d / 3, dx = 1 - d % 3;
                 if (cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl) m1 |= 1u << d;
             }
-            srow_s[tid] = srow; row_s[tid] = r; e_s[tid] = e; valid_s[tid] = valid; copy_s[tid] = cp;
-            cx_s[tid] = cx; cy_s[tid] = cy; inb_s[tid] = (A == 1) ? 1u : m1;
+            srow_s[t] = srow; row_s[t] = r; e_s[t] = e;
+            flag_s[t] = valid | (cp << 1);
+            inb_s[t] = valid ? ((A == 1) ? 1u : m1) : 0u;
         }
-        for (int t = tid; t < OUT * kMB; t += kNT) out_s[t] = 0.0f;
+        float out[8][3];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) out[i][j] = 0.0f;
         for (int d = A - 1; d >= 0; --d) {
             __syncthreads();
             const float* gsrc = a.L.goWT + static_cast<size_t>(d) * OUT * OUT;
             for (int t = tid; t < OUT * OUT / 4; t += kNT)
-                reinterpret_cast<float4*>(gw_s)[t] = __ldg(reinterpret_cast<const float4*>(gsrc) + t);
-            for (int t = tid; t < OUT * kMB; t += kNT) {
-                const int b = t % kMB, i = t / kMB;
+                reinterpret_cast<float4*>(Bs)[t] = __ldg(reinterpret_cast<const float4*>(gsrc) + t);
+            for (int t = tid; t < BM * OUT; t += kNT) {      // coalesced along each qh row
+                const int i = t % OUT, r = t / OUT;
                 float v = 0.0f;
-                if (valid_s[b] && ((inb_s[b] >> d) & 1u))
-                    v = a.S_in[(static_cast<size_t>(srow_s[b]) * A + d) * (3 * OUT) + i];
-                qh_s[i * kMB + b] = v;
+                if ((inb_s[r] >> d) & 1u)
+                    v = a.S_in[(static_cast<size_t>(srow_s[r]) * A + d) * (3 * OUT) + i];
+                As[i * AST + r] = v;
             }
             __syncthreads();
-            for (int item = tid; item < OP * kGroups; item += kNT) {
-                const int op = item % OP, g = item / OP;
-                float acc0[kEPT], acc1[kEPT];
+            float acc[8][3];
 #pragma unroll
-                for (int b = 0; b < kEPT; ++b) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) acc[i][j] = 0.0f;
 #pragma unroll 4
-                for (int i = 0; i < OUT; ++i) {
-                    const float2 w = *reinterpret_cast<const float2*>(gw_s + i * OUT + 2 * op);
-                    const float4 x0 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT);
-                    const float4 x1 = *reinterpret_cast<const float4*>(qh_s + i * kMB + g * kEPT + 4);
-                    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            for (int k = 0; k < OUT; ++k) {
+                const float4 a0 = *reinterpret_cast<const float4*>(As + k * AST + rgi * 8);
+                const float4 a1 = *reinterpret_cast<const float4*>(As + k * AST + rgi * 8 + 4);
+                const float b0 = Bs[k * OUT + cgi * 3 + 0];
+                const float b1 = Bs[k * OUT + cgi * 3 + 1];
+                const float b2 = Bs[k * OUT + cgi * 3 + 2];
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-                    for (int b = 0; b < kEPT; ++b) {
-                        acc0[b] = fmaf(w.x, xs[b], acc0[b]);
-                        acc1[b] = fmaf(w.y, xs[b], acc1[b]);
-                    }
-                }
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b) {
-                    out_s[(2 * op) * kMB + g * kEPT + b] += acc0[b];
-                    out_s[(2 * op + 1) * kMB + g * kEPT + b] += acc1[b];
+                for (int i = 0; i < 8; ++i) {
+                    acc[i][0] = fmaf(b0, av[i], acc[i][0]);
+                    acc[i][1] = fmaf(b1, av[i], acc[i][1]);
+                    acc[i][2] = fmaf(b2, av[i], acc[i][2]);
                 }
             }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) out[i][j] = out[i][j] + acc[i][j];
+        }
+        // residual (add_inplace) into the pre-LN tile
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = rgi * 8 + i;
+            if (!(flag_s[r] & 1)) continue;
+            const float* res = a.R_in + static_cast<size_t>(srow_s[r]) * OUT + cgi * 3;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) Ys[r * (OUT + 1) + cgi * 3 + j] = out[i][j] + res[j];
         }
         __syncthreads();
-        if (tid < kMB && valid_s[tid]) {
-            const int b = tid;
-            const float* r = a.R_in + static_cast<size_t>(srow_s[b]) * OUT;
+        // LayerNorm per event: sequential fp64 sums, then normalise in place
+        for (int r = tid; r < BM; r += kNT) {
+            if (!(flag_s[r] & 1)) continue;
+            float* y = Ys + r * (OUT + 1);
             double sum = 0.0;
-            for (int o = 0; o < OUT; ++o) {
-                const float v = out_s[o * kMB + b] + r[o];
-                out_s[o * kMB + b] = v;
-                sum += static_cast<double>(v);
-            }
+            for (int o = 0; o < OUT; ++o) sum += static_cast<double>(y[o]);
             const double mean = sum / static_cast<double>(OUT);
             double var = 0.0;
             for (int o = 0; o < OUT; ++o) {
-                const double dd = static_cast<double>(out_s[o * kMB + b]) - mean;
+                const double dd = static_cast<double>(y[o]) - mean;
                 var += dd * dd;
             }
             var /= static_cast<double>(OUT);
-            mean_s[b] = mean;
-            inv_s[b] = 1.0 / sqrt(var + static_cast<double>(1e-5f));
-        }
-        __syncthreads();
-        for (int t = tid; t < OUT * kMB; t += kNT) {
-            const int o = t / kMB, b = t % kMB;
-            float xv = 0.0f;
-            if (valid_s[b]) {
-                const double v = (static_cast<double>(out_s[t]) - mean_s[b]) * inv_s[b];
-                xv = static_cast<float>(v * static_cast<double>(__ldg(a.L.gamma + o)) +
-                                        static_cast<double>(__ldg(a.L.beta + o)));
+            const double inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+            for (int o = 0; o < OUT; ++o) {
+                const double v = (static_cast<double>(y[o]) - mean) * inv;
+                y[o] = static_cast<float>(v * static_cast<double>(__ldg(a.L.gamma + o)) +
+                                          static_cast<double>(__ldg(a.L.beta + o)));
             }
-            x_s[t] = xv;
         }
         __syncthreads();
-        // ---- outputs: layer feature (row-major per event), copy residual of
-        //      the stage's second layer, stage outputs, drain_n slot ----
-        for (int t = tid; t < OUT * kMB; t += kNT) {
-            const int b = t / OUT, o = t % OUT;
-            if (!valid_s[b]) continue;
-            const float xv = x_s[o * kMB + b];
-            if (a.X_out) a.X_out[static_cast<size_t>(row_s[b]) * OUT + o] = xv;
-            if (copy_s[b]) a.R_next[static_cast<size_t>(row_s[b]) * OUT + o] = xv;
-            if (a.stage_out && a.second) a.stage_out[static_cast<size_t>(e_s[b]) * OUT + o] = xv;
+        // outputs: layer feature rows, copy residual of the stage's second
+        // layer, stage outputs, drain_n slot contents
+        for (int t = tid; t < BM * OUT; t += kNT) {
+            const int o = t % OUT, r = t / OUT;
+            const int f = flag_s[r];
+            if (!(f & 1)) continue;
+            const float xv = Ys[r * (OUT + 1) + o];
+            if (a.X_out) a.X_out[static_cast<size_t>(row_s[r]) * OUT + o] = xv;
+            if (f & 2) a.R_next[static_cast<size_t>(row_s[r]) * OUT + o] = xv;
+            if (a.stage_out && a.second) a.stage_out[static_cast<size_t>(e_s[r]) * OUT + o] = xv;
             if (a.slot_feat) {
-                a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + o] = xv;
-                if (OUT == 48) a.slot_feat[static_cast<size_t>(e_s[b]) * 96 + 48 + o] = 0.0f;
+                a.slot_feat[static_cast<size_t>(e_s[r]) * 96 + o] = xv;
+                if (OUT == 48) a.slot_feat[static_cast<size_t>(e_s[r]) * 96 + 48 + o] = 0.0f;
             }
         }
-        if (HEAD) {
-            // cls / reg 1x1 convs (BN folded, bias-first accumulation) + SiLU
-            for (int item = tid; item < 192 * kGroups; item += kNT) {
-                const int j = item % 192, g = item / 192;
-                const int jo = j % 96;
-                const float* Wt = (j < 96) ? a.head.cls_convT : a.head.reg_convT;
-                const float bias = __ldg(((j < 96) ? a.head.cls_conv_b : a.head.reg_conv_b) + jo);
-                float acc[kEPT];
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b) acc[b] = bias;
-#pragma unroll 4
-                for (int i = 0; i < 96; ++i) {
-                    const float wv = __ldg(Wt + i * 96 + jo);
-                    const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
-                    const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
-                    acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
-                    acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
-                    acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
-                    acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
-                }
-#pragma unroll
-                for (int b = 0; b < kEPT; ++b)
-                    act_s[j * kMB + g * kEPT + b] = acc[b] * ssla_sigmoidf(acc[b]);
-            }
-            __syncthreads();
-            const int ncls = a.g.ncls, cols = 5 + ncls;
-            for (int item = tid; item < kMB * cols; item += kNT) {
-                const int b = item % kMB, r = item / kMB;
-                if (!valid_s[b]) continue;
-                float acc;
-                if (r < 4) {
-                    acc = __ldg(a.head.reg_pred_b + r);
-                    for (int i = 0; i < 96; ++i)
-                        acc = fmaf(__ldg(a.head.reg_predT + i * 4 + r), act_s[(96 + i) * kMB + b], acc);
-                } else if (r == 4) {
-                    acc = __ldg(a.head.obj_pred_b);
-                    for (int i = 0; i < 96; ++i)
-                        acc = fmaf(__ldg(a.head.obj_predT + i), act_s[(96 + i) * kMB + b], acc);
-                } else {
-                    const int c = r - 5;
-                    acc = __ldg(a.head.cls_pred_b + c);
-                    for (int i = 0; i < 96; ++i)
-                        acc = fmaf(__ldg(a.head.cls_predT + i * ncls + c), act_s[i * kMB + b], acc);
-                }
-                res_s[b][r] = acc;
-            }
-            __syncthreads();
-            for (int item = tid; item < kMB * cols; item += kNT) {
-                const int b = item % kMB, r = item / kMB;
-                if (!valid_s[b]) continue;
-                const float v = res_s[b][r];
-                float d;
-                if (r == 0) d = (v + static_cast<float>(cx_s[b])) * static_cast<float>(a.g.stride_w);
-                else if (r == 1) d = (v + static_cast<float>(cy_s[b])) * static_cast<float>(a.g.stride_h);
-                else if (r == 2) d = ssla_expf(v) * static_cast<float>(a.g.stride_w);
-                else if (r == 3) d = ssla_expf(v) * static_cast<float>(a.g.stride_h);
-                else d = v;
-                a.head_dec[static_cast<size_t>(row_s[b]) * cols + r] = d;
-                a.head_raw[static_cast<size_t>(row_s[b]) * cols + r] = v;
-            }
+    }
+}
+
+template <int OUT>
+constexpr size_t gather_smem_bytes() {
+    constexpr int BM = (kNT / (OUT / 3)) * 8;
+    return sizeof(float) * (static_cast<size_t>(OUT) * OUT + static_cast<size_t>(OUT) * (BM + 4) +
+                            static_cast<size_t>(BM) * (OUT + 1)) + sizeof(int) * 5 * BM;
+}
+
+// ---------------------------------------------------------------------------
+// k_head: YOLOX head on the stage-3 features of head events
+// (decode_yolox_cell_ct, vendor/openeva/heads/async_yolox.h:203-254):
+// cls / reg 1x1 convs with BN folded (bias-first fmaf chains) + SiLU, then
+// the cls (ncls), reg (4) and obj (1) predictions, then the box decode.
+// 32 events per batch; X holds the features in E_4 row order.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
+    __shared__ __align__(16) float x_s[96 * kMB];
+    __shared__ __align__(16) float act_s[192 * kMB];
+    __shared__ float res_s[kMB][24];
+    __shared__ int valid_s[kMB], cx_s[kMB], cy_s[kMB];
+    const int tid = threadIdx.x;
+    const int n = min(a.count[4], a.g.cap[4]);
+    const int ncls = a.g.ncls, cols = 5 + ncls;
+    for (int batch = blockIdx.x; batch * kMB < n; batch += gridDim.x) {
+        __syncthreads();
+        if (tid < kMB) {
+            const int r = batch * kMB + tid;
+            valid_s[tid] = r < n;
+            const uint32_t xy0 = (r < n) ? a.E4[r].xy0 : 0u;
+            cx_s[tid] = static_cast<int>(xy0 & 0xFFFFu) >> 3;
+            cy_s[tid] = static_cast<int>(xy0 >> 16) >> 3;
+        }
+        for (int t = tid; t < 96 * kMB; t += kNT) {
+            const int i = t % 96, b = t / 96;
+            const int r = batch * kMB + b;
+            x_s[i * kMB + b] = (r < n) ? a.X[static_cast<size_t>(r) * 96 + i] : 0.0f;
         }
         __syncthreads();
+        for (int item = tid; item < 192 * kGroups; item += kNT) {
+            const int j = item % 192, g = item / 192;
+            const int jo = j % 96;
+            const float* Wt = (j < 96) ? a.head.cls_convT : a.head.reg_convT;
+            const float bias = __ldg(((j < 96) ? a.head.cls_conv_b : a.head.reg_conv_b) + jo);
+            float acc[kEPT];
+#pragma unroll
+            for (int b = 0; b < kEPT; ++b) acc[b] = bias;
+#pragma unroll 4
+            for (int i = 0; i < 96; ++i) {
+                const float wv = __ldg(Wt + i * 96 + jo);
+                const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
+                const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
+                acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
+                acc[2] = fmaf(wv, x0.z, acc[2]); acc[3] = fmaf(wv, x0.w, acc[3]);
+                acc[4] = fmaf(wv, x1.x, acc[4]); acc[5] = fmaf(wv, x1.y, acc[5]);
+                acc[6] = fmaf(wv, x1.z, acc[6]); acc[7] = fmaf(wv, x1.w, acc[7]);
+            }
+#pragma unroll
+            for (int b = 0; b < kEPT; ++b)
+                act_s[j * kMB + g * kEPT + b] = acc[b] * ssla_sigmoidf(acc[b]);
+        }
+        __syncthreads();
+        for (int item = tid; item < kMB * cols; item += kNT) {
+            const int b = item % kMB, r = item / kMB;
+            if (!valid_s[b]) continue;
+            float acc;
+            if (r < 4) {
+                acc = __ldg(a.head.reg_pred_b + r);
+                for (int i = 0; i < 96; ++i)
+                    acc = fmaf(__ldg(a.head.reg_predT + i * 4 + r), act_s[(96 + i) * kMB + b], acc);
+            } else if (r == 4) {
+                acc = __ldg(a.head.obj_pred_b);
+                for (int i = 0; i < 96; ++i)
+                    acc = fmaf(__ldg(a.head.obj_predT + i), act_s[(96 + i) * kMB + b], acc);
+            } else {
+                const int c = r - 5;
+                acc = __ldg(a.head.cls_pred_b + c);
+                for (int i = 0; i < 96; ++i)
+                    acc = fmaf(__ldg(a.head.cls_predT + i * ncls + c), act_s[i * kMB + b], acc);
+            }
+            res_s[b][r] = acc;
+        }
+        __syncthreads();
+        for (int item = tid; item < kMB * cols; item += kNT) {
+            const int b = item % kMB, r = item / kMB;
+            if (!valid_s[b]) continue;
+            const int row = batch * kMB + b;
+            const float v = res_s[b][r];
+            float d;
+            if (r == 0) d = (v + static_cast<float>(cx_s[b])) * static_cast<float>(a.g.stride_w);
+            else if (r == 1) d = (v + static_cast<float>(cy_s[b])) * static_cast<float>(a.g.stride_h);
+            else if (r == 2) d = ssla_expf(v) * static_cast<float>(a.g.stride_w);
+            else if (r == 3) d = ssla_expf(v) * static_cast<float>(a.g.stride_h);
+            else d = v;
+            a.head_dec[static_cast<size_t>(row) * cols + r] = d;
+            a.head_raw[static_cast<size_t>(row) * cols + r] = v;
+        }
     }
 }
 
@@ -1072,24 +1120,25 @@ void launch_scan(cudaStream_t st, int layer, const ScanArgs& a) {
     }
 }
 
-void launch_gather(cudaStream_t st, int layer, bool head, const GatherArgs& a, int grid) {
-    if (grid < 1) grid = 1;
-    auto go = [&](auto kern, int OUT, int extra) {
-        const size_t smem = sizeof(float) * (static_cast<size_t>(OUT) * OUT + 3 * OUT * kMB + extra);
+void launch_gather(cudaStream_t st, int layer, const GatherArgs& a, long long max_rows) {
+    auto go = [&](auto kern, int OUT, size_t smem) {
+        const int BM = (kNT / (OUT / 3)) * 8;
+        const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + BM - 1) / BM, 148LL * 8)));
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         kern<<<grid, kNT, smem, st>>>(a);
     };
     switch (layer) {
-        case 0: go(k_gather<1, 12, false>, 12, 0); break;
-        case 1: go(k_gather<9, 12, false>, 12, 0); break;
-        case 2: case 3: go(k_gather<9, 24, false>, 24, 0); break;
-        case 4: case 5: go(k_gather<9, 48, false>, 48, 0); break;
-        case 6: go(k_gather<9, 96, false>, 96, 0); break;
-        default:
-            if (head) go(k_gather<9, 96, true>, 96, 192 * kMB);
-            else go(k_gather<9, 96, false>, 96, 0);
-            break;
+        case 0: go(k_gather<1, 12>, 12, gather_smem_bytes<12>()); break;
+        case 1: go(k_gather<9, 12>, 12, gather_smem_bytes<12>()); break;
+        case 2: case 3: go(k_gather<9, 24>, 24, gather_smem_bytes<24>()); break;
+        case 4: case 5: go(k_gather<9, 48>, 48, gather_smem_bytes<48>()); break;
+        default: go(k_gather<9, 96>, 96, gather_smem_bytes<96>()); break;
     }
+}
+
+void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows) {
+    const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + kMB - 1) / kMB, 148LL * 8)));
+    k_head<<<grid, kNT, 0, st>>>(a);
 }
 
 int gemm_cols(int layer, int colmode) {

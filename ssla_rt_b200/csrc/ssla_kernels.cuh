@@ -87,10 +87,17 @@ struct GatherArgs {
     float* X_out;            // [row][OUT] layer output (may be null)
     float* R_next;           // copy residual of the stage's second layer
     DevLayer L;
-    DevHead head;
     float* stage_out;        // optional [N][OUT] per chunk event (second layers)
     float* slot_feat;        // drain_n: [N][96] the reference's s3_feat slot
-    float* head_dec;         // head: [cap4][5+ncls]
+};
+
+struct HeadArgs {
+    Geo g;
+    const int* count;        // count[4] = head events
+    const StageEntry* E4;
+    const float* X;          // [row][96] stage-3 features in E_4 order
+    DevHead head;
+    float* head_dec;         // [cap4][5+ncls]
     float* head_raw;
 };
 
@@ -135,7 +142,8 @@ void launch_gates(cudaStream_t st, const GateArgs& a);
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a);
 void launch_compact(cudaStream_t st, const CompactArgs& a);
 void launch_scan(cudaStream_t st, int layer, const ScanArgs& a);
-void launch_gather(cudaStream_t st, int layer, bool head, const GatherArgs& a, int grid);
+void launch_gather(cudaStream_t st, int layer, const GatherArgs& a, long long max_rows);
+void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows);
 // GEMM for next layer `layer` (its IN = K, OUT2, A2) with the given columns.
 void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_rows);
 int gemm_cols(int layer, int colmode);
