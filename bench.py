@@ -93,9 +93,10 @@ def total_macs(macs: dict) -> int:
 def phase_flops(macs: dict, name: str) -> float:
     """Algorithmic FLOPs of one engine phase (2 per MAC); 0 for integer or
     scan phases."""
-    if name.startswith("gather_L"):
-        l = int(name[8])
-        return 2.0 * (macs[l]["gather"] + (macs["head"] if l == 7 else 0))
+    if name.startswith("contrib_L"):
+        return 2.0 * macs[int(name[9])]["gather"]
+    if name == "head":
+        return 2.0 * macs["head"]
     if name.startswith("gemm_L"):
         l = int(name[6])
         kind = name.split("_")[-1]

@@ -162,7 +162,7 @@ struct Workspace {
     int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, n_active = 0;
     long long cap_part[5] = {0}, cap[5] = {0};
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
-    DevBuf tl[4], tl_cnt[4], S_A, S_B, R_A, R_B, X, head_dec, head_raw, feat, slot_feat, stamps;
+    DevBuf tl[4], tl_cnt[4], S_A, S_B, R_A, R_B, X, C, head_dec, head_raw, feat, slot_feat, stamps;
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -213,6 +213,12 @@ struct Workspace {
         }
         S_A.alloc(sa * 4); S_B.alloc(sb * 4); R_A.alloc(ra * 4); R_B.alloc(rb * 4);
         X.alloc(ra * 4);                        // layer outputs, [rows][C_s]
+        size_t cmax = 0;                        // contributions, [rows][A][C_s]
+        for (int s = s_first; s < 4; ++s) {
+            const size_t k = static_cast<size_t>(std::max<long long>(cap[s], 1));
+            cmax = std::max(cmax, k * 9 * chans(s));
+        }
+        C.alloc(cmax * 4);
         const int cols = 5 + g.ncls;
         head_dec.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
         head_raw.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
@@ -240,8 +246,10 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
                 const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof) {
     static const char* kScan[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
                                    "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
-    static const char* kGather[8] = {"gather_L0", "gather_L1", "gather_L2", "gather_L3",
-                                     "gather_L4", "gather_L5", "gather_L6", "gather_L7"};
+    static const char* kContrib[8] = {"contrib_L0", "contrib_L1", "contrib_L2", "contrib_L3",
+                                      "contrib_L4", "contrib_L5", "contrib_L6", "contrib_L7"};
+    static const char* kGather[8] = {"ln_L0", "ln_L1", "ln_L2", "ln_L3",
+                                     "ln_L4", "ln_L5", "ln_L6", "ln_L7"};
     static const char* kVG[8] = {"", "gemm_L1_vg", "", "gemm_L3_vg", "", "gemm_L5_vg", "", "gemm_L7_vg"};
     static const char* kQ[8] = {"", "gemm_L1_q", "", "gemm_L3_q", "", "gemm_L5_q", "", "gemm_L7_q"};
     static const char* kAll[8] = {"", "", "gemm_L2_all", "", "gemm_L4_all", "", "gemm_L6_all", ""};
@@ -264,28 +272,34 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             check_launch("k_scan");
             prof.mark(kScan[l], 1, st);
 
-            GatherArgs ga{};
-            ga.g = g; ga.stage = s; ga.second = half; ga.count = d_count;
-            ga.ev_xy = w.ev_xy.as<uint32_t>(); ga.rflags = w.rflags.as<uint8_t>();
-            ga.S_in = S_l; ga.R_in = R_l; ga.L = L[l];
-            ga.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
-            ga.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
-            ga.X_out = X;
             const bool last = (l == 7);
+            ContribArgs ca{};
+            LnArgs la{};
+            ca.g = la.g = g; ca.stage = la.stage = s; ca.second = la.second = half;
+            ca.count = la.count = d_count;
+            ca.ev_xy = la.ev_xy = w.ev_xy.as<uint32_t>();
+            ca.rflags = la.rflags = w.rflags.as<uint8_t>();
+            ca.S = S_l; ca.goWT = L[l].goWT; ca.C = w.C.as<float>();
+            la.C = w.C.as<float>(); la.R_in = R_l; la.L = L[l]; la.X_out = X;
+            la.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
+            la.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
             long long n_rows;
             if (half == 0) {
-                if (s == 0) { ga.list = 0; ga.n_static = w.n_active; }
-                else { ga.list = s; ga.E = w.E[s].as<StageEntry>(); }
+                if (s == 0) { ca.list = la.list = 0; ca.n_static = la.n_static = w.n_active; }
+                else { ca.list = la.list = s; ca.E = la.E = w.E[s].as<StageEntry>(); }
                 n_rows = n_s;
-                ga.copyres_bit = static_cast<uint8_t>(F_R1 << s);      // R_{s+1}
-                ga.R_next = w.R_B.as<float>();
+                la.copyres_bit = static_cast<uint8_t>(F_R1 << s);      // R_{s+1}
+                la.R_next = w.R_B.as<float>();
             } else {
-                ga.list = s + 1;
-                ga.E = w.E[s + 1].as<StageEntry>();
+                ca.list = la.list = s + 1;
+                ca.E = la.E = w.E[s + 1].as<StageEntry>();
                 n_rows = w.cap[s + 1];
             }
-            launch_gather(st, l, ga, n_rows);
-            check_launch("k_gather");
+            launch_contrib(st, l, ca, n_rows);
+            check_launch("k_contrib");
+            prof.mark(kContrib[l], 1, st);
+            launch_ln(st, l, la, n_rows);
+            check_launch("k_ln");
             prof.mark(kGather[l], 1, st);
             if (last) {
                 if (do_head) {

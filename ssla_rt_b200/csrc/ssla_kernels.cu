@@ -8,9 +8,10 @@
 //                 layer-0 qvg/residual, one warp per (partition, s3 block)
 //   k_compact_*   stream-ordered stage lists E_1..E_4
 //   k_filter(s1..s3)
-//   per layer l:  k_scan (cell-major LRU update), k_gather (event-major
-//                 9-owner gather / residual / LayerNorm, or the head), then
-//                 k_gemm (the next layer's qvg as a tiled FP32 GEMM)
+//   per layer l:  k_scan (cell-major LRU update), k_contrib (the 9-owner goW
+//                 contributions as a tiled FP32 GEMM per patch position),
+//                 k_ln (ordered contribution sum + residual + LayerNorm),
+//                 then k_gemm (the next layer's qvg) or k_head
 //   k_commit      last head write per s3 cell -> predictions + version
 // Reference behaviour each kernel reproduces is cited inline.
 #include "ssla_kernels.cuh"
@@ -551,164 +552,218 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// k_gather: the 9-owner gather + residual + LayerNorm of one layer as a
-// register-tiled FP32 GEMM over a tile of BM output-producing events
-// (layer_forward_ct, src/ssla_kernels.cpp:340-384):
-//   out[e][o] = sum over delta = 8..0 (reference patch order) of
-//               (fmaf chain over i of goW[delta][o][i] * qh[e][delta][i]),
-//   then + residual, then LayerNorm with sequential fp64 sums
-//   (layernorm.h:41-62).
-// Per delta the BM qh rows and goW[delta] are staged in shared memory; a
-// thread owns 8 events x 3 outputs (BM = 2048 * 3 / OUT: 512 / 256 / 128 /
-// 64 events for OUT = 12 / 24 / 48 / 96).  Out-of-bounds patch positions
-// contribute +0, which leaves every sum bit-identical to skipping them.
+// Gather, phase 1 -- k_contrib: per patch position delta, the goW
+// contribution of every output-producing event (layer_forward_ct,
+// src/ssla_kernels.cpp:340-351, matvec_accum_ct linear.h:92-101):
+//   C[row][delta][o] = fmaf chain over i of goW[delta][o][i] * qh[row][delta][i]
+// A register-tiled FP32 GEMM per (delta, tile of BM rows): the tile's qh
+// vectors (one contiguous S row segment each) and goW[delta] are staged in
+// shared memory with batched 16-byte loads; a thread owns 8 rows x 3 outputs.
+// Rows whose patch position is out of bounds are skipped (never read).
 // ---------------------------------------------------------------------------
 template <int A, int OUT>
-__global__ void __launch_bounds__(kNT) k_gather(GatherArgs a) {
-    constexpr int CG = OUT / 3;                 // column groups
-    constexpr int RG = kNT / CG;                // row groups
-    constexpr int BM = RG * 8;
-    constexpr int AST = BM + 4;                 // padded stride of the transposed qh tile
+struct ContribShape {
+    static constexpr int CG = OUT / 3;           // column groups
+    static constexpr int RG = kNT / CG;          // row groups
+    static constexpr int BM = RG * 8;            // rows per tile
+    static constexpr int BMP = BM + 4;           // padded transposed stride
+    static constexpr size_t smem = sizeof(float) * (static_cast<size_t>(OUT) * OUT +
+                                                    static_cast<size_t>(OUT) * BMP) +
+                                   sizeof(int) * BM;
+};
+
+template <int A, int OUT>
+__global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
+    using Sh = ContribShape<A, OUT>;
+    constexpr int BM = Sh::BM, BMP = Sh::BMP, CG = Sh::CG;
+    constexpr int Q4 = OUT / 4;                  // float4 per qh row
+    constexpr int NA = (BM * Q4 + kNT - 1) / kNT;
+    constexpr int NB = (OUT * OUT / 4 + kNT - 1) / kNT;
     extern __shared__ __align__(16) float dsm[];
-    float* Bs = dsm;                            // [OUT][OUT]  goWT[delta] (i-major)
-    float* As = Bs + OUT * OUT;                 // [OUT][AST]  qh rows, transposed
-    float* Ys = As + OUT * AST;                 // [BM][OUT+1] pre-LN values
-    int* srow_s = reinterpret_cast<int*>(Ys + BM * (OUT + 1));
-    int* row_s = srow_s + BM;
-    int* e_s = row_s + BM;
-    int* flag_s = e_s + BM;                     // bit0 valid, bit1 copy residual
-    unsigned* inb_s = reinterpret_cast<unsigned*>(flag_s + BM);
+    float* Bs = dsm;                             // [OUT][OUT]  goWT[delta] (i-major)
+    float* As = Bs + OUT * OUT;                  // [OUT][BMP]  qh rows, transposed
+    int* srow_s = reinterpret_cast<int*>(As + OUT * BMP);   // S row or -1
     const int tid = threadIdx.x;
-    const int cgi = tid % CG, rgi = tid / CG;
+    const int cg = tid % CG, rg = tid / CG;
     const int s = a.stage;
     const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
+    const int n_tiles = (n_list + BM - 1) / BM;
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-
-    for (int tile = blockIdx.x; tile * BM < n_list; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < n_tiles * A; unit += gridDim.x) {
+        const int d = (A - 1) - unit % A, tile = unit / A;
+        const int dy = 1 - d / 3, dx = 1 - d % 3;
         __syncthreads();
         for (int t = tid; t < BM; t += kNT) {
             const int r = tile * BM + t;
-            int valid = 0, srow = 0, e = 0, cp = 0;
-            uint32_t xy0 = 0;
+            int srow = -1;
             if (r < n_list) {
+                uint32_t xy0;
+                int sr;
+                bool ok;
                 if (a.list == 0) {
-                    e = r; srow = r; xy0 = a.ev_xy[r];
-                    valid = (a.rflags[r] & F_VALID) ? 1 : 0;
+                    xy0 = a.ev_xy[r]; sr = r; ok = (a.rflags[r] & F_VALID) != 0;
                 } else {
                     const StageEntry se = a.E[r];
-                    e = se.e; xy0 = se.xy0; valid = 1;
-                    srow = a.second ? se.kprev : r;
+                    xy0 = se.xy0; sr = a.second ? se.kprev : r; ok = true;
                 }
-                if (valid && a.copyres_bit) cp = (a.rflags[e] & a.copyres_bit) ? 1 : 0;
+                const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
+                if (A == 9) ok = ok && cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl;
+                if (ok) srow = sr;
             }
-            const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
-            unsigned m1 = 0;
-#pragma unroll
-            for (int d = 0; d < 9; ++d) {
-                const int dy = 1 - d / 3, dx = 1 - d % 3;
-                if (cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl) m1 |= 1u << d;
-            }
-            srow_s[t] = srow; row_s[t] = r; e_s[t] = e;
-            flag_s[t] = valid | (cp << 1);
-            inb_s[t] = valid ? ((A == 1) ? 1u : m1) : 0u;
+            srow_s[t] = srow;
         }
-        float out[8][3];
+        __syncthreads();
+        {   // batched loads: goW[delta] and the tile's qh rows
+            const float4* gsrc = reinterpret_cast<const float4*>(a.goWT + static_cast<size_t>(d) * OUT * OUT);
+            float4 bv[NB];
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int t = tid + q * kNT;
+                if (t < OUT * OUT / 4) bv[q] = __ldg(gsrc + t);
+            }
+            float4 av[NA];
+#pragma unroll
+            for (int q = 0; q < NA; ++q) {
+                const int t = tid + q * kNT;
+                const int r = t % BM, k4 = t / BM;
+                av[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t < BM * Q4 && srow_s[r] >= 0)
+                    av[q] = *reinterpret_cast<const float4*>(
+                        a.S + (static_cast<size_t>(srow_s[r]) * A + d) * (3 * OUT) + 4 * k4);
+            }
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int t = tid + q * kNT;
+                if (t < OUT * OUT / 4) reinterpret_cast<float4*>(Bs)[t] = bv[q];
+            }
+#pragma unroll
+            for (int q = 0; q < NA; ++q) {
+                const int t = tid + q * kNT;
+                if (t < BM * Q4) {
+                    const int r = t % BM, k4 = t / BM;
+                    As[(4 * k4 + 0) * BMP + r] = av[q].x;
+                    As[(4 * k4 + 1) * BMP + r] = av[q].y;
+                    As[(4 * k4 + 2) * BMP + r] = av[q].z;
+                    As[(4 * k4 + 3) * BMP + r] = av[q].w;
+                }
+            }
+        }
+        __syncthreads();
+        float acc[8][3];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 3; ++j) out[i][j] = 0.0f;
-        for (int d = A - 1; d >= 0; --d) {
-            __syncthreads();
-            const float* gsrc = a.L.goWT + static_cast<size_t>(d) * OUT * OUT;
-            for (int t = tid; t < OUT * OUT / 4; t += kNT)
-                reinterpret_cast<float4*>(Bs)[t] = __ldg(reinterpret_cast<const float4*>(gsrc) + t);
-            for (int t = tid; t < BM * OUT; t += kNT) {      // coalesced along each qh row
-                const int i = t % OUT, r = t / OUT;
-                float v = 0.0f;
-                if ((inb_s[r] >> d) & 1u)
-                    v = a.S_in[(static_cast<size_t>(srow_s[r]) * A + d) * (3 * OUT) + i];
-                As[i * AST + r] = v;
-            }
-            __syncthreads();
-            float acc[8][3];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 3; ++j) acc[i][j] = 0.0f;
+            for (int j = 0; j < 3; ++j) acc[i][j] = 0.0f;
 #pragma unroll 4
-            for (int k = 0; k < OUT; ++k) {
-                const float4 a0 = *reinterpret_cast<const float4*>(As + k * AST + rgi * 8);
-                const float4 a1 = *reinterpret_cast<const float4*>(As + k * AST + rgi * 8 + 4);
-                const float b0 = Bs[k * OUT + cgi * 3 + 0];
-                const float b1 = Bs[k * OUT + cgi * 3 + 1];
-                const float b2 = Bs[k * OUT + cgi * 3 + 2];
-                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        for (int k = 0; k < OUT; ++k) {
+            const float4 a0 = *reinterpret_cast<const float4*>(As + k * BMP + rg * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(As + k * BMP + rg * 8 + 4);
+            const float b0 = Bs[k * OUT + cg * 3 + 0];
+            const float b1 = Bs[k * OUT + cg * 3 + 1];
+            const float b2 = Bs[k * OUT + cg * 3 + 2];
+            const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    acc[i][0] = fmaf(b0, av[i], acc[i][0]);
-                    acc[i][1] = fmaf(b1, av[i], acc[i][1]);
-                    acc[i][2] = fmaf(b2, av[i], acc[i][2]);
-                }
+            for (int i = 0; i < 8; ++i) {
+                acc[i][0] = fmaf(b0, x[i], acc[i][0]);
+                acc[i][1] = fmaf(b1, x[i], acc[i][1]);
+                acc[i][2] = fmaf(b2, x[i], acc[i][2]);
             }
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 3; ++j) out[i][j] = out[i][j] + acc[i][j];
         }
-        // residual (add_inplace) into the pre-LN tile
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int r = rgi * 8 + i;
-            if (!(flag_s[r] & 1)) continue;
-            const float* res = a.R_in + static_cast<size_t>(srow_s[r]) * OUT + cgi * 3;
-#pragma unroll
-            for (int j = 0; j < 3; ++j) Ys[r * (OUT + 1) + cgi * 3 + j] = out[i][j] + res[j];
+            const int rr = rg * 8 + i;
+            if (srow_s[rr] < 0) continue;
+            float* c = a.C + (static_cast<size_t>(tile * BM + rr) * A + d) * OUT + cg * 3;
+            c[0] = acc[i][0]; c[1] = acc[i][1]; c[2] = acc[i][2];
         }
-        __syncthreads();
-        // LayerNorm per event: sequential fp64 sums, then normalise in place
-        for (int r = tid; r < BM; r += kNT) {
-            if (!(flag_s[r] & 1)) continue;
-            float* y = Ys + r * (OUT + 1);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Gather, phase 2 -- k_ln: one warp per output-producing event:
+//   out[o] = ((0 + C[8][o]) + C[7][o]) + ... + C[0][o]   (in-bounds only,
+//             the reference's patch order), + residual (add_inplace), then
+//   LayerNorm: mean / variance as sequential fp64 sums by lane 0
+//   (layernorm.h:41-62), normalise with gamma / beta.
+// Writes the layer output row, the copy residual of the stage's second
+// layer, per-event stage outputs and the drain_n slot contents.
+// ---------------------------------------------------------------------------
+template <int A, int OUT>
+__global__ void __launch_bounds__(kNT) k_ln(LnArgs a) {
+    constexpr int CPL = (OUT + 31) / 32;
+    __shared__ float ybuf[kNT / 32][OUT];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int s = a.stage;
+    const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
+    const int Wl = a.g.W[s], Hl = a.g.H[s];
+    float* y = ybuf[warp];
+    for (int r = blockIdx.x * (kNT / 32) + warp; r < n_list; r += gridDim.x * (kNT / 32)) {
+        uint32_t xy0;
+        int sr, e;
+        bool ok;
+        if (a.list == 0) {
+            xy0 = a.ev_xy[r]; sr = r; e = r; ok = (a.rflags[r] & F_VALID) != 0;
+        } else {
+            const StageEntry se = a.E[r];
+            xy0 = se.xy0; sr = a.second ? se.kprev : r; e = se.e; ok = true;
+        }
+        if (!ok) continue;
+        const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
+        float v[CPL];
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) v[c] = 0.0f;
+        for (int d = A - 1; d >= 0; --d) {
+            if (A == 9) {
+                const int dy = 1 - d / 3, dx = 1 - d % 3;
+                if (cx + dx < 0 || cx + dx >= Wl || cy + dy < 0 || cy + dy >= Hl) continue;
+            }
+            const float* c_row = a.C + (static_cast<size_t>(r) * A + d) * OUT;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) {
+                const int o = lane + 32 * c;
+                if (o < OUT) v[c] = v[c] + c_row[o];
+            }
+        }
+        const float* res = a.R_in + static_cast<size_t>(sr) * OUT;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const int o = lane + 32 * c;
+            if (o < OUT) y[o] = v[c] + res[o];
+        }
+        __syncwarp();
+        double mean = 0.0, inv = 0.0;
+        if (lane == 0) {
             double sum = 0.0;
             for (int o = 0; o < OUT; ++o) sum += static_cast<double>(y[o]);
-            const double mean = sum / static_cast<double>(OUT);
+            mean = sum / static_cast<double>(OUT);
             double var = 0.0;
             for (int o = 0; o < OUT; ++o) {
                 const double dd = static_cast<double>(y[o]) - mean;
                 var += dd * dd;
             }
             var /= static_cast<double>(OUT);
-            const double inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
-            for (int o = 0; o < OUT; ++o) {
-                const double v = (static_cast<double>(y[o]) - mean) * inv;
-                y[o] = static_cast<float>(v * static_cast<double>(__ldg(a.L.gamma + o)) +
-                                          static_cast<double>(__ldg(a.L.beta + o)));
-            }
+            inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
         }
-        __syncthreads();
-        // outputs: layer feature rows, copy residual of the stage's second
-        // layer, stage outputs, drain_n slot contents
-        for (int t = tid; t < BM * OUT; t += kNT) {
-            const int o = t % OUT, r = t / OUT;
-            const int f = flag_s[r];
-            if (!(f & 1)) continue;
-            const float xv = Ys[r * (OUT + 1) + o];
-            if (a.X_out) a.X_out[static_cast<size_t>(row_s[r]) * OUT + o] = xv;
-            if (f & 2) a.R_next[static_cast<size_t>(row_s[r]) * OUT + o] = xv;
-            if (a.stage_out && a.second) a.stage_out[static_cast<size_t>(e_s[r]) * OUT + o] = xv;
+        mean = __shfl_sync(0xffffffffu, mean, 0);
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        const bool cp = a.copyres_bit && (a.rflags[e] & a.copyres_bit);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const int o = lane + 32 * c;
+            if (o >= OUT) continue;
+            const double t = (static_cast<double>(y[o]) - mean) * inv;
+            const float xv = static_cast<float>(t * static_cast<double>(__ldg(a.L.gamma + o)) +
+                                                static_cast<double>(__ldg(a.L.beta + o)));
+            if (a.X_out) a.X_out[static_cast<size_t>(r) * OUT + o] = xv;
+            if (cp) a.R_next[static_cast<size_t>(r) * OUT + o] = xv;
+            if (a.stage_out && a.second) a.stage_out[static_cast<size_t>(e) * OUT + o] = xv;
             if (a.slot_feat) {
-                a.slot_feat[static_cast<size_t>(e_s[r]) * 96 + o] = xv;
-                if (OUT == 48) a.slot_feat[static_cast<size_t>(e_s[r]) * 96 + 48 + o] = 0.0f;
+                a.slot_feat[static_cast<size_t>(e) * 96 + o] = xv;
+                if (OUT == 48) a.slot_feat[static_cast<size_t>(e) * 96 + 48 + o] = 0.0f;
             }
         }
+        __syncwarp();
     }
-}
-
-template <int OUT>
-constexpr size_t gather_smem_bytes() {
-    constexpr int BM = (kNT / (OUT / 3)) * 8;
-    return sizeof(float) * (static_cast<size_t>(OUT) * OUT + static_cast<size_t>(OUT) * (BM + 4) +
-                            static_cast<size_t>(BM) * (OUT + 1)) + sizeof(int) * 5 * BM;
 }
 
 // ---------------------------------------------------------------------------
@@ -806,31 +861,38 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
 // k_gemm: next-layer fused qvg (matvec_ct<IN,3*OUT>, linear.h:80-90) for a set
 // of events and a set of weight columns, as a register-tiled FP32 GEMM:
 //   Y[row][col] = sum_k X[row][k] * W[k][col]   (fmaf chain, k ascending)
-// Columns (per patch position delta of the next layer, J2 = 3*OUT2):
-//   COLS_ALL  every q, v, g column          (first layers: output always used)
-//   COLS_VG   the v and g columns           (second layers: every event)
-//   COLS_Q    the q columns                 (second layers: events whose
-//                                            output is consumed)
-//   COLS_RES  input_proj (the residual, matvec_ct<IN,OUT>)
+// Columns are ordered part-major (all q, then all v, then all g; inside a
+// part by patch position delta, then output channel), so a warp's columns
+// share one part and the sigmoid of the g part is warp-uniform:
+//   COLS_ALL  q, v, g      (first layers: every output is consumed)
+//   COLS_VG   v, g         (second layers: every event)
+//   COLS_Q    q            (second layers: events whose output is consumed)
+//   COLS_RES  input_proj   (the residual, matvec_ct<IN,OUT>)
 // g columns are stored as sigmoid(g).  A CTA computes a BM x BN tile with the
-// whole K extent of X and W staged in shared memory; a thread owns 8 rows x
-// 4 columns.  grid-stride over (row tile, column tile).
+// whole K extent of X and W staged in shared memory (batched 16-byte loads);
+// a thread owns 8 rows x 4 columns.  grid-stride over (row tile, col tile).
 // ---------------------------------------------------------------------------
 template <int K, int OUT2, int BM, int BN>
 __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
     constexpr int J2 = 3 * OUT2;
     constexpr int TN = BN / 4;                  // column groups (threads per row group)
     static_assert((BM / 8) * TN == kNT, "tile shape");
+    constexpr int BMP = BM + 4;
+    constexpr int NA = (BM * (K / 4) + kNT - 1) / kNT;
+    constexpr int NB = (K * (BN / 4) + kNT - 1) / kNT;
     extern __shared__ __align__(16) float dsm[];
-    float* As = dsm;                            // [K][BM]
-    float* Bs = dsm + K * BM;                   // [K][BN]
+    float* As = dsm;                            // [K][BMP]
+    float* Bs = dsm + K * BMP;                  // [K][BN]
     __shared__ int xrow_s[BM];
     const int tid = threadIdx.x;
     const int tx = tid % TN, ty = tid / TN;
     const int n_rows = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g_cap);
     const int n_rt = (n_rows + BM - 1) / BM;
     const int n_ct = (a.n_cols + BN - 1) / BN;
-    const size_t srow_stride = static_cast<size_t>(a.A2) * J2;
+    const int A2 = a.A2;
+    const int per_part = A2 * OUT2;
+    const int part0 = (a.colmode == COLS_VG) ? 1 : 0;
+    const size_t srow_stride = static_cast<size_t>(A2) * J2;
     for (int unit = blockIdx.x; unit < n_rt * n_ct; unit += gridDim.x) {
         const int rt = unit / n_ct, ct = unit % n_ct;
         const int r0 = rt * BM, c0 = ct * BN;
@@ -840,27 +902,51 @@ __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
             xrow_s[tid] = (r < n_rows) ? (a.E ? a.E[r].kprev : r) : -1;
         }
         __syncthreads();
-        for (int t = tid; t < K * BM; t += kNT) {
-            const int r = t % BM, k = t / BM;
-            const int xr = xrow_s[r];
-            As[k * BM + r] = (xr >= 0) ? a.X[static_cast<size_t>(xr) * K + k] : 0.0f;
+        float4 av[NA], bv[NB];
+#pragma unroll
+        for (int q = 0; q < NA; ++q) {
+            const int t = tid + q * kNT;
+            const int r = t % BM, k4 = t / BM;
+            av[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < BM * (K / 4) && xrow_s[r] >= 0)
+                av[q] = *reinterpret_cast<const float4*>(a.X + static_cast<size_t>(xrow_s[r]) * K + 4 * k4);
         }
-        for (int t = tid; t < K * BN; t += kNT) {
-            const int c = t % BN, k = t / BN;
-            const int col = c0 + c;
-            float w = 0.0f;
-            if (col < a.n_cols) {
+#pragma unroll
+        for (int q = 0; q < NB; ++q) {
+            const int t = tid + q * kNT;
+            const int c4 = t % (BN / 4), k = t / (BN / 4);
+            const int col = c0 + 4 * c4;
+            bv[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < K * (BN / 4) && col < a.n_cols) {
+                const float* src;
                 if (a.colmode == COLS_RES) {
-                    w = __ldg(a.W + static_cast<size_t>(k) * OUT2 + col);
+                    src = a.W + static_cast<size_t>(k) * OUT2 + col;
                 } else {
-                    int d, jj;
-                    if (a.colmode == COLS_ALL) { d = col / J2; jj = col % J2; }
-                    else if (a.colmode == COLS_VG) { d = col / (2 * OUT2); jj = OUT2 + col % (2 * OUT2); }
-                    else { d = col / OUT2; jj = col % OUT2; }
-                    w = __ldg(a.W + (static_cast<size_t>(d) * K + k) * J2 + jj);
+                    const int part = part0 + col / per_part, rem = col % per_part;
+                    const int d = rem / OUT2, o = rem % OUT2;
+                    src = a.W + (static_cast<size_t>(d) * K + k) * J2 + part * OUT2 + o;
                 }
+                bv[q] = __ldg(reinterpret_cast<const float4*>(src));
             }
-            Bs[k * BN + c] = w;
+        }
+#pragma unroll
+        for (int q = 0; q < NA; ++q) {
+            const int t = tid + q * kNT;
+            if (t < BM * (K / 4)) {
+                const int r = t % BM, k4 = t / BM;
+                As[(4 * k4 + 0) * BMP + r] = av[q].x;
+                As[(4 * k4 + 1) * BMP + r] = av[q].y;
+                As[(4 * k4 + 2) * BMP + r] = av[q].z;
+                As[(4 * k4 + 3) * BMP + r] = av[q].w;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < NB; ++q) {
+            const int t = tid + q * kNT;
+            if (t < K * (BN / 4)) {
+                const int c4 = t % (BN / 4), k = t / (BN / 4);
+                *reinterpret_cast<float4*>(Bs + k * BN + 4 * c4) = bv[q];
+            }
         }
         __syncthreads();
         float acc[8][4];
@@ -870,27 +956,24 @@ __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
             for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 #pragma unroll 4
         for (int k = 0; k < K; ++k) {
-            const float4 a0 = *reinterpret_cast<const float4*>(As + k * BM + ty * 8);
-            const float4 a1 = *reinterpret_cast<const float4*>(As + k * BM + ty * 8 + 4);
+            const float4 a0 = *reinterpret_cast<const float4*>(As + k * BMP + ty * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(As + k * BMP + ty * 8 + 4);
             const float4 b = *reinterpret_cast<const float4*>(Bs + k * BN + tx * 4);
-            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            const float bv[4] = {b.x, b.y, b.z, b.w};
+            const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float w[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(x[i], w[j], acc[i][j]);
         }
-        // epilogue: 4 consecutive columns never straddle a delta block
+        // epilogue: 4 consecutive columns share part and delta
         const int col = c0 + tx * 4;
         if (col < a.n_cols) {
             int jcol = col, part = 0;
-            if (a.colmode == COLS_ALL) { jcol = col; part = (col % J2) / OUT2; }
-            else if (a.colmode == COLS_VG) {
-                const int d = col / (2 * OUT2), cc = col % (2 * OUT2);
-                jcol = d * J2 + OUT2 + cc; part = 1 + cc / OUT2;
-            } else if (a.colmode == COLS_Q) {
-                const int d = col / OUT2;
-                jcol = d * J2 + col % OUT2; part = 0;
+            if (a.colmode != COLS_RES) {
+                part = part0 + col / per_part;
+                const int rem = col % per_part;
+                jcol = (rem / OUT2) * J2 + part * OUT2 + rem % OUT2;
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -1120,19 +1203,31 @@ void launch_scan(cudaStream_t st, int layer, const ScanArgs& a) {
     }
 }
 
-void launch_gather(cudaStream_t st, int layer, const GatherArgs& a, long long max_rows) {
-    auto go = [&](auto kern, int OUT, size_t smem) {
-        const int BM = (kNT / (OUT / 3)) * 8;
-        const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + BM - 1) / BM, 148LL * 8)));
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        kern<<<grid, kNT, smem, st>>>(a);
+void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long max_rows) {
+    auto go = [&](auto kern, auto shape) {
+        using Sh = decltype(shape);
+        const long long units = ((max_rows + Sh::BM - 1) / Sh::BM) * (layer == 0 ? 1 : 9);
+        const int grid = static_cast<int>(std::max(1LL, std::min(units, 148LL * 16)));
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Sh::smem));
+        kern<<<grid, kNT, Sh::smem, st>>>(a);
     };
     switch (layer) {
-        case 0: go(k_gather<1, 12>, 12, gather_smem_bytes<12>()); break;
-        case 1: go(k_gather<9, 12>, 12, gather_smem_bytes<12>()); break;
-        case 2: case 3: go(k_gather<9, 24>, 24, gather_smem_bytes<24>()); break;
-        case 4: case 5: go(k_gather<9, 48>, 48, gather_smem_bytes<48>()); break;
-        default: go(k_gather<9, 96>, 96, gather_smem_bytes<96>()); break;
+        case 0: go(k_contrib<1, 12>, ContribShape<1, 12>{}); break;
+        case 1: go(k_contrib<9, 12>, ContribShape<9, 12>{}); break;
+        case 2: case 3: go(k_contrib<9, 24>, ContribShape<9, 24>{}); break;
+        case 4: case 5: go(k_contrib<9, 48>, ContribShape<9, 48>{}); break;
+        default: go(k_contrib<9, 96>, ContribShape<9, 96>{}); break;
+    }
+}
+
+void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows) {
+    const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + 7) / 8, 148LL * 16)));
+    switch (layer) {
+        case 0: k_ln<1, 12><<<grid, kNT, 0, st>>>(a); break;
+        case 1: k_ln<9, 12><<<grid, kNT, 0, st>>>(a); break;
+        case 2: case 3: k_ln<9, 24><<<grid, kNT, 0, st>>>(a); break;
+        case 4: case 5: k_ln<9, 48><<<grid, kNT, 0, st>>>(a); break;
+        default: k_ln<9, 96><<<grid, kNT, 0, st>>>(a); break;
     }
 }
 
@@ -1156,7 +1251,7 @@ void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_ro
     auto go = [&](auto kern, int K, int BM, int BN) {
         const long long units = ((max_rows + BM - 1) / BM) * ((a.n_cols + BN - 1) / BN);
         const int grid = static_cast<int>(std::max(1LL, std::min(units, 148LL * 12)));
-        const size_t smem = sizeof(float) * static_cast<size_t>(K) * (BM + BN);
+        const size_t smem = sizeof(float) * static_cast<size_t>(K) * (BM + 4 + BN);
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         kern<<<grid, kNT, smem, st>>>(a);
     };

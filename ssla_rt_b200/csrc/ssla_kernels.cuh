@@ -69,22 +69,37 @@ struct ScanArgs {
     int second;              // 1: second layer of the stage
 };
 
-// Rows of a gather / GEMM launch: the first `count[list]` entries of a stage
-// list (list 1..4), or `n_static` chunk events (list 0).
-struct GatherArgs {
+// Rows of a contrib / ln / GEMM launch: the first `count[list]` entries of a
+// stage list (list 1..4), or `n_static` chunk events (list 0).
+struct ContribArgs {
     Geo g;
     int stage;               // stage of the gathered layer
-    int second;              // 1: second layer of the stage (rows carry kprev)
+    int second;              // 1: second layer of the stage (rows read S row kprev)
     int list;
     int n_static;
     const int* count;
     const StageEntry* E;     // row entries (list > 0)
     const uint32_t* ev_xy;   // list == 0
     const uint8_t* rflags;
+    const float* S;          // layer's (qh, v, a) rows [k][A][3*OUT]
+    const float* goWT;       // [A][OUT][OUT]
+    float* C;                // [row][A][OUT] contributions
+};
+
+struct LnArgs {
+    Geo g;
+    int stage;
+    int second;
+    int list;
+    int n_static;
+    const int* count;
+    const StageEntry* E;
+    const uint32_t* ev_xy;
+    const uint8_t* rflags;
     uint8_t copyres_bit;     // first layer: R_next = x for events with this bit
-    const float* S_in;       // (qh, v, a) rows of the layer
-    const float* R_in;       // residual rows of the layer
-    float* X_out;            // [row][OUT] layer output (may be null)
+    const float* C;          // contributions [row][A][OUT]
+    const float* R_in;       // residual rows of the layer (S row index)
+    float* X_out;            // [row][OUT] layer output
     float* R_next;           // copy residual of the stage's second layer
     DevLayer L;
     float* stage_out;        // optional [N][OUT] per chunk event (second layers)
@@ -102,6 +117,7 @@ struct HeadArgs {
 };
 
 enum { COLS_ALL = 0, COLS_VG = 1, COLS_Q = 2, COLS_RES = 3 };
+
 
 struct GemmArgs {
     int list;
@@ -142,7 +158,8 @@ void launch_gates(cudaStream_t st, const GateArgs& a);
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a);
 void launch_compact(cudaStream_t st, const CompactArgs& a);
 void launch_scan(cudaStream_t st, int layer, const ScanArgs& a);
-void launch_gather(cudaStream_t st, int layer, const GatherArgs& a, long long max_rows);
+void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long max_rows);
+void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows);
 void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows);
 // GEMM for next layer `layer` (its IN = K, OUT2, A2) with the given columns.
 void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_rows);
