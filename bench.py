@@ -91,17 +91,28 @@ def total_macs(macs: dict) -> int:
 
 
 def phase_flops(macs: dict, name: str) -> float:
-    """Algorithmic FLOPs of one engine phase (2 per MAC); 0 for integer or
-    scan phases."""
-    if name.startswith("contrib_L"):
-        return 2.0 * macs[int(name[9])]["gather"]
+    """Algorithmic FLOPs of one engine phase (2 per MAC).  Layers 1-3 compute
+    their qvg matvecs inside the scan; layers 4-7 in GEMM phases; k_ln of a
+    stage's second layer also computes the next stage's input_proj
+    residual; gates covers layer 0."""
+    parts = name.split("_")
     if name == "head":
         return 2.0 * macs["head"]
-    if name.startswith("gemm_L"):
-        l = int(name[6])
-        kind = name.split("_")[-1]
-        m = macs[l]
-        return 2.0 * {"vg": m["vg"], "q": m["q"], "all": m["vg"] + m["q"], "res": m["resid"]}[kind]
+    if name == "gates":
+        m = macs[0]
+        return 2.0 * (m["vg"] + m["q"] + m["gather"] + m["resid"])
+    if len(parts) < 2 or not parts[1].startswith("L"):
+        return 0.0
+    l = int(parts[1][1])
+    m = macs[l]
+    if parts[0] == "scan":
+        return 2.0 * (m["vg"] + m["q"]) if l <= 3 else 0.0
+    if parts[0] == "contrib":
+        return 2.0 * m["gather"]
+    if parts[0] == "ln":
+        return 2.0 * (macs[l + 1]["resid"] if (l % 2 == 1 and l < 7) else 0)
+    if parts[0] == "gemm":
+        return 2.0 * {"vg": m["vg"], "q": m["q"], "all": m["vg"] + m["q"]}[parts[2]]
     return 0.0
 
 

@@ -162,7 +162,7 @@ struct Workspace {
     int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, n_active = 0;
     long long cap_part[5] = {0}, cap[5] = {0};
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
-    DevBuf tl[4], tl_cnt[4], S_A, S_B, R_A, R_B, X, C, head_dec, head_raw, feat, slot_feat, stamps;
+    DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps;
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -203,30 +203,23 @@ struct Workspace {
             tl[s].alloc(slots * g.seg * sizeof(int2));
             tl_cnt[s].alloc(slots * sizeof(int));
         }
-        size_t sa = 0, sb = 0, ra = 0, rb = 0;
+        // Stage 0-1 layers keep compact q*h rows (QH); stage 2-3 layers use
+        // GEMM-built (q, v, sigmoid(g)) rows (S_A first layers, S_B second).
+        size_t sa = 1, qh = 1, rx = 1, cmax = 1;
         for (int s = s_first; s < 4; ++s) {
             const size_t c = chans(s), k = static_cast<size_t>(std::max<long long>(cap[s], 1));
-            sa = std::max(sa, k * (s == 0 ? 1 : 9) * 3 * c);
-            sb = std::max(sb, k * 9 * 3 * c);
-            ra = std::max(ra, k * c);
-            rb = std::max(rb, k * c);
+            if (s >= 2) sa = std::max(sa, k * 9 * 3 * c);
+            else qh = std::max(qh, k * 9 * c);
+            rx = std::max(rx, k * 2 * c);       // X rows, residual rows (next-stage width)
+            cmax = std::max(cmax, k * 9 * c);
         }
-        S_A.alloc(sa * 4); S_B.alloc(sb * 4); R_A.alloc(ra * 4); R_B.alloc(rb * 4);
-        X.alloc(ra * 4);                        // layer outputs, [rows][C_s]
-        size_t cmax = 0;                        // contributions, [rows][A][C_s]
-        for (int s = s_first; s < 4; ++s) {
-            const size_t k = static_cast<size_t>(std::max<long long>(cap[s], 1));
-            cmax = std::max(cmax, k * 9 * chans(s));
-        }
-        C.alloc(cmax * 4);
+        S_A.alloc(sa * 4); S_B.alloc(sa * 4); QH.alloc(qh * 4);
+        R_A.alloc(rx * 4); R_B.alloc(rx * 4); X.alloc(rx * 4); C.alloc(cmax * 4);
         const int cols = 5 + g.ncls;
         head_dec.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
         head_raw.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
         stamps.alloc(sizeof(unsigned long long) * 2);
-        if (s_first == 2) {
-            feat.alloc(sizeof(float) * 24 * n_max);
-            slot_feat.alloc(sizeof(float) * 96 * n_max);
-        }
+        if (s_first == 2) slot_feat.alloc(sizeof(float) * 96 * n_max);
         for (int s = 0; s < 4; ++s) {
             if (record) stage_out[s].alloc(sizeof(float) * chans(s) * static_cast<size_t>(n_max));
             else stage_out[s].release();
@@ -234,120 +227,111 @@ struct Workspace {
     }
 };
 
-// Enqueues stages s_first..3 (layers 2*s_first..7) for a planned workspace.
-// On entry S_A / R_A hold the (q, v, sigmoid(g)) rows and residuals of the
-// first layer of stage s_first.  Per stage s (first layer 2s, second 2s+1):
-//   scan 2s on S_A | gather 2s -> X (E_s rows), R_B = X for events whose
-//   second-layer output is used | GEMM v,g cols of layer 2s+1 for all E_s
-//   rows and q cols for E_{s+1} rows -> S_B | scan 2s+1 on S_B |
-//   gather 2s+1 -> X (E_{s+1} rows) | GEMM layer 2s+2 all cols + input_proj
-//   -> S_A, R_A   (stage 3: gather 7 runs the head instead).
+// Enqueues layers 1..7 (s_first = 0; layer 0 is done by k_gates) or 4..7
+// (s_first = 2, drain_n).  On entry X holds the input rows of the first
+// layer to run and R_B (s_first = 0) / R_A (s_first = 2) its residuals.
+// Per layer l (stage s, half = l % 2):
+//   stages 0-1: k_scan_fused (qvg computed per hit from X rows, q*h -> QH)
+//   stages 2-3: k_gemm builds the (q, v, sigmoid(g)) rows of the layer from X
+//               (all columns for first layers; v,g for every event and q
+//               for output-producing events for second layers), k_scan
+//   then k_contrib (goW contributions) and k_ln (ordered sum, residual,
+//   LayerNorm) write the layer output back into X, plus the residual of the
+//   next layer (copy for a stage's second layer, input_proj for the next
+//   stage's first); after layer 7 k_head.
 void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_parts,
                 const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof) {
     static const char* kScan[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
                                    "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
     static const char* kContrib[8] = {"contrib_L0", "contrib_L1", "contrib_L2", "contrib_L3",
                                       "contrib_L4", "contrib_L5", "contrib_L6", "contrib_L7"};
-    static const char* kGather[8] = {"ln_L0", "ln_L1", "ln_L2", "ln_L3",
-                                     "ln_L4", "ln_L5", "ln_L6", "ln_L7"};
-    static const char* kVG[8] = {"", "gemm_L1_vg", "", "gemm_L3_vg", "", "gemm_L5_vg", "", "gemm_L7_vg"};
-    static const char* kQ[8] = {"", "gemm_L1_q", "", "gemm_L3_q", "", "gemm_L5_q", "", "gemm_L7_q"};
-    static const char* kAll[8] = {"", "", "gemm_L2_all", "", "gemm_L4_all", "", "gemm_L6_all", ""};
-    static const char* kRes[8] = {"", "", "gemm_L2_res", "", "gemm_L4_res", "", "gemm_L6_res", ""};
+    static const char* kLn[8] = {"ln_L0", "ln_L1", "ln_L2", "ln_L3", "ln_L4", "ln_L5", "ln_L6", "ln_L7"};
+    static const char* kGemmA[8] = {"", "", "", "", "gemm_L4_all", "gemm_L5_vg", "gemm_L6_all", "gemm_L7_vg"};
     const int* d_count = w.count.as<int>();
     float* X = w.X.as<float>();
-    for (int s = w.s_first; s < 4; ++s) {
+    float* R_first = w.R_A.as<float>();        // residual rows of first layers
+    float* R_second = w.R_B.as<float>();       // residual rows of second layers
+    const int l0 = (w.s_first == 0) ? 1 : 4;
+    for (int l = l0; l < 8; ++l) {
+        const int s = l / 2, half = l % 2;
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
-        const int2* tl = w.tl[s].as<int2>();
-        const int* tl_cnt = w.tl_cnt[s].as<int>();
+        // rows of this layer's scan entries (the stage list) and of its output
         const long long n_s = (s == 0) ? w.n_active : w.cap[s];
-        for (int half = 0; half < 2; ++half) {
-            const int l = 2 * s + half;
-            float* S_l = (half == 0) ? w.S_A.as<float>() : w.S_B.as<float>();
-            float* R_l = (half == 0) ? w.R_A.as<float>() : w.R_B.as<float>();
-            ScanArgs sa{};
-            sa.g = g; sa.stage = s; sa.layer = l; sa.tl = tl; sa.tl_cnt = tl_cnt; sa.range = range;
-            sa.S = S_l; sa.parts = d_parts; sa.rflags = w.rflags.as<uint8_t>(); sa.second = half;
-            launch_scan(st, l, sa);
-            check_launch("k_scan");
+        const long long n_out = half ? w.cap[s + 1] : n_s;
+        const float* S_rows;
+        int qstride;
+        if (s < 2) {
+            ScanFusedArgs fa{};
+            fa.g = g; fa.stage = s; fa.layer = l; fa.tl = w.tl[s].as<int2>(); fa.tl_cnt = w.tl_cnt[s].as<int>();
+            fa.range = range; fa.parts = d_parts; fa.rflags = w.rflags.as<uint8_t>(); fa.second = half;
+            fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>();
+            launch_scan_fused(st, l, fa);
+            check_launch("k_scan_fused");
             prof.mark(kScan[l], 1, st);
-
-            const bool last = (l == 7);
-            ContribArgs ca{};
-            LnArgs la{};
-            ca.g = la.g = g; ca.stage = la.stage = s; ca.second = la.second = half;
-            ca.count = la.count = d_count;
-            ca.ev_xy = la.ev_xy = w.ev_xy.as<uint32_t>();
-            ca.rflags = la.rflags = w.rflags.as<uint8_t>();
-            ca.S = S_l; ca.goWT = L[l].goWT; ca.C = w.C.as<float>();
-            la.C = w.C.as<float>(); la.R_in = R_l; la.L = L[l]; la.X_out = X;
-            la.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
-            la.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
-            long long n_rows;
-            if (half == 0) {
-                if (s == 0) { ca.list = la.list = 0; ca.n_static = la.n_static = w.n_active; }
-                else { ca.list = la.list = s; ca.E = la.E = w.E[s].as<StageEntry>(); }
-                n_rows = n_s;
-                la.copyres_bit = static_cast<uint8_t>(F_R1 << s);      // R_{s+1}
-                la.R_next = w.R_B.as<float>();
-            } else {
-                ca.list = la.list = s + 1;
-                ca.E = la.E = w.E[s + 1].as<StageEntry>();
-                n_rows = w.cap[s + 1];
-            }
-            launch_contrib(st, l, ca, n_rows);
-            check_launch("k_contrib");
-            prof.mark(kContrib[l], 1, st);
-            launch_ln(st, l, la, n_rows);
-            check_launch("k_ln");
-            prof.mark(kGather[l], 1, st);
-            if (last) {
-                if (do_head) {
-                    HeadArgs ha{};
-                    ha.g = g; ha.count = d_count; ha.E4 = w.E[4].as<StageEntry>(); ha.X = X;
-                    ha.head = *head; ha.head_dec = w.head_dec.as<float>(); ha.head_raw = w.head_raw.as<float>();
-                    launch_head(st, ha, w.cap[4]);
-                    check_launch("k_head");
-                    prof.mark("head", 1, st);
-                }
-                break;
-            }
-
+            S_rows = w.QH.as<float>();
+            qstride = chans(s);
+        } else {
+            float* S_l = half ? w.S_B.as<float>() : w.S_A.as<float>();
             GemmArgs gm{};
-            gm.count = d_count; gm.X = X; gm.A2 = 9;
-            if (half == 0) {
-                // layer l+1 (second layer of stage s): v,g for every E_s row
-                gm.W = L[l + 1].qvgT; gm.S = w.S_B.as<float>();
-                if (s == 0) { gm.list = 0; gm.n_static = w.n_active; gm.g_cap = w.n_active; }
-                else { gm.list = s; gm.g_cap = static_cast<int>(w.cap[s]); }
-                gm.colmode = COLS_VG; gm.n_cols = gemm_cols(l + 1, COLS_VG);
-                launch_gemm(st, l + 1, gm, n_s);
-                check_launch("k_gemm vg");
-                prof.mark(kVG[l + 1], 1, st);
-                // q columns only for events whose layer-(l+1) output is used
+            gm.count = d_count; gm.X = X; gm.A2 = 9; gm.W = L[l].qvgT; gm.S = S_l;
+            gm.list = s; gm.g_cap = static_cast<int>(w.cap[s]);
+            gm.colmode = half ? COLS_VG : COLS_ALL;
+            gm.n_cols = gemm_cols(l, gm.colmode);
+            launch_gemm(st, l, gm, n_s);
+            check_launch("k_gemm");
+            prof.mark(kGemmA[l], 1, st);
+            if (half) {
                 GemmArgs gq = gm;
                 gq.list = s + 1; gq.g_cap = static_cast<int>(w.cap[s + 1]);
                 gq.E = w.E[s + 1].as<StageEntry>();
-                gq.colmode = COLS_Q; gq.n_cols = gemm_cols(l + 1, COLS_Q);
-                launch_gemm(st, l + 1, gq, w.cap[s + 1]);
+                gq.colmode = COLS_Q; gq.n_cols = gemm_cols(l, COLS_Q);
+                launch_gemm(st, l, gq, w.cap[s + 1]);
                 check_launch("k_gemm q");
-                prof.mark(kQ[l + 1], 1, st);
-            } else {
-                // layer l+1 = first layer of stage s+1: all columns + input_proj
-                gm.list = s + 1; gm.g_cap = static_cast<int>(w.cap[s + 1]);
-                gm.W = L[l + 1].qvgT; gm.S = w.S_A.as<float>();
-                gm.colmode = COLS_ALL; gm.n_cols = gemm_cols(l + 1, COLS_ALL);
-                launch_gemm(st, l + 1, gm, w.cap[s + 1]);
-                check_launch("k_gemm all");
-                prof.mark(kAll[l + 1], 1, st);
-                GemmArgs gr = gm;
-                gr.W = L[l + 1].ipT; gr.R = w.R_A.as<float>();
-                gr.colmode = COLS_RES; gr.n_cols = gemm_cols(l + 1, COLS_RES);
-                launch_gemm(st, l + 1, gr, w.cap[s + 1]);
-                check_launch("k_gemm res");
-                prof.mark(kRes[l + 1], 1, st);
+                prof.mark(l == 5 ? "gemm_L5_q" : "gemm_L7_q", 1, st);
             }
+            ScanArgs sa{};
+            sa.g = g; sa.stage = s; sa.layer = l; sa.tl = w.tl[s].as<int2>(); sa.tl_cnt = w.tl_cnt[s].as<int>();
+            sa.range = range; sa.S = S_l; sa.parts = d_parts; sa.rflags = w.rflags.as<uint8_t>(); sa.second = half;
+            launch_scan(st, l, sa);
+            check_launch("k_scan");
+            prof.mark(kScan[l], 1, st);
+            S_rows = S_l;
+            qstride = 3 * chans(s);
         }
+        ContribArgs ca{};
+        LnArgs la{};
+        ca.g = la.g = g; ca.stage = la.stage = s; ca.second = la.second = half;
+        ca.count = la.count = d_count;
+        ca.ev_xy = la.ev_xy = w.ev_xy.as<uint32_t>();
+        ca.rflags = la.rflags = w.rflags.as<uint8_t>();
+        ca.S = S_rows; ca.qstride = qstride; ca.goWT = L[l].goWT; ca.C = w.C.as<float>();
+        la.C = w.C.as<float>(); la.R_in = half ? R_second : R_first; la.L = L[l]; la.X_out = X;
+        la.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
+        la.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;
+        if (half == 0) {
+            if (s == 0) { ca.list = la.list = 0; ca.n_static = la.n_static = w.n_active; }
+            else { ca.list = la.list = s; ca.E = la.E = w.E[s].as<StageEntry>(); }
+            la.copyres_bit = static_cast<uint8_t>(F_R1 << s);      // R_{s+1}
+            la.R_next = R_second;
+        } else {
+            ca.list = la.list = s + 1;
+            ca.E = la.E = w.E[s + 1].as<StageEntry>();
+            if (s < 3) { la.ipT_next = L[l + 1].ipT; la.R_ipnext = R_first; }
+        }
+        launch_contrib(st, l, ca, n_out);
+        check_launch("k_contrib");
+        prof.mark(kContrib[l], 1, st);
+        launch_ln(st, l, la, n_out);
+        check_launch("k_ln");
+        prof.mark(kLn[l], 1, st);
+    }
+    if (do_head) {
+        HeadArgs ha{};
+        ha.g = g; ha.count = d_count; ha.E4 = w.E[4].as<StageEntry>(); ha.X = X;
+        ha.head = *head; ha.head_dec = w.head_dec.as<float>(); ha.head_raw = w.head_raw.as<float>();
+        launch_head(st, ha, w.cap[4]);
+        check_launch("k_head");
+        prof.mark("head", 1, st);
     }
 }
 
@@ -517,7 +501,7 @@ struct Engine {
         GateArgs ga{};
         ga.g = g; ga.ev = ev; ga.ev_off = ws.ev_off.as<int>(); ga.tl0 = ws.tl[0].as<int2>();
         ga.tl0_cnt = ws.tl_cnt[0].as<int>(); ga.parts = parts.as<PartState>();
-        ga.rflags = ws.rflags.as<uint8_t>(); ga.S0 = ws.S_A.as<float>(); ga.R0 = ws.R_A.as<float>();
+        ga.rflags = ws.rflags.as<uint8_t>(); ga.X1 = ws.X.as<float>(); ga.Rcopy = ws.R_B.as<float>();
         ga.L0 = L[0];
         launch_gates(st, ga);
         check_launch("k_gates");
@@ -644,7 +628,7 @@ struct DrainN {
                 SSLA_CK(cudaMemcpyAsync(d.rec.as<HybridInputRec>() + off[b], rings[b],
                                         sizeof(HybridInputRec) * ns[b], cudaMemcpyDeviceToDevice, st));
         launch_prep_records(st, d.rec.p, n, w.E[2].as<StageEntry>(), w.ev_xy.as<uint32_t>(),
-                            w.rflags.as<uint8_t>(), w.feat.as<float>());
+                            w.rflags.as<uint8_t>(), w.X.as<float>());
         check_launch("k_prep_records");
         const Geo& g = d.g;
         FilterArgs f2{};
@@ -681,13 +665,10 @@ struct DrainN {
             const LayerWeightsS2S3& lw = cfg->layers[0][li];
             L[4 + li] = DevLayer{lw.qvgIn, lw.goW, lw.input_proj, lw.ln_gamma, lw.ln_beta};
         }
-        // record features -> layer-4 qvg (all columns) + residual
-        GemmArgs ge{};
-        ge.list = 2; ge.count = w.count.as<int>(); ge.g_cap = n; ge.X = w.feat.as<float>(); ge.A2 = 9;
-        ge.W = L[4].qvgT; ge.S = w.S_A.as<float>(); ge.colmode = COLS_ALL; ge.n_cols = gemm_cols(4, COLS_ALL);
-        launch_gemm(st, 4, ge, n);
-        check_launch("k_gemm entry");
-        GemmArgs gr = ge;
+        // layer-4 residual (input_proj * feat1); the layer's qvg GEMM reads
+        // the same X rows inside run_layers
+        GemmArgs gr{};
+        gr.list = 2; gr.count = w.count.as<int>(); gr.g_cap = n; gr.X = w.X.as<float>(); gr.A2 = 9;
         gr.W = L[4].ipT; gr.R = w.R_A.as<float>(); gr.colmode = COLS_RES; gr.n_cols = gemm_cols(4, COLS_RES);
         launch_gemm(st, 4, gr, n);
         check_launch("k_gemm entry res");

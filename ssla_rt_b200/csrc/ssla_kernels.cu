@@ -157,7 +157,8 @@ __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
 //   gate 0 / 1 / 2 / 3 on the layout's grids (all cells of an event's gates
 //               lie inside its s3 block, so the block owns every counter it
 //               touches)
-//   layer 0 qvg (q, v, sigmoid(g)) and residual input_proj * (dt, p).
+//   layer 0 entirely (K = 1: the event's own pixel), writing its output row
+//               and, for events entering stage 1, the layer-1 residual.
 // Same-key ordering inside a 32-event window uses __match_any_sync ranks.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
@@ -170,7 +171,18 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
     const int window = a.g.window;
     __shared__ double lt[64];
     __shared__ int c0[16], c1[4], c2[4], c3[1];
+    // layer-0 weights: qvgT [2][36] | ipT [2][12] | goWT [12][12] | gamma | beta
+    __shared__ float w0[264];
+    __shared__ float h0[64 * 12];
     const int W0 = a.g.W[0], W1 = a.g.W[1], W2 = a.g.W[2];
+    for (int i = lane; i < 72; i += 32) w0[i] = a.L0.qvgT[i];
+    for (int i = lane; i < 24; i += 32) w0[72 + i] = a.L0.ipT[i];
+    for (int i = lane; i < 144; i += 32) w0[96 + i] = a.L0.goWT[i];
+    if (lane < 12) { w0[240 + lane] = a.L0.gamma[lane]; w0[252 + lane] = a.L0.beta[lane]; }
+    for (int i = lane; i < 64 * 12; i += 32) {
+        const int px = i / 12, c = i % 12;
+        h0[i] = ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c];
+    }
     for (int i = lane; i < 64; i += 32)
         lt[i] = ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)];
     if (lane < 16) c0[lane] = ps.cnt[0][(by * 4 + lane / 4) * W1 + bx * 4 + (lane % 4)];
@@ -187,8 +199,6 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
     const int tile = by * a.g.tx[0] + bx;     // s0 tiles are the s3 blocks
     const int n_p = a.ev_off[p + 1] - a.ev_off[p];
     const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[0]);
-    const float* qT = a.L0.qvgT;               // [1][2][36]
-    const float* ipT = a.L0.ipT;               // [2][12]
     for (int seg = 0; seg < nseg; ++seg) {
         const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0] + seg;
         const int cnt = a.tl0_cnt[slot];
@@ -242,20 +252,65 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
                 if (in3) f |= F_R3;
                 if (in3 && pass3) f |= F_R4;
                 a.rflags[k] = f;
-                // layer 0: qvg = qvgIn[0] * (dt, p) (matvec_ct<2,36>), residual
-                // = input_proj * (dt, p) (matvec_ct<2,12>).
-                float* S = a.S0 + static_cast<size_t>(k) * 36;
-#pragma unroll 4
-                for (int jj = 0; jj < 36; ++jj) {
-                    float acc = fmaf(__ldg(qT + jj), dt, 0.0f);
-                    acc = fmaf(__ldg(qT + 36 + jj), e.w, acc);
-                    S[jj] = (jj >= 24) ? ssla_sigmoidf(acc) : acc;
+            }
+            // ---- layer 0 (K = 1, 2 -> 12), one lane per event: qvg
+            // (matvec_ct<2,36>), residual (matvec_ct<2,12>), the pixel's
+            // lru_step in stream order (same-pixel lanes take turns by rank),
+            // the goW contribution, residual add and LayerNorm
+            // (layer_forward_ct, src/ssla_kernels.cpp:315-385). ----
+            float q[12], v[12], ag[12], res[12], qh[12];
+            if (own) {
+#pragma unroll
+                for (int c = 0; c < 12; ++c) {
+                    q[c] = fmaf(w0[36 + c], e.w, fmaf(w0[c], dt, 0.0f));
+                    v[c] = fmaf(w0[36 + 12 + c], e.w, fmaf(w0[12 + c], dt, 0.0f));
+                    ag[c] = ssla_sigmoidf(fmaf(w0[36 + 24 + c], e.w, fmaf(w0[24 + c], dt, 0.0f)));
+                    res[c] = fmaf(w0[72 + 12 + c], e.w, fmaf(w0[72 + c], dt, 0.0f));
                 }
-                float* R = a.R0 + static_cast<size_t>(k) * 12;
-#pragma unroll 4
+            }
+            const int rank = __popc(peers & lanemask_lt());
+            const int rounds = __reduce_max_sync(0xffffffffu, own ? rank + 1 : 0);
+            for (int rd = 0; rd < rounds; ++rd) {
+                if (own && rank == rd) {
+                    float* h = h0 + pix * 12;
+#pragma unroll
+                    for (int c = 0; c < 12; ++c) {
+                        const float hc = fmaf(ag[c], h[c], v[c]);
+                        h[c] = hc;
+                        qh[c] = q[c] * hc;
+                    }
+                }
+                __syncwarp();
+            }
+            if (own) {
+                float y[12];
+                double sum = 0.0;
+#pragma unroll
                 for (int o = 0; o < 12; ++o) {
-                    float acc = fmaf(__ldg(ipT + o), dt, 0.0f);
-                    R[o] = fmaf(__ldg(ipT + 12 + o), e.w, acc);
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 12; ++i) acc = fmaf(w0[96 + i * 12 + o], qh[i], acc);
+                    y[o] = (0.0f + acc) + res[o];
+                    sum += static_cast<double>(y[o]);
+                }
+                const double mean = sum / 12.0;
+                double var = 0.0;
+#pragma unroll
+                for (int o = 0; o < 12; ++o) {
+                    const double dd = static_cast<double>(y[o]) - mean;
+                    var += dd * dd;
+                }
+                var /= 12.0;
+                const double inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+                float* xo = a.X1 + static_cast<size_t>(k) * 12;
+                float* rc = (pass0 && a.Rcopy) ? a.Rcopy + static_cast<size_t>(k) * 12 : nullptr;
+#pragma unroll
+                for (int o = 0; o < 12; ++o) {
+                    const double t = (static_cast<double>(y[o]) - mean) * inv;
+                    const float xv = static_cast<float>(t * static_cast<double>(w0[240 + o]) +
+                                                        static_cast<double>(w0[252 + o]));
+                    xo[o] = xv;
+                    if (rc) rc[o] = xv;
                 }
             }
         }
@@ -263,6 +318,10 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
     __syncwarp();
     for (int i = lane; i < 64; i += 32)
         ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)] = lt[i];
+    for (int i = lane; i < 64 * 12; i += 32) {
+        const int px = i / 12, c = i % 12;
+        ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c] = h0[i];
+    }
     if (lane < 16) ps.cnt[0][(by * 4 + lane / 4) * W1 + bx * 4 + (lane % 4)] = static_cast<uint8_t>(c0[lane]);
     if (lane < 4) ps.cnt[1][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)] = static_cast<uint8_t>(c1[lane]);
     if (hyb) {
@@ -552,6 +611,106 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// k_scan_fused: the per-cell LRU scan of a small layer (IN, OUT <= 24: layers
+// 1-3, whose qvg weights fit in shared memory) with the fused qvg matvec
+// computed per hit from the event's input row (matvec_ct<IN,3*OUT>,
+// linear.h:80-90): q, v, g for the hit's patch position, then
+// h = sigmoid(g) * h + v (fmaf) and, when the layer's output is consumed,
+// qh = q * h into the compact QH rows [(entry * 9 + delta) * OUT].
+// One warp per cell (lanes = channels), 16 cells per CTA, the layer's
+// 9 x IN x 3*OUT weights staged once per CTA.  grid (P, tiles, 4).
+// ---------------------------------------------------------------------------
+template <int IN, int OUT>
+__global__ void __launch_bounds__(512) k_scan_fused(ScanFusedArgs a) {
+    constexpr int J2 = 3 * OUT;
+    constexpr int HB = (IN <= 12) ? 4 : 2;      // hits per batch
+    extern __shared__ __align__(16) float Ws[];  // [9][IN][J2]
+    const int p = blockIdx.x, tile = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int s = a.stage;
+    for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x)
+        reinterpret_cast<float4*>(Ws)[t] = __ldg(reinterpret_cast<const float4*>(a.W) + t);
+    __syncthreads();
+    const int local = blockIdx.z * 16 + warp;              // 0..63 in the tile
+    const int cx = (tile % a.g.tx[s]) * kTile + (local % kTile);
+    const int cy = (tile / a.g.tx[s]) * kTile + (local / kTile);
+    const int Wl = a.g.W[s], Hl = a.g.H[s];
+    if (cx >= Wl || cy >= Hl) return;
+    float* hp = a.parts[p].hidden[a.layer] + (static_cast<size_t>(cy) * Wl + cx) * OUT;
+    const bool lo = lane < OUT;
+    float h = lo ? hp[lane] : 0.0f;
+    const int ntiles = a.g.tx[s] * a.g.ty[s];
+    const int n_p = a.range[p + 1] - a.range[p];
+    const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
+    for (int seg = 0; seg < nseg; ++seg) {
+        const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
+        const int cnt = a.tl_cnt[slot];
+        const int2* lst = a.tl + slot * a.g.seg;
+        for (int j0 = 0; j0 < cnt; j0 += 32) {
+            const int j = j0 + lane;
+            int2 ent = make_int2(0, 0);
+            if (j < cnt) ent = lst[j];
+            const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
+            const int dx = cx - ex, dy = cy - ey;
+            const bool hit = (j < cnt) && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1;
+            const int delta = (1 - dy) * 3 + (1 - dx);
+            int outf = 1;
+            if (a.second) {
+                if (s == 0) outf = (hit && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
+                else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
+            }
+            const int pkf = (((ent.x << 4) | delta) << 1) | outf;
+            unsigned m = __ballot_sync(0xffffffffu, hit);
+            while (m) {
+                int kk[HB], dd[HB], of[HB];
+                int nh = 0;
+#pragma unroll
+                for (int q = 0; q < HB; ++q) {
+                    const int src = m ? (__ffs(m) - 1) : 0;
+                    const int v = __shfl_sync(0xffffffffu, pkf, src);
+                    kk[q] = v >> 5;
+                    dd[q] = (v >> 1) & 15;
+                    of[q] = (m != 0u) ? (v & 1) : 0;
+                    nh += (m != 0u) ? 1 : 0;
+                    m &= (m - 1u);
+                }
+                float x[HB][IN];
+#pragma unroll
+                for (int q = 0; q < HB; ++q) {
+                    const float4* xr = reinterpret_cast<const float4*>(a.X + static_cast<size_t>(kk[q]) * IN);
+#pragma unroll
+                    for (int i4 = 0; i4 < IN / 4; ++i4) {
+                        const float4 t = (q < nh) ? __ldg(xr + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        x[q][4 * i4] = t.x; x[q][4 * i4 + 1] = t.y;
+                        x[q][4 * i4 + 2] = t.z; x[q][4 * i4 + 3] = t.w;
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < HB; ++q) {
+                    if (q < nh && lo) {
+                        const float* w = Ws + static_cast<size_t>(dd[q]) * IN * J2 + lane;
+                        float vq = 0.0f, vv = 0.0f, vg = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < IN; ++i) {
+                            vv = fmaf(w[i * J2 + OUT], x[q][i], vv);
+                            vg = fmaf(w[i * J2 + 2 * OUT], x[q][i], vg);
+                        }
+                        const float ga = ssla_sigmoidf(vg);
+                        h = fmaf(ga, h, vv);
+                        if (of[q]) {
+#pragma unroll
+                            for (int i = 0; i < IN; ++i) vq = fmaf(w[i * J2], x[q][i], vq);
+                            a.QH[(static_cast<size_t>(kk[q]) * 9 + dd[q]) * OUT + lane] = vq * h;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    if (lo) hp[lane] = h;
+}
+
+// ---------------------------------------------------------------------------
 // Gather, phase 1 -- k_contrib: per patch position delta, the goW
 // contribution of every output-producing event (layer_forward_ct,
 // src/ssla_kernels.cpp:340-351, matvec_accum_ct linear.h:92-101):
@@ -629,7 +788,7 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
                 av[q] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (t < BM * Q4 && srow_s[r] >= 0)
                     av[q] = *reinterpret_cast<const float4*>(
-                        a.S + (static_cast<size_t>(srow_s[r]) * A + d) * (3 * OUT) + 4 * k4);
+                        a.S + (static_cast<size_t>(srow_s[r]) * A + d) * a.qstride + 4 * k4);
             }
 #pragma unroll
             for (int q = 0; q < NB; ++q) {
@@ -760,6 +919,17 @@ __global__ void __launch_bounds__(kNT) k_ln(LnArgs a) {
             if (a.slot_feat) {
                 a.slot_feat[static_cast<size_t>(e) * 96 + o] = xv;
                 if (OUT == 48) a.slot_feat[static_cast<size_t>(e) * 96 + 48 + o] = 0.0f;
+            }
+            y[o] = xv;
+        }
+        __syncwarp();
+        if (a.ipT_next) {
+            // residual of the next stage's first layer: input_proj * x
+            // (matvec_ct<OUT, 2*OUT>), row r of the same list
+            for (int o2 = lane; o2 < 2 * OUT; o2 += 32) {
+                float acc = 0.0f;
+                for (int i = 0; i < OUT; ++i) acc = fmaf(__ldg(a.ipT_next + i * 2 * OUT + o2), y[i], acc);
+                a.R_ipnext[static_cast<size_t>(r) * 2 * OUT + o2] = acc;
             }
         }
         __syncwarp();
@@ -1217,6 +1387,21 @@ void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long 
         case 2: case 3: go(k_contrib<9, 24>, ContribShape<9, 24>{}); break;
         case 4: case 5: go(k_contrib<9, 48>, ContribShape<9, 48>{}); break;
         default: go(k_contrib<9, 96>, ContribShape<9, 96>{}); break;
+    }
+}
+
+void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
+    const int s = layer / 2;
+    const dim3 grid(a.g.P, a.g.tx[s] * a.g.ty[s], 4);
+    auto go = [&](auto kern, int IN, int OUT) {
+        const size_t smem = sizeof(float) * 9 * IN * 3 * OUT;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        kern<<<grid, 512, smem, st>>>(a);
+    };
+    switch (layer) {
+        case 1: go(k_scan_fused<12, 12>, 12, 12); break;
+        case 2: go(k_scan_fused<12, 24>, 12, 24); break;
+        default: go(k_scan_fused<24, 24>, 24, 24); break;
     }
 }
 

@@ -27,8 +27,8 @@ struct GateArgs {
     const int* tl0_cnt;
     const PartState* parts;
     uint8_t* rflags;
-    float* S0;               // L0 (q, v, sigmoid(g)) per event  [N][36]
-    float* R0;               // L0 residual per event            [N][12]
+    float* X1;               // [N][12] layer-0 output per event
+    float* Rcopy;            // [N][12] layer-1 residual (events entering stage 1)
     DevLayer L0;
 };
 
@@ -71,6 +71,20 @@ struct ScanArgs {
 
 // Rows of a contrib / ln / GEMM launch: the first `count[list]` entries of a
 // stage list (list 1..4), or `n_static` chunk events (list 0).
+struct ScanFusedArgs {
+    Geo g;
+    int stage, layer;
+    const int2* tl;
+    const int* tl_cnt;
+    const int* range;        // [P+1] this stage's partition ranges
+    const PartState* parts;
+    const uint8_t* rflags;   // stage-0 second-layer output flags
+    int second;              // 1: second layer of the stage
+    const float* X;          // [entry][IN] layer input rows
+    const float* W;          // qvgT [9][IN][3*OUT]
+    float* QH;               // [(entry * 9 + delta) * OUT] q * h rows
+};
+
 struct ContribArgs {
     Geo g;
     int stage;               // stage of the gathered layer
@@ -81,7 +95,8 @@ struct ContribArgs {
     const StageEntry* E;     // row entries (list > 0)
     const uint32_t* ev_xy;   // list == 0
     const uint8_t* rflags;
-    const float* S;          // layer's (qh, v, a) rows [k][A][3*OUT]
+    const float* S;          // qh rows at (k * A + delta) * qstride
+    int qstride;             // 3*OUT (GEMM-fed S rows) or OUT (compact QH rows)
     const float* goWT;       // [A][OUT][OUT]
     float* C;                // [row][A][OUT] contributions
 };
@@ -104,6 +119,8 @@ struct LnArgs {
     DevLayer L;
     float* stage_out;        // optional [N][OUT] per chunk event (second layers)
     float* slot_feat;        // drain_n: [N][96] the reference's s3_feat slot
+    const float* ipT_next;   // next stage's input_proj [OUT][2*OUT] (or null)
+    float* R_ipnext;         // its residual rows [row][2*OUT]
 };
 
 struct HeadArgs {
@@ -160,6 +177,7 @@ void launch_compact(cudaStream_t st, const CompactArgs& a);
 void launch_scan(cudaStream_t st, int layer, const ScanArgs& a);
 void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long max_rows);
 void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows);
+void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a);
 void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows);
 // GEMM for next layer `layer` (its IN = K, OUT2, A2) with the given columns.
 void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_rows);
