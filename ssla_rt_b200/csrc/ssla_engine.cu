@@ -162,7 +162,7 @@ struct Workspace {
     int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, n_active = 0;
     long long cap_part[5] = {0}, cap[5] = {0};
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
-    DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps;
+    DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps, work;
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -219,6 +219,7 @@ struct Workspace {
         head_dec.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
         head_raw.alloc(sizeof(float) * cols * std::max<long long>(cap[4], 1));
         stamps.alloc(sizeof(unsigned long long) * 2);
+        work.alloc(sizeof(int) * 8);
         if (s_first == 2) slot_feat.alloc(sizeof(float) * 96 * n_max);
         for (int s = 0; s < 4; ++s) {
             if (record) stage_out[s].alloc(sizeof(float) * chans(s) * static_cast<size_t>(n_max));
@@ -252,6 +253,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
     float* R_first = w.R_A.as<float>();        // residual rows of first layers
     float* R_second = w.R_B.as<float>();       // residual rows of second layers
     const int l0 = (w.s_first == 0) ? 1 : 4;
+    if (l0 < 4) SSLA_CK(cudaMemsetAsync(w.work.p, 0, sizeof(int) * 8, st));
     for (int l = l0; l < 8; ++l) {
         const int s = l / 2, half = l % 2;
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
@@ -264,7 +266,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             ScanFusedArgs fa{};
             fa.g = g; fa.stage = s; fa.layer = l; fa.tl = w.tl[s].as<int2>(); fa.tl_cnt = w.tl_cnt[s].as<int>();
             fa.range = range; fa.parts = d_parts; fa.rflags = w.rflags.as<uint8_t>(); fa.second = half;
-            fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>();
+            fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>(); fa.work = w.work.as<int>() + l;
             launch_scan_fused(st, l, fa);
             check_launch("k_scan_fused");
             prof.mark(kScan[l], 1, st);

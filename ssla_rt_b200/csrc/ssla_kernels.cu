@@ -611,103 +611,236 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// k_scan_fused: the per-cell LRU scan of a small layer (IN, OUT <= 24: layers
-// 1-3, whose qvg weights fit in shared memory) with the fused qvg matvec
-// computed per hit from the event's input row (matvec_ct<IN,3*OUT>,
-// linear.h:80-90): q, v, g for the hit's patch position, then
-// h = sigmoid(g) * h + v (fmaf) and, when the layer's output is consumed,
-// qh = q * h into the compact QH rows [(entry * 9 + delta) * OUT].
-// One warp per cell (lanes = channels), 16 cells per CTA, the layer's
-// 9 x IN x 3*OUT weights staged once per CTA.  grid (P, tiles, 4).
+// k_scan_group: per-cell LRU scan of a small layer (layers 1-3: IN, OUT <= 24,
+// the 9 x IN x 3*OUT qvg weights fit in shared memory) fused with that
+// layer's qvg matvec (matvec_ct<IN,3*OUT>, linear.h:80-90).
+// Work item = (partition, 8x8 tile, 2x2 cell group), taken by one warp from
+// an atomic counter; warps never wait on one another.  The warp walks the
+// tile's ordered event list and queues, in stream order, one slot per
+// (event, cell of the group inside the event's 3x3 patch).  Per 32 slots:
+//   B) lane = slot: v and sigmoid(g) as fmaf chains over the input channels
+//      (weights from shared memory, delta rows padded to distinct banks);
+//   C) lane = (cell, channel): the cell's slots in order apply
+//      h = a * h + v (fmaf); the state after a consumed slot replaces a;
+//   D) lane = slot, slots whose output is consumed: q, then q * h into the
+//      compact QH rows [(entry * 9 + delta) * OUT] read by k_contrib.
+// One owner per cell, no atomics on state; results equal the per-event
+// reference (fmaf order over input channels, sigmoid, fmaf update, q * h).
 // ---------------------------------------------------------------------------
-template <int IN, int OUT>
-__global__ void __launch_bounds__(512) k_scan_fused(ScanFusedArgs a) {
-    constexpr int J2 = 3 * OUT;
-    constexpr int HB = (IN <= 12) ? 4 : 2;      // hits per batch
-    extern __shared__ __align__(16) float Ws[];  // [9][IN][J2]
-    const int p = blockIdx.x, tile = blockIdx.y;
+template <int IN, int OUT, int WPC>
+struct ScanGroupShape {
+    static constexpr int NT = 32 * WPC;
+    static constexpr int J2 = 3 * OUT;
+    static constexpr int DS = IN * J2 + ((IN * J2) % 32 == 16 ? 4 : ((IN * J2) % 32 == 0 ? 4 : 0));
+    static constexpr int QR = ((2 * OUT / 4) % 2 == 0) ? 2 * OUT + 4 : 2 * OUT;   // [a | v] row
+    static constexpr int QCAP = 160;                    // < 32 pending + 32 events x 4 cells
+    static constexpr int R = (4 * OUT + 31) / 32;       // (cell, channel) pairs per lane
+    static constexpr size_t per_warp = sizeof(float) * 32 * QR + (sizeof(int) + 1) * QCAP;
+    static constexpr size_t smem = sizeof(float) * 9 * DS + WPC * per_warp;
+    static_assert(IN % 4 == 0 && OUT % 4 == 0 && DS % 4 == 0, "shape");
+};
+
+template <int IN, int OUT, int WPC>
+__global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
+    using Sh = ScanGroupShape<IN, OUT, WPC>;
+    constexpr int J2 = Sh::J2, DS = Sh::DS, QR = Sh::QR, QCAP = Sh::QCAP, R = Sh::R;
+    extern __shared__ __align__(16) float dsm[];
+    float* Ws = dsm;                                              // [9][DS]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int s = a.stage;
-    for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x)
-        reinterpret_cast<float4*>(Ws)[t] = __ldg(reinterpret_cast<const float4*>(a.W) + t);
+    float* Qs = Ws + 9 * DS + warp * (Sh::per_warp / sizeof(float));   // [32][QR]
+    int* qk = reinterpret_cast<int*>(Qs + 32 * QR);                    // [QCAP] entry
+    unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<6
+    for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
+        const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
+        *reinterpret_cast<float4*>(Ws + d * DS + 4 * r) = __ldg(reinterpret_cast<const float4*>(a.W) + t);
+    }
     __syncthreads();
-    const int local = blockIdx.z * 16 + warp;              // 0..63 in the tile
-    const int cx = (tile % a.g.tx[s]) * kTile + (local % kTile);
-    const int cy = (tile / a.g.tx[s]) * kTile + (local / kTile);
+    const int s = a.stage;
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    if (cx >= Wl || cy >= Hl) return;
-    float* hp = a.parts[p].hidden[a.layer] + (static_cast<size_t>(cy) * Wl + cx) * OUT;
-    const bool lo = lane < OUT;
-    float h = lo ? hp[lane] : 0.0f;
     const int ntiles = a.g.tx[s] * a.g.ty[s];
-    const int n_p = a.range[p + 1] - a.range[p];
-    const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
-    for (int seg = 0; seg < nseg; ++seg) {
-        const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
-        const int cnt = a.tl_cnt[slot];
-        const int2* lst = a.tl + slot * a.g.seg;
-        for (int j0 = 0; j0 < cnt; j0 += 32) {
-            const int j = j0 + lane;
-            int2 ent = make_int2(0, 0);
-            if (j < cnt) ent = lst[j];
-            const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
-            const int dx = cx - ex, dy = cy - ey;
-            const bool hit = (j < cnt) && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1;
-            const int delta = (1 - dy) * 3 + (1 - dx);
-            int outf = 1;
-            if (a.second) {
-                if (s == 0) outf = (hit && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
-                else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
+    const int n_items = a.g.P * ntiles * 16;
+    float* const QH = a.QH;
+    for (;;) {
+        int item = 0;
+        if (lane == 0) item = atomicAdd(a.work, 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= n_items) break;
+        const int grp = item & 15, tile = (item >> 4) % ntiles, p = (item >> 4) / ntiles;
+        const int gx0 = (tile % a.g.tx[s]) * kTile + (grp & 3) * 2;
+        const int gy0 = (tile / a.g.tx[s]) * kTile + (grp >> 2) * 2;
+        if (gx0 >= Wl || gy0 >= Hl) continue;
+        float* const hid = a.parts[p].hidden[a.layer];
+        float h[R];
+        int hoff[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int pair = r * 32 + lane;
+            const int c = pair / OUT, ch = pair % OUT;
+            const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
+            const bool ok = pair < 4 * OUT && cx < Wl && cy < Hl;
+            hoff[r] = ok ? (cy * Wl + cx) * OUT + ch : -1;
+            h[r] = ok ? hid[hoff[r]] : 0.0f;
+        }
+        int np = 0;                                   // queued slots (warp-uniform)
+        // Runs B, C, D on the first nb (1..32) queued slots.
+        auto batch = [&](int nb) {
+            const bool valid = lane < nb;
+            const int sl = valid ? lane : 0;
+            const int k = qk[sl];
+            const int m = qm[sl];
+            const int d = m & 15, cell = (m >> 4) & 3;
+            const bool out = valid && ((m >> 6) & 1);
+            float x[IN];
+#pragma unroll
+            for (int i4 = 0; i4 < IN / 4; ++i4) {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(a.X + static_cast<size_t>(k) * IN) + i4);
+                x[4 * i4] = t.x; x[4 * i4 + 1] = t.y; x[4 * i4 + 2] = t.z; x[4 * i4 + 3] = t.w;
             }
-            const int pkf = (((ent.x << 4) | delta) << 1) | outf;
-            unsigned m = __ballot_sync(0xffffffffu, hit);
-            while (m) {
-                int kk[HB], dd[HB], of[HB];
-                int nh = 0;
+            const float* wr = Ws + d * DS;
+            float* qr = Qs + lane * QR;
+            float acc[OUT];
+            // B: a = sigmoid(g) -> [0, OUT), v -> [OUT, 2*OUT)
 #pragma unroll
-                for (int q = 0; q < HB; ++q) {
-                    const int src = m ? (__ffs(m) - 1) : 0;
-                    const int v = __shfl_sync(0xffffffffu, pkf, src);
-                    kk[q] = v >> 5;
-                    dd[q] = (v >> 1) & 15;
-                    of[q] = (m != 0u) ? (v & 1) : 0;
-                    nh += (m != 0u) ? 1 : 0;
-                    m &= (m - 1u);
-                }
-                float x[HB][IN];
+            for (int part = 2; part >= 1; --part) {
 #pragma unroll
-                for (int q = 0; q < HB; ++q) {
-                    const float4* xr = reinterpret_cast<const float4*>(a.X + static_cast<size_t>(kk[q]) * IN);
+                for (int j = 0; j < OUT; ++j) acc[j] = 0.0f;
 #pragma unroll
-                    for (int i4 = 0; i4 < IN / 4; ++i4) {
-                        const float4 t = (q < nh) ? __ldg(xr + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
-                        x[q][4 * i4] = t.x; x[q][4 * i4 + 1] = t.y;
-                        x[q][4 * i4 + 2] = t.z; x[q][4 * i4 + 3] = t.w;
+                for (int i = 0; i < IN; ++i) {
+#pragma unroll
+                    for (int j4 = 0; j4 < OUT / 4; ++j4) {
+                        const float4 w4 = *reinterpret_cast<const float4*>(wr + i * J2 + part * OUT + 4 * j4);
+                        acc[4 * j4] = fmaf(w4.x, x[i], acc[4 * j4]);
+                        acc[4 * j4 + 1] = fmaf(w4.y, x[i], acc[4 * j4 + 1]);
+                        acc[4 * j4 + 2] = fmaf(w4.z, x[i], acc[4 * j4 + 2]);
+                        acc[4 * j4 + 3] = fmaf(w4.w, x[i], acc[4 * j4 + 3]);
                     }
                 }
+                if (part == 2) {
 #pragma unroll
-                for (int q = 0; q < HB; ++q) {
-                    if (q < nh && lo) {
-                        const float* w = Ws + static_cast<size_t>(dd[q]) * IN * J2 + lane;
-                        float vq = 0.0f, vv = 0.0f, vg = 0.0f;
+                    for (int j = 0; j < OUT; ++j) acc[j] = ssla_sigmoidf(acc[j]);
+                }
+                const int col = (part == 2) ? 0 : OUT;
 #pragma unroll
-                        for (int i = 0; i < IN; ++i) {
-                            vv = fmaf(w[i * J2 + OUT], x[q][i], vv);
-                            vg = fmaf(w[i * J2 + 2 * OUT], x[q][i], vg);
-                        }
-                        const float ga = ssla_sigmoidf(vg);
-                        h = fmaf(ga, h, vv);
-                        if (of[q]) {
+                for (int j4 = 0; j4 < OUT / 4; ++j4)
+                    *reinterpret_cast<float4*>(qr + col + 4 * j4) =
+                        make_float4(acc[4 * j4], acc[4 * j4 + 1], acc[4 * j4 + 2], acc[4 * j4 + 3]);
+            }
+            unsigned cm[4];
 #pragma unroll
-                            for (int i = 0; i < IN; ++i) vq = fmaf(w[i * J2], x[q][i], vq);
-                            a.QH[(static_cast<size_t>(kk[q]) * 9 + dd[q]) * OUT + lane] = vq * h;
-                        }
+            for (int c = 0; c < 4; ++c) cm[c] = __ballot_sync(0xffffffffu, valid && cell == c);
+            const unsigned om = __ballot_sync(0xffffffffu, out);
+            __syncwarp();
+            // C: ordered updates per (cell, channel)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (hoff[r] < 0) continue;
+                const int pair = r * 32 + lane;
+                const int c = pair / OUT, ch = pair % OUT;
+                unsigned mk = (c == 0) ? cm[0] : (c == 1) ? cm[1] : (c == 2) ? cm[2] : cm[3];
+                float hc = h[r];
+                while (mk) {
+                    const int s2 = __ffs(mk) - 1;
+                    mk &= mk - 1u;
+                    float* q2 = Qs + s2 * QR;
+                    hc = fmaf(q2[ch], hc, q2[OUT + ch]);
+                    if ((om >> s2) & 1u) q2[ch] = hc;
+                }
+                h[r] = hc;
+            }
+            __syncwarp();
+            // D: q * h for consumed slots
+            if (om) {
+#pragma unroll
+                for (int j = 0; j < OUT; ++j) acc[j] = 0.0f;
+#pragma unroll
+                for (int i = 0; i < IN; ++i) {
+#pragma unroll
+                    for (int j4 = 0; j4 < OUT / 4; ++j4) {
+                        const float4 w4 = *reinterpret_cast<const float4*>(wr + i * J2 + 4 * j4);
+                        acc[4 * j4] = fmaf(w4.x, x[i], acc[4 * j4]);
+                        acc[4 * j4 + 1] = fmaf(w4.y, x[i], acc[4 * j4 + 1]);
+                        acc[4 * j4 + 2] = fmaf(w4.z, x[i], acc[4 * j4 + 2]);
+                        acc[4 * j4 + 3] = fmaf(w4.w, x[i], acc[4 * j4 + 3]);
+                    }
+                }
+                if (out) {
+                    float* dst = QH + (static_cast<size_t>(k) * 9 + d) * OUT;
+#pragma unroll
+                    for (int j4 = 0; j4 < OUT / 4; ++j4) {
+                        const float4 hv = *reinterpret_cast<const float4*>(qr + 4 * j4);
+                        *reinterpret_cast<float4*>(dst + 4 * j4) =
+                            make_float4(acc[4 * j4] * hv.x, acc[4 * j4 + 1] * hv.y,
+                                        acc[4 * j4 + 2] * hv.z, acc[4 * j4 + 3] * hv.w);
+                    }
+                }
+            }
+            __syncwarp();
+        };
+        const int n_p = a.range[p + 1] - a.range[p];
+        const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
+        for (int seg = 0; seg < nseg; ++seg) {
+            const size_t lslot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
+            const int cnt = a.tl_cnt[lslot];
+            const int2* lst = a.tl + lslot * a.g.seg;
+            for (int j0 = 0; j0 < cnt; j0 += 32) {
+                const int j = j0 + lane;
+                int2 ent = make_int2(0, 0);
+                if (j < cnt) ent = lst[j];
+                const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
+                int outf = 1;
+                if (a.second) {
+                    if (s == 0) outf = (j < cnt && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
+                    else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
+                }
+                unsigned cmask = 0;
+                if (j < cnt) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
+                        const int dx = cx - ex, dy = cy - ey;
+                        if (cx < Wl && cy < Hl && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1) cmask |= 1u << c;
+                    }
+                }
+                const int nc = __popc(cmask);
+                int incl = nc;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const int tot = __shfl_sync(0xffffffffu, incl, 31);
+                int pos = np + incl - nc;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if ((cmask >> c) & 1u) {
+                        const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
+                        const int d = (1 - (cy - ey)) * 3 + (1 - (cx - ex));
+                        qk[pos] = ent.x;
+                        qm[pos] = static_cast<unsigned char>(d | (c << 4) | (outf << 6));
+                        ++pos;
+                    }
+                }
+                np += tot;
+                __syncwarp();
+                while (np >= 32) {
+                    batch(32);
+                    np -= 32;
+                    // move the remaining queued slots to the front
+                    for (int b = 0; b < np; b += 32) {
+                        int kk = 0, mm = 0;
+                        if (b + lane < np) { kk = qk[32 + b + lane]; mm = qm[32 + b + lane]; }
+                        __syncwarp();
+                        if (b + lane < np) { qk[b + lane] = kk; qm[b + lane] = static_cast<unsigned char>(mm); }
+                        __syncwarp();
                     }
                 }
             }
         }
+        if (np > 0) batch(np);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if (hoff[r] >= 0) hid[hoff[r]] = h[r];
     }
-    if (lo) hp[lane] = h;
 }
 
 // ---------------------------------------------------------------------------
@@ -1391,17 +1524,27 @@ void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long 
 }
 
 void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
-    const int s = layer / 2;
-    const dim3 grid(a.g.P, a.g.tx[s] * a.g.ty[s], 4);
-    auto go = [&](auto kern, int IN, int OUT) {
-        const size_t smem = sizeof(float) * 9 * IN * 3 * OUT;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        kern<<<grid, 512, smem, st>>>(a);
+    auto go = [&](auto kern, auto shape) {
+        using Sh = decltype(shape);
+        static int grid = 0;                       // resident CTAs, per kernel
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Sh::smem));
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (grid == 0) {
+            int dev = 0, sms = 0, per_sm = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::NT, Sh::smem);
+            grid = std::max(1, sms * std::max(1, per_sm));
+        }
+        const int s = layer / 2;
+        const int items = a.g.P * a.g.tx[s] * a.g.ty[s] * 16;
+        const int need = (items + (Sh::NT / 32) - 1) / (Sh::NT / 32);
+        kern<<<std::min(grid, need), Sh::NT, Sh::smem, st>>>(a);
     };
     switch (layer) {
-        case 1: go(k_scan_fused<12, 12>, 12, 12); break;
-        case 2: go(k_scan_fused<12, 24>, 12, 24); break;
-        default: go(k_scan_fused<24, 24>, 24, 24); break;
+        case 1: go(k_scan_group<12, 12, 8>, ScanGroupShape<12, 12, 8>{}); break;
+        case 2: go(k_scan_group<12, 24, 16>, ScanGroupShape<12, 24, 16>{}); break;
+        default: go(k_scan_group<24, 24, 16>, ScanGroupShape<24, 24, 16>{}); break;
     }
 }
 

@@ -83,6 +83,7 @@ struct ScanFusedArgs {
     const float* X;          // [entry][IN] layer input rows
     const float* W;          // qvgT [9][IN][3*OUT]
     float* QH;               // [(entry * 9 + delta) * OUT] q * h rows
+    int* work;               // work-item counter of this launch, zero on entry
 };
 
 struct ContribArgs {
