@@ -307,6 +307,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         ca.ev_xy = la.ev_xy = w.ev_xy.as<uint32_t>();
         ca.rflags = la.rflags = w.rflags.as<uint8_t>();
         ca.S = S_rows; ca.qstride = qstride; ca.goWT = L[l].goWT; ca.C = w.C.as<float>();
+        if (s < 2) { ca.Xq = X; ca.Wq = L[l].qvgT; }
         la.C = w.C.as<float>(); la.R_in = half ? R_second : R_first; la.L = L[l]; la.X_out = X;
         la.stage_out = record ? w.stage_out[s].as<float>() : nullptr;
         la.slot_feat = (w.s_first == 2) ? w.slot_feat.as<float>() : nullptr;

@@ -621,11 +621,11 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 //   B) lane = slot: v and sigmoid(g) as fmaf chains over the input channels
 //      (weights from shared memory, delta rows padded to distinct banks);
 //   C) lane = (cell, channel): the cell's slots in order apply
-//      h = a * h + v (fmaf); the state after a consumed slot replaces a;
-//   D) lane = slot, slots whose output is consumed: q, then q * h into the
-//      compact QH rows [(entry * 9 + delta) * OUT] read by k_contrib.
+//      h = a * h + v (fmaf); after a slot whose output is consumed the
+//      state goes to the compact rows QH[(entry * 9 + delta) * OUT], where
+//      k_contrib forms q and q * h.
 // One owner per cell, no atomics on state; results equal the per-event
-// reference (fmaf order over input channels, sigmoid, fmaf update, q * h).
+// reference (fmaf order over input channels, sigmoid, fmaf update).
 // ---------------------------------------------------------------------------
 template <int IN, int OUT, int WPC>
 struct ScanGroupShape {
@@ -741,38 +741,12 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
                 while (mk) {
                     const int s2 = __ffs(mk) - 1;
                     mk &= mk - 1u;
-                    float* q2 = Qs + s2 * QR;
+                    const float* q2 = Qs + s2 * QR;
                     hc = fmaf(q2[ch], hc, q2[OUT + ch]);
-                    if ((om >> s2) & 1u) q2[ch] = hc;
+                    if ((om >> s2) & 1u)
+                        QH[(static_cast<size_t>(qk[s2]) * 9 + (qm[s2] & 15)) * OUT + ch] = hc;
                 }
                 h[r] = hc;
-            }
-            __syncwarp();
-            // D: q * h for consumed slots
-            if (om) {
-#pragma unroll
-                for (int j = 0; j < OUT; ++j) acc[j] = 0.0f;
-#pragma unroll
-                for (int i = 0; i < IN; ++i) {
-#pragma unroll
-                    for (int j4 = 0; j4 < OUT / 4; ++j4) {
-                        const float4 w4 = *reinterpret_cast<const float4*>(wr + i * J2 + 4 * j4);
-                        acc[4 * j4] = fmaf(w4.x, x[i], acc[4 * j4]);
-                        acc[4 * j4 + 1] = fmaf(w4.y, x[i], acc[4 * j4 + 1]);
-                        acc[4 * j4 + 2] = fmaf(w4.z, x[i], acc[4 * j4 + 2]);
-                        acc[4 * j4 + 3] = fmaf(w4.w, x[i], acc[4 * j4 + 3]);
-                    }
-                }
-                if (out) {
-                    float* dst = QH + (static_cast<size_t>(k) * 9 + d) * OUT;
-#pragma unroll
-                    for (int j4 = 0; j4 < OUT / 4; ++j4) {
-                        const float4 hv = *reinterpret_cast<const float4*>(qr + 4 * j4);
-                        *reinterpret_cast<float4*>(dst + 4 * j4) =
-                            make_float4(acc[4 * j4] * hv.x, acc[4 * j4 + 1] * hv.y,
-                                        acc[4 * j4 + 2] * hv.z, acc[4 * j4 + 3] * hv.w);
-                    }
-                }
             }
             __syncwarp();
         };
@@ -852,21 +826,27 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
 // vectors (one contiguous S row segment each) and goW[delta] are staged in
 // shared memory with batched 16-byte loads; a thread owns 8 rows x 3 outputs.
 // Rows whose patch position is out of bounds are skipped (never read).
+// QIN > 0 (layers 1-3): the staged rows are the cell states after each
+// consumed hit; the tile's q = fmaf chain over i of qvgT[delta][i][o] *
+// x[row][i] (matvec_ct, linear.h:80-90) is computed first, with the same
+// thread tiling, and q * h replaces each staged value.
 // ---------------------------------------------------------------------------
-template <int A, int OUT>
+template <int A, int OUT, int QIN = 0>
 struct ContribShape {
     static constexpr int CG = OUT / 3;           // column groups
     static constexpr int RG = kNT / CG;          // row groups
     static constexpr int BM = RG * 8;            // rows per tile
     static constexpr int BMP = BM + 4;           // padded transposed stride
     static constexpr size_t smem = sizeof(float) * (static_cast<size_t>(OUT) * OUT +
-                                                    static_cast<size_t>(OUT) * BMP) +
+                                                    static_cast<size_t>(OUT) * BMP +
+                                                    static_cast<size_t>(QIN) * OUT +
+                                                    static_cast<size_t>(QIN) * BMP) +
                                    sizeof(int) * BM;
 };
 
-template <int A, int OUT>
+template <int A, int OUT, int QIN = 0>
 __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
-    using Sh = ContribShape<A, OUT>;
+    using Sh = ContribShape<A, OUT, QIN>;
     constexpr int BM = Sh::BM, BMP = Sh::BMP, CG = Sh::CG;
     constexpr int Q4 = OUT / 4;                  // float4 per qh row
     constexpr int NA = (BM * Q4 + kNT - 1) / kNT;
@@ -874,7 +854,9 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
     extern __shared__ __align__(16) float dsm[];
     float* Bs = dsm;                             // [OUT][OUT]  goWT[delta] (i-major)
     float* As = Bs + OUT * OUT;                  // [OUT][BMP]  qh rows, transposed
-    int* srow_s = reinterpret_cast<int*>(As + OUT * BMP);   // S row or -1
+    float* Wqs = As + OUT * BMP;                 // [QIN][OUT]  q weights of delta
+    float* Xs = Wqs + QIN * OUT;                 // [QIN][BMP]  input rows, transposed
+    int* srow_s = reinterpret_cast<int*>(Xs + QIN * BMP);   // S row or -1
     const int tid = threadIdx.x;
     const int cg = tid % CG, rg = tid / CG;
     const int s = a.stage;
@@ -939,6 +921,50 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
                     As[(4 * k4 + 3) * BMP + r] = av[q].w;
                 }
             }
+        }
+        if constexpr (QIN > 0) {
+            for (int t = tid; t < QIN * OUT; t += kNT) {
+                const int i = t / OUT, c = t % OUT;
+                Wqs[t] = __ldg(a.Wq + (static_cast<size_t>(d) * QIN + i) * (3 * OUT) + c);
+            }
+            for (int t = tid; t < BM * (QIN / 4); t += kNT) {
+                const int r = t % BM, k4 = t / BM;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (srow_s[r] >= 0)
+                    v = __ldg(reinterpret_cast<const float4*>(a.Xq + static_cast<size_t>(srow_s[r]) * QIN) + k4);
+                Xs[(4 * k4 + 0) * BMP + r] = v.x;
+                Xs[(4 * k4 + 1) * BMP + r] = v.y;
+                Xs[(4 * k4 + 2) * BMP + r] = v.z;
+                Xs[(4 * k4 + 3) * BMP + r] = v.w;
+            }
+            __syncthreads();
+            float qa[8][3];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) qa[i][j] = 0.0f;
+#pragma unroll 4
+            for (int k = 0; k < QIN; ++k) {
+                const float4 x0 = *reinterpret_cast<const float4*>(Xs + k * BMP + rg * 8);
+                const float4 x1 = *reinterpret_cast<const float4*>(Xs + k * BMP + rg * 8 + 4);
+                const float w0 = Wqs[k * OUT + cg * 3 + 0];
+                const float w1 = Wqs[k * OUT + cg * 3 + 1];
+                const float w2 = Wqs[k * OUT + cg * 3 + 2];
+                const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    qa[i][0] = fmaf(w0, x[i], qa[i][0]);
+                    qa[i][1] = fmaf(w1, x[i], qa[i][1]);
+                    qa[i][2] = fmaf(w2, x[i], qa[i][2]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    float* e = As + (cg * 3 + j) * BMP + rg * 8 + i;
+                    *e = qa[i][j] * *e;
+                }
         }
         __syncthreads();
         float acc[8][3];
@@ -1516,8 +1542,9 @@ void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long 
     };
     switch (layer) {
         case 0: go(k_contrib<1, 12>, ContribShape<1, 12>{}); break;
-        case 1: go(k_contrib<9, 12>, ContribShape<9, 12>{}); break;
-        case 2: case 3: go(k_contrib<9, 24>, ContribShape<9, 24>{}); break;
+        case 1: go(k_contrib<9, 12, 12>, ContribShape<9, 12, 12>{}); break;
+        case 2: go(k_contrib<9, 24, 12>, ContribShape<9, 24, 12>{}); break;
+        case 3: go(k_contrib<9, 24, 24>, ContribShape<9, 24, 24>{}); break;
         case 4: case 5: go(k_contrib<9, 48>, ContribShape<9, 48>{}); break;
         default: go(k_contrib<9, 96>, ContribShape<9, 96>{}); break;
     }

@@ -100,6 +100,10 @@ struct ContribArgs {
     int qstride;             // 3*OUT (GEMM-fed S rows) or OUT (compact QH rows)
     const float* goWT;       // [A][OUT][OUT]
     float* C;                // [row][A][OUT] contributions
+    // Stages 0-1: S holds the state after each consumed hit (h, not q * h);
+    // q = X row . qvgT[delta][:, 0:OUT] is formed here and multiplied in.
+    const float* Xq;         // [row][IN] layer input rows
+    const float* Wq;         // qvgT [9][IN][3*OUT]
 };
 
 struct LnArgs {
