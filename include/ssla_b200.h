@@ -152,6 +152,25 @@ int  ssla_s2s3_drain_n(const HybridS2S3Config* cfg,
                        unsigned long long* batch_clk0,
                        unsigned long long* batch_clk1, void* stream);
 
+/* Allocation-free gate pass.  No counterpart in the reference: its drain
+ * kernels always run the full layer stack.  For callers that cannot allocate
+ * device or pinned memory at the call site (a per-batch real-time loop where
+ * cudaMalloc / cudaFree may synchronise the device, or a host whose device
+ * memory is owned by another runtime's pool): evaluates the stage-2 and
+ * stage-3 tdrop gates of ssla_s2s3_drain_n_multi for every record (ring
+ * order per block), advances cfg's tdrop counters in place and writes the
+ * pass2 / pass3 codes of each output slot exactly as the drain would; hidden
+ * state and s3_feat are untouched.  Scratch lives in a fixed file-scope
+ * device array: at most SSLA_NOALLOC_MAX_RECORDS records per call (larger
+ * calls fail with SSLA_ERR_CAPACITY).  Enqueues on `stream` and returns
+ * without synchronising.  The first call on a device looks the scratch array
+ * up and should precede any stream capture on that device; calls that
+ * overlap in time on one device share the scratch and race. */
+#define SSLA_NOALLOC_MAX_RECORDS 65536
+int  ssla_s2s3_gate_codes_noalloc(const HybridS2S3Config* cfg,
+                                  const HybridInputRec* const* rings, const int* ns,
+                                  HybridS2S3OutputSlot* const* outs, void* stream);
+
 /* Per-phase timing (the analogue of the reference's clock64 phase stamps,
  * orin/kernels/ssla_s2_s3_head_celled_profile.cuh:17-40): when enabled,
  * every drain records a CUDA event after each phase on its stream;

@@ -90,5 +90,6 @@ EXPORTED = (
     "ssla_engine_read_state", "ssla_engine_write_state", "ssla_engine_state_ptr",
     "ssla_engine_info", "ssla_s2s3_drain_n_multi", "ssla_s2s3_drain_n",
     "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak",
-    "ssla_expf_host", "ssla_last_error", "ssla_version",
+    "ssla_expf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
 )
+NOALLOC_MAX_RECORDS = 65536

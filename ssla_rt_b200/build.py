@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libssla_b200.so")
-SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp"]
+SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp", "ssla_noalloc.cu"]
 HEADERS = ["ssla_device.cuh", "ssla_kernels.cuh", "ssla_weights.h"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
               "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-shared",

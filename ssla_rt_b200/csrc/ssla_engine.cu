@@ -340,6 +340,9 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
 
 }  // namespace
 
+// Error text of the calling thread, for entry points defined in other files.
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
 // ---------------------------------------------------------------------------
 // Engine
 // ---------------------------------------------------------------------------

@@ -51,6 +51,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_info": (i, [vp, C.POINTER(abi.SslaEngineInfo)]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
         "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
+        "ssla_s2s3_gate_codes_noalloc": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp]),
         "ssla_engine_set_profiling": (i, [vp, i]),
         "ssla_engine_phase_times": (i, [vp, vp, i, C.POINTER(C.c_int)]),
         "ssla_measure_fp32_peak": (i, [i, C.POINTER(C.c_double)]),
@@ -220,3 +221,17 @@ def drain_n_multi(cfg: abi.HybridS2S3Config, rings: Sequence[int], ns: Sequence[
                                        C.cast(o, C.c_void_p) if o is not None else None,
                                        C.cast(k, C.c_void_p) if k is not None else None,
                                        _stream(stream)))
+
+
+def gate_codes_noalloc(cfg: abi.HybridS2S3Config, rings: Sequence[int], ns: Sequence[int],
+                       outs: Optional[Sequence[int]] = None, stream=None) -> None:
+    """Allocation-free gate pass (ssla_s2s3_gate_codes_noalloc): pass2 / pass3
+    codes and tdrop counter updates of a drain_n call, enqueued on `stream`."""
+    lib = load_library()
+    P = len(rings)
+    r = (C.c_void_p * P)(*rings)
+    n = (C.c_int * P)(*ns)
+    o = (C.c_void_p * P)(*outs) if outs is not None else None
+    _check(lib.ssla_s2s3_gate_codes_noalloc(C.byref(cfg), C.cast(r, C.c_void_p), C.cast(n, C.c_void_p),
+                                            C.cast(o, C.c_void_p) if o is not None else None,
+                                            _stream(stream)))
