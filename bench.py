@@ -190,6 +190,53 @@ def cpu_baseline(parts, weights_dir: str, reps: int = 3) -> dict:
                       f"{len(parts[0])} events, one host thread per stream, best of {reps}"}
 
 
+def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
+                    warmup: int = 50, samples: int = 1000) -> dict:
+    """Batch-of-1 emit -> prediction latency of a live stream: a 1-partition
+    engine sized for small batches; each sample hands one event (pinned host
+    memory) to ssla_engine_drain_host and reads the partition's decoded
+    predictions back.  Host wall time per event, p50 / p99 in us."""
+    import torch
+    from ssla_rt_b200 import abi
+    from ssla_rt_b200.engine import SslaEngine
+    eng = SslaEngine(weights_dir, n_partitions=1, max_events=64, layout=abi.LAYOUT_HYBRID,
+                     device=device)
+    off = eng.offsets([1])
+    one = torch.empty((1, 4), dtype=torch.float32).pin_memory().numpy()
+    flag = torch.empty(1, dtype=torch.uint8).pin_memory().numpy()
+    lat, head = [], 0
+    for i in range(warmup + samples):
+        one[0] = stream_events[i % len(stream_events)]
+        one[0, 0] += (i // len(stream_events)) * 1e6
+        t0 = time.perf_counter()
+        eng.drain_host(one, off, flag)
+        eng.preds_dec(0)
+        t1 = time.perf_counter()
+        if i >= warmup:
+            lat.append((t1 - t0) * 1e6)
+            head += int(flag[0] & abi.F_R4 != 0)
+    eng.close()
+    lat.sort()
+    return {"p50": lat[len(lat) // 2], "p99": lat[int(len(lat) * 0.99) - 1], "n": len(lat),
+            "head_events": head,
+            "method": "host wall time of one event through ssla_engine_drain_host (pinned host "
+                      "event in, flags out) plus the predictions read-back; the drain runs the "
+                      "same fixed kernel sequence whether or not the event reaches the head"}
+
+
+def measured_traffic(phase: str):
+    """DRAM bytes per launch of `phase` from the committed ncu summary
+    (profiles/traffic.json: dram__bytes_read.sum + dram__bytes_write.sum of
+    the phase's kernel on this workload), or None."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            t = json.load(f)
+        return t[phase]["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
 def run_reference(args, rank: int) -> None:
     if rank != 0:
         return
@@ -244,6 +291,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-latency", action="store_true", help="skip the batch-of-1 latency samples")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -356,6 +404,9 @@ def main() -> int:
     e2e = world * N_EVENTS * args.steps / e2e_total / 1e6
     d2h = N_EVENTS + sum(p.nbytes for p in preds)
 
+    # ---- batch-of-1 latency: one event in, its predictions out ----
+    latency = None if args.no_latency else measure_latency(wdir, parts[0], local)
+
     # ---- roofline of the dominant phase (live CUDA-event durations) ----
     flags_dev = torch.zeros(N_EVENTS, dtype=torch.uint8, device=dev)
     eng.drain(ev, off, flags=flags_dev, stream=stream)
@@ -372,7 +423,7 @@ def main() -> int:
         "kernel": dom_name, "bound": "fp32",
         "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
         "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
-        "traffic": None,
+        "traffic": measured_traffic(dom_name),
         "peak_source": "measured FFMA peak (ssla_measure_fp32_peak, this run); the path is FP32 "
                        "CUDA-core work, MEASURED_PEAKS.json holds only HBM and bf16 tensor peaks",
         "avg_ms": dom_ms, "algorithmic_flops_per_launch": dflops,
@@ -393,6 +444,7 @@ def main() -> int:
             "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(ev_np.nbytes),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
+            "latency_us": latency,
             "algorithmic_mac_per_event": tot_macs / N_EVENTS,
             "stage_events": [int(x) for x in eng.info().stage_events],
             "phase_ms": phases,

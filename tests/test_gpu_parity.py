@@ -151,3 +151,27 @@ def test_capacity_errors_are_reported(stub_dir):
     with pytest.raises(SslaError) as ei:
         eng.drain(ev, np.array([0, 60, 50], np.int32))
     assert ei.value.code == abi.SSLA_ERR_ARG
+
+
+def test_config1_full_size(oracle_mod, stub_dir):
+    """The bench workload itself (config 1: 200,000 uniform events at 80x64 in
+    8 partitions of 25,000, HYBRID gates), two consecutive drains (the
+    streams continue), compared exactly with the oracle run over the same
+    event streams."""
+    d = stub_dir(64, 80, 1, 4)
+    parts = E.split_partitions(E.config_events(1), 8)
+    span = float(max(p[:, 0].max() for p in parts)) + 1.0
+    second = [p.copy() for p in parts]
+    for p in second:
+        p[:, 0] += span
+    eng = _engine(d, n_partitions=8, max_events=200_000, layout=abi.LAYOUT_HYBRID,
+                  record_stage_outputs=True, max_events_per_partition=max(len(p) for p in parts))
+    drain_device(eng, parts)
+    drain_device(eng, second)
+    oracles = []
+    for a, b in zip(parts, second):
+        orc = oracle_mod.Oracle(oracle_mod.load_npz(d), 64, 80, 4, abi.LAYOUT_HYBRID)
+        orc.run_events(a, want_stage_out=False)
+        flags, so = orc.run_events(b)
+        oracles.append((orc, flags, so))
+    assert_engine_equals_oracle(eng, oracles, second, abi.LAYOUT_HYBRID)
