@@ -35,7 +35,13 @@ float or_expf(float x) {
     if (x != x) return x;                              /* NaN */
     if (x > 88.8f) return INFINITY;
     if (x < -104.0f) return 0.0f;
-    const float n = rintf(x * 1.44269502f);            /* nearest, ties even */
+    /* n = nearest integer to x*log2(e), ties to even: adding 1.5*2^23 leaves
+     * an integer-spaced float (|x*log2e| < 2^22 here), so the sum rounds
+     * exactly as rintf would and the subtraction is exact; the integer is
+     * read from the sum's low mantissa bits. */
+    union { float f; int32_t i; } big;
+    big.f = x * 1.44269502f + 12582912.0f;
+    const float n = big.f - 12582912.0f;
     float r = fmaf(-n, 0.693115234375f, x);
     r = fmaf(-n, 3.19461833e-05f, r);
     float p = 1.98412701e-04f;                         /* 1/7! */
@@ -46,7 +52,7 @@ float or_expf(float x) {
     p = fmaf(p, r, 0.5f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    const int ni = (int)n;                             /* -150 .. 129 */
+    const int ni = big.i - 0x4B400000;                 /* -150 .. 129 */
     const int n1 = ni / 2;
     const int n2 = ni - n1;
     return (p * pow2i(n1)) * pow2i(n2);

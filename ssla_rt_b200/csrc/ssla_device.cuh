@@ -107,7 +107,10 @@ __host__ __device__ __forceinline__ float ssla_expf(float x) {
     if (x != x) return x;
     if (x > 88.8f) return __builtin_huge_valf();
     if (x < -104.0f) return 0.0f;
-    const float n = rintf(x * 1.44269502f);
+    // nearest integer, ties to even, without a conversion instruction
+    // (1.5 * 2^23 trick; |x * log2e| < 2^22 after the range checks)
+    const float big = x * 1.44269502f + 12582912.0f;
+    const float n = big - 12582912.0f;
     float r = fmaf(-n, 0.693115234375f, x);
     r = fmaf(-n, 3.19461833e-05f, r);
     float p = 1.98412701e-04f;
@@ -118,7 +121,13 @@ __host__ __device__ __forceinline__ float ssla_expf(float x) {
     p = fmaf(p, r, 0.5f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    const int ni = static_cast<int>(n);
+#ifdef __CUDA_ARCH__
+    const int ni = __float_as_int(big) - 0x4B400000;
+#else
+    union { float f; int32_t i; } bb;
+    bb.f = big;
+    const int ni = bb.i - 0x4B400000;
+#endif
     const int n1 = ni / 2;
     const int n2 = ni - n1;
     return (p * ssla_pow2i(n1)) * ssla_pow2i(n2);

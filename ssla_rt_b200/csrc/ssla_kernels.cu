@@ -150,22 +150,31 @@ __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// k_gates: one warp per (partition, s3 block).  Walks the block's own events
-// in stream order (from the stage-0 tile list of the block) and computes
-//   preprocess  dt_norm = clamp((t - last_t[pix]) / 1e5, 0, 1), 1 on a first
-//               hit (src/ssla_kernels.cpp:288-309)
-//   gate 0 / 1 / 2 / 3 on the layout's grids (all cells of an event's gates
-//               lie inside its s3 block, so the block owns every counter it
-//               touches)
-//   layer 0 entirely (K = 1: the event's own pixel), writing its output row
-//               and, for events entering stage 1, the layer-1 residual.
-// Same-key ordering inside a 32-event window uses __match_any_sync ranks.
+// k_gates: one 4-warp CTA per (partition, s3 block).
+//   Phase 1 (warp 0): walks the block's own events in stream order (the
+//     stage-0 tile list of the block, next window prefetched) and computes
+//       the previous timestamp of the event's pixel (preprocess,
+//         src/ssla_kernels.cpp:288-309; the pixel's last_t advances),
+//       gate 0 / 1 / 2 / 3 on the layout's grids (all cells of an event's
+//         gates lie inside its s3 block, so the block owns every counter
+//         it touches; same-key order inside a window by __match_any_sync),
+//     writing the event's flags and buffering (entry, pixel, previous t,
+//     t, p, pass0) of up to kGateBuf events.
+//   Phase 2 (all warps): warp w owns the pixels with x % 4 == w and runs
+//     layer 0 (K = 1, the event's own pixel) on its buffered events in full
+//     32-lane batches: dt_norm, qvg, the pixel's lru_step in stream order
+//     (same-pixel lanes take turns by rank), goW contribution, residual and
+//     LayerNorm (layer_forward_ct, src/ssla_kernels.cpp:315-385), writing
+//     the output row and, for events entering stage 1, the layer-1 residual.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(32) k_gates(GateArgs a) {
+constexpr int kGateBuf = 256;
+constexpr int kGateWarps = 4;
+
+__global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
     const int p = blockIdx.x, blk = blockIdx.y;
     const int W3 = a.g.W[3];
     const int bx = blk % W3, by = blk / W3;
-    const int lane = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const PartState ps = a.parts[p];
     const bool hyb = a.g.layout == LAYOUT_HYBRID;
     const int window = a.g.window;
@@ -174,100 +183,162 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
     // layer-0 weights: qvgT [2][36] | ipT [2][12] | goWT [12][12] | gamma | beta
     __shared__ float w0[264];
     __shared__ float h0[64 * 12];
+    __shared__ double b_prev[kGateBuf];
+    __shared__ float b_t[kGateBuf], b_p[kGateBuf];
+    __shared__ int b_k[kGateBuf];
+    __shared__ unsigned char b_pix[kGateBuf], b_pass0[kGateBuf];
+    __shared__ unsigned short wl[kGateWarps][kGateBuf];
+    __shared__ int b_n, b_done;
     const int W0 = a.g.W[0], W1 = a.g.W[1], W2 = a.g.W[2];
-    for (int i = lane; i < 72; i += 32) w0[i] = a.L0.qvgT[i];
-    for (int i = lane; i < 24; i += 32) w0[72 + i] = a.L0.ipT[i];
-    for (int i = lane; i < 144; i += 32) w0[96 + i] = a.L0.goWT[i];
-    if (lane < 12) { w0[240 + lane] = a.L0.gamma[lane]; w0[252 + lane] = a.L0.beta[lane]; }
-    for (int i = lane; i < 64 * 12; i += 32) {
+    for (int i = tid; i < 72; i += blockDim.x) w0[i] = a.L0.qvgT[i];
+    for (int i = tid; i < 24; i += blockDim.x) w0[72 + i] = a.L0.ipT[i];
+    for (int i = tid; i < 144; i += blockDim.x) w0[96 + i] = a.L0.goWT[i];
+    if (tid < 12) { w0[240 + tid] = a.L0.gamma[tid]; w0[252 + tid] = a.L0.beta[tid]; }
+    for (int i = tid; i < 64 * 12; i += blockDim.x) {
         const int px = i / 12, c = i % 12;
         h0[i] = ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c];
     }
-    for (int i = lane; i < 64; i += 32)
+    for (int i = tid; i < 64; i += blockDim.x)
         lt[i] = ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)];
-    if (lane < 16) c0[lane] = ps.cnt[0][(by * 4 + lane / 4) * W1 + bx * 4 + (lane % 4)];
-    if (lane < 4) c1[lane] = ps.cnt[1][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)];
+    if (tid < 16) c0[tid] = ps.cnt[0][(by * 4 + tid / 4) * W1 + bx * 4 + (tid % 4)];
+    if (tid < 4) c1[tid] = ps.cnt[1][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
     if (hyb) {
-        if (lane < 4) c2[lane] = ps.cnt[2][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)];
-        if (lane == 0) c3[0] = ps.cnt[3][by * W3 + bx];
-    } else if (lane == 0) {
+        if (tid < 4) c2[tid] = ps.cnt[2][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
+        if (tid == 0) c3[0] = ps.cnt[3][by * W3 + bx];
+    } else if (tid == 0) {
         c2[0] = ps.cnt[2][by * W3 + bx];
     }
-    __syncwarp();
+    __syncthreads();
 
     const int ntiles = a.g.tx[0] * a.g.ty[0];
     const int tile = by * a.g.tx[0] + bx;     // s0 tiles are the s3 blocks
     const int n_p = a.ev_off[p + 1] - a.ev_off[p];
     const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[0]);
-    for (int seg = 0; seg < nseg; ++seg) {
-        const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0] + seg;
-        const int cnt = a.tl0_cnt[slot];
-        const int2* lst = a.tl0 + slot * a.g.seg;
-        for (int j0 = 0; j0 < cnt; j0 += 32) {
-            const int j = j0 + lane;
-            int2 ent = make_int2(0, 0);
-            if (j < cnt) ent = lst[j];
-            const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
-            const bool own = (j < cnt) && (x0 >> 3) == bx && (y0 >> 3) == by;
-            if (__ballot_sync(0xffffffffu, own) == 0u) continue;
-            const int k = ent.x;
-            float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (own) e = a.ev[k];
-            // preprocess
-            const int pix = own ? ((y0 & 7) * 8 + (x0 & 7)) : (64 + lane);
-            const unsigned peers = __match_any_sync(0xffffffffu, pix);
-            const unsigned prevm = peers & lanemask_lt();
-            const int src = prevm ? hi_lane(prevm) : lane;
-            const float t_prev_lane = __shfl_sync(0xffffffffu, e.x, src);
+    // phase-1 cursor and prefetched window (warp 0 only)
+    int seg = 0, j0 = 0, cnt = -1;
+    const int2* lst = nullptr;
+    int2 ent_n = make_int2(0, 0);
+    float4 ev_n = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool own_n = false, have_n = false;
+    auto prefetch = [&]() {
+        have_n = false;
+        while (seg < nseg) {
+            if (cnt < 0) {
+                const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0] + seg;
+                cnt = a.tl0_cnt[slot];
+                lst = a.tl0 + slot * a.g.seg;
+                j0 = 0;
+            }
+            if (j0 < cnt) {
+                const int j = j0 + lane;
+                ent_n = make_int2(0, 0);
+                if (j < cnt) ent_n = lst[j];
+                const int x0 = ent_n.y & 0xFFFF, y0 = (ent_n.y >> 16) & 0x7FFF;
+                own_n = (j < cnt) && (x0 >> 3) == bx && (y0 >> 3) == by;
+                ev_n = own_n ? a.ev[ent_n.x] : make_float4(0.f, 0.f, 0.f, 0.f);
+                j0 += 32;
+                have_n = true;
+                return;
+            }
+            ++seg;
+            cnt = -1;
+        }
+    };
+    if (warp == 0) prefetch();
+
+    for (;;) {
+        // ---- phase 1: gates and previous timestamps, buffer the own events
+        if (warp == 0) {
+            int n = 0;
+            while (have_n && n <= kGateBuf - 32) {
+                const int2 ent = ent_n;
+                const float4 e = ev_n;
+                const bool own = own_n;
+                prefetch();                          // next window in flight
+                const unsigned om = __ballot_sync(0xffffffffu, own);
+                if (om == 0u) continue;
+                const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
+                const int k = ent.x;
+                const int pix = own ? ((y0 & 7) * 8 + (x0 & 7)) : (64 + lane);
+                const unsigned peers = __match_any_sync(0xffffffffu, pix);
+                const unsigned prevm = peers & lanemask_lt();
+                const int src = prevm ? hi_lane(prevm) : lane;
+                const float t_prev_lane = __shfl_sync(0xffffffffu, e.x, src);
+                double prev = 0.0;
+                if (own) prev = prevm ? static_cast<double>(t_prev_lane) : lt[pix];
+                __syncwarp();
+                if (own && lane == hi_lane(peers)) lt[pix] = static_cast<double>(e.x);
+                __syncwarp();
+                const int k0 = own ? (((y0 >> 1) & 3) * 4 + ((x0 >> 1) & 3)) : (100 + lane);
+                const bool pass0 = warp_gate(own, k0, c0, window);
+                const bool in1 = own && pass0;
+                const int sub2 = ((y0 >> 2) & 1) * 2 + ((x0 >> 2) & 1);
+                const bool pass1 = warp_gate(in1, in1 ? sub2 : 100 + lane, c1, window);
+                const bool in2 = in1 && pass1;
+                const bool pass2 = warp_gate(in2, in2 ? (hyb ? sub2 : 0) : 100 + lane, c2, window);
+                const bool in3 = in2 && pass2;
+                bool pass3 = true;
+                if (hyb) pass3 = warp_gate(in3, in3 ? 0 : 100 + lane, c3, window);
+                if (own) {
+                    uint8_t f = F_VALID;
+                    if (pass0) f |= F_R1;
+                    if (in2) f |= F_R2;
+                    if (in3) f |= F_R3;
+                    if (in3 && pass3) f |= F_R4;
+                    a.rflags[k] = f;
+                    const int pos = n + __popc(om & lanemask_lt());
+                    b_k[pos] = k;
+                    b_pix[pos] = static_cast<unsigned char>(pix);
+                    b_prev[pos] = prev;
+                    b_t[pos] = e.x;
+                    b_p[pos] = e.w;
+                    b_pass0[pos] = pass0 ? 1 : 0;
+                }
+                n += __popc(om);
+            }
+            if (lane == 0) { b_n = n; b_done = have_n ? 0 : 1; }
+        }
+        __syncthreads();
+        const int n = b_n;
+        const int done = b_done;
+        // ---- phase 2: layer 0 of the buffered events, pixel-partitioned
+        int my_n = 0;
+        for (int base = 0; base < n; base += 32) {
+            const int i = base + lane;
+            const bool mine = i < n && (b_pix[i] & 3) == warp;
+            const unsigned m = __ballot_sync(0xffffffffu, mine);
+            if (mine) wl[warp][my_n + __popc(m & lanemask_lt())] = static_cast<unsigned short>(i);
+            my_n += __popc(m);
+        }
+        __syncwarp();
+        for (int b0 = 0; b0 < my_n; b0 += 32) {
+            const bool own = b0 + lane < my_n;
+            const int idx = own ? wl[warp][b0 + lane] : 0;
+            const int k = b_k[idx];
+            const int pix = own ? b_pix[idx] : (64 + lane);
+            const float ep = b_p[idx];
             float dt = 0.0f;
             if (own) {
-                const double prev = prevm ? static_cast<double>(t_prev_lane) : lt[pix];
+                const double prev = b_prev[idx];
                 if (prev < 0.0) {
                     dt = 1.0f;
                 } else {
-                    double v = (static_cast<double>(e.x) - prev) / 1e5;
+                    double v = (static_cast<double>(b_t[idx]) - prev) / 1e5;
                     if (v < 0.0) v = 0.0;
                     if (v > 1.0) v = 1.0;
                     dt = static_cast<float>(v);
                 }
             }
-            __syncwarp();
-            if (own && lane == hi_lane(peers)) lt[pix] = static_cast<double>(e.x);
-            __syncwarp();
-            // gates
-            const int k0 = own ? (((y0 >> 1) & 3) * 4 + ((x0 >> 1) & 3)) : (100 + lane);
-            const bool pass0 = warp_gate(own, k0, c0, window);
-            const bool in1 = own && pass0;
-            const int sub2 = ((y0 >> 2) & 1) * 2 + ((x0 >> 2) & 1);
-            const bool pass1 = warp_gate(in1, in1 ? sub2 : 100 + lane, c1, window);
-            const bool in2 = in1 && pass1;
-            const bool pass2 = warp_gate(in2, in2 ? (hyb ? sub2 : 0) : 100 + lane, c2, window);
-            const bool in3 = in2 && pass2;
-            bool pass3 = true;
-            if (hyb) pass3 = warp_gate(in3, in3 ? 0 : 100 + lane, c3, window);
-            if (own) {
-                uint8_t f = F_VALID;
-                if (pass0) f |= F_R1;
-                if (in2) f |= F_R2;
-                if (in3) f |= F_R3;
-                if (in3 && pass3) f |= F_R4;
-                a.rflags[k] = f;
-            }
-            // ---- layer 0 (K = 1, 2 -> 12), one lane per event: qvg
-            // (matvec_ct<2,36>), residual (matvec_ct<2,12>), the pixel's
-            // lru_step in stream order (same-pixel lanes take turns by rank),
-            // the goW contribution, residual add and LayerNorm
-            // (layer_forward_ct, src/ssla_kernels.cpp:315-385). ----
-            float q[12], v[12], ag[12], res[12], qh[12];
+            // v and sigmoid(g); the pixel's state after this event -> hh
+            float v[12], ag[12], hh[12];
             if (own) {
 #pragma unroll
                 for (int c = 0; c < 12; ++c) {
-                    q[c] = fmaf(w0[36 + c], e.w, fmaf(w0[c], dt, 0.0f));
-                    v[c] = fmaf(w0[36 + 12 + c], e.w, fmaf(w0[12 + c], dt, 0.0f));
-                    ag[c] = ssla_sigmoidf(fmaf(w0[36 + 24 + c], e.w, fmaf(w0[24 + c], dt, 0.0f)));
-                    res[c] = fmaf(w0[72 + 12 + c], e.w, fmaf(w0[72 + c], dt, 0.0f));
+                    v[c] = fmaf(w0[36 + 12 + c], ep, fmaf(w0[12 + c], dt, 0.0f));
+                    ag[c] = ssla_sigmoidf(fmaf(w0[36 + 24 + c], ep, fmaf(w0[24 + c], dt, 0.0f)));
                 }
             }
+            const unsigned peers = __match_any_sync(0xffffffffu, pix);
             const int rank = __popc(peers & lanemask_lt());
             const int rounds = __reduce_max_sync(0xffffffffu, own ? rank + 1 : 0);
             for (int rd = 0; rd < rounds; ++rd) {
@@ -277,20 +348,23 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
                     for (int c = 0; c < 12; ++c) {
                         const float hc = fmaf(ag[c], h[c], v[c]);
                         h[c] = hc;
-                        qh[c] = q[c] * hc;
+                        hh[c] = hc;
                     }
                 }
                 __syncwarp();
             }
             if (own) {
+                // qh = q * h (q = qvg rows 0..11), goW contribution + residual
+#pragma unroll
+                for (int c = 0; c < 12; ++c) hh[c] = fmaf(w0[36 + c], ep, fmaf(w0[c], dt, 0.0f)) * hh[c];
                 float y[12];
                 double sum = 0.0;
 #pragma unroll
                 for (int o = 0; o < 12; ++o) {
                     float acc = 0.0f;
 #pragma unroll
-                    for (int i = 0; i < 12; ++i) acc = fmaf(w0[96 + i * 12 + o], qh[i], acc);
-                    y[o] = (0.0f + acc) + res[o];
+                    for (int i = 0; i < 12; ++i) acc = fmaf(w0[96 + i * 12 + o], hh[i], acc);
+                    y[o] = (0.0f + acc) + fmaf(w0[72 + 12 + o], ep, fmaf(w0[72 + o], dt, 0.0f));
                     sum += static_cast<double>(y[o]);
                 }
                 const double mean = sum / 12.0;
@@ -303,7 +377,7 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
                 var /= 12.0;
                 const double inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
                 float* xo = a.X1 + static_cast<size_t>(k) * 12;
-                float* rc = (pass0 && a.Rcopy) ? a.Rcopy + static_cast<size_t>(k) * 12 : nullptr;
+                float* rc = (b_pass0[idx] && a.Rcopy) ? a.Rcopy + static_cast<size_t>(k) * 12 : nullptr;
 #pragma unroll
                 for (int o = 0; o < 12; ++o) {
                     const double t = (static_cast<double>(y[o]) - mean) * inv;
@@ -314,20 +388,21 @@ __global__ void __launch_bounds__(32) k_gates(GateArgs a) {
                 }
             }
         }
+        __syncthreads();
+        if (done) break;
     }
-    __syncwarp();
-    for (int i = lane; i < 64; i += 32)
+    for (int i = tid; i < 64; i += blockDim.x)
         ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)] = lt[i];
-    for (int i = lane; i < 64 * 12; i += 32) {
+    for (int i = tid; i < 64 * 12; i += blockDim.x) {
         const int px = i / 12, c = i % 12;
         ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c] = h0[i];
     }
-    if (lane < 16) ps.cnt[0][(by * 4 + lane / 4) * W1 + bx * 4 + (lane % 4)] = static_cast<uint8_t>(c0[lane]);
-    if (lane < 4) ps.cnt[1][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)] = static_cast<uint8_t>(c1[lane]);
+    if (tid < 16) ps.cnt[0][(by * 4 + tid / 4) * W1 + bx * 4 + (tid % 4)] = static_cast<uint8_t>(c0[tid]);
+    if (tid < 4) ps.cnt[1][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)] = static_cast<uint8_t>(c1[tid]);
     if (hyb) {
-        if (lane < 4) ps.cnt[2][(by * 2 + lane / 2) * W2 + bx * 2 + (lane % 2)] = static_cast<uint8_t>(c2[lane]);
-        if (lane == 0) ps.cnt[3][by * W3 + bx] = static_cast<uint8_t>(c3[0]);
-    } else if (lane == 0) {
+        if (tid < 4) ps.cnt[2][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)] = static_cast<uint8_t>(c2[tid]);
+        if (tid == 0) ps.cnt[3][by * W3 + bx] = static_cast<uint8_t>(c3[0]);
+    } else if (tid == 0) {
         ps.cnt[2][by * W3 + bx] = static_cast<uint8_t>(c2[0]);
     }
 }
@@ -998,100 +1073,163 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Gather, phase 2 -- k_ln: one warp per output-producing event:
-//   out[o] = ((0 + C[8][o]) + C[7][o]) + ... + C[0][o]   (in-bounds only,
-//             the reference's patch order), + residual (add_inplace), then
-//   LayerNorm: mean / variance as sequential fp64 sums by lane 0
-//   (layernorm.h:41-62), normalise with gamma / beta.
-// Writes the layer output row, the copy residual of the stage's second
-// layer, per-event stage outputs and the drain_n slot contents.
+// Gather, phase 2 -- k_ln: EV output-producing events per CTA.
+//   1) (event, channel) pairs: out[o] = ((0 + C[8][o]) + C[7][o]) + ... +
+//      C[0][o] (in-bounds patch positions only, the reference's patch
+//      order), + residual (add_inplace);
+//   2) lane = event: LayerNorm mean / variance as sequential fp64 sums over
+//      the channels (layernorm.h:41-62), EV events at once;
+//   3) (event, channel) pairs: normalise with gamma / beta and write the
+//      layer output row, the copy residual of the stage's second layer,
+//      per-event stage outputs and the drain_n slot contents;
+//   4) second layers with a next stage: that stage's first-layer residual
+//      input_proj * x (matvec_ct<OUT, 2*OUT>), weights staged in smem.
+// Every thread owns PPT pairs, fully unrolled so their loads overlap.
 // ---------------------------------------------------------------------------
+template <int OUT>
+struct LnShape {
+    static constexpr int EV = OUT <= 24 ? 32 : (OUT == 48 ? 16 : 8);   // events per CTA
+    static constexpr int NT = OUT == 12 ? 128 : 256;                   // threads
+    static constexpr int PPT = EV * OUT / NT;                          // pairs per thread
+    static constexpr int PPT4 = EV * 2 * OUT / NT;                     // residual pairs
+    static_assert(EV * OUT % NT == 0 && EV <= 32, "shape");
+};
+
 template <int A, int OUT>
-__global__ void __launch_bounds__(kNT) k_ln(LnArgs a) {
-    constexpr int CPL = (OUT + 31) / 32;
-    __shared__ float ybuf[kNT / 32][OUT];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 128)) k_ln(LnArgs a) {
+    using Sh = LnShape<OUT>;
+    constexpr int EV = Sh::EV, NT = Sh::NT, PPT = Sh::PPT;
+    constexpr int ST = OUT + 1;                  // conflict-free lane-per-event rows
+    constexpr int IPN = (A == 9 && OUT <= 48) ? OUT * 2 * OUT : 1;
+    __shared__ float ybuf[EV * ST];
+    __shared__ float ipw[IPN];
+    __shared__ double mean_s[EV], inv_s[EV];
+    __shared__ int ev_r[EV], ev_sr[EV], ev_e[EV], ev_cx[EV], ev_cy[EV];
+    __shared__ unsigned char ev_ok[EV], ev_cp[EV];
+    const int tid = threadIdx.x;
     const int s = a.stage;
     const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    float* y = ybuf[warp];
-    for (int r = blockIdx.x * (kNT / 32) + warp; r < n_list; r += gridDim.x * (kNT / 32)) {
-        uint32_t xy0;
-        int sr, e;
-        bool ok;
-        if (a.list == 0) {
-            xy0 = a.ev_xy[r]; sr = r; e = r; ok = (a.rflags[r] & F_VALID) != 0;
-        } else {
-            const StageEntry se = a.E[r];
-            xy0 = se.xy0; sr = a.second ? se.kprev : r; e = se.e; ok = true;
-        }
-        if (!ok) continue;
-        const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
-        float v[CPL];
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) v[c] = 0.0f;
-        for (int d = A - 1; d >= 0; --d) {
-            if (A == 9) {
-                const int dy = 1 - d / 3, dx = 1 - d % 3;
-                if (cx + dx < 0 || cx + dx >= Wl || cy + dy < 0 || cy + dy >= Hl) continue;
+    const bool ipn = (IPN > 1) && a.ipT_next != nullptr;
+    if (ipn)
+        for (int t = tid; t < IPN; t += NT) ipw[t] = __ldg(a.ipT_next + t);
+    for (int r0 = blockIdx.x * EV; r0 < n_list; r0 += gridDim.x * EV) {
+        __syncthreads();
+        if (tid < EV) {
+            const int r = r0 + tid;
+            int ok = 0, sr = 0, e = 0;
+            uint32_t xy0 = 0;
+            if (r < n_list) {
+                if (a.list == 0) {
+                    xy0 = a.ev_xy[r]; sr = r; e = r; ok = (a.rflags[r] & F_VALID) != 0;
+                } else {
+                    const StageEntry se = a.E[r];
+                    xy0 = se.xy0; sr = a.second ? se.kprev : r; e = se.e; ok = 1;
+                }
             }
-            const float* c_row = a.C + (static_cast<size_t>(r) * A + d) * OUT;
+            ev_r[tid] = r; ev_sr[tid] = sr; ev_e[tid] = e; ev_ok[tid] = static_cast<unsigned char>(ok);
+            ev_cx[tid] = static_cast<int>(xy0 & 0xFFFFu) >> s;
+            ev_cy[tid] = static_cast<int>(xy0 >> 16) >> s;
+            ev_cp[tid] = (ok && a.copyres_bit && (a.rflags[e] & a.copyres_bit)) ? 1 : 0;
+        }
+        __syncthreads();
+        // 1) ordered patch sum + residual
+        {
+            float c[PPT][A], rv[PPT];
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) {
-                const int o = lane + 32 * c;
-                if (o < OUT) v[c] = v[c] + c_row[o];
+            for (int j = 0; j < PPT; ++j) {
+                const int t = tid + j * NT;
+                const int ei = t / OUT, o = t % OUT;
+                const bool ok = ev_ok[ei];
+                const int r = ev_r[ei], cx = ev_cx[ei], cy = ev_cy[ei];
+#pragma unroll
+                for (int d = 0; d < A; ++d) {
+                    bool in = ok;
+                    if (A == 9) {
+                        const int dy = 1 - d / 3, dx = 1 - d % 3;
+                        in = in && cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl;
+                    }
+                    c[j][d] = in ? __ldg(a.C + (static_cast<size_t>(r) * A + d) * OUT + o) : 0.0f;
+                }
+                rv[j] = ok ? __ldg(a.R_in + static_cast<size_t>(ev_sr[ei]) * OUT + o) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < PPT; ++j) {
+                const int t = tid + j * NT;
+                const int ei = t / OUT, o = t % OUT;
+                const int cx = ev_cx[ei], cy = ev_cy[ei];
+                float v = 0.0f;
+#pragma unroll
+                for (int d = A - 1; d >= 0; --d) {
+                    if (A == 9) {
+                        const int dy = 1 - d / 3, dx = 1 - d % 3;
+                        if (cx + dx < 0 || cx + dx >= Wl || cy + dy < 0 || cy + dy >= Hl) continue;
+                    }
+                    v = v + c[j][d];
+                }
+                ybuf[ei * ST + o] = v + rv[j];
             }
         }
-        const float* res = a.R_in + static_cast<size_t>(sr) * OUT;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-            const int o = lane + 32 * c;
-            if (o < OUT) y[o] = v[c] + res[o];
-        }
-        __syncwarp();
-        double mean = 0.0, inv = 0.0;
-        if (lane == 0) {
+        __syncthreads();
+        // 2) sequential fp64 statistics, one lane per event
+        if (tid < EV && ev_ok[tid]) {
+            const float* y = ybuf + tid * ST;
             double sum = 0.0;
             for (int o = 0; o < OUT; ++o) sum += static_cast<double>(y[o]);
-            mean = sum / static_cast<double>(OUT);
+            const double mean = sum / static_cast<double>(OUT);
             double var = 0.0;
             for (int o = 0; o < OUT; ++o) {
                 const double dd = static_cast<double>(y[o]) - mean;
                 var += dd * dd;
             }
             var /= static_cast<double>(OUT);
-            inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+            mean_s[tid] = mean;
+            inv_s[tid] = 1.0 / sqrt(var + static_cast<double>(1e-5f));
         }
-        mean = __shfl_sync(0xffffffffu, mean, 0);
-        inv = __shfl_sync(0xffffffffu, inv, 0);
-        const bool cp = a.copyres_bit && (a.rflags[e] & a.copyres_bit);
+        __syncthreads();
+        // 3) normalise and write
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-            const int o = lane + 32 * c;
-            if (o >= OUT) continue;
-            const double t = (static_cast<double>(y[o]) - mean) * inv;
-            const float xv = static_cast<float>(t * static_cast<double>(__ldg(a.L.gamma + o)) +
+        for (int j = 0; j < PPT; ++j) {
+            const int t = tid + j * NT;
+            const int ei = t / OUT, o = t % OUT;
+            if (!ev_ok[ei]) continue;
+            const int r = ev_r[ei], e = ev_e[ei];
+            const double tt = (static_cast<double>(ybuf[ei * ST + o]) - mean_s[ei]) * inv_s[ei];
+            const float xv = static_cast<float>(tt * static_cast<double>(__ldg(a.L.gamma + o)) +
                                                 static_cast<double>(__ldg(a.L.beta + o)));
             if (a.X_out) a.X_out[static_cast<size_t>(r) * OUT + o] = xv;
-            if (cp) a.R_next[static_cast<size_t>(r) * OUT + o] = xv;
+            if (ev_cp[ei]) a.R_next[static_cast<size_t>(r) * OUT + o] = xv;
             if (a.stage_out && a.second) a.stage_out[static_cast<size_t>(e) * OUT + o] = xv;
             if (a.slot_feat) {
                 a.slot_feat[static_cast<size_t>(e) * 96 + o] = xv;
                 if (OUT == 48) a.slot_feat[static_cast<size_t>(e) * 96 + 48 + o] = 0.0f;
             }
-            y[o] = xv;
+            ybuf[ei * ST + o] = xv;
         }
-        __syncwarp();
-        if (a.ipT_next) {
-            // residual of the next stage's first layer: input_proj * x
-            // (matvec_ct<OUT, 2*OUT>), row r of the same list
-            for (int o2 = lane; o2 < 2 * OUT; o2 += 32) {
-                float acc = 0.0f;
-                for (int i = 0; i < OUT; ++i) acc = fmaf(__ldg(a.ipT_next + i * 2 * OUT + o2), y[i], acc);
-                a.R_ipnext[static_cast<size_t>(r) * 2 * OUT + o2] = acc;
+        if (ipn) {
+            __syncthreads();
+            // 4) next stage's first-layer residual, row r of the same list
+            constexpr int P4 = (IPN > 1) ? Sh::PPT4 : 1;
+            float acc[P4];
+            int ei4[P4], o24[P4];
+#pragma unroll
+            for (int j = 0; j < P4; ++j) {
+                const int t = tid + j * NT;
+                ei4[j] = t / (2 * OUT);
+                o24[j] = t % (2 * OUT);
+                acc[j] = 0.0f;
             }
+#pragma unroll 2
+            for (int i = 0; i < OUT; ++i) {
+#pragma unroll
+                for (int j = 0; j < P4; ++j)
+                    acc[j] = fmaf(ipw[i * 2 * OUT + o24[j]], ybuf[ei4[j] * ST + i], acc[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < P4; ++j)
+                if (ev_ok[ei4[j]])
+                    a.R_ipnext[static_cast<size_t>(ev_r[ei4[j]]) * 2 * OUT + o24[j]] = acc[j];
         }
-        __syncwarp();
     }
 }
 
@@ -1218,10 +1356,10 @@ __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
     const int n_rows = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g_cap);
     const int n_rt = (n_rows + BM - 1) / BM;
     const int n_ct = (a.n_cols + BN - 1) / BN;
-    const int A2 = a.A2;
-    const int per_part = A2 * OUT2;
+    constexpr int A2 = 9;                       // layers 4-7: 3x3 patches
+    constexpr int per_part = A2 * OUT2;
     const int part0 = (a.colmode == COLS_VG) ? 1 : 0;
-    const size_t srow_stride = static_cast<size_t>(A2) * J2;
+    constexpr size_t srow_stride = static_cast<size_t>(A2) * J2;
     for (int unit = blockIdx.x; unit < n_rt * n_ct; unit += gridDim.x) {
         const int rt = unit / n_ct, ct = unit % n_ct;
         const int r0 = rt * BM, c0 = ct * BN;
@@ -1506,7 +1644,7 @@ void launch_filter(cudaStream_t st, const FilterArgs& a, dim3 grid) {
 }
 
 void launch_gates(cudaStream_t st, const GateArgs& a) {
-    k_gates<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), 32, 0, st>>>(a);
+    k_gates<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), 32 * kGateWarps, 0, st>>>(a);
 }
 
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a) {
@@ -1576,13 +1714,17 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
 }
 
 void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows) {
-    const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + 7) / 8, 148LL * 16)));
+    auto go = [&](auto kern, auto shape) {
+        using Sh = decltype(shape);
+        const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + Sh::EV - 1) / Sh::EV, 148LL * 32)));
+        kern<<<grid, Sh::NT, 0, st>>>(a);
+    };
     switch (layer) {
-        case 0: k_ln<1, 12><<<grid, kNT, 0, st>>>(a); break;
-        case 1: k_ln<9, 12><<<grid, kNT, 0, st>>>(a); break;
-        case 2: case 3: k_ln<9, 24><<<grid, kNT, 0, st>>>(a); break;
-        case 4: case 5: k_ln<9, 48><<<grid, kNT, 0, st>>>(a); break;
-        default: k_ln<9, 96><<<grid, kNT, 0, st>>>(a); break;
+        case 0: go(k_ln<1, 12>, LnShape<12>{}); break;
+        case 1: go(k_ln<9, 12>, LnShape<12>{}); break;
+        case 2: case 3: go(k_ln<9, 24>, LnShape<24>{}); break;
+        case 4: case 5: go(k_ln<9, 48>, LnShape<48>{}); break;
+        default: go(k_ln<9, 96>, LnShape<96>{}); break;
     }
 }
 
