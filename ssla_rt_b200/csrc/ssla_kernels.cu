@@ -152,54 +152,62 @@ __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
 // ---------------------------------------------------------------------------
 // k_gates: one 4-warp CTA per (partition, s3 block).
 //   Phase 1 (warp 0): walks the block's own events in stream order (the
-//     stage-0 tile list of the block, next window prefetched) and computes
+//     stage-0 tile list of the block, two windows in flight) and computes
 //       the previous timestamp of the event's pixel (preprocess,
 //         src/ssla_kernels.cpp:288-309; the pixel's last_t advances),
 //       gate 0 / 1 / 2 / 3 on the layout's grids (all cells of an event's
 //         gates lie inside its s3 block, so the block owns every counter
 //         it touches; same-key order inside a window by __match_any_sync),
-//     writing the event's flags and buffering (entry, pixel, previous t,
-//     t, p, pass0) of up to kGateBuf events.
-//   Phase 2 (all warps): warp w owns the pixels with x % 4 == w and runs
-//     layer 0 (K = 1, the event's own pixel) on its buffered events in full
-//     32-lane batches: dt_norm, qvg, the pixel's lru_step in stream order
-//     (same-pixel lanes take turns by rank), goW contribution, residual and
-//     LayerNorm (layer_forward_ct, src/ssla_kernels.cpp:315-385), writing
-//     the output row and, for events entering stage 1, the layer-1 residual.
+//     writing the event's flags and buffering (entry, pixel, rank among
+//     the buffer's events at that pixel, previous t, t, p, pass0) of up to
+//     kGateBuf events.
+//   Phase 2 (all threads), layer 0 (K = 1: the event's own pixel,
+//     layer_forward_ct, src/ssla_kernels.cpp:315-385):
+//     a) per event: dt_norm, v and sigmoid(g) (matvec_ct<2,36> rows);
+//     b) per (pixel, channel): the pixel's lru_step over its buffered
+//        events in stream order, h after each event;
+//     c) per event: q * h, goW contribution, residual, LayerNorm; writes
+//        the output row and, for events entering stage 1, the layer-1
+//        residual.
 // ---------------------------------------------------------------------------
 constexpr int kGateBuf = 256;
-constexpr int kGateWarps = 4;
+constexpr int kGateNT = 128;
 
-__global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
+__global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
     const int p = blockIdx.x, blk = blockIdx.y;
     const int W3 = a.g.W[3];
     const int bx = blk % W3, by = blk / W3;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const PartState ps = a.parts[p];
     const bool hyb = a.g.layout == LAYOUT_HYBRID;
-    const int window = a.g.window;
     __shared__ double lt[64];
     __shared__ int c0[16], c1[4], c2[4], c3[1];
+    __shared__ unsigned char passtab[256];
     // layer-0 weights: qvgT [2][36] | ipT [2][12] | goWT [12][12] | gamma | beta
     __shared__ float w0[264];
     __shared__ float h0[64 * 12];
     __shared__ double b_prev[kGateBuf];
-    __shared__ float b_t[kGateBuf], b_p[kGateBuf];
+    __shared__ float b_t[kGateBuf], b_p[kGateBuf], b_dt[kGateBuf];
     __shared__ int b_k[kGateBuf];
-    __shared__ unsigned char b_pix[kGateBuf], b_pass0[kGateBuf];
-    __shared__ unsigned short wl[kGateWarps][kGateBuf];
+    __shared__ unsigned char b_pix[kGateBuf], b_rank[kGateBuf], b_pass0[kGateBuf];
+    __shared__ float b_v[kGateBuf * 12], b_h[kGateBuf * 12];   // v; sigmoid(g) then h after
+    __shared__ int pc[64], po[64];
+    __shared__ unsigned char pl[kGateBuf];
     __shared__ int b_n, b_done;
     const int W0 = a.g.W[0], W1 = a.g.W[1], W2 = a.g.W[2];
-    for (int i = tid; i < 72; i += blockDim.x) w0[i] = a.L0.qvgT[i];
-    for (int i = tid; i < 24; i += blockDim.x) w0[72 + i] = a.L0.ipT[i];
-    for (int i = tid; i < 144; i += blockDim.x) w0[96 + i] = a.L0.goWT[i];
+    for (int i = tid; i < 72; i += kGateNT) w0[i] = a.L0.qvgT[i];
+    for (int i = tid; i < 24; i += kGateNT) w0[72 + i] = a.L0.ipT[i];
+    for (int i = tid; i < 144; i += kGateNT) w0[96 + i] = a.L0.goWT[i];
     if (tid < 12) { w0[240 + tid] = a.L0.gamma[tid]; w0[252 + tid] = a.L0.beta[tid]; }
-    for (int i = tid; i < 64 * 12; i += blockDim.x) {
+    for (int i = tid; i < 256; i += kGateNT) passtab[i] = gate_pass(i, a.g.window) ? 1 : 0;
+    for (int i = tid; i < 64 * 12; i += kGateNT) {
         const int px = i / 12, c = i % 12;
         h0[i] = ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c];
     }
-    for (int i = tid; i < 64; i += blockDim.x)
+    for (int i = tid; i < 64; i += kGateNT) {
         lt[i] = ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)];
+        pc[i] = 0;
+    }
     if (tid < 16) c0[tid] = ps.cnt[0][(by * 4 + tid / 4) * W1 + bx * 4 + (tid % 4)];
     if (tid < 4) c1[tid] = ps.cnt[1][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
     if (hyb) {
@@ -210,18 +218,30 @@ __global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
     }
     __syncthreads();
 
+    // Ordered gate over the active lanes of warp 0 (table lookup of the
+    // tdrop rule; the counter advances by the number of active peers).
+    auto gate = [&](bool active, int key, int* cnt) {
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        bool pass = false;
+        if (active) pass = passtab[(cnt[key] + __popc(peers & lanemask_lt())) & 255] != 0;
+        __syncwarp();
+        if (active && lane == hi_lane(peers)) cnt[key] += __popc(peers);
+        __syncwarp();
+        return pass;
+    };
+
     const int ntiles = a.g.tx[0] * a.g.ty[0];
     const int tile = by * a.g.tx[0] + bx;     // s0 tiles are the s3 blocks
     const int n_p = a.ev_off[p + 1] - a.ev_off[p];
     const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[0]);
-    // phase-1 cursor and prefetched window (warp 0 only)
+    // Phase-1 window pipeline (warp 0): the entries of window w+2 and the
+    // events of window w+1 are loaded while window w is processed.
     int seg = 0, j0 = 0, cnt = -1;
     const int2* lst = nullptr;
-    int2 ent_n = make_int2(0, 0);
-    float4 ev_n = make_float4(0.f, 0.f, 0.f, 0.f);
-    bool own_n = false, have_n = false;
-    auto prefetch = [&]() {
-        have_n = false;
+    auto next_entries = [&](int2& ent, bool& valid, bool& have) {
+        have = false;
+        valid = false;
+        ent = make_int2(0, 0);
         while (seg < nseg) {
             if (cnt < 0) {
                 const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0] + seg;
@@ -231,30 +251,43 @@ __global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
             }
             if (j0 < cnt) {
                 const int j = j0 + lane;
-                ent_n = make_int2(0, 0);
-                if (j < cnt) ent_n = lst[j];
-                const int x0 = ent_n.y & 0xFFFF, y0 = (ent_n.y >> 16) & 0x7FFF;
-                own_n = (j < cnt) && (x0 >> 3) == bx && (y0 >> 3) == by;
-                ev_n = own_n ? a.ev[ent_n.x] : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j < cnt) { ent = lst[j]; valid = true; }
                 j0 += 32;
-                have_n = true;
+                have = true;
                 return;
             }
             ++seg;
             cnt = -1;
         }
     };
-    if (warp == 0) prefetch();
+    auto is_own = [&](int2 ent, bool valid) {
+        const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
+        return valid && (x0 >> 3) == bx && (y0 >> 3) == by;
+    };
+    int2 ent1 = make_int2(0, 0), ent2 = make_int2(0, 0);
+    bool val1 = false, val2 = false, have1 = false, have2 = false, own1 = false;
+    float4 ev1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (warp == 0) {
+        next_entries(ent1, val1, have1);
+        own1 = is_own(ent1, val1);
+        if (own1) ev1 = a.ev[ent1.x];
+        next_entries(ent2, val2, have2);
+    }
 
     for (;;) {
         // ---- phase 1: gates and previous timestamps, buffer the own events
         if (warp == 0) {
             int n = 0;
-            while (have_n && n <= kGateBuf - 32) {
-                const int2 ent = ent_n;
-                const float4 e = ev_n;
-                const bool own = own_n;
-                prefetch();                          // next window in flight
+            while (have1 && n <= kGateBuf - 32) {
+                const int2 ent = ent1;
+                const float4 e = ev1;
+                const bool own = own1;
+                // advance the pipeline: window w+1 <- w+2 (event load issued), w+2 <- next
+                ent1 = ent2; val1 = val2; have1 = have2;
+                own1 = have1 && is_own(ent1, val1);
+                ev1 = own1 ? a.ev[ent1.x] : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (have1) next_entries(ent2, val2, have2);
+                else have2 = false;
                 const unsigned om = __ballot_sync(0xffffffffu, own);
                 if (om == 0u) continue;
                 const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
@@ -265,20 +298,31 @@ __global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
                 const int src = prevm ? hi_lane(prevm) : lane;
                 const float t_prev_lane = __shfl_sync(0xffffffffu, e.x, src);
                 double prev = 0.0;
-                if (own) prev = prevm ? static_cast<double>(t_prev_lane) : lt[pix];
+                int rank = 0;
+                if (own) {
+                    prev = prevm ? static_cast<double>(t_prev_lane) : lt[pix];
+                    rank = pc[pix] + __popc(prevm);
+                }
                 __syncwarp();
-                if (own && lane == hi_lane(peers)) lt[pix] = static_cast<double>(e.x);
+                if (own && lane == hi_lane(peers)) {
+                    lt[pix] = static_cast<double>(e.x);
+                    pc[pix] += __popc(peers);
+                }
                 __syncwarp();
                 const int k0 = own ? (((y0 >> 1) & 3) * 4 + ((x0 >> 1) & 3)) : (100 + lane);
-                const bool pass0 = warp_gate(own, k0, c0, window);
+                const bool pass0 = gate(own, k0, c0);
                 const bool in1 = own && pass0;
                 const int sub2 = ((y0 >> 2) & 1) * 2 + ((x0 >> 2) & 1);
-                const bool pass1 = warp_gate(in1, in1 ? sub2 : 100 + lane, c1, window);
-                const bool in2 = in1 && pass1;
-                const bool pass2 = warp_gate(in2, in2 ? (hyb ? sub2 : 0) : 100 + lane, c2, window);
-                const bool in3 = in2 && pass2;
-                bool pass3 = true;
-                if (hyb) pass3 = warp_gate(in3, in3 ? 0 : 100 + lane, c3, window);
+                bool in2 = false, in3 = false, pass3 = true;
+                if (__ballot_sync(0xffffffffu, in1)) {
+                    const bool pass1 = gate(in1, in1 ? sub2 : 100 + lane, c1);
+                    in2 = in1 && pass1;
+                    if (__ballot_sync(0xffffffffu, in2)) {
+                        const bool pass2 = gate(in2, in2 ? (hyb ? sub2 : 0) : 100 + lane, c2);
+                        in3 = in2 && pass2;
+                        if (hyb && __ballot_sync(0xffffffffu, in3)) pass3 = gate(in3, in3 ? 0 : 100 + lane, c3);
+                    }
+                }
                 if (own) {
                     uint8_t f = F_VALID;
                     if (pass0) f |= F_R1;
@@ -289,6 +333,7 @@ __global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
                     const int pos = n + __popc(om & lanemask_lt());
                     b_k[pos] = k;
                     b_pix[pos] = static_cast<unsigned char>(pix);
+                    b_rank[pos] = static_cast<unsigned char>(rank);
                     b_prev[pos] = prev;
                     b_t[pos] = e.x;
                     b_p[pos] = e.w;
@@ -296,104 +341,101 @@ __global__ void __launch_bounds__(32 * kGateWarps, 5) k_gates(GateArgs a) {
                 }
                 n += __popc(om);
             }
-            if (lane == 0) { b_n = n; b_done = have_n ? 0 : 1; }
+            if (lane == 0) { b_n = n; b_done = have1 ? 0 : 1; }
+            // per-pixel list offsets of this buffer
+            int c_lo = pc[2 * lane], c_hi = pc[2 * lane + 1];
+            int incl = c_lo + c_hi;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            po[2 * lane] = incl - c_lo - c_hi;
+            po[2 * lane + 1] = incl - c_hi;
         }
         __syncthreads();
         const int n = b_n;
         const int done = b_done;
-        // ---- phase 2: layer 0 of the buffered events, pixel-partitioned
-        int my_n = 0;
-        for (int base = 0; base < n; base += 32) {
-            const int i = base + lane;
-            const bool mine = i < n && (b_pix[i] & 3) == warp;
-            const unsigned m = __ballot_sync(0xffffffffu, mine);
-            if (mine) wl[warp][my_n + __popc(m & lanemask_lt())] = static_cast<unsigned short>(i);
-            my_n += __popc(m);
+        // ---- phase 2a: per event dt_norm, v, sigmoid(g); pixel lists
+        for (int i = tid; i < n; i += kGateNT) {
+            const double prev = b_prev[i];
+            float dt;
+            if (prev < 0.0) {
+                dt = 1.0f;
+            } else {
+                double v = (static_cast<double>(b_t[i]) - prev) / 1e5;
+                if (v < 0.0) v = 0.0;
+                if (v > 1.0) v = 1.0;
+                dt = static_cast<float>(v);
+            }
+            const float ep = b_p[i];
+            b_dt[i] = dt;
+#pragma unroll 2
+            for (int c = 0; c < 12; ++c) {
+                b_v[i * 12 + c] = fmaf(w0[36 + 12 + c], ep, fmaf(w0[12 + c], dt, 0.0f));
+                b_h[i * 12 + c] = ssla_sigmoidf(fmaf(w0[36 + 24 + c], ep, fmaf(w0[24 + c], dt, 0.0f)));
+            }
+            pl[po[b_pix[i]] + b_rank[i]] = static_cast<unsigned char>(i);
         }
-        __syncwarp();
-        for (int b0 = 0; b0 < my_n; b0 += 32) {
-            const bool own = b0 + lane < my_n;
-            const int idx = own ? wl[warp][b0 + lane] : 0;
-            const int k = b_k[idx];
-            const int pix = own ? b_pix[idx] : (64 + lane);
-            const float ep = b_p[idx];
-            float dt = 0.0f;
-            if (own) {
-                const double prev = b_prev[idx];
-                if (prev < 0.0) {
-                    dt = 1.0f;
-                } else {
-                    double v = (static_cast<double>(b_t[idx]) - prev) / 1e5;
-                    if (v < 0.0) v = 0.0;
-                    if (v > 1.0) v = 1.0;
-                    dt = static_cast<float>(v);
-                }
+        __syncthreads();
+        // ---- phase 2b: the pixel chains, thread = (pixel, channel)
+        for (int pr = tid; pr < 64 * 12; pr += kGateNT) {
+            const int px = pr / 12, c = pr % 12;
+            const int lo = po[px], m = pc[px];
+            float h = h0[pr];
+            for (int j = 0; j < m; ++j) {
+                const int i = pl[lo + j];
+                h = fmaf(b_h[i * 12 + c], h, b_v[i * 12 + c]);
+                b_h[i * 12 + c] = h;
             }
-            // v and sigmoid(g); the pixel's state after this event -> hh
-            float v[12], ag[12], hh[12];
-            if (own) {
+            h0[pr] = h;
+        }
+        __syncthreads();
+        // ---- phase 2c: per event q * h, goW, residual, LayerNorm
+        for (int i = tid; i < n; i += kGateNT) {
+            const float dt = b_dt[i], ep = b_p[i];
+            float qh[12];
 #pragma unroll
-                for (int c = 0; c < 12; ++c) {
-                    v[c] = fmaf(w0[36 + 12 + c], ep, fmaf(w0[12 + c], dt, 0.0f));
-                    ag[c] = ssla_sigmoidf(fmaf(w0[36 + 24 + c], ep, fmaf(w0[24 + c], dt, 0.0f)));
-                }
+            for (int c = 0; c < 12; ++c) qh[c] = fmaf(w0[36 + c], ep, fmaf(w0[c], dt, 0.0f)) * b_h[i * 12 + c];
+            float y[12];
+            double sum = 0.0;
+#pragma unroll 3
+            for (int o = 0; o < 12; ++o) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int ii = 0; ii < 12; ++ii) acc = fmaf(w0[96 + ii * 12 + o], qh[ii], acc);
+                y[o] = (0.0f + acc) + fmaf(w0[72 + 12 + o], ep, fmaf(w0[72 + o], dt, 0.0f));
+                sum += static_cast<double>(y[o]);
             }
-            const unsigned peers = __match_any_sync(0xffffffffu, pix);
-            const int rank = __popc(peers & lanemask_lt());
-            const int rounds = __reduce_max_sync(0xffffffffu, own ? rank + 1 : 0);
-            for (int rd = 0; rd < rounds; ++rd) {
-                if (own && rank == rd) {
-                    float* h = h0 + pix * 12;
+            const double mean = sum / 12.0;
+            double var = 0.0;
 #pragma unroll
-                    for (int c = 0; c < 12; ++c) {
-                        const float hc = fmaf(ag[c], h[c], v[c]);
-                        h[c] = hc;
-                        hh[c] = hc;
-                    }
-                }
-                __syncwarp();
+            for (int o = 0; o < 12; ++o) {
+                const double dd = static_cast<double>(y[o]) - mean;
+                var += dd * dd;
             }
-            if (own) {
-                // qh = q * h (q = qvg rows 0..11), goW contribution + residual
+            var /= 12.0;
+            const double inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+            const int k = b_k[i];
+            float* xo = a.X1 + static_cast<size_t>(k) * 12;
+            float* rc = (b_pass0[i] && a.Rcopy) ? a.Rcopy + static_cast<size_t>(k) * 12 : nullptr;
 #pragma unroll
-                for (int c = 0; c < 12; ++c) hh[c] = fmaf(w0[36 + c], ep, fmaf(w0[c], dt, 0.0f)) * hh[c];
-                float y[12];
-                double sum = 0.0;
-#pragma unroll
-                for (int o = 0; o < 12; ++o) {
-                    float acc = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 12; ++i) acc = fmaf(w0[96 + i * 12 + o], hh[i], acc);
-                    y[o] = (0.0f + acc) + fmaf(w0[72 + 12 + o], ep, fmaf(w0[72 + o], dt, 0.0f));
-                    sum += static_cast<double>(y[o]);
-                }
-                const double mean = sum / 12.0;
-                double var = 0.0;
-#pragma unroll
-                for (int o = 0; o < 12; ++o) {
-                    const double dd = static_cast<double>(y[o]) - mean;
-                    var += dd * dd;
-                }
-                var /= 12.0;
-                const double inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
-                float* xo = a.X1 + static_cast<size_t>(k) * 12;
-                float* rc = (b_pass0[idx] && a.Rcopy) ? a.Rcopy + static_cast<size_t>(k) * 12 : nullptr;
-#pragma unroll
-                for (int o = 0; o < 12; ++o) {
-                    const double t = (static_cast<double>(y[o]) - mean) * inv;
-                    const float xv = static_cast<float>(t * static_cast<double>(w0[240 + o]) +
-                                                        static_cast<double>(w0[252 + o]));
-                    xo[o] = xv;
-                    if (rc) rc[o] = xv;
-                }
+            for (int o = 0; o < 12; ++o) {
+                const double t = (static_cast<double>(y[o]) - mean) * inv;
+                const float xv = static_cast<float>(t * static_cast<double>(w0[240 + o]) +
+                                                    static_cast<double>(w0[252 + o]));
+                xo[o] = xv;
+                if (rc) rc[o] = xv;
             }
         }
         __syncthreads();
+        for (int i = tid; i < 64; i += kGateNT) pc[i] = 0;
+        __syncthreads();
         if (done) break;
     }
-    for (int i = tid; i < 64; i += blockDim.x)
+    for (int i = tid; i < 64; i += kGateNT)
         ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)] = lt[i];
-    for (int i = tid; i < 64 * 12; i += blockDim.x) {
+    for (int i = tid; i < 64 * 12; i += kGateNT) {
         const int px = i / 12, c = i % 12;
         ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c] = h0[i];
     }
@@ -1644,7 +1686,7 @@ void launch_filter(cudaStream_t st, const FilterArgs& a, dim3 grid) {
 }
 
 void launch_gates(cudaStream_t st, const GateArgs& a) {
-    k_gates<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), 32 * kGateWarps, 0, st>>>(a);
+    k_gates<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), kGateNT, 0, st>>>(a);
 }
 
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a) {
