@@ -220,8 +220,19 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
 
     // Ordered gate over the active lanes of warp 0 (table lookup of the
     // tdrop rule; the counter advances by the number of active peers).
-    auto gate = [&](bool active, int key, int* cnt) {
-        const unsigned peers = __match_any_sync(0xffffffffu, key);
+    // Peers = active lanes with the same BITS-bit key, from one ballot per
+    // key bit.
+    auto peers_of = [&](bool active, int key, int bits) {
+        unsigned m = __ballot_sync(0xffffffffu, active);
+        for (int b = 0; b < bits; ++b) {
+            const bool bit = (key >> b) & 1;
+            const unsigned bb = __ballot_sync(0xffffffffu, active && bit);
+            m &= bit ? bb : ~bb;
+        }
+        return m;
+    };
+    auto gate = [&](bool active, int key, int bits, int* cnt) {
+        const unsigned peers = peers_of(active, key, bits);
         bool pass = false;
         if (active) pass = passtab[(cnt[key] + __popc(peers & lanemask_lt())) & 255] != 0;
         __syncwarp();
@@ -292,8 +303,8 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                 if (om == 0u) continue;
                 const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
                 const int k = ent.x;
-                const int pix = own ? ((y0 & 7) * 8 + (x0 & 7)) : (64 + lane);
-                const unsigned peers = __match_any_sync(0xffffffffu, pix);
+                const int pix = (y0 & 7) * 8 + (x0 & 7);
+                const unsigned peers = peers_of(own, pix, 6);
                 const unsigned prevm = peers & lanemask_lt();
                 const int src = prevm ? hi_lane(prevm) : lane;
                 const float t_prev_lane = __shfl_sync(0xffffffffu, e.x, src);
@@ -309,18 +320,18 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                     pc[pix] += __popc(peers);
                 }
                 __syncwarp();
-                const int k0 = own ? (((y0 >> 1) & 3) * 4 + ((x0 >> 1) & 3)) : (100 + lane);
-                const bool pass0 = gate(own, k0, c0);
+                const int k0 = ((y0 >> 1) & 3) * 4 + ((x0 >> 1) & 3);
+                const bool pass0 = gate(own, k0, 4, c0);
                 const bool in1 = own && pass0;
                 const int sub2 = ((y0 >> 2) & 1) * 2 + ((x0 >> 2) & 1);
                 bool in2 = false, in3 = false, pass3 = true;
                 if (__ballot_sync(0xffffffffu, in1)) {
-                    const bool pass1 = gate(in1, in1 ? sub2 : 100 + lane, c1);
+                    const bool pass1 = gate(in1, sub2, 2, c1);
                     in2 = in1 && pass1;
                     if (__ballot_sync(0xffffffffu, in2)) {
-                        const bool pass2 = gate(in2, in2 ? (hyb ? sub2 : 0) : 100 + lane, c2);
+                        const bool pass2 = hyb ? gate(in2, sub2, 2, c2) : gate(in2, 0, 0, c2);
                         in3 = in2 && pass2;
-                        if (hyb && __ballot_sync(0xffffffffu, in3)) pass3 = gate(in3, in3 ? 0 : 100 + lane, c3);
+                        if (hyb && __ballot_sync(0xffffffffu, in3)) pass3 = gate(in3, 0, 0, c3);
                     }
                 }
                 if (own) {
