@@ -30,6 +30,7 @@ constexpr int kMB = 32;             // events per k_event batch
 constexpr int kEPT = 8;             // events per thread in k_event tiles
 constexpr int kGroups = kMB / kEPT; // event groups per batch
 constexpr int kTile = 8;            // tile side (cells) of tile lists
+constexpr int kMaxTileCols = 64;    // tiles per row (stage-0 width <= 512)
 constexpr int kMaxParts = 1024;
 constexpr uint32_t kInvalidXY = 0xFFFFFFFFu;
 constexpr int kCompactTile = 4096;  // events per compaction tile

@@ -147,6 +147,7 @@ void make_geo(Geo& g, int H, int W, int P, int layout, int window, int ncls) {
         g.tx[s] = (g.W[s] + kTile - 1) / kTile;
         g.ty[s] = (g.H[s] + kTile - 1) / kTile;
     }
+    if (g.tx[0] > kMaxTileCols) throw std::invalid_argument("sensor wider than 512 pixels");
     g.P = P;
     g.layout = layout;
     g.window = window;
@@ -500,7 +501,7 @@ struct Engine {
         FilterArgs fa{};
         fa.g = g; fa.stage = 0; fa.ev_xy = ws.ev_xy.as<uint32_t>(); fa.rflags = ws.rflags.as<uint8_t>();
         fa.range = ws.ev_off.as<int>(); fa.tl = ws.tl[0].as<int2>(); fa.tl_cnt = ws.tl_cnt[0].as<int>();
-        launch_filter(st, fa, dim3(P, g.tx[0] * g.ty[0], g.nseg[0]));
+        launch_filter(st, fa);
         check_launch("k_filter s0");
         prof.mark("filter_s0", 1, st);
         // gates + preprocess + layer-0 qvg
@@ -527,7 +528,7 @@ struct Engine {
             f.g = g; f.stage = s; f.E = ws.E[s].as<StageEntry>(); f.rflags = ws.rflags.as<uint8_t>();
             f.range = ws.off[s].as<int>(); f.tl = ws.tl[s].as<int2>(); f.tl_cnt = ws.tl_cnt[s].as<int>();
             f.out_bit = static_cast<uint8_t>(F_R1 << s);
-            launch_filter(st, f, dim3(P, g.tx[s] * g.ty[s], g.nseg[s]));
+            launch_filter(st, f);
             check_launch("k_filter");
         }
         prof.mark("filter_s123", 3, st);
@@ -641,7 +642,7 @@ struct DrainN {
         f2.g = g; f2.stage = 2; f2.E = w.E[2].as<StageEntry>(); f2.rflags = w.rflags.as<uint8_t>();
         f2.range = w.off[2].as<int>(); f2.tl = w.tl[2].as<int2>(); f2.tl_cnt = w.tl_cnt[2].as<int>();
         f2.out_bit = 0;   // gates not known yet; refiltered below
-        launch_filter(st, f2, dim3(P, g.tx[2] * g.ty[2], g.nseg[2]));
+        launch_filter(st, f2);
         check_launch("k_filter s2");
         Gate2Args ga{};
         ga.g = g; ga.rec_off = w.ev_off.as<int>(); ga.tl2 = w.tl[2].as<int2>(); ga.tl2_cnt = w.tl_cnt[2].as<int>();
@@ -661,7 +662,7 @@ struct DrainN {
             f.g = g; f.stage = s; f.E = w.E[s].as<StageEntry>(); f.rflags = w.rflags.as<uint8_t>();
             f.range = w.off[s].as<int>(); f.tl = w.tl[s].as<int2>(); f.tl_cnt = w.tl_cnt[s].as<int>();
             f.out_bit = static_cast<uint8_t>(F_R1 << s);
-            launch_filter(st, f, dim3(P, g.tx[s] * g.ty[s], g.nseg[s]));
+            launch_filter(st, f);
             check_launch("k_filter");
         }
         // count[2] = n for the entry kernel

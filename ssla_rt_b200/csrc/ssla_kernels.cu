@@ -92,11 +92,95 @@ __global__ void k_prep_records(const HybridInputRec* __restrict__ rec, int n,
 }
 
 // ---------------------------------------------------------------------------
-// k_filter: for (partition, tile, segment) compact, in stream order, the
-// stage entries whose stage cell lies in the tile grown by one cell (the
-// entries whose 3x3 patch touches the tile).  grid (P, tiles, segments).
+// k_filter (stage 0): for (partition, row of tiles, segment) compact, in
+// stream order,
+// the stage entries whose stage cell lies in each tile of the row grown by
+// one cell (the entries whose 3x3 patch touches the tile).  Each entry is
+// read once; it touches at most two tiles of the row, and its position in
+// each tile's list is its rank among this chunk's hits of that tile (one
+// ballot per tile).  grid (P, tile rows, segments).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
+    const int p = blockIdx.x, trow = blockIdx.y, seg = blockIdx.z;
+    const int s = a.stage;
+    const int tx = a.g.tx[s];
+    const int ntiles = tx * a.g.ty[s];
+    const int lo = a.range[p], hi = a.range[p + 1];
+    const int seg_lo = lo + seg * a.g.seg;
+    if (seg_lo >= hi || seg >= a.g.nseg[s]) return;
+    const int seg_hi = min(hi, seg_lo + a.g.seg);
+    const int ty0 = trow * kTile;
+    __shared__ int wc[kNT / 32][kMaxTileCols];
+    __shared__ int run[kMaxTileCols];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int t = tid; t < tx; t += kNT) run[t] = 0;
+    for (int j0 = seg_lo; j0 < seg_hi; j0 += kNT) {
+        const int j = j0 + tid;
+        int t_lo = 1, t_hi = 0;                  // empty tile range
+        int2 ent = make_int2(0, 0);
+        if (j < seg_hi) {
+            uint32_t xy0;
+            uint32_t flag = 0;
+            if (s == 0) {
+                xy0 = a.ev_xy[j];
+            } else {
+                const StageEntry se = a.E[j];
+                xy0 = se.xy0;
+                flag = (a.rflags[se.e] & a.out_bit) ? 1u : 0u;
+            }
+            if (xy0 != kInvalidXY) {
+                const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s;
+                const int cy = static_cast<int>(xy0 >> 16) >> s;
+                if (cy >= ty0 - 1 && cy <= ty0 + kTile) {
+                    t_lo = max(0, (cx - 1) >> 3);
+                    t_hi = min(tx - 1, (cx + 1) >> 3);
+                }
+                ent = make_int2(j, static_cast<int>(static_cast<uint32_t>(cx) |
+                                                    (static_cast<uint32_t>(cy) << 16) | (flag << 31)));
+            }
+        }
+        int r_lo = 0, r_hi = 0;
+        for (int t = 0; t < tx; ++t) {
+            const unsigned m = __ballot_sync(0xffffffffu, t_lo <= t && t <= t_hi);
+            if (lane == 0) wc[warp][t] = __popc(m);
+            const int r = __popc(m & lanemask_lt());
+            if (t == t_lo) r_lo = r;
+            if (t == t_hi) r_hi = r;
+        }
+        __syncthreads();
+        if (t_lo <= t_hi) {
+#pragma unroll 2
+            for (int q = 0; q < 2; ++q) {
+                const int t = q ? t_hi : t_lo;
+                if (q && t_hi == t_lo) break;
+                int woff = 0;
+                for (int w = 0; w < warp; ++w) woff += wc[w][t];
+                const size_t slot = (static_cast<size_t>(p) * ntiles + trow * tx + t) * a.g.nseg[s] + seg;
+                a.tl[slot * a.g.seg + run[t] + woff + (q ? r_hi : r_lo)] = ent;
+            }
+        }
+        __syncthreads();
+        for (int t = tid; t < tx; t += kNT) {
+            int tot = 0;
+#pragma unroll
+            for (int w = 0; w < kNT / 32; ++w) tot += wc[w][t];
+            run[t] += tot;
+        }
+    }
+    __syncthreads();
+    for (int t = tid; t < tx; t += kNT) {
+        const size_t slot = (static_cast<size_t>(p) * ntiles + trow * tx + t) * a.g.nseg[s] + seg;
+        a.tl_cnt[slot] = run[t];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_filter_tiles: one CTA per (partition, tile, segment) -- the form for the
+// small later stages, where a CTA per tile keeps enough CTAs busy: compacts,
+// in stream order, the stage entries whose stage cell lies in the tile
+// grown by one cell.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kNT) k_filter_tiles(FilterArgs a) {
     const int p = blockIdx.x, tile = blockIdx.y, seg = blockIdx.z;
     const int s = a.stage;
     const int ntiles = a.g.tx[s] * a.g.ty[s];
@@ -157,7 +241,7 @@ __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
 //         src/ssla_kernels.cpp:288-309; the pixel's last_t advances),
 //       gate 0 / 1 / 2 / 3 on the layout's grids (all cells of an event's
 //         gates lie inside its s3 block, so the block owns every counter
-//         it touches; same-key order inside a window by __match_any_sync),
+//         it touches; same-key order inside a window from peer masks),
 //     writing the event's flags and buffering (entry, pixel, rank among
 //     the buffer's events at that pixel, previous t, t, p, pass0) of up to
 //     kGateBuf events.
@@ -1692,8 +1776,12 @@ void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2
                                                       E2, ev_xy, rflags, feat);
 }
 
-void launch_filter(cudaStream_t st, const FilterArgs& a, dim3 grid) {
-    k_filter<<<grid, kNT, 0, st>>>(a);
+void launch_filter(cudaStream_t st, const FilterArgs& a) {
+    const int s = a.stage;
+    if (s == 0)
+        k_filter<<<dim3(a.g.P, a.g.ty[0], a.g.nseg[0]), kNT, 0, st>>>(a);
+    else
+        k_filter_tiles<<<dim3(a.g.P, a.g.tx[s] * a.g.ty[s], a.g.nseg[s]), kNT, 0, st>>>(a);
 }
 
 void launch_gates(cudaStream_t st, const GateArgs& a) {

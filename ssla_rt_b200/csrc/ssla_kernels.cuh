@@ -175,7 +175,7 @@ void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
                  uint32_t* ev_xy, uint8_t* rflags);
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
                          uint32_t* ev_xy, uint8_t* rflags, float* feat);
-void launch_filter(cudaStream_t st, const FilterArgs& a, dim3 grid);
+void launch_filter(cudaStream_t st, const FilterArgs& a);
 void launch_gates(cudaStream_t st, const GateArgs& a);
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a);
 void launch_compact(cudaStream_t st, const CompactArgs& a);
