@@ -120,6 +120,20 @@ int  ssla_engine_drain_host(SslaEngine* eng, const float* events_host,
                             const int* part_offsets, uint8_t* flags_host,
                             void* stream);
 
+/* Stages 0-1 only (HYBRID layout): preprocess, gates 0-1, layers 0-3 for
+ * every event (state of stages 0-1 advances), and one HybridInputRec per
+ * event that passed gate 1 -- t, stage-2 x / y, feat1 = the stage-1 output;
+ * seq_done, t_push_ns and t_emit_ns zero -- written to records_dev
+ * (device memory, room for records_cap >= the drain's event count),
+ * partition-major in stream order.  record_offsets (host, n_partitions+1
+ * ints) receives each partition's record range.  Synchronises `stream`.
+ * Replaces the shard workers' stage-0/1 path that feeds the GPU rings
+ * (src/lib_stage01_to_gpu.cpp:157-311). */
+int  ssla_engine_drain_records(SslaEngine* eng, const float* events_dev,
+                               const int* part_offsets, void* records_dev,
+                               int records_cap, int* record_offsets,
+                               uint8_t* flags_dev, void* stream);
+
 int  ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes);
 int  ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index,
                             void* host_dst, size_t bytes);

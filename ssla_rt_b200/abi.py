@@ -91,5 +91,12 @@ EXPORTED = (
     "ssla_engine_info", "ssla_s2s3_drain_n_multi", "ssla_s2s3_drain_n",
     "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak",
     "ssla_expf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
+    "ssla_engine_drain_records",
+)
+# Every symbol include/stage01_to_gpu.h declares (the libstage01_to_gpu ABI).
+S01G_EXPORTED = (
+    "s01g_init", "s01g_init_full", "s01g_attach_gpu_rings", "s01g_attach_gpu_rings_multi",
+    "s01g_submit_batch", "s01g_snapshot_stats", "s01g_reset_stats", "s01g_start_synthetic",
+    "s01g_stop_synthetic", "s01g_synthetic_n_pushed", "s01g_shutdown", "s01g_flush",
 )
 NOALLOC_MAX_RECORDS = 65536

@@ -9,6 +9,7 @@ multiply-add), which is what makes results bit-identical to the CPU oracle.
 from __future__ import annotations
 
 import os
+import shutil
 import subprocess
 import sys
 
@@ -16,7 +17,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libssla_b200.so")
-SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp", "ssla_noalloc.cu"]
+# The same library under the reference's name, for callers that load the
+# s01g_* ABI as libstage01_to_gpu.so (orin/orin/hybrid_common.py S01gAPI).
+S01G_LIB = os.path.join(HERE, "libstage01_to_gpu.so")
+SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp", "ssla_noalloc.cu", "ssla_s01g.cpp"]
 HEADERS = ["ssla_device.cuh", "ssla_kernels.cuh", "ssla_weights.h"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
               "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-shared",
@@ -35,8 +39,8 @@ def _stale() -> bool:
         return True
     t = os.path.getmtime(LIB)
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
-    deps += [os.path.join(REPO, "include", f) for f in ("ssla_b200.h", "ssla_abi_types.h")]
-    return any(os.path.getmtime(d) > t for d in deps)
+    deps += [os.path.join(REPO, "include", f) for f in ("ssla_b200.h", "ssla_abi_types.h", "stage01_to_gpu.h")]
+    return any(os.path.getmtime(d) > t for d in deps) or not os.path.exists(S01G_LIB)
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -47,6 +51,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
+    shutil.copyfile(LIB, S01G_LIB)
+    os.chmod(S01G_LIB, 0o755)
     return LIB
 
 

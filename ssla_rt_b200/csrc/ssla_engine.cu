@@ -242,7 +242,8 @@ struct Workspace {
 //   next layer (copy for a stage's second layer, input_proj for the next
 //   stage's first); after layer 7 k_head.
 void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_parts,
-                const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof) {
+                const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof,
+                int l_end = 8) {
     static const char* kScan[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
                                    "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
     static const char* kContrib[8] = {"contrib_L0", "contrib_L1", "contrib_L2", "contrib_L3",
@@ -255,7 +256,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
     float* R_second = w.R_B.as<float>();       // residual rows of second layers
     const int l0 = (w.s_first == 0) ? 1 : 4;
     if (l0 < 4) SSLA_CK(cudaMemsetAsync(w.work.p, 0, sizeof(int) * 8, st));
-    for (int l = l0; l < 8; ++l) {
+    for (int l = l0; l < l_end; ++l) {
         const int s = l / 2, half = l % 2;
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
         // rows of this layer's scan entries (the stage list) and of its output
@@ -320,7 +321,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         } else {
             ca.list = la.list = s + 1;
             ca.E = la.E = w.E[s + 1].as<StageEntry>();
-            if (s < 3) { la.ipT_next = L[l + 1].ipT; la.R_ipnext = R_first; }
+            if (s < 3 && l + 1 < l_end) { la.ipT_next = L[l + 1].ipT; la.R_ipnext = R_first; }
         }
         launch_contrib(st, l, ca, n_out);
         check_launch("k_contrib");
@@ -363,12 +364,21 @@ struct Engine {
     std::vector<PartState> h_parts;
     Workspace ws;
     Prof prof;
+    // Pinned staging of the partition offsets: a ring of slots, each reused
+    // only after the copy that read it has executed.
+    static constexpr int kOffSlots = 8;
     int* pinned_off = nullptr;
+    int* pinned_rec_off = nullptr;
+    cudaEvent_t off_done[kOffSlots] = {};
+    int off_slot = 0;
     long long last_counts[5] = {0};
     int last_n = 0;
 
     ~Engine() {
+        for (auto& e : off_done)
+            if (e) cudaEventDestroy(e);
         if (pinned_off) cudaFreeHost(pinned_off);
+        if (pinned_rec_off) cudaFreeHost(pinned_rec_off);
     }
 
     size_t state_elems(int kind, int index) const {
@@ -462,7 +472,9 @@ struct Engine {
         }
         upload(parts, h_parts);
         ws.plan(g, P, mpe, max_events, 0, record);
-        SSLA_CK(cudaMallocHost(&pinned_off, sizeof(int) * (P + 1)));
+        SSLA_CK(cudaMallocHost(&pinned_off, sizeof(int) * (P + 1) * kOffSlots));
+        for (auto& e : off_done) SSLA_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        SSLA_CK(cudaMallocHost(&pinned_rec_off, sizeof(int) * (P + 1)));
         reset(nullptr);
         SSLA_CK(cudaStreamSynchronize(nullptr));
     }
@@ -477,7 +489,40 @@ struct Engine {
         check_launch("k_reset_preds");
     }
 
-    void drain(const float* ev_dev, const int* off, uint8_t* flags_dev, cudaStream_t st) {
+    // Stages 0-1 of every event and one ring record per event that passed
+    // gate 1 (partition-major, stream order) into rec_dev; rec_off receives
+    // the per-partition record offsets.  Synchronises `st`.
+    void drain_records(const float* ev_dev, const int* off, void* rec_dev, int rec_cap, int* rec_off,
+                       uint8_t* flags_dev, cudaStream_t st) {
+        if (layout != LAYOUT_HYBRID) throw std::invalid_argument("ring records need the HYBRID layout");
+        const int n = off[g.P];
+        if (rec_cap < n) throw std::length_error("records_cap below the drain's event count");
+        drain(ev_dev, off, flags_dev, st, 1);
+        launch_records(st, n, ws.count.as<int>() + 2, ws.E[2].as<StageEntry>(),
+                       reinterpret_cast<const float4*>(ev_dev), ws.X.as<float>(), rec_dev);
+        check_launch("k_records");
+        SSLA_CK(cudaMemcpyAsync(pinned_rec_off, ws.off[2].p, sizeof(int) * (g.P + 1), cudaMemcpyDeviceToHost, st));
+        SSLA_CK(cudaStreamSynchronize(st));
+        std::memcpy(rec_off, pinned_rec_off, sizeof(int) * (g.P + 1));
+    }
+
+    // Uploads the partition offsets into ws.ev_off through the next pinned
+    // slot (waits only if that slot's previous copy has not run yet).
+    void upload_offsets(const int* off, cudaStream_t st) {
+        const int P = g.P;
+        const int slot = off_slot;
+        off_slot = (off_slot + 1) % kOffSlots;
+        SSLA_CK(cudaEventSynchronize(off_done[slot]));
+        int* dst = pinned_off + static_cast<size_t>(slot) * (P + 1);
+        std::memcpy(dst, off, sizeof(int) * (P + 1));
+        SSLA_CK(cudaMemcpyAsync(ws.ev_off.p, dst, sizeof(int) * (P + 1), cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaEventRecord(off_done[slot], st));
+    }
+
+    // s_last = 3: the full path (s0..s3, head, commit).  s_last = 1: stages
+    // 0-1 with gates 0-1 only (HYBRID layout), leaving the stage-2 list and
+    // its layer-3 output rows for k_records.
+    void drain(const float* ev_dev, const int* off, uint8_t* flags_dev, cudaStream_t st, int s_last = 3) {
         DeviceGuard dg(device);
         const int P = g.P;
         if (off[0] != 0) throw std::invalid_argument("part_offsets[0] must be 0");
@@ -491,8 +536,7 @@ struct Engine {
         ws.n_active = n;
         last_n = n;
         prof.begin(st);
-        std::memcpy(pinned_off, off, sizeof(int) * (P + 1));
-        SSLA_CK(cudaMemcpyAsync(ws.ev_off.p, pinned_off, sizeof(int) * (P + 1), cudaMemcpyHostToDevice, st));
+        upload_offsets(off, st);
         const float4* ev = reinterpret_cast<const float4*>(ev_dev);
         launch_prep(st, ev, n, g.W[0], g.H[0], ws.ev_xy.as<uint32_t>(), ws.rflags.as<uint8_t>());
         check_launch("k_prep");
@@ -510,6 +554,7 @@ struct Engine {
         ga.tl0_cnt = ws.tl_cnt[0].as<int>(); ga.parts = parts.as<PartState>();
         ga.rflags = ws.rflags.as<uint8_t>(); ga.X1 = ws.X.as<float>(); ga.Rcopy = ws.R_B.as<float>();
         ga.L0 = L[0];
+        ga.n_gates = (s_last >= 3) ? 4 : 2;
         launch_gates(st, ga);
         check_launch("k_gates");
         prof.mark("gates", 1, st);
@@ -523,7 +568,7 @@ struct Engine {
         launch_compact(st, ca);
         check_launch("k_compact");
         prof.mark("compact", 3, st);
-        for (int s = 1; s < 4; ++s) {
+        for (int s = 1; s <= s_last; ++s) {
             FilterArgs f{};
             f.g = g; f.stage = s; f.E = ws.E[s].as<StageEntry>(); f.rflags = ws.rflags.as<uint8_t>();
             f.range = ws.off[s].as<int>(); f.tl = ws.tl[s].as<int2>(); f.tl_cnt = ws.tl_cnt[s].as<int>();
@@ -531,7 +576,13 @@ struct Engine {
             launch_filter(st, f);
             check_launch("k_filter");
         }
-        prof.mark("filter_s123", 3, st);
+        prof.mark("filter_s123", s_last, st);
+        if (s_last < 3) {
+            run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, 2 * (s_last + 1));
+            if (flags_dev && n > 0)
+                SSLA_CK(cudaMemcpyAsync(flags_dev, ws.rflags.p, n, cudaMemcpyDeviceToDevice, st));
+            return;
+        }
         run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record, prof);
         CommitArgs cm{};
         cm.g = g; cm.E4 = ws.E[4].as<StageEntry>(); cm.off4 = ws.off[4].as<int>();
@@ -808,6 +859,22 @@ int ssla_engine_drain_host(SslaEngine* eng, const float* events_host, const int*
         if (flags_host && n > 0)
             SSLA_CK(cudaMemcpyAsync(flags_host, e.ws.rflags.p, n, cudaMemcpyDeviceToHost, st));
         SSLA_CK(cudaStreamSynchronize(st));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_drain_records(SslaEngine* eng, const float* events_dev, const int* part_offsets,
+                              void* records_dev, int records_cap, int* record_offsets,
+                              uint8_t* flags_dev, void* stream) {
+    if (!eng || !part_offsets || !record_offsets || (!records_dev && records_cap > 0)) {
+        ssla::g_last_error = "null argument";
+        return SSLA_ERR_ARG;
+    }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        e.drain_records(events_dev, part_offsets, records_dev, records_cap, record_offsets, flags_dev,
+                        static_cast<cudaStream_t>(stream));
         return SSLA_OK;
     });
 }

@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                 if (__ballot_sync(0xffffffffu, in1)) {
                     const bool pass1 = gate(in1, sub2, 2, c1);
                     in2 = in1 && pass1;
-                    if (__ballot_sync(0xffffffffu, in2)) {
+                    if (a.n_gates > 2 && __ballot_sync(0xffffffffu, in2)) {
                         const bool pass2 = hyb ? gate(in2, sub2, 2, c2) : gate(in2, 0, 0, c2);
                         in3 = in2 && pass2;
                         if (hyb && __ballot_sync(0xffffffffu, in3)) pass3 = gate(in3, 0, 0, c3);
@@ -1774,6 +1774,37 @@ void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2
     if (n <= 0) return;
     k_prep_records<<<grid_for(n, kNT), kNT, 0, st>>>(static_cast<const HybridInputRec*>(rec), n,
                                                       E2, ev_xy, rflags, feat);
+}
+
+// ---------------------------------------------------------------------------
+// k_records: the ring record of every event that passed gate 1 (stage-2
+// list entry r): t, stage-2 coordinates, the stage-1 output feat1 -- the
+// record the shard workers push after stage 1 (lib_stage01_to_gpu.cpp:
+// 262-300).  seq_done / t_push_ns / t_emit_ns are left zero for the host.
+// ---------------------------------------------------------------------------
+__global__ void k_records(int n_cap, const int* __restrict__ count2, const StageEntry* __restrict__ E2,
+                          const float4* __restrict__ ev, const float* __restrict__ feat1,
+                          HybridInputRec* __restrict__ rec) {
+    const int n = min(count2[0], n_cap);
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
+        const StageEntry se = E2[r];
+        HybridInputRec o;
+        o.seq_done = 0;
+        o.t = ev[se.e].x;
+        o.x = static_cast<uint16_t>((se.xy0 & 0xFFFFu) >> 2);
+        o.y = static_cast<uint16_t>((se.xy0 >> 16) >> 2);
+#pragma unroll
+        for (int c = 0; c < 24; ++c) o.feat1[c] = feat1[static_cast<size_t>(r) * 24 + c];
+        o.t_push_ns = 0;
+        o.t_emit_ns = 0;
+        rec[r] = o;
+    }
+}
+
+void launch_records(cudaStream_t st, int n_cap, const int* count2, const StageEntry* E2,
+                    const float4* ev, const float* feat1, void* rec) {
+    k_records<<<grid_for(n_cap, kNT), kNT, 0, st>>>(n_cap, count2, E2, ev, feat1,
+                                                     static_cast<HybridInputRec*>(rec));
 }
 
 void launch_filter(cudaStream_t st, const FilterArgs& a) {

@@ -30,6 +30,7 @@ struct GateArgs {
     float* X1;               // [N][12] layer-0 output per event
     float* Rcopy;            // [N][12] layer-1 residual (events entering stage 1)
     DevLayer L0;
+    int n_gates;             // gates applied: 4 (full path) or 2 (stages 0-1 only)
 };
 
 // Gates for drain_n records entering at stage 2 (tdrop_s2 on the s2 grid,
@@ -176,6 +177,9 @@ void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
                          uint32_t* ev_xy, uint8_t* rflags, float* feat);
 void launch_filter(cudaStream_t st, const FilterArgs& a);
+// One HybridInputRec (t, s2 x / y, feat1) per stage-2 list entry.
+void launch_records(cudaStream_t st, int n_cap, const int* count2, const StageEntry* E2,
+                    const float4* ev, const float* feat1, void* rec);
 void launch_gates(cudaStream_t st, const GateArgs& a);
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a);
 void launch_compact(cudaStream_t st, const CompactArgs& a);

@@ -49,6 +49,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_write_state": (i, [vp, i, i, i, vp, C.c_size_t]),
         "ssla_engine_state_ptr": (vp, [vp, i, i, i]),
         "ssla_engine_info": (i, [vp, C.POINTER(abi.SslaEngineInfo)]),
+        "ssla_engine_drain_records": (i, [vp, vp, vp, vp, i, vp, vp, vp]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
         "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
         "ssla_s2s3_gate_codes_noalloc": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp]),
@@ -146,6 +147,18 @@ class SslaEngine:
         off = np.ascontiguousarray(part_offsets, dtype=np.int32)
         _check(self.lib.ssla_engine_drain_host(self.h, _ptr(events), off.ctypes.data,
                                                _ptr(flags), _stream(stream)))
+
+    def drain_records(self, events, part_offsets, records, records_cap: int, flags=None,
+                      stream=None) -> np.ndarray:
+        """Stages 0-1 only; one HybridInputRec per event passing gate 1 into
+        the device buffer ``records``.  Returns the per-partition record
+        offsets (synchronises)."""
+        off = np.ascontiguousarray(part_offsets, dtype=np.int32)
+        rec_off = np.zeros(self.n_partitions + 1, dtype=np.int32)
+        _check(self.lib.ssla_engine_drain_records(self.h, _ptr(events), off.ctypes.data, _ptr(records),
+                                                  records_cap, rec_off.ctypes.data, _ptr(flags),
+                                                  _stream(stream)))
+        return rec_off
 
     def _read(self, kind: int, partition: int, index: int, dtype) -> np.ndarray:
         nb = C.c_size_t()
