@@ -120,6 +120,28 @@ int  ssla_engine_drain_host(SslaEngine* eng, const float* events_host,
                             const int* part_offsets, uint8_t* flags_host,
                             void* stream);
 
+/* One event (t, x, y, p; host memory, passed by value to the kernel) of
+ * `partition` through preprocess, the gates, stages 0-3 and the head in a
+ * single launch -- the batch-of-1 path.  Leaves exactly the state a drain
+ * of that one event leaves.  flag_out (may be NULL) receives the event's
+ * SSLA_F_* bits; pred_out (may be NULL, 5+ncls floats) receives the decoded
+ * prediction row of the event's stage-3 cell when the event reached the
+ * head.  Both may be device memory or pinned host memory (written by the
+ * kernel directly).  Asynchronous on `stream`.  Replaces one
+ * SslaSPipeline::step (src/ssla_kernels.cpp:927-989) / one ring record of
+ * the persistent kernel (ssla_s2_s3_head_celled.cuh:1547-1784). */
+int  ssla_engine_step(SslaEngine* eng, int partition, const float* event,
+                      uint8_t* flag_out, float* pred_out, void* stream);
+
+/* Batch-of-1 latency: steps the n events (host array of 4-float rows) one
+ * at a time with ssla_engine_step -- flags and prediction row written by
+ * the kernel into pinned host memory -- and records, per event, the host
+ * time from the call to the stream synchronize returning (microseconds).
+ * flags_out (may be NULL) receives each event's SSLA_F_* bits.  Measurement
+ * support; the engine's state advances as with ssla_engine_step. */
+int  ssla_engine_step_latency(SslaEngine* eng, int partition, const float* events_host,
+                              int n, double* latency_us, uint8_t* flags_out);
+
 /* Stages 0-1 only (HYBRID layout): preprocess, gates 0-1, layers 0-3 for
  * every event (state of stages 0-1 advances), and one HybridInputRec per
  * event that passed gate 1 -- t, stage-2 x / y, feat1 = the stage-1 output;

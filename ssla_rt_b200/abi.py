@@ -91,7 +91,7 @@ EXPORTED = (
     "ssla_engine_info", "ssla_s2s3_drain_n_multi", "ssla_s2s3_drain_n",
     "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak",
     "ssla_expf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
-    "ssla_engine_drain_records",
+    "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
 )
 # Every symbol include/stage01_to_gpu.h declares (the libstage01_to_gpu ABI).
 S01G_EXPORTED = (

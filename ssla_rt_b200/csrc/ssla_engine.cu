@@ -15,6 +15,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <chrono>
 #include <vector>
 
 #include "ssla_b200.h"
@@ -489,6 +490,22 @@ struct Engine {
         check_launch("k_reset_preds");
     }
 
+    // One event of partition p through the whole path (k_step); flag_out /
+    // pred_out may be device or pinned host memory.  Asynchronous on st.
+    void step(int p, const float* e4, uint8_t* flag_out, float* pred_out, cudaStream_t st) {
+        if (p < 0 || p >= g.P) throw std::invalid_argument("partition out of range");
+        StepArgs a{};
+        a.g = g;
+        a.ps = h_parts[p];
+        for (int l = 0; l < 8; ++l) a.L[l] = L[l];
+        a.head = head;
+        a.ev = make_float4(e4[0], e4[1], e4[2], e4[3]);
+        a.flag_out = flag_out;
+        a.pred_out = pred_out;
+        SSLA_CK(launch_step(st, a));
+        check_launch("k_step");
+    }
+
     // Stages 0-1 of every event and one ring record per event that passed
     // gate 1 (partition-major, stream order) into rec_dev; rec_off receives
     // the per-partition record offsets.  Synchronises `st`.
@@ -859,6 +876,44 @@ int ssla_engine_drain_host(SslaEngine* eng, const float* events_host, const int*
         if (flags_host && n > 0)
             SSLA_CK(cudaMemcpyAsync(flags_host, e.ws.rflags.p, n, cudaMemcpyDeviceToHost, st));
         SSLA_CK(cudaStreamSynchronize(st));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_step(SslaEngine* eng, int partition, const float* event, uint8_t* flag_out,
+                     float* pred_out, void* stream) {
+    if (!eng || !event) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        e.step(partition, event, flag_out, pred_out, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_step_latency(SslaEngine* eng, int partition, const float* events_host, int n,
+                             double* latency_us, uint8_t* flags_out) {
+    if (!eng || !events_host || !latency_us || n < 0) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        cudaStream_t st = nullptr;
+        uint8_t* flag = nullptr;
+        float* pred = nullptr;
+        SSLA_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        SSLA_CK(cudaMallocHost(&flag, 1));
+        SSLA_CK(cudaMallocHost(&pred, sizeof(float) * (5 + e.g.ncls)));
+        for (int i = 0; i < n; ++i) {
+            const auto t0 = std::chrono::steady_clock::now();
+            e.step(partition, events_host + 4 * i, flag, pred, st);
+            SSLA_CK(cudaStreamSynchronize(st));
+            const auto t1 = std::chrono::steady_clock::now();
+            latency_us[i] = std::chrono::duration<double, std::micro>(t1 - t0).count();
+            if (flags_out) flags_out[i] = *flag;
+        }
+        cudaFreeHost(pred);
+        cudaFreeHost(flag);
+        cudaStreamDestroy(st);
         return SSLA_OK;
     });
 }

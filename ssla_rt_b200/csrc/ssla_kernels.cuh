@@ -157,6 +157,17 @@ struct GemmArgs {
     float* R;                // [*][OUT2]
 };
 
+// One event through the whole path (ssla_step.cu).
+struct StepArgs {
+    Geo g;
+    PartState ps;            // the partition's state
+    DevLayer L[8];
+    DevHead head;
+    float4 ev;               // t, x, y, p
+    uint8_t* flag_out;       // SSLA_F_* bits of the event (or null)
+    float* pred_out;         // decoded prediction row when the event reached the head (or null)
+};
+
 struct CommitArgs {
     Geo g;
     const StageEntry* E4;
@@ -177,6 +188,7 @@ void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
                          uint32_t* ev_xy, uint8_t* rflags, float* feat);
 void launch_filter(cudaStream_t st, const FilterArgs& a);
+cudaError_t launch_step(cudaStream_t st, const StepArgs& a);
 // One HybridInputRec (t, s2 x / y, feat1) per stage-2 list entry.
 void launch_records(cudaStream_t st, int n_cap, const int* count2, const StageEntry* E2,
                     const float4* ev, const float* feat1, void* rec);

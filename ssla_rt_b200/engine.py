@@ -50,6 +50,8 @@ def load_library() -> C.CDLL:
         "ssla_engine_state_ptr": (vp, [vp, i, i, i]),
         "ssla_engine_info": (i, [vp, C.POINTER(abi.SslaEngineInfo)]),
         "ssla_engine_drain_records": (i, [vp, vp, vp, vp, i, vp, vp, vp]),
+        "ssla_engine_step": (i, [vp, i, vp, vp, vp, vp]),
+        "ssla_engine_step_latency": (i, [vp, i, vp, i, vp, vp]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
         "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
         "ssla_s2s3_gate_codes_noalloc": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp]),
@@ -147,6 +149,24 @@ class SslaEngine:
         off = np.ascontiguousarray(part_offsets, dtype=np.int32)
         _check(self.lib.ssla_engine_drain_host(self.h, _ptr(events), off.ctypes.data,
                                                _ptr(flags), _stream(stream)))
+
+    def step(self, event, partition: int = 0, flag_out=None, pred_out=None, stream=None) -> None:
+        """One event (4 floats t, x, y, p) through the whole path in one
+        launch; outputs (device or pinned host buffers) written by the
+        kernel.  Asynchronous."""
+        e = np.ascontiguousarray(event, dtype=np.float32).reshape(4)
+        _check(self.lib.ssla_engine_step(self.h, partition, e.ctypes.data, _ptr(flag_out), _ptr(pred_out),
+                                         _stream(stream)))
+
+    def step_latency(self, events: np.ndarray, partition: int = 0):
+        """Per-event host latency (us) of ssla_engine_step + synchronize,
+        measured inside the library; returns (latency_us, flags)."""
+        ev = np.ascontiguousarray(events, dtype=np.float32).reshape(-1, 4)
+        lat = np.zeros(ev.shape[0], dtype=np.float64)
+        fl = np.zeros(ev.shape[0], dtype=np.uint8)
+        _check(self.lib.ssla_engine_step_latency(self.h, partition, ev.ctypes.data, ev.shape[0],
+                                                 lat.ctypes.data, fl.ctypes.data))
+        return lat, fl
 
     def drain_records(self, events, part_offsets, records, records_cap: int, flags=None,
                       stream=None) -> np.ndarray:
