@@ -2,17 +2,20 @@
 // stages 0-3 and the head in one launch, for batch-of-1 latency.
 //
 // A cluster of 9 CTAs; CTA rank d owns patch position d (delta = (1-dy)*3 +
-// (1-dx), the reference's numbering).  CTA 0 also runs preprocess and the
-// gates, holds the layer input, the residual and the LayerNorm, and runs
-// the head.  Per layer: every CTA copies the input row from CTA 0 (DSMEM),
-// computes q, v, sigmoid(g) of its patch cell (matvec_ct<IN,3*OUT>,
-// linear.h:80-90), updates the cell's state (lru_step, rnn.h:80-91) and,
-// when the layer output is used, its goW contribution; after a cluster
-// barrier CTA 0 sums the contributions in the reference's patch order
-// (delta = 8..0, in-bounds only), adds the residual and normalises
-// (layer_forward_ct, src/ssla_kernels.cpp:315-385; layernorm.h:41-62).
+// (1-dx), the reference's numbering).  CTA 0 runs preprocess and the gates
+// and all of stages 0-1 (their weights fit one CTA), holds the layer input,
+// the residual and the LayerNorm, and runs the head.  Layers 4-7: every
+// CTA copies the input row from CTA 0 (DSMEM), computes q, v, sigmoid(g) of
+// its patch cell (matvec_ct<IN,3*OUT>, linear.h:80-90), updates the cell's
+// state (lru_step, rnn.h:80-91) and, when the layer output is used, its goW
+// contribution; after a cluster barrier CTA 0 sums the contributions in the
+// reference's patch order (delta = 8..0, in-bounds only), adds the residual
+// and normalises (layer_forward_ct, src/ssla_kernels.cpp:315-385;
+// layernorm.h:41-62).
 // Every value is formed with the same fmaf chains as the chunk engine and
 // the C oracle, so a stepped event leaves bit-identical state.
+// Weights, gamma / beta and the cells' state rows of the next layer are
+// copied into shared memory with cp.async while the current layer runs.
 #include <cooperative_groups.h>
 
 #include <atomic>
@@ -26,177 +29,154 @@ namespace ssla {
 namespace {
 
 constexpr int kStepNT = 512;
-// weight staging buffer (floats): the largest qvg slice + goW slice (layer 7),
-// also reused for the residual and head weights
-constexpr int kStepW = 96 * 288 + 96 * 96;
 constexpr int kStepCTAs = 9;
 
-__device__ __forceinline__ bool step_gate(uint8_t* c, int window) {
-    const int pre = *c;
-    *c = static_cast<uint8_t>(pre + 1);
+// ---- shared-memory plan (floats) -------------------------------------------
+// Layer buffers: [qvg A*IN*3*OUT][goW A*OUT*OUT][gamma][beta][cell rows A*OUT]
+// [input_proj IN*OUT (first layers)], then (layers 0-3) scratch
+// [qvg values A*3*OUT][q*h A*OUT][contributions A*OUT].
+template <int IN, int OUT, int A>
+struct [[maybe_unused]] Lay {
+    static constexpr int J2 = 3 * OUT;
+    static constexpr int WQ = A * IN * J2, WG = A * OUT * OUT;
+    static constexpr int GAM = WQ + WG, BET = GAM + OUT, HR = BET + OUT, WI = HR + A * OUT;
+    static constexpr int QV = WI + IN * OUT, QH = QV + A * J2, CON = QH + A * OUT;
+    static constexpr int total = CON + A * OUT;
+    static constexpr int layer = WI + IN * OUT;      // cluster layers: no scratch
+};
+// layers 0-3 (CTA 0): even layers at 0, odd layers at kSmallOdd
+constexpr int kSmallOdd = Lay<12, 24, 9>::total;
+// every CTA's layer-4 buffer, filled while CTA 0 runs layers 0-3
+constexpr int kL4Base = kSmallOdd + Lay<24, 24, 9>::total;
+// layers 5-7 and the head reuse the low region
+constexpr int kSmem = kL4Base + Lay<24, 48, 1>::layer;
+static_assert(Lay<2, 12, 1>::total <= kSmallOdd && Lay<12, 12, 9>::total <= kL4Base - kSmallOdd, "small");
+static_assert(Lay<48, 48, 1>::layer <= kSmem && Lay<48, 96, 1>::layer <= kSmem &&
+              Lay<96, 96, 1>::WI <= kSmem, "layers 5-7");
+static_assert(kSmallOdd % 4 == 0 && kL4Base % 4 == 0, "alignment");
+
+__device__ __forceinline__ bool step_gate(int pre, int window) {
     return window <= 1 || ((pre & 255) % window) == 0;
 }
 
 struct StepShared {
     float x[96];          // layer input (CTA 0 holds the authoritative copy)
-    float qvg[288];       // q | v | g of this CTA's patch cell
+    float qvg[288];       // q | v | g of this CTA's patch cell (layers 4-7)
     float qh[96];
     float contrib[96];    // goW[delta] * qh
     float res[96];        // CTA 0: residual of the current layer
     float y[96];          // CTA 0: pre-norm output
+    float gb[192];        // CTA 0: gamma | beta kept aside from the copies
     float act[192];       // CTA 0: head conv activations (cls | reg)
     float hrow[24];       // CTA 0: head outputs (raw)
     double mean, inv;
+    double d2[96];        // CTA 0: squared deviations of the LayerNorm
+    double lt_prev;       // CTA 0: gate inputs loaded in parallel
+    int cnt_in[4];
     int flags;
     int px, py;           // stage-0 pixel
 };
 
-// Copies n floats (n % 4 == 0, 16-byte aligned) into shared memory with
-// independent 16-byte loads from every thread.
-__device__ __forceinline__ void stage(float* dst, const float* src, int n) {
-    for (int t = threadIdx.x; t < n / 4; t += blockDim.x)
-        reinterpret_cast<float4*>(dst)[t] = __ldg(reinterpret_cast<const float4*>(src) + t);
-}
-
-// Same, as asynchronous 16-byte copies (cp.async); complete after
-// async_wait() + __syncthreads().
+// Asynchronous 16-byte copies (cp.async) of n floats (n % 4 == 0, both
+// sides 16-byte aligned) by every thread of the CTA; async_commit() closes
+// the group, async_wait() + __syncthreads() completes it.
 __device__ __forceinline__ void stage_async(float* dst, const float* src, int n) {
     for (int t = threadIdx.x; t < n / 4; t += blockDim.x) {
         const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(dst + 4 * t));
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(src + 4 * t) : "memory");
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void async_wait() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// The patch cell of position d at stage s around (cx0, cy0); A == 1 is the
+// event's own cell.
+__device__ __forceinline__ bool patch_cell(int A, int d, int cx0, int cy0, int Ws, int Hs, int& cx, int& cy) {
+    if (A == 1) { cx = cx0; cy = cy0; return true; }
+    cx = cx0 + 1 - d % 3;
+    cy = cy0 + 1 - d / 3;
+    return cx >= 0 && cx < Ws && cy >= 0 && cy < Hs;
 }
 
-__device__ __forceinline__ void async_wait() {
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
-// One layer of the event's path as seen by one CTA.
-struct StepLayer {
-    int l, s, half, IN, OUT, A;
-    bool used;      // the layer output is consumed (else state-only, last layer)
-    bool act;       // this CTA's patch cell is in bounds
-    int d, cx, cy;  // patch position and cell
-};
-
-__device__ __forceinline__ bool step_layer(int idx, int flags, int px, int py, int rank, const Geo& g,
-                                           StepLayer& L) {
-    const int s = idx / 2, half = idx % 2;
-    if (s > 3) return false;
-    if (s > 0 && !(flags & (F_R1 << (s - 1)))) return false;
-    if (half == 1) {
-        // the first layer of the stage always runs; the second follows it
-    }
-    L.l = idx;
-    L.s = s;
-    L.half = half;
-    L.OUT = chans(s);
-    L.IN = (idx == 0) ? 2 : (half == 0 ? chans(s - 1) : L.OUT);
-    L.A = (idx == 0) ? 1 : 9;
-    L.used = half == 0 || (s < 3 ? (flags & (F_R1 << s)) != 0 : (flags & F_R4) != 0);
-    const int cx0 = px >> s, cy0 = py >> s;
-    if (L.A == 1) {
-        L.d = 0;
-        L.cx = cx0;
-        L.cy = cy0;
-        L.act = rank == 0;
-    } else {
-        L.d = rank;
-        L.cx = cx0 + 1 - rank % 3;
-        L.cy = cy0 + 1 - rank / 3;
-        L.act = L.cx >= 0 && L.cx < g.W[s] && L.cy >= 0 && L.cy < g.H[s];
-    }
-    return true;
-}
-
-// Issues the weight copies a CTA needs for layer L into wsm:
-// qvg [IN][3*OUT] | goW [OUT][OUT] | (CTA 0, first layers) input_proj [IN][OUT].
-__device__ __forceinline__ void issue_layer(const StepLayer& L, const DevLayer* layers, int rank, float* wsm) {
-    const int J2 = 3 * L.OUT;
-    const DevLayer& W = layers[L.l];
-    if (L.act) {
-        stage_async(wsm, W.qvgT + static_cast<size_t>(L.d) * L.IN * J2, L.IN * J2);
-        if (L.used) stage_async(wsm + L.IN * J2, W.goWT + static_cast<size_t>(L.d) * L.OUT * L.OUT, L.OUT * L.OUT);
-    }
-    if (rank == 0 && L.used && L.half == 0)
-        stage_async(wsm + L.IN * J2 + L.OUT * L.OUT, W.ipT, L.IN * L.OUT);
-}
-
-// Head weights for CTA 0: cls conv | reg conv [96][96], reg pred [96][4]
-// (obj / cls preds are read directly, they are small).
-__device__ __forceinline__ void issue_head(const DevHead& hd, float* wsm) {
-    stage_async(wsm, hd.cls_convT, 96 * 96);
-    stage_async(wsm + 96 * 96, hd.reg_convT, 96 * 96);
-    stage_async(wsm + 2 * 96 * 96, hd.reg_predT, 96 * 4);
-}
-
-// LayerNorm of sh.y (OUT values) into sh.x: sequential fp64 statistics by
-// one thread (layernorm.h:41-62), then the per-channel normalisation.
-__device__ __forceinline__ void step_ln(StepShared& sh, int OUT, const DevLayer& L) {
+// LayerNorm of sh.y (OUT values) into sh.x: the two fp64 sums run
+// sequentially in channel order by one thread, the squared deviations
+// (the same rounded products) by all threads (layernorm.h:41-62).
+__device__ __forceinline__ void step_ln(StepShared& sh, int OUT, const float* gam, const float* bet) {
     const int tid = threadIdx.x;
     if (tid == 0) {
         double sum = 0.0;
         for (int o = 0; o < OUT; ++o) sum += static_cast<double>(sh.y[o]);
-        const double mean = sum / static_cast<double>(OUT);
+        sh.mean = sum / static_cast<double>(OUT);
+    }
+    __syncthreads();
+    const double mean = sh.mean;
+    for (int o = tid; o < OUT; o += kStepNT) {
+        const double dd = static_cast<double>(sh.y[o]) - mean;
+        sh.d2[o] = dd * dd;
+    }
+    __syncthreads();
+    if (tid == 0) {
         double var = 0.0;
-        for (int o = 0; o < OUT; ++o) {
-            const double dd = static_cast<double>(sh.y[o]) - mean;
-            var += dd * dd;
-        }
+        for (int o = 0; o < OUT; ++o) var += sh.d2[o];
         var /= static_cast<double>(OUT);
-        sh.mean = mean;
         sh.inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
     }
     __syncthreads();
     for (int t = tid; t < OUT; t += kStepNT) {
         const double tt = (static_cast<double>(sh.y[t]) - sh.mean) * sh.inv;
-        sh.x[t] = static_cast<float>(tt * static_cast<double>(__ldg(L.gamma + t)) +
-                                     static_cast<double>(__ldg(L.beta + t)));
+        sh.x[t] = static_cast<float>(tt * static_cast<double>(gam[t]) + static_cast<double>(bet[t]));
     }
 }
 
-// One of layers 0-3 of one event by one CTA, every patch position: the
-// weights of all positions are staged, then (position, column) items form
-// q, v, sigmoid(g), (position, channel) items update the cells and
-// (position, output) items form the goW contributions; the ordered sum,
-// residual and LayerNorm follow.  Returns false when the layer is the
-// event's last (state-only).
+// ---- layers 0-3 on CTA 0 ---------------------------------------------------
+// Issues the copies of small layer l into its buffer: weights of every
+// patch position, gamma / beta, the state rows of the in-bounds cells.
 template <int IN, int OUT, int A>
-__device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py, StepShared& sh, float* wsm) {
-    constexpr int J2 = 3 * OUT;
+__device__ void issue_small(int l, bool used, const StepArgs& a, int px, int py, float* wsm) {
+    using Lo = Lay<IN, OUT, A>;
+    const DevLayer& L = a.L[l];
+    const int s = l / 2;
+    float* b = wsm + ((l & 1) ? kSmallOdd : 0);
+    stage_async(b, L.qvgT, Lo::WQ);
+    if (used) {
+        stage_async(b + Lo::WQ, L.goWT, Lo::WG);
+        stage_async(b + Lo::GAM, L.gamma, OUT);
+        stage_async(b + Lo::BET, L.beta, OUT);
+        if ((l & 1) == 0) stage_async(b + Lo::WI, L.ipT, IN * OUT);
+    }
+    const int Ws = a.g.W[s], Hs = a.g.H[s];
+    for (int d = 0; d < A; ++d) {
+        int cx, cy;
+        if (patch_cell(A, d, px >> s, py >> s, Ws, Hs, cx, cy))
+            stage_async(b + Lo::HR + d * OUT, a.ps.hidden[l] + (static_cast<size_t>(cy) * Ws + cx) * OUT, OUT);
+    }
+    async_commit();
+}
+
+// One of layers 0-3 by CTA 0, every patch position: (position, column)
+// items form q, v, sigmoid(g), (position, channel) items update the cells
+// and (position, output) items form the goW contributions; the ordered
+// sum, residual and LayerNorm follow.  Returns false when the layer is the
+// event's last (state-only).
+template <int IN, int OUT, int A, typename Next>
+__device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py, StepShared& sh, float* wsm,
+                            Next next_issue) {
+    using Lo = Lay<IN, OUT, A>;
+    constexpr int J2 = Lo::J2;
     const int tid = threadIdx.x;
     const int s = l / 2, half = l % 2;
-    const DevLayer& L = a.L[l];
-    const Geo& g = a.g;
-    const int Ws = g.W[s], Hs = g.H[s], cx0 = px >> s, cy0 = py >> s;
-    float* wq = wsm;                              // [A][IN][J2]
-    float* wg = wq + A * IN * J2;                 // [A][OUT][OUT]
-    float* wi = wg + A * OUT * OUT;               // [IN][OUT]
-    float* qvg = wi + IN * OUT;                   // [A][J2]
-    float* qh = qvg + A * J2;                     // [A][OUT]
-    float* con = qh + A * OUT;                    // [A][OUT]
-    auto cell_of = [&](int d, int& cx, int& cy) {
-        if (A == 1) { cx = cx0; cy = cy0; return true; }
-        cx = cx0 + 1 - d % 3;
-        cy = cy0 + 1 - d / 3;
-        return cx >= 0 && cx < Ws && cy >= 0 && cy < Hs;
-    };
-    // this thread's (position, channel) item: its cell state, loaded early
-    const int hd = tid / OUT, ht = tid % OUT;
-    float* hp = nullptr;
-    float h_old = 0.0f;
-    if (tid < A * OUT) {
-        int cx, cy;
-        if (cell_of(hd, cx, cy)) {
-            hp = a.ps.hidden[l] + (static_cast<size_t>(cy) * Ws + cx) * OUT + ht;
-            h_old = *hp;
-        }
-    }
-    stage(wq, L.qvgT, A * IN * J2);
-    if (used) stage(wg, L.goWT, A * OUT * OUT);
-    if (used && half == 0) stage(wi, L.ipT, IN * OUT);
+    const int Ws = a.g.W[s], Hs = a.g.H[s], cx0 = px >> s, cy0 = py >> s;
+    float* b = wsm + ((l & 1) ? kSmallOdd : 0);
+    const float* wq = b;
+    const float* wg = b + Lo::WQ;
+    const float* wi = b + Lo::WI;
+    const float* hr = b + Lo::HR;
+    float* qvg = b + Lo::QV;
+    float* qh = b + Lo::QH;
+    float* con = b + Lo::CON;
+    async_wait();                                // this layer's copies (issued earlier)
     __syncthreads();
+    next_issue();                                // the next layer's, into the other buffer
     if (used) {
         for (int t = tid; t < OUT; t += kStepNT) {
             float acc;
@@ -214,7 +194,7 @@ __device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py,
     for (int it = tid; it < A * (J2 - c0); it += kStepNT) {
         const int d = it / (J2 - c0), col = c0 + it % (J2 - c0);
         int cx, cy;
-        if (!cell_of(d, cx, cy)) continue;
+        if (!patch_cell(A, d, cx0, cy0, Ws, Hs, cx, cy)) continue;
         float acc = 0.0f;
         const float* w = wq + d * IN * J2 + col;
 #pragma unroll
@@ -222,24 +202,24 @@ __device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py,
         qvg[d * J2 + col] = acc;
     }
     __syncthreads();
-    if (hp) {
+    const int hd = tid / OUT, ht = tid % OUT;
+    int hcx = 0, hcy = 0;
+    const bool hact = tid < A * OUT && patch_cell(A, hd, cx0, cy0, Ws, Hs, hcx, hcy);
+    if (hact) {
         const float* q = qvg + hd * J2;
-        const float h = fmaf(ssla_sigmoidf(q[2 * OUT + ht]), h_old, q[OUT + ht]);
-        *hp = h;
+        const float h = fmaf(ssla_sigmoidf(q[2 * OUT + ht]), hr[hd * OUT + ht], q[OUT + ht]);
+        a.ps.hidden[l][(static_cast<size_t>(hcy) * Ws + hcx) * OUT + ht] = h;
         if (used) qh[hd * OUT + ht] = q[ht] * h;
     }
     if (!used) return false;                     // state-only second layer: the event ends
     __syncthreads();
-    if (tid < A * OUT) {
-        int cx, cy;
-        if (cell_of(hd, cx, cy)) {
-            const float* w = wg + hd * OUT * OUT + ht;
-            const float* q = qh + hd * OUT;
-            float acc = 0.0f;
+    if (hact) {
+        const float* w = wg + hd * OUT * OUT + ht;
+        const float* q = qh + hd * OUT;
+        float acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < OUT; ++i) acc = fmaf(w[i * OUT], q[i], acc);
-            con[hd * OUT + ht] = acc;
-        }
+        for (int i = 0; i < OUT; ++i) acc = fmaf(w[i * OUT], q[i], acc);
+        con[hd * OUT + ht] = acc;
     }
     __syncthreads();
     for (int t = tid; t < OUT; t += kStepNT) {
@@ -247,37 +227,94 @@ __device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py,
 #pragma unroll
         for (int d = A - 1; d >= 0; --d) {
             int cx, cy;
-            if (!cell_of(d, cx, cy)) continue;
+            if (!patch_cell(A, d, cx0, cy0, Ws, Hs, cx, cy)) continue;
             v = v + con[d * OUT + t];
         }
         sh.y[t] = v + sh.res[t];
     }
     __syncthreads();
-    step_ln(sh, OUT, L);
+    step_ln(sh, OUT, b + Lo::GAM, b + Lo::BET);
     __syncthreads();
     return true;
 }
 
-// Layers 0-3 (the event reaches stage 1 when gate 0 passed).  Leaves the
+// Layers 0-3 (layer 0's copies were issued at kernel start).  Leaves the
 // stage-2 input in sh.x when the event passes gate 1.
 __device__ void small_layers(const StepArgs& a, int flags, int px, int py, StepShared& sh, float* wsm) {
-    if (!small_layer<2, 12, 1>(0, true, a, px, py, sh, wsm)) return;
-    if (!small_layer<12, 12, 9>(1, (flags & F_R1) != 0, a, px, py, sh, wsm)) return;
-    if (!small_layer<12, 24, 9>(2, true, a, px, py, sh, wsm)) return;
-    small_layer<24, 24, 9>(3, (flags & F_R2) != 0, a, px, py, sh, wsm);
+    const bool r1 = (flags & F_R1) != 0, r2 = (flags & F_R2) != 0;
+    if (!small_layer<2, 12, 1>(0, true, a, px, py, sh, wsm,
+                               [&] { issue_small<12, 12, 9>(1, r1, a, px, py, wsm); }))
+        return;
+    if (!small_layer<12, 12, 9>(1, r1, a, px, py, sh, wsm,
+                                [&] { if (r1) issue_small<12, 24, 9>(2, true, a, px, py, wsm); }))
+        return;
+    if (!small_layer<12, 24, 9>(2, true, a, px, py, sh, wsm,
+                                [&] { issue_small<24, 24, 9>(3, r2, a, px, py, wsm); }))
+        return;
+    small_layer<24, 24, 9>(3, r2, a, px, py, sh, wsm, [] {});
 }
 
-// One CTA's part of layers 4-7: residual (CTA 0), q / v / sigmoid(g) of its
-// patch cell, the cell's state update and its goW contribution.
+// ---- layers 4-7 on the cluster ---------------------------------------------
+struct StepLayer {
+    int l, s, half, IN, OUT;
+    bool used;      // the layer output is consumed (else state-only, last layer)
+    bool act;       // this CTA's patch cell is in bounds
+    int cx, cy;     // this CTA's patch cell
+};
+
+__device__ __forceinline__ bool step_layer(int l, int flags, int px, int py, int rank, const Geo& g,
+                                           StepLayer& L) {
+    const int s = l / 2, half = l % 2;
+    if (s > 3 || s < 2) return false;
+    if (!(flags & (F_R1 << (s - 1)))) return false;
+    L.l = l;
+    L.s = s;
+    L.half = half;
+    L.OUT = chans(s);
+    L.IN = half == 0 ? chans(s - 1) : L.OUT;
+    L.used = half == 0 || (s < 3 ? (flags & (F_R1 << s)) != 0 : (flags & F_R4) != 0);
+    L.act = patch_cell(9, rank, px >> s, py >> s, g.W[s], g.H[s], L.cx, L.cy);
+    return true;
+}
+
+__device__ __forceinline__ float* layer_base(float* wsm, int l) { return wsm + (l == 4 ? kL4Base : 0); }
+
+// Offsets inside a layer-4..7 buffer (Lay<IN, OUT, 1> with runtime sizes).
+__device__ __forceinline__ int off_gam(int IN, int OUT) { return IN * 3 * OUT + OUT * OUT; }
+
+// Issues the copies a CTA needs for layer L: its patch position's weights
+// and state row; CTA 0 also gamma, beta and input_proj (first layers).
+__device__ void issue_layer(const StepLayer& L, const StepArgs& a, int rank, float* wsm) {
+    const int IN = L.IN, OUT = L.OUT, J2 = 3 * OUT;
+    const DevLayer& W = a.L[L.l];
+    float* b = layer_base(wsm, L.l);
+    const int gam = off_gam(IN, OUT);
+    if (L.act) {
+        stage_async(b, W.qvgT + static_cast<size_t>(rank) * IN * J2, IN * J2);
+        if (L.used) stage_async(b + IN * J2, W.goWT + static_cast<size_t>(rank) * OUT * OUT, OUT * OUT);
+        stage_async(b + gam + 2 * OUT,
+                    a.ps.hidden[L.l] + (static_cast<size_t>(L.cy) * a.g.W[L.s] + L.cx) * OUT, OUT);
+    }
+    if (rank == 0 && L.used) {
+        stage_async(b + gam, W.gamma, OUT);
+        stage_async(b + gam + OUT, W.beta, OUT);
+        if (L.half == 0) stage_async(b + gam + 3 * OUT, W.ipT, IN * OUT);
+    }
+    async_commit();
+}
+
+// One CTA's part of a layer 4-7: residual (CTA 0), q / v / sigmoid(g) of
+// its patch cell, the cell's state update and its goW contribution.
 template <int IN, int OUT>
 __device__ void cl_compute(const StepLayer& cur, bool rank0, const StepArgs& a, StepShared& sh,
-                           const float* wsm, float h_old, float* hp) {
+                           const float* b) {
     constexpr int J2 = 3 * OUT;
+    constexpr int GAM = IN * J2 + OUT * OUT;
     const int tid = threadIdx.x;
     const bool used = cur.used;
-    const float* wq = wsm;
-    const float* wg = wsm + IN * J2;
-    const float* wi = wg + OUT * OUT;
+    const float* wq = b;
+    const float* wg = b + IN * J2;
+    const float* wi = b + GAM + 3 * OUT;
     if (rank0 && used) {
         for (int t = tid; t < OUT; t += kStepNT) {
             float acc;
@@ -300,9 +337,9 @@ __device__ void cl_compute(const StepLayer& cur, bool rank0, const StepArgs& a, 
             sh.qvg[col] = acc;
         }
         __syncthreads();
-        if (hp) {
-            const float h = fmaf(ssla_sigmoidf(sh.qvg[2 * OUT + tid]), h_old, sh.qvg[OUT + tid]);
-            *hp = h;
+        if (tid < OUT) {
+            const float h = fmaf(ssla_sigmoidf(sh.qvg[2 * OUT + tid]), b[GAM + 2 * OUT + tid], sh.qvg[OUT + tid]);
+            a.ps.hidden[cur.l][(static_cast<size_t>(cur.cy) * a.g.W[cur.s] + cur.cx) * OUT + tid] = h;
             if (used) sh.qh[tid] = sh.qvg[tid] * h;
         }
         __syncthreads();
@@ -313,6 +350,30 @@ __device__ void cl_compute(const StepLayer& cur, bool rank0, const StepArgs& a, 
             sh.contrib[tid] = acc;
         }
     }
+    if (rank0 && used) {
+        // gamma / beta aside: the next layer's copies may reuse this buffer
+        for (int t = tid; t < OUT; t += kStepNT) {
+            sh.gb[t] = b[GAM + t];
+            sh.gb[96 + t] = b[GAM + OUT + t];
+        }
+    }
+}
+
+// ---- head (CTA 0) ------------------------------------------------------------
+// cls conv | reg conv [96][96], reg pred [96][4], obj pred [96], cls pred
+// [96][ncls], cls | reg conv biases [96] each.
+constexpr int kHeadRp = 2 * 96 * 96, kHeadOb = kHeadRp + 96 * 4, kHeadCp = kHeadOb + 96;
+__device__ __forceinline__ int head_cb(int ncls) { return kHeadCp + ((96 * ncls + 3) & ~3); }
+
+__device__ void issue_head(const DevHead& hd, int ncls, float* wsm) {
+    stage_async(wsm, hd.cls_convT, 96 * 96);
+    stage_async(wsm + 96 * 96, hd.reg_convT, 96 * 96);
+    stage_async(wsm + kHeadRp, hd.reg_predT, 96 * 4);
+    stage_async(wsm + kHeadOb, hd.obj_predT, 96);
+    stage_async(wsm + kHeadCp, hd.cls_predT, 96 * ncls);
+    stage_async(wsm + head_cb(ncls), hd.cls_conv_b, 96);
+    stage_async(wsm + head_cb(ncls) + 96, hd.reg_conv_b, 96);
+    async_commit();
 }
 
 __global__ void __launch_bounds__(kStepNT) k_step(StepArgs a) {
@@ -320,102 +381,109 @@ __global__ void __launch_bounds__(kStepNT) k_step(StepArgs a) {
     const int rank = static_cast<int>(cluster.block_rank());
     const int tid = threadIdx.x;
     __shared__ StepShared sh;
-    extern __shared__ __align__(16) float wsm[];      // [kStepW] staged weights
+    extern __shared__ __align__(16) float wsm[];
     StepShared* sh0 = cluster.map_shared_rank(&sh, 0);
     const PartState& ps = a.ps;
     const Geo& g = a.g;
     const bool hyb = g.layout == LAYOUT_HYBRID;
 
-    // ---- preprocess + gates (CTA 0, one thread) ----
-    if (rank == 0 && tid == 0) {
+    // ---- preprocess + gates (CTA 0): inputs loaded in parallel, decided by
+    // one thread in gate order (each counter advances at most once) ----
+    if (rank == 0) {
         const float4 e = a.ev;
-        int flags = 0;
-        if (e.y > -1.0f && e.y < static_cast<float>(g.W[0]) && e.z > -1.0f && e.z < static_cast<float>(g.H[0])) {
-            const int x = static_cast<int>(e.y), y = static_cast<int>(e.z);
-            double* lt = ps.last_t + y * g.W[0] + x;
-            const double prev = *lt;
-            float dt;
-            if (prev < 0.0) {
-                dt = 1.0f;
-            } else {
-                double v = (static_cast<double>(e.x) - prev) / 1e5;
-                if (v < 0.0) v = 0.0;
-                if (v > 1.0) v = 1.0;
-                dt = static_cast<float>(v);
-            }
-            *lt = static_cast<double>(e.x);
-            flags = F_VALID;
-            const int w = g.window;
-            const bool pass0 = step_gate(ps.cnt[0] + (y >> 1) * g.W[1] + (x >> 1), w);
-            if (pass0) {
-                flags |= F_R1;
-                const bool pass1 = step_gate(ps.cnt[1] + (y >> 2) * g.W[2] + (x >> 2), w);
-                if (pass1) {
-                    flags |= F_R2;
-                    const bool pass2 = hyb ? step_gate(ps.cnt[2] + (y >> 2) * g.W[2] + (x >> 2), w)
-                                           : step_gate(ps.cnt[2] + (y >> 3) * g.W[3] + (x >> 3), w);
-                    if (pass2) {
-                        flags |= F_R3;
-                        const bool pass3 = hyb ? step_gate(ps.cnt[3] + (y >> 3) * g.W[3] + (x >> 3), w) : true;
-                        if (pass3) flags |= F_R4;
+        const bool valid = e.y > -1.0f && e.y < static_cast<float>(g.W[0]) && e.z > -1.0f &&
+                           e.z < static_cast<float>(g.H[0]);
+        const int x = valid ? static_cast<int>(e.y) : 0, y = valid ? static_cast<int>(e.z) : 0;
+        const int k0 = (y >> 1) * g.W[1] + (x >> 1), k1 = (y >> 2) * g.W[2] + (x >> 2);
+        const int k2 = hyb ? k1 : (y >> 3) * g.W[3] + (x >> 3), k3 = (y >> 3) * g.W[3] + (x >> 3);
+        if (valid) {
+            issue_small<2, 12, 1>(0, true, a, x, y, wsm);       // layer 0, needed by any valid event
+            if (tid == 0) sh.lt_prev = ps.last_t[y * g.W[0] + x];
+            else if (tid == 1) sh.cnt_in[0] = ps.cnt[0][k0];
+            else if (tid == 2) sh.cnt_in[1] = ps.cnt[1][k1];
+            else if (tid == 3) sh.cnt_in[2] = ps.cnt[2][k2];
+            else if (tid == 4 && hyb) sh.cnt_in[3] = ps.cnt[3][k3];
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int flags = 0;
+            if (valid) {
+                const double prev = sh.lt_prev;
+                float dt;
+                if (prev < 0.0) {
+                    dt = 1.0f;
+                } else {
+                    double v = (static_cast<double>(e.x) - prev) / 1e5;
+                    if (v < 0.0) v = 0.0;
+                    if (v > 1.0) v = 1.0;
+                    dt = static_cast<float>(v);
+                }
+                ps.last_t[y * g.W[0] + x] = static_cast<double>(e.x);
+                flags = F_VALID;
+                const int w = g.window;
+                ps.cnt[0][k0] = static_cast<uint8_t>(sh.cnt_in[0] + 1);
+                if (step_gate(sh.cnt_in[0], w)) {
+                    flags |= F_R1;
+                    ps.cnt[1][k1] = static_cast<uint8_t>(sh.cnt_in[1] + 1);
+                    if (step_gate(sh.cnt_in[1], w)) {
+                        flags |= F_R2;
+                        ps.cnt[2][k2] = static_cast<uint8_t>(sh.cnt_in[2] + 1);
+                        if (step_gate(sh.cnt_in[2], w)) {
+                            flags |= F_R3;
+                            bool pass3 = true;
+                            if (hyb) {
+                                ps.cnt[3][k3] = static_cast<uint8_t>(sh.cnt_in[3] + 1);
+                                pass3 = step_gate(sh.cnt_in[3], w);
+                            }
+                            if (pass3) flags |= F_R4;
+                        }
                     }
                 }
+                sh.px = x;
+                sh.py = y;
+                sh.x[0] = dt;
+                sh.x[1] = e.w;
             }
-            sh.px = x;
-            sh.py = y;
-            sh.x[0] = dt;
-            sh.x[1] = e.w;
+            sh.flags = flags;
+            if (a.flag_out) *a.flag_out = static_cast<uint8_t>(flags);
         }
-        sh.flags = flags;
-        if (a.flag_out) *a.flag_out = static_cast<uint8_t>(flags);
     }
     cluster.sync();
     const int flags = sh0->flags;
     const int px = sh0->px, py = sh0->py;
 
     if (flags & F_VALID) {
-        // ---- stages 0-1 (layers 0-3) on CTA 0 alone: all patch positions of
-        // these small layers fit one CTA, so no cluster barrier is needed;
-        // the other CTAs prefetch their layer-4 weights meanwhile.
+        // layer-4 copies of every CTA land while CTA 0 runs layers 0-3
         StepLayer cur;
-        bool have = (flags & F_R2) && step_layer(4, flags, px, py, rank, g, cur);
-        if (have && rank != 0) issue_layer(cur, a.L, rank, wsm);
+        bool have = step_layer(4, flags, px, py, rank, g, cur);
+        if (have) issue_layer(cur, a, rank, wsm);
         if (rank == 0) small_layers(a, flags, px, py, sh, wsm);
         cluster.sync();                    // stage-2 input ready in CTA 0
-        if (have && rank == 0) issue_layer(cur, a.L, rank, wsm);
         bool head_issued = false;
         while (have) {
-            const int IN = cur.IN, OUT = cur.OUT;
+            const int OUT = cur.OUT;
             const int s = cur.s;
             const int Ws = g.W[s], Hs = g.H[s];
             const int cx0 = px >> s, cy0 = py >> s;
-            const bool used = cur.used;
-            const DevLayer& L = a.L[cur.l];
-            // the cell state and the layer input (DSMEM) while the weights arrive
-            float* hp = nullptr;
-            float h_old = 0.0f;
-            if (cur.act && tid < OUT) {
-                hp = ps.hidden[cur.l] + (static_cast<size_t>(cur.cy) * Ws + cur.cx) * OUT + tid;
-                h_old = *hp;
-            }
+            const float* b = layer_base(wsm, cur.l);
             if (rank != 0)
-                for (int t = tid; t < IN; t += kStepNT) sh.x[t] = sh0->x[t];
+                for (int t = tid; t < cur.IN; t += kStepNT) sh.x[t] = sh0->x[t];
             async_wait();
             __syncthreads();
             switch (cur.l) {
-                case 4: cl_compute<24, 48>(cur, rank == 0, a, sh, wsm, h_old, hp); break;
-                case 5: cl_compute<48, 48>(cur, rank == 0, a, sh, wsm, h_old, hp); break;
-                case 6: cl_compute<48, 96>(cur, rank == 0, a, sh, wsm, h_old, hp); break;
-                default: cl_compute<96, 96>(cur, rank == 0, a, sh, wsm, h_old, hp); break;
+                case 4: cl_compute<24, 48>(cur, rank == 0, a, sh, b); break;
+                case 5: cl_compute<48, 48>(cur, rank == 0, a, sh, b); break;
+                case 6: cl_compute<48, 96>(cur, rank == 0, a, sh, b); break;
+                default: cl_compute<96, 96>(cur, rank == 0, a, sh, b); break;
             }
             __syncthreads();               // this layer's weights are consumed
-            if (!used) break;              // state-only second layer: the event ends here
+            if (!cur.used) break;          // state-only second layer: the event ends here
             StepLayer nxt;
             have = step_layer(cur.l + 1, flags, px, py, rank, g, nxt);
             if (have) {
-                issue_layer(nxt, a.L, rank, wsm);   // lands during the gather / LayerNorm below
+                issue_layer(nxt, a, rank, wsm);   // lands during the gather / LayerNorm below
             } else if (rank == 0 && (flags & F_R4)) {
-                issue_head(a.head, wsm);
+                issue_head(a.head, g.ncls, wsm);
                 head_issued = true;
             }
             cluster.sync();                // contributions ready, inputs copied
@@ -438,7 +506,7 @@ __global__ void __launch_bounds__(kStepNT) k_step(StepArgs a) {
                     sh.y[t] = v + sh.res[t];
                 }
                 __syncthreads();
-                step_ln(sh, OUT, L);
+                step_ln(sh, OUT, sh.gb, sh.gb + 96);
             }
             cluster.sync();                // next input ready in CTA 0
             cur = nxt;
@@ -448,43 +516,39 @@ __global__ void __launch_bounds__(kStepNT) k_step(StepArgs a) {
         // ---- head and commit (CTA 0) ----
         if (rank == 0 && (flags & F_R4)) {
             const DevHead& hd = a.head;
-            // staged (issue_head): cls conv | reg conv [96][96] each, reg [96][4];
-            // obj [96] and cls [96][ncls] follow here
-            float* wc = wsm;
-            float* wr = wsm + 96 * 96;
-            float* wrp = wsm + 2 * 96 * 96;
-            float* wob = wrp + 96 * 4;
-            float* wcp = wob + 96;
-            if (!head_issued) {
-                stage(wc, hd.cls_convT, 96 * 96);
-                stage(wr, hd.reg_convT, 96 * 96);
-                stage(wrp, hd.reg_predT, 96 * 4);
-            }
-            for (int t = tid; t < 96; t += kStepNT) wob[t] = __ldg(hd.obj_predT + t);
-            for (int t = tid; t < 96 * g.ncls; t += kStepNT) wcp[t] = __ldg(hd.cls_predT + t);
+            const int ncls = g.ncls;
+            if (!head_issued) issue_head(hd, ncls, wsm);
+            const float obj_b = __ldg(hd.obj_pred_b);
+            async_wait();
             __syncthreads();
+            const float* wc = wsm;
+            const float* wr = wsm + 96 * 96;
+            const float* wrp = wsm + kHeadRp;
+            const float* wob = wsm + kHeadOb;
+            const float* wcp = wsm + kHeadCp;
+            const float* cb = wsm + head_cb(ncls);
             for (int j = tid; j < 192; j += kStepNT) {
                 const int jo = j % 96;
                 const float* Wt = (j < 96) ? wc : wr;
-                float acc = __ldg(((j < 96) ? hd.cls_conv_b : hd.reg_conv_b) + jo);
+                float acc = cb[j];
 #pragma unroll 8
                 for (int i = 0; i < 96; ++i) acc = fmaf(Wt[i * 96 + jo], sh.x[i], acc);
                 sh.act[j] = acc * ssla_sigmoidf(acc);
             }
             __syncthreads();
-            const int cols = 5 + g.ncls;
+            const int cols = 5 + ncls;
             for (int r = tid; r < cols; r += kStepNT) {
                 float acc;
                 if (r < 4) {
                     acc = __ldg(hd.reg_pred_b + r);
                     for (int i = 0; i < 96; ++i) acc = fmaf(wrp[i * 4 + r], sh.act[96 + i], acc);
                 } else if (r == 4) {
-                    acc = __ldg(hd.obj_pred_b);
+                    acc = obj_b;
                     for (int i = 0; i < 96; ++i) acc = fmaf(wob[i], sh.act[96 + i], acc);
                 } else {
                     const int c = r - 5;
                     acc = __ldg(hd.cls_pred_b + c);
-                    for (int i = 0; i < 96; ++i) acc = fmaf(wcp[i * g.ncls + c], sh.act[i], acc);
+                    for (int i = 0; i < 96; ++i) acc = fmaf(wcp[i * ncls + c], sh.act[i], acc);
                 }
                 sh.hrow[r] = acc;
             }
@@ -510,13 +574,14 @@ __global__ void __launch_bounds__(kStepNT) k_step(StepArgs a) {
             if (own && tid == 0) ps.version[cell] += 1u;
         }
     }
+    async_wait();                          // no copy in flight at exit
     cluster.sync();                        // no CTA leaves while its smem may be read
 }
 
 }  // namespace
 
 cudaError_t launch_step(cudaStream_t st, const StepArgs& a) {
-    constexpr size_t smem = sizeof(float) * kStepW;
+    constexpr size_t smem = sizeof(float) * kSmem;
     // function attributes are per device: set once for each device used
     static std::atomic<unsigned long long> attr_done{0};
     int dev = 0;
