@@ -370,6 +370,9 @@ struct Engine {
     static constexpr int kOffSlots = 8;
     int* pinned_off = nullptr;
     int* pinned_rec_off = nullptr;
+    // Status word of the step kernel (host-mapped): bits of bounded waits
+    // that ran out, read and cleared by the next step call.
+    unsigned* step_err = nullptr;
     cudaEvent_t off_done[kOffSlots] = {};
     int off_slot = 0;
     long long last_counts[5] = {0};
@@ -380,6 +383,7 @@ struct Engine {
             if (e) cudaEventDestroy(e);
         if (pinned_off) cudaFreeHost(pinned_off);
         if (pinned_rec_off) cudaFreeHost(pinned_rec_off);
+        if (step_err) cudaFreeHost(step_err);
     }
 
     size_t state_elems(int kind, int index) const {
@@ -476,6 +480,8 @@ struct Engine {
         SSLA_CK(cudaMallocHost(&pinned_off, sizeof(int) * (P + 1) * kOffSlots));
         for (auto& e : off_done) SSLA_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         SSLA_CK(cudaMallocHost(&pinned_rec_off, sizeof(int) * (P + 1)));
+        SSLA_CK(cudaHostAlloc(&step_err, sizeof(unsigned), cudaHostAllocMapped));
+        *step_err = 0;
         reset(nullptr);
         SSLA_CK(cudaStreamSynchronize(nullptr));
     }
@@ -502,8 +508,21 @@ struct Engine {
         a.ev = make_float4(e4[0], e4[1], e4[2], e4[3]);
         a.flag_out = flag_out;
         a.pred_out = pred_out;
+        a.err = step_err;
+        check_step_status();
         SSLA_CK(launch_step(st, a));
         check_launch("k_step");
+    }
+
+    // Raises (and clears) the status of earlier steps: a wait inside k_step
+    // that ran out means that step's outputs are not valid.
+    void check_step_status() {
+        const unsigned v = __atomic_load_n(step_err, __ATOMIC_ACQUIRE);
+        if (v) {
+            __atomic_store_n(step_err, 0u, __ATOMIC_RELEASE);
+            throw std::runtime_error("k_step: a bounded wait ran out (status " + std::to_string(v) +
+                                     "; 1 = weight copies, 2 = layer input, 4 = contributions)");
+        }
     }
 
     // Stages 0-1 of every event and one ring record per event that passed
@@ -914,6 +933,7 @@ int ssla_engine_step_latency(SslaEngine* eng, int partition, const float* events
         cudaFreeHost(pred);
         cudaFreeHost(flag);
         cudaStreamDestroy(st);
+        e.check_step_status();
         return SSLA_OK;
     });
 }

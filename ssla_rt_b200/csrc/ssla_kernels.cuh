@@ -166,6 +166,7 @@ struct StepArgs {
     float4 ev;               // t, x, y, p
     uint8_t* flag_out;       // SSLA_F_* bits of the event (or null)
     float* pred_out;         // decoded prediction row when the event reached the head (or null)
+    unsigned* err;           // status bits of waits that ran out (host-mapped, or null)
 };
 
 struct CommitArgs {

@@ -2,27 +2,27 @@
 // stages 0-3 and the head in one launch, for batch-of-1 latency.
 //
 // A cluster of 9 CTAs; CTA rank d owns patch position d (delta = (1-dy)*3 +
-// (1-dx), the reference's numbering).  CTA 0 runs preprocess and the gates
-// and all of stages 0-1 (their weights fit one CTA), holds the layer input,
-// the residual and the LayerNorm, and runs the head.  Layers 4-7: every
-// CTA copies the input row from CTA 0 (DSMEM), computes q, v, sigmoid(g) of
-// its patch cell (matvec_ct<IN,3*OUT>, linear.h:80-90), updates the cell's
-// state (lru_step, rnn.h:80-91) and, when the layer output is used, its goW
-// contribution; after a cluster barrier CTA 0 sums the contributions in the
-// reference's patch order (delta = 8..0, in-bounds only), adds the residual
-// and normalises (layer_forward_ct, src/ssla_kernels.cpp:315-385;
-// layernorm.h:41-62).
+// (1-dx), the reference's numbering).  Every CTA reads the gate counters and
+// derives the event's reach bits itself, so no CTA waits for a decision.
+// CTA 0 runs preprocess and all of stages 0-1 (their weights fit one CTA),
+// holds the layer input, the residual and the LayerNorm, and runs the head.
+// Layers 4-7 are message-passing between CTA 0 and the CTAs whose patch cell
+// is in bounds: CTA 0 sends the layer input into their shared memory
+// (st.async, completing on the receiver's mbarrier); each computes q, v,
+// sigmoid(g) of its cell (matvec_ct<IN,3*OUT>, linear.h:80-90), updates the
+// cell's state (lru_step, rnn.h:80-91) and sends its goW contribution back
+// the same way; CTA 0 sums the contributions in the reference's patch order
+// (delta = 8..0, in-bounds only), adds the residual and normalises
+// (layer_forward_ct, src/ssla_kernels.cpp:315-385; layernorm.h:41-62).
+// Weights, gamma / beta and the cells' state rows reach shared memory by bulk
+// copies issued as soon as their buffer is free, each layer completing on its
+// own mbarrier.  Every wait is bounded (kWaitNs); a wait that runs out sets a
+// bit in the caller's status word and the kernel carries on to its end.
 // Every value is formed with the same fmaf chains as the chunk engine and
 // the C oracle, so a stepped event leaves bit-identical state.
-// Weights, gamma / beta and the cells' state rows of the next layer are
-// copied into shared memory with cp.async while the current layer runs.
-#include <cooperative_groups.h>
-
 #include <atomic>
 
 #include "ssla_kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace ssla {
 
@@ -30,64 +30,145 @@ namespace {
 
 constexpr int kStepNT = 512;
 constexpr int kStepCTAs = 9;
+constexpr int kIssuer = kStepNT - 32;                         // lane 0 of the last warp issues copies
+constexpr unsigned long long kWaitNs = 20ull * 1000ull * 1000ull;   // bound of every wait (20 ms)
+constexpr int kMaxBlockSmem = 232448;                         // 227 KB per CTA on sm_100
 
 // ---- shared-memory plan (floats) -------------------------------------------
-// Layer buffers: [qvg A*IN*3*OUT][goW A*OUT*OUT][gamma][beta][cell rows A*OUT]
+// A layer buffer: [qvg A*IN*3*OUT][goW A*OUT*OUT][gamma][beta][cell rows A*OUT]
 // [input_proj IN*OUT (first layers)], then (layers 0-3) scratch
 // [qvg values A*3*OUT][q*h A*OUT][contributions A*OUT].
+#pragma nv_diag_suppress 177   // not every layer uses every offset of its plan
 template <int IN, int OUT, int A>
-struct [[maybe_unused]] Lay {
+struct Lay {
     static constexpr int J2 = 3 * OUT;
     static constexpr int WQ = A * IN * J2, WG = A * OUT * OUT;
     static constexpr int GAM = WQ + WG, BET = GAM + OUT, HR = BET + OUT, WI = HR + A * OUT;
     static constexpr int QV = WI + IN * OUT, QH = QV + A * J2, CON = QH + A * OUT;
     static constexpr int total = CON + A * OUT;
-    static constexpr int layer = WI + IN * OUT;      // cluster layers: no scratch
+    static constexpr int layer = WI + IN * OUT;      // layers 4-7: no scratch
 };
-// layers 0-3 (CTA 0): even layers at 0, odd layers at kSmallOdd
-constexpr int kSmallOdd = Lay<12, 24, 9>::total;
-// every CTA's layer-4 buffer, filled while CTA 0 runs layers 0-3
-constexpr int kL4Base = kSmallOdd + Lay<24, 24, 9>::total;
-// layers 5-7 and the head reuse the low region
-constexpr int kSmem = kL4Base + Lay<24, 48, 1>::layer;
-static_assert(Lay<2, 12, 1>::total <= kSmallOdd && Lay<12, 12, 9>::total <= kL4Base - kSmallOdd, "small");
-static_assert(Lay<48, 48, 1>::layer <= kSmem && Lay<48, 96, 1>::layer <= kSmem &&
-              Lay<96, 96, 1>::WI <= kSmem, "layers 5-7");
-static_assert(kSmallOdd % 4 == 0 && kL4Base % 4 == 0, "alignment");
+// CTA 0, from kernel start: layers 0-3 back to back, then layer 4.
+constexpr int kS1 = Lay<2, 12, 1>::total;
+constexpr int kS2 = kS1 + Lay<12, 12, 9>::total;
+constexpr int kS3 = kS2 + Lay<12, 24, 9>::total;
+constexpr int kR4 = kS3 + Lay<24, 24, 9>::total;
+// Layers 5-7 (one patch position each): layer 6 at 0, layer 5 above it; layer
+// 7's qvg block over the layer 4/5 buffers, its goW | gamma | beta | row at 0.
+// The head (CTA 0) at 0 once layers 6 and 7 no longer need it.
+constexpr int kR6 = 0;
+constexpr int kR5 = Lay<48, 96, 1>::layer;
+constexpr int kR7q = kR5;
+constexpr int kR7 = 0;
+constexpr int kRH = 0;
+constexpr int kDyn = (kR4 + Lay<24, 48, 1>::layer) > (kR7q + 96 * 288) ? (kR4 + Lay<24, 48, 1>::layer)
+                                                                       : (kR7q + 96 * 288);
+static_assert(kR5 + Lay<48, 48, 1>::WI <= kR4, "layer 5 below layer 4");
+static_assert(kR7 + 96 * 96 + 3 * 96 <= kR7q, "layer 7 goW below its qvg block");
+static_assert(kS1 % 4 == 0 && kS2 % 4 == 0 && kS3 % 4 == 0 && kR4 % 4 == 0 && kR5 % 4 == 0,
+              "16-byte aligned buffers");
+// head: cls conv | reg conv [96][96], reg pred [96][4], obj pred [96],
+// cls pred [96][ncls], cls | reg conv biases [96] each.
+constexpr int kHeadRp = 2 * 96 * 96, kHeadOb = kHeadRp + 96 * 4, kHeadCp = kHeadOb + 96;
+__host__ __device__ constexpr int head_cb(int ncls) { return kHeadCp + 96 * ncls; }
+__host__ __device__ constexpr int head_floats(int ncls) { return head_cb(ncls) + 192; }
+
+struct StepShared {
+    uint64_t bar_w[10];   // copies: layers 0-7, head (8), layer-7 qvg block (9)
+    uint64_t bar_x[8];    // layer input received (layers 4-7)
+    uint64_t bar_c[8];    // CTA 0: contributions received (layers 4-7)
+    double ln_mean, ln_inv;
+    double lnbuf[96];     // CTA 0: LayerNorm operands
+    float x[96];          // layer input
+    float qvg[288];       // q | v | g of this CTA's patch cell (layers 4-7)
+    float qh[96];
+    float res[96];        // CTA 0: residual of the current layer
+    float gb[192];        // CTA 0: gamma | beta of layers 4-7, kept aside from the copies
+    float con[9][96];     // CTA 0: goW contributions by patch position; head activations
+};
+static_assert(sizeof(StepShared) + sizeof(float) * kDyn <= kMaxBlockSmem, "shared memory");
+
+// ---- PTX wrappers ------------------------------------------------------------
+__device__ __forceinline__ uint32_t su32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t cta_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(su32(bar))
+        : "memory");
+    return ok != 0;
+}
+// Waits for phase 0 of `bar` (every barrier completes once per launch).
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned* err, unsigned code) {
+    if (mbar_test(bar)) return;
+    const unsigned long long t0 = gtime();
+    while (!mbar_test(bar)) {
+        if (gtime() - t0 > kWaitNs) {
+            if (err) atomicOr_system(err, code);
+            return;
+        }
+    }
+}
+// n floats global -> own shared memory, completing on `bar` (the issuing
+// thread also raises the barrier's expected byte count).
+__device__ __forceinline__ void bulk(float* dst, const float* src, int n, uint64_t* bar) {
+    const uint32_t bytes = static_cast<uint32_t>(n) * 4u;
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     su32(dst)),
+                 "l"(src), "r"(bytes), "r"(su32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ uint32_t peer(uint32_t addr, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// One float into CTA `rank`'s shared memory at the address of `dst` in this
+// CTA, completing 4 bytes on that CTA's barrier at the address of `bar`.
+__device__ __forceinline__ void send(const float* dst, const uint64_t* bar, int rank, float v) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                     peer(su32(dst), rank)),
+                 "r"(__float_as_uint(v)), "r"(peer(su32(bar), rank))
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// status bits: a wait for copies, for the layer input, for contributions ran out
+constexpr unsigned kErrWeights = 1u, kErrInput = 2u, kErrContrib = 4u;
 
 __device__ __forceinline__ bool step_gate(int pre, int window) {
     return window <= 1 || ((pre & 255) % window) == 0;
 }
-
-struct StepShared {
-    float x[96];          // layer input (CTA 0 holds the authoritative copy)
-    float qvg[288];       // q | v | g of this CTA's patch cell (layers 4-7)
-    float qh[96];
-    float contrib[96];    // goW[delta] * qh
-    float res[96];        // CTA 0: residual of the current layer
-    float y[96];          // CTA 0: pre-norm output
-    float gb[192];        // CTA 0: gamma | beta kept aside from the copies
-    float act[192];       // CTA 0: head conv activations (cls | reg)
-    float hrow[24];       // CTA 0: head outputs (raw)
-    double mean, inv;
-    double d2[96];        // CTA 0: squared deviations of the LayerNorm
-    double lt_prev;       // CTA 0: gate inputs loaded in parallel
-    int cnt_in[4];
-    int flags;
-    int px, py;           // stage-0 pixel
-};
-
-// Asynchronous 16-byte copies (cp.async) of n floats (n % 4 == 0, both
-// sides 16-byte aligned) by every thread of the CTA; async_commit() closes
-// the group, async_wait() + __syncthreads() completes it.
-__device__ __forceinline__ void stage_async(float* dst, const float* src, int n) {
-    for (int t = threadIdx.x; t < n / 4; t += blockDim.x) {
-        const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(dst + 4 * t));
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(src + 4 * t) : "memory");
-    }
-}
-__device__ __forceinline__ void async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void async_wait() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // The patch cell of position d at stage s around (cx0, cy0); A == 1 is the
 // event's own cell.
@@ -98,75 +179,215 @@ __device__ __forceinline__ bool patch_cell(int A, int d, int cx0, int cy0, int W
     return cx >= 0 && cx < Ws && cy >= 0 && cy < Hs;
 }
 
-// LayerNorm of sh.y (OUT values) into sh.x: the two fp64 sums run
-// sequentially in channel order by one thread, the squared deviations
-// (the same rounded products) by all threads (layernorm.h:41-62).
-__device__ __forceinline__ void step_ln(StepShared& sh, int OUT, const float* gam, const float* bet) {
-    const int tid = threadIdx.x;
-    if (tid == 0) {
-        double sum = 0.0;
-        for (int o = 0; o < OUT; ++o) sum += static_cast<double>(sh.y[o]);
-        sh.mean = sum / static_cast<double>(OUT);
-    }
-    __syncthreads();
-    const double mean = sh.mean;
-    for (int o = tid; o < OUT; o += kStepNT) {
-        const double dd = static_cast<double>(sh.y[o]) - mean;
-        sh.d2[o] = dd * dd;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        double var = 0.0;
-        for (int o = 0; o < OUT; ++o) var += sh.d2[o];
-        var /= static_cast<double>(OUT);
-        sh.inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
-    }
-    __syncthreads();
-    for (int t = tid; t < OUT; t += kStepNT) {
-        const double tt = (static_cast<double>(sh.y[t]) - sh.mean) * sh.inv;
-        sh.x[t] = static_cast<float>(tt * static_cast<double>(gam[t]) + static_cast<double>(bet[t]));
+// What the event does, derived identically by every CTA.
+struct Plan {
+    int flags, px, py;
+    bool runs[8];     // the layer runs (its stage is reached)
+    bool used[8];     // its output is consumed (else state-only: the event ends there)
+    unsigned inb[8];  // bit d: patch position d's cell is in bounds (layers 1-7)
+};
+
+__device__ __forceinline__ void make_plan(Plan& P, int flags, int px, int py, const Geo& g) {
+    P.flags = flags;
+    P.px = px;
+    P.py = py;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+        const int s = l / 2, half = l % 2;
+        P.runs[l] = (flags & F_VALID) && (s == 0 || (flags & (F_R1 << (s - 1))));
+        P.used[l] = P.runs[l] && (half == 0 || (s < 3 ? (flags & (F_R1 << s)) != 0 : (flags & F_R4) != 0));
+        unsigned m = 0;
+        for (int d = 0; d < 9; ++d) {
+            int cx, cy;
+            if (patch_cell(9, d, px >> s, py >> s, g.W[s], g.H[s], cx, cy)) m |= 1u << d;
+        }
+        P.inb[l] = m;
     }
 }
 
-// ---- layers 0-3 on CTA 0 ---------------------------------------------------
-// Issues the copies of small layer l into its buffer: weights of every
-// patch position, gamma / beta, the state rows of the in-bounds cells.
+__device__ __forceinline__ int cl_in(int l) { return l == 4 ? 24 : l == 7 ? 96 : 48; }
+__device__ __forceinline__ int cl_out(int l) { return l < 6 ? 48 : 96; }
+__device__ __forceinline__ float* cl_wq(float* wsm, int l) {
+    return wsm + (l == 4 ? kR4 : l == 5 ? kR5 : l == 6 ? kR6 : kR7q);
+}
+// goW | gamma | beta | cell row | input_proj of a layer 4-7 buffer
+__device__ __forceinline__ float* cl_rest(float* wsm, int l) {
+    return l == 7 ? wsm + kR7 : cl_wq(wsm, l) + cl_in(l) * 3 * cl_out(l);
+}
+// This CTA takes part in layer l (4-7): its cell is in bounds, or it is CTA 0
+// and the layer's output is used (residual, gather, LayerNorm).
+__device__ __forceinline__ bool cl_part(const Plan& P, int l, int rank) {
+    return P.runs[l] && (((P.inb[l] >> rank) & 1u) || (rank == 0 && P.used[l]));
+}
+
+// ---- copies (issuer thread) -----------------------------------------------------
 template <int IN, int OUT, int A>
-__device__ void issue_small(int l, bool used, const StepArgs& a, int px, int py, float* wsm) {
+__device__ void issue_small(int l, const Plan& P, const StepArgs& a, float* b, uint64_t* bar) {
     using Lo = Lay<IN, OUT, A>;
     const DevLayer& L = a.L[l];
     const int s = l / 2;
-    float* b = wsm + ((l & 1) ? kSmallOdd : 0);
-    stage_async(b, L.qvgT, Lo::WQ);
-    if (used) {
-        stage_async(b + Lo::WQ, L.goWT, Lo::WG);
-        stage_async(b + Lo::GAM, L.gamma, OUT);
-        stage_async(b + Lo::BET, L.beta, OUT);
-        if ((l & 1) == 0) stage_async(b + Lo::WI, L.ipT, IN * OUT);
+    bulk(b, L.qvgT, Lo::WQ, bar);
+    if (P.used[l]) {
+        bulk(b + Lo::WQ, L.goWT, Lo::WG, bar);
+        bulk(b + Lo::GAM, L.gamma, OUT, bar);
+        bulk(b + Lo::BET, L.beta, OUT, bar);
+        if ((l & 1) == 0) bulk(b + Lo::WI, L.ipT, IN * OUT, bar);
     }
     const int Ws = a.g.W[s], Hs = a.g.H[s];
     for (int d = 0; d < A; ++d) {
         int cx, cy;
-        if (patch_cell(A, d, px >> s, py >> s, Ws, Hs, cx, cy))
-            stage_async(b + Lo::HR + d * OUT, a.ps.hidden[l] + (static_cast<size_t>(cy) * Ws + cx) * OUT, OUT);
+        if (patch_cell(A, d, P.px >> s, P.py >> s, Ws, Hs, cx, cy))
+            bulk(b + Lo::HR + d * OUT, a.ps.hidden[l] + (static_cast<size_t>(cy) * Ws + cx) * OUT, OUT, bar);
     }
-    async_commit();
+    mbar_arrive(bar);
 }
 
-// One of layers 0-3 by CTA 0, every patch position: (position, column)
-// items form q, v, sigmoid(g), (position, channel) items update the cells
-// and (position, output) items form the goW contributions; the ordered
-// sum, residual and LayerNorm follow.  Returns false when the layer is the
-// event's last (state-only).
-template <int IN, int OUT, int A, typename Next>
-__device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py, StepShared& sh, float* wsm,
-                            Next next_issue) {
+// Layer l (4-7) copies of CTA `rank`: part 1 = its qvg block, part 2 = the
+// rest (goW, cell row; CTA 0 also gamma, beta, input_proj), 3 = both.
+// Layer 7's qvg block completes on its own barrier.
+__device__ void issue_cl(int l, int part, const Plan& P, int rank, const StepArgs& a, float* wsm,
+                         StepShared& sh) {
+    const int IN = cl_in(l), OUT = cl_out(l), J2 = 3 * OUT, s = l / 2;
+    const bool act = (P.inb[l] >> rank) & 1u;
+    const DevLayer& W = a.L[l];
+    if ((part & 1) && act) {
+        uint64_t* bar = l == 7 ? &sh.bar_w[9] : &sh.bar_w[l];
+        bulk(cl_wq(wsm, l), W.qvgT + static_cast<size_t>(rank) * IN * J2, IN * J2, bar);
+        if (l == 7) mbar_arrive(bar);
+    }
+    if (part & 2) {
+        uint64_t* bar = &sh.bar_w[l];
+        float* r = cl_rest(wsm, l);
+        if (act) {
+            if (P.used[l]) bulk(r, W.goWT + static_cast<size_t>(rank) * OUT * OUT, OUT * OUT, bar);
+            int cx, cy;
+            patch_cell(9, rank, P.px >> s, P.py >> s, a.g.W[s], a.g.H[s], cx, cy);
+            bulk(r + OUT * OUT + 2 * OUT, a.ps.hidden[l] + (static_cast<size_t>(cy) * a.g.W[s] + cx) * OUT, OUT,
+                 bar);
+        }
+        if (rank == 0 && P.used[l]) {
+            bulk(r + OUT * OUT, W.gamma, OUT, bar);
+            bulk(r + OUT * OUT + OUT, W.beta, OUT, bar);
+            if ((l & 1) == 0) bulk(r + OUT * OUT + 3 * OUT, W.ipT, IN * OUT, bar);
+        }
+        mbar_arrive(bar);
+    }
+}
+
+__device__ void issue_head(const DevHead& hd, int ncls, float* wsm, uint64_t* bar) {
+    float* h = wsm + kRH;
+    bulk(h, hd.cls_convT, 96 * 96, bar);
+    bulk(h + 96 * 96, hd.reg_convT, 96 * 96, bar);
+    bulk(h + kHeadRp, hd.reg_predT, 96 * 4, bar);
+    bulk(h + kHeadOb, hd.obj_predT, 96, bar);
+    bulk(h + kHeadCp, hd.cls_predT, 96 * ncls, bar);
+    bulk(h + head_cb(ncls), hd.cls_conv_b, 96, bar);
+    bulk(h + head_cb(ncls) + 96, hd.reg_conv_b, 96, bar);
+    mbar_arrive(bar);
+}
+
+// Copies that wait for a buffer to be consumed, issued at point p: p = 3
+// when layers 0-3 are done (CTA 0) or at the start (other CTAs), p = l
+// after layer l's compute.  Layer 7's qvg block needs the layer 4/5 buffers
+// free, its rest and the head need the layer 6 (and 7) buffers free.
+struct Deferred {
+    bool q7, r7, head;
+};
+
+__device__ void issue_deferred(int p, Deferred& D, const Plan& P, int rank, const StepArgs& a, float* wsm,
+                               StepShared& sh) {
+    const bool u4 = cl_part(P, 4, rank), u5 = cl_part(P, 5, rank), u6 = cl_part(P, 6, rank),
+               u7 = cl_part(P, 7, rank);
+    if (!D.q7 && u7 && (!u4 || p >= 4) && (!u5 || p >= 5)) {
+        issue_cl(7, 1, P, rank, a, wsm, sh);
+        D.q7 = true;
+    }
+    if (!D.r7 && u7 && (!u6 || p >= 6)) {
+        issue_cl(7, 2, P, rank, a, wsm, sh);
+        D.r7 = true;
+    }
+    if (!D.head && rank == 0 && (P.flags & F_R4) && (!u6 || p >= 6) && (!u7 || p >= 7)) {
+        issue_head(a.head, a.g.ncls, wsm, &sh.bar_w[8]);
+        D.head = true;
+    }
+}
+
+// ---- LayerNorm (warp 0 of CTA 0) --------------------------------------------
+// y[t] = (sum over in-bounds positions d = A-1..0 of con[d][t]) + res[t];
+// x = LN(y) into sh.x, also sent to the CTAs of `bmask` (layer nl's input).
+// The two fp64 sums run sequentially in channel order on lane 0; the
+// deviations and the normalisation are per lane (layernorm.h:41-62).
+template <int OUT, int A>
+__device__ void gather_ln(StepShared& sh, const float* con, int cstride, unsigned inb, const float* gam,
+                          const float* bet, int nl, unsigned bmask) {
+    constexpr int KP = (OUT + 31) / 32;
+    const int lane = threadIdx.x;
+    float yv[KP];
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int t = lane + 32 * k;
+        if (t < OUT) {
+            float v = 0.0f;
+#pragma unroll
+            for (int d = A - 1; d >= 0; --d)
+                if ((inb >> d) & 1u) v = v + con[d * cstride + t];
+            yv[k] = v + sh.res[t];
+            sh.lnbuf[t] = static_cast<double>(yv[k]);
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        double sum = 0.0;
+#pragma unroll
+        for (int o = 0; o < OUT; ++o) sum += sh.lnbuf[o];
+        sh.ln_mean = sum / static_cast<double>(OUT);
+    }
+    __syncwarp();
+    const double mean = sh.ln_mean;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int t = lane + 32 * k;
+        if (t < OUT) {
+            const double dd = static_cast<double>(yv[k]) - mean;
+            sh.lnbuf[t] = dd * dd;
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        double var = 0.0;
+#pragma unroll
+        for (int o = 0; o < OUT; ++o) var += sh.lnbuf[o];
+        var /= static_cast<double>(OUT);
+        sh.ln_inv = 1.0 / sqrt(var + static_cast<double>(1e-5f));
+    }
+    __syncwarp();
+    const double inv = sh.ln_inv;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int t = lane + 32 * k;
+        if (t < OUT) {
+            const double tt = (static_cast<double>(yv[k]) - mean) * inv;
+            const float xv = static_cast<float>(tt * static_cast<double>(gam[t]) + static_cast<double>(bet[t]));
+            sh.x[t] = xv;
+            for (int r = 1; r < kStepCTAs; ++r)
+                if ((bmask >> r) & 1u) send(&sh.x[t], &sh.bar_x[nl], r, xv);
+        }
+    }
+}
+
+// ---- layers 0-3 (CTA 0) -----------------------------------------------------------
+// Every patch position: (position, column) items form q, v, sigmoid(g),
+// (position, channel) items update the cells and (position, output) items
+// form the goW contributions; warp 0 sums, adds the residual and
+// normalises.  Returns false when the layer is the event's last.
+template <int IN, int OUT, int A>
+__device__ bool small_layer(int l, const Plan& P, const StepArgs& a, StepShared& sh, float* b, unsigned bmask) {
     using Lo = Lay<IN, OUT, A>;
     constexpr int J2 = Lo::J2;
     const int tid = threadIdx.x;
     const int s = l / 2, half = l % 2;
-    const int Ws = a.g.W[s], Hs = a.g.H[s], cx0 = px >> s, cy0 = py >> s;
-    float* b = wsm + ((l & 1) ? kSmallOdd : 0);
+    const bool used = P.used[l];
+    const int Ws = a.g.W[s], Hs = a.g.H[s], cx0 = P.px >> s, cy0 = P.py >> s;
     const float* wq = b;
     const float* wg = b + Lo::WQ;
     const float* wi = b + Lo::WI;
@@ -174,21 +395,17 @@ __device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py,
     float* qvg = b + Lo::QV;
     float* qh = b + Lo::QH;
     float* con = b + Lo::CON;
-    async_wait();                                // this layer's copies (issued earlier)
-    __syncthreads();
-    next_issue();                                // the next layer's, into the other buffer
-    if (used) {
-        for (int t = tid; t < OUT; t += kStepNT) {
-            float acc;
-            if (half == 0) {
-                acc = 0.0f;
+    mbar_wait(&sh.bar_w[l], a.err, kErrWeights);
+    if (used && tid < OUT) {
+        float acc;
+        if (half == 0) {
+            acc = 0.0f;
 #pragma unroll
-                for (int i = 0; i < IN; ++i) acc = fmaf(wi[i * OUT + t], sh.x[i], acc);
-            } else {
-                acc = sh.x[t];
-            }
-            sh.res[t] = acc;
+            for (int i = 0; i < IN; ++i) acc = fmaf(wi[i * OUT + tid], sh.x[i], acc);
+        } else {
+            acc = sh.x[tid];
         }
+        sh.res[tid] = acc;
     }
     const int c0 = used ? 0 : OUT;
     for (int it = tid; it < A * (J2 - c0); it += kStepNT) {
@@ -205,130 +422,73 @@ __device__ bool small_layer(int l, bool used, const StepArgs& a, int px, int py,
     const int hd = tid / OUT, ht = tid % OUT;
     int hcx = 0, hcy = 0;
     const bool hact = tid < A * OUT && patch_cell(A, hd, cx0, cy0, Ws, Hs, hcx, hcy);
+    float h = 0.0f;
     if (hact) {
         const float* q = qvg + hd * J2;
-        const float h = fmaf(ssla_sigmoidf(q[2 * OUT + ht]), hr[hd * OUT + ht], q[OUT + ht]);
-        a.ps.hidden[l][(static_cast<size_t>(hcy) * Ws + hcx) * OUT + ht] = h;
+        h = fmaf(ssla_sigmoidf(q[2 * OUT + ht]), hr[hd * OUT + ht], q[OUT + ht]);
         if (used) qh[hd * OUT + ht] = q[ht] * h;
     }
+    if (used) {
+        __syncthreads();
+        if (hact) {
+            const float* w = wg + hd * OUT * OUT + ht;
+            const float* q = qh + hd * OUT;
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < OUT; ++i) acc = fmaf(w[i * OUT], q[i], acc);
+            con[hd * OUT + ht] = acc;
+        }
+    }
+    if (hact) a.ps.hidden[l][(static_cast<size_t>(hcy) * Ws + hcx) * OUT + ht] = h;
     if (!used) return false;                     // state-only second layer: the event ends
     __syncthreads();
-    if (hact) {
-        const float* w = wg + hd * OUT * OUT + ht;
-        const float* q = qh + hd * OUT;
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < OUT; ++i) acc = fmaf(w[i * OUT], q[i], acc);
-        con[hd * OUT + ht] = acc;
-    }
-    __syncthreads();
-    for (int t = tid; t < OUT; t += kStepNT) {
-        float v = 0.0f;
-#pragma unroll
-        for (int d = A - 1; d >= 0; --d) {
-            int cx, cy;
-            if (!patch_cell(A, d, cx0, cy0, Ws, Hs, cx, cy)) continue;
-            v = v + con[d * OUT + t];
-        }
-        sh.y[t] = v + sh.res[t];
-    }
-    __syncthreads();
-    step_ln(sh, OUT, b + Lo::GAM, b + Lo::BET);
-    __syncthreads();
-    return true;
-}
-
-// Layers 0-3 (layer 0's copies were issued at kernel start).  Leaves the
-// stage-2 input in sh.x when the event passes gate 1.
-__device__ void small_layers(const StepArgs& a, int flags, int px, int py, StepShared& sh, float* wsm) {
-    const bool r1 = (flags & F_R1) != 0, r2 = (flags & F_R2) != 0;
-    if (!small_layer<2, 12, 1>(0, true, a, px, py, sh, wsm,
-                               [&] { issue_small<12, 12, 9>(1, r1, a, px, py, wsm); }))
-        return;
-    if (!small_layer<12, 12, 9>(1, r1, a, px, py, sh, wsm,
-                                [&] { if (r1) issue_small<12, 24, 9>(2, true, a, px, py, wsm); }))
-        return;
-    if (!small_layer<12, 24, 9>(2, true, a, px, py, sh, wsm,
-                                [&] { issue_small<24, 24, 9>(3, r2, a, px, py, wsm); }))
-        return;
-    small_layer<24, 24, 9>(3, r2, a, px, py, sh, wsm, [] {});
-}
-
-// ---- layers 4-7 on the cluster ---------------------------------------------
-struct StepLayer {
-    int l, s, half, IN, OUT;
-    bool used;      // the layer output is consumed (else state-only, last layer)
-    bool act;       // this CTA's patch cell is in bounds
-    int cx, cy;     // this CTA's patch cell
-};
-
-__device__ __forceinline__ bool step_layer(int l, int flags, int px, int py, int rank, const Geo& g,
-                                           StepLayer& L) {
-    const int s = l / 2, half = l % 2;
-    if (s > 3 || s < 2) return false;
-    if (!(flags & (F_R1 << (s - 1)))) return false;
-    L.l = l;
-    L.s = s;
-    L.half = half;
-    L.OUT = chans(s);
-    L.IN = half == 0 ? chans(s - 1) : L.OUT;
-    L.used = half == 0 || (s < 3 ? (flags & (F_R1 << s)) != 0 : (flags & F_R4) != 0);
-    L.act = patch_cell(9, rank, px >> s, py >> s, g.W[s], g.H[s], L.cx, L.cy);
-    return true;
-}
-
-__device__ __forceinline__ float* layer_base(float* wsm, int l) { return wsm + (l == 4 ? kL4Base : 0); }
-
-// Offsets inside a layer-4..7 buffer (Lay<IN, OUT, 1> with runtime sizes).
-__device__ __forceinline__ int off_gam(int IN, int OUT) { return IN * 3 * OUT + OUT * OUT; }
-
-// Issues the copies a CTA needs for layer L: its patch position's weights
-// and state row; CTA 0 also gamma, beta and input_proj (first layers).
-__device__ void issue_layer(const StepLayer& L, const StepArgs& a, int rank, float* wsm) {
-    const int IN = L.IN, OUT = L.OUT, J2 = 3 * OUT;
-    const DevLayer& W = a.L[L.l];
-    float* b = layer_base(wsm, L.l);
-    const int gam = off_gam(IN, OUT);
-    if (L.act) {
-        stage_async(b, W.qvgT + static_cast<size_t>(rank) * IN * J2, IN * J2);
-        if (L.used) stage_async(b + IN * J2, W.goWT + static_cast<size_t>(rank) * OUT * OUT, OUT * OUT);
-        stage_async(b + gam + 2 * OUT,
-                    a.ps.hidden[L.l] + (static_cast<size_t>(L.cy) * a.g.W[L.s] + L.cx) * OUT, OUT);
-    }
-    if (rank == 0 && L.used) {
-        stage_async(b + gam, W.gamma, OUT);
-        stage_async(b + gam + OUT, W.beta, OUT);
-        if (L.half == 0) stage_async(b + gam + 3 * OUT, W.ipT, IN * OUT);
-    }
-    async_commit();
-}
-
-// One CTA's part of a layer 4-7: residual (CTA 0), q / v / sigmoid(g) of
-// its patch cell, the cell's state update and its goW contribution.
-template <int IN, int OUT>
-__device__ void cl_compute(const StepLayer& cur, bool rank0, const StepArgs& a, StepShared& sh,
-                           const float* b) {
-    constexpr int J2 = 3 * OUT;
-    constexpr int GAM = IN * J2 + OUT * OUT;
-    const int tid = threadIdx.x;
-    const bool used = cur.used;
-    const float* wq = b;
-    const float* wg = b + IN * J2;
-    const float* wi = b + GAM + 3 * OUT;
-    if (rank0 && used) {
-        for (int t = tid; t < OUT; t += kStepNT) {
-            float acc;
-            if (cur.half == 0) {
-                acc = 0.0f;
-#pragma unroll
-                for (int i = 0; i < IN; ++i) acc = fmaf(wi[i * OUT + t], sh.x[i], acc);
-            } else {
-                acc = sh.x[t];
+    if (tid < 32) {
+        unsigned inb = 1u;
+        if (A > 1) {
+            inb = 0;
+            for (int d = 0; d < A; ++d) {
+                int cx, cy;
+                if (patch_cell(A, d, cx0, cy0, Ws, Hs, cx, cy)) inb |= 1u << d;
             }
-            sh.res[t] = acc;
         }
+        gather_ln<OUT, A>(sh, con, OUT, inb, b + Lo::GAM, b + Lo::BET, l + 1, bmask);
     }
-    if (cur.act) {
+    __syncthreads();
+    return true;
+}
+
+// ---- layers 4-7 -----------------------------------------------------------------
+// One CTA's part: residual (CTA 0), q / v / sigmoid(g) of its patch cell,
+// the cell's state update and its goW contribution (kept by CTA 0, sent to
+// CTA 0 by the others).
+template <int IN, int OUT>
+__device__ void cl_layer(int l, const Plan& P, int rank, const StepArgs& a, StepShared& sh, float* wsm) {
+    constexpr int J2 = 3 * OUT;
+    const int tid = threadIdx.x;
+    const int s = l / 2;
+    const bool used = P.used[l];
+    const bool act = (P.inb[l] >> rank) & 1u;
+    const float* wq = cl_wq(wsm, l);
+    const float* rest = cl_rest(wsm, l);
+    const float* wg = rest;
+    const float* hr = rest + OUT * OUT + 2 * OUT;
+    const float* wi = rest + OUT * OUT + 3 * OUT;
+    if (rank != 0) mbar_wait(&sh.bar_x[l], a.err, kErrInput);
+    mbar_wait(&sh.bar_w[l], a.err, kErrWeights);
+    if (l == 7 && act) mbar_wait(&sh.bar_w[9], a.err, kErrWeights);
+    if (rank == 0 && used && tid < OUT) {
+        float acc;
+        if ((l & 1) == 0) {
+            acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < IN; ++i) acc = fmaf(wi[i * OUT + tid], sh.x[i], acc);
+        } else {
+            acc = sh.x[tid];
+        }
+        sh.res[tid] = acc;
+    }
+    if (rank == 0 && used && tid < 2 * OUT) sh.gb[tid] = rest[OUT * OUT + tid];
+    if (act) {
         for (int col = tid + (used ? 0 : OUT); col < J2; col += kStepNT) {
             float acc = 0.0f;
             const float* w = wq + col;
@@ -337,251 +497,248 @@ __device__ void cl_compute(const StepLayer& cur, bool rank0, const StepArgs& a, 
             sh.qvg[col] = acc;
         }
         __syncthreads();
+        float h = 0.0f;
         if (tid < OUT) {
-            const float h = fmaf(ssla_sigmoidf(sh.qvg[2 * OUT + tid]), b[GAM + 2 * OUT + tid], sh.qvg[OUT + tid]);
-            a.ps.hidden[cur.l][(static_cast<size_t>(cur.cy) * a.g.W[cur.s] + cur.cx) * OUT + tid] = h;
+            h = fmaf(ssla_sigmoidf(sh.qvg[2 * OUT + tid]), hr[tid], sh.qvg[OUT + tid]);
             if (used) sh.qh[tid] = sh.qvg[tid] * h;
         }
-        __syncthreads();
-        if (used && tid < OUT) {
-            float acc = 0.0f;
+        if (used) {
+            __syncthreads();
+            if (tid < OUT) {
+                float acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < OUT; ++i) acc = fmaf(wg[i * OUT + tid], sh.qh[i], acc);
-            sh.contrib[tid] = acc;
+                for (int i = 0; i < OUT; ++i) acc = fmaf(wg[i * OUT + tid], sh.qh[i], acc);
+                if (rank == 0) sh.con[0][tid] = acc;
+                else send(&sh.con[rank][tid], &sh.bar_c[l], 0, acc);
+            }
+        }
+        if (tid < OUT) {
+            int cx, cy;
+            patch_cell(9, rank, P.px >> s, P.py >> s, a.g.W[s], a.g.H[s], cx, cy);
+            a.ps.hidden[l][(static_cast<size_t>(cy) * a.g.W[s] + cx) * OUT + tid] = h;
         }
     }
-    if (rank0 && used) {
-        // gamma / beta aside: the next layer's copies may reuse this buffer
-        for (int t = tid; t < OUT; t += kStepNT) {
-            sh.gb[t] = b[GAM + t];
-            sh.gb[96 + t] = b[GAM + OUT + t];
-        }
+    __syncthreads();                   // buffers consumed; CTA 0: residual and own contribution visible
+}
+
+__device__ void run_cl(int l, const Plan& P, int rank, const StepArgs& a, StepShared& sh, float* wsm) {
+    switch (l) {
+        case 4: cl_layer<24, 48>(l, P, rank, a, sh, wsm); break;
+        case 5: cl_layer<48, 48>(l, P, rank, a, sh, wsm); break;
+        case 6: cl_layer<48, 96>(l, P, rank, a, sh, wsm); break;
+        default: cl_layer<96, 96>(l, P, rank, a, sh, wsm); break;
     }
 }
 
-// ---- head (CTA 0) ------------------------------------------------------------
-// cls conv | reg conv [96][96], reg pred [96][4], obj pred [96], cls pred
-// [96][ncls], cls | reg conv biases [96] each.
-constexpr int kHeadRp = 2 * 96 * 96, kHeadOb = kHeadRp + 96 * 4, kHeadCp = kHeadOb + 96;
-__device__ __forceinline__ int head_cb(int ncls) { return kHeadCp + ((96 * ncls + 3) & ~3); }
-
-__device__ void issue_head(const DevHead& hd, int ncls, float* wsm) {
-    stage_async(wsm, hd.cls_convT, 96 * 96);
-    stage_async(wsm + 96 * 96, hd.reg_convT, 96 * 96);
-    stage_async(wsm + kHeadRp, hd.reg_predT, 96 * 4);
-    stage_async(wsm + kHeadOb, hd.obj_predT, 96);
-    stage_async(wsm + kHeadCp, hd.cls_predT, 96 * ncls);
-    stage_async(wsm + head_cb(ncls), hd.cls_conv_b, 96);
-    stage_async(wsm + head_cb(ncls) + 96, hd.reg_conv_b, 96);
-    async_commit();
+// CTA 0 after layer l's compute: the gathered, normalised output, sent on as
+// layer l+1's input.
+__device__ void cl_gather(int l, const Plan& P, const StepArgs& a, StepShared& sh, float* wsm) {
+    if (threadIdx.x < 32) {
+        mbar_wait(&sh.bar_c[l], a.err, kErrContrib);
+        const unsigned bmask = (l < 7 && P.runs[l + 1]) ? (P.inb[l + 1] & ~1u) : 0u;
+        if (cl_out(l) == 48) gather_ln<48, 9>(sh, &sh.con[0][0], 96, P.inb[l], sh.gb, sh.gb + 48, l + 1, bmask);
+        else gather_ln<96, 9>(sh, &sh.con[0][0], 96, P.inb[l], sh.gb, sh.gb + 96, l + 1, bmask);
+    }
+    __syncthreads();
 }
 
-__global__ void __launch_bounds__(kStepNT) k_step(StepArgs a) {
-    cg::cluster_group cluster = cg::this_cluster();
-    const int rank = static_cast<int>(cluster.block_rank());
+// ---- head and commit (CTA 0) -----------------------------------------------------
+// async_yolox.h:203-254: cls / reg convs with SiLU, then the 2 + 4 + 1
+// predictions; decoded row written to the owned cell, raw row beside it.
+__device__ void run_head(const Plan& P, const StepArgs& a, StepShared& sh, float* wsm, float pbias) {
     const int tid = threadIdx.x;
-    __shared__ StepShared sh;
-    extern __shared__ __align__(16) float wsm[];
-    StepShared* sh0 = cluster.map_shared_rank(&sh, 0);
+    const Geo& g = a.g;
+    const PartState& ps = a.ps;
+    const int ncls = g.ncls, cols = 5 + ncls;
+    mbar_wait(&sh.bar_w[8], a.err, kErrWeights);
+    const float* h = wsm + kRH;
+    float* act = &sh.con[0][0];
+    if (tid < 192) {
+        const int jo = tid % 96;
+        const float* Wt = h + (tid < 96 ? 0 : 96 * 96) + jo;
+        float acc = h[head_cb(ncls) + tid];
+#pragma unroll
+        for (int i = 0; i < 96; ++i) acc = fmaf(Wt[i * 96], sh.x[i], acc);
+        act[tid] = acc * ssla_sigmoidf(acc);
+    }
+    __syncthreads();
+    float v = 0.0f;
+    if (tid < cols) {
+        float acc = pbias;
+        if (tid < 4) {
+            const float* w = h + kHeadRp + tid;
+#pragma unroll
+            for (int i = 0; i < 96; ++i) acc = fmaf(w[i * 4], act[96 + i], acc);
+        } else if (tid == 4) {
+            const float* w = h + kHeadOb;
+#pragma unroll
+            for (int i = 0; i < 96; ++i) acc = fmaf(w[i], act[96 + i], acc);
+        } else {
+            const float* w = h + kHeadCp + (tid - 5);
+#pragma unroll 16
+            for (int i = 0; i < 96; ++i) acc = fmaf(w[i * ncls], act[i], acc);
+        }
+        v = acc;
+    }
+    const int c3x = P.px >> 3, c3y = P.py >> 3;
+    const int x2 = P.px >> 2, y2 = P.py >> 2;
+    const bool own = x2 >= ps.own_x0 && x2 < ps.own_x1 && y2 >= ps.own_y0 && y2 < ps.own_y1;
+    const int cell = c3y * g.W[3] + c3x;
+    if (tid < cols) {
+        const int r = tid;
+        float dv;
+        if (r == 0) dv = (v + static_cast<float>(c3x)) * static_cast<float>(g.stride_w);
+        else if (r == 1) dv = (v + static_cast<float>(c3y)) * static_cast<float>(g.stride_h);
+        else if (r == 2) dv = ssla_expf(v) * static_cast<float>(g.stride_w);
+        else if (r == 3) dv = ssla_expf(v) * static_cast<float>(g.stride_h);
+        else dv = v;
+        if (a.pred_out) a.pred_out[r] = dv;
+        if (own) {
+            ps.preds_dec[static_cast<size_t>(cell) * cols + r] = dv;
+            ps.preds_raw[static_cast<size_t>(cell) * cols + r] = v;
+        }
+    }
+    if (own && tid == 0) ps.version[cell] += 1u;
+}
+
+__global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
+    __shared__ __align__(16) StepShared sh;
+    extern __shared__ __align__(128) float wsm[];
+    const int rank = static_cast<int>(cta_rank());
+    const int tid = threadIdx.x;
     const PartState& ps = a.ps;
     const Geo& g = a.g;
     const bool hyb = g.layout == LAYOUT_HYBRID;
 
-    // ---- preprocess + gates (CTA 0): inputs loaded in parallel, decided by
-    // one thread in gate order (each counter advances at most once) ----
-    if (rank == 0) {
-        const float4 e = a.ev;
-        const bool valid = e.y > -1.0f && e.y < static_cast<float>(g.W[0]) && e.z > -1.0f &&
-                           e.z < static_cast<float>(g.H[0]);
-        const int x = valid ? static_cast<int>(e.y) : 0, y = valid ? static_cast<int>(e.z) : 0;
-        const int k0 = (y >> 1) * g.W[1] + (x >> 1), k1 = (y >> 2) * g.W[2] + (x >> 2);
-        const int k2 = hyb ? k1 : (y >> 3) * g.W[3] + (x >> 3), k3 = (y >> 3) * g.W[3] + (x >> 3);
-        if (valid) {
-            issue_small<2, 12, 1>(0, true, a, x, y, wsm);       // layer 0, needed by any valid event
-            if (tid == 0) sh.lt_prev = ps.last_t[y * g.W[0] + x];
-            else if (tid == 1) sh.cnt_in[0] = ps.cnt[0][k0];
-            else if (tid == 2) sh.cnt_in[1] = ps.cnt[1][k1];
-            else if (tid == 3) sh.cnt_in[2] = ps.cnt[2][k2];
-            else if (tid == 4 && hyb) sh.cnt_in[3] = ps.cnt[3][k3];
+    // ---- gate inputs (every CTA), preprocess inputs and head biases (CTA 0) ----
+    const float4 e = a.ev;
+    const bool valid = e.y > -1.0f && e.y < static_cast<float>(g.W[0]) && e.z > -1.0f &&
+                       e.z < static_cast<float>(g.H[0]);
+    const int px = valid ? static_cast<int>(e.y) : 0, py = valid ? static_cast<int>(e.z) : 0;
+    const int k0 = (py >> 1) * g.W[1] + (px >> 1), k1 = (py >> 2) * g.W[2] + (px >> 2);
+    const int k2 = hyb ? k1 : (py >> 3) * g.W[3] + (px >> 3), k3 = (py >> 3) * g.W[3] + (px >> 3);
+    int c[4] = {0, 0, 0, 0};
+    if (valid) {
+        c[0] = ps.cnt[0][k0];
+        c[1] = ps.cnt[1][k1];
+        c[2] = ps.cnt[2][k2];
+        if (hyb) c[3] = ps.cnt[3][k3];
+    }
+    double lt_prev = 0.0;
+    if (rank == 0 && tid == 0 && valid) lt_prev = ps.last_t[py * g.W[0] + px];
+    float pbias = 0.0f;
+    if (rank == 0 && tid < 5 + g.ncls)
+        pbias = tid < 4 ? __ldg(a.head.reg_pred_b + tid)
+                        : tid == 4 ? __ldg(a.head.obj_pred_b) : __ldg(a.head.cls_pred_b + (tid - 5));
+    int flags = 0;
+    if (valid) {
+        const int w = g.window;
+        flags = F_VALID;
+        if (step_gate(c[0], w)) {
+            flags |= F_R1;
+            if (step_gate(c[1], w)) {
+                flags |= F_R2;
+                if (step_gate(c[2], w)) {
+                    flags |= F_R3;
+                    if (!hyb || step_gate(c[3], w)) flags |= F_R4;
+                }
+            }
         }
-        __syncthreads();
-        if (tid == 0) {
-            int flags = 0;
-            if (valid) {
-                const double prev = sh.lt_prev;
+    }
+    Plan P;
+    make_plan(P, flags, px, py, g);
+
+    // ---- barriers, expected messages, first copies ----
+    if (tid == 0) {
+        for (int i = 0; i < 10; ++i) mbar_init(&sh.bar_w[i]);
+        for (int i = 0; i < 8; ++i) {
+            mbar_init(&sh.bar_x[i]);
+            mbar_init(&sh.bar_c[i]);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int l = 4; l < 8; ++l) {
+            if (rank != 0 && P.runs[l] && ((P.inb[l] >> rank) & 1u)) mbar_arrive_tx(&sh.bar_x[l], 4u * cl_in(l));
+            if (rank == 0 && P.used[l])
+                mbar_arrive_tx(&sh.bar_c[l], 4u * cl_out(l) * __popc(P.inb[l] & ~1u));
+        }
+    }
+    __syncthreads();
+    Deferred D{false, false, false};
+    if (tid == kIssuer) {
+        if (rank == 0) {
+            if (P.runs[0]) issue_small<2, 12, 1>(0, P, a, wsm, &sh.bar_w[0]);
+            if (P.runs[1]) issue_small<12, 12, 9>(1, P, a, wsm + kS1, &sh.bar_w[1]);
+            if (P.runs[2]) issue_small<12, 24, 9>(2, P, a, wsm + kS2, &sh.bar_w[2]);
+            if (P.runs[3]) issue_small<24, 24, 9>(3, P, a, wsm + kS3, &sh.bar_w[3]);
+            if (cl_part(P, 4, 0)) issue_cl(4, 3, P, 0, a, wsm, sh);
+        } else {
+            for (int l = 4; l < 7; ++l)
+                if (cl_part(P, l, rank)) issue_cl(l, 3, P, rank, a, wsm, sh);
+            issue_deferred(3, D, P, rank, a, wsm, sh);
+        }
+    }
+    cluster_arrive();                  // every CTA has read the counters and set up its barriers
+
+    if (rank == 0) {
+        if (valid) {
+            if (tid == 0) {
                 float dt;
-                if (prev < 0.0) {
+                if (lt_prev < 0.0) {
                     dt = 1.0f;
                 } else {
-                    double v = (static_cast<double>(e.x) - prev) / 1e5;
+                    double v = (static_cast<double>(e.x) - lt_prev) / 1e5;
                     if (v < 0.0) v = 0.0;
                     if (v > 1.0) v = 1.0;
                     dt = static_cast<float>(v);
                 }
-                ps.last_t[y * g.W[0] + x] = static_cast<double>(e.x);
-                flags = F_VALID;
-                const int w = g.window;
-                ps.cnt[0][k0] = static_cast<uint8_t>(sh.cnt_in[0] + 1);
-                if (step_gate(sh.cnt_in[0], w)) {
-                    flags |= F_R1;
-                    ps.cnt[1][k1] = static_cast<uint8_t>(sh.cnt_in[1] + 1);
-                    if (step_gate(sh.cnt_in[1], w)) {
-                        flags |= F_R2;
-                        ps.cnt[2][k2] = static_cast<uint8_t>(sh.cnt_in[2] + 1);
-                        if (step_gate(sh.cnt_in[2], w)) {
-                            flags |= F_R3;
-                            bool pass3 = true;
-                            if (hyb) {
-                                ps.cnt[3][k3] = static_cast<uint8_t>(sh.cnt_in[3] + 1);
-                                pass3 = step_gate(sh.cnt_in[3], w);
-                            }
-                            if (pass3) flags |= F_R4;
-                        }
-                    }
-                }
-                sh.px = x;
-                sh.py = y;
                 sh.x[0] = dt;
                 sh.x[1] = e.w;
             }
-            sh.flags = flags;
-            if (a.flag_out) *a.flag_out = static_cast<uint8_t>(flags);
+            __syncthreads();
+            small_layer<2, 12, 1>(0, P, a, sh, wsm, 0u);
         }
+        cluster_wait();
+        if (valid && tid == 0) {       // the counters may change now that every CTA has read them
+            ps.last_t[py * g.W[0] + px] = static_cast<double>(e.x);
+            ps.cnt[0][k0] = static_cast<uint8_t>(c[0] + 1);
+            if (flags & F_R1) ps.cnt[1][k1] = static_cast<uint8_t>(c[1] + 1);
+            if (flags & F_R2) ps.cnt[2][k2] = static_cast<uint8_t>(c[2] + 1);
+            if (hyb && (flags & F_R3)) ps.cnt[3][k3] = static_cast<uint8_t>(c[3] + 1);
+        }
+        if (P.runs[1] && small_layer<12, 12, 9>(1, P, a, sh, wsm + kS1, 0u) &&
+            small_layer<12, 24, 9>(2, P, a, sh, wsm + kS2, 0u)) {
+            const unsigned b4 = P.runs[4] ? (P.inb[4] & ~1u) : 0u;
+            if (small_layer<24, 24, 9>(3, P, a, sh, wsm + kS3, b4) && tid == kIssuer) {
+                // layers 0-3 are done: their buffers take layers 5 and 6
+                for (int l = 5; l < 7; ++l)
+                    if (cl_part(P, l, 0)) issue_cl(l, 3, P, 0, a, wsm, sh);
+                issue_deferred(3, D, P, 0, a, wsm, sh);
+            }
+        }
+    } else {
+        cluster_wait();
     }
-    cluster.sync();
-    const int flags = sh0->flags;
-    const int px = sh0->px, py = sh0->py;
 
-    if (flags & F_VALID) {
-        // layer-4 copies of every CTA land while CTA 0 runs layers 0-3
-        StepLayer cur;
-        bool have = step_layer(4, flags, px, py, rank, g, cur);
-        if (have) issue_layer(cur, a, rank, wsm);
-        if (rank == 0) small_layers(a, flags, px, py, sh, wsm);
-        cluster.sync();                    // stage-2 input ready in CTA 0
-        bool head_issued = false;
-        while (have) {
-            const int OUT = cur.OUT;
-            const int s = cur.s;
-            const int Ws = g.W[s], Hs = g.H[s];
-            const int cx0 = px >> s, cy0 = py >> s;
-            const float* b = layer_base(wsm, cur.l);
-            if (rank != 0)
-                for (int t = tid; t < cur.IN; t += kStepNT) sh.x[t] = sh0->x[t];
-            async_wait();
-            __syncthreads();
-            switch (cur.l) {
-                case 4: cl_compute<24, 48>(cur, rank == 0, a, sh, b); break;
-                case 5: cl_compute<48, 48>(cur, rank == 0, a, sh, b); break;
-                case 6: cl_compute<48, 96>(cur, rank == 0, a, sh, b); break;
-                default: cl_compute<96, 96>(cur, rank == 0, a, sh, b); break;
-            }
-            __syncthreads();               // this layer's weights are consumed
-            if (!cur.used) break;          // state-only second layer: the event ends here
-            StepLayer nxt;
-            have = step_layer(cur.l + 1, flags, px, py, rank, g, nxt);
-            if (have) {
-                issue_layer(nxt, a, rank, wsm);   // lands during the gather / LayerNorm below
-            } else if (rank == 0 && (flags & F_R4)) {
-                issue_head(a.head, g.ncls, wsm);
-                head_issued = true;
-            }
-            cluster.sync();                // contributions ready, inputs copied
-            if (rank == 0) {
-                for (int t = tid; t < OUT; t += kStepNT) {
-                    float c[9];
-#pragma unroll
-                    for (int dd = 0; dd < 9; ++dd) {          // all remote loads in flight
-                        const int ccx = cx0 + 1 - dd % 3, ccy = cy0 + 1 - dd / 3;
-                        const bool in = ccx >= 0 && ccx < Ws && ccy >= 0 && ccy < Hs;
-                        c[dd] = in ? cluster.map_shared_rank(&sh, dd)->contrib[t] : 0.0f;
-                    }
-                    float v = 0.0f;
-#pragma unroll
-                    for (int dd = 8; dd >= 0; --dd) {
-                        const int ccx = cx0 + 1 - dd % 3, ccy = cy0 + 1 - dd / 3;
-                        if (ccx < 0 || ccx >= Ws || ccy < 0 || ccy >= Hs) continue;
-                        v = v + c[dd];
-                    }
-                    sh.y[t] = v + sh.res[t];
-                }
-                __syncthreads();
-                step_ln(sh, OUT, sh.gb, sh.gb + 96);
-            }
-            cluster.sync();                // next input ready in CTA 0
-            cur = nxt;
-        }
-        async_wait();
-        __syncthreads();
-        // ---- head and commit (CTA 0) ----
-        if (rank == 0 && (flags & F_R4)) {
-            const DevHead& hd = a.head;
-            const int ncls = g.ncls;
-            if (!head_issued) issue_head(hd, ncls, wsm);
-            const float obj_b = __ldg(hd.obj_pred_b);
-            async_wait();
-            __syncthreads();
-            const float* wc = wsm;
-            const float* wr = wsm + 96 * 96;
-            const float* wrp = wsm + kHeadRp;
-            const float* wob = wsm + kHeadOb;
-            const float* wcp = wsm + kHeadCp;
-            const float* cb = wsm + head_cb(ncls);
-            for (int j = tid; j < 192; j += kStepNT) {
-                const int jo = j % 96;
-                const float* Wt = (j < 96) ? wc : wr;
-                float acc = cb[j];
-#pragma unroll 8
-                for (int i = 0; i < 96; ++i) acc = fmaf(Wt[i * 96 + jo], sh.x[i], acc);
-                sh.act[j] = acc * ssla_sigmoidf(acc);
-            }
-            __syncthreads();
-            const int cols = 5 + ncls;
-            for (int r = tid; r < cols; r += kStepNT) {
-                float acc;
-                if (r < 4) {
-                    acc = __ldg(hd.reg_pred_b + r);
-                    for (int i = 0; i < 96; ++i) acc = fmaf(wrp[i * 4 + r], sh.act[96 + i], acc);
-                } else if (r == 4) {
-                    acc = obj_b;
-                    for (int i = 0; i < 96; ++i) acc = fmaf(wob[i], sh.act[96 + i], acc);
-                } else {
-                    const int c = r - 5;
-                    acc = __ldg(hd.cls_pred_b + c);
-                    for (int i = 0; i < 96; ++i) acc = fmaf(wcp[i * ncls + c], sh.act[i], acc);
-                }
-                sh.hrow[r] = acc;
-            }
-            __syncthreads();
-            const int c3x = px >> 3, c3y = py >> 3;
-            const int x2 = px >> 2, y2 = py >> 2;
-            const bool own = x2 >= ps.own_x0 && x2 < ps.own_x1 && y2 >= ps.own_y0 && y2 < ps.own_y1;
-            const int cell = c3y * g.W[3] + c3x;
-            for (int r = tid; r < cols; r += kStepNT) {
-                const float v = sh.hrow[r];
-                float dv;
-                if (r == 0) dv = (v + static_cast<float>(c3x)) * static_cast<float>(g.stride_w);
-                else if (r == 1) dv = (v + static_cast<float>(c3y)) * static_cast<float>(g.stride_h);
-                else if (r == 2) dv = ssla_expf(v) * static_cast<float>(g.stride_w);
-                else if (r == 3) dv = ssla_expf(v) * static_cast<float>(g.stride_h);
-                else dv = v;
-                if (own) {
-                    ps.preds_dec[static_cast<size_t>(cell) * cols + r] = dv;
-                    ps.preds_raw[static_cast<size_t>(cell) * cols + r] = v;
-                }
-                if (a.pred_out) a.pred_out[r] = dv;
-            }
-            if (own && tid == 0) ps.version[cell] += 1u;
-        }
+    // ---- layers 4-7 ----
+    for (int l = 4; l < 8; ++l) {
+        if (!P.runs[l]) break;
+        if (cl_part(P, l, rank)) run_cl(l, P, rank, a, sh, wsm);
+        if (tid == kIssuer) issue_deferred(l, D, P, rank, a, wsm, sh);
+        if (!P.used[l]) break;         // state-only second layer: the event ends here
+        if (rank == 0) cl_gather(l, P, a, sh, wsm);
     }
-    async_wait();                          // no copy in flight at exit
-    cluster.sync();                        // no CTA leaves while its smem may be read
+
+    if (rank == 0) {
+        if (P.flags & F_R4) run_head(P, a, sh, wsm, pbias);
+        if (tid == 0 && a.flag_out) *a.flag_out = static_cast<uint8_t>(flags);
+    }
 }
 
 }  // namespace
 
 cudaError_t launch_step(cudaStream_t st, const StepArgs& a) {
-    constexpr size_t smem = sizeof(float) * kSmem;
+    constexpr size_t smem = sizeof(float) * kDyn;
+    if (head_floats(a.g.ncls) > kDyn) return cudaErrorInvalidValue;
     // function attributes are per device: set once for each device used
     static std::atomic<unsigned long long> attr_done{0};
     int dev = 0;
