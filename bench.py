@@ -301,6 +301,142 @@ def config_dict() -> dict:
             "parallelism": "per-GPU independent partitions"}
 
 
+# ---------------------------------------------------------------------------
+# Config 3: 320x256 sensor, horizontal strips with a halo, one strip per GPU
+# ---------------------------------------------------------------------------
+STRIP_EVENTS = 10_000_000
+STRIP_H, STRIP_W = 256, 320
+STRIP_CHUNK = 1 << 20
+
+
+def run_strips(args, rank: int, world: int, local: int) -> int:
+    """Strong scaling: the one 10M-event stream of config 3 split into `world`
+    horizontal strips (ssla_rt_b200/strips.py); each rank drains its strip
+    plus halo, in stream order, in chunks of STRIP_CHUNK events; value = the
+    stream's events / the slowest rank's device time."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from ssla_rt_b200 import abi, events, strips, stub
+    from ssla_rt_b200.engine import SslaEngine
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    wdir = tempfile.mkdtemp(prefix="ssla_stub_")
+    stub.write_stub(wdir, h=STRIP_H, w=STRIP_W, seed=1, tdrop=4)
+    ev_all = events.config_events(3)
+    span = float(ev_all[:, 0].max()) + 1.0
+    (lo, hi), sev, own = strips.shard(ev_all, STRIP_H, world, args.halo_rows)[rank]
+    del ev_all
+    n = len(sev)
+    eng = SslaEngine(wdir, n_partitions=1, max_events=STRIP_CHUNK, layout=abi.LAYOUT_HYBRID, device=local)
+    eng.set_owned(0, *strips.owned_s2(lo, hi, STRIP_W))
+    ev = torch.from_numpy(sev).to(dev)
+    chunks = [(c, min(c + STRIP_CHUNK, n)) for c in range(0, n, STRIP_CHUNK)]
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def one_pass():
+        for c0, c1 in chunks:
+            eng.drain(ev[c0:c1], [0, c1 - c0], stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        ev[:, 0] += span
+        one_pass()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler()
+    clocks.start()
+    time.sleep(0.3)
+    launches = 0
+    total_ms = 0.0
+    barrier()
+    torch.cuda.synchronize(dev)
+    for _ in range(args.steps):
+        ev[:, 0] += span
+        flush.fill_(1.0)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        one_pass()
+        b.record(stream)
+        b.synchronize()
+        total_ms += a.elapsed_time(b)
+        launches += eng.info().launches * len(chunks)
+    barrier()
+    clk = clocks.stop(local)
+    my_ms = total_ms
+    total_ms = max_over_ranks(total_ms)
+    value = STRIP_EVENTS * args.steps / (total_ms * 1e-3) / 1e6
+
+    # e2e: pinned host events copied in per chunk, flags copied out
+    host = torch.from_numpy(sev).pin_memory().numpy()
+    host_flags = torch.empty(STRIP_CHUNK, dtype=torch.uint8).pin_memory().numpy()
+    host[:, 0] += span * (args.warmup + args.steps + 1)
+    barrier()
+    e2e_s = 0.0
+    for _ in range(args.steps):
+        host[:, 0] += span
+        flush.fill_(2.0)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for c0, c1 in chunks:
+            eng.drain_host(host[c0:c1], [0, c1 - c0], host_flags[: c1 - c0], stream=stream)
+        preds = eng.preds_dec(0)
+        e2e_s += time.perf_counter() - t0
+    e2e_s = max_over_ranks(e2e_s)
+    e2e = STRIP_EVENTS * args.steps / e2e_s / 1e6
+
+    routed = torch.tensor([n, int(own.sum())], dtype=torch.int64, device=dev)
+    per_rank = [routed.clone() for _ in range(world)]
+    rank_ms = torch.tensor([my_ms], dtype=torch.float64, device=dev)
+    all_ms = [rank_ms.clone() for _ in range(world)]
+    if world > 1:
+        dist.all_gather(per_rank, routed)
+        dist.all_gather(all_ms, rank_ms)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "Mev/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"config3: 10,000,000 events at 320x256 (70% from 16 moving Gaussian blobs "
+                                   f"sigma 4, 30% uniform, Poisson 20 Mev/s) in {world} horizontal strip(s) with "
+                                   f"a {args.halo_rows}-row halo, one strip per GPU, full s0..s3 + YOLOX head",
+                       "model": "SSLA-S stub (320x256, seed 1, tdrop 4)", "events_per_step": STRIP_EVENTS,
+                       "chunk_events": STRIP_CHUNK, "halo_rows": args.halo_rows,
+                       "l2": "flushed between steps (256 MiB write, untimed); inputs 160 MB > L2",
+                       "parallelism": f"strips{world} (halo replication, no collective on the data path)"},
+            "strips": {"bounds": strips.strip_bounds(STRIP_H, world),
+                       "routed_events": [int(x[0]) for x in per_rank],
+                       "owned_events": [int(x[1]) for x in per_rank],
+                       "rank_ms": [float(x.item()) / args.steps for x in all_ms]},
+            "clocks": clk,
+            "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(sev.nbytes),
+                    "d2h_bytes_per_step": int(n + preds.nbytes)},
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -309,6 +445,10 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true", help="skip the batch-of-1 latency samples")
+    ap.add_argument("--workload", default="config1", choices=["config1", "strips"],
+                    help="config1: 80x64 partitions per GPU (weak scaling); strips: config 3, one "
+                         "320x256 stream in horizontal strips across the GPUs (strong scaling)")
+    ap.add_argument("--halo-rows", type=int, default=16, help="strips: halo in stage-0 rows (multiple of 8)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -317,6 +457,8 @@ def main() -> int:
     if args.impl == "reference":
         run_reference(args, rank)
         return 0
+    if args.workload == "strips":
+        return run_strips(args, rank, world, local)
 
     import torch
     import torch.distributed as dist

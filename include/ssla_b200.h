@@ -142,6 +142,56 @@ int  ssla_engine_step(SslaEngine* eng, int partition, const float* event,
 int  ssla_engine_step_latency(SslaEngine* eng, int partition, const float* events_host,
                               int n, double* latency_us, uint8_t* flags_out);
 
+/* Live loop: a resident cluster that takes raw events from a ring in pinned
+ * host memory (openeva::Event rows, the SPSC head / tail protocol of
+ * include/spsc.h:9-11 and orin/orin/ring.py:34-152) and runs each through
+ * preprocess, the gates, stages 0-3 and the head, in ring order, one event
+ * at a time -- the full-pipeline counterpart of the reference's polling
+ * kernel k_ssla_s2s3_celled_persistent_multi (ssla_s2_s3_head_celled.cuh:
+ * 1547-1784) with its tails / events_done / stop_flag words
+ * (orin/hybrid_runner_multi.py:445-462).  Every pointer is pinned host
+ * memory (cudaHostAlloc / cudaMallocHost / torch pin_memory). */
+typedef struct SslaLiveRing {
+    const float* events;             /* [capacity][4] t, x, y, p, written by the host          */
+    unsigned long long capacity;     /* power of two                                           */
+    unsigned long long* head;        /* events published: host release-stores after the slots  */
+    unsigned long long* tail;        /* events taken from the ring (device)                    */
+    unsigned long long* events_done; /* events finished, outputs and state visible (device)    */
+    uint8_t* flags;                  /* [capacity] SSLA_F_* bits of each event, or NULL        */
+    float* preds;                    /* [capacity][5+ncls] decoded row of head events, or NULL */
+    int* stop_flag;                  /* host sets non-zero to end the loop                      */
+} SslaLiveRing;
+
+/* Status bits of a live loop (ssla_engine_live_join). */
+enum {
+    SSLA_LIVE_ERR_WEIGHTS = 1,   /* a weight copy did not complete in time        */
+    SSLA_LIVE_ERR_INPUT = 2,     /* a layer input message did not arrive          */
+    SSLA_LIVE_ERR_CONTRIB = 4,   /* contributions did not arrive                  */
+    SSLA_LIVE_ERR_EVENT = 8,     /* no event message within the idle bound        */
+    SSLA_LIVE_ERR_DONE = 16,     /* an event's completion did not arrive          */
+    SSLA_LIVE_EXIT_STOP = 0x100, /* left the loop on the stop flag                */
+    SSLA_LIVE_EXIT_IDLE = 0x200  /* left the loop after idle_timeout_ms           */
+};
+
+/* Launches the live loop of `partition` on `stream` and returns; events
+ * are taken from index *ring->tail on.  The loop ends when *stop_flag is
+ * non-zero or after idle_timeout_ms without a new event.  The partition's
+ * state belongs to the loop until ssla_engine_live_join returns. */
+int  ssla_engine_live_start(SslaEngine* eng, int partition, const SslaLiveRing* ring,
+                            unsigned idle_timeout_ms, void* stream);
+/* Waits for the loop to end; *status (may be NULL) receives SSLA_LIVE_*
+ * bits.  Returns SSLA_ERR_CUDA if a wait inside the loop ran out. */
+int  ssla_engine_live_join(SslaEngine* eng, unsigned* status);
+
+/* Batch-of-1 latency through the live loop: publishes the n events (host
+ * array of 4-float rows) one at a time into a pinned ring and records, per
+ * event, the host time from publishing the event to observing
+ * events_done pass it (microseconds).  flags_out (may be NULL) receives
+ * each event's SSLA_F_* bits and preds_out (may be NULL, n x (5+ncls))
+ * each head event's decoded row (other rows untouched). */
+int  ssla_engine_live_latency(SslaEngine* eng, int partition, const float* events_host, int n,
+                              double* latency_us, uint8_t* flags_out, float* preds_out);
+
 /* Stages 0-1 only (HYBRID layout): preprocess, gates 0-1, layers 0-3 for
  * every event (state of stages 0-1 advances), and one HybridInputRec per
  * event that passed gate 1 -- t, stage-2 x / y, feat1 = the stage-1 output;
@@ -155,6 +205,14 @@ int  ssla_engine_drain_records(SslaEngine* eng, const float* events_dev,
                                const int* part_offsets, void* records_dev,
                                int records_cap, int* record_offsets,
                                uint8_t* flags_dev, void* stream);
+
+/* Owned range of `partition` in stage-2 cells, [x0, x1) x [y0, y1) (default:
+ * the whole grid).  Events outside it still update state (halo) but commit
+ * no prediction -- the owned_lo / owned_hi / owned_y_lo / owned_y_hi bounds
+ * of the reference's HybridStrip (ssla_s2_s3_head_celled.cuh:84-127,
+ * :1663-1670) for strip-sharded sensors.  Synchronises `stream`. */
+int  ssla_engine_set_owned(SslaEngine* eng, int partition, int x0, int x1, int y0, int y1,
+                           void* stream);
 
 int  ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes);
 int  ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index,

@@ -73,6 +73,18 @@ class SslaEngineInfo(C.Structure):
                 ("launches", C.c_int), ("_pad", C.c_int)]
 
 
+class SslaLiveRing(C.Structure):
+    """include/ssla_b200.h SslaLiveRing: every pointer pinned host memory."""
+    _fields_ = [("events", C.c_void_p), ("capacity", C.c_uint64), ("head", C.c_void_p),
+                ("tail", C.c_void_p), ("events_done", C.c_void_p), ("flags", C.c_void_p),
+                ("preds", C.c_void_p), ("stop_flag", C.c_void_p)]
+
+
+# SSLA_LIVE_* status bits
+LIVE_ERR_WEIGHTS, LIVE_ERR_INPUT, LIVE_ERR_CONTRIB, LIVE_ERR_EVENT, LIVE_ERR_DONE = 1, 2, 4, 8, 16
+LIVE_EXIT_STOP, LIVE_EXIT_IDLE = 0x100, 0x200
+
+
 class SslaPhaseTime(C.Structure):
     _fields_ = [("name", C.c_char * 40), ("ms", C.c_float), ("launches", C.c_int)]
 
@@ -92,6 +104,8 @@ EXPORTED = (
     "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak",
     "ssla_expf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
     "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
+    "ssla_engine_live_start", "ssla_engine_live_join", "ssla_engine_live_latency",
+    "ssla_engine_set_owned",
 )
 # Every symbol include/stage01_to_gpu.h declares (the libstage01_to_gpu ABI).
 S01G_EXPORTED = (

@@ -373,6 +373,10 @@ struct Engine {
     // Status word of the step kernel (host-mapped): bits of bounded waits
     // that ran out, read and cleared by the next step call.
     unsigned* step_err = nullptr;
+    // Live loop: status word (host-mapped) and the stream it runs on.
+    unsigned* live_err = nullptr;
+    cudaStream_t live_stream = nullptr;
+    bool live_running = false;
     cudaEvent_t off_done[kOffSlots] = {};
     int off_slot = 0;
     long long last_counts[5] = {0};
@@ -383,7 +387,9 @@ struct Engine {
             if (e) cudaEventDestroy(e);
         if (pinned_off) cudaFreeHost(pinned_off);
         if (pinned_rec_off) cudaFreeHost(pinned_rec_off);
+        if (live_running) cudaStreamSynchronize(live_stream);   // ends on its stop flag or idle bound
         if (step_err) cudaFreeHost(step_err);
+        if (live_err) cudaFreeHost(live_err);
     }
 
     size_t state_elems(int kind, int index) const {
@@ -482,6 +488,8 @@ struct Engine {
         SSLA_CK(cudaMallocHost(&pinned_rec_off, sizeof(int) * (P + 1)));
         SSLA_CK(cudaHostAlloc(&step_err, sizeof(unsigned), cudaHostAllocMapped));
         *step_err = 0;
+        SSLA_CK(cudaHostAlloc(&live_err, sizeof(unsigned), cudaHostAllocMapped));
+        *live_err = 0;
         reset(nullptr);
         SSLA_CK(cudaStreamSynchronize(nullptr));
     }
@@ -523,6 +531,82 @@ struct Engine {
             throw std::runtime_error("k_step: a bounded wait ran out (status " + std::to_string(v) +
                                      "; 1 = weight copies, 2 = layer input, 4 = contributions)");
         }
+    }
+
+    // Owned range of a partition in stage-2 cells [x0, x1) x [y0, y1): only
+    // events there commit predictions (the reference's HybridStrip owned
+    // bounds, ssla_s2_s3_head_celled.cuh:1663-1670); the rest are halo.
+    void set_owned(int p, int x0, int x1, int y0, int y1, cudaStream_t st) {
+        if (p < 0 || p >= g.P) throw std::invalid_argument("partition out of range");
+        if (x0 < 0 || y0 < 0 || x1 > g.W[2] || y1 > g.H[2] || x0 > x1 || y0 > y1)
+            throw std::invalid_argument("owned range outside the stage-2 grid");
+        PartState& ps = h_parts[p];
+        ps.own_x0 = x0; ps.own_x1 = x1; ps.own_y0 = y0; ps.own_y1 = y1;
+        SSLA_CK(cudaMemcpyAsync(parts.as<PartState>() + p, &ps, sizeof(PartState), cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaStreamSynchronize(st));
+    }
+
+    // The live loop touches the ring from the device: every buffer must be
+    // pinned host memory that the device reaches at the same address.
+    static void need_mapped(const void* p, size_t bytes, const char* what) {
+        if (!p) throw std::invalid_argument(std::string("live ring: ") + what + " is NULL");
+        for (const char* q : {static_cast<const char*>(p), static_cast<const char*>(p) + bytes - 1}) {
+            cudaPointerAttributes at{};
+            if (cudaPointerGetAttributes(&at, q) != cudaSuccess || at.type != cudaMemoryTypeHost ||
+                at.devicePointer != at.hostPointer) {
+                cudaGetLastError();
+                throw std::invalid_argument(std::string("live ring: ") + what +
+                                            " is not pinned, device-mapped host memory");
+            }
+        }
+    }
+
+    void live_start(int p, const SslaLiveRing& r, unsigned idle_ms, cudaStream_t st) {
+        if (p < 0 || p >= g.P) throw std::invalid_argument("partition out of range");
+        if (live_running) throw std::invalid_argument("a live loop is already running on this engine");
+        if (r.capacity < 2 || (r.capacity & (r.capacity - 1))) throw std::invalid_argument("ring capacity must be a power of two >= 2");
+        if (g.ncls > live_max_ncls()) throw std::invalid_argument("too many classes for the live loop");
+        if (reinterpret_cast<uintptr_t>(r.events) % 16) throw std::invalid_argument("live ring: events must be 16-byte aligned");
+        const size_t cols = 5 + static_cast<size_t>(g.ncls);
+        need_mapped(r.events, 16 * r.capacity, "events");
+        need_mapped(r.head, 8, "head");
+        need_mapped(r.tail, 8, "tail");
+        need_mapped(r.events_done, 8, "events_done");
+        need_mapped(r.stop_flag, 4, "stop_flag");
+        if (r.flags) need_mapped(r.flags, r.capacity, "flags");
+        if (r.preds) need_mapped(r.preds, sizeof(float) * cols * r.capacity, "preds");
+        LiveArgs a{};
+        a.g = g;
+        a.ps = h_parts[p];
+        for (int l = 0; l < 8; ++l) a.L[l] = L[l];
+        a.head = head;
+        a.events = reinterpret_cast<const float4*>(r.events);
+        a.mask = r.capacity - 1;
+        a.head_idx = r.head;
+        a.tail = r.tail;
+        a.done = r.events_done;
+        a.flags_out = r.flags;
+        a.preds_out = r.preds;
+        a.stop = r.stop_flag;
+        a.start = __atomic_load_n(r.tail, __ATOMIC_ACQUIRE);
+        a.idle_ns = static_cast<unsigned long long>(idle_ms) * 1000000ull;
+        a.err = live_err;
+        __atomic_store_n(live_err, 0u, __ATOMIC_RELEASE);
+        SSLA_CK(launch_live(st, a));
+        check_launch("k_live");
+        live_stream = st;
+        live_running = true;
+    }
+
+    unsigned live_join() {
+        if (!live_running) throw std::invalid_argument("no live loop is running on this engine");
+        live_running = false;
+        SSLA_CK(cudaStreamSynchronize(live_stream));
+        const unsigned v = __atomic_load_n(live_err, __ATOMIC_ACQUIRE);
+        if (v & 0xFFu)
+            throw CudaError("k_live: a bounded wait ran out (status " + std::to_string(v) +
+                            "; 1 weights, 2 layer input, 4 contributions, 8 event message, 16 completion)");
+        return v;
     }
 
     // Stages 0-1 of every event and one ring record per event that passed
@@ -934,6 +1018,94 @@ int ssla_engine_step_latency(SslaEngine* eng, int partition, const float* events
         cudaFreeHost(flag);
         cudaStreamDestroy(st);
         e.check_step_status();
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_set_owned(SslaEngine* eng, int partition, int x0, int x1, int y0, int y1, void* stream) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.set_owned(partition, x0, x1, y0, y1, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_live_start(SslaEngine* eng, int partition, const SslaLiveRing* ring, unsigned idle_timeout_ms,
+                           void* stream) {
+    if (!eng || !ring) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.live_start(partition, *ring, idle_timeout_ms, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_live_join(SslaEngine* eng, unsigned* status) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        const unsigned v = eng->e.live_join();
+        if (status) *status = v;
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_live_latency(SslaEngine* eng, int partition, const float* events_host, int n,
+                             double* latency_us, uint8_t* flags_out, float* preds_out) {
+    if (!eng || !events_host || !latency_us || n < 0) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::Engine& e = eng->e;
+        ssla::DeviceGuard dg(e.device);
+        constexpr unsigned long long cap = 1024;
+        const int cols = 5 + e.g.ncls;
+        struct Pinned {
+            void* p = nullptr;
+            ~Pinned() { if (p) cudaFreeHost(p); }
+        } ev, words, fl, pr;
+        SSLA_CK(cudaHostAlloc(&ev.p, 16 * cap, cudaHostAllocMapped));
+        SSLA_CK(cudaHostAlloc(&words.p, 64, cudaHostAllocMapped));
+        SSLA_CK(cudaHostAlloc(&fl.p, cap, cudaHostAllocMapped));
+        SSLA_CK(cudaHostAlloc(&pr.p, sizeof(float) * cols * cap, cudaHostAllocMapped));
+        std::memset(words.p, 0, 64);
+        auto* w = static_cast<unsigned long long*>(words.p);
+        SslaLiveRing r{};
+        r.events = static_cast<float*>(ev.p);
+        r.capacity = cap;
+        r.head = w;
+        r.tail = w + 1;
+        r.events_done = w + 2;
+        r.stop_flag = reinterpret_cast<int*>(w + 3);
+        r.flags = static_cast<uint8_t*>(fl.p);
+        r.preds = static_cast<float*>(pr.p);
+        cudaStream_t st = nullptr;
+        SSLA_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() { cudaStreamDestroy(s); }
+        } sg{st};
+        e.live_start(partition, r, 2000, st);
+        bool timed_out = false;
+        for (int i = 0; i < n && !timed_out; ++i) {
+            const unsigned long long slot = static_cast<unsigned long long>(i) & (cap - 1);
+            std::memcpy(static_cast<float*>(ev.p) + 4 * slot, events_host + 4 * static_cast<size_t>(i), 16);
+            __atomic_store_n(r.head, static_cast<unsigned long long>(i) + 1, __ATOMIC_RELEASE);
+            const auto t0 = std::chrono::steady_clock::now();
+            auto t1 = t0;
+            while (__atomic_load_n(r.events_done, __ATOMIC_ACQUIRE) < static_cast<unsigned long long>(i) + 1) {
+                t1 = std::chrono::steady_clock::now();
+                if (t1 - t0 > std::chrono::seconds(1)) { timed_out = true; break; }
+            }
+            t1 = std::chrono::steady_clock::now();
+            latency_us[i] = std::chrono::duration<double, std::micro>(t1 - t0).count();
+            const uint8_t f = r.flags[slot];
+            if (flags_out) flags_out[i] = f;
+            if (preds_out && (f & SSLA_F_R4))
+                std::memcpy(preds_out + static_cast<size_t>(i) * cols, r.preds + slot * cols, sizeof(float) * cols);
+        }
+        __atomic_store_n(r.stop_flag, 1, __ATOMIC_RELEASE);
+        e.live_join();
+        if (timed_out) throw ssla::CudaError("live loop: an event was not finished within 1 s");
         return SSLA_OK;
     });
 }

@@ -169,6 +169,25 @@ struct StepArgs {
     unsigned* err;           // status bits of waits that ran out (host-mapped, or null)
 };
 
+// Live loop (ssla_live.cu): a resident cluster fed by a pinned host ring.
+struct LiveArgs {
+    Geo g;
+    PartState ps;
+    DevLayer L[8];
+    DevHead head;
+    const float4* events;                // ring slots (pinned host memory)
+    unsigned long long mask;             // capacity - 1
+    const unsigned long long* head_idx;  // events published (host)
+    unsigned long long* tail;            // events taken (device)
+    unsigned long long* done;            // events finished (device)
+    uint8_t* flags_out;                  // [capacity] or null
+    float* preds_out;                    // [capacity][5+ncls] or null
+    const int* stop;                     // non-zero ends the loop
+    unsigned long long start;            // index of the first event
+    unsigned long long idle_ns;          // leave the loop after this long without an event
+    unsigned* err;                       // SSLA_LIVE_* status bits (host-mapped)
+};
+
 struct CommitArgs {
     Geo g;
     const StageEntry* E4;
@@ -189,6 +208,8 @@ void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
                          uint32_t* ev_xy, uint8_t* rflags, float* feat);
 void launch_filter(cudaStream_t st, const FilterArgs& a);
+cudaError_t launch_live(cudaStream_t st, const LiveArgs& a);
+int live_max_ncls();
 cudaError_t launch_step(cudaStream_t st, const StepArgs& a);
 // One HybridInputRec (t, s2 x / y, feat1) per stage-2 list entry.
 void launch_records(cudaStream_t st, int n_cap, const int* count2, const StageEntry* E2,

@@ -16,23 +16,24 @@
 // (layer_forward_ct, src/ssla_kernels.cpp:315-385; layernorm.h:41-62).
 // Weights, gamma / beta and the cells' state rows reach shared memory by bulk
 // copies issued as soon as their buffer is free, each layer completing on its
-// own mbarrier.  Every wait is bounded (kWaitNs); a wait that runs out sets a
+// own mbarrier.  Every wait is bounded (cl::kWaitNs); a wait that runs out sets a
 // bit in the caller's status word and the kernel carries on to its end.
 // Every value is formed with the same fmaf chains as the chunk engine and
 // the C oracle, so a stepped event leaves bit-identical state.
 #include <atomic>
 
+#include "ssla_cluster.cuh"
 #include "ssla_kernels.cuh"
 
 namespace ssla {
 
 namespace {
 
+using namespace cl;
+
 constexpr int kStepNT = 512;
 constexpr int kStepCTAs = 9;
 constexpr int kIssuer = kStepNT - 32;                         // lane 0 of the last warp issues copies
-constexpr unsigned long long kWaitNs = 20ull * 1000ull * 1000ull;   // bound of every wait (20 ms)
-constexpr int kMaxBlockSmem = 232448;                         // 227 KB per CTA on sm_100
 
 // ---- shared-memory plan (floats) -------------------------------------------
 // A layer buffer: [qvg A*IN*3*OUT][goW A*OUT*OUT][gamma][beta][cell rows A*OUT]
@@ -88,122 +89,8 @@ struct StepShared {
 };
 static_assert(sizeof(StepShared) + sizeof(float) * kDyn <= kMaxBlockSmem, "shared memory");
 
-// ---- PTX wrappers ------------------------------------------------------------
-__device__ __forceinline__ uint32_t su32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint32_t cta_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ unsigned long long gtime() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t* bar) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n"
-        " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(su32(bar))
-        : "memory");
-    return ok != 0;
-}
-// Waits for phase 0 of `bar` (every barrier completes once per launch).
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned* err, unsigned code) {
-    if (mbar_test(bar)) return;
-    const unsigned long long t0 = gtime();
-    while (!mbar_test(bar)) {
-        if (gtime() - t0 > kWaitNs) {
-            if (err) atomicOr_system(err, code);
-            return;
-        }
-    }
-}
-// n floats global -> own shared memory, completing on `bar` (the issuing
-// thread also raises the barrier's expected byte count).
-__device__ __forceinline__ void bulk(float* dst, const float* src, int n, uint64_t* bar) {
-    const uint32_t bytes = static_cast<uint32_t>(n) * 4u;
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     su32(dst)),
-                 "l"(src), "r"(bytes), "r"(su32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ uint32_t peer(uint32_t addr, int rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-// One float into CTA `rank`'s shared memory at the address of `dst` in this
-// CTA, completing 4 bytes on that CTA's barrier at the address of `bar`.
-__device__ __forceinline__ void send(const float* dst, const uint64_t* bar, int rank, float v) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
-                     peer(su32(dst), rank)),
-                 "r"(__float_as_uint(v)), "r"(peer(su32(bar), rank))
-                 : "memory");
-}
-__device__ __forceinline__ void cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // status bits: a wait for copies, for the layer input, for contributions ran out
 constexpr unsigned kErrWeights = 1u, kErrInput = 2u, kErrContrib = 4u;
-
-__device__ __forceinline__ bool step_gate(int pre, int window) {
-    return window <= 1 || ((pre & 255) % window) == 0;
-}
-
-// The patch cell of position d at stage s around (cx0, cy0); A == 1 is the
-// event's own cell.
-__device__ __forceinline__ bool patch_cell(int A, int d, int cx0, int cy0, int Ws, int Hs, int& cx, int& cy) {
-    if (A == 1) { cx = cx0; cy = cy0; return true; }
-    cx = cx0 + 1 - d % 3;
-    cy = cy0 + 1 - d / 3;
-    return cx >= 0 && cx < Ws && cy >= 0 && cy < Hs;
-}
-
-// What the event does, derived identically by every CTA.
-struct Plan {
-    int flags, px, py;
-    bool runs[8];     // the layer runs (its stage is reached)
-    bool used[8];     // its output is consumed (else state-only: the event ends there)
-    unsigned inb[8];  // bit d: patch position d's cell is in bounds (layers 1-7)
-};
-
-__device__ __forceinline__ void make_plan(Plan& P, int flags, int px, int py, const Geo& g) {
-    P.flags = flags;
-    P.px = px;
-    P.py = py;
-#pragma unroll
-    for (int l = 0; l < 8; ++l) {
-        const int s = l / 2, half = l % 2;
-        P.runs[l] = (flags & F_VALID) && (s == 0 || (flags & (F_R1 << (s - 1))));
-        P.used[l] = P.runs[l] && (half == 0 || (s < 3 ? (flags & (F_R1 << s)) != 0 : (flags & F_R4) != 0));
-        unsigned m = 0;
-        for (int d = 0; d < 9; ++d) {
-            int cx, cy;
-            if (patch_cell(9, d, px >> s, py >> s, g.W[s], g.H[s], cx, cy)) m |= 1u << d;
-        }
-        P.inb[l] = m;
-    }
-}
 
 __device__ __forceinline__ int cl_in(int l) { return l == 4 ? 24 : l == 7 ? 96 : 48; }
 __device__ __forceinline__ int cl_out(int l) { return l < 6 ? 48 : 96; }
@@ -217,7 +104,7 @@ __device__ __forceinline__ float* cl_rest(float* wsm, int l) {
 // This CTA takes part in layer l (4-7): its cell is in bounds, or it is CTA 0
 // and the layer's output is used (residual, gather, LayerNorm).
 __device__ __forceinline__ bool cl_part(const Plan& P, int l, int rank) {
-    return P.runs[l] && (((P.inb[l] >> rank) & 1u) || (rank == 0 && P.used[l]));
+    return P.runs(l) && (((P.inb(l) >> rank) & 1u) || (rank == 0 && P.used(l)));
 }
 
 // ---- copies (issuer thread) -----------------------------------------------------
@@ -227,7 +114,7 @@ __device__ void issue_small(int l, const Plan& P, const StepArgs& a, float* b, u
     const DevLayer& L = a.L[l];
     const int s = l / 2;
     bulk(b, L.qvgT, Lo::WQ, bar);
-    if (P.used[l]) {
+    if (P.used(l)) {
         bulk(b + Lo::WQ, L.goWT, Lo::WG, bar);
         bulk(b + Lo::GAM, L.gamma, OUT, bar);
         bulk(b + Lo::BET, L.beta, OUT, bar);
@@ -248,7 +135,7 @@ __device__ void issue_small(int l, const Plan& P, const StepArgs& a, float* b, u
 __device__ void issue_cl(int l, int part, const Plan& P, int rank, const StepArgs& a, float* wsm,
                          StepShared& sh) {
     const int IN = cl_in(l), OUT = cl_out(l), J2 = 3 * OUT, s = l / 2;
-    const bool act = (P.inb[l] >> rank) & 1u;
+    const bool act = (P.inb(l) >> rank) & 1u;
     const DevLayer& W = a.L[l];
     if ((part & 1) && act) {
         uint64_t* bar = l == 7 ? &sh.bar_w[9] : &sh.bar_w[l];
@@ -259,13 +146,13 @@ __device__ void issue_cl(int l, int part, const Plan& P, int rank, const StepArg
         uint64_t* bar = &sh.bar_w[l];
         float* r = cl_rest(wsm, l);
         if (act) {
-            if (P.used[l]) bulk(r, W.goWT + static_cast<size_t>(rank) * OUT * OUT, OUT * OUT, bar);
+            if (P.used(l)) bulk(r, W.goWT + static_cast<size_t>(rank) * OUT * OUT, OUT * OUT, bar);
             int cx, cy;
             patch_cell(9, rank, P.px >> s, P.py >> s, a.g.W[s], a.g.H[s], cx, cy);
             bulk(r + OUT * OUT + 2 * OUT, a.ps.hidden[l] + (static_cast<size_t>(cy) * a.g.W[s] + cx) * OUT, OUT,
                  bar);
         }
-        if (rank == 0 && P.used[l]) {
+        if (rank == 0 && P.used(l)) {
             bulk(r + OUT * OUT, W.gamma, OUT, bar);
             bulk(r + OUT * OUT + OUT, W.beta, OUT, bar);
             if ((l & 1) == 0) bulk(r + OUT * OUT + 3 * OUT, W.ipT, IN * OUT, bar);
@@ -386,7 +273,7 @@ __device__ bool small_layer(int l, const Plan& P, const StepArgs& a, StepShared&
     constexpr int J2 = Lo::J2;
     const int tid = threadIdx.x;
     const int s = l / 2, half = l % 2;
-    const bool used = P.used[l];
+    const bool used = P.used(l);
     const int Ws = a.g.W[s], Hs = a.g.H[s], cx0 = P.px >> s, cy0 = P.py >> s;
     const float* wq = b;
     const float* wg = b + Lo::WQ;
@@ -395,7 +282,7 @@ __device__ bool small_layer(int l, const Plan& P, const StepArgs& a, StepShared&
     float* qvg = b + Lo::QV;
     float* qh = b + Lo::QH;
     float* con = b + Lo::CON;
-    mbar_wait(&sh.bar_w[l], a.err, kErrWeights);
+    mbar_wait(&sh.bar_w[l], 0, a.err, kErrWeights);
     if (used && tid < OUT) {
         float acc;
         if (half == 0) {
@@ -466,16 +353,16 @@ __device__ void cl_layer(int l, const Plan& P, int rank, const StepArgs& a, Step
     constexpr int J2 = 3 * OUT;
     const int tid = threadIdx.x;
     const int s = l / 2;
-    const bool used = P.used[l];
-    const bool act = (P.inb[l] >> rank) & 1u;
+    const bool used = P.used(l);
+    const bool act = (P.inb(l) >> rank) & 1u;
     const float* wq = cl_wq(wsm, l);
     const float* rest = cl_rest(wsm, l);
     const float* wg = rest;
     const float* hr = rest + OUT * OUT + 2 * OUT;
     const float* wi = rest + OUT * OUT + 3 * OUT;
-    if (rank != 0) mbar_wait(&sh.bar_x[l], a.err, kErrInput);
-    mbar_wait(&sh.bar_w[l], a.err, kErrWeights);
-    if (l == 7 && act) mbar_wait(&sh.bar_w[9], a.err, kErrWeights);
+    if (rank != 0) mbar_wait(&sh.bar_x[l], 0, a.err, kErrInput);
+    mbar_wait(&sh.bar_w[l], 0, a.err, kErrWeights);
+    if (l == 7 && act) mbar_wait(&sh.bar_w[9], 0, a.err, kErrWeights);
     if (rank == 0 && used && tid < OUT) {
         float acc;
         if ((l & 1) == 0) {
@@ -534,10 +421,10 @@ __device__ void run_cl(int l, const Plan& P, int rank, const StepArgs& a, StepSh
 // layer l+1's input.
 __device__ void cl_gather(int l, const Plan& P, const StepArgs& a, StepShared& sh, float* wsm) {
     if (threadIdx.x < 32) {
-        mbar_wait(&sh.bar_c[l], a.err, kErrContrib);
-        const unsigned bmask = (l < 7 && P.runs[l + 1]) ? (P.inb[l + 1] & ~1u) : 0u;
-        if (cl_out(l) == 48) gather_ln<48, 9>(sh, &sh.con[0][0], 96, P.inb[l], sh.gb, sh.gb + 48, l + 1, bmask);
-        else gather_ln<96, 9>(sh, &sh.con[0][0], 96, P.inb[l], sh.gb, sh.gb + 96, l + 1, bmask);
+        mbar_wait(&sh.bar_c[l], 0, a.err, kErrContrib);
+        const unsigned bmask = (l < 7 && P.runs(l + 1)) ? (P.inb(l + 1) & ~1u) : 0u;
+        if (cl_out(l) == 48) gather_ln<48, 9>(sh, &sh.con[0][0], 96, P.inb(l), sh.gb, sh.gb + 48, l + 1, bmask);
+        else gather_ln<96, 9>(sh, &sh.con[0][0], 96, P.inb(l), sh.gb, sh.gb + 96, l + 1, bmask);
     }
     __syncthreads();
 }
@@ -550,7 +437,7 @@ __device__ void run_head(const Plan& P, const StepArgs& a, StepShared& sh, float
     const Geo& g = a.g;
     const PartState& ps = a.ps;
     const int ncls = g.ncls, cols = 5 + ncls;
-    mbar_wait(&sh.bar_w[8], a.err, kErrWeights);
+    mbar_wait(&sh.bar_w[8], 0, a.err, kErrWeights);
     const float* h = wsm + kRH;
     float* act = &sh.con[0][0];
     if (tid < 192) {
@@ -615,14 +502,14 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
     const bool valid = e.y > -1.0f && e.y < static_cast<float>(g.W[0]) && e.z > -1.0f &&
                        e.z < static_cast<float>(g.H[0]);
     const int px = valid ? static_cast<int>(e.y) : 0, py = valid ? static_cast<int>(e.z) : 0;
-    const int k0 = (py >> 1) * g.W[1] + (px >> 1), k1 = (py >> 2) * g.W[2] + (px >> 2);
-    const int k2 = hyb ? k1 : (py >> 3) * g.W[3] + (px >> 3), k3 = (py >> 3) * g.W[3] + (px >> 3);
+    int k[4];
+    gate_cells(g, px, py, k);
     int c[4] = {0, 0, 0, 0};
     if (valid) {
-        c[0] = ps.cnt[0][k0];
-        c[1] = ps.cnt[1][k1];
-        c[2] = ps.cnt[2][k2];
-        if (hyb) c[3] = ps.cnt[3][k3];
+        c[0] = ps.cnt[0][k[0]];
+        c[1] = ps.cnt[1][k[1]];
+        c[2] = ps.cnt[2][k[2]];
+        if (hyb) c[3] = ps.cnt[3][k[3]];
     }
     double lt_prev = 0.0;
     if (rank == 0 && tid == 0 && valid) lt_prev = ps.last_t[py * g.W[0] + px];
@@ -630,46 +517,32 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
     if (rank == 0 && tid < 5 + g.ncls)
         pbias = tid < 4 ? __ldg(a.head.reg_pred_b + tid)
                         : tid == 4 ? __ldg(a.head.obj_pred_b) : __ldg(a.head.cls_pred_b + (tid - 5));
-    int flags = 0;
-    if (valid) {
-        const int w = g.window;
-        flags = F_VALID;
-        if (step_gate(c[0], w)) {
-            flags |= F_R1;
-            if (step_gate(c[1], w)) {
-                flags |= F_R2;
-                if (step_gate(c[2], w)) {
-                    flags |= F_R3;
-                    if (!hyb || step_gate(c[3], w)) flags |= F_R4;
-                }
-            }
-        }
-    }
+    const int flags = gate_flags(valid, c, g.window, hyb);
     Plan P;
     make_plan(P, flags, px, py, g);
 
     // ---- barriers, expected messages, first copies ----
     if (tid == 0) {
-        for (int i = 0; i < 10; ++i) mbar_init(&sh.bar_w[i]);
+        for (int i = 0; i < 10; ++i) mbar_init(&sh.bar_w[i], 1);
         for (int i = 0; i < 8; ++i) {
-            mbar_init(&sh.bar_x[i]);
-            mbar_init(&sh.bar_c[i]);
+            mbar_init(&sh.bar_x[i], 1);
+            mbar_init(&sh.bar_c[i], 1);
         }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_mbar_init();
         for (int l = 4; l < 8; ++l) {
-            if (rank != 0 && P.runs[l] && ((P.inb[l] >> rank) & 1u)) mbar_arrive_tx(&sh.bar_x[l], 4u * cl_in(l));
-            if (rank == 0 && P.used[l])
-                mbar_arrive_tx(&sh.bar_c[l], 4u * cl_out(l) * __popc(P.inb[l] & ~1u));
+            if (rank != 0 && P.runs(l) && ((P.inb(l) >> rank) & 1u)) mbar_arrive_tx(&sh.bar_x[l], 4u * cl_in(l));
+            if (rank == 0 && P.used(l))
+                mbar_arrive_tx(&sh.bar_c[l], 4u * cl_out(l) * __popc(P.inb(l) & ~1u));
         }
     }
     __syncthreads();
     Deferred D{false, false, false};
     if (tid == kIssuer) {
         if (rank == 0) {
-            if (P.runs[0]) issue_small<2, 12, 1>(0, P, a, wsm, &sh.bar_w[0]);
-            if (P.runs[1]) issue_small<12, 12, 9>(1, P, a, wsm + kS1, &sh.bar_w[1]);
-            if (P.runs[2]) issue_small<12, 24, 9>(2, P, a, wsm + kS2, &sh.bar_w[2]);
-            if (P.runs[3]) issue_small<24, 24, 9>(3, P, a, wsm + kS3, &sh.bar_w[3]);
+            if (P.runs(0)) issue_small<2, 12, 1>(0, P, a, wsm, &sh.bar_w[0]);
+            if (P.runs(1)) issue_small<12, 12, 9>(1, P, a, wsm + kS1, &sh.bar_w[1]);
+            if (P.runs(2)) issue_small<12, 24, 9>(2, P, a, wsm + kS2, &sh.bar_w[2]);
+            if (P.runs(3)) issue_small<24, 24, 9>(3, P, a, wsm + kS3, &sh.bar_w[3]);
             if (cl_part(P, 4, 0)) issue_cl(4, 3, P, 0, a, wsm, sh);
         } else {
             for (int l = 4; l < 7; ++l)
@@ -682,16 +555,7 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
     if (rank == 0) {
         if (valid) {
             if (tid == 0) {
-                float dt;
-                if (lt_prev < 0.0) {
-                    dt = 1.0f;
-                } else {
-                    double v = (static_cast<double>(e.x) - lt_prev) / 1e5;
-                    if (v < 0.0) v = 0.0;
-                    if (v > 1.0) v = 1.0;
-                    dt = static_cast<float>(v);
-                }
-                sh.x[0] = dt;
+                sh.x[0] = dt_norm(lt_prev, e.x);
                 sh.x[1] = e.w;
             }
             __syncthreads();
@@ -700,14 +564,14 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
         cluster_wait();
         if (valid && tid == 0) {       // the counters may change now that every CTA has read them
             ps.last_t[py * g.W[0] + px] = static_cast<double>(e.x);
-            ps.cnt[0][k0] = static_cast<uint8_t>(c[0] + 1);
-            if (flags & F_R1) ps.cnt[1][k1] = static_cast<uint8_t>(c[1] + 1);
-            if (flags & F_R2) ps.cnt[2][k2] = static_cast<uint8_t>(c[2] + 1);
-            if (hyb && (flags & F_R3)) ps.cnt[3][k3] = static_cast<uint8_t>(c[3] + 1);
+            ps.cnt[0][k[0]] = static_cast<uint8_t>(c[0] + 1);
+            if (flags & F_R1) ps.cnt[1][k[1]] = static_cast<uint8_t>(c[1] + 1);
+            if (flags & F_R2) ps.cnt[2][k[2]] = static_cast<uint8_t>(c[2] + 1);
+            if (hyb && (flags & F_R3)) ps.cnt[3][k[3]] = static_cast<uint8_t>(c[3] + 1);
         }
-        if (P.runs[1] && small_layer<12, 12, 9>(1, P, a, sh, wsm + kS1, 0u) &&
+        if (P.runs(1) && small_layer<12, 12, 9>(1, P, a, sh, wsm + kS1, 0u) &&
             small_layer<12, 24, 9>(2, P, a, sh, wsm + kS2, 0u)) {
-            const unsigned b4 = P.runs[4] ? (P.inb[4] & ~1u) : 0u;
+            const unsigned b4 = P.runs(4) ? (P.inb(4) & ~1u) : 0u;
             if (small_layer<24, 24, 9>(3, P, a, sh, wsm + kS3, b4) && tid == kIssuer) {
                 // layers 0-3 are done: their buffers take layers 5 and 6
                 for (int l = 5; l < 7; ++l)
@@ -721,10 +585,10 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
 
     // ---- layers 4-7 ----
     for (int l = 4; l < 8; ++l) {
-        if (!P.runs[l]) break;
+        if (!P.runs(l)) break;
         if (cl_part(P, l, rank)) run_cl(l, P, rank, a, sh, wsm);
         if (tid == kIssuer) issue_deferred(l, D, P, rank, a, wsm, sh);
-        if (!P.used[l]) break;         // state-only second layer: the event ends here
+        if (!P.used(l)) break;         // state-only second layer: the event ends here
         if (rank == 0) cl_gather(l, P, a, sh, wsm);
     }
 

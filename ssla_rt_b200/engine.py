@@ -52,6 +52,10 @@ def load_library() -> C.CDLL:
         "ssla_engine_drain_records": (i, [vp, vp, vp, vp, i, vp, vp, vp]),
         "ssla_engine_step": (i, [vp, i, vp, vp, vp, vp]),
         "ssla_engine_step_latency": (i, [vp, i, vp, i, vp, vp]),
+        "ssla_engine_live_start": (i, [vp, i, C.POINTER(abi.SslaLiveRing), C.c_uint, vp]),
+        "ssla_engine_live_join": (i, [vp, C.POINTER(C.c_uint)]),
+        "ssla_engine_live_latency": (i, [vp, i, vp, i, vp, vp, vp]),
+        "ssla_engine_set_owned": (i, [vp, i, i, i, i, i, vp]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
         "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
         "ssla_s2s3_gate_codes_noalloc": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp]),
@@ -167,6 +171,39 @@ class SslaEngine:
         _check(self.lib.ssla_engine_step_latency(self.h, partition, ev.ctypes.data, ev.shape[0],
                                                  lat.ctypes.data, fl.ctypes.data))
         return lat, fl
+
+    def set_owned(self, partition: int, x0: int, x1: int, y0: int, y1: int, stream=None) -> None:
+        """Owned stage-2 range [x0, x1) x [y0, y1) of a partition (the rest is
+        halo: state only, no committed predictions)."""
+        _check(self.lib.ssla_engine_set_owned(self.h, partition, x0, x1, y0, y1, _stream(stream)))
+
+    def live_start(self, ring: "abi.SslaLiveRing", partition: int = 0, idle_timeout_ms: int = 2000,
+                   stream=None) -> None:
+        """Launches the live loop on ``ring`` (pinned host buffers) and
+        returns; end it with the ring's stop flag, then ``live_join``."""
+        self._live_ring = ring
+        _check(self.lib.ssla_engine_live_start(self.h, partition, C.byref(ring), idle_timeout_ms,
+                                               _stream(stream)))
+
+    def live_join(self) -> int:
+        """Waits for the live loop to end; returns its SSLA_LIVE_* status."""
+        st = C.c_uint(0)
+        _check(self.lib.ssla_engine_live_join(self.h, C.byref(st)))
+        self._live_ring = None
+        return st.value
+
+    def live_latency(self, events: np.ndarray, partition: int = 0):
+        """Per-event host latency (us) from publishing an event in the live
+        loop's pinned ring to seeing events_done pass it, measured inside the
+        library; returns (latency_us, flags, preds) with the decoded row of
+        every head event."""
+        ev = np.ascontiguousarray(events, dtype=np.float32).reshape(-1, 4)
+        lat = np.zeros(ev.shape[0], dtype=np.float64)
+        fl = np.zeros(ev.shape[0], dtype=np.uint8)
+        pr = np.zeros((ev.shape[0], 5 + self.ncls), dtype=np.float32)
+        _check(self.lib.ssla_engine_live_latency(self.h, partition, ev.ctypes.data, ev.shape[0],
+                                                 lat.ctypes.data, fl.ctypes.data, pr.ctypes.data))
+        return lat, fl, pr
 
     def drain_records(self, events, part_offsets, records, records_cap: int, flags=None,
                       stream=None) -> np.ndarray:
