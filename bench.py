@@ -191,54 +191,48 @@ def cpu_baseline(parts, weights_dir: str, reps: int = 3) -> dict:
 
 
 def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
-                    warmup: int = 200, samples: int = 20000) -> dict:
-    """Batch-of-1 emit -> prediction latency of a live stream: each event is
-    handed to ssla_engine_step (one launch, the event passed by value) and
-    the kernel writes its flags and, for head events, the decoded
-    prediction row straight into pinned host memory; the host waits for
-    the stream.  Host wall time per event, p50 / p99 in us, over all events
-    and over the events that produced a prediction."""
-    import torch
+                    warmup: int = 500, samples: int = 20000) -> dict:
+    """Batch-of-1 emit -> prediction latency of a live stream, p50 / p99 in
+    us, over all events and over the events that produced a prediction.
+
+    Primary: the live loop (ssla_engine_live_latency) -- a resident cluster
+    polls a pinned host ring; per event the host writes the slot, publishes
+    the ring head and spins until the kernel's events_done passes the event
+    (flags and the decoded prediction row are in pinned memory by then).
+    Also reported: the one-launch step (ssla_engine_step + stream
+    synchronize, ssla_engine_step_latency).  Both timed in the library's
+    C++ host loop with steady_clock."""
     from ssla_rt_b200 import abi
     from ssla_rt_b200.engine import SslaEngine
-    eng = SslaEngine(weights_dir, n_partitions=1, max_events=64, layout=abi.LAYOUT_HYBRID,
-                     device=device)
-    stream = torch.cuda.Stream(device)
-    flag = torch.zeros(1, dtype=torch.uint8).pin_memory()
-    pred = torch.zeros(5 + eng.ncls, dtype=torch.float32).pin_memory()
-    lat, lat_head = [], []
-    n = len(stream_events)
-    for i in range(warmup + samples):
-        e = stream_events[i % n].copy()
-        e[0] += (i // n) * 1e6
-        t0 = time.perf_counter()
-        eng.step(e, 0, flag, pred, stream=stream)
-        stream.synchronize()
-        t1 = time.perf_counter()
-        if i >= warmup:
-            us = (t1 - t0) * 1e6
-            lat.append(us)
-            if int(flag[0]) & abi.F_R4:
-                lat_head.append(us)
-    # the same stream continued, timed inside the library (C++ host loop)
-    later = stream_events.copy()
-    later[:, 0] += (warmup + samples) // n * 1e6 + 2e6
-    clat, cfl = eng.step_latency(later[:samples])
-    eng.close()
 
     def pct(v, q):
         v = sorted(v)
         return v[min(len(v) - 1, max(0, int(round(q * len(v))) - 1))] if v else None
-    chead = [x for x, f in zip(clat.tolist(), cfl.tolist()) if f & abi.F_R4]
-    return {"p50": pct(clat, 0.50), "p99": pct(clat, 0.99), "n": len(clat),
-            "head_p50": pct(chead, 0.50), "head_p99": pct(chead, 0.99), "head_events": len(chead),
-            "python": {"p50": pct(lat, 0.50), "p99": pct(lat, 0.99), "head_p50": pct(lat_head, 0.50),
-                       "head_p99": pct(lat_head, 0.99), "head_events": len(lat_head)},
-            "method": "per event: ssla_engine_step (one 9-CTA cluster launch through preprocess, gates, "
-                      "s0..s3 and the head; event by value, flags and prediction row written by the kernel "
-                      "into pinned host memory) + stream synchronize, host wall time measured in the "
-                      "library's C++ loop (ssla_engine_step_latency); 'python' = the same call timed "
-                      "around the Python binding; head_* over events that produced a prediction"}
+
+    def summary(lat, fl):
+        lat = lat.tolist()
+        head = [x for x, f in zip(lat, fl.tolist()) if f & abi.F_R4]
+        return {"p50": pct(lat, 0.50), "p99": pct(lat, 0.99), "n": len(lat),
+                "head_p50": pct(head, 0.50), "head_p99": pct(head, 0.99), "head_events": len(head)}
+
+    ev = np.ascontiguousarray(stream_events[: warmup + samples])
+    out = {}
+    for mode in ("live", "step"):
+        eng = SslaEngine(weights_dir, n_partitions=1, max_events=64, layout=abi.LAYOUT_HYBRID, device=device)
+        if mode == "live":
+            lat, fl, _ = eng.live_latency(ev)
+        else:
+            lat, fl = eng.step_latency(ev)
+        eng.close()
+        out[mode] = summary(lat[warmup:], fl[warmup:])
+    res = dict(out["live"])
+    res["step"] = out["step"]
+    res["method"] = ("live: resident 11-CTA cluster (ssla_engine_live_*) polling a pinned raw-event ring; per "
+                     "event the host publishes the ring head and spins on events_done (the reference's "
+                     "persistent-kernel protocol), host steady_clock from publish to completion seen, in "
+                     "the library's C++ loop; step: one 9-CTA cluster launch per event + stream synchronize; "
+                     "head_* over events that produced a prediction; config-0 uniform stream, tdrop 4")
+    return res
 
 
 def measured_traffic(phase: str):
@@ -564,7 +558,8 @@ def main() -> int:
     d2h = N_EVENTS + sum(p.nbytes for p in preds)
 
     # ---- batch-of-1 latency: one event in, its predictions out ----
-    latency = None if args.no_latency else measure_latency(wdir, parts[0], local)
+    from ssla_rt_b200 import events as ev_gen
+    latency = None if args.no_latency else measure_latency(wdir, ev_gen.config_events(0, n=50_000), local)
 
     # ---- roofline of the dominant phase (live CUDA-event durations) ----
     flags_dev = torch.zeros(N_EVENTS, dtype=torch.uint8, device=dev)

@@ -214,6 +214,21 @@ int  ssla_engine_drain_records(SslaEngine* eng, const float* events_dev,
 int  ssla_engine_set_owned(SslaEngine* eng, int partition, int x0, int x1, int y0, int y1,
                            void* stream);
 
+/* Prediction-tensor checkpoints in the reference's OracleRecorder file
+ * format (include/oracle.h:10-19; read by its diff_dumps / oracle_diff,
+ * src/oracle_diff.cpp): header {magic 'OEVA', version 1, num_anchors, cols,
+ * num_checkpoints}, then per checkpoint {uint64 event_idx, float
+ * [num_anchors][cols]}.  Host-only: writes the given checkpoints. */
+int  ssla_write_oracle_dump(const char* path, int num_anchors, int cols, int n_checkpoints,
+                            const uint64_t* event_idx, const float* preds);
+/* Runs the n host events (4-float rows) of one stream through `partition`
+ * (drains split after events 0, every, 2*every, ...) and dumps the decoded
+ * predictions tensor after each of those events -- OracleRecorder::record
+ * (include/oracle.h:43-54) driven the way src/legacy/schemes/
+ * s2_decomp_st.cpp:195-207 drives it.  The partition's state advances. */
+int  ssla_engine_oracle_dump(SslaEngine* eng, int partition, const float* events_host, int n,
+                             int every, const char* path);
+
 int  ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes);
 int  ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index,
                             void* host_dst, size_t bytes);

@@ -23,6 +23,7 @@
 #include <thread>
 #include <vector>
 
+#include "oracle.h"
 #include "ssla_kernels.h"
 
 namespace {
@@ -136,6 +137,38 @@ void ref_reset(void* p) {
 
 int ref_num_anchors(void* p) { return static_cast<RefHandle*>(p)->pipe.num_anchors_total(); }
 int ref_cols(void* p) { return static_cast<RefHandle*>(p)->pipe.cols(); }
+
+// The reference's own OracleRecorder over a run of the n events: after
+// event i it records pipe.last_output() (record keeps i % every == 0), the
+// way src/legacy/schemes/s2_decomp_st.cpp:195-207 drives it; then save().
+int ref_oracle_dump(void* p, int layout, const float* ev, int n, int every, const char* path) {
+    auto* h = static_cast<RefHandle*>(p);
+    try {
+        deploy::OracleRecorder rec(h->pipe.num_anchors_total(), h->pipe.cols(), static_cast<std::size_t>(every),
+                                   path);
+        for (int i = 0; i < n; ++i) {
+            run_one(h, layout, ev + 4 * static_cast<std::size_t>(i), nullptr, nullptr, nullptr, nullptr, nullptr);
+            rec.record(static_cast<std::uint64_t>(i), h->pipe.last_output());
+        }
+        rec.save();
+        return static_cast<int>(rec.num_checkpoints());
+    } catch (const std::exception&) {
+        return -1;
+    }
+}
+
+// The reference's diff_dumps (include/oracle.h:100-151).
+int ref_diff_dumps(const char* a, const char* b, double tol, double* max_abs, int* n_cp, int* n_mismatched) {
+    try {
+        const deploy::DiffReport r = deploy::diff_dumps(a, b, tol);
+        *max_abs = r.max_abs_delta;
+        *n_cp = static_cast<int>(r.n_cp);
+        *n_mismatched = static_cast<int>(r.n_mismatched_cp);
+        return r.ok ? 1 : 0;
+    } catch (const std::exception&) {
+        return -1;
+    }
+}
 
 void ref_run_events(void* p, int layout, const float* ev, int n, std::uint8_t* flags,
                     float* so0, float* so1, float* so2, float* so3) {

@@ -105,7 +105,7 @@ EXPORTED = (
     "ssla_expf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
     "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
     "ssla_engine_live_start", "ssla_engine_live_join", "ssla_engine_live_latency",
-    "ssla_engine_set_owned",
+    "ssla_engine_set_owned", "ssla_write_oracle_dump", "ssla_engine_oracle_dump",
 )
 # Every symbol include/stage01_to_gpu.h declares (the libstage01_to_gpu ABI).
 S01G_EXPORTED = (

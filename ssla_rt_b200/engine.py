@@ -56,6 +56,8 @@ def load_library() -> C.CDLL:
         "ssla_engine_live_join": (i, [vp, C.POINTER(C.c_uint)]),
         "ssla_engine_live_latency": (i, [vp, i, vp, i, vp, vp, vp]),
         "ssla_engine_set_owned": (i, [vp, i, i, i, i, i, vp]),
+        "ssla_write_oracle_dump": (i, [C.c_char_p, i, i, i, vp, vp]),
+        "ssla_engine_oracle_dump": (i, [vp, i, vp, i, i, C.c_char_p]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
         "ssla_s2s3_drain_n": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, i, i, vp, vp, vp, vp, vp]),
         "ssla_s2s3_gate_codes_noalloc": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp]),
@@ -171,6 +173,14 @@ class SslaEngine:
         _check(self.lib.ssla_engine_step_latency(self.h, partition, ev.ctypes.data, ev.shape[0],
                                                  lat.ctypes.data, fl.ctypes.data))
         return lat, fl
+
+    def oracle_dump(self, events: np.ndarray, every: int, path: str, partition: int = 0) -> None:
+        """Runs the host events through `partition` and writes the decoded
+        predictions after events 0, every, 2*every, ... as an OracleRecorder
+        dump (include/oracle.h:10-19)."""
+        ev = np.ascontiguousarray(events, dtype=np.float32).reshape(-1, 4)
+        _check(self.lib.ssla_engine_oracle_dump(self.h, partition, ev.ctypes.data, ev.shape[0], every,
+                                                os.fsencode(path)))
 
     def set_owned(self, partition: int, x0: int, x1: int, y0: int, y1: int, stream=None) -> None:
         """Owned stage-2 range [x0, x1) x [y0, y1) of a partition (the rest is
