@@ -229,6 +229,41 @@ int  ssla_write_oracle_dump(const char* path, int num_anchors, int cols, int n_c
 int  ssla_engine_oracle_dump(SslaEngine* eng, int partition, const float* events_host, int n,
                              int every, const char* path);
 
+/* Exact strip sharding (one partition per engine).  The engine drains its
+ * own stage-0 rows [lo, hi) plus `band_rows` (a multiple of 8) of each
+ * present neighbour's rows, and after each of layers 1-6 exchanges with its
+ * neighbours the next-layer inputs of the events in their bands, so the
+ * events it owns get exactly the single-sensor results (no halo drift);
+ * only owned events commit predictions.  cap_rows bounds the band rows of
+ * one stage list per drain (larger bands set SSLA_STRIP_ERR_CAPACITY).
+ * Side 0 is the neighbour above (rows < lo), side 1 the one below. */
+enum {
+    SSLA_STRIP_ERR_CAPACITY = 1,  /* more band rows than cap_rows            */
+    SSLA_STRIP_ERR_TIMEOUT = 2,   /* a neighbour's rows did not arrive       */
+    SSLA_STRIP_ERR_MISMATCH = 4   /* a neighbour sent a different row count  */
+};
+int  ssla_engine_strip_init(SslaEngine* eng, int lo, int hi, int band_rows, int has_up, int has_down,
+                            int cap_rows);
+/* This engine's receive buffer of `side`: its device address (for a
+ * neighbour in the same process) and a cudaIpcMemHandle_t (64 bytes, may be
+ * NULL) for a neighbour in another process. */
+int  ssla_engine_strip_recv_buffer(SslaEngine* eng, int side, void** dev_ptr, void* ipc_handle);
+/* Where this engine's rows for `side` go: the receive buffer of that
+ * neighbour for the opposite side, by device address or IPC handle. */
+int  ssla_engine_strip_connect(SslaEngine* eng, int side, void* peer_dev_ptr, const void* peer_ipc_handle);
+/* One drain of the strip's events (device rows, stream order) with the
+ * exchanges; waits for the neighbours' rows on the device (bounded), so
+ * each neighbour must drain the chunk with the same global event range on
+ * its own GPU concurrently.  Asynchronous on `stream`. */
+int  ssla_engine_strip_drain(SslaEngine* eng, const float* events_dev, int n, uint8_t* flags_dev,
+                             void* stream);
+/* The same for k strips sharing one GPU and one stream: the engines' steps
+ * run in lockstep, each exchange after both sides' layers (no device waits). */
+int  ssla_strip_drain_lockstep(SslaEngine* const* engines, int k, const float* const* events_dev,
+                               const int* n, uint8_t* const* flags_dev, void* stream);
+/* SSLA_STRIP_ERR_* bits since the last call (read and cleared; synchronises). */
+int  ssla_engine_strip_status(SslaEngine* eng, unsigned* status);
+
 int  ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes);
 int  ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index,
                             void* host_dst, size_t bytes);

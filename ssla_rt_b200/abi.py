@@ -106,7 +106,11 @@ EXPORTED = (
     "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
     "ssla_engine_live_start", "ssla_engine_live_join", "ssla_engine_live_latency",
     "ssla_engine_set_owned", "ssla_write_oracle_dump", "ssla_engine_oracle_dump",
+    "ssla_engine_strip_init", "ssla_engine_strip_recv_buffer", "ssla_engine_strip_connect",
+    "ssla_engine_strip_drain", "ssla_strip_drain_lockstep", "ssla_engine_strip_status",
 )
+# SSLA_STRIP_ERR_* bits
+STRIP_ERR_CAPACITY, STRIP_ERR_TIMEOUT, STRIP_ERR_MISMATCH = 1, 2, 4
 # Every symbol include/stage01_to_gpu.h declares (the libstage01_to_gpu ABI).
 S01G_EXPORTED = (
     "s01g_init", "s01g_init_full", "s01g_attach_gpu_rings", "s01g_attach_gpu_rings_multi",

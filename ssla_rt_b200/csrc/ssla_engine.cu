@@ -242,9 +242,13 @@ struct Workspace {
 //   LayerNorm) write the layer output back into X, plus the residual of the
 //   next layer (copy for a stage's second layer, input_proj for the next
 //   stage's first); after layer 7 k_head.
+// Layers [l_begin, l_end) of a drain, then the head when do_head; l_stop is
+// the layer after which the whole drain ends (the last layers' fused
+// next-stage residual is skipped there).
 void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_parts,
                 const DevLayer* L, const DevHead* head, bool do_head, bool record, Prof& prof,
-                int l_end = 8) {
+                int l_end = 8, int l_begin = 0, int l_stop = -1) {
+    if (l_stop < 0) l_stop = l_end;
     static const char* kScan[8] = {"scan_L0", "scan_L1", "scan_L2", "scan_L3",
                                    "scan_L4", "scan_L5", "scan_L6", "scan_L7"};
     static const char* kContrib[8] = {"contrib_L0", "contrib_L1", "contrib_L2", "contrib_L3",
@@ -256,8 +260,8 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
     float* R_first = w.R_A.as<float>();        // residual rows of first layers
     float* R_second = w.R_B.as<float>();       // residual rows of second layers
     const int l0 = (w.s_first == 0) ? 1 : 4;
-    if (l0 < 4) SSLA_CK(cudaMemsetAsync(w.work.p, 0, sizeof(int) * 8, st));
-    for (int l = l0; l < l_end; ++l) {
+    if (l0 < 4 && l_begin <= l0) SSLA_CK(cudaMemsetAsync(w.work.p, 0, sizeof(int) * 8, st));
+    for (int l = std::max(l0, l_begin); l < l_end; ++l) {
         const int s = l / 2, half = l % 2;
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
         // rows of this layer's scan entries (the stage list) and of its output
@@ -322,7 +326,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         } else {
             ca.list = la.list = s + 1;
             ca.E = la.E = w.E[s + 1].as<StageEntry>();
-            if (s < 3 && l + 1 < l_end) { la.ipT_next = L[l + 1].ipT; la.R_ipnext = R_first; }
+            if (s < 3 && l + 1 < l_stop) { la.ipT_next = L[l + 1].ipT; la.R_ipnext = R_first; }
         }
         launch_contrib(st, l, ca, n_out);
         check_launch("k_contrib");
@@ -388,6 +392,9 @@ struct Engine {
         if (pinned_off) cudaFreeHost(pinned_off);
         if (pinned_rec_off) cudaFreeHost(pinned_rec_off);
         if (live_running) cudaStreamSynchronize(live_stream);   // ends on its stop flag or idle bound
+        for (void* p : strip.opened)
+            if (p) cudaIpcCloseMemHandle(p);
+        if (strip.err) cudaFreeHost(strip.err);
         if (step_err) cudaFreeHost(step_err);
         if (live_err) cudaFreeHost(live_err);
     }
@@ -533,6 +540,142 @@ struct Engine {
         }
     }
 
+    // ---- exact strip sharding (ssla_strip.cu) ----
+    struct Strip {
+        bool on = false;
+        int lo = 0, hi = 0, band = 0, cap = 0;
+        int has[2] = {0, 0};
+        DevBuf idx, cnt, recv[2], ctr;
+        char* peer[2] = {nullptr, nullptr};     // the neighbour's receive buffer for my rows of side s
+        void* opened[2] = {nullptr, nullptr};   // IPC mappings to close
+        unsigned long long seq = 0;
+        unsigned* err = nullptr;                // host-mapped SSLA_STRIP_ERR_* bits
+    } strip;
+    static constexpr size_t kStripHdr = 32;     // u64 sequence, u64 row count per parity, pad
+
+    size_t strip_recv_bytes() const { return kStripHdr + 2 * static_cast<size_t>(strip.cap) * 96 * sizeof(float); }
+
+    void strip_init(int lo, int hi, int band, int has_up, int has_down, int cap) {
+        if (g.P != 1) throw std::invalid_argument("strip sharding needs an engine with one partition");
+        if (lo < 0 || hi > g.H[0] || lo >= hi || lo % 8 || hi % 8 || band <= 0 || band % 8 || cap <= 0)
+            throw std::invalid_argument("strip rows must be multiples of 8 inside the sensor, band > 0");
+        if ((has_up && lo == 0) || (has_down && hi == g.H[0]))
+            throw std::invalid_argument("a neighbour beyond the sensor edge");
+        strip.lo = lo; strip.hi = hi; strip.band = band; strip.cap = cap;
+        strip.has[0] = has_up ? 1 : 0; strip.has[1] = has_down ? 1 : 0;
+        strip.idx.alloc(sizeof(int) * 12 * static_cast<size_t>(cap));
+        strip.cnt.alloc(sizeof(int) * 12);
+        strip.ctr.alloc(sizeof(unsigned) * 2);
+        SSLA_CK(cudaMemset(strip.ctr.p, 0, sizeof(unsigned) * 2));
+        for (int sd = 0; sd < 2; ++sd)
+            if (strip.has[sd]) {
+                strip.recv[sd].alloc(strip_recv_bytes());
+                SSLA_CK(cudaMemset(strip.recv[sd].p, 0, strip_recv_bytes()));
+            }
+        if (!strip.err) SSLA_CK(cudaHostAlloc(&strip.err, sizeof(unsigned), cudaHostAllocMapped));
+        *strip.err = 0;
+        strip.seq = 0;
+        set_owned(0, 0, g.W[2], lo >> 2, hi >> 2, nullptr);
+        strip.on = true;
+    }
+
+    void strip_recv_buffer(int side, void** ptr, void* handle) {
+        if (!strip.on || side < 0 || side > 1 || !strip.has[side]) throw std::invalid_argument("no such strip side");
+        if (ptr) *ptr = strip.recv[side].p;
+        if (handle)
+            SSLA_CK(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), strip.recv[side].p));
+    }
+
+    void strip_connect(int side, void* ptr, const void* handle) {
+        if (!strip.on || side < 0 || side > 1 || !strip.has[side]) throw std::invalid_argument("no such strip side");
+        if (handle) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, handle, sizeof h);
+            void* p = nullptr;
+            SSLA_CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+            strip.opened[side] = p;
+            strip.peer[side] = static_cast<char*>(p);
+        } else {
+            if (!ptr) throw std::invalid_argument("strip_connect needs a device address or an IPC handle");
+            strip.peer[side] = static_cast<char*>(ptr);
+        }
+    }
+
+    // Step j of a strip drain: 0 = front, band lists, layer 1; 1..5 = layer
+    // j+1; 6 = layer 7, head and commit.
+    void strip_step(int j, const float* ev, int n, uint8_t* flags, cudaStream_t st) {
+        if (!strip.on) throw std::invalid_argument("strip_init first");
+        if (j == 0) {
+            const int off[2] = {0, n};
+            drain_front(ev, off, st, 3);
+            StripSelectArgs sa{};
+            for (int k = 0; k <= 4; ++k) { sa.E[k] = ws.E[k].as<StageEntry>(); sa.g_cap[k] = g.cap[k]; }
+            sa.count = ws.count.as<int>();
+            sa.lo = strip.lo; sa.hi = strip.hi; sa.band = strip.band;
+            sa.has[0] = strip.has[0]; sa.has[1] = strip.has[1];
+            sa.cap = strip.cap; sa.idx = strip.idx.as<int>(); sa.cnt = strip.cnt.as<int>(); sa.err = strip.err;
+            launch_band_select(st, sa);
+            check_launch("k_band_select");
+            run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, 2, 0, 8);
+        } else if (j < 6) {
+            run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, j + 2, j + 1, 8);
+        } else {
+            run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record, prof, 8, 7, 8);
+            drain_back(n, flags, st);
+        }
+    }
+
+    // Exchange after layer j + 1 (j = 0..5): the next layer's input rows,
+    // stage list k = (j + 2) / 2, channels chans((j + 1) / 2).
+    void strip_xfer(int j, bool do_export, unsigned long long seq, bool wait, cudaStream_t st) {
+        const int l = j + 1, k = (l + 1) / 2, C = chans(l / 2);
+        const int parity = static_cast<int>(seq & 1u);
+        const size_t data_off = kStripHdr + static_cast<size_t>(parity) * strip.cap * 96 * sizeof(float);
+        for (int sd = 0; sd < 2; ++sd) {
+            if (!strip.has[sd]) continue;
+            StripXferArgs xa{};
+            xa.X = ws.X.as<float>(); xa.C = C; xa.cap = strip.cap; xa.parity = parity; xa.seq = seq;
+            xa.err = strip.err;
+            const int q = (k - 1) * 4 + sd * 2 + (do_export ? 0 : 1);
+            xa.idx = strip.idx.as<int>() + static_cast<size_t>(q) * strip.cap;
+            xa.cnt = strip.cnt.as<int>() + q;
+            if (do_export) {
+                if (!strip.peer[sd]) throw std::invalid_argument("strip side not connected");
+                xa.data = reinterpret_cast<float*>(strip.peer[sd] + data_off);
+                xa.header = reinterpret_cast<unsigned long long*>(strip.peer[sd]);
+                xa.done_ctr = strip.ctr.as<unsigned>() + sd;
+                launch_strip_export(st, xa);
+                check_launch("k_strip_export");
+            } else {
+                xa.data = reinterpret_cast<float*>(strip.recv[sd].as<char>() + data_off);
+                xa.header = strip.recv[sd].as<unsigned long long>();
+                xa.wait = wait ? 1 : 0;
+                xa.wait_ns = 5ull * 1000ull * 1000ull * 1000ull;
+                launch_strip_import(st, xa);
+                check_launch("k_strip_import");
+            }
+        }
+    }
+
+    // One strip drain on this GPU, the neighbours' rows awaited on the device.
+    void strip_drain(const float* ev, int n, uint8_t* flags, cudaStream_t st) {
+        for (int j = 0; j < 7; ++j) {
+            strip_step(j, ev, n, flags, st);
+            if (j < 6) {
+                const unsigned long long seq = ++strip.seq;
+                strip_xfer(j, true, seq, false, st);
+                strip_xfer(j, false, seq, true, st);
+            }
+        }
+    }
+
+    unsigned strip_status() {
+        if (!strip.err) return 0;
+        SSLA_CK(cudaDeviceSynchronize());
+        const unsigned v = __atomic_exchange_n(strip.err, 0u, __ATOMIC_ACQ_REL);
+        return v;
+    }
+
     // Owned range of a partition in stage-2 cells [x0, x1) x [y0, y1): only
     // events there commit predictions (the reference's HybridStrip owned
     // bounds, ssla_s2_s3_head_celled.cuh:1663-1670); the rest are halo.
@@ -644,6 +787,20 @@ struct Engine {
     // its layer-3 output rows for k_records.
     void drain(const float* ev_dev, const int* off, uint8_t* flags_dev, cudaStream_t st, int s_last = 3) {
         DeviceGuard dg(device);
+        const int n = drain_front(ev_dev, off, st, s_last);
+        if (s_last < 3) {
+            run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, 2 * (s_last + 1));
+            if (flags_dev && n > 0)
+                SSLA_CK(cudaMemcpyAsync(flags_dev, ws.rflags.p, n, cudaMemcpyDeviceToDevice, st));
+            return;
+        }
+        run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record, prof);
+        drain_back(n, flags_dev, st);
+    }
+
+    // Preprocess, stage-0 tile lists, gates with layer 0, stage lists and
+    // their tile lists up to stage s_last; returns the event count.
+    int drain_front(const float* ev_dev, const int* off, cudaStream_t st, int s_last) {
         const int P = g.P;
         if (off[0] != 0) throw std::invalid_argument("part_offsets[0] must be 0");
         for (int p = 0; p < P; ++p)
@@ -697,13 +854,11 @@ struct Engine {
             check_launch("k_filter");
         }
         prof.mark("filter_s123", s_last, st);
-        if (s_last < 3) {
-            run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, 2 * (s_last + 1));
-            if (flags_dev && n > 0)
-                SSLA_CK(cudaMemcpyAsync(flags_dev, ws.rflags.p, n, cudaMemcpyDeviceToDevice, st));
-            return;
-        }
-        run_layers(st, g, ws, parts.as<PartState>(), L, &head, true, record, prof);
+        return n;
+    }
+
+    // Last-writer prediction commit and the event flags.
+    void drain_back(int n, uint8_t* flags_dev, cudaStream_t st) {
         CommitArgs cm{};
         cm.g = g; cm.E4 = ws.E[4].as<StageEntry>(); cm.off4 = ws.off[4].as<int>();
         cm.head_dec = ws.head_dec.as<float>(); cm.head_raw = ws.head_raw.as<float>();
@@ -1027,6 +1182,77 @@ int ssla_engine_set_owned(SslaEngine* eng, int partition, int x0, int x1, int y0
     return ssla::guarded([&] {
         ssla::DeviceGuard dg(eng->e.device);
         eng->e.set_owned(partition, x0, x1, y0, y1, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_strip_init(SslaEngine* eng, int lo, int hi, int band_rows, int has_up, int has_down,
+                           int cap_rows) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.strip_init(lo, hi, band_rows, has_up, has_down, cap_rows);
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_strip_recv_buffer(SslaEngine* eng, int side, void** dev_ptr, void* ipc_handle) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.strip_recv_buffer(side, dev_ptr, ipc_handle);
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_strip_connect(SslaEngine* eng, int side, void* peer_dev_ptr, const void* peer_ipc_handle) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.strip_connect(side, peer_dev_ptr, peer_ipc_handle);
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_strip_drain(SslaEngine* eng, const float* events_dev, int n, uint8_t* flags_dev, void* stream) {
+    if (!eng || n < 0 || (n > 0 && !events_dev)) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.strip_drain(events_dev, n, flags_dev, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_strip_drain_lockstep(SslaEngine* const* engines, int k, const float* const* events_dev, const int* n,
+                              uint8_t* const* flags_dev, void* stream) {
+    if (!engines || k < 1 || !events_dev || !n) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        for (int i = 0; i < k; ++i) {
+            if (!engines[i] || n[i] < 0) throw std::invalid_argument("null engine or negative count");
+            if (engines[i]->e.device != engines[0]->e.device)
+                throw std::invalid_argument("lockstep strips share one device");
+        }
+        ssla::DeviceGuard dg(engines[0]->e.device);
+        for (int j = 0; j < 7; ++j) {
+            for (int i = 0; i < k; ++i)
+                engines[i]->e.strip_step(j, events_dev[i], n[i], flags_dev ? flags_dev[i] : nullptr, st);
+            if (j < 6) {
+                unsigned long long seq = 0;
+                for (int i = 0; i < k; ++i) seq = ++engines[i]->e.strip.seq;
+                for (int i = 0; i < k; ++i) engines[i]->e.strip_xfer(j, true, seq, false, st);
+                for (int i = 0; i < k; ++i) engines[i]->e.strip_xfer(j, false, seq, false, st);
+            }
+        }
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_strip_status(SslaEngine* eng, unsigned* status) {
+    if (!eng || !status) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        *status = eng->e.strip_status();
         return SSLA_OK;
     });
 }

@@ -169,6 +169,39 @@ struct StepArgs {
     unsigned* err;           // status bits of waits that ran out (host-mapped, or null)
 };
 
+// Strip exchange (ssla_strip.cu).
+struct StripSelectArgs {
+    const StageEntry* E[5];
+    const int* count;
+    int g_cap[5];
+    int lo, hi, band;        // own stage-0 rows [lo, hi), band rows
+    int has[2];              // neighbour above (rows < lo) / below (rows >= hi)
+    int cap;                 // rows per index list
+    int* idx;                // [3 lists][4: side*2 + kind][cap] entry indices, stream order
+    int* cnt;                // [3][4]
+    unsigned* err;
+};
+
+struct StripXferArgs {
+    float* X;                    // layer-input rows of the stage list
+    int C;                       // channels of a row
+    const int* idx;              // entry indices (send: mine in the band; receive: foreign)
+    const int* cnt;
+    int cap;
+    float* data;                 // packed rows in the receiver's buffer
+    unsigned long long* header;  // receiver's header: [0] sequence, [1 + parity] row count
+    int parity;
+    unsigned long long seq;
+    unsigned* done_ctr;          // export: CTA completion counter
+    int wait;                    // import: wait for the sequence (bounded) or expect it
+    unsigned long long wait_ns;
+    unsigned* err;
+};
+
+void launch_band_select(cudaStream_t st, const StripSelectArgs& a);
+void launch_strip_export(cudaStream_t st, const StripXferArgs& a);
+void launch_strip_import(cudaStream_t st, const StripXferArgs& a);
+
 // Live loop (ssla_live.cu): a resident cluster fed by a pinned host ring.
 struct LiveArgs {
     Geo g;

@@ -56,6 +56,12 @@ def load_library() -> C.CDLL:
         "ssla_engine_live_join": (i, [vp, C.POINTER(C.c_uint)]),
         "ssla_engine_live_latency": (i, [vp, i, vp, i, vp, vp, vp]),
         "ssla_engine_set_owned": (i, [vp, i, i, i, i, i, vp]),
+        "ssla_engine_strip_init": (i, [vp, i, i, i, i, i, i]),
+        "ssla_engine_strip_recv_buffer": (i, [vp, i, C.POINTER(vp), vp]),
+        "ssla_engine_strip_connect": (i, [vp, i, vp, vp]),
+        "ssla_engine_strip_drain": (i, [vp, vp, i, vp, vp]),
+        "ssla_strip_drain_lockstep": (i, [vp, i, vp, vp, vp, vp]),
+        "ssla_engine_strip_status": (i, [vp, C.POINTER(C.c_uint)]),
         "ssla_write_oracle_dump": (i, [C.c_char_p, i, i, i, vp, vp]),
         "ssla_engine_oracle_dump": (i, [vp, i, vp, i, i, C.c_char_p]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
@@ -181,6 +187,35 @@ class SslaEngine:
         ev = np.ascontiguousarray(events, dtype=np.float32).reshape(-1, 4)
         _check(self.lib.ssla_engine_oracle_dump(self.h, partition, ev.ctypes.data, ev.shape[0], every,
                                                 os.fsencode(path)))
+
+    # ---- exact strip sharding ----
+    def strip_init(self, lo: int, hi: int, band_rows: int, has_up: bool, has_down: bool, cap_rows: int) -> None:
+        """Own stage-0 rows [lo, hi) of the sensor; neighbours' band rows
+        exchanged per layer (one partition)."""
+        _check(self.lib.ssla_engine_strip_init(self.h, lo, hi, band_rows, int(has_up), int(has_down), cap_rows))
+
+    def strip_recv_buffer(self, side: int):
+        """(device address, 64-byte IPC handle) of this engine's receive
+        buffer for `side` (0 = neighbour above, 1 = below)."""
+        ptr = C.c_void_p()
+        handle = (C.c_ubyte * 64)()
+        _check(self.lib.ssla_engine_strip_recv_buffer(self.h, side, C.byref(ptr), handle))
+        return ptr.value, bytes(handle)
+
+    def strip_connect(self, side: int, peer_ptr: Optional[int] = None, peer_handle: Optional[bytes] = None) -> None:
+        """Send `side`'s rows to the neighbour's receive buffer (its opposite
+        side), by device address (same process) or IPC handle."""
+        h = (C.c_ubyte * 64).from_buffer_copy(peer_handle) if peer_handle is not None else None
+        _check(self.lib.ssla_engine_strip_connect(self.h, side, peer_ptr, h))
+
+    def strip_drain(self, events, n: int, flags=None, stream=None) -> None:
+        """One strip drain with device-side waits for the neighbours' rows."""
+        _check(self.lib.ssla_engine_strip_drain(self.h, _ptr(events), n, _ptr(flags), _stream(stream)))
+
+    def strip_status(self) -> int:
+        st = C.c_uint(0)
+        _check(self.lib.ssla_engine_strip_status(self.h, C.byref(st)))
+        return st.value
 
     def set_owned(self, partition: int, x0: int, x1: int, y0: int, y1: int, stream=None) -> None:
         """Owned stage-2 range [x0, x1) x [y0, y1) of a partition (the rest is
@@ -315,3 +350,16 @@ def gate_codes_noalloc(cfg: abi.HybridS2S3Config, rings: Sequence[int], ns: Sequ
     _check(lib.ssla_s2s3_gate_codes_noalloc(C.byref(cfg), C.cast(r, C.c_void_p), C.cast(n, C.c_void_p),
                                             C.cast(o, C.c_void_p) if o is not None else None,
                                             _stream(stream)))
+
+
+def strip_drain_lockstep(engines: Sequence["SslaEngine"], events: Sequence, flags: Optional[Sequence] = None,
+                         stream=None) -> None:
+    """Drains strips that share one GPU in lockstep on one stream: every
+    engine's layers, then each exchange (ssla_strip_drain_lockstep)."""
+    k = len(engines)
+    lib = engines[0].lib
+    e_arr = (C.c_void_p * k)(*[e.h.value if isinstance(e.h, C.c_void_p) else e.h for e in engines])
+    ev_arr = (C.c_void_p * k)(*[_ptr(x) for x in events])
+    n_arr = (C.c_int * k)(*[int(x.shape[0]) for x in events])
+    f_arr = (C.c_void_p * k)(*[_ptr(f) for f in flags]) if flags is not None else None
+    _check(lib.ssla_strip_drain_lockstep(e_arr, k, ev_arr, n_arr, f_arr, _stream(stream)))
