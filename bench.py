@@ -300,14 +300,26 @@ def config_dict() -> dict:
 # ---------------------------------------------------------------------------
 STRIP_EVENTS = 10_000_000
 STRIP_H, STRIP_W = 256, 320
-STRIP_CHUNK = 1 << 20
+STRIP_CHUNK = 1 << 20            # halo mode: events per drain of a rank
+STRIP_GLOBAL_CHUNK = 1 << 22     # exact mode: global stream events per aligned chunk
+STRIP_BAND = 16                  # exact mode: band rows (2 stage-3 rows)
 
 
 def run_strips(args, rank: int, world: int, local: int) -> int:
     """Strong scaling: the one 10M-event stream of config 3 split into `world`
-    horizontal strips (ssla_rt_b200/strips.py); each rank drains its strip
-    plus halo, in stream order, in chunks of STRIP_CHUNK events; value = the
-    stream's events / the slowest rank's device time."""
+    horizontal strips (ssla_rt_b200/strips.py), one per rank, drained in
+    stream order.  value = the stream's events / the slowest rank's device
+    time.
+
+    exact (default): each rank drains its own rows plus a 16-row band of each
+    neighbour's rows and, after every layer, exchanges the band events' next-
+    layer inputs with its neighbours (ssla_engine_strip_drain, peer memory
+    over NVLink through CUDA IPC handles); owned results equal the single-
+    sensor run bit for bit.  Chunks are aligned on the global stream (chunk c
+    = global events [c*G, (c+1)*G)), so neighbours exchange for the same
+    events.
+    halo: the reference's replication -- own rows plus a halo, no exchange,
+    approximate near the edges."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -323,19 +335,48 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     stub.write_stub(wdir, h=STRIP_H, w=STRIP_W, seed=1, tdrop=4)
     ev_all = events.config_events(3)
     span = float(ev_all[:, 0].max()) + 1.0
-    (lo, hi), sev, own = strips.shard(ev_all, STRIP_H, world, args.halo_rows)[rank]
+    exact = args.strip_mode == "exact"
+    band = STRIP_BAND if exact else args.halo_rows
+    lo, hi = strips.strip_bounds(STRIP_H, world)[rank]
+    mask = strips.route_mask(ev_all, lo, hi, STRIP_H, band)
+    gidx = np.nonzero(mask)[0]
+    sev = np.ascontiguousarray(ev_all[mask])
+    own = strips.owned_mask(sev, lo, hi)
     del ev_all
     n = len(sev)
-    eng = SslaEngine(wdir, n_partitions=1, max_events=STRIP_CHUNK, layout=abi.LAYOUT_HYBRID, device=local)
-    eng.set_owned(0, *strips.owned_s2(lo, hi, STRIP_W))
+    G = STRIP_GLOBAL_CHUNK if exact else STRIP_CHUNK
+    if exact:
+        cuts = np.searchsorted(gidx, np.arange(0, STRIP_EVENTS + G, G))
+        chunks = [(int(cuts[c]), int(cuts[c + 1])) for c in range(len(cuts) - 1)]
+        cap_ev = max(1, max(b - a for a, b in chunks))
+    else:
+        chunks = [(c, min(c + G, n)) for c in range(0, n, G)]
+        cap_ev = G
+    eng = SslaEngine(wdir, n_partitions=1, max_events=cap_ev, layout=abi.LAYOUT_HYBRID, device=local)
+    if exact:
+        eng.strip_init(lo, hi, band, rank > 0, rank < world - 1, max(1, cap_ev // 2))
+        if world > 1:
+            mine = [eng.strip_recv_buffer(sd)[1] if (sd == 0 and rank > 0) or (sd == 1 and rank < world - 1)
+                    else None for sd in (0, 1)]
+            allh = [None] * world
+            dist.all_gather_object(allh, mine)
+            if rank > 0:
+                eng.strip_connect(0, peer_handle=allh[rank - 1][1])
+            if rank < world - 1:
+                eng.strip_connect(1, peer_handle=allh[rank + 1][0])
+            dist.barrier()
+    else:
+        eng.set_owned(0, *strips.owned_s2(lo, hi, STRIP_W))
     ev = torch.from_numpy(sev).to(dev)
-    chunks = [(c, min(c + STRIP_CHUNK, n)) for c in range(0, n, STRIP_CHUNK)]
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
 
     def one_pass():
         for c0, c1 in chunks:
-            eng.drain(ev[c0:c1], [0, c1 - c0], stream=stream)
+            if exact:
+                eng.strip_drain(ev[c0:], c1 - c0, stream=stream)
+            elif c1 > c0:
+                eng.drain(ev[c0:c1], [0, c1 - c0], stream=stream)
 
     def barrier():
         if world > 1:
@@ -362,6 +403,7 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     for _ in range(args.steps):
         ev[:, 0] += span
         flush.fill_(1.0)
+        barrier()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -372,29 +414,37 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
         launches += eng.info().launches * len(chunks)
     barrier()
     clk = clocks.stop(local)
+    status = eng.strip_status() if exact else 0
     my_ms = total_ms
     total_ms = max_over_ranks(total_ms)
     value = STRIP_EVENTS * args.steps / (total_ms * 1e-3) / 1e6
 
-    # e2e: pinned host events copied in per chunk, flags copied out
-    host = torch.from_numpy(sev).pin_memory().numpy()
-    host_flags = torch.empty(STRIP_CHUNK, dtype=torch.uint8).pin_memory().numpy()
+    # e2e: pinned host events copied in per chunk (halo: with flags out)
+    host = torch.from_numpy(sev).pin_memory()
     host[:, 0] += span * (args.warmup + args.steps + 1)
+    host_np = host.numpy()
+    host_flags = torch.empty(max(1, cap_ev), dtype=torch.uint8).pin_memory().numpy()
     barrier()
     e2e_s = 0.0
     for _ in range(args.steps):
         host[:, 0] += span
         flush.fill_(2.0)
         torch.cuda.synchronize(dev)
+        barrier()
         t0 = time.perf_counter()
-        for c0, c1 in chunks:
-            eng.drain_host(host[c0:c1], [0, c1 - c0], host_flags[: c1 - c0], stream=stream)
+        if exact:
+            ev.copy_(host, non_blocking=True)
+            one_pass()
+        else:
+            for c0, c1 in chunks:
+                eng.drain_host(host_np[c0:c1], [0, c1 - c0], host_flags[: c1 - c0], stream=stream)
         preds = eng.preds_dec(0)
         e2e_s += time.perf_counter() - t0
     e2e_s = max_over_ranks(e2e_s)
     e2e = STRIP_EVENTS * args.steps / e2e_s / 1e6
+    status = status | (eng.strip_status() if exact else 0)
 
-    routed = torch.tensor([n, int(own.sum())], dtype=torch.int64, device=dev)
+    routed = torch.tensor([n, int(own.sum()), status], dtype=torch.int64, device=dev)
     per_rank = [routed.clone() for _ in range(world)]
     rank_ms = torch.tensor([my_ms], dtype=torch.float64, device=dev)
     all_ms = [rank_ms.clone() for _ in range(world)]
@@ -402,25 +452,30 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
         dist.all_gather(per_rank, routed)
         dist.all_gather(all_ms, rank_ms)
     if rank == 0:
+        how = ("exact: per-layer exchange of band-event inputs between neighbouring strips over peer memory "
+               f"(band {band} rows), owned results bit-identical to one sensor" if exact else
+               f"halo replication ({band} rows), no exchange")
         line = {
             "metric": METRIC, "value": value, "unit": "Mev/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": f"config3: 10,000,000 events at 320x256 (70% from 16 moving Gaussian blobs "
-                                   f"sigma 4, 30% uniform, Poisson 20 Mev/s) in {world} horizontal strip(s) with "
-                                   f"a {args.halo_rows}-row halo, one strip per GPU, full s0..s3 + YOLOX head",
+                                   f"sigma 4, 30% uniform, Poisson 20 Mev/s) in {world} horizontal strip(s), one "
+                                   f"per GPU, full s0..s3 + YOLOX head; {how}",
                        "model": "SSLA-S stub (320x256, seed 1, tdrop 4)", "events_per_step": STRIP_EVENTS,
-                       "chunk_events": STRIP_CHUNK, "halo_rows": args.halo_rows,
+                       "chunk_events": G, "chunking": "global stream ranges" if exact else "per-rank",
+                       "strip_mode": args.strip_mode, "band_rows": band,
                        "l2": "flushed between steps (256 MiB write, untimed); inputs 160 MB > L2",
-                       "parallelism": f"strips{world} (halo replication, no collective on the data path)"},
+                       "parallelism": f"strips{world}"},
             "strips": {"bounds": strips.strip_bounds(STRIP_H, world),
                        "routed_events": [int(x[0]) for x in per_rank],
                        "owned_events": [int(x[1]) for x in per_rank],
+                       "exchange_status": [int(x[2]) for x in per_rank],
                        "rank_ms": [float(x.item()) / args.steps for x in all_ms]},
             "clocks": clk,
             "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(sev.nbytes),
-                    "d2h_bytes_per_step": int(n + preds.nbytes)},
+                    "d2h_bytes_per_step": int(preds.nbytes + (0 if exact else n))},
             "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
@@ -442,7 +497,9 @@ def main() -> int:
     ap.add_argument("--workload", default="config1", choices=["config1", "strips"],
                     help="config1: 80x64 partitions per GPU (weak scaling); strips: config 3, one "
                          "320x256 stream in horizontal strips across the GPUs (strong scaling)")
-    ap.add_argument("--halo-rows", type=int, default=16, help="strips: halo in stage-0 rows (multiple of 8)")
+    ap.add_argument("--strip-mode", default="exact", choices=["exact", "halo"],
+                    help="strips: exact per-layer band exchange (default) or halo replication")
+    ap.add_argument("--halo-rows", type=int, default=16, help="strips, halo mode: halo in stage-0 rows (multiple of 8)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -44,7 +44,8 @@ enum {
     SSLA_F_R1 = 2,     /* passed gate 0, entered stage 1 */
     SSLA_F_R2 = 4,     /* entered stage 2                */
     SSLA_F_R3 = 8,     /* entered stage 3                */
-    SSLA_F_R4 = 16     /* produced a head prediction     */
+    SSLA_F_R4 = 16,    /* produced a head prediction     */
+    SSLA_F_FOREIGN = 32 /* strip mode: a neighbour's band event (its outputs are the neighbour's) */
 };
 
 typedef struct SslaEngine SslaEngine;

@@ -35,7 +35,7 @@ constexpr int kMaxParts = 1024;
 constexpr uint32_t kInvalidXY = 0xFFFFFFFFu;
 constexpr int kCompactTile = 4096;  // events per compaction tile
 
-enum : uint8_t { F_VALID = 1, F_R1 = 2, F_R2 = 4, F_R3 = 8, F_R4 = 16 };
+enum : uint8_t { F_VALID = 1, F_R1 = 2, F_R2 = 4, F_R3 = 8, F_R4 = 16, F_FOREIGN = 32 };
 enum { LAYOUT_DECOMP = 0, LAYOUT_HYBRID = 1 };
 
 __host__ __device__ constexpr int chans(int s) { return s == 0 ? 12 : s == 1 ? 24 : s == 2 ? 48 : 96; }
@@ -77,6 +77,7 @@ struct Geo {
     int seg;             // tile-list segment length
     int nseg[4];         // allocated segments per (partition, tile) per stage
     int cap[5];          // allocated entries of each stage list (E_0 = events)
+    int row_lo[4], row_hi[4];   // rows of each stage's grid the scans update (strips: own rows + 1)
 };
 
 struct StageEntry {      // one event in a stage list E_s, stream order

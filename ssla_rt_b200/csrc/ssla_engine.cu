@@ -147,6 +147,8 @@ void make_geo(Geo& g, int H, int W, int P, int layout, int window, int ncls) {
         g.W[s] = W >> s;
         g.tx[s] = (g.W[s] + kTile - 1) / kTile;
         g.ty[s] = (g.H[s] + kTile - 1) / kTile;
+        g.row_lo[s] = 0;
+        g.row_hi[s] = g.H[s];
     }
     if (g.tx[0] > kMaxTileCols) throw std::invalid_argument("sensor wider than 512 pixels");
     g.P = P;
@@ -576,6 +578,11 @@ struct Engine {
         *strip.err = 0;
         strip.seq = 0;
         set_owned(0, 0, g.W[2], lo >> 2, hi >> 2, nullptr);
+        // scans update the rows owned events read: own rows and one beyond each side
+        for (int s = 0; s < 4; ++s) {
+            g.row_lo[s] = std::max(0, (lo >> s) - 1);
+            g.row_hi[s] = std::min(g.H[s], (hi >> s) + 1);
+        }
         strip.on = true;
     }
 
@@ -616,6 +623,8 @@ struct Engine {
             sa.cap = strip.cap; sa.idx = strip.idx.as<int>(); sa.cnt = strip.cnt.as<int>(); sa.err = strip.err;
             launch_band_select(st, sa);
             check_launch("k_band_select");
+            launch_mark_foreign(st, n, ws.ev_xy.as<uint32_t>(), ws.rflags.as<uint8_t>(), strip.lo, strip.hi);
+            check_launch("k_mark_foreign");
             run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, 2, 0, 8);
         } else if (j < 6) {
             run_layers(st, g, ws, parts.as<PartState>(), L, &head, false, record, prof, j + 2, j + 1, 8);

@@ -739,7 +739,7 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
     const int cx = (tile % a.g.tx[s]) * kTile + (local % kTile);
     const int cy = (tile / a.g.tx[s]) * kTile + (local / kTile);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    if (cx >= Wl || cy >= Hl) return;
+    if (cx >= Wl || cy >= Hl || cy < a.g.row_lo[s] || cy >= a.g.row_hi[s]) return;
     float* hp = a.parts[p].hidden[a.layer] + (static_cast<size_t>(cy) * Wl + cx) * OUT;
     float h[CPL];
 #pragma unroll
@@ -880,7 +880,7 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
         const int grp = item & 15, tile = (item >> 4) % ntiles, p = (item >> 4) / ntiles;
         const int gx0 = (tile % a.g.tx[s]) * kTile + (grp & 3) * 2;
         const int gy0 = (tile / a.g.tx[s]) * kTile + (grp >> 2) * 2;
-        if (gx0 >= Wl || gy0 >= Hl) continue;
+        if (gx0 >= Wl || gy0 >= Hl || gy0 + 1 < a.g.row_lo[s] || gy0 >= a.g.row_hi[s]) continue;
         float* const hid = a.parts[p].hidden[a.layer];
         float h[R];
         int hoff[R];
@@ -1087,10 +1087,10 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
                 int sr;
                 bool ok;
                 if (a.list == 0) {
-                    xy0 = a.ev_xy[r]; sr = r; ok = (a.rflags[r] & F_VALID) != 0;
+                    xy0 = a.ev_xy[r]; sr = r; ok = (a.rflags[r] & (F_VALID | F_FOREIGN)) == F_VALID;
                 } else {
                     const StageEntry se = a.E[r];
-                    xy0 = se.xy0; sr = a.second ? se.kprev : r; ok = true;
+                    xy0 = se.xy0; sr = a.second ? se.kprev : r; ok = (a.rflags[se.e] & F_FOREIGN) == 0;
                 }
                 const int cx = static_cast<int>(xy0 & 0xFFFFu) >> s, cy = static_cast<int>(xy0 >> 16) >> s;
                 if (A == 9) ok = ok && cx + dx >= 0 && cx + dx < Wl && cy + dy >= 0 && cy + dy < Hl;
@@ -1258,10 +1258,10 @@ __global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 
             uint32_t xy0 = 0;
             if (r < n_list) {
                 if (a.list == 0) {
-                    xy0 = a.ev_xy[r]; sr = r; e = r; ok = (a.rflags[r] & F_VALID) != 0;
+                    xy0 = a.ev_xy[r]; sr = r; e = r; ok = (a.rflags[r] & (F_VALID | F_FOREIGN)) == F_VALID;
                 } else {
                     const StageEntry se = a.E[r];
-                    xy0 = se.xy0; sr = a.second ? se.kprev : r; e = se.e; ok = 1;
+                    xy0 = se.xy0; sr = a.second ? se.kprev : r; e = se.e; ok = (a.rflags[e] & F_FOREIGN) == 0;
                 }
             }
             ev_r[tid] = r; ev_sr[tid] = sr; ev_e[tid] = e; ev_ok[tid] = static_cast<unsigned char>(ok);

@@ -199,6 +199,7 @@ struct StripXferArgs {
 };
 
 void launch_band_select(cudaStream_t st, const StripSelectArgs& a);
+void launch_mark_foreign(cudaStream_t st, int n, const uint32_t* ev_xy, uint8_t* rflags, int lo, int hi);
 void launch_strip_export(cudaStream_t st, const StripXferArgs& a);
 void launch_strip_import(cudaStream_t st, const StripXferArgs& a);
 

@@ -150,7 +150,22 @@ __global__ void __launch_bounds__(256) k_strip_import(StripXferArgs a) {
     }
 }
 
+// Events outside the strip's own rows (its neighbours' band events): their
+// outputs are the neighbours' to compute, so contributions and LayerNorm
+// skip them.
+__global__ void k_mark_foreign(int n, const uint32_t* __restrict__ ev_xy, uint8_t* __restrict__ rflags, int lo,
+                               int hi) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int y = static_cast<int>(ev_xy[i] >> 16);
+        if ((rflags[i] & F_VALID) && (y < lo || y >= hi)) rflags[i] |= F_FOREIGN;
+    }
+}
+
 }  // namespace
+
+void launch_mark_foreign(cudaStream_t st, int n, const uint32_t* ev_xy, uint8_t* rflags, int lo, int hi) {
+    if (n > 0) k_mark_foreign<<<(n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184, 256, 0, st>>>(n, ev_xy, rflags, lo, hi);
+}
 
 void launch_band_select(cudaStream_t st, const StripSelectArgs& a) {
     k_band_select<<<3, kSelNT, 0, st>>>(a);

@@ -2,7 +2,8 @@
 inputs of their boundary-band events after every layer give, for the events
 and cells each strip owns, exactly the single-sensor engine's results --
 flags, hidden state of every stage, gate counters, predictions and
-versions -- across consecutive drains.  The strips share one GPU here and
+versions -- across consecutive drains, including drains where some strips
+have no events.  The strips share one GPU here and
 run in lockstep (ssla_strip_drain_lockstep); across GPUs the same steps
 wait for the neighbours' rows on the device."""
 import numpy as np
@@ -29,8 +30,9 @@ def test_exact_strips_lockstep(stub_dir, n_strips, window):
     from ssla_rt_b200.engine import SslaEngine, strip_drain_lockstep
     H, W = 256, 320
     d = stub_dir(H, W, 1, window)
-    ev = E.make_events(160_000, H, W, rate_mev=20.0, seed=11, n_blobs=16, blob_frac=0.7, sigma=4.0)
-    chunks = [ev[:90_000], ev[90_000:]]
+    ev = E.make_events(180_000, H, W, rate_mev=20.0, seed=11, n_blobs=16, blob_frac=0.7, sigma=4.0)
+    late = ev[160_000:]
+    chunks = [ev[:90_000], ev[90_000:160_000], late[late[:, 2] < 40]]    # the last: most strips empty
     full = SslaEngine(d, n_partitions=1, max_events=90_000, layout=abi.LAYOUT_HYBRID)
     bounds = strips.strip_bounds(H, n_strips)
     engs = []
