@@ -266,6 +266,8 @@ int  ssla_strip_drain_lockstep(SslaEngine* const* engines, int k, const float* c
 int  ssla_engine_strip_status(SslaEngine* eng, unsigned* status);
 
 int  ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes);
+/* partition -1 (kinds HIDDEN .. VERSION): every partition's buffer back to
+ * back, in partition order, in one copy. */
 int  ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index,
                             void* host_dst, size_t bytes);
 int  ssla_engine_write_state(SslaEngine* eng, int kind, int partition, int index,

@@ -1369,7 +1369,9 @@ int ssla_engine_state_bytes(SslaEngine* eng, int kind, int index, size_t* bytes)
 
 static int state_args_ok(SslaEngine* eng, int kind, int partition, int index) {
     if (!eng) return 0;
-    if (partition < 0 || partition >= eng->e.g.P) return 0;
+    // partition -1: every partition's buffer of a per-partition state kind, back to back
+    const bool all = partition == -1 && kind <= SSLA_STATE_VERSION;
+    if (!all && (partition < 0 || partition >= eng->e.g.P)) return 0;
     if (kind == SSLA_STATE_HIDDEN && (index < 0 || index > 7)) return 0;
     if (kind == SSLA_STATE_COUNTER && (index < 0 || index > 3)) return 0;
     if (kind == SSLA_STATE_STAGE_OUT && (index < 0 || index > 3 || !eng->e.record)) return 0;
@@ -1385,10 +1387,12 @@ int ssla_engine_read_state(SslaEngine* eng, int kind, int partition, int index, 
     return ssla::guarded([&] {
         ssla::Engine& e = eng->e;
         ssla::DeviceGuard dg(e.device);
-        const size_t full = e.state_elems(kind, index) * ssla::Engine::elem_size(kind);
+        const size_t full = e.state_elems(kind, index) * ssla::Engine::elem_size(kind) *
+                            (partition < 0 ? static_cast<size_t>(e.g.P) : 1u);
         if (bytes > full) throw std::invalid_argument("read larger than the state buffer");
         SSLA_CK(cudaDeviceSynchronize());
-        SSLA_CK(cudaMemcpy(host_dst, e.state_ptr(kind, partition, index), bytes, cudaMemcpyDeviceToHost));
+        SSLA_CK(cudaMemcpy(host_dst, e.state_ptr(kind, partition < 0 ? 0 : partition, index), bytes,
+                           cudaMemcpyDeviceToHost));
         return SSLA_OK;
     });
 }

@@ -288,6 +288,14 @@ class SslaEngine:
     def preds_dec(self, partition: int = 0) -> np.ndarray:
         return self._read(abi.STATE_PREDS_DEC, partition, 0, np.float32).reshape(-1, 5 + self.ncls)
 
+    def preds_dec_all(self) -> np.ndarray:
+        """Decoded predictions of every partition, (P, cells, 5+ncls), one copy."""
+        nb = C.c_size_t()
+        _check(self.lib.ssla_engine_state_bytes(self.h, abi.STATE_PREDS_DEC, 0, C.byref(nb)))
+        out = np.empty((self.n_partitions, nb.value // 4 // (5 + self.ncls), 5 + self.ncls), dtype=np.float32)
+        _check(self.lib.ssla_engine_read_state(self.h, abi.STATE_PREDS_DEC, -1, 0, out.ctypes.data, out.nbytes))
+        return out
+
     def preds_raw(self, partition: int = 0) -> np.ndarray:
         return self._read(abi.STATE_PREDS_RAW, partition, 0, np.float32).reshape(-1, 5 + self.ncls)
 
