@@ -166,10 +166,10 @@ class ClockSampler:
 # CPU baseline: the reference's own SslaSPipeline (oracle/_ref), else the
 # C restatement (oracle/), same 8 independent streams, host threads.
 # ---------------------------------------------------------------------------
-def cpu_baseline(parts, weights_dir: str, reps: int = 3) -> dict:
+def cpu_baseline(parts, weights_dir: str, reps: int = 3, threads: int = 0, sample: str = "") -> dict:
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
-    threads = min(len(parts), os.cpu_count() or 1)
+    threads = min(len(parts), threads or os.cpu_count() or 1)
     n = sum(len(p) for p in parts)
     single = None
     if os.path.exists(O.REF_SO):
@@ -191,8 +191,8 @@ def cpu_baseline(parts, weights_dir: str, reps: int = 3) -> dict:
         best = time.perf_counter() - t0
         kind = "port"
     return {"value": n / best / 1e6, "unit": "Mev/s", "cores": threads, "kind": kind,
-            "sample": f"the full step workload: {len(parts)} independent streams x "
-                      f"{len(parts[0])} events, one host thread per stream, best of {reps}",
+            "sample": (sample or f"the full step workload: {len(parts)} independent streams x "
+                                 f"{len(parts[0])} events, one host thread per stream") + f", best of {reps}",
             "single_thread": single}
 
 
@@ -492,6 +492,230 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Config 4: 64 independent 80x64 camera streams, each through its own pinned
+# ring; stream s on rank s % N
+# ---------------------------------------------------------------------------
+N_STREAMS = 64
+STREAM_EVENTS = 1_000_000
+STREAM_RING = 1 << 16            # ring slots per stream
+STREAM_DRAIN = 1 << 18           # events per drain of a rank, split evenly over its rings
+STREAM_CPU_SAMPLE = 20_000       # events per stream in the CPU baseline
+STREAM_LOG = 100_000             # drains logged per serve
+
+
+def _pct(a: np.ndarray, q: float):
+    return float(np.percentile(a, q)) if len(a) else None
+
+
+def run_streams(args, rank: int, world: int, local: int) -> int:
+    """Config 4.  Each rank serves its streams (s = rank, rank + N, ...), one
+    ring and one engine partition per stream.
+
+    value   = device-resident drains of STREAM_DRAIN events (STREAM_DRAIN / P
+              from each of the rank's P streams, consecutive slices of the
+              streams), CUDA-event time, max over ranks, L2 flushed between.
+    e2e     = the whole job through the rings: the replay producer publishes
+              every stream's 1,000,000 events as fast as ring space allows,
+              ssla_engine_serve_rings drains them (ring slots read from
+              pinned host memory, flags and head-event rows written back) --
+              all streams' events / the slowest rank's wall time.
+    latency = the same job replayed in real time (2 Mev/s per stream, every
+              event published at its timestamp): emit (the event's due time)
+              to the host seeing its drain complete, p50 / p99 over all
+              events and over head events."""
+    import torch
+    import torch.distributed as dist
+    import concurrent.futures as cf
+    from datetime import timedelta
+
+    from ssla_rt_b200 import abi, stub
+    from ssla_rt_b200 import events as ev_gen
+    from ssla_rt_b200.engine import SslaEngine, measure_fp32_peak
+    from ssla_rt_b200.rings import Replay, RingSet
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    wdir = tempfile.mkdtemp(prefix="ssla_stub_")
+    stub.write_stub(wdir, h=H, w=W, seed=1, tdrop=4)
+    mine = list(range(rank, N_STREAMS, world))
+    P = len(mine)
+    per_ring = STREAM_DRAIN // P
+    with cf.ThreadPoolExecutor(min(8, os.cpu_count() or 1)) as ex:
+        streams = list(ex.map(lambda s: ev_gen.config_events(4, stream=s), mine))
+    eng = SslaEngine(wdir, n_partitions=P, max_events=per_ring * P, layout=abi.LAYOUT_HYBRID,
+                     device=local, max_events_per_partition=per_ring)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def reduce(vals, op):
+        if world == 1:
+            return list(vals)
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op)
+        return [float(x) for x in t.tolist()]
+
+    # ---- (1) device-resident drains ----
+    dev_all = torch.from_numpy(np.stack(streams)).to(dev)            # [P, 1M, 4]
+    n_slices = STREAM_EVENTS // per_ring
+    span = float(max(s[:, 0].max() for s in streams)) + 1.0
+    off = eng.offsets([per_ring] * P)
+
+    def batch(b: int):
+        i0 = (b % n_slices) * per_ring
+        x = dev_all[:, i0:i0 + per_ring].reshape(-1, 4).clone()
+        x[:, 0] += span * (b // n_slices)
+        return x
+
+    for b in range(args.warmup):
+        eng.drain(batch(b), off, stream=stream)
+    torch.cuda.synchronize(dev)
+    eng.set_profiling(True)
+    phase_acc, flops_acc, step_ms = {}, {}, []
+    flags_dev = torch.zeros(per_ring * P, dtype=torch.uint8, device=dev)
+    clocks = ClockSampler()
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    for k in range(args.steps):
+        x = batch(args.warmup + k)
+        flush.fill_(float(k))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        eng.drain(x, off, flags=flags_dev, stream=stream)
+        b.record(stream)
+        b.synchronize()
+        step_ms.append(a.elapsed_time(b))
+        macs = algorithmic_macs(x.cpu().numpy(), flags_dev.cpu().numpy())
+        for name, ms, nl in eng.phase_times():
+            acc = phase_acc.setdefault(name, [0.0, 0])
+            acc[0] += ms
+            acc[1] += 1
+            flops_acc[name] = flops_acc.get(name, 0.0) + phase_flops(macs, name)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop(local)
+    eng.set_profiling(False)
+    launches = eng.info().launches * args.steps
+    my_ms = sum(step_ms)
+    total_ms = reduce([my_ms], dist.ReduceOp.MAX if world > 1 else None)[0]
+    step_events = reduce([per_ring * P * args.steps], dist.ReduceOp.SUM if world > 1 else None)[0]
+    value = step_events / (total_ms * 1e-3) / 1e6
+    head_frac = float((flags_dev.cpu().numpy() & abi.F_R4).astype(bool).mean())
+    del dev_all
+    fp32_peak = measure_fp32_peak(local)
+    dom_name, (dom_ms_sum, dom_n) = max(phase_acc.items(), key=lambda kv: kv[1][0])
+    achieved = flops_acc[dom_name] / (dom_ms_sum * 1e-3) / 1e12 if flops_acc.get(dom_name) else None
+    roofline = {
+        "kernel": dom_name, "bound": "fp32", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+        "frac": (achieved / fp32_peak) if (achieved and fp32_peak) else None,
+        "traffic": None,
+        "peak_source": "measured FFMA peak (ssla_measure_fp32_peak, this run)",
+        "avg_ms": dom_ms_sum / dom_n, "algorithmic_flops_per_launch": flops_acc.get(dom_name, 0.0) / dom_n,
+        "share_of_step": dom_ms_sum / my_ms,
+    }
+
+    # ---- (2) e2e: the whole job through the rings, as fast as they drain ----
+    rings = RingSet(P, STREAM_RING, cols=5 + eng.ncls)
+    total_events = P * STREAM_EVENTS
+
+    def serve(time_scale: float, hist=None):
+        eng.reset(stream)
+        torch.cuda.synchronize(dev)
+        eng.rings_attach(rings)
+        barrier()
+        rp = Replay(rings, streams, time_scale=time_scale)
+        try:
+            out = eng.serve_rings(per_ring, total_events, idle_timeout_ms=10_000, log_cap=STREAM_LOG,
+                                  flags_hist=hist)
+        finally:
+            rp.stop()
+            st = rp.join()
+        if out["served"] != total_events or st["published"] != total_events or out["drains"] > STREAM_LOG:
+            raise RuntimeError(f"rank {rank}: served {out['served']} / published {st['published']} "
+                               f"of {total_events} in {out['drains']} drains")
+        return out, st
+
+    out, st = serve(0.0)
+    wall_s = (int(out["done_ns"][-1]) - st["start_ns"]) * 1e-9
+    e2e_s = reduce([wall_s], dist.ReduceOp.MAX if world > 1 else None)[0]
+    all_events = reduce([total_events], dist.ReduceOp.SUM if world > 1 else None)[0]
+    e2e = all_events / e2e_s / 1e6
+    drains = out["drains"]
+    per_drain = total_events / drains
+
+    # ---- (3) real-time replay: emit -> prediction latency ----
+    hist = [np.zeros(STREAM_EVENTS, np.uint8) for _ in range(P)]
+    out, st = serve(1.0, hist)
+    cum = np.cumsum(out["taken"], axis=0)
+    lat_all, lat_head = [], []
+    for r, ev in enumerate(streams):
+        k = np.searchsorted(cum[:, r], np.arange(len(ev)), side="right")
+        lat = (out["done_ns"][k].astype(np.float64) - (st["start_ns"] + ev[:, 0].astype(np.float64) * 1000.0)) / 1e3
+        lat_all.append(lat)
+        lat_head.append(lat[(hist[r] & abi.F_R4) != 0])
+    lat_all = np.concatenate(lat_all)
+    lat_head = np.concatenate(lat_head)
+    paced_s = (int(out["done_ns"][-1]) - st["start_ns"]) * 1e-9
+    lat_vals = reduce([_pct(lat_all, 50), _pct(lat_all, 99), _pct(lat_head, 50), _pct(lat_head, 99),
+                       st["max_lag_ns"] / 1e3, paced_s], dist.ReduceOp.MAX if world > 1 else None)
+    latency = {"p50": lat_vals[0], "p99": lat_vals[1], "head_p50": lat_vals[2], "head_p99": lat_vals[3],
+               "n": int(len(lat_all)) * world, "head_events": int(len(lat_head)),
+               "producer_max_lag_us": lat_vals[4], "paced_wall_s": lat_vals[5],
+               "paced_mev_s": all_events / lat_vals[5] / 1e6, "drains": out["drains"],
+               "method": "real-time replay (ssla_replay_*: each event published at its timestamp, 2 Mev/s per "
+                         "stream) into pinned rings served by ssla_engine_serve_rings; latency = host "
+                         "CLOCK_MONOTONIC when the drain holding the event is seen complete (its flags and "
+                         "prediction rows written back to the ring) minus the event's due time; max over ranks"}
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            sample = [ev_gen.config_events(4, stream=s, n=STREAM_CPU_SAMPLE) for s in range(N_STREAMS)]
+            cpu = cpu_baseline(sample, wdir, reps=1, threads=os.cpu_count() or 1,
+                               sample=f"the first {STREAM_CPU_SAMPLE:,} events of each of the {N_STREAMS} "
+                                      "streams, independent pipelines over all host threads")
+        line = {
+            "metric": METRIC, "value": value, "unit": "Mev/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"config4: {N_STREAMS} independent 80x64 streams x {STREAM_EVENTS:,} events "
+                                   "(50% uniform / 50% 4 moving blobs sigma 3, Poisson 2 Mev/s each), stream s on "
+                                   "GPU s % N, each through its own pinned ring; full s0..s3 + YOLOX head",
+                       "model": "SSLA-S stub (tools/make_ssla_stub.py schema, seed 1, tdrop 4)",
+                       "streams_per_gpu": P, "events_per_step": per_ring * P,
+                       "step": f"one drain of {per_ring} events from each of the GPU's {P} streams",
+                       "ring_slots": STREAM_RING,
+                       "l2": "flushed between steps (256 MiB write, untimed)",
+                       "parallelism": f"streams over {world} GPU(s), no collective on the data path"},
+            "clocks": clk,
+            "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(16 * per_drain),
+                    "d2h_bytes_per_step": int(per_drain * (1 + head_frac * 4 * (5 + eng.ncls))),
+                    "events": int(all_events), "wall_s": e2e_s, "drains_per_gpu": drains,
+                    "method": "replay producer at full speed into pinned rings, ssla_engine_serve_rings until "
+                              "every stream is drained; slowest rank's wall time"},
+            "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
+            "latency_us": latency,
+            "phase_ms": {k: round(v[0] / v[1], 4) for k, v in sorted(phase_acc.items(), key=lambda kv: -kv[1][0])},
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -500,9 +724,10 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true", help="skip the batch-of-1 latency samples")
-    ap.add_argument("--workload", default="config1", choices=["config1", "strips"],
+    ap.add_argument("--workload", default="config1", choices=["config1", "strips", "streams"],
                     help="config1: 80x64 partitions per GPU (weak scaling); strips: config 3, one "
-                         "320x256 stream in horizontal strips across the GPUs (strong scaling)")
+                         "320x256 stream in horizontal strips across the GPUs (strong scaling); "
+                         "streams: config 4, 64 camera streams through pinned rings spread over the GPUs")
     ap.add_argument("--strip-mode", default="exact", choices=["exact", "halo"],
                     help="strips: exact per-layer band exchange (default) or halo replication")
     ap.add_argument("--halo-rows", type=int, default=16, help="strips, halo mode: halo in stage-0 rows (multiple of 8)")
@@ -516,6 +741,8 @@ def main() -> int:
         return 0
     if args.workload == "strips":
         return run_strips(args, rank, world, local)
+    if args.workload == "streams":
+        return run_streams(args, rank, world, local)
 
     import torch
     import torch.distributed as dist

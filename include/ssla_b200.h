@@ -193,6 +193,76 @@ int  ssla_engine_live_join(SslaEngine* eng, unsigned* status);
 int  ssla_engine_live_latency(SslaEngine* eng, int partition, const float* events_host, int n,
                               double* latency_us, uint8_t* flags_out, float* preds_out);
 
+/* Ring drains: one pinned SslaLiveRing per partition -- independent event
+ * streams (camera streams, ring partitions), each with its own producer --
+ * drained together by the chunk path.  The reference's shard workers feed
+ * GPU rings that its persistent kernel drains in ring order
+ * (src/lib_stage01_to_gpu.cpp:157-311, ssla_s2_s3_head_celled.cuh:
+ * 1547-1784); here the rings carry raw events and every stage runs on the
+ * GPU.  stop_flag is not used.  Attach once (synchronises the device); each
+ * ring's tail at attach is where draining starts. */
+int  ssla_engine_rings_attach(SslaEngine* eng, const SslaLiveRing* rings, int n_rings);
+
+/* One ring drain on `stream`: takes, from every ring, up to max_per_ring of
+ * its published events (head read with acquire; at most max_total events in
+ * all, and within max_events / max_events_per_partition), copies them from
+ * the rings into the device (releasing each ring's tail once copied), runs
+ * the full path over them and then writes each event's SSLA_F_* bits into
+ * flags[index & (capacity-1)] and each head event's decoded prediction row
+ * into preds[index & (capacity-1)] (either may be NULL) before releasing
+ * events_done.  *n_taken receives the events taken (0: nothing published);
+ * taken (may be NULL, n_partitions ints) each ring's share.  Asynchronous. */
+int  ssla_engine_drain_rings(SslaEngine* eng, int max_per_ring, long long max_total, int* taken,
+                             int* n_taken, void* stream);
+
+/* Per-drain record of ssla_engine_serve_rings. */
+typedef struct SslaServeLog {
+    unsigned long long* done_ns;    /* [cap] CLOCK_MONOTONIC ns when drain k was seen complete, or NULL */
+    int* taken;                     /* [cap][n_partitions] events of each ring in drain k, or NULL      */
+    int cap;                        /* entries of done_ns / taken                                        */
+    int n;                          /* out: entries written, min(drains, cap)                            */
+    int drains;                     /* out: drains completed                                              */
+    uint8_t* const* flags_hist;     /* [n_partitions] arrays receiving each drained event's flags at
+                                       (ring index - the ring's tail at attach), or NULL                  */
+    unsigned long long hist_len;    /* length of each flags_hist array                                    */
+} SslaServeLog;
+
+/* Serves the rings until `total` events have been drained, or until
+ * idle_timeout_ms passes with nothing published and nothing in flight:
+ * each drain is formed (ssla_engine_drain_rings) while the previous one
+ * runs, and is logged when it completes.  *served receives the events
+ * drained.  Synchronises `stream`. */
+int  ssla_engine_serve_rings(SslaEngine* eng, int max_per_ring, unsigned long long total,
+                             unsigned idle_timeout_ms, SslaServeLog* log, unsigned long long* served,
+                             void* stream);
+
+/* Paced replay producer: a host thread that publishes each stream's events
+ * into its ring at their timestamps -- event i (t_i microseconds) of ring r
+ * is due at start_ns + t_i * 1000 * time_scale on CLOCK_MONOTONIC; with
+ * time_scale 0 every event is due at start_ns and only ring space paces
+ * the thread.  Slots are written, then head is release-stored; free space is
+ * read from tail (acquire).  The synthetic producer of the reference
+ * (s01g_start_synthetic, src/lib_stage01_to_gpu.cpp:637-672) draws random
+ * events at a rate; this one replays given streams, so the same events can
+ * be checked against the oracle.  Host-only; the arrays must stay valid
+ * until ssla_replay_join.  start_ns 0 = 2 ms after the call.  NULL on bad
+ * arguments (ssla_last_error). */
+typedef struct SslaReplay SslaReplay;
+typedef struct SslaReplayStats {
+    unsigned long long published;   /* events published                                        */
+    unsigned long long start_ns;    /* event time 0 on CLOCK_MONOTONIC                          */
+    long long max_lag_ns;           /* latest publish after its due time (pacing or full rings) */
+    unsigned long long full_waits;  /* rounds in which a due event found its ring full          */
+} SslaReplayStats;
+SslaReplay* ssla_replay_start(const SslaLiveRing* rings, int n_rings, const float* const* events,
+                              const unsigned long long* counts, double time_scale,
+                              unsigned long long start_ns);
+/* Asks the thread to stop early (it ends after its current round). */
+void ssla_replay_stop(SslaReplay* rp);
+/* Waits for the thread (every event published, or stopped), fills *stats
+ * (may be NULL) and frees the handle. */
+int  ssla_replay_join(SslaReplay* rp, SslaReplayStats* stats);
+
 /* Stages 0-1 only (HYBRID layout): preprocess, gates 0-1, layers 0-3 for
  * every event (state of stages 0-1 advances), and one HybridInputRec per
  * event that passed gate 1 -- t, stage-2 x / y, feat1 = the stage-1 output;

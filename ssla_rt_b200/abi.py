@@ -80,6 +80,18 @@ class SslaLiveRing(C.Structure):
                 ("preds", C.c_void_p), ("stop_flag", C.c_void_p)]
 
 
+class SslaServeLog(C.Structure):
+    """include/ssla_b200.h SslaServeLog: per-drain record of ssla_engine_serve_rings."""
+    _fields_ = [("done_ns", C.c_void_p), ("taken", C.c_void_p), ("cap", C.c_int), ("n", C.c_int),
+                ("drains", C.c_int), ("flags_hist", C.c_void_p), ("hist_len", C.c_uint64)]
+
+
+class SslaReplayStats(C.Structure):
+    """include/ssla_b200.h SslaReplayStats."""
+    _fields_ = [("published", C.c_uint64), ("start_ns", C.c_uint64), ("max_lag_ns", C.c_int64),
+                ("full_waits", C.c_uint64)]
+
+
 # SSLA_LIVE_* status bits
 LIVE_ERR_WEIGHTS, LIVE_ERR_INPUT, LIVE_ERR_CONTRIB, LIVE_ERR_EVENT, LIVE_ERR_DONE = 1, 2, 4, 8, 16
 LIVE_EXIT_STOP, LIVE_EXIT_IDLE = 0x100, 0x200
@@ -108,6 +120,8 @@ EXPORTED = (
     "ssla_engine_set_owned", "ssla_write_oracle_dump", "ssla_engine_oracle_dump",
     "ssla_engine_strip_init", "ssla_engine_strip_recv_buffer", "ssla_engine_strip_connect",
     "ssla_engine_strip_drain", "ssla_strip_drain_lockstep", "ssla_engine_strip_status",
+    "ssla_engine_rings_attach", "ssla_engine_drain_rings", "ssla_engine_serve_rings",
+    "ssla_replay_start", "ssla_replay_stop", "ssla_replay_join",
 )
 # SSLA_STRIP_ERR_* bits
 STRIP_ERR_CAPACITY, STRIP_ERR_TIMEOUT, STRIP_ERR_MISMATCH = 1, 2, 4

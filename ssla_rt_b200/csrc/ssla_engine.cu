@@ -16,6 +16,8 @@
 #include <stdexcept>
 #include <string>
 #include <chrono>
+#include <thread>
+#include <time.h>
 #include <vector>
 
 #include "ssla_b200.h"
@@ -761,6 +763,204 @@ struct Engine {
         return v;
     }
 
+    // ---- ring drains (ssla_rings.cu): one pinned ring per partition ----
+    struct Rings {
+        static constexpr int kSlots = 4;
+        std::vector<SslaLiveRing> r;
+        std::vector<unsigned long long> next;    // ring index after every enqueued take
+        std::vector<unsigned long long> first;   // ring index at attach
+        std::vector<int> off;
+        RingTake* pinned = nullptr;              // [kSlots][P] staging of the take descriptors
+        DevBuf dev[kSlots];
+        cudaEvent_t copied[kSlots] = {};
+        int slot = 0;
+        DevBuf ctr;
+        ~Rings() {
+            for (auto& e : copied)
+                if (e) cudaEventDestroy(e);
+            if (pinned) cudaFreeHost(pinned);
+        }
+    } rings;
+
+    void rings_attach(const SslaLiveRing* rr, int n) {
+        if (n != g.P) throw std::invalid_argument("rings_attach needs one ring per partition");
+        if (live_running) throw std::invalid_argument("a live loop is running on this engine");
+        const size_t cols = 5 + static_cast<size_t>(g.ncls);
+        for (int p = 0; p < n; ++p) {
+            const SslaLiveRing& r = rr[p];
+            if (r.capacity < 2 || (r.capacity & (r.capacity - 1)))
+                throw std::invalid_argument("ring capacity must be a power of two >= 2");
+            if (reinterpret_cast<uintptr_t>(r.events) % 16) throw std::invalid_argument("ring events must be 16-byte aligned");
+            need_mapped(r.events, 16 * r.capacity, "events");
+            need_mapped(r.head, 8, "head");
+            need_mapped(r.tail, 8, "tail");
+            need_mapped(r.events_done, 8, "events_done");
+            if (r.flags) need_mapped(r.flags, r.capacity, "flags");
+            if (r.preds) need_mapped(r.preds, sizeof(float) * cols * r.capacity, "preds");
+        }
+        SSLA_CK(cudaDeviceSynchronize());        // no drain in flight reads the old descriptors
+        rings.r.assign(rr, rr + n);
+        rings.next.resize(n);
+        rings.first.resize(n);
+        for (int p = 0; p < n; ++p) rings.next[p] = rings.first[p] = __atomic_load_n(rr[p].tail, __ATOMIC_ACQUIRE);
+        rings.off.assign(n + 1, 0);
+        if (!rings.pinned) {
+            SSLA_CK(cudaMallocHost(&rings.pinned, sizeof(RingTake) * Rings::kSlots * n));
+            for (int k = 0; k < Rings::kSlots; ++k) {
+                rings.dev[k].alloc(sizeof(RingTake) * n);
+                SSLA_CK(cudaEventCreateWithFlags(&rings.copied[k], cudaEventDisableTiming));
+            }
+            rings.ctr.alloc(sizeof(unsigned));
+            SSLA_CK(cudaMemset(rings.ctr.p, 0, sizeof(unsigned)));
+        }
+    }
+
+    // Takes up to max_per_ring published events from every ring (at most
+    // max_total in all) and drains them; returns the number taken, taken[p]
+    // (may be null) the share of ring p.  Asynchronous on st.
+    int drain_rings(int max_per_ring, long long max_total, cudaStream_t st, int* taken) {
+        if (rings.r.empty()) throw std::invalid_argument("ssla_engine_rings_attach first");
+        if (max_per_ring < 1) throw std::invalid_argument("max_per_ring must be >= 1");
+        const int P = g.P;
+        std::vector<int>& off = rings.off;
+        long long budget = std::min<long long>(max_total, max_events);
+        off[0] = 0;
+        for (int p = 0; p < P; ++p) {
+            const SslaLiveRing& r = rings.r[p];
+            const unsigned long long h = __atomic_load_n(r.head, __ATOMIC_ACQUIRE);
+            const unsigned long long t = rings.next[p];
+            if (h < t || h - t > r.capacity)
+                throw std::runtime_error("ring " + std::to_string(p) + ": head outside [tail, tail + capacity]");
+            const long long n = std::max(0LL, std::min({static_cast<long long>(h - t), static_cast<long long>(max_per_ring),
+                                                        static_cast<long long>(mpe), budget}));
+            budget -= n;
+            off[p + 1] = off[p] + static_cast<int>(n);
+        }
+        const int total = off[P];
+        if (taken)
+            for (int p = 0; p < P; ++p) taken[p] = off[p + 1] - off[p];
+        if (total == 0) return 0;
+        const int slot = rings.slot;
+        rings.slot = (slot + 1) % Rings::kSlots;
+        SSLA_CK(cudaEventSynchronize(rings.copied[slot]));
+        RingTake* tk = rings.pinned + static_cast<size_t>(slot) * P;
+        for (int p = 0; p < P; ++p) {
+            const SslaLiveRing& r = rings.r[p];
+            tk[p] = RingTake{reinterpret_cast<const float4*>(r.events), r.capacity - 1, rings.next[p], r.tail,
+                             r.events_done, r.flags, r.preds, off[p], off[p + 1] - off[p]};
+        }
+        SSLA_CK(cudaMemcpyAsync(rings.dev[slot].p, tk, sizeof(RingTake) * P, cudaMemcpyHostToDevice, st));
+        SSLA_CK(cudaEventRecord(rings.copied[slot], st));
+        RingArgs a{};
+        a.P = P; a.n_total = total; a.cols = 5 + g.ncls;
+        a.take = rings.dev[slot].as<RingTake>();
+        a.ev = ws.ev.as<float4>();
+        a.rflags = ws.rflags.as<uint8_t>();
+        a.E4 = ws.E[4].as<StageEntry>(); a.count4 = ws.count.as<int>() + 4; a.cap4 = g.cap[4];
+        a.head_dec = ws.head_dec.as<float>();
+        a.ctr = rings.ctr.as<unsigned>();
+        launch_ring_gather(st, a);
+        check_launch("k_ring_gather");
+        for (int p = 0; p < P; ++p) rings.next[p] += static_cast<unsigned long long>(off[p + 1] - off[p]);
+        drain(ws.ev.as<float>(), off.data(), nullptr, st);
+        launch_ring_scatter(st, a);
+        check_launch("k_ring_scatter");
+        prof.launches += 2;
+        return total;
+    }
+
+    static unsigned long long mono_ns() {
+        timespec ts;
+        clock_gettime(CLOCK_MONOTONIC, &ts);
+        return static_cast<unsigned long long>(ts.tv_sec) * 1000000000ull + static_cast<unsigned long long>(ts.tv_nsec);
+    }
+
+    // Serves the rings until `total` events have been drained or idle_ms
+    // passes with nothing published and nothing in flight.  Each drain is
+    // formed while the previous one runs; when a drain completes its time
+    // and per-ring shares are logged and its events' flags copied out.
+    unsigned long long serve_rings(int max_per_ring, unsigned long long total, unsigned idle_ms, SslaServeLog* log,
+                                   cudaStream_t st) {
+        if (rings.r.empty()) throw std::invalid_argument("ssla_engine_rings_attach first");
+        const int P = g.P;
+        struct Drain {
+            std::vector<unsigned long long> base;
+            std::vector<int> n;
+            int total = 0;
+            cudaEvent_t ev = nullptr;
+        } dr[2];
+        for (auto& d : dr) {
+            d.base.resize(P);
+            d.n.resize(P);
+            SSLA_CK(cudaEventCreateWithFlags(&d.ev, cudaEventDisableTiming));
+        }
+        struct EvGuard {
+            Drain* d;
+            ~EvGuard() {
+                for (int k = 0; k < 2; ++k) cudaEventDestroy(d[k].ev);
+            }
+        } guard{dr};
+        if (log) { log->n = 0; log->drains = 0; }
+        unsigned long long taken = 0, done = 0;
+        int cur = 0;
+        bool prev = false;
+        unsigned long long last_new = mono_ns();
+        const unsigned long long idle = static_cast<unsigned long long>(idle_ms) * 1000000ull;
+        while (done < total) {
+            Drain& d = dr[cur];
+            int n = 0;
+            if (taken < total) {
+                d.base = rings.next;
+                n = drain_rings(max_per_ring, static_cast<long long>(total - taken), st, d.n.data());
+            }
+            if (n > 0) {
+                SSLA_CK(cudaEventRecord(d.ev, st));
+                d.total = n;
+                taken += static_cast<unsigned long long>(n);
+                last_new = mono_ns();
+            }
+            if (prev) {
+                Drain& q = dr[cur ^ 1];
+                SSLA_CK(cudaEventSynchronize(q.ev));
+                const unsigned long long t = mono_ns();
+                done += static_cast<unsigned long long>(q.total);
+                if (log) log_drain(*log, q.base, q.n, t);
+                prev = false;
+            }
+            if (n > 0) {
+                cur ^= 1;
+                prev = true;
+            } else if (!prev) {
+                if (mono_ns() - last_new > idle) break;
+                std::this_thread::yield();
+            }
+        }
+        return done;
+    }
+
+    void log_drain(SslaServeLog& log, const std::vector<unsigned long long>& base, const std::vector<int>& n,
+                   unsigned long long t) {
+        const int P = g.P;
+        const int k = log.drains++;
+        if (k < log.cap) {
+            if (log.done_ns) log.done_ns[k] = t;
+            if (log.taken)
+                for (int p = 0; p < P; ++p) log.taken[static_cast<size_t>(k) * P + p] = n[p];
+            log.n = k + 1;
+        }
+        if (!log.flags_hist) return;
+        for (int p = 0; p < P; ++p) {
+            const SslaLiveRing& r = rings.r[p];
+            uint8_t* h = log.flags_hist[p];
+            if (!h || !r.flags) continue;
+            for (int j = 0; j < n[p]; ++j) {
+                const unsigned long long idx = base[p] + static_cast<unsigned long long>(j);
+                const unsigned long long rel = idx - rings.first[p];
+                if (rel < log.hist_len) h[rel] = r.flags[idx & (r.capacity - 1)];
+            }
+        }
+    }
+
     // Stages 0-1 of every event and one ring record per event that passed
     // gate 1 (partition-major, stream order) into rec_dev; rec_off receives
     // the per-partition record offsets.  Synchronises `st`.
@@ -1182,6 +1382,38 @@ int ssla_engine_step_latency(SslaEngine* eng, int partition, const float* events
         cudaFreeHost(flag);
         cudaStreamDestroy(st);
         e.check_step_status();
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_rings_attach(SslaEngine* eng, const SslaLiveRing* rings, int n_rings) {
+    if (!eng || !rings) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.rings_attach(rings, n_rings);
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_drain_rings(SslaEngine* eng, int max_per_ring, long long max_total, int* taken, int* n_taken,
+                            void* stream) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        const int n = eng->e.drain_rings(max_per_ring, max_total, static_cast<cudaStream_t>(stream), taken);
+        if (n_taken) *n_taken = n;
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_serve_rings(SslaEngine* eng, int max_per_ring, unsigned long long total, unsigned idle_timeout_ms,
+                            SslaServeLog* log, unsigned long long* served, void* stream) {
+    if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        const unsigned long long n =
+            eng->e.serve_rings(max_per_ring, total, idle_timeout_ms, log, static_cast<cudaStream_t>(stream));
+        if (served) *served = n;
         return SSLA_OK;
     });
 }

@@ -198,6 +198,34 @@ struct StripXferArgs {
     unsigned* err;
 };
 
+// One ring's share of a ring drain (ssla_engine_drain_rings): events
+// [base, base + n) of the ring, chunk rows [off, off + n).
+struct RingTake {
+    const float4* events;         // ring slots (pinned host memory, device-mapped)
+    unsigned long long mask;      // capacity - 1
+    unsigned long long base;      // ring index of the first event taken
+    unsigned long long* tail;     // released after the slots are copied
+    unsigned long long* done;     // released after flags and prediction rows
+    uint8_t* flags;               // [capacity] or null
+    float* preds;                 // [capacity][cols] or null
+    int off, n;
+};
+
+struct RingArgs {
+    int P, n_total, cols;
+    const RingTake* take;         // [P], device copy
+    float4* ev;                   // chunk events (gather output)
+    const uint8_t* rflags;        // chunk event flags (scatter input)
+    const StageEntry* E4;         // head events of the chunk
+    const int* count4;
+    int cap4;
+    const float* head_dec;        // [cap4][cols]
+    unsigned* ctr;                // CTA completion counter, zero between launches
+};
+
+void launch_ring_gather(cudaStream_t st, const RingArgs& a);
+void launch_ring_scatter(cudaStream_t st, const RingArgs& a);
+
 void launch_band_select(cudaStream_t st, const StripSelectArgs& a);
 void launch_mark_foreign(cudaStream_t st, int n, const uint32_t* ev_xy, uint8_t* rflags, int lo, int hi);
 void launch_strip_export(cudaStream_t st, const StripXferArgs& a);

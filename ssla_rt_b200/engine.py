@@ -62,6 +62,13 @@ def load_library() -> C.CDLL:
         "ssla_engine_strip_drain": (i, [vp, vp, i, vp, vp]),
         "ssla_strip_drain_lockstep": (i, [vp, i, vp, vp, vp, vp]),
         "ssla_engine_strip_status": (i, [vp, C.POINTER(C.c_uint)]),
+        "ssla_engine_rings_attach": (i, [vp, vp, i]),
+        "ssla_engine_drain_rings": (i, [vp, i, C.c_longlong, vp, C.POINTER(i), vp]),
+        "ssla_engine_serve_rings": (i, [vp, i, C.c_uint64, C.c_uint, C.POINTER(abi.SslaServeLog),
+                                        C.POINTER(C.c_uint64), vp]),
+        "ssla_replay_start": (vp, [vp, i, vp, vp, C.c_double, C.c_uint64]),
+        "ssla_replay_stop": (None, [vp]),
+        "ssla_replay_join": (i, [vp, C.POINTER(abi.SslaReplayStats)]),
         "ssla_write_oracle_dump": (i, [C.c_char_p, i, i, i, vp, vp]),
         "ssla_engine_oracle_dump": (i, [vp, i, vp, i, i, C.c_char_p]),
         "ssla_s2s3_drain_n_multi": (i, [C.POINTER(abi.HybridS2S3Config), vp, vp, vp, vp, vp]),
@@ -249,6 +256,45 @@ class SslaEngine:
         _check(self.lib.ssla_engine_live_latency(self.h, partition, ev.ctypes.data, ev.shape[0],
                                                  lat.ctypes.data, fl.ctypes.data, pr.ctypes.data))
         return lat, fl, pr
+
+    def rings_attach(self, rings) -> None:
+        """One pinned ring per partition (a ``rings.RingSet``); draining
+        starts at each ring's current tail."""
+        if rings.n != self.n_partitions:
+            raise ValueError("one ring per partition")
+        self._rings = rings
+        _check(self.lib.ssla_engine_rings_attach(self.h, C.addressof(rings.descs), rings.n))
+
+    def drain_rings(self, max_per_ring: int, max_total: int = 1 << 62, stream=None) -> np.ndarray:
+        """One ring drain (asynchronous); returns each ring's share."""
+        taken = np.zeros(self.n_partitions, dtype=np.int32)
+        n = C.c_int(0)
+        _check(self.lib.ssla_engine_drain_rings(self.h, max_per_ring, max_total, taken.ctypes.data,
+                                                C.byref(n), _stream(stream)))
+        return taken
+
+    def serve_rings(self, max_per_ring: int, total: int, idle_timeout_ms: int = 2000, log_cap: int = 0,
+                    flags_hist: Optional[Sequence[np.ndarray]] = None, stream=None) -> dict:
+        """Drains the attached rings until ``total`` events are done (or idle);
+        returns {"served", "drains", "done_ns" [n], "taken" [n, P]} and fills
+        ``flags_hist`` (per ring, flags by ring index since attach)."""
+        P = self.n_partitions
+        done = np.zeros(max(log_cap, 1), dtype=np.uint64)
+        taken = np.zeros((max(log_cap, 1), P), dtype=np.int32)
+        log = abi.SslaServeLog(done.ctypes.data, taken.ctypes.data, log_cap, 0, 0, None, 0)
+        keep = None
+        if flags_hist is not None:
+            hl = len(flags_hist[0])
+            if len(flags_hist) != P or any(len(h) != hl or h.dtype != np.uint8 for h in flags_hist):
+                raise ValueError("flags_hist: one uint8 array per ring, all of one length")
+            keep = (C.c_void_p * P)(*[h.ctypes.data for h in flags_hist])
+            log.flags_hist = C.addressof(keep)
+            log.hist_len = hl
+        served = C.c_uint64(0)
+        _check(self.lib.ssla_engine_serve_rings(self.h, max_per_ring, total, idle_timeout_ms, C.byref(log),
+                                                C.byref(served), _stream(stream)))
+        return {"served": served.value, "drains": log.drains, "done_ns": done[:log.n].copy(),
+                "taken": taken[:log.n].copy()}
 
     def drain_records(self, events, part_offsets, records, records_cap: int, flags=None,
                       stream=None) -> np.ndarray:

@@ -69,22 +69,22 @@ def make_events(n: int, h: int, w: int, *, rate_mev: float, seed: int,
 def config_events(cfg: int, *, n: int | None = None, seed: int | None = None,
                   stream: int = 0) -> np.ndarray:
     if cfg == 0:
-        return make_events(n or 50_000, 64, 80, rate_mev=2.0,
+        return make_events(50_000 if n is None else n, 64, 80, rate_mev=2.0,
                            seed=0 if seed is None else seed)
     if cfg == 1:
-        return make_events(n or 200_000, 64, 80, rate_mev=2.0,
+        return make_events(200_000 if n is None else n, 64, 80, rate_mev=2.0,
                            seed=1 if seed is None else seed)
     if cfg == 2:
-        return make_events(n or 1_000_000, 64, 80, rate_mev=5.0,
+        return make_events(1_000_000 if n is None else n, 64, 80, rate_mev=5.0,
                            seed=2 if seed is None else seed, n_blobs=6,
                            blob_frac=0.9, sigma=3.0)
     if cfg == 3:
-        return make_events(n or 10_000_000, 256, 320, rate_mev=20.0,
+        return make_events(10_000_000 if n is None else n, 256, 320, rate_mev=20.0,
                            seed=3 if seed is None else seed, n_blobs=16,
                            blob_frac=0.7, sigma=4.0)
     if cfg == 4:
         base = 4000 if seed is None else seed
-        return make_events(n or 1_000_000, 64, 80, rate_mev=2.0,
+        return make_events(1_000_000 if n is None else n, 64, 80, rate_mev=2.0,
                            seed=base + stream, n_blobs=4, blob_frac=0.5,
                            sigma=3.0)
     raise ValueError(f"unknown config {cfg}")
