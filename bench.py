@@ -39,6 +39,7 @@ sys.path.insert(0, REPO)
 METRIC = "Mev/s drained (output events) at 1/2/4/8 B200; p50/p99 emit→prediction µs"
 N_EVENTS = 200_000
 N_PARTS = 8
+WL_CFG = 1                       # BASELINE config of the default workload
 H, W = 64, 80
 CHANS = (12, 24, 48, 96)
 LAYER_DIMS = ((2, 12, 1), (12, 12, 9), (12, 24, 9), (24, 24, 9), (24, 48, 9), (48, 48, 9),
@@ -47,8 +48,15 @@ LAYER_DIMS = ((2, 12, 1), (12, 12, 9), (12, 24, 9), (24, 24, 9), (24, 48, 9), (4
 
 def workload(rank: int):
     from ssla_rt_b200 import events
-    ev = events.config_events(1, seed=1 + 1000 * rank)
+    ev = events.config_events(WL_CFG, seed=WL_CFG + 1000 * rank)
     return events.split_partitions(ev, N_PARTS)
+
+
+def use_config2() -> None:
+    """Config 2 in place of config 1: one stream of 1,000,000 clustered
+    events at 80x64 per step."""
+    global N_EVENTS, N_PARTS, WL_CFG
+    N_EVENTS, N_PARTS, WL_CFG = 1_000_000, 1, 2
 
 
 # ---------------------------------------------------------------------------
@@ -292,8 +300,11 @@ def run_reference(args, rank: int) -> None:
 
 
 def config_dict() -> dict:
-    return {"workload": "config1: 200,000 uniform events at 80x64 in 8 ring partitions of 25,000 "
-                        "(independent streams), full s0..s3 + YOLOX head",
+    what = ("config1: 200,000 uniform events at 80x64 in 8 ring partitions of 25,000 (independent streams)"
+            if WL_CFG == 1 else
+            "config2: 1,000,000 clustered events at 80x64 (6 Gaussian blobs sigma 3 moving at 5-20 px/ms, "
+            "10% uniform, Poisson 5 Mev/s) in one stream")
+    return {"workload": what + ", full s0..s3 + YOLOX head",
             "model": "SSLA-S stub (tools/make_ssla_stub.py schema, seed 1, tdrop 4)",
             "events_per_step": N_EVENTS, "partitions": N_PARTS, "sensor": "80x64",
             "gate_layout": "hybrid (lib_stage01_to_gpu + celled kernel)",
@@ -724,8 +735,9 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true", help="skip the batch-of-1 latency samples")
-    ap.add_argument("--workload", default="config1", choices=["config1", "strips", "streams"],
-                    help="config1: 80x64 partitions per GPU (weak scaling); strips: config 3, one "
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "strips", "streams"],
+                    help="config1: 80x64 partitions per GPU (weak scaling); config2: one clustered "
+                         "80x64 stream of 1 M events per GPU (hot cells); strips: config 3, one "
                          "320x256 stream in horizontal strips across the GPUs (strong scaling); "
                          "streams: config 4, 64 camera streams through pinned rings spread over the GPUs")
     ap.add_argument("--strip-mode", default="exact", choices=["exact", "halo"],
@@ -733,6 +745,8 @@ def main() -> int:
     ap.add_argument("--halo-rows", type=int, default=16, help="strips, halo mode: halo in stage-0 rows (multiple of 8)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "config2":
+        use_config2()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
