@@ -361,7 +361,7 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     own = strips.owned_mask(sev, lo, hi)
     del ev_all
     n = len(sev)
-    G = STRIP_GLOBAL_CHUNK if exact else STRIP_CHUNK
+    G = args.strip_chunk or (STRIP_GLOBAL_CHUNK if exact else STRIP_CHUNK)
     if exact:
         cuts = np.searchsorted(gidx, np.arange(0, STRIP_EVENTS + G, G))
         chunks = [(int(cuts[c]), int(cuts[c + 1])) for c in range(len(cuts) - 1)]
@@ -743,6 +743,9 @@ def main() -> int:
     ap.add_argument("--strip-mode", default="exact", choices=["exact", "halo"],
                     help="strips: exact per-layer band exchange (default) or halo replication")
     ap.add_argument("--halo-rows", type=int, default=16, help="strips, halo mode: halo in stage-0 rows (multiple of 8)")
+    ap.add_argument("--strip-chunk", type=int, default=0,
+                    help="strips: events per chunk (exact: global stream events; halo: routed events per rank); "
+                         "0 = the mode's default")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "config2":

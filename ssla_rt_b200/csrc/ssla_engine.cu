@@ -169,6 +169,7 @@ struct Workspace {
     long long cap_part[5] = {0}, cap[5] = {0};
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
     DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps, work;
+    DevBuf hot[2], hot_flag[2];    // hot tiles of stages 0-1 (k_hot_tiles)
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -208,6 +209,11 @@ struct Workspace {
             const size_t slots = static_cast<size_t>(P) * g.tx[s] * g.ty[s] * g.nseg[s];
             tl[s].alloc(slots * g.seg * sizeof(int2));
             tl_cnt[s].alloc(slots * sizeof(int));
+            if (s < 2) {
+                const size_t nt = static_cast<size_t>(P) * g.tx[s] * g.ty[s];
+                hot[s].alloc(sizeof(int) * (nt + 1));
+                hot_flag[s].alloc(nt);
+            }
         }
         // Stage 0-1 layers keep compact q*h rows (QH); stage 2-3 layers use
         // GEMM-built (q, v, sigmoid(g)) rows (S_A first layers, S_B second).
@@ -274,10 +280,19 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         const float* S_rows;
         int qstride;
         if (s < 2) {
+            if (l == 1 || l == 2) {
+                HotArgs ha{};
+                ha.g = g; ha.stage = s; ha.tl_cnt = w.tl_cnt[s].as<int>(); ha.range = range;
+                ha.hot = w.hot[s].as<int>(); ha.hot_flag = w.hot_flag[s].as<uint8_t>();
+                launch_hot_tiles(st, ha);
+                check_launch("k_hot_tiles");
+                prof.mark(s == 0 ? "hot_s0" : "hot_s1", 1, st);
+            }
             ScanFusedArgs fa{};
             fa.g = g; fa.stage = s; fa.layer = l; fa.tl = w.tl[s].as<int2>(); fa.tl_cnt = w.tl_cnt[s].as<int>();
             fa.range = range; fa.parts = d_parts; fa.rflags = w.rflags.as<uint8_t>(); fa.second = half;
             fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>(); fa.work = w.work.as<int>() + l;
+            fa.hot = w.hot[s].as<int>(); fa.hot_flag = w.hot_flag[s].as<uint8_t>();
             launch_scan_fused(st, l, fa);
             check_launch("k_scan_fused");
             prof.mark(kScan[l], 1, st);

@@ -823,11 +823,56 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// k_hot_tiles: one CTA lists, in ascending order, the (partition, tile)
+// pairs of a stage whose tile lists hold more than kHotTileEntries entries.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
+    const int s = a.stage;
+    const int ntiles = a.g.tx[s] * a.g.ty[s];
+    const int total = a.g.P * ntiles;
+    __shared__ int wsum[32];
+    __shared__ int run;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) run = 0;
+    __syncthreads();
+    for (int t0 = 0; t0 < total; t0 += 1024) {
+        const int t = t0 + static_cast<int>(threadIdx.x);
+        bool hot = false;
+        if (t < total) {
+            const int p = t / ntiles;
+            const int n_p = a.range[p + 1] - a.range[p];
+            const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
+            int sum = 0;
+            for (int sg = 0; sg < nseg; ++sg) sum += a.tl_cnt[static_cast<size_t>(t) * a.g.nseg[s] + sg];
+            hot = sum > kHotTileEntries;
+            a.hot_flag[t] = hot ? 1 : 0;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, hot);
+        if (lane == 0) wsum[warp] = __popc(m);
+        __syncthreads();
+        int before = 0, tot = 0;
+        for (int w = 0; w < 32; ++w) {
+            before += (w < warp) ? wsum[w] : 0;
+            tot += wsum[w];
+        }
+        if (hot) a.hot[1 + run + before + __popc(m & lanemask_lt())] = t;
+        __syncthreads();
+        if (threadIdx.x == 0) run += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) a.hot[0] = run;
+}
+
+// ---------------------------------------------------------------------------
 // k_scan_group: per-cell LRU scan of a small layer (layers 1-3: IN, OUT <= 24,
 // the 9 x IN x 3*OUT qvg weights fit in shared memory) fused with that
 // layer's qvg matvec (matvec_ct<IN,3*OUT>, linear.h:80-90).
 // Work item = (partition, 8x8 tile, 2x2 cell group), taken by one warp from
-// an atomic counter; warps never wait on one another.  The warp walks the
+// an atomic counter; warps never wait on one another.  Tiles whose lists
+// exceed kHotTileEntries (hot cells: clustered events, strips of a large
+// sensor) are listed by k_hot_tiles and scanned with one item per cell
+// instead, after the group items: four times the parallelism where one
+// tile holds much of the drain.  The warp walks the
 // tile's ordered event list and queues, in stream order, one slot per
 // (event, cell of the group inside the event's 3x3 patch).  Per 32 slots:
 //   B) lane = slot: v and sigmoid(g) as fmaf chains over the input channels
@@ -853,7 +898,7 @@ struct ScanGroupShape {
 };
 
 template <int IN, int OUT, int WPC>
-__global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
+__global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanFusedArgs a) {
     using Sh = ScanGroupShape<IN, OUT, WPC>;
     constexpr int J2 = Sh::J2, DS = Sh::DS, QR = Sh::QR, QCAP = Sh::QCAP, R = Sh::R;
     extern __shared__ __align__(16) float dsm[];
@@ -870,17 +915,33 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
     const int s = a.stage;
     const int Wl = a.g.W[s], Hl = a.g.H[s];
     const int ntiles = a.g.tx[s] * a.g.ty[s];
-    const int n_items = a.g.P * ntiles * 16;
+    const int n_groups = a.g.P * ntiles * 16;
+    const int n_items = n_groups + a.hot[0] * 64;
     float* const QH = a.QH;
     for (;;) {
         int item = 0;
         if (lane == 0) item = atomicAdd(a.work, 1);
         item = __shfl_sync(0xffffffffu, item, 0);
         if (item >= n_items) break;
-        const int grp = item & 15, tile = (item >> 4) % ntiles, p = (item >> 4) / ntiles;
-        const int gx0 = (tile % a.g.tx[s]) * kTile + (grp & 3) * 2;
-        const int gy0 = (tile / a.g.tx[s]) * kTile + (grp >> 2) * 2;
-        if (gx0 >= Wl || gy0 >= Hl || gy0 + 1 < a.g.row_lo[s] || gy0 >= a.g.row_hi[s]) continue;
+        int p, tile, gx0, gy0, ncell;
+        if (item < n_groups) {
+            const int grp = item & 15;
+            tile = (item >> 4) % ntiles;
+            p = (item >> 4) / ntiles;
+            if (a.hot_flag[p * ntiles + tile]) continue;      // scanned cell by cell
+            gx0 = (tile % a.g.tx[s]) * kTile + (grp & 3) * 2;
+            gy0 = (tile / a.g.tx[s]) * kTile + (grp >> 2) * 2;
+            ncell = 4;
+        } else {
+            const int h = (item - n_groups) >> 6, cell = (item - n_groups) & 63;
+            const int pt = a.hot[1 + h];
+            tile = pt % ntiles;
+            p = pt / ntiles;
+            gx0 = (tile % a.g.tx[s]) * kTile + (cell & 7);
+            gy0 = (tile / a.g.tx[s]) * kTile + (cell >> 3);
+            ncell = 1;
+        }
+        if (gx0 >= Wl || gy0 >= Hl || gy0 + (ncell > 1 ? 1 : 0) < a.g.row_lo[s] || gy0 >= a.g.row_hi[s]) continue;
         float* const hid = a.parts[p].hidden[a.layer];
         float h[R];
         int hoff[R];
@@ -889,7 +950,7 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
             const int pair = r * 32 + lane;
             const int c = pair / OUT, ch = pair % OUT;
             const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
-            const bool ok = pair < 4 * OUT && cx < Wl && cy < Hl;
+            const bool ok = pair < ncell * OUT && cx < Wl && cy < Hl;
             hoff[r] = ok ? (cy * Wl + cx) * OUT + ch : -1;
             h[r] = ok ? hid[hoff[r]] : 0.0f;
         }
@@ -950,13 +1011,28 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
                 const int c = pair / OUT, ch = pair % OUT;
                 unsigned mk = (c == 0) ? cm[0] : (c == 1) ? cm[1] : (c == 2) ? cm[2] : cm[3];
                 float hc = h[r];
+                // four hits per round: their a, v loads are issued before the
+                // chain of fmafs, so one shared-memory latency covers four
                 while (mk) {
-                    const int s2 = __ffs(mk) - 1;
-                    mk &= mk - 1u;
-                    const float* q2 = Qs + s2 * QR;
-                    hc = fmaf(q2[ch], hc, q2[OUT + ch]);
-                    if ((om >> s2) & 1u)
-                        QH[(static_cast<size_t>(qk[s2]) * 9 + (qm[s2] & 15)) * OUT + ch] = hc;
+                    int s4[4];
+                    bool on[4];
+                    float av[4], vv[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        on[q] = mk != 0u;
+                        s4[q] = on[q] ? __ffs(mk) - 1 : 0;
+                        mk &= mk - 1u;
+                        const float* q2 = Qs + s4[q] * QR;
+                        av[q] = q2[ch];
+                        vv[q] = q2[OUT + ch];
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (!on[q]) break;
+                        hc = fmaf(av[q], hc, vv[q]);
+                        if ((om >> s4[q]) & 1u)
+                            QH[(static_cast<size_t>(qk[s4[q]]) * 9 + (qm[s4[q]] & 15)) * OUT + ch] = hc;
+                    }
                 }
                 h[r] = hc;
             }
@@ -984,7 +1060,8 @@ __global__ void __launch_bounds__(32 * WPC) k_scan_group(ScanFusedArgs a) {
                     for (int c = 0; c < 4; ++c) {
                         const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
                         const int dx = cx - ex, dy = cy - ey;
-                        if (cx < Wl && cy < Hl && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1) cmask |= 1u << c;
+                        if (c < ncell && cx < Wl && cy < Hl && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1)
+                            cmask |= 1u << c;
                     }
                 }
                 const int nc = __popc(cmask);
@@ -1874,7 +1951,7 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
             grid = std::max(1, sms * std::max(1, per_sm));
         }
         const int s = layer / 2;
-        const int items = a.g.P * a.g.tx[s] * a.g.ty[s] * 16;
+        const int items = a.g.P * a.g.tx[s] * a.g.ty[s] * 64;      // bound with every tile hot
         const int need = (items + (Sh::NT / 32) - 1) / (Sh::NT / 32);
         kern<<<std::min(grid, need), Sh::NT, Sh::smem, st>>>(a);
     };
@@ -1883,6 +1960,10 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
         case 2: go(k_scan_group<12, 24, 16>, ScanGroupShape<12, 24, 16>{}); break;
         default: go(k_scan_group<24, 24, 16>, ScanGroupShape<24, 24, 16>{}); break;
     }
+}
+
+void launch_hot_tiles(cudaStream_t st, const HotArgs& a) {
+    k_hot_tiles<<<1, 1024, 0, st>>>(a);
 }
 
 void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows) {

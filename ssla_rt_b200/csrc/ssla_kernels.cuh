@@ -85,7 +85,24 @@ struct ScanFusedArgs {
     const float* W;          // qvgT [9][IN][3*OUT]
     float* QH;               // [(entry * 9 + delta) * OUT] q * h rows
     int* work;               // work-item counter of this launch, zero on entry
+    const int* hot;          // hot tiles of the stage: [0] count, [1..] (p * ntiles + tile)
+    const uint8_t* hot_flag; // [P * ntiles] 1 = the tile is scanned cell by cell
 };
+
+// Tiles whose event lists exceed this many entries are scanned with one
+// work item per cell instead of one per 2x2 cell group.
+constexpr int kHotTileEntries = 4096;
+
+struct HotArgs {
+    Geo g;
+    int stage;
+    const int* tl_cnt;
+    const int* range;        // [P+1] this stage's partition ranges
+    int* hot;                // [0] count, [1..] hot (p * ntiles + tile), ascending
+    uint8_t* hot_flag;       // [P * ntiles]
+};
+
+void launch_hot_tiles(cudaStream_t st, const HotArgs& a);
 
 struct ContribArgs {
     Geo g;

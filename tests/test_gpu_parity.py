@@ -110,6 +110,22 @@ def test_window3_hot_cells_and_invalid_events(oracle_mod, stub_dir):
                                 [ev], abi.LAYOUT_DECOMP)
 
 
+def test_hot_tiles_scanned_cell_by_cell(oracle_mod, stub_dir):
+    """A near-stationary blob puts most of 40,000 events into one s3 block:
+    its stage-0 and stage-1 tile lists exceed the hot-tile bound, so those
+    tiles are scanned with one work item per cell; a second partition stays
+    uniform.  Everything still equals the oracle."""
+    d = stub_dir(64, 80, 1, 4)
+    hot = E.make_events(40_000, 64, 80, rate_mev=5.0, seed=21, n_blobs=1, blob_frac=0.97, sigma=2.0,
+                        speed_px_per_ms=(0.0, 0.05))
+    parts = [hot, E.config_events(0, n=3000, seed=22)]
+    eng = _engine(d, n_partitions=2, max_events=43_000, layout=abi.LAYOUT_HYBRID, record_stage_outputs=True,
+                  max_events_per_partition=40_000)
+    drain_device(eng, parts)
+    oracles = run_oracle(oracle_mod, d, 64, 80, 4, abi.LAYOUT_HYBRID, parts)
+    assert_engine_equals_oracle(eng, oracles, parts, abi.LAYOUT_HYBRID)
+
+
 def test_state_carries_across_drains(oracle_mod, stub_dir):
     """Three consecutive drain calls == one sequential run."""
     d = stub_dir(64, 80, 1, 4)
