@@ -1049,11 +1049,6 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                 int2 ent = make_int2(0, 0);
                 if (j < cnt) ent = lst[j];
                 const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
-                int outf = 1;
-                if (a.second) {
-                    if (s == 0) outf = (j < cnt && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
-                    else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
-                }
                 unsigned cmask = 0;
                 if (j < cnt) {
 #pragma unroll
@@ -1064,15 +1059,22 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                             cmask |= 1u << c;
                     }
                 }
-                const int nc = __popc(cmask);
-                int incl = nc;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += y;
+                // output flag of a hit (the stage-0 flag byte is read for hits only)
+                int outf = 1;
+                if (a.second) {
+                    if (s == 0) outf = (cmask && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
+                    else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
                 }
-                const int tot = __shfl_sync(0xffffffffu, incl, 31);
-                int pos = np + incl - nc;
+                // queue positions: exclusive prefix of the hit counts (0..4)
+                // from one ballot per bit
+                const int nc = __popc(cmask);
+                const unsigned v0 = __ballot_sync(0xffffffffu, nc & 1);
+                const unsigned v1 = __ballot_sync(0xffffffffu, nc & 2);
+                const unsigned v2 = __ballot_sync(0xffffffffu, nc & 4);
+                const unsigned lt = lanemask_lt();
+                const int tot = __popc(v0) + 2 * __popc(v1) + 4 * __popc(v2);
+                if (tot == 0) continue;
+                int pos = np + __popc(v0 & lt) + 2 * __popc(v1 & lt) + 4 * __popc(v2 & lt);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if ((cmask >> c) & 1u) {
