@@ -318,7 +318,7 @@ def config_dict() -> dict:
 STRIP_EVENTS = 10_000_000
 STRIP_H, STRIP_W = 256, 320
 STRIP_CHUNK = 1 << 20            # halo mode: events per drain of a rank
-STRIP_GLOBAL_CHUNK = 1 << 22     # exact mode: global stream events per aligned chunk
+STRIP_GLOBAL_CHUNK = 10_000_000  # exact mode: global stream events per aligned chunk (the whole stream)
 STRIP_BAND = 16                  # exact mode: band rows (2 stage-3 rows)
 
 

@@ -281,7 +281,12 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         int qstride;
         if (s < 2) {
             if (l == 1 || l == 2) {
+                // split hot tiles only when the 2x2-group items of the rows
+                // this engine scans are fewer than the kernel's resident warps
+                const int ty_lo = g.row_lo[s] / kTile, ty_hi = (g.row_hi[s] + kTile - 1) / kTile;
+                const long long groups = static_cast<long long>(g.P) * g.tx[s] * std::max(0, ty_hi - ty_lo) * 16;
                 HotArgs ha{};
+                ha.threshold = groups < scan_fused_resident_warps(l) ? kHotTileEntries : 0x7FFFFFFF;
                 ha.g = g; ha.stage = s; ha.tl_cnt = w.tl_cnt[s].as<int>(); ha.range = range;
                 ha.hot = w.hot[s].as<int>(); ha.hot_flag = w.hot_flag[s].as<uint8_t>();
                 launch_hot_tiles(st, ha);

@@ -824,7 +824,7 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 
 // ---------------------------------------------------------------------------
 // k_hot_tiles: one CTA lists, in ascending order, the (partition, tile)
-// pairs of a stage whose tile lists hold more than kHotTileEntries entries.
+// pairs of a stage whose tile lists hold more than a.threshold entries.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
     const int s = a.stage;
@@ -844,7 +844,7 @@ __global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
             const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
             int sum = 0;
             for (int sg = 0; sg < nseg; ++sg) sum += a.tl_cnt[static_cast<size_t>(t) * a.g.nseg[s] + sg];
-            hot = sum > kHotTileEntries;
+            hot = sum > a.threshold;
             a.hot_flag[t] = hot ? 1 : 0;
         }
         const unsigned m = __ballot_sync(0xffffffffu, hot);
@@ -868,11 +868,12 @@ __global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
 // the 9 x IN x 3*OUT qvg weights fit in shared memory) fused with that
 // layer's qvg matvec (matvec_ct<IN,3*OUT>, linear.h:80-90).
 // Work item = (partition, 8x8 tile, 2x2 cell group), taken by one warp from
-// an atomic counter; warps never wait on one another.  Tiles whose lists
-// exceed kHotTileEntries (hot cells: clustered events, strips of a large
-// sensor) are listed by k_hot_tiles and scanned with one item per cell
-// instead, after the group items: four times the parallelism where one
-// tile holds much of the drain.  The warp walks the
+// an atomic counter; warps never wait on one another.  When the group items
+// are fewer than the resident warps (one clustered stream, a strip of a
+// large sensor), tiles whose lists exceed kHotTileEntries are listed by
+// k_hot_tiles and scanned with one item per cell instead, after the group
+// items: four times the parallelism where few tiles hold the drain.  With
+// items to spare, splitting would only repeat each tile's list walk.  The warp walks the
 // tile's ordered event list and queues, in stream order, one slot per
 // (event, cell of the group inside the event's 3x3 patch).  Per 32 slots:
 //   B) lane = slot: v and sigmoid(g) as fmaf chains over the input channels
@@ -1939,19 +1940,34 @@ void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long 
     }
 }
 
+// Resident CTAs of a stage-0/1 scan kernel (computed once per kernel).
+template <typename K, typename Sh>
+int scan_fused_grid(K kern, Sh) {
+    static int grid = 0;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Sh::smem));
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (grid == 0) {
+        int dev = 0, sms = 0, per_sm = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::NT, Sh::smem);
+        grid = std::max(1, sms * std::max(1, per_sm));
+    }
+    return grid;
+}
+
+int scan_fused_resident_warps(int layer) {
+    switch (layer) {
+        case 1: return scan_fused_grid(k_scan_group<12, 12, 8>, ScanGroupShape<12, 12, 8>{}) * 8;
+        case 2: return scan_fused_grid(k_scan_group<12, 24, 16>, ScanGroupShape<12, 24, 16>{}) * 16;
+        default: return scan_fused_grid(k_scan_group<24, 24, 16>, ScanGroupShape<24, 24, 16>{}) * 16;
+    }
+}
+
 void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
     auto go = [&](auto kern, auto shape) {
         using Sh = decltype(shape);
-        static int grid = 0;                       // resident CTAs, per kernel
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Sh::smem));
-        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        if (grid == 0) {
-            int dev = 0, sms = 0, per_sm = 0;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::NT, Sh::smem);
-            grid = std::max(1, sms * std::max(1, per_sm));
-        }
+        const int grid = scan_fused_grid(kern, shape);
         const int s = layer / 2;
         const int items = a.g.P * a.g.tx[s] * a.g.ty[s] * 64;      // bound with every tile hot
         const int need = (items + (Sh::NT / 32) - 1) / (Sh::NT / 32);

@@ -89,13 +89,15 @@ struct ScanFusedArgs {
     const uint8_t* hot_flag; // [P * ntiles] 1 = the tile is scanned cell by cell
 };
 
-// Tiles whose event lists exceed this many entries are scanned with one
-// work item per cell instead of one per 2x2 cell group.
+// When a stage-0/1 scan has fewer 2x2-group work items than resident warps,
+// tiles whose event lists exceed this many entries are scanned with one work
+// item per cell instead.
 constexpr int kHotTileEntries = 4096;
 
 struct HotArgs {
     Geo g;
     int stage;
+    int threshold;           // list entries above which a tile is hot
     const int* tl_cnt;
     const int* range;        // [P+1] this stage's partition ranges
     int* hot;                // [0] count, [1..] hot (p * ntiles + tile), ascending
@@ -103,6 +105,8 @@ struct HotArgs {
 };
 
 void launch_hot_tiles(cudaStream_t st, const HotArgs& a);
+// Warps of the stage-0/1 scan kernel of `layer` resident on the device.
+int scan_fused_resident_warps(int layer);
 
 struct ContribArgs {
     Geo g;
