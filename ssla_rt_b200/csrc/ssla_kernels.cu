@@ -972,32 +972,33 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             }
             const float* wr = Ws + d * DS;
             float* qr = Qs + lane * QR;
-            float acc[OUT];
-            // B: a = sigmoid(g) -> [0, OUT), v -> [OUT, 2*OUT)
+            float2 acc[OUT / 2];
+            // B: a = sigmoid(g) -> [0, OUT), v -> [OUT, 2*OUT); paired
+            // output channels per packed FMA (each component an fmaf)
 #pragma unroll
             for (int part = 2; part >= 1; --part) {
 #pragma unroll
-                for (int j = 0; j < OUT; ++j) acc[j] = 0.0f;
+                for (int j = 0; j < OUT / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
 #pragma unroll
                 for (int i = 0; i < IN; ++i) {
+                    const float2 xx = make_float2(x[i], x[i]);
 #pragma unroll
                     for (int j4 = 0; j4 < OUT / 4; ++j4) {
                         const float4 w4 = *reinterpret_cast<const float4*>(wr + i * J2 + part * OUT + 4 * j4);
-                        acc[4 * j4] = fmaf(w4.x, x[i], acc[4 * j4]);
-                        acc[4 * j4 + 1] = fmaf(w4.y, x[i], acc[4 * j4 + 1]);
-                        acc[4 * j4 + 2] = fmaf(w4.z, x[i], acc[4 * j4 + 2]);
-                        acc[4 * j4 + 3] = fmaf(w4.w, x[i], acc[4 * j4 + 3]);
+                        acc[2 * j4] = __ffma2_rn(make_float2(w4.x, w4.y), xx, acc[2 * j4]);
+                        acc[2 * j4 + 1] = __ffma2_rn(make_float2(w4.z, w4.w), xx, acc[2 * j4 + 1]);
                     }
                 }
                 if (part == 2) {
 #pragma unroll
-                    for (int j = 0; j < OUT; ++j) acc[j] = ssla_sigmoidf(acc[j]);
+                    for (int j = 0; j < OUT / 2; ++j)
+                        acc[j] = make_float2(ssla_sigmoidf(acc[j].x), ssla_sigmoidf(acc[j].y));
                 }
                 const int col = (part == 2) ? 0 : OUT;
 #pragma unroll
                 for (int j4 = 0; j4 < OUT / 4; ++j4)
                     *reinterpret_cast<float4*>(qr + col + 4 * j4) =
-                        make_float4(acc[4 * j4], acc[4 * j4 + 1], acc[4 * j4 + 2], acc[4 * j4 + 3]);
+                        make_float4(acc[2 * j4].x, acc[2 * j4].y, acc[2 * j4 + 1].x, acc[2 * j4 + 1].y);
             }
             unsigned cm[4];
 #pragma unroll
