@@ -1243,13 +1243,18 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
                 const float w0 = Wqs[k * OUT + cg * 3 + 0];
                 const float w1 = Wqs[k * OUT + cg * 3 + 1];
                 const float w2 = Wqs[k * OUT + cg * 3 + 2];
-                const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const float2 xp[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w),
+                                      make_float2(x1.x, x1.y), make_float2(x1.z, x1.w)};
+                const float2 ww[3] = {make_float2(w0, w0), make_float2(w1, w1), make_float2(w2, w2)};
+                // row pairs per packed FMA (each component an fmaf)
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    qa[i][0] = fmaf(w0, x[i], qa[i][0]);
-                    qa[i][1] = fmaf(w1, x[i], qa[i][1]);
-                    qa[i][2] = fmaf(w2, x[i], qa[i][2]);
-                }
+                for (int i2 = 0; i2 < 4; ++i2)
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) {
+                        const float2 r = __ffma2_rn(ww[j], xp[i2], make_float2(qa[2 * i2][j], qa[2 * i2 + 1][j]));
+                        qa[2 * i2][j] = r.x;
+                        qa[2 * i2 + 1][j] = r.y;
+                    }
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
@@ -1272,13 +1277,18 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
             const float b0 = Bs[k * OUT + cg * 3 + 0];
             const float b1 = Bs[k * OUT + cg * 3 + 1];
             const float b2 = Bs[k * OUT + cg * 3 + 2];
-            const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float2 xp[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w),
+                                  make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
+            const float2 bb[3] = {make_float2(b0, b0), make_float2(b1, b1), make_float2(b2, b2)};
+            // row pairs per packed FMA (each component an fmaf)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                acc[i][0] = fmaf(b0, x[i], acc[i][0]);
-                acc[i][1] = fmaf(b1, x[i], acc[i][1]);
-                acc[i][2] = fmaf(b2, x[i], acc[i][2]);
-            }
+            for (int i2 = 0; i2 < 4; ++i2)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    const float2 r = __ffma2_rn(bb[j], xp[i2], make_float2(acc[2 * i2][j], acc[2 * i2 + 1][j]));
+                    acc[2 * i2][j] = r.x;
+                    acc[2 * i2 + 1][j] = r.y;
+                }
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -1634,22 +1644,29 @@ __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
             }
         }
         __syncthreads();
-        float acc[8][4];
+        // column pairs per packed FMA (each component an fmaf)
+        float2 acc2[8][2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+        for (int i = 0; i < 8; ++i) acc2[i][0] = acc2[i][1] = make_float2(0.0f, 0.0f);
 #pragma unroll 4
         for (int k = 0; k < K; ++k) {
             const float4 a0 = *reinterpret_cast<const float4*>(As + k * BMP + ty * 8);
             const float4 a1 = *reinterpret_cast<const float4*>(As + k * BMP + ty * 8 + 4);
             const float4 b = *reinterpret_cast<const float4*>(Bs + k * BN + tx * 4);
             const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            const float w[4] = {b.x, b.y, b.z, b.w};
+            const float2 w01 = make_float2(b.x, b.y), w23 = make_float2(b.z, b.w);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < 8; ++i) {
+                const float2 xx = make_float2(x[i], x[i]);
+                acc2[i][0] = __ffma2_rn(xx, w01, acc2[i][0]);
+                acc2[i][1] = __ffma2_rn(xx, w23, acc2[i][1]);
+            }
+        }
+        float acc[8][4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(x[i], w[j], acc[i][j]);
+        for (int i = 0; i < 8; ++i) {
+            acc[i][0] = acc2[i][0].x; acc[i][1] = acc2[i][0].y;
+            acc[i][2] = acc2[i][1].x; acc[i][3] = acc2[i][1].y;
         }
         // epilogue: 4 consecutive columns share part and delta
         const int col = c0 + tx * 4;
