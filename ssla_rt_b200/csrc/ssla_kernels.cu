@@ -1243,18 +1243,13 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
                 const float w0 = Wqs[k * OUT + cg * 3 + 0];
                 const float w1 = Wqs[k * OUT + cg * 3 + 1];
                 const float w2 = Wqs[k * OUT + cg * 3 + 2];
-                const float2 xp[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w),
-                                      make_float2(x1.x, x1.y), make_float2(x1.z, x1.w)};
-                const float2 ww[3] = {make_float2(w0, w0), make_float2(w1, w1), make_float2(w2, w2)};
-                // row pairs per packed FMA (each component an fmaf)
+                const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-                for (int i2 = 0; i2 < 4; ++i2)
-#pragma unroll
-                    for (int j = 0; j < 3; ++j) {
-                        const float2 r = __ffma2_rn(ww[j], xp[i2], make_float2(qa[2 * i2][j], qa[2 * i2 + 1][j]));
-                        qa[2 * i2][j] = r.x;
-                        qa[2 * i2 + 1][j] = r.y;
-                    }
+                for (int i = 0; i < 8; ++i) {
+                    qa[i][0] = fmaf(w0, x[i], qa[i][0]);
+                    qa[i][1] = fmaf(w1, x[i], qa[i][1]);
+                    qa[i][2] = fmaf(w2, x[i], qa[i][2]);
+                }
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
