@@ -170,6 +170,7 @@ struct Workspace {
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
     DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps, work;
     DevBuf hot[2], hot_flag[2];    // hot tiles of stages 0-1 (k_hot_tiles)
+    bool hot_on[2] = {false, false};   // this drain splits hot tiles of stage s
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -285,19 +286,23 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
                 // this engine scans are fewer than the kernel's resident warps
                 const int ty_lo = g.row_lo[s] / kTile, ty_hi = (g.row_hi[s] + kTile - 1) / kTile;
                 const long long groups = static_cast<long long>(g.P) * g.tx[s] * std::max(0, ty_hi - ty_lo) * 16;
-                HotArgs ha{};
-                ha.threshold = groups < scan_fused_resident_warps(l) ? kHotTileEntries : 0x7FFFFFFF;
-                ha.g = g; ha.stage = s; ha.tl_cnt = w.tl_cnt[s].as<int>(); ha.range = range;
-                ha.hot = w.hot[s].as<int>(); ha.hot_flag = w.hot_flag[s].as<uint8_t>();
-                launch_hot_tiles(st, ha);
-                check_launch("k_hot_tiles");
-                prof.mark(s == 0 ? "hot_s0" : "hot_s1", 1, st);
+                w.hot_on[s] = groups < scan_fused_resident_warps(l);
+                if (w.hot_on[s]) {
+                    HotArgs ha{};
+                    ha.threshold = kHotTileEntries;
+                    ha.g = g; ha.stage = s; ha.tl_cnt = w.tl_cnt[s].as<int>(); ha.range = range;
+                    ha.hot = w.hot[s].as<int>(); ha.hot_flag = w.hot_flag[s].as<uint8_t>();
+                    launch_hot_tiles(st, ha);
+                    check_launch("k_hot_tiles");
+                    prof.mark(s == 0 ? "hot_s0" : "hot_s1", 1, st);
+                }
             }
             ScanFusedArgs fa{};
             fa.g = g; fa.stage = s; fa.layer = l; fa.tl = w.tl[s].as<int2>(); fa.tl_cnt = w.tl_cnt[s].as<int>();
             fa.range = range; fa.parts = d_parts; fa.rflags = w.rflags.as<uint8_t>(); fa.second = half;
             fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>(); fa.work = w.work.as<int>() + l;
-            fa.hot = w.hot[s].as<int>(); fa.hot_flag = w.hot_flag[s].as<uint8_t>();
+            fa.hot = w.hot_on[s] ? w.hot[s].as<int>() : nullptr;
+            fa.hot_flag = w.hot_on[s] ? w.hot_flag[s].as<uint8_t>() : nullptr;
             launch_scan_fused(st, l, fa);
             check_launch("k_scan_fused");
             prof.mark(kScan[l], 1, st);

@@ -917,7 +917,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
     const int Wl = a.g.W[s], Hl = a.g.H[s];
     const int ntiles = a.g.tx[s] * a.g.ty[s];
     const int n_groups = a.g.P * ntiles * 16;
-    const int n_items = n_groups + a.hot[0] * 64;
+    const int n_items = n_groups + (a.hot ? a.hot[0] * 64 : 0);
     float* const QH = a.QH;
     for (;;) {
         int item = 0;
@@ -929,7 +929,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             const int grp = item & 15;
             tile = (item >> 4) % ntiles;
             p = (item >> 4) / ntiles;
-            if (a.hot_flag[p * ntiles + tile]) continue;      // scanned cell by cell
+            if (a.hot_flag && a.hot_flag[p * ntiles + tile]) continue;      // scanned cell by cell
             gx0 = (tile % a.g.tx[s]) * kTile + (grp & 3) * 2;
             gy0 = (tile / a.g.tx[s]) * kTile + (grp >> 2) * 2;
             ncell = 4;

@@ -85,8 +85,8 @@ struct ScanFusedArgs {
     const float* W;          // qvgT [9][IN][3*OUT]
     float* QH;               // [(entry * 9 + delta) * OUT] q * h rows
     int* work;               // work-item counter of this launch, zero on entry
-    const int* hot;          // hot tiles of the stage: [0] count, [1..] (p * ntiles + tile)
-    const uint8_t* hot_flag; // [P * ntiles] 1 = the tile is scanned cell by cell
+    const int* hot;          // hot tiles of the stage: [0] count, [1..] (p * ntiles + tile); null: none
+    const uint8_t* hot_flag; // [P * ntiles] 1 = the tile is scanned cell by cell; null: none
 };
 
 // When a stage-0/1 scan has fewer 2x2-group work items than resident warps,
