@@ -587,35 +587,44 @@ def run_streams(args, rank: int, world: int, local: int) -> int:
     for b in range(args.warmup):
         eng.drain(batch(b), off, stream=stream)
     torch.cuda.synchronize(dev)
-    eng.set_profiling(True)
-    phase_acc, flops_acc, step_ms = {}, {}, []
     flags_dev = torch.zeros(per_ring * P, dtype=torch.uint8, device=dev)
+
+    def run_steps(b0: int, profile: bool):
+        eng.set_profiling(profile)
+        ph, fl, ms_l = {}, {}, []
+        for k in range(args.steps):
+            x = batch(b0 + k)
+            flush.fill_(float(k))
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            eng.drain(x, off, flags=flags_dev, stream=stream)
+            b.record(stream)
+            b.synchronize()
+            ms_l.append(a.elapsed_time(b))
+            if profile:
+                macs = algorithmic_macs(x.cpu().numpy(), flags_dev.cpu().numpy())
+                for name, ms, nl in eng.phase_times():
+                    acc = ph.setdefault(name, [0.0, 0])
+                    acc[0] += ms
+                    acc[1] += 1
+                    fl[name] = fl.get(name, 0.0) + phase_flops(macs, name)
+        eng.set_profiling(False)
+        return ph, fl, ms_l
+
     clocks = ClockSampler()
     clocks.start()
     time.sleep(0.3)
     barrier()
     torch.cuda.synchronize(dev)
-    for k in range(args.steps):
-        x = batch(args.warmup + k)
-        flush.fill_(float(k))
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        eng.drain(x, off, flags=flags_dev, stream=stream)
-        b.record(stream)
-        b.synchronize()
-        step_ms.append(a.elapsed_time(b))
-        macs = algorithmic_macs(x.cpu().numpy(), flags_dev.cpu().numpy())
-        for name, ms, nl in eng.phase_times():
-            acc = phase_acc.setdefault(name, [0.0, 0])
-            acc[0] += ms
-            acc[1] += 1
-            flops_acc[name] = flops_acc.get(name, 0.0) + phase_flops(macs, name)
+    _, _, step_ms = run_steps(args.warmup, False)          # timed: no per-phase events
     torch.cuda.synchronize(dev)
     barrier()
     clk = clocks.stop(local)
-    eng.set_profiling(False)
     launches = eng.info().launches * args.steps
+    # the next K slices with an event after every phase: phase times and the
+    # dominant kernel's duration for the roofline
+    phase_acc, flops_acc, prof_ms = run_steps(args.warmup + args.steps, True)
     my_ms = sum(step_ms)
     total_ms = reduce([my_ms], dist.ReduceOp.MAX if world > 1 else None)[0]
     step_events = reduce([per_ring * P * args.steps], dist.ReduceOp.SUM if world > 1 else None)[0]
@@ -631,7 +640,9 @@ def run_streams(args, rank: int, world: int, local: int) -> int:
         "traffic": None,
         "peak_source": "measured FFMA peak (ssla_measure_fp32_peak, this run)",
         "avg_ms": dom_ms_sum / dom_n, "algorithmic_flops_per_launch": flops_acc.get(dom_name, 0.0) / dom_n,
-        "share_of_step": dom_ms_sum / my_ms,
+        "share_of_step": dom_ms_sum / sum(prof_ms),
+        "timing": "phase durations from a profiled pass over the next K slices (CUDA events after every "
+                  "phase); the headline value is timed without them",
     }
 
     # ---- (2) e2e: the whole job through the rings, as fast as they drain ----
@@ -805,35 +816,41 @@ def main() -> int:
         eng.drain(ev, off, stream=stream)
     torch.cuda.synchronize(dev)
 
-    # ---- timed: K device-timed drains, per-phase events on ----
-    eng.set_profiling(True)
-    phase_acc = {}
-    step_ms = []
+    # ---- timed: K device-timed drains (no per-phase events: they cost ~5%) ----
+    def run_steps(profile: bool):
+        eng.set_profiling(profile)
+        acc_ph, ms_l = {}, []
+        for _ in range(args.steps):
+            advance()
+            flush_l2()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            eng.drain(ev, off, stream=stream)
+            b.record(stream)
+            b.synchronize()
+            ms_l.append(a.elapsed_time(b))
+            for name, ms, nl in (eng.phase_times() if profile else []):
+                acc = acc_ph.setdefault(name, [0.0, 0, 0])
+                acc[0] += ms
+                acc[1] += 1
+                acc[2] += nl
+        eng.set_profiling(False)
+        return acc_ph, ms_l
+
     clocks = ClockSampler()
     clocks.start()
     time.sleep(0.3)
     barrier()
     torch.cuda.synchronize(dev)
-    for _ in range(args.steps):
-        advance()
-        flush_l2()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        eng.drain(ev, off, stream=stream)
-        b.record(stream)
-        b.synchronize()
-        step_ms.append(a.elapsed_time(b))
-        for name, ms, nl in eng.phase_times():
-            acc = phase_acc.setdefault(name, [0.0, 0, 0])
-            acc[0] += ms
-            acc[1] += 1
-            acc[2] += nl
+    _, step_ms = run_steps(False)
     torch.cuda.synchronize(dev)
     barrier()
     clk = clocks.stop(local)
-    eng.set_profiling(False)
     launches = eng.info().launches * args.steps
+    # the same K drains again with an event after every phase: phase times
+    # and the dominant kernel's duration for the roofline
+    phase_acc, prof_ms = run_steps(True)
     total_ms = sum(step_ms)
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
@@ -888,7 +905,9 @@ def main() -> int:
         "peak_source": "measured FFMA peak (ssla_measure_fp32_peak, this run); the path is FP32 "
                        "CUDA-core work, MEASURED_PEAKS.json holds only HBM and bf16 tensor peaks",
         "avg_ms": dom_ms, "algorithmic_flops_per_launch": dflops,
-        "share_of_step": dom_ms_sum / total_ms if world == 1 else None,
+        "share_of_step": dom_ms_sum / sum(prof_ms),
+        "timing": "phase durations from a profiled pass of the same K drains (CUDA events after every "
+                  "phase); the headline value is timed without them",
     }
     phases = {k: round(v[0] / v[1], 4) for k, v in sorted(phase_acc.items(), key=lambda kv: -kv[1][0])}
 

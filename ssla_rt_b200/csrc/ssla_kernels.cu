@@ -34,6 +34,18 @@ __device__ __forceinline__ unsigned lanemask_lt() {
 
 __device__ __forceinline__ int hi_lane(unsigned m) { return 31 - __clz(m); }
 
+// Programmatic dependent launch: a drain kernel lets the next one in the
+// stream be scheduled once all of its own CTAs have started, and waits for
+// the previous kernel to complete (and its memory to be visible) before
+// touching anything that kernel may write.  Without the launch attribute
+// both are no-ops.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+    pdl_trigger();
+    pdl_wait();
+}
+
 // uint8 counter rule of tdrop_check_at (src/ssla_kernels.cpp:912-921) and
 // parallel_tdrop (ssla_s2_s3_head_celled.cuh:742-745): pass iff window <= 1
 // or the pre-increment count (mod 256) is a multiple of the window.
@@ -65,6 +77,7 @@ __device__ __forceinline__ bool warp_gate(bool active, int key, int* cnt, int wi
 // ---------------------------------------------------------------------------
 __global__ void k_prep(const float4* __restrict__ ev, int n, int W0, int H0,
                        uint32_t* __restrict__ ev_xy, uint8_t* __restrict__ rflags) {
+    pdl_enter();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float4 e = ev[i];
         uint32_t xy = kInvalidXY;
@@ -101,6 +114,7 @@ __global__ void k_prep_records(const HybridInputRec* __restrict__ rec, int n,
 // ballot per tile).  grid (P, tile rows, segments).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
+    pdl_enter();
     const int p = blockIdx.x, trow = blockIdx.y, seg = blockIdx.z;
     const int s = a.stage;
     const int tx = a.g.tx[s];
@@ -181,6 +195,7 @@ __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
 // grown by one cell.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_filter_tiles(FilterArgs a) {
+    pdl_enter();
     const int p = blockIdx.x, tile = blockIdx.y, seg = blockIdx.z;
     const int s = a.stage;
     const int ntiles = a.g.tx[s] * a.g.ty[s];
@@ -258,6 +273,7 @@ constexpr int kGateBuf = 256;
 constexpr int kGateNT = 128;
 
 __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
+    pdl_enter();
     const int p = blockIdx.x, blk = blockIdx.y;
     const int W3 = a.g.W[3];
     const int bx = blk % W3, by = blk / W3;
@@ -595,6 +611,7 @@ __global__ void __launch_bounds__(32) k_gates_s2(Gate2Args a) {
 // set, for lists s_first+1 .. 4.  Compaction tiles never straddle partitions.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_compact_count(CompactArgs a) {
+    pdl_enter();
     const int p = blockIdx.x, t = blockIdx.y;
     const int lo = a.ev_off[p] + t * kCompactTile;
     const int hi = min(a.ev_off[p + 1], lo + kCompactTile);
@@ -621,6 +638,7 @@ __global__ void __launch_bounds__(kNT) k_compact_count(CompactArgs a) {
 }
 
 __global__ void __launch_bounds__(kNT) k_compact_scan(CompactArgs a) {
+    pdl_enter();
     const int n = a.g.P * a.tiles_per_part;
     __shared__ int carry[4];
     __shared__ int wsum[kNT / 32][4];
@@ -670,6 +688,7 @@ __global__ void __launch_bounds__(kNT) k_compact_scan(CompactArgs a) {
 }
 
 __global__ void __launch_bounds__(kNT) k_compact_scatter(CompactArgs a) {
+    pdl_enter();
     const int p = blockIdx.x, t = blockIdx.y;
     const int lo = a.ev_off[p] + t * kCompactTile;
     const int hi = min(a.ev_off[p + 1], lo + kCompactTile);
@@ -731,6 +750,7 @@ __global__ void __launch_bounds__(kNT) k_compact_scatter(CompactArgs a) {
 // ---------------------------------------------------------------------------
 template <int A, int OUT>
 __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
+    pdl_enter();
     constexpr int CPL = (OUT + 31) / 32;
     const int p = blockIdx.x, tile = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -827,6 +847,7 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
 // pairs of a stage whose tile lists hold more than a.threshold entries.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
+    pdl_enter();
     const int s = a.stage;
     const int ntiles = a.g.tx[s] * a.g.ty[s];
     const int total = a.g.P * ntiles;
@@ -908,10 +929,13 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
     float* Qs = Ws + 9 * DS + warp * (Sh::per_warp / sizeof(float));   // [32][QR]
     int* qk = reinterpret_cast<int*>(Qs + 32 * QR);                    // [QCAP] entry
     unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<6
+    pdl_trigger();
+    // the weights are constant: staged while the previous kernel finishes
     for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
         const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
         *reinterpret_cast<float4*>(Ws + d * DS + 4 * r) = __ldg(reinterpret_cast<const float4*>(a.W) + t);
     }
+    pdl_wait();
     __syncthreads();
     const int s = a.stage;
     const int Wl = a.g.W[s], Hl = a.g.H[s];
@@ -1139,6 +1163,7 @@ struct ContribShape {
 
 template <int A, int OUT, int QIN = 0>
 __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
+    pdl_enter();
     using Sh = ContribShape<A, OUT, QIN>;
     constexpr int BM = Sh::BM, BMP = Sh::BMP, CG = Sh::CG;
     constexpr int Q4 = OUT / 4;                  // float4 per qh row
@@ -1320,6 +1345,7 @@ struct LnShape {
 
 template <int A, int OUT>
 __global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 128)) k_ln(LnArgs a) {
+    pdl_enter();
     using Sh = LnShape<OUT>;
     constexpr int EV = Sh::EV, NT = Sh::NT, PPT = Sh::PPT;
     constexpr int ST = OUT + 1;                  // conflict-free lane-per-event rows
@@ -1464,6 +1490,7 @@ __global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 
 // 32 events per batch; X holds the features in E_4 row order.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
+    pdl_enter();
     __shared__ __align__(16) float x_s[96 * kMB];
     __shared__ __align__(16) float act_s[192 * kMB];
     __shared__ float res_s[kMB][24];
@@ -1564,6 +1591,7 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
 // ---------------------------------------------------------------------------
 template <int K, int OUT2, int BM, int BN>
 __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
+    pdl_enter();
     constexpr int J2 = 3 * OUT2;
     constexpr int TN = BN / 4;                  // column groups (threads per row group)
     static_assert((BM / 8) * TN == kNT, "tile shape");
@@ -1699,6 +1727,7 @@ __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
 // 887-901 ownership + version).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_commit(CommitArgs a) {
+    pdl_enter();
     const int p = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int W3 = a.g.W[3], H3 = a.g.H[3];
@@ -1856,10 +1885,28 @@ int grid_for(size_t n, int per_block, int cap = 148 * 16) {
 }
 }  // namespace
 
+// Launches a drain kernel with programmatic stream serialization: it may be
+// scheduled while the previous kernel of the stream drains, and waits for
+// it in pdl_enter / pdl_wait.  Errors surface through cudaGetLastError.
+template <typename... P, typename... A>
+void pdl_launch(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<P>(args)...);
+}
+
 void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
                  uint32_t* ev_xy, uint8_t* rflags) {
     if (n <= 0) return;
-    k_prep<<<grid_for(n, kNT), kNT, 0, st>>>(ev, n, W0, H0, ev_xy, rflags);
+    pdl_launch(k_prep, grid_for(n, kNT), kNT, 0, st, ev, n, W0, H0, ev_xy, rflags);
 }
 
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
@@ -1903,13 +1950,13 @@ void launch_records(cudaStream_t st, int n_cap, const int* count2, const StageEn
 void launch_filter(cudaStream_t st, const FilterArgs& a) {
     const int s = a.stage;
     if (s == 0)
-        k_filter<<<dim3(a.g.P, a.g.ty[0], a.g.nseg[0]), kNT, 0, st>>>(a);
+        pdl_launch(k_filter, dim3(a.g.P, a.g.ty[0], a.g.nseg[0]), kNT, 0, st, a);
     else
-        k_filter_tiles<<<dim3(a.g.P, a.g.tx[s] * a.g.ty[s], a.g.nseg[s]), kNT, 0, st>>>(a);
+        pdl_launch(k_filter_tiles, dim3(a.g.P, a.g.tx[s] * a.g.ty[s], a.g.nseg[s]), kNT, 0, st, a);
 }
 
 void launch_gates(cudaStream_t st, const GateArgs& a) {
-    k_gates<<<dim3(a.g.P, a.g.W[3] * a.g.H[3]), kGateNT, 0, st>>>(a);
+    pdl_launch(k_gates, dim3(a.g.P, a.g.W[3] * a.g.H[3]), kGateNT, 0, st, a);
 }
 
 void launch_gates_s2(cudaStream_t st, const Gate2Args& a) {
@@ -1918,20 +1965,20 @@ void launch_gates_s2(cudaStream_t st, const Gate2Args& a) {
 
 void launch_compact(cudaStream_t st, const CompactArgs& a) {
     const dim3 grid(a.g.P, a.tiles_per_part);
-    k_compact_count<<<grid, kNT, 0, st>>>(a);
-    k_compact_scan<<<1, kNT, 0, st>>>(a);
-    k_compact_scatter<<<grid, kNT, 0, st>>>(a);
+    pdl_launch(k_compact_count, grid, kNT, 0, st, a);
+    pdl_launch(k_compact_scan, 1, kNT, 0, st, a);
+    pdl_launch(k_compact_scatter, grid, kNT, 0, st, a);
 }
 
 void launch_scan(cudaStream_t st, int layer, const ScanArgs& a) {
     const int s = layer / 2;
     const dim3 grid(a.g.P, a.g.tx[s] * a.g.ty[s], (kTile * kTile) / (kNT / 32));
     switch (layer) {
-        case 0: k_scan<1, 12><<<grid, kNT, 0, st>>>(a); break;
-        case 1: k_scan<9, 12><<<grid, kNT, 0, st>>>(a); break;
-        case 2: case 3: k_scan<9, 24><<<grid, kNT, 0, st>>>(a); break;
-        case 4: case 5: k_scan<9, 48><<<grid, kNT, 0, st>>>(a); break;
-        default: k_scan<9, 96><<<grid, kNT, 0, st>>>(a); break;
+        case 0: pdl_launch(k_scan<1, 12>, grid, kNT, 0, st, a); break;
+        case 1: pdl_launch(k_scan<9, 12>, grid, kNT, 0, st, a); break;
+        case 2: case 3: pdl_launch(k_scan<9, 24>, grid, kNT, 0, st, a); break;
+        case 4: case 5: pdl_launch(k_scan<9, 48>, grid, kNT, 0, st, a); break;
+        default: pdl_launch(k_scan<9, 96>, grid, kNT, 0, st, a); break;
     }
 }
 
@@ -1941,7 +1988,7 @@ void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long 
         const long long units = ((max_rows + Sh::BM - 1) / Sh::BM) * (layer == 0 ? 1 : 9);
         const int grid = static_cast<int>(std::max(1LL, std::min(units, 148LL * 16)));
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Sh::smem));
-        kern<<<grid, kNT, Sh::smem, st>>>(a);
+        pdl_launch(kern, grid, kNT, Sh::smem, st, a);
     };
     switch (layer) {
         case 0: go(k_contrib<1, 12>, ContribShape<1, 12>{}); break;
@@ -1984,7 +2031,7 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
         const int s = layer / 2;
         const int items = a.g.P * a.g.tx[s] * a.g.ty[s] * 64;      // bound with every tile hot
         const int need = (items + (Sh::NT / 32) - 1) / (Sh::NT / 32);
-        kern<<<std::min(grid, need), Sh::NT, Sh::smem, st>>>(a);
+        pdl_launch(kern, std::min(grid, need), Sh::NT, Sh::smem, st, a);
     };
     switch (layer) {
         case 1: go(k_scan_group<12, 12, 8>, ScanGroupShape<12, 12, 8>{}); break;
@@ -1994,14 +2041,14 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
 }
 
 void launch_hot_tiles(cudaStream_t st, const HotArgs& a) {
-    k_hot_tiles<<<1, 1024, 0, st>>>(a);
+    pdl_launch(k_hot_tiles, 1, 1024, 0, st, a);
 }
 
 void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows) {
     auto go = [&](auto kern, auto shape) {
         using Sh = decltype(shape);
         const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + Sh::EV - 1) / Sh::EV, 148LL * 32)));
-        kern<<<grid, Sh::NT, 0, st>>>(a);
+        pdl_launch(kern, grid, Sh::NT, 0, st, a);
     };
     switch (layer) {
         case 0: go(k_ln<1, 12>, LnShape<12>{}); break;
@@ -2014,7 +2061,7 @@ void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows) 
 
 void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows) {
     const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + kMB - 1) / kMB, 148LL * 8)));
-    k_head<<<grid, kNT, 0, st>>>(a);
+    pdl_launch(k_head, grid, kNT, 0, st, a);
 }
 
 int gemm_cols(int layer, int colmode) {
@@ -2034,7 +2081,7 @@ void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_ro
         const int grid = static_cast<int>(std::max(1LL, std::min(units, 148LL * 12)));
         const size_t smem = sizeof(float) * static_cast<size_t>(K) * (BM + 4 + BN);
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        kern<<<grid, kNT, smem, st>>>(a);
+        pdl_launch(kern, grid, kNT, smem, st, a);
     };
     switch (layer) {                       // next layer: K = its IN, OUT2 = its OUT
         case 1: go(k_gemm<12, 12, 128, 64>, 12, 128, 64); break;
@@ -2049,7 +2096,7 @@ void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_ro
 
 void launch_commit(cudaStream_t st, const CommitArgs& a) {
     const int n3 = a.g.W[3] * a.g.H[3];
-    k_commit<<<dim3(a.g.P, (n3 + 7) / 8), kNT, 0, st>>>(a);
+    pdl_launch(k_commit, dim3(a.g.P, (n3 + 7) / 8), kNT, 0, st, a);
 }
 
 void launch_reset_preds(cudaStream_t st, const Geo& g, const PartState* parts, const DevHead& hd) {
