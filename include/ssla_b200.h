@@ -121,6 +121,19 @@ int  ssla_engine_drain_host(SslaEngine* eng, const float* events_host,
                             const int* part_offsets, uint8_t* flags_host,
                             void* stream);
 
+/* Pipelined form of ssla_engine_drain_host for pinned host buffers: the
+ * copy of the events runs on an engine-owned copy stream into one of two
+ * device buffers, so it overlaps the previous drain on `stream`.  The drain
+ * waits for it, then copies the flags (flags_host, may be NULL) and every
+ * partition's decoded predictions (preds_host, n_partitions x cells x
+ * (5+ncls) floats, may be NULL) back on `stream`.  Returns without
+ * waiting: the host buffers belong to the call until `stream` passes it.
+ * The shard threads of the reference overlap their ring pushes with the
+ * GPU drain the same way (src/lib_stage01_to_gpu.cpp:157-311). */
+int  ssla_engine_drain_host_async(SslaEngine* eng, const float* events_host,
+                                  const int* part_offsets, uint8_t* flags_host,
+                                  float* preds_host, void* stream);
+
 /* One event (t, x, y, p; host memory, passed by value to the kernel) of
  * `partition` through preprocess, the gates, stages 0-3 and the head in a
  * single launch -- the batch-of-1 path.  Leaves exactly the state a drain

@@ -110,7 +110,8 @@ F_VALID, F_R1, F_R2, F_R3, F_R4 = 1, 2, 4, 8, 16
 # Every symbol include/ssla_b200.h declares (tests check the .so exports them).
 EXPORTED = (
     "ssla_engine_create", "ssla_engine_destroy", "ssla_engine_reset",
-    "ssla_engine_drain_device", "ssla_engine_drain_host", "ssla_engine_state_bytes",
+    "ssla_engine_drain_device", "ssla_engine_drain_host", "ssla_engine_drain_host_async",
+    "ssla_engine_state_bytes",
     "ssla_engine_read_state", "ssla_engine_write_state", "ssla_engine_state_ptr",
     "ssla_engine_info", "ssla_s2s3_drain_n_multi", "ssla_s2s3_drain_n",
     "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak",

@@ -426,6 +426,12 @@ struct Engine {
         if (strip.err) cudaFreeHost(strip.err);
         if (step_err) cudaFreeHost(step_err);
         if (live_err) cudaFreeHost(live_err);
+        if (hpipe.st) cudaStreamSynchronize(hpipe.st);
+        for (int k = 0; k < 2; ++k) {
+            if (hpipe.copied[k]) cudaEventDestroy(hpipe.copied[k]);
+            if (hpipe.consumed[k]) cudaEventDestroy(hpipe.consumed[k]);
+        }
+        if (hpipe.st) cudaStreamDestroy(hpipe.st);
     }
 
     size_t state_elems(int kind, int index) const {
@@ -786,6 +792,50 @@ struct Engine {
             throw CudaError("k_live: a bounded wait ran out (status " + std::to_string(v) +
                             "; 1 weights, 2 layer input, 4 contributions, 8 event message, 16 completion)");
         return v;
+    }
+
+    // ---- pipelined host drains: copy-in on a copy stream, double-buffered ----
+    struct HostPipe {
+        cudaStream_t st = nullptr;
+        DevBuf ev[2];
+        cudaEvent_t copied[2] = {}, consumed[2] = {};
+        int slot = 0;
+    } hpipe;
+
+    // Events from pinned host memory: the copy of this drain's events runs on
+    // the engine's copy stream, into the device buffer the drain before last
+    // used, while earlier drains may still run on `st`; the drain waits for
+    // its copy, then its flags and all partitions' decoded predictions are
+    // copied back to flags_host / preds_host (either may be null) on `st`.
+    // Returns without waiting; the host buffers belong to the call until
+    // `st` has passed it.
+    void drain_host_async(const float* ev_host, const int* off, uint8_t* flags_host, float* preds_host,
+                          cudaStream_t st) {
+        const int n = off[g.P];
+        if (n < 0 || n > max_events) throw std::length_error("more events than max_events");
+        if (n > 0 && !ev_host) throw std::invalid_argument("null events");
+        if (!hpipe.st) {
+            SSLA_CK(cudaStreamCreateWithFlags(&hpipe.st, cudaStreamNonBlocking));
+            for (int k = 0; k < 2; ++k) {
+                hpipe.ev[k].alloc(static_cast<size_t>(max_events) * sizeof(float4));
+                SSLA_CK(cudaEventCreateWithFlags(&hpipe.copied[k], cudaEventDisableTiming));
+                SSLA_CK(cudaEventCreateWithFlags(&hpipe.consumed[k], cudaEventDisableTiming));
+                SSLA_CK(cudaEventRecord(hpipe.consumed[k], hpipe.st));
+            }
+        }
+        const int k = hpipe.slot;
+        hpipe.slot ^= 1;
+        SSLA_CK(cudaStreamWaitEvent(hpipe.st, hpipe.consumed[k], 0));
+        if (n > 0)
+            SSLA_CK(cudaMemcpyAsync(hpipe.ev[k].p, ev_host, sizeof(float) * 4 * n, cudaMemcpyHostToDevice, hpipe.st));
+        SSLA_CK(cudaEventRecord(hpipe.copied[k], hpipe.st));
+        SSLA_CK(cudaStreamWaitEvent(st, hpipe.copied[k], 0));
+        drain(hpipe.ev[k].as<float>(), off, nullptr, st);
+        SSLA_CK(cudaEventRecord(hpipe.consumed[k], st));
+        if (flags_host && n > 0)
+            SSLA_CK(cudaMemcpyAsync(flags_host, ws.rflags.p, n, cudaMemcpyDeviceToHost, st));
+        if (preds_host)
+            SSLA_CK(cudaMemcpyAsync(preds_host, preds_dec.p, preds_dec.n, cudaMemcpyDeviceToHost, st));
     }
 
     // ---- ring drains (ssla_rings.cu): one pinned ring per partition ----
@@ -1347,6 +1397,17 @@ int ssla_engine_drain_device(SslaEngine* eng, const float* events_dev, const int
     }
     return ssla::guarded([&] {
         eng->e.drain(events_dev, part_offsets, flags_dev, static_cast<cudaStream_t>(stream));
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_drain_host_async(SslaEngine* eng, const float* events_host, const int* part_offsets,
+                                 uint8_t* flags_host, float* preds_host, void* stream) {
+    if (!eng || !part_offsets) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        eng->e.drain_host_async(events_host, part_offsets, flags_host, preds_host,
+                                static_cast<cudaStream_t>(stream));
         return SSLA_OK;
     });
 }

@@ -44,6 +44,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_reset": (i, [vp, vp]),
         "ssla_engine_drain_device": (i, [vp, vp, vp, vp, vp]),
         "ssla_engine_drain_host": (i, [vp, vp, vp, vp, vp]),
+        "ssla_engine_drain_host_async": (i, [vp, vp, vp, vp, vp, vp]),
         "ssla_engine_state_bytes": (i, [vp, i, i, C.POINTER(C.c_size_t)]),
         "ssla_engine_read_state": (i, [vp, i, i, i, vp, C.c_size_t]),
         "ssla_engine_write_state": (i, [vp, i, i, i, vp, C.c_size_t]),
@@ -168,6 +169,15 @@ class SslaEngine:
         off = np.ascontiguousarray(part_offsets, dtype=np.int32)
         _check(self.lib.ssla_engine_drain_host(self.h, _ptr(events), off.ctypes.data,
                                                _ptr(flags), _stream(stream)))
+
+    def drain_host_async(self, events, part_offsets, flags=None, preds=None, stream=None) -> None:
+        """Pipelined host drain: pinned ``events`` in (copied on the engine's
+        copy stream, overlapping the previous drain), flags and all decoded
+        predictions (``preds``: (P, cells, 5+ncls) float32, pinned) out on
+        ``stream``; returns without waiting."""
+        off = np.ascontiguousarray(part_offsets, dtype=np.int32)
+        _check(self.lib.ssla_engine_drain_host_async(self.h, _ptr(events), off.ctypes.data, _ptr(flags),
+                                                     _ptr(preds), _stream(stream)))
 
     def step(self, event, partition: int = 0, flag_out=None, pred_out=None, stream=None) -> None:
         """One event (4 floats t, x, y, p) through the whole path in one

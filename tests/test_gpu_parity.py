@@ -191,3 +191,42 @@ def test_config1_full_size(oracle_mod, stub_dir):
         flags, so = orc.run_events(b)
         oracles.append((orc, flags, so))
     assert_engine_equals_oracle(eng, oracles, second, abi.LAYOUT_HYBRID)
+
+
+def test_pipelined_host_drains_match_sync(stub_dir):
+    """ssla_engine_drain_host_async (copies on the engine's copy stream,
+    two device buffers in turn, results copied back on the caller's stream)
+    gives, drain for drain, the flags, predictions and state of the
+    synchronous host path, with several drains in flight."""
+    d = stub_dir(64, 80, 1, 4)
+    parts = E.split_partitions(E.config_events(1, n=40_000, seed=31), 4)
+    base = np.ascontiguousarray(np.concatenate(parts))
+    span = float(base[:, 0].max()) + 1.0
+    off = np.array([0] + list(np.cumsum([len(p) for p in parts])), np.int32)
+    n = len(base)
+    sync = _engine(d, n_partitions=4, max_events=n, layout=abi.LAYOUT_HYBRID,
+                   max_events_per_partition=max(len(p) for p in parts))
+    pipe = _engine(d, n_partitions=4, max_events=n, layout=abi.LAYOUT_HYBRID,
+                   max_events_per_partition=max(len(p) for p in parts))
+    steps = 4
+    ins = [torch.from_numpy(base.copy()).pin_memory() for _ in range(steps)]
+    for k in range(steps):
+        ins[k][:, 0] += span * k
+    flags = [torch.zeros(n, dtype=torch.uint8).pin_memory() for _ in range(steps)]
+    preds = [torch.zeros(tuple(sync.preds_dec_all().shape), dtype=torch.float32).pin_memory()
+             for _ in range(steps)]
+    stream = torch.cuda.current_stream()
+    for k in range(steps):
+        pipe.drain_host_async(ins[k], off, flags[k], preds[k], stream=stream)
+    torch.cuda.synchronize()
+    for k in range(steps):
+        f = np.zeros(n, np.uint8)
+        sync.drain_host(ins[k].numpy(), off, f)
+        np.testing.assert_array_equal(flags[k].numpy(), f, err_msg=f"flags of drain {k}")
+        np.testing.assert_array_equal(preds[k].numpy(), sync.preds_dec_all(), err_msg=f"preds of drain {k}")
+    for p in range(4):
+        for l in range(8):
+            np.testing.assert_array_equal(pipe.hidden(l, p), sync.hidden(l, p))
+        np.testing.assert_array_equal(pipe.version(p), sync.version(p))
+    sync.close()
+    pipe.close()
