@@ -921,7 +921,7 @@ def main() -> int:
     line = None
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             cpu = cpu_baseline(parts, wdir)
         line = {
             "metric": METRIC, "value": value, "unit": "Mev/s", "n_gpus": world,
