@@ -34,17 +34,15 @@ __device__ __forceinline__ unsigned lanemask_lt() {
 
 __device__ __forceinline__ int hi_lane(unsigned m) { return 31 - __clz(m); }
 
-// Programmatic dependent launch: a drain kernel lets the next one in the
-// stream be scheduled once all of its own CTAs have started, and waits for
-// the previous kernel to complete (and its memory to be visible) before
-// touching anything that kernel may write.  Without the launch attribute
-// both are no-ops.
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Programmatic dependent launch: a drain kernel is launched while the
+// previous one in the stream completes and waits here for it to complete
+// (and its memory to be visible) before touching anything it may write.
+// No kernel triggers its dependants early: CTAs of the next kernel waiting
+// on the SMs slowed the running one (measured), so the dependant is
+// released at completion and only the launch latency overlaps.  Without
+// the launch attribute the wait is a no-op.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_enter() {
-    pdl_trigger();
-    pdl_wait();
-}
+__device__ __forceinline__ void pdl_enter() { pdl_wait(); }
 
 // uint8 counter rule of tdrop_check_at (src/ssla_kernels.cpp:912-921) and
 // parallel_tdrop (ssla_s2_s3_head_celled.cuh:742-745): pass iff window <= 1
@@ -929,8 +927,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
     float* Qs = Ws + 9 * DS + warp * (Sh::per_warp / sizeof(float));   // [32][QR]
     int* qk = reinterpret_cast<int*>(Qs + 32 * QR);                    // [QCAP] entry
     unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<6
-    pdl_trigger();
-    // the weights are constant: staged while the previous kernel finishes
+    // the weights are constant: staged before the wait
     for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
         const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
         *reinterpret_cast<float4*>(Ws + d * DS + 4 * r) = __ldg(reinterpret_cast<const float4*>(a.W) + t);
