@@ -74,7 +74,7 @@ def patches(coords_xy: np.ndarray, s: int) -> np.ndarray:
 
 
 def algorithmic_macs(ev: np.ndarray, flags: np.ndarray) -> dict:
-    """MACs per layer (survey 8(d) model with exact in-bounds patch counts):
+    """MACs per layer (the per-layer work model of the path, with exact in-bounds patch counts):
     vg / q = the v,g and q rows of the fused qvg matvec, gather = the goW
     contributions, resid = input_proj; plus the head."""
     from ssla_rt_b200 import abi
