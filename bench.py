@@ -20,6 +20,13 @@ e2e    = same metric through ssla_engine_drain_host_async (pinned host events
          inside the timing; step k+1's copy-in overlaps step k's drain)
 N > 1  = one rank per GPU (torchrun), each drains its own 200k-event set
          (weak scaling, no collective on the data path).
+parity = BASELINE config 0 in full (50,000 events) through the engine and
+         through the reference's own C++ pipeline (oracle/_ref): drop drift,
+         max|d| s3_feat, per-stage and per-layer max|d| (rank 0, untimed)
+strips = config 3 (10,000,000 events at 320x256) in N exact strips, one per
+         GPU (strong scaling), device-timed with clocks and exchange status,
+         with its own parity check of every rank's owned results against one
+         sensor on the stream's first 200,000 events
 """
 from __future__ import annotations
 
@@ -101,9 +108,11 @@ def total_macs(macs: dict) -> int:
 
 def phase_flops(macs: dict, name: str) -> float:
     """Algorithmic FLOPs of one engine phase (2 per MAC).  Layers 1-3 compute
-    their qvg matvecs inside the scan; layers 4-7 in GEMM phases; k_ln of a
-    stage's second layer also computes the next stage's input_proj
-    residual; gates covers layer 0."""
+    their v and g rows inside the scan and their q rows (for events whose
+    output is used) in the contribution GEMM, before the goW products;
+    layers 4-7 build q, v, g in GEMM phases; k_ln of a stage's second layer
+    also computes the next stage's input_proj residual; gates covers layer
+    0."""
     parts = name.split("_")
     if name == "head":
         return 2.0 * macs["head"]
@@ -115,9 +124,9 @@ def phase_flops(macs: dict, name: str) -> float:
     l = int(parts[1][1])
     m = macs[l]
     if parts[0] == "scan":
-        return 2.0 * (m["vg"] + m["q"]) if l <= 3 else 0.0
+        return 2.0 * m["vg"] if l <= 3 else 0.0
     if parts[0] == "contrib":
-        return 2.0 * m["gather"]
+        return 2.0 * (m["gather"] + (m["q"] if l <= 3 else 0))
     if parts[0] == "ln":
         return 2.0 * (macs[l + 1]["resid"] if (l % 2 == 1 and l < 7) else 0)
     if parts[0] == "gemm":
@@ -175,6 +184,30 @@ class ClockSampler:
 # CPU baseline: the reference's own SslaSPipeline (oracle/_ref), else the
 # C restatement (oracle/), same 8 independent streams, host threads.
 # ---------------------------------------------------------------------------
+def host_info() -> dict:
+    """CPU model and core counts of this host (the CPU baseline's yardstick)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        usable = os.cpu_count()
+    return {"cpu_model": model, "host_cores": os.cpu_count(), "usable_cores": usable}
+
+
+CPU_CLAIM = ("value: one host thread per independent stream (each stream is sequential, so a stream "
+             "cannot use more than one thread; threads = min(streams, usable cores)); single_thread: "
+             "the reference pipeline's own sequential semantics on one core, the yardstick of the "
+             ">=100x target")
+
+
 def cpu_baseline(parts, weights_dir: str, reps: int = 3, threads: int = 0, sample: str = "") -> dict:
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle as O
@@ -202,11 +235,14 @@ def cpu_baseline(parts, weights_dir: str, reps: int = 3, threads: int = 0, sampl
     return {"value": n / best / 1e6, "unit": "Mev/s", "cores": threads, "kind": kind,
             "sample": (sample or f"the full step workload: {len(parts)} independent streams x "
                                  f"{len(parts[0])} events, one host thread per stream") + f", best of {reps}",
-            "single_thread": single}
+            "single_thread": single, **host_info(), "claim": CPU_CLAIM}
+
+
+LAT_SAMPLES = 280_000            # ~1,100 head events at tdrop 4 (0.4 % of a uniform stream)
 
 
 def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
-                    warmup: int = 500, samples: int = 20000) -> dict:
+                    warmup: int = 500, samples: int = LAT_SAMPLES) -> dict:
     """Batch-of-1 emit -> prediction latency of a live stream, p50 / p99 in
     us, over all events and over the events that produced a prediction.
 
@@ -246,8 +282,66 @@ def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
                      "event the host publishes the ring head and spins on events_done (the reference's "
                      "persistent-kernel protocol), host steady_clock from publish to completion seen, in "
                      "the library's C++ loop; step: one 9-CTA cluster launch per event + stream synchronize; "
-                     "head_* over events that produced a prediction; config-0 uniform stream, tdrop 4")
+                     "head_* over events that produced a prediction (the reference's latency population); "
+                     f"a {samples:,}-event stream with config 0's distribution (uniform 80x64, Poisson "
+                     "2 Mev/s), tdrop 4")
     return res
+
+
+PARITY_TOL_STAGE = 1e-3          # stated per-stage fp32 tolerance against the reference build
+PARITY_S3_BUDGET = 5.0           # the reference's own P1 budget on max|d| s3_feat
+
+
+def acceptance_parity(weights_dir: str, device: int) -> dict:
+    """BASELINE config 0 in full -- 50,000 uniform events at 80x64, seed 0 --
+    through the engine (one drain on `device`) and through the reference's
+    own C++ pipeline (oracle/_ref; the C restatement when that is absent):
+    drop drift (events whose gate flags differ), max|d| s3_feat over the
+    events that reach the head (the reference's P1 gates,
+    orin/bench_s2_s3_head_celled.py:285-332), per-stage and per-layer
+    max|d|, and the decoded predictions.  Runs outside any timed region."""
+    import torch
+    from ssla_rt_b200 import abi, events
+    from ssla_rt_b200.engine import SslaEngine
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    ev = events.config_events(0)
+    n = len(ev)
+    eng = SslaEngine(weights_dir, n_partitions=1, max_events=n, layout=abi.LAYOUT_HYBRID, device=device,
+                     record_stage_outputs=True)
+    eng.drain(torch.from_numpy(np.ascontiguousarray(ev)).to(torch.device("cuda", device)), [0, n])
+    torch.cuda.synchronize(device)
+    flags = eng.flags(n)
+    so = [eng.stage_out(st, n) for st in range(4)]
+    hid = [eng.hidden(l) for l in range(8)]
+    preds = eng.preds_dec(0)
+    eng.close()
+    if os.path.exists(O.REF_SO):
+        ref = O.RefPipeline(weights_dir, O.LAYOUT_HYBRID)
+        kind = "reference build (the reference's own SslaSPipeline, oracle/_ref)"
+        rpreds = lambda: ref.predictions()  # noqa: E731
+    else:
+        ref = O.Oracle(O.load_npz(weights_dir), H, W, 4, O.LAYOUT_HYBRID)
+        kind = "C restatement (oracle/_ref absent)"
+        rpreds = lambda: ref.preds_dec()  # noqa: E731
+    rflags, rso = ref.run_events(ev)
+    bits = [abi.F_R1, abi.F_R2, abi.F_R3, abi.F_R4]
+    stage = []
+    for st in range(4):
+        m = (rflags & bits[st]) != 0
+        stage.append(float(np.abs(so[st][m] - rso[st][m]).max()) if m.any() else 0.0)
+    hidden = [float(np.abs(hid[l] - ref.hidden(l)).max()) for l in range(8)]
+    dpred = float(np.abs(preds - rpreds()).max())
+    drift = int((flags != rflags).sum())
+    ok = drift == 0 and stage[3] <= PARITY_S3_BUDGET and max(stage + hidden + [dpred]) <= PARITY_TOL_STAGE
+    return {"workload": "config0: 50,000 uniform events at 80x64 (seed 0, Poisson 2 Mev/s), one stream, "
+                        "full s0..s3 + head",
+            "against": kind, "drop_drift": drift, "max_abs_s3_feat": stage[3], "max_abs_stage": stage,
+            "max_abs_hidden": hidden, "max_abs_preds": dpred,
+            "events_reaching_stage": [int(((rflags & b) != 0).sum()) for b in bits],
+            "tolerance": {"drop_drift": 0, "s3_feat": PARITY_S3_BUDGET, "stage_hidden_preds": PARITY_TOL_STAGE},
+            "ok": ok}
 
 
 def measured_traffic(phase: str):
@@ -263,16 +357,21 @@ def measured_traffic(phase: str):
         return None
 
 
-def run_reference(args, rank: int) -> None:
+def run_reference(args, rank: int, world: int) -> None:
+    """The reference's own CPU pipeline on the work of all `world` ranks of
+    our arm (each rank's 8 streams with that rank's seed), on rank 0, with
+    one host thread per stream up to the usable cores."""
     if rank != 0:
         return
     from ssla_rt_b200 import stub
     with tempfile.TemporaryDirectory() as d:
         stub.write_stub(d, h=H, w=W, seed=1, tdrop=4)
-        parts = workload(0)
+        parts = [p for r in range(world) for p in workload(r)]
+        n_events = sum(len(p) for p in parts)
         sys.path.insert(0, os.path.join(REPO, "oracle"))
         import oracle as O
-        threads = min(len(parts), os.cpu_count() or 1)
+        hi = host_info()
+        threads = max(1, min(len(parts), hi["usable_cores"] or 1))
         kind = "reference" if os.path.exists(O.REF_SO) else "port"
         times = []
         for i in range(args.warmup + args.steps):
@@ -280,12 +379,12 @@ def run_reference(args, rank: int) -> None:
             if kind == "reference":
                 dt = O.RefPipeline(d, O.LAYOUT_HYBRID).time_streams(parts, threads)
             else:
-                dt = cpu_baseline(parts, d, reps=1)["value"]
-                dt = N_EVENTS / (dt * 1e6)
+                dt = cpu_baseline(parts, d, reps=1, threads=threads)["value"]
+                dt = n_events / (dt * 1e6)
             if i >= args.warmup:
                 times.append(dt)
         total = sum(times)
-        value = N_EVENTS * args.steps / total / 1e6
+        value = n_events * args.steps / total / 1e6
         line = {
             "impl": "reference", "metric": METRIC, "value": value, "unit": "Mev/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -293,8 +392,9 @@ def run_reference(args, rank: int) -> None:
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_dict(),
             "cpu_baseline": {"value": value, "unit": "Mev/s", "cores": threads, "kind": kind,
-                             "sample": f"{N_PARTS} independent streams x {N_EVENTS // N_PARTS} events "
-                                       f"per step, one host thread per stream"},
+                             "sample": f"the work of all {world} rank(s) of our arm: {len(parts)} independent "
+                                       f"streams x {N_EVENTS // N_PARTS} events per step, one host thread per "
+                                       f"stream up to the usable cores", **hi, "claim": CPU_CLAIM},
             "e2e": {"value": value, "unit": "Mev/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
         print(json.dumps(line), flush=True)
@@ -323,38 +423,61 @@ STRIP_GLOBAL_CHUNK = 10_000_000  # exact mode: global stream events per aligned 
 STRIP_BAND = 16                  # exact mode: band rows (2 stage-3 rows)
 
 
-def run_strips(args, rank: int, world: int, local: int) -> int:
-    """Strong scaling: the one 10M-event stream of config 3 split into `world`
+STRIP_PARITY_EVENTS = 200_000    # prefix of the stream checked against one sensor
+
+
+def strips_measure(args, rank: int, world: int, local: int, steps: int, warmup: int) -> dict:
+    """Strong scaling of config 3: the one 10M-event stream split into `world`
     horizontal strips (ssla_rt_b200/strips.py), one per rank, drained in
     stream order.  value = the stream's events / the slowest rank's device
-    time.
+    time.  Needs the process group when world > 1.  Returns the measurement
+    on rank 0 (None elsewhere).
 
     exact (default): each rank drains its own rows plus a 16-row band of each
     neighbour's rows and, after every layer, exchanges the band events' next-
     layer inputs with its neighbours (ssla_engine_strip_drain, peer memory
     over NVLink through CUDA IPC handles); owned results equal the single-
-    sensor run bit for bit.  Chunks are aligned on the global stream (chunk c
-    = global events [c*G, (c+1)*G)), so neighbours exchange for the same
-    events.
+    sensor run bit for bit, which `parity` checks on the stream's first
+    200,000 events (every rank against one sensor drained on its own GPU).
+    Chunks are aligned on the global stream (chunk c = global events
+    [c*G, (c+1)*G)), so neighbours exchange for the same events.
     halo: the reference's replication -- own rows plus a halo, no exchange,
     approximate near the edges."""
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
 
     from ssla_rt_b200 import abi, events, strips, stub
     from ssla_rt_b200.engine import SslaEngine
 
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     wdir = tempfile.mkdtemp(prefix="ssla_stub_")
     stub.write_stub(wdir, h=STRIP_H, w=STRIP_W, seed=1, tdrop=4)
     ev_all = events.config_events(3)
     span = float(ev_all[:, 0].max()) + 1.0
     exact = args.strip_mode == "exact"
     band = STRIP_BAND if exact else args.halo_rows
+    parity = None
+    if exact:       # outside the timed region: owned results against one sensor
+        parity = strips.exact_strip_parity(wdir, ev_all[:STRIP_PARITY_EVENTS], rank, world, local,
+                                           dist.all_gather_object if world > 1 else None, barrier, band)
+        if world > 1:
+            allp = [None] * world
+            dist.all_gather_object(allp, parity)
+            parity = allp
+        else:
+            parity = [parity]
     lo, hi = strips.strip_bounds(STRIP_H, world)[rank]
     mask = strips.route_mask(ev_all, lo, hi, STRIP_H, band)
     gidx = np.nonzero(mask)[0]
@@ -374,14 +497,7 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     if exact:
         eng.strip_init(lo, hi, band, rank > 0, rank < world - 1, max(1, cap_ev // 2))
         if world > 1:
-            mine = [eng.strip_recv_buffer(sd)[1] if (sd == 0 and rank > 0) or (sd == 1 and rank < world - 1)
-                    else None for sd in (0, 1)]
-            allh = [None] * world
-            dist.all_gather_object(allh, mine)
-            if rank > 0:
-                eng.strip_connect(0, peer_handle=allh[rank - 1][1])
-            if rank < world - 1:
-                eng.strip_connect(1, peer_handle=allh[rank + 1][0])
+            strips.connect_exact(eng, rank, world, dist.all_gather_object)
             dist.barrier()
     else:
         eng.set_owned(0, *strips.owned_s2(lo, hi, STRIP_W))
@@ -396,18 +512,7 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
             elif c1 > c0:
                 eng.drain(ev[c0:c1], [0, c1 - c0], stream=stream)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         ev[:, 0] += span
         one_pass()
     torch.cuda.synchronize(dev)
@@ -418,7 +523,7 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     total_ms = 0.0
     barrier()
     torch.cuda.synchronize(dev)
-    for _ in range(args.steps):
+    for _ in range(steps):
         ev[:, 0] += span
         flush.fill_(1.0)
         barrier()
@@ -435,16 +540,16 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     status = eng.strip_status() if exact else 0
     my_ms = total_ms
     total_ms = max_over_ranks(total_ms)
-    value = STRIP_EVENTS * args.steps / (total_ms * 1e-3) / 1e6
+    value = STRIP_EVENTS * steps / (total_ms * 1e-3) / 1e6
 
     # e2e: pinned host events copied in per chunk (halo: with flags out)
     host = torch.from_numpy(sev).pin_memory()
-    host[:, 0] += span * (args.warmup + args.steps + 1)
+    host[:, 0] += span * (warmup + steps + 1)
     host_np = host.numpy()
     host_flags = torch.empty(max(1, cap_ev), dtype=torch.uint8).pin_memory().numpy()
     barrier()
     e2e_s = 0.0
-    for _ in range(args.steps):
+    for _ in range(steps):
         host[:, 0] += span
         flush.fill_(2.0)
         torch.cuda.synchronize(dev)
@@ -459,7 +564,7 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
         preds = eng.preds_dec(0)
         e2e_s += time.perf_counter() - t0
     e2e_s = max_over_ranks(e2e_s)
-    e2e = STRIP_EVENTS * args.steps / e2e_s / 1e6
+    e2e = STRIP_EVENTS * steps / e2e_s / 1e6
     status = status | (eng.strip_status() if exact else 0)
 
     routed = torch.tensor([n, int(own.sum()), status], dtype=torch.int64, device=dev)
@@ -469,35 +574,74 @@ def run_strips(args, rank: int, world: int, local: int) -> int:
     if world > 1:
         dist.all_gather(per_rank, routed)
         dist.all_gather(all_ms, rank_ms)
+    eng.close()
+    del ev, flush
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    how = ("exact: per-layer exchange of band-event inputs between neighbouring strips over peer memory "
+           f"(band {band} rows), owned results bit-identical to one sensor" if exact else
+           f"halo replication ({band} rows), no exchange")
+    out = {
+        "value": value, "unit": "Mev/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": total_ms / steps, "scaling": "strong",
+        "workload": f"config3: 10,000,000 events at 320x256 (70% from 16 moving Gaussian blobs sigma 4, 30% "
+                    f"uniform, Poisson 20 Mev/s) in {world} horizontal strip(s), one per GPU, full s0..s3 + "
+                    f"YOLOX head; {how}",
+        "chunk_events": G, "chunking": "global stream ranges" if exact else "per-rank",
+        "strip_mode": args.strip_mode, "band_rows": band,
+        "bounds": strips.strip_bounds(STRIP_H, world),
+        "routed_events": [int(x[0]) for x in per_rank],
+        "owned_events": [int(x[1]) for x in per_rank],
+        "exchange_status": [int(x[2]) for x in per_rank],
+        "rank_ms": [float(x.item()) / steps for x in all_ms],
+        "clocks": clk,
+        "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(sev.nbytes),
+                "d2h_bytes_per_step": int(preds.nbytes + (0 if exact else n))},
+        "gpu_launches": launches,
+        "timing": "device time (CUDA events) of each pass over the whole stream, max over ranks; L2 flushed "
+                  "between passes (256 MiB write, untimed); inputs 160 MB > L2",
+    }
+    if parity is not None:
+        out["parity"] = {
+            "ok": all(p["ok"] for p in parity),
+            "against": "one sensor drained by the same engine on each rank's GPU (itself bit-identical to the "
+                       "C oracle); every rank compares its owned flags, hidden rows of every layer, counters, "
+                       "predictions and versions",
+            "events": STRIP_PARITY_EVENTS, "per_rank": parity}
+    return out
+
+
+def run_strips(args, rank: int, world: int, local: int) -> int:
+    """`--workload strips`: config 3 as the line's own metric."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    m = strips_measure(args, rank, world, local, args.steps, args.warmup)
     if rank == 0:
-        how = ("exact: per-layer exchange of band-event inputs between neighbouring strips over peer memory "
-               f"(band {band} rows), owned results bit-identical to one sensor" if exact else
-               f"halo replication ({band} rows), no exchange")
         line = {
-            "metric": METRIC, "value": value, "unit": "Mev/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "metric": METRIC, "value": m["value"], "unit": "Mev/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": f"config3: 10,000,000 events at 320x256 (70% from 16 moving Gaussian blobs "
-                                   f"sigma 4, 30% uniform, Poisson 20 Mev/s) in {world} horizontal strip(s), one "
-                                   f"per GPU, full s0..s3 + YOLOX head; {how}",
+            "config": {"workload": m["workload"],
                        "model": "SSLA-S stub (320x256, seed 1, tdrop 4)", "events_per_step": STRIP_EVENTS,
-                       "chunk_events": G, "chunking": "global stream ranges" if exact else "per-rank",
-                       "strip_mode": args.strip_mode, "band_rows": band,
+                       "chunk_events": m["chunk_events"], "chunking": m["chunking"],
+                       "strip_mode": m["strip_mode"], "band_rows": m["band_rows"],
                        "l2": "flushed between steps (256 MiB write, untimed); inputs 160 MB > L2",
                        "parallelism": f"strips{world}"},
-            "strips": {"bounds": strips.strip_bounds(STRIP_H, world),
-                       "routed_events": [int(x[0]) for x in per_rank],
-                       "owned_events": [int(x[1]) for x in per_rank],
-                       "exchange_status": [int(x[2]) for x in per_rank],
-                       "rank_ms": [float(x.item()) / args.steps for x in all_ms]},
-            "clocks": clk,
-            "e2e": {"value": e2e, "unit": "Mev/s", "h2d_bytes_per_step": int(sev.nbytes),
-                    "d2h_bytes_per_step": int(preds.nbytes + (0 if exact else n))},
-            "gpu_launches": launches,
+            "strips": {k: m[k] for k in ("bounds", "routed_events", "owned_events", "exchange_status",
+                                         "rank_ms")},
+            "clocks": m["clocks"], "e2e": m["e2e"], "gpu_launches": m["gpu_launches"],
         }
+        if "parity" in m:
+            line["parity"] = m["parity"]
         print(json.dumps(line), flush=True)
-    eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -747,6 +891,9 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true", help="skip the batch-of-1 latency samples")
+    ap.add_argument("--no-parity", action="store_true", help="skip the config-0 parity check against the reference")
+    ap.add_argument("--no-strips", action="store_true",
+                    help="skip the config-3 strips measurement carried by the default line")
     ap.add_argument("--workload", default="config1", choices=["config1", "config2", "strips", "streams"],
                     help="config1: 80x64 partitions per GPU (weak scaling); config2: one clustered "
                          "80x64 stream of 1 M events per GPU (hot cells); strips: config 3, one "
@@ -766,7 +913,7 @@ def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return 0
     if args.workload == "strips":
         return run_strips(args, rank, world, local)
@@ -888,9 +1035,10 @@ def main() -> int:
     d2h = N_EVENTS + host_preds[0].numel() * 4
     del staged
 
-    # ---- batch-of-1 latency: one event in, its predictions out ----
+    # ---- batch-of-1 latency: one event in, its predictions out (rank 0) ----
     from ssla_rt_b200 import events as ev_gen
-    latency = None if args.no_latency else measure_latency(wdir, ev_gen.config_events(0, n=50_000), local)
+    latency = None if (args.no_latency or rank != 0) else measure_latency(
+        wdir, ev_gen.config_events(0, n=LAT_SAMPLES + 500), local)
 
     # ---- roofline of the dominant phase (live CUDA-event durations) ----
     flags_dev = torch.zeros(N_EVENTS, dtype=torch.uint8, device=dev)
@@ -917,6 +1065,18 @@ def main() -> int:
                   "phase); the headline value is timed without them",
     }
     phases = {k: round(v[0] / v[1], 4) for k, v in sorted(phase_acc.items(), key=lambda kv: -kv[1][0])}
+    stage_events = [int(x) for x in eng.info().stage_events]
+    eng.close()
+    del ev, flush, flags_dev
+    torch.cuda.empty_cache()
+
+    # ---- acceptance parity: config 0 against the reference build (rank 0) ----
+    parity = None if (args.no_parity or rank != 0) else acceptance_parity(wdir, local)
+
+    # ---- config 3 in N strips (the north star's strong-scaling target) ----
+    strips_line = None
+    if not args.no_strips:
+        strips_line = strips_measure(args, rank, world, local, max(2, min(args.steps, 5)), 3)
 
     line = None
     if rank == 0:
@@ -936,11 +1096,12 @@ def main() -> int:
             "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
             "latency_us": latency,
             "algorithmic_mac_per_event": tot_macs / N_EVENTS,
-            "stage_events": [int(x) for x in eng.info().stage_events],
+            "stage_events": stage_events,
             "phase_ms": phases,
+            "parity": parity,
+            "strips": strips_line,
         }
         print(json.dumps(line), flush=True)
-    eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

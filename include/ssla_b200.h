@@ -197,6 +197,15 @@ int  ssla_engine_live_start(SslaEngine* eng, int partition, const SslaLiveRing* 
  * bits.  Returns SSLA_ERR_CUDA if a wait inside the loop ran out. */
 int  ssla_engine_live_join(SslaEngine* eng, unsigned* status);
 
+/* Test hook for the loop's timeout path, no reference counterpart: the next
+ * live loop started on `eng` withholds the completion message of ring event
+ * `ring_index` (-1: none) from its head CTA.  The head CTA's bounded wait
+ * then runs out, every CTA leaves through the loop's exit barrier, and
+ * ssla_engine_live_join reports SSLA_LIVE_ERR_DONE in *status and returns
+ * SSLA_ERR_CUDA; events before `ring_index` are finished normally.  Not
+ * allowed while a loop is running. */
+int  ssla_engine_live_withhold_completion(SslaEngine* eng, long long ring_index);
+
 /* Batch-of-1 latency through the live loop: publishes the n events (host
  * array of 4-float rows) one at a time into a pinned ring and records, per
  * event, the host time from publishing the event to observing
@@ -391,12 +400,16 @@ int  ssla_s2s3_drain_n(const HybridS2S3Config* cfg,
  * order per block), advances cfg's tdrop counters in place and writes the
  * pass2 / pass3 codes of each output slot exactly as the drain would; hidden
  * state and s3_feat are untouched.  Scratch lives in a fixed file-scope
- * device array: at most SSLA_NOALLOC_MAX_RECORDS records per call (larger
- * calls fail with SSLA_ERR_CAPACITY).  Enqueues on `stream` and returns
- * without synchronising.  The first call on a device looks the scratch array
+ * device array of 864 KiB per device: at most SSLA_NOALLOC_MAX_RECORDS
+ * records and SSLA_NOALLOC_MAX_CELLS blocks x stage-3 cells per call (larger
+ * calls fail with SSLA_ERR_CAPACITY).  Work is linear in the records (they
+ * are bucketed by stage-3 cell inside the scratch before the gates).
+ * Enqueues on `stream` and returns without synchronising.  The first call on
+ * a device (and the first after its context changed) looks the scratch array
  * up and should precede any stream capture on that device; calls that
  * overlap in time on one device share the scratch and race. */
 #define SSLA_NOALLOC_MAX_RECORDS 65536
+#define SSLA_NOALLOC_MAX_CELLS 65535
 int  ssla_s2s3_gate_codes_noalloc(const HybridS2S3Config* cfg,
                                   const HybridInputRec* const* rings, const int* ns,
                                   HybridS2S3OutputSlot* const* outs, void* stream);

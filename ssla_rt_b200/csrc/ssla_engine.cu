@@ -410,6 +410,7 @@ struct Engine {
     unsigned* live_err = nullptr;
     cudaStream_t live_stream = nullptr;
     bool live_running = false;
+    unsigned long long live_withhold = ~0ull;   // test hook for the next live loop (~0: off)
     cudaEvent_t off_done[kOffSlots] = {};
     int off_slot = 0;
     long long last_counts[5] = {0};
@@ -776,6 +777,8 @@ struct Engine {
         a.start = __atomic_load_n(r.tail, __ATOMIC_ACQUIRE);
         a.idle_ns = static_cast<unsigned long long>(idle_ms) * 1000000ull;
         a.err = live_err;
+        a.withhold_fin = live_withhold;
+        live_withhold = ~0ull;
         __atomic_store_n(live_err, 0u, __ATOMIC_RELEASE);
         SSLA_CK(launch_live(st, a));
         check_launch("k_live");
@@ -783,15 +786,19 @@ struct Engine {
         live_running = true;
     }
 
-    unsigned live_join() {
+    // Waits for the loop to end and returns its status word; with `check`,
+    // a wait that ran out inside the loop is raised as an error.
+    unsigned live_join(bool check = true) {
         if (!live_running) throw std::invalid_argument("no live loop is running on this engine");
         live_running = false;
         SSLA_CK(cudaStreamSynchronize(live_stream));
         const unsigned v = __atomic_load_n(live_err, __ATOMIC_ACQUIRE);
-        if (v & 0xFFu)
-            throw CudaError("k_live: a bounded wait ran out (status " + std::to_string(v) +
-                            "; 1 weights, 2 layer input, 4 contributions, 8 event message, 16 completion)");
+        if (check && (v & 0xFFu)) throw CudaError(live_status_text(v));
         return v;
+    }
+    static std::string live_status_text(unsigned v) {
+        return "k_live: a bounded wait ran out (status " + std::to_string(v) +
+               "; 1 weights, 2 layer input, 4 contributions, 8 event message, 16 completion)";
     }
 
     // ---- pipelined host drains: copy-in on a copy stream, double-buffered ----
@@ -1598,8 +1605,21 @@ int ssla_engine_live_join(SslaEngine* eng, unsigned* status) {
     if (!eng) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
     return ssla::guarded([&] {
         ssla::DeviceGuard dg(eng->e.device);
-        const unsigned v = eng->e.live_join();
+        const unsigned v = eng->e.live_join(false);
         if (status) *status = v;
+        if (v & 0xFFu) {
+            ssla::g_last_error = ssla::Engine::live_status_text(v);
+            return static_cast<int>(SSLA_ERR_CUDA);
+        }
+        return static_cast<int>(SSLA_OK);
+    });
+}
+
+int ssla_engine_live_withhold_completion(SslaEngine* eng, long long ring_index) {
+    if (!eng || ring_index < -1) { ssla::g_last_error = "bad argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        if (eng->e.live_running) throw std::invalid_argument("a live loop is running on this engine");
+        eng->e.live_withhold = ring_index < 0 ? ~0ull : static_cast<unsigned long long>(ring_index);
         return SSLA_OK;
     });
 }

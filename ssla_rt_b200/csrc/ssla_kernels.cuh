@@ -269,6 +269,8 @@ struct LiveArgs {
     unsigned long long start;            // index of the first event
     unsigned long long idle_ns;          // leave the loop after this long without an event
     unsigned* err;                       // SSLA_LIVE_* status bits (host-mapped)
+    unsigned long long withhold_fin;     // test hook: ring index whose completion message is
+                                         // withheld from the head CTA (~0: none)
 };
 
 struct CommitArgs {

@@ -111,14 +111,41 @@ struct LiveShared {
     float4 e;           // coordinator: the event taken from the ring
     int cmd;            // coordinator: 0 event, 1 stop flag, 2 idle
     int flags;          // coordinator: the event's flags
+    // bulk copy in flight on barrier i: 0 none, else 1 + the parity of the
+    // phase it completes (set by the issuing thread, cleared by thread 0
+    // once that phase has been waited for)
+    uint8_t inflight[kNBar];
 };
 static_assert(sizeof(LiveShared) + sizeof(float) * kDyn <= kMaxBlockSmem, "shared memory");
 
 __device__ __forceinline__ bool wait_bar(LiveShared& sh, int i, uint32_t& ph, unsigned* err, unsigned code,
                                          unsigned long long limit = kWaitNs) {
     const bool ok = mbar_wait(&sh.bar[i], (ph >> i) & 1u, err, code, limit);
+    if (ok && threadIdx.x == 0 && sh.inflight[i]) sh.inflight[i] = 0;
     ph ^= 1u << i;
     return ok;
+}
+
+// The issuing thread records a bulk copy completing on barrier i (before
+// issuing it): the copy lands in the phase this thread waits for next.
+__device__ __forceinline__ void mark_copy(LiveShared& sh, int i, uint32_t ph) {
+    sh.inflight[i] = static_cast<uint8_t>(1u + ((ph >> i) & 1u));
+}
+
+// Every CTA leaves through here, on every path (stop, idle, or a wait that
+// ran out): no bulk copy of its own may still be writing its shared memory
+// (bounded wait for each one recorded in flight), and no CTA returns
+// before every other CTA of the cluster has stopped sending messages and
+// remote arrivals into it (cluster barrier; every earlier wait is bounded,
+// so every CTA gets here).
+__device__ void live_exit(LiveShared& sh) {
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kNBar; ++i)
+            if (sh.inflight[i]) mbar_wait(&sh.bar[i], sh.inflight[i] - 1u, nullptr, 0u);
+    __syncthreads();
+    cluster_arrive();
+    cluster_wait();
 }
 
 // ---- system-scope accesses to the ring (pinned host memory) -----------------------
@@ -398,8 +425,10 @@ __device__ void coordinator(const LiveArgs& a, LiveShared& sh, float* wsm, uint3
                 if (P.used(l)) mbar_arrive_tx(&sh.bar[B_C + l - 4], 4u * chans(l / 2) * __popc(P.inb(l)));
         // the event message, once the workers are done with the previous event
         // and the head CTA has taken its inputs
-        if (done_pending) wait_bar(sh, B_DONE, ph, a.err, SSLA_LIVE_ERR_DONE);
-        if (pending) wait_bar(sh, B_HDONE, ph, a.err, SSLA_LIVE_ERR_DONE);
+        bool acked = true;
+        if (done_pending) acked = wait_bar(sh, B_DONE, ph, a.err, SSLA_LIVE_ERR_DONE) && acked;
+        if (pending) acked = wait_bar(sh, B_HDONE, ph, a.err, SSLA_LIVE_ERR_DONE) && acked;
+        if (!__syncthreads_and(acked)) return;       // the loop cannot go on: the status word says why
         pending = true;
         if (tid >= 32 && tid < 32 + kLiveCTAs - 1) {
             const int r = tid - 31;
@@ -431,13 +460,12 @@ __device__ void coordinator(const LiveArgs& a, LiveShared& sh, float* wsm, uint3
         // event; when no worker took part, their acknowledgement can wait ----
         if (P.runs(4)) ok = wait_bar(sh, B_DONE, ph, a.err, SSLA_LIVE_ERR_DONE) && ok;
         done_pending = !P.runs(4);
-        if (tid < 32) {
+        if (tid < 32 && seq != a.withhold_fin) {
             if (flags & F_R4)
                 for (int t = tid; t < 96; t += 32) send(&sh.xh[seq & 1][t], &sh.bar[B_FIN], kHeadCta, sh.x[t]);
             if (tid == 0) send(&sh.fin, &sh.bar[B_FIN], kHeadCta, __int_as_float(flags));
         }
-        __syncthreads();
-        if (!ok) return;               // a wait ran out: the status word says which
+        if (!__syncthreads_and(ok)) return;   // a wait ran out: the status word says which
     }
 }
 
@@ -465,6 +493,7 @@ __device__ bool w_layer(int l, int d, const Plan& P, const LiveArgs& a, LiveShar
     }
     __syncthreads();
     if (l == 6 && issue7q && tid == kIssuer) {         // layer 6's qvg block is consumed
+        mark_copy(sh, B_S7Q, ph);
         bulk(wsm + kWS, a.L[7].qvgT + static_cast<size_t>(d) * 96 * 288, 96 * 288, &sh.bar[B_S7Q]);
         mbar_arrive(&sh.bar[B_S7Q]);
     }
@@ -486,6 +515,7 @@ __device__ bool w_layer(int l, int d, const Plan& P, const LiveArgs& a, LiveShar
     }
     __syncthreads();                   // this layer's buffers are consumed
     if (l == 6 && issue7g && tid == kIssuer) {
+        mark_copy(sh, B_S7G, ph);
         bulk(wsm + kWSg, a.L[7].goWT + static_cast<size_t>(d) * 96 * 96, 96 * 96, &sh.bar[B_S7G]);
         mbar_arrive(&sh.bar[B_S7G]);
     }
@@ -497,7 +527,8 @@ __device__ void worker(int d, const LiveArgs& a, LiveShared& sh, float* wsm, uin
     const Geo& g = a.g;
     for (;;) {
         if (tid == 0) mbar_arrive_tx(&sh.bar[B_EV], 20u);
-        if (!wait_bar(sh, B_EV, ph, a.err, SSLA_LIVE_ERR_EVENT, a.idle_ns + kIdleMargin)) return;
+        if (!__syncthreads_and(wait_bar(sh, B_EV, ph, a.err, SSLA_LIVE_ERR_EVENT, a.idle_ns + kIdleMargin)))
+            return;
         const unsigned fw = __float_as_uint(sh.ev[4]);
         if (fw & kStopMsg) return;
         const float4 e = make_float4(sh.ev[0], sh.ev[1], sh.ev[2], sh.ev[3]);
@@ -524,13 +555,16 @@ __device__ void worker(int d, const LiveArgs& a, LiveShared& sh, float* wsm, uin
                 if (act[l]) mbar_arrive_tx(&sh.bar[B_X + l - 4], 4u * (l == 4 ? 24 : l == 7 ? 96 : 48));
         if (tid == kIssuer) {
             if (act[6]) {
+                mark_copy(sh, B_S6, ph);
                 bulk(wsm + kWS, a.L[6].qvgT + static_cast<size_t>(d) * 48 * 288, 48 * 288, &sh.bar[B_S6]);
                 bulk(wsm + kWSg, a.L[6].goWT + static_cast<size_t>(d) * 96 * 96, 96 * 96, &sh.bar[B_S6]);
                 mbar_arrive(&sh.bar[B_S6]);
             } else if (act[7]) {       // the stream area is free now
+                mark_copy(sh, B_S7Q, ph);
                 bulk(wsm + kWS, a.L[7].qvgT + static_cast<size_t>(d) * 96 * 288, 96 * 288, &sh.bar[B_S7Q]);
                 mbar_arrive(&sh.bar[B_S7Q]);
                 if (P.used(7)) {
+                    mark_copy(sh, B_S7G, ph);
                     bulk(wsm + kWSg, a.L[7].goWT + static_cast<size_t>(d) * 96 * 96, 96 * 96, &sh.bar[B_S7G]);
                     mbar_arrive(&sh.bar[B_S7G]);
                 }
@@ -550,9 +584,9 @@ __device__ void worker(int d, const LiveArgs& a, LiveShared& sh, float* wsm, uin
             }
             if (!P.used(l)) break;
         }
-        __syncthreads();               // every state row of the event is written
+        const bool all_ok = __syncthreads_and(ok);   // every state row of the event is written
         if (tid == 0) mbar_arrive_remote(&sh.bar[B_DONE], 0);
-        if (!ok) return;
+        if (!all_ok) return;
     }
 }
 
@@ -573,7 +607,8 @@ __device__ void head_cta(const LiveArgs& a, LiveShared& sh, float* wsm, uint32_t
     float* act = wsm + head_act(ncls);
     for (unsigned long long seq = a.start;; ++seq) {
         if (tid == 0) mbar_arrive_tx(&sh.bar[B_EV], 20u);
-        if (!wait_bar(sh, B_EV, ph, a.err, SSLA_LIVE_ERR_EVENT, a.idle_ns + kIdleMargin)) return;
+        if (!__syncthreads_and(wait_bar(sh, B_EV, ph, a.err, SSLA_LIVE_ERR_EVENT, a.idle_ns + kIdleMargin)))
+            return;
         const unsigned fw = __float_as_uint(sh.ev[4]);
         if (fw & kStopMsg) return;
         const int flags = static_cast<int>(fw);
@@ -581,8 +616,9 @@ __device__ void head_cta(const LiveArgs& a, LiveShared& sh, float* wsm, uint32_t
         const int py = (flags & F_VALID) ? static_cast<int>(sh.ev[2]) : 0;
         const bool head = (flags & F_R4) != 0;
         if (tid == 0) mbar_arrive_tx(&sh.bar[B_FIN], head ? 4u + 96u * 4u : 4u);
-        if (!wait_bar(sh, B_FIN, ph, a.err, SSLA_LIVE_ERR_DONE, a.idle_ns + kIdleMargin)) return;
-        __syncthreads();               // every thread has taken the event message
+        // every thread has taken the event message
+        if (!__syncthreads_and(wait_bar(sh, B_FIN, ph, a.err, SSLA_LIVE_ERR_DONE, a.idle_ns + kIdleMargin)))
+            return;
         if (tid == 0) mbar_arrive_remote_relaxed(&sh.bar[B_HDONE], 0);
         const float* x = sh.xh[seq & 1];
         const unsigned long long slot = seq & a.mask;
@@ -634,18 +670,26 @@ __global__ void __launch_bounds__(kLiveNT, 1) k_live(LiveArgs a) {
     const int rank = static_cast<int>(cta_rank());
     const int tid = threadIdx.x;
     if (tid == 0) {
-        for (int i = 0; i < kNBar; ++i) mbar_init(&sh.bar[i], i == B_DONE ? kWorkers : 1);
+        for (int i = 0; i < kNBar; ++i) {
+            mbar_init(&sh.bar[i], i == B_DONE ? kWorkers : 1);
+            sh.inflight[i] = 0;
+        }
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == kIssuer) issue_resident(rank, a, wsm, &sh.bar[B_INIT]);
+    if (tid == kIssuer) {
+        mark_copy(sh, B_INIT, 0u);
+        issue_resident(rank, a, wsm, &sh.bar[B_INIT]);
+    }
     cluster_arrive();                  // every CTA's barriers exist before any message
     cluster_wait();
     uint32_t ph = 0;
-    if (!wait_bar(sh, B_INIT, ph, a.err, SSLA_LIVE_ERR_WEIGHTS)) return;
-    if (rank == 0) coordinator(a, sh, wsm, ph);
-    else if (rank == kHeadCta) head_cta(a, sh, wsm, ph);
-    else worker(rank - 1, a, sh, wsm, ph);
+    if (__syncthreads_and(wait_bar(sh, B_INIT, ph, a.err, SSLA_LIVE_ERR_WEIGHTS))) {
+        if (rank == 0) coordinator(a, sh, wsm, ph);
+        else if (rank == kHeadCta) head_cta(a, sh, wsm, ph);
+        else worker(rank - 1, a, sh, wsm, ph);
+    }
+    live_exit(sh);
 }
 
 }  // namespace

@@ -7,9 +7,8 @@
 // milliseconds), or a host that runs the drain inside a memory pool owned by
 // another runtime and must not grow the process's device footprint.  This
 // entry point therefore takes all of its scratch memory from one file-scope
-// __device__ array of fixed size (kMaxRecords records) and calls no
-// allocating routine at all: no cudaMalloc / cudaFree / cudaMallocHost, no
-// library call that allocates.
+// __device__ array of fixed size and calls no allocating routine at all: no
+// device, pinned or managed allocation, no library call that allocates.
 //
 // It evaluates the same stage-2 and stage-3 temporal-dropout gates as
 // ssla_s2s3_drain_n_multi (k_gates_s2 / k_write_slots in ssla_kernels.cu,
@@ -19,13 +18,20 @@
 // records outside the block's owned strip).  It leaves the hidden state and
 // the s3_feat words of the slots untouched.
 //
-// Set-up: the first call on a device looks up the scratch array's device
-// address (cudaGetSymbolAddress, with that device current) and keeps it for
-// later calls; that first call may load the module and should therefore come
-// before any stream capture on the device.
+// Work per call is linear in the records: the records are first bucketed
+// by (block, stage-3 cell) inside the scratch array -- a stable two-pass
+// LSD radix sort of (key << 16 | record) words, so each bucket keeps ring
+// order -- and each gate warp then walks only its own cell's bucket.
+//
+// Set-up: the first call on a device (and the first call after the
+// device's context changed, e.g. after cudaDeviceReset) looks up the scratch
+// array's device address with cudaGetSymbolAddress, with that device
+// current, and keeps it for later calls; that call may load the module and
+// should therefore come before any stream capture on the device.
 // Concurrency: every call on a device shares the one scratch array, so two
 // calls whose work overlaps in time on the same device (different streams or
 // threads without ordering between them) race and give undefined results.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -41,17 +47,28 @@ void set_last_error(const std::string& msg);   // ssla_engine.cu
 
 namespace {
 
-constexpr int kMaxRecords = SSLA_NOALLOC_MAX_RECORDS;
+constexpr int kMaxRecords = SSLA_NOALLOC_MAX_RECORDS;   // record index fits 16 bits
+constexpr int kMaxKeys = SSLA_NOALLOC_MAX_CELLS;        // blocks x stage-3 cells; key fits 16 bits
+constexpr uint32_t kNoKey = 0xFFFFu;                    // records outside the stage-2 grid
 constexpr int kMaxDevices = 64;
 constexpr int kNT = 256;
+constexpr int kTile = 2048;                             // records per radix-sort tile
+constexpr int kMaxTiles = kMaxRecords / kTile;
+static_assert(kMaxRecords <= 65536 && kMaxKeys < 65536, "keys and record indices are 16-bit fields");
+static_assert(kMaxRecords % kTile == 0 && kTile % kNT == 0, "tiles of whole rounds");
 
-// Per-record scratch.  xy: packed stage-0 coordinates of the record (the
-// packing of the drain_n record prologue); flag: gate results, bit 0 = passed
-// gate 2, bit 1 = passed gate 3.  Every flag of the call's records must start
-// at zero (a record no gate warp visits keeps "did not pass"); k_na_pack
-// clears them at the start of each call.
+// Per-call scratch.  xy: packed stage-0 coordinates of each record (the
+// packing of the drain_n record prologue); sorted: (key << 16 | record)
+// words, ping-pong buffers of the radix sort (buffer 0 ends up sorted by
+// key, ring order inside each key); hist: per-tile digit counts, then their
+// exclusive offsets; flag: gate results, bit 0 = passed gate 2, bit 1 =
+// passed gate 3.  Every flag of the call's records must start at zero (a
+// record no gate warp visits keeps "did not pass"); k_na_pack clears them at
+// the start of each call.
 struct NoAllocScratch {
     uint32_t xy[kMaxRecords];
+    uint32_t sorted[2][kMaxRecords];
+    uint32_t hist[256 * kMaxTiles];
     uint8_t flag[kMaxRecords];
 };
 
@@ -99,20 +116,108 @@ __device__ __forceinline__ bool na_warp_gate(bool active, int key, int* cnt, int
     return pass;
 }
 
-// 1) records -> packed coordinates; clear the gate flags.
+// 1) records -> packed coordinates and (key, record) words; clear the gate
+// flags.  key = block * (W3 * H3) + stage-3 cell.
 __global__ void k_na_pack(NaParams a, NoAllocScratch* sc) {
+    const int cells = a.W3 * a.H3;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
         const int p = na_block_of(a, i);
         const HybridInputRec& r = a.ring[p][i - a.off[p]];
         const uint32_t x2 = r.x, y2 = r.y;
         sc->xy[i] = (x2 << 2) | ((y2 << 2) << 16);
         sc->flag[i] = 0;
+        const bool in = x2 < static_cast<uint32_t>(a.W2) && y2 < static_cast<uint32_t>(a.H2);
+        const uint32_t key = in ? static_cast<uint32_t>(p * cells) + (y2 >> 1) * a.W3 + (x2 >> 1) : kNoKey;
+        sc->sorted[0][i] = (key << 16) | static_cast<uint32_t>(i);
     }
 }
 
-// 2) one warp per (block, stage-3 cell): the block's records in ring order,
+// 2) one stable LSD radix pass over the 8-bit digit at `shift` (16 or 24):
+// per-tile digit counts, their exclusive offsets in digit-major order, and
+// an ordered scatter (records of a tile in rounds of 256, ranks within a
+// round from warp matches and per-warp digit counts).
+__global__ void __launch_bounds__(kNT) k_na_hist(int n, const uint32_t* src, int shift, uint32_t* hist) {
+    __shared__ uint32_t h[256];
+    const int t = blockIdx.x, T = gridDim.x;
+    h[threadIdx.x] = 0;
+    __syncthreads();
+    const int i1 = min(n, (t + 1) * kTile);
+    for (int i = t * kTile + threadIdx.x; i < i1; i += kNT) atomicAdd(&h[(src[i] >> shift) & 255u], 1u);
+    __syncthreads();
+    hist[threadIdx.x * T + t] = h[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kNT) k_na_scan(int T, uint32_t* hist) {
+    __shared__ uint32_t part[kNT];
+    const int d = threadIdx.x;                  // thread d owns entries [d*T, d*T + T)
+    uint32_t s = 0;
+    for (int t = 0; t < T; ++t) s += hist[d * T + t];
+    part[d] = s;
+    __syncthreads();
+    if (d == 0) {
+        uint32_t run = 0;
+        for (int k = 0; k < kNT; ++k) {
+            const uint32_t v = part[k];
+            part[k] = run;
+            run += v;
+        }
+    }
+    __syncthreads();
+    uint32_t run = part[d];
+    for (int t = 0; t < T; ++t) {
+        const uint32_t v = hist[d * T + t];
+        hist[d * T + t] = run;
+        run += v;
+    }
+}
+
+__global__ void __launch_bounds__(kNT) k_na_scatter(int n, const uint32_t* src, uint32_t* dst, int shift,
+                                                    const uint32_t* hist) {
+    constexpr int kWarps = kNT / 32;
+    __shared__ uint32_t cursor[256];
+    __shared__ uint32_t wc[kWarps][256];
+    const int t = blockIdx.x, T = gridDim.x;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    cursor[tid] = hist[tid * T + t];
+    for (int i0 = t * kTile; i0 < min(n, (t + 1) * kTile); i0 += kNT) {
+        for (int k = 0; k < kWarps; ++k) wc[k][tid] = 0;
+        __syncthreads();
+        const int i = i0 + tid;
+        const bool act = i < n;
+        const uint32_t v = act ? src[i] : 0u;
+        const int d = act ? static_cast<int>((v >> shift) & 255u) : 256 + lane;
+        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        const int rank = __popc(peers & na_lanemask_lt());
+        if (act && rank == 0) wc[w][d] = __popc(peers);
+        __syncthreads();
+        {   // per digit: offsets of the warps' groups, in warp order
+            uint32_t run = cursor[tid];
+            for (int k = 0; k < kWarps; ++k) {
+                const uint32_t c = wc[k][tid];
+                wc[k][tid] = run;
+                run += c;
+            }
+            cursor[tid] = run;
+        }
+        __syncthreads();
+        if (act) dst[wc[w][d] + rank] = v;
+        __syncthreads();
+    }
+}
+
+// 3) one warp per (block, stage-3 cell): the cell's bucket in ring order,
 // gate 2 on the record's stage-2 cell counter, gate 3 on the stage-3 cell
 // counter for records that passed gate 2 (k_gates_s2 without tile lists).
+__device__ __forceinline__ int na_lower_bound(const uint32_t* v, int n, uint32_t x) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (v[mid] < x) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
 __global__ void __launch_bounds__(32) k_na_gates(NaParams a, NoAllocScratch* sc) {
     const int p = blockIdx.x, cell = blockIdx.y;
     const int gx = cell % a.W3, gy = cell / a.W3;
@@ -120,17 +225,19 @@ __global__ void __launch_bounds__(32) k_na_gates(NaParams a, NoAllocScratch* sc)
     __shared__ int c2[4], c3[1];
     uint8_t* cnt2 = a.cnt2[p];
     uint8_t* cnt3 = a.cnt3[p];
+    const uint32_t key = static_cast<uint32_t>(p * a.W3 * a.H3 + cell);
+    const uint32_t* sorted = sc->sorted[0];
+    const int lo = na_lower_bound(sorted, a.n, key << 16);
+    const int hi = na_lower_bound(sorted, a.n, (key + 1) << 16);
+    if (lo == hi) return;                      // no record in this cell: counters unchanged
     if (lane < 4) c2[lane] = cnt2[(gy * 2 + lane / 2) * a.W2 + gx * 2 + (lane % 2)];
     if (lane == 0) c3[0] = cnt3[gy * a.W3 + gx];
     __syncwarp();
-    const int lo = a.off[p], hi = a.off[p + 1];
     for (int j0 = lo; j0 < hi; j0 += 32) {
-        const int j = j0 + lane;
-        uint32_t xy0 = 0;
-        if (j < hi) xy0 = sc->xy[j];
+        const bool own = j0 + lane < hi;
+        const int j = own ? static_cast<int>(sorted[j0 + lane] & 0xFFFFu) : 0;
+        const uint32_t xy0 = own ? sc->xy[j] : 0u;
         const int x2 = static_cast<int>(xy0 & 0xFFFFu) >> 2, y2 = static_cast<int>(xy0 >> 16) >> 2;
-        const bool own = (j < hi) && (x2 >> 1) == gx && (y2 >> 1) == gy;
-        if (__ballot_sync(0xffffffffu, own) == 0u) continue;
         const int sub = (y2 & 1) * 2 + (x2 & 1);
         const bool p2 = na_warp_gate(own, own ? sub : 100 + lane, c2, a.window);
         const bool in3 = own && p2;
@@ -142,7 +249,7 @@ __global__ void __launch_bounds__(32) k_na_gates(NaParams a, NoAllocScratch* sc)
     if (lane == 0) cnt3[gy * a.W3 + gx] = static_cast<uint8_t>(c3[0]);
 }
 
-// 3) pass codes of the output slots (k_write_slots' rule: -1 outside the
+// 4) pass codes of the output slots (k_write_slots' rule: -1 outside the
 // owned strip, pass3 only meaningful after pass2).
 __global__ void k_na_codes(NaParams a, const NoAllocScratch* sc) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
@@ -159,23 +266,53 @@ __global__ void k_na_codes(NaParams a, const NoAllocScratch* sc) {
     }
 }
 
+// ---- set-up: the scratch array's device address, per device and context ----
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+struct ScratchSlot {
+    CUcontext ctx = nullptr;
+    NoAllocScratch* ptr = nullptr;
+};
+
 std::mutex g_setup_mu;
-NoAllocScratch* g_scratch_ptr[kMaxDevices] = {};
+ScratchSlot g_scratch_slot[kMaxDevices];
+CtxGetCurrentFn g_ctx_get_current = nullptr;
 
 // Device address of the scratch array on the current device (looked up once
-// per device).  Returns nullptr and sets the error text on failure.
+// per device, and again if the device's current context is a new one).
+// Returns nullptr and sets the error text on failure.
 NoAllocScratch* scratch_for(int device) {
     std::lock_guard<std::mutex> lk(g_setup_mu);
-    if (g_scratch_ptr[device] == nullptr) {
+    if (g_ctx_get_current == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        const cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+            ssla::set_last_error("ssla_s2s3_gate_codes_noalloc: cuCtxGetCurrent entry point not found");
+            return nullptr;
+        }
+        g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    }
+    // A thread the runtime has not used yet may have no current context;
+    // the symbol lookup binds the device's primary context to it.
+    CUcontext ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    ScratchSlot& s = g_scratch_slot[device];
+    if (s.ptr == nullptr || ctx == nullptr || s.ctx != ctx) {
         void* ptr = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
         if (e != cudaSuccess || ptr == nullptr) {
             ssla::set_last_error(std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
             return nullptr;
         }
-        g_scratch_ptr[device] = static_cast<NoAllocScratch*>(ptr);
+        if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+            ssla::set_last_error("ssla_s2s3_gate_codes_noalloc: no current CUDA context");
+            return nullptr;
+        }
+        s.ctx = ctx;
+        s.ptr = static_cast<NoAllocScratch*>(ptr);
     }
-    return g_scratch_ptr[device];
+    return s.ptr;
 }
 
 int launch_grid(int n) {
@@ -199,8 +336,9 @@ extern "C" int ssla_s2s3_gate_codes_noalloc(const HybridS2S3Config* cfg,
     NaParams a{};
     a.P = P; a.W2 = cfg->W2; a.H2 = cfg->H2; a.W3 = cfg->W3; a.H3 = cfg->H3;
     a.window = cfg->tdrop_window;
-    if (static_cast<long long>(cfg->W3) * cfg->H3 > 65535) {
-        return fail(SSLA_ERR_ARG, "stage-3 grid larger than 65535 cells");
+    if (static_cast<long long>(cfg->W3) * cfg->H3 * P > kMaxKeys) {
+        return fail(SSLA_ERR_CAPACITY, "ssla_s2s3_gate_codes_noalloc: blocks x stage-3 cells exceed the "
+                                       "allocation-free limit of " + std::to_string(kMaxKeys));
     }
     long long total = 0;
     for (int b = 0; b < P; ++b) {
@@ -237,7 +375,15 @@ extern "C" int ssla_s2s3_gate_codes_noalloc(const HybridS2S3Config* cfg,
     if (!sc) return SSLA_ERR_CUDA;
     if (a.n == 0) return SSLA_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int T = (a.n + kTile - 1) / kTile;
     k_na_pack<<<launch_grid(a.n), kNT, 0, st>>>(a, sc);
+    for (int pass = 0; pass < 2; ++pass) {       // key bits 16-23, then 24-31
+        const uint32_t* src = sc->sorted[pass];
+        uint32_t* dst = sc->sorted[pass ^ 1];
+        k_na_hist<<<T, kNT, 0, st>>>(a.n, src, 16 + 8 * pass, sc->hist);
+        k_na_scan<<<1, kNT, 0, st>>>(T, sc->hist);
+        k_na_scatter<<<T, kNT, 0, st>>>(a.n, src, dst, 16 + 8 * pass, sc->hist);
+    }
     k_na_gates<<<dim3(P, a.W3 * a.H3), 32, 0, st>>>(a, sc);
     k_na_codes<<<launch_grid(a.n), kNT, 0, st>>>(a, sc);
     e = cudaGetLastError();

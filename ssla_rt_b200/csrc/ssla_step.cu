@@ -86,6 +86,7 @@ struct StepShared {
     float res[96];        // CTA 0: residual of the current layer
     float gb[192];        // CTA 0: gamma | beta of layers 4-7, kept aside from the copies
     float con[9][96];     // CTA 0: goW contributions by patch position; head activations
+    unsigned wmask;       // copy barriers the issuing thread has armed (bit i: bar_w[i])
 };
 static_assert(sizeof(StepShared) + sizeof(float) * kDyn <= kMaxBlockSmem, "shared memory");
 
@@ -108,8 +109,15 @@ __device__ __forceinline__ bool cl_part(const Plan& P, int l, int rank) {
 }
 
 // ---- copies (issuer thread) -----------------------------------------------------
+// The issuing thread's arrival on a copy barrier, recorded so that the CTA
+// can wait for every copy it issued before it exits.
+__device__ __forceinline__ void arrive_w(StepShared& sh, uint64_t* bar) {
+    sh.wmask |= 1u << static_cast<unsigned>(bar - sh.bar_w);
+    mbar_arrive(bar);
+}
+
 template <int IN, int OUT, int A>
-__device__ void issue_small(int l, const Plan& P, const StepArgs& a, float* b, uint64_t* bar) {
+__device__ void issue_small(int l, const Plan& P, const StepArgs& a, float* b, uint64_t* bar, StepShared& sh) {
     using Lo = Lay<IN, OUT, A>;
     const DevLayer& L = a.L[l];
     const int s = l / 2;
@@ -126,7 +134,7 @@ __device__ void issue_small(int l, const Plan& P, const StepArgs& a, float* b, u
         if (patch_cell(A, d, P.px >> s, P.py >> s, Ws, Hs, cx, cy))
             bulk(b + Lo::HR + d * OUT, a.ps.hidden[l] + (static_cast<size_t>(cy) * Ws + cx) * OUT, OUT, bar);
     }
-    mbar_arrive(bar);
+    arrive_w(sh, bar);
 }
 
 // Layer l (4-7) copies of CTA `rank`: part 1 = its qvg block, part 2 = the
@@ -140,7 +148,7 @@ __device__ void issue_cl(int l, int part, const Plan& P, int rank, const StepArg
     if ((part & 1) && act) {
         uint64_t* bar = l == 7 ? &sh.bar_w[9] : &sh.bar_w[l];
         bulk(cl_wq(wsm, l), W.qvgT + static_cast<size_t>(rank) * IN * J2, IN * J2, bar);
-        if (l == 7) mbar_arrive(bar);
+        if (l == 7) arrive_w(sh, bar);
     }
     if (part & 2) {
         uint64_t* bar = &sh.bar_w[l];
@@ -157,11 +165,11 @@ __device__ void issue_cl(int l, int part, const Plan& P, int rank, const StepArg
             bulk(r + OUT * OUT + OUT, W.beta, OUT, bar);
             if ((l & 1) == 0) bulk(r + OUT * OUT + 3 * OUT, W.ipT, IN * OUT, bar);
         }
-        mbar_arrive(bar);
+        arrive_w(sh, bar);
     }
 }
 
-__device__ void issue_head(const DevHead& hd, int ncls, float* wsm, uint64_t* bar) {
+__device__ void issue_head(const DevHead& hd, int ncls, float* wsm, uint64_t* bar, StepShared& sh) {
     float* h = wsm + kRH;
     bulk(h, hd.cls_convT, 96 * 96, bar);
     bulk(h + 96 * 96, hd.reg_convT, 96 * 96, bar);
@@ -170,7 +178,7 @@ __device__ void issue_head(const DevHead& hd, int ncls, float* wsm, uint64_t* ba
     bulk(h + kHeadCp, hd.cls_predT, 96 * ncls, bar);
     bulk(h + head_cb(ncls), hd.cls_conv_b, 96, bar);
     bulk(h + head_cb(ncls) + 96, hd.reg_conv_b, 96, bar);
-    mbar_arrive(bar);
+    arrive_w(sh, bar);
 }
 
 // Copies that wait for a buffer to be consumed, issued at point p: p = 3
@@ -194,7 +202,7 @@ __device__ void issue_deferred(int p, Deferred& D, const Plan& P, int rank, cons
         D.r7 = true;
     }
     if (!D.head && rank == 0 && (P.flags & F_R4) && (!u6 || p >= 6) && (!u7 || p >= 7)) {
-        issue_head(a.head, a.g.ncls, wsm, &sh.bar_w[8]);
+        issue_head(a.head, a.g.ncls, wsm, &sh.bar_w[8], sh);
         D.head = true;
     }
 }
@@ -524,6 +532,7 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
     // ---- barriers, expected messages, first copies ----
     if (tid == 0) {
         for (int i = 0; i < 10; ++i) mbar_init(&sh.bar_w[i], 1);
+        sh.wmask = 0u;
         for (int i = 0; i < 8; ++i) {
             mbar_init(&sh.bar_x[i], 1);
             mbar_init(&sh.bar_c[i], 1);
@@ -539,10 +548,10 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
     Deferred D{false, false, false};
     if (tid == kIssuer) {
         if (rank == 0) {
-            if (P.runs(0)) issue_small<2, 12, 1>(0, P, a, wsm, &sh.bar_w[0]);
-            if (P.runs(1)) issue_small<12, 12, 9>(1, P, a, wsm + kS1, &sh.bar_w[1]);
-            if (P.runs(2)) issue_small<12, 24, 9>(2, P, a, wsm + kS2, &sh.bar_w[2]);
-            if (P.runs(3)) issue_small<24, 24, 9>(3, P, a, wsm + kS3, &sh.bar_w[3]);
+            if (P.runs(0)) issue_small<2, 12, 1>(0, P, a, wsm, &sh.bar_w[0], sh);
+            if (P.runs(1)) issue_small<12, 12, 9>(1, P, a, wsm + kS1, &sh.bar_w[1], sh);
+            if (P.runs(2)) issue_small<12, 24, 9>(2, P, a, wsm + kS2, &sh.bar_w[2], sh);
+            if (P.runs(3)) issue_small<24, 24, 9>(3, P, a, wsm + kS3, &sh.bar_w[3], sh);
             if (cl_part(P, 4, 0)) issue_cl(4, 3, P, 0, a, wsm, sh);
         } else {
             for (int l = 4; l < 7; ++l)
@@ -596,6 +605,17 @@ __global__ void __launch_bounds__(kStepNT, 1) k_step(StepArgs a) {
         if (P.flags & F_R4) run_head(P, a, sh, wsm, pbias);
         if (tid == 0 && a.flag_out) *a.flag_out = static_cast<uint8_t>(flags);
     }
+
+    // ---- exit: no copy of this CTA still writing its shared memory (bounded
+    // waits: a copy whose wait ran out above may still be in flight), and no
+    // CTA leaves while a peer could still send into it ----
+    __syncthreads();
+    if (tid == 0)
+        for (int i = 0; i < 10; ++i)
+            if ((sh.wmask >> i) & 1u) mbar_wait(&sh.bar_w[i], 0, nullptr, 0u);
+    __syncthreads();
+    cluster_arrive();
+    cluster_wait();
 }
 
 }  // namespace

@@ -55,6 +55,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_step_latency": (i, [vp, i, vp, i, vp, vp]),
         "ssla_engine_live_start": (i, [vp, i, C.POINTER(abi.SslaLiveRing), C.c_uint, vp]),
         "ssla_engine_live_join": (i, [vp, C.POINTER(C.c_uint)]),
+        "ssla_engine_live_withhold_completion": (i, [vp, C.c_longlong]),
         "ssla_engine_live_latency": (i, [vp, i, vp, i, vp, vp, vp]),
         "ssla_engine_set_owned": (i, [vp, i, i, i, i, i, vp]),
         "ssla_engine_strip_init": (i, [vp, i, i, i, i, i, i]),
@@ -247,12 +248,21 @@ class SslaEngine:
         _check(self.lib.ssla_engine_live_start(self.h, partition, C.byref(ring), idle_timeout_ms,
                                                _stream(stream)))
 
-    def live_join(self) -> int:
-        """Waits for the live loop to end; returns its SSLA_LIVE_* status."""
+    def live_join(self, check: bool = True) -> int:
+        """Waits for the live loop to end; returns its SSLA_LIVE_* status.
+        With ``check`` a bounded wait that ran out inside the loop raises
+        SslaError; without it the status is returned either way."""
         st = C.c_uint(0)
-        _check(self.lib.ssla_engine_live_join(self.h, C.byref(st)))
+        rc = self.lib.ssla_engine_live_join(self.h, C.byref(st))
         self._live_ring = None
+        if check or rc != abi.SSLA_ERR_CUDA:
+            _check(rc)
         return st.value
+
+    def live_withhold_completion(self, ring_index: int) -> None:
+        """Test hook of the loop's timeout path: the next live loop withholds
+        the completion message of ring event ``ring_index`` (-1: none)."""
+        _check(self.lib.ssla_engine_live_withhold_completion(self.h, ring_index))
 
     def live_latency(self, events: np.ndarray, partition: int = 0):
         """Per-event host latency (us) from publishing an event in the live

@@ -70,3 +70,86 @@ def shard(events: np.ndarray, height: int, n: int, halo_rows: int = HALO_ROWS):
         ev = np.ascontiguousarray(events[m])
         out.append(((lo, hi), ev, owned_mask(ev, lo, hi)))
     return out
+
+
+# ---------------------------------------------------------------------------
+# Exact strips across GPUs, checked against one sensor
+# ---------------------------------------------------------------------------
+CHANS = (12, 24, 48, 96)
+
+
+def connect_exact(eng, rank: int, world: int, all_gather_object) -> None:
+    """Connects an engine set up by strip_init to its neighbours' receive
+    buffers through CUDA IPC handles, exchanged with `all_gather_object`
+    (torch.distributed's, or any callable with its signature)."""
+    mine = [eng.strip_recv_buffer(sd)[1] if (sd == 0 and rank > 0) or (sd == 1 and rank < world - 1)
+            else None for sd in (0, 1)]
+    allh = [None] * world
+    all_gather_object(allh, mine)
+    if rank > 0:
+        eng.strip_connect(0, peer_handle=allh[rank - 1][1])
+    if rank < world - 1:
+        eng.strip_connect(1, peer_handle=allh[rank + 1][0])
+
+
+def _rows(a: np.ndarray, height: int, width: int, s: int, lo: int, hi: int) -> np.ndarray:
+    """Rows [lo >> s, hi >> s) of a per-cell array on the stage-s grid."""
+    hs, ws = height >> s, width >> s
+    return a.reshape(hs, ws, -1)[lo >> s:hi >> s]
+
+
+def exact_strip_parity(weights_dir: str, events: np.ndarray, rank: int, world: int, device: int,
+                       all_gather_object, barrier, band: int = 16) -> dict:
+    """One aligned chunk of `events` (a prefix of the sensor's stream) drained
+    as `world` exact strips, one per rank and GPU, with the per-layer band
+    exchange over peer memory; then the same events drained as one sensor on
+    this rank's GPU.  Compares this rank's owned results with the
+    single-sensor run: the flags of its owned events, the hidden state of its
+    rows at every layer, its gate counters, predictions and versions.
+    Returns {"ok", "events", "routed", "owned", "exchange_status",
+    "mismatch": [names]}; every rank must call it together."""
+    import torch
+    from . import abi
+    from .engine import SslaEngine
+
+    full = SslaEngine(weights_dir, n_partitions=1, max_events=max(1, len(events)), layout=abi.LAYOUT_HYBRID,
+                      device=device)
+    H, W = full.H, full.W
+    lo, hi = strip_bounds(H, world)[rank]
+    mask = route_mask(events, lo, hi, H, band)
+    sev = np.ascontiguousarray(events[mask])
+    own = owned_mask(sev, lo, hi)
+    n = len(sev)
+    eng = SslaEngine(weights_dir, n_partitions=1, max_events=max(1, n), layout=abi.LAYOUT_HYBRID, device=device)
+    eng.strip_init(lo, hi, band, rank > 0, rank < world - 1, max(1, n // 2))
+    if world > 1:
+        connect_exact(eng, rank, world, all_gather_object)
+    barrier()
+    dev = torch.device("cuda", device)
+    sflags = torch.zeros(max(1, n), dtype=torch.uint8, device=dev)
+    eng.strip_drain(torch.from_numpy(sev).to(dev), n, flags=sflags)
+    torch.cuda.synchronize(dev)
+    status = eng.strip_status()
+    ff = torch.zeros(max(1, len(events)), dtype=torch.uint8, device=dev)
+    full.drain(torch.from_numpy(np.ascontiguousarray(events)).to(dev), [0, len(events)], flags=ff)
+    torch.cuda.synchronize(dev)
+    bad = []
+    idx = np.nonzero(mask)[0]
+    if not np.array_equal(sflags.cpu().numpy()[:n][own], ff.cpu().numpy()[idx[own]]):
+        bad.append("flags")
+    for l in range(8):
+        s = l // 2
+        if not np.array_equal(_rows(eng.hidden(l), H, W, s, lo, hi), _rows(full.hidden(l), H, W, s, lo, hi)):
+            bad.append(f"hidden{l}")
+    for g, s in enumerate((1, 2, 2, 3)):
+        if not np.array_equal(_rows(eng.counters(g), H, W, s, lo, hi), _rows(full.counters(g), H, W, s, lo, hi)):
+            bad.append(f"counter{g}")
+    if not np.array_equal(_rows(eng.preds_dec(), H, W, 3, lo, hi), _rows(full.preds_dec(), H, W, 3, lo, hi)):
+        bad.append("preds")
+    if not np.array_equal(_rows(eng.version(), H, W, 3, lo, hi), _rows(full.version(), H, W, 3, lo, hi)):
+        bad.append("version")
+    barrier()                 # no rank closes its buffers while a neighbour may still read them
+    eng.close()
+    full.close()
+    return {"ok": not bad and status == 0, "events": int(len(events)), "routed": int(n),
+            "owned": int(own.sum()), "exchange_status": int(status), "mismatch": bad}

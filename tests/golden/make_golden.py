@@ -1,7 +1,8 @@
 """Regenerates the committed golden fixtures from the reference itself.
 
-Run in a container that has the reference checkout (default
-/root/reference, or $SSLA_REFERENCE) and the built oracle/_ref library
+Run in a container that has the reference checkout (default: a directory
+named `reference` beside this repository, or $SSLA_REFERENCE) and the built
+oracle/_ref library
 (`make -C oracle ref`):
 
     python tests/golden/make_golden.py
@@ -33,7 +34,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("SSLA_REFERENCE", "/root/reference")
+REF = os.environ.get("SSLA_REFERENCE", os.path.join(os.path.dirname(REPO), "reference"))
 sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 

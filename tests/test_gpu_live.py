@@ -128,3 +128,48 @@ def test_live_rejects_pageable_ring(stub_dir):
     with pytest.raises(SslaError):
         eng.live_start(ring)
     eng.close()
+
+
+def test_live_timeout_path_ends_cleanly(oracle_mod, stub_dir):
+    """The loop's error path, made to run on purpose without any fault: the
+    test hook withholds the completion message of ring event 3 from the
+    head CTA.  Events 0-2 finish; the head CTA's bounded wait for event 3
+    runs out, so does the coordinator's wait for the head CTA's
+    acknowledgement at event 4, and the workers' wait for the next event
+    message.  Every CTA leaves through the exit barrier, the status word
+    names the waits that ran out, and the context stays usable: a drain
+    afterwards equals the oracle."""
+    from ssla_rt_b200.engine import SslaEngine, SslaError
+    O = oracle_mod
+    d = stub_dir(64, 80, 1, 4)
+    eng = SslaEngine(d, n_partitions=1, max_events=4000, layout=abi.LAYOUT_HYBRID)
+    cap, n = 16, 8
+    ev = E.config_events(0, n=4000)
+    events = torch.zeros((cap, 4), dtype=torch.float32).pin_memory()
+    words = torch.zeros(8, dtype=torch.int64).pin_memory()     # head, tail, done, stop
+    base = words.data_ptr()
+    ring = abi.SslaLiveRing(events.data_ptr(), cap, base, base + 8, base + 16, None, None, base + 24)
+    events[:n] = torch.from_numpy(ev[:n])
+    words[0] = n
+    eng.live_withhold_completion(3)
+    eng.live_start(ring, idle_timeout_ms=100)
+    t0 = time.time()
+    status = eng.live_join(check=False)
+    assert time.time() - t0 < 30
+    assert status & abi.LIVE_ERR_DONE
+    assert not status & (abi.LIVE_EXIT_STOP | abi.LIVE_ERR_WEIGHTS)
+    assert int(words[2]) == 3                     # events 0-2 finished, event 3 withheld
+    taken = int(words[1])                         # the loop took events 0-4
+    assert taken == 5
+    eng.live_withhold_completion(taken)           # again, on the next loop's first event
+    eng.live_start(ring, idle_timeout_ms=100)
+    with pytest.raises(SslaError):                # a checked join raises the same status
+        eng.live_join()
+    eng.reset()
+    torch.cuda.synchronize()
+    eng.drain(torch.from_numpy(np.ascontiguousarray(ev)).cuda(), [0, len(ev)])
+    torch.cuda.synchronize()
+    orc = O.Oracle(O.load_npz(d), 64, 80, 4, O.LAYOUT_HYBRID)
+    orc.run_events(ev, want_stage_out=False)
+    _assert_state(eng, orc, abi.LAYOUT_HYBRID)
+    eng.close()

@@ -64,3 +64,14 @@ def test_expf_accuracy_vs_libm():
         ulp = float(np.spacing(np.float32(ref)))
         worst = max(worst, abs(float(got) - ref) / ulp)
     assert worst <= 2.0, worst
+
+
+def test_noalloc_source_names_no_allocating_call():
+    """The allocation-free entry point's translation unit calls nothing that
+    allocates device, pinned or managed memory (comments excluded)."""
+    src = open(os.path.join(REPO, "ssla_rt_b200", "csrc", "ssla_noalloc.cu")).read()
+    code = re.sub(r"//[^\n]*", "", re.sub(r"/\*.*?\*/", "", src, flags=re.S))
+    for name in ("cudaMalloc", "cudaFree", "cudaHostAlloc", "cudaMallocHost", "cudaMallocAsync",
+                 "cudaMallocManaged", "cudaMallocPitch", "cudaMalloc3D", "cudaMallocArray", "cuMemAlloc",
+                 "cuMemCreate", "malloc(", "new ", "std::vector", "torch"):
+        assert name not in code, name
