@@ -261,10 +261,13 @@ def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
         return v[min(len(v) - 1, max(0, int(round(q * len(v))) - 1))] if v else None
 
     def summary(lat, fl):
+        # p50 / p99 over the events that produced a prediction (the
+        # reference's latency population, docs/PROFILE.md:56-67); all_* over
+        # every event
         lat = lat.tolist()
         head = [x for x, f in zip(lat, fl.tolist()) if f & abi.F_R4]
-        return {"p50": pct(lat, 0.50), "p99": pct(lat, 0.99), "n": len(lat),
-                "head_p50": pct(head, 0.50), "head_p99": pct(head, 0.99), "head_events": len(head)}
+        return {"p50": pct(head, 0.50), "p99": pct(head, 0.99), "head_events": len(head),
+                "all_p50": pct(lat, 0.50), "all_p99": pct(lat, 0.99), "n": len(lat)}
 
     ev = np.ascontiguousarray(stream_events[: warmup + samples])
     out = {}
@@ -282,7 +285,8 @@ def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
                      "event the host publishes the ring head and spins on events_done (the reference's "
                      "persistent-kernel protocol), host steady_clock from publish to completion seen, in "
                      "the library's C++ loop; step: one 9-CTA cluster launch per event + stream synchronize; "
-                     "head_* over events that produced a prediction (the reference's latency population); "
+                     "p50/p99 over events that produced a prediction (the reference's latency population), "
+                     "all_* over every event; "
                      f"a {samples:,}-event stream with config 0's distribution (uniform 80x64, Poisson "
                      "2 Mev/s), tdrop 4")
     return res
