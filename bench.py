@@ -292,6 +292,113 @@ def measure_latency(weights_dir: str, stream_events: np.ndarray, device: int,
     return res
 
 
+SWEEP_BLOCKS = (8, 16, 32, 64, 148)
+SWEEP_RECORDS = 200_000
+
+
+def consumer_sweep(weights_dir: str, device: int, reps: int = 3) -> dict:
+    """BASELINE config 1's persistent-block sweep through the reference's own
+    kernel ABI: 200,000 stage-2 ring records, drawn as the reference's sweep
+    harness draws them (uniform stage-2 coordinates, feat1 ~ N(0, 0.5^2),
+    orin/perf_celled_multi.py:176-190), split evenly over B rings, one
+    288-thread block per ring (k_ssla_s2s3_celled_drain_n_multi of the
+    consumer module, prebuilt sm_100a cubin; weights from the engine through
+    ssla_engine_fill_s2s3_config), for B from 8 to the SM count.  A
+    HybridS2S3Config names at most 16 blocks, so B > 16 runs as concurrent
+    launches of <= 16 blocks on their own streams.  Records/s = records /
+    device time from the first launch to the last completion (CUDA events),
+    best of `reps`, L2 flushed before each rep (untimed)."""
+    import ctypes as Cc
+    import torch
+    from ssla_rt_b200 import abi, consumer
+    from ssla_rt_b200.engine import SslaEngine
+
+    dev = torch.device("cuda", device)
+    eng = SslaEngine(weights_dir, n_partitions=1, max_events=16, layout=abi.LAYOUT_HYBRID, device=device)
+    H2, W2 = H >> 2, W >> 2
+    H3, W3 = H2 // 2, W2 // 2
+    mod = consumer.ConsumerModule(None)
+    rng = np.random.default_rng(1)
+    rec = np.zeros(SWEEP_RECORDS, dtype=abi.INPUT_DTYPE)
+    rec["x"] = rng.integers(0, W2, SWEEP_RECORDS)
+    rec["y"] = rng.integers(0, H2, SWEEP_RECORDS)
+    rec["feat1"] = rng.normal(scale=0.5, size=(SWEEP_RECORDS, 24))
+    rec["t"] = rng.uniform(0, 1, SWEEP_RECORDS)
+    rec["seq_done"] = np.arange(1, SWEEP_RECORDS + 1)
+    rec_dev = torch.from_numpy(rec.view(np.uint8).copy()).to(dev)
+    out_dev = torch.zeros(SWEEP_RECORDS * abi.OUTPUT_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    cells2, cells3 = H2 * W2, H3 * W3
+    points = []
+    for B in SWEEP_BLOCKS:
+        per = SWEEP_RECORDS // B
+        n_launch = (B + 15) // 16
+        hidden = torch.zeros(B * (2 * cells2 * 48 + 2 * cells3 * 96), dtype=torch.float32, device=dev)
+        td2 = torch.zeros(B * cells2, dtype=torch.uint8, device=dev)
+        td3 = torch.zeros(B * cells3, dtype=torch.uint8, device=dev)
+        keep, launches = [], []
+        for L in range(n_launch):
+            b0, b1 = 16 * L, min(B, 16 * L + 16)
+            cfg = abi.HybridS2S3Config()
+            cfg.H2, cfg.W2, cfg.H3, cfg.W3 = H2, W2, H3, W3
+            cfg.tdrop_window, cfg.n_blocks = 4, b1 - b0
+            strip_w = max(1, W2 // B)
+            rings, ns, outs = [], [], []
+            for k, blk in enumerate(range(b0, b1)):
+                eng.fill_s2s3_config(cfg, k)
+                lo, hi = blk * strip_w, ((blk + 1) * strip_w if blk < B - 1 else W2)
+                s = cfg.strip[k]
+                s.owned_lo, s.owned_hi, s.s3_owned_lo, s.s3_owned_hi = lo, hi, lo >> 1, hi >> 1
+                s.owned_y_lo, s.owned_y_hi, s.s3_owned_y_lo, s.s3_owned_y_hi = 0, H2, 0, H3
+                hb = hidden[blk * (2 * cells2 * 48 + 2 * cells3 * 96):]
+                offs = (0, cells2 * 48, 2 * cells2 * 48, 2 * cells2 * 48 + cells3 * 96)
+                for li in range(4):
+                    cfg.hidden[k][li] = hb[offs[li]:].data_ptr()
+                cfg.tdrop_s2[k] = td2[blk * cells2:].data_ptr()
+                cfg.tdrop_s3[k] = td3[blk * cells3:].data_ptr()
+                rings.append(rec_dev[blk * per * 128:].data_ptr())
+                outs.append(out_dev[blk * per * abi.OUTPUT_DTYPE.itemsize:].data_ptr())
+                ns.append(per)
+            cfg_dev = torch.frombuffer(bytearray(bytes(cfg)), dtype=torch.uint8).to(dev)
+            rings_dev = torch.tensor(rings, dtype=torch.int64, device=dev)
+            ns_dev = torch.tensor(ns, dtype=torch.int32, device=dev)
+            outs_dev = torch.tensor(outs, dtype=torch.int64, device=dev)
+            keep += [cfg_dev, rings_dev, ns_dev, outs_dev]
+            launches.append((b1 - b0, [consumer.ptr(cfg_dev.data_ptr()), consumer.ptr(rings_dev.data_ptr()),
+                                       consumer.ptr(ns_dev.data_ptr()), consumer.ptr(outs_dev.data_ptr()),
+                                       consumer.ptr(0)]))
+        streams = [torch.cuda.Stream(device=dev) for _ in launches]
+        main = torch.cuda.current_stream(dev)
+        best = None
+        for _ in range(reps):
+            td2.zero_()
+            td3.zero_()
+            flush.fill_(1.0)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(main)
+            for st, (grid, args) in zip(streams, launches):
+                st.wait_event(a)
+                mod.launch("k_ssla_s2s3_celled_drain_n_multi", grid, args, stream=st.cuda_stream)
+            for st in streams:
+                main.wait_stream(st)
+            b.record(main)
+            b.synchronize()
+            ms = a.elapsed_time(b)
+            best = ms if best is None else min(best, ms)
+        points.append({"blocks": B, "launches": len(launches), "records_per_ring": per, "ms": best,
+                       "mrec_s": per * B / (best * 1e-3) / 1e6})
+        del hidden, td2, td3, keep
+    mod.close()
+    eng.close()
+    return {"kernel": "k_ssla_s2s3_celled_drain_n_multi (consumer module, prebuilt sm_100a; the reference's "
+                      "launch shape: one 288-thread block per ring, 166,128 B dynamic shared memory)",
+            "records": SWEEP_RECORDS, "unit": "M ring records/s (post-stage-1 records, the reference's kev/s unit)",
+            "points": points,
+            "timing": "CUDA events around concurrent launches (<= 16 blocks each), best of "
+                      f"{reps}, L2 flushed before each rep"}
+
+
 PARITY_TOL_STAGE = 1e-3          # stated per-stage fp32 tolerance against the reference build
 PARITY_S3_BUDGET = 5.0           # the reference's own P1 budget on max|d| s3_feat
 
@@ -896,6 +1003,8 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true", help="skip the batch-of-1 latency samples")
     ap.add_argument("--no-parity", action="store_true", help="skip the config-0 parity check against the reference")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip config 1's persistent-block sweep through the reference kernel ABI")
     ap.add_argument("--no-strips", action="store_true",
                     help="skip the config-3 strips measurement carried by the default line")
     ap.add_argument("--workload", default="config1", choices=["config1", "config2", "strips", "streams"],
@@ -1077,6 +1186,9 @@ def main() -> int:
     # ---- acceptance parity: config 0 against the reference build (rank 0) ----
     parity = None if (args.no_parity or rank != 0) else acceptance_parity(wdir, local)
 
+    # ---- config 1's persistent-block sweep through the reference kernel ABI (rank 0) ----
+    sweep = None if (args.no_sweep or rank != 0) else consumer_sweep(wdir, local)
+
     # ---- config 3 in N strips (the north star's strong-scaling target) ----
     strips_line = None
     if not args.no_strips:
@@ -1103,6 +1215,7 @@ def main() -> int:
             "stage_events": stage_events,
             "phase_ms": phases,
             "parity": parity,
+            "sweep": sweep,
             "strips": strips_line,
         }
         print(json.dumps(line), flush=True)

@@ -115,5 +115,10 @@ static_assert(sizeof(HybridStrip) == 32, "HybridStrip layout");
 static_assert(sizeof(LayerWeightsS2S3) == 40, "LayerWeightsS2S3 layout");
 static_assert(offsetof(HybridS2S3Config, strip) == 32, "cfg.strip");
 static_assert(offsetof(HybridS2S3Config, layers) == 32 + 16 * 32, "cfg.layers");
+static_assert(offsetof(HybridS2S3Config, hidden) == 3104, "cfg.hidden");
+static_assert(offsetof(HybridS2S3Config, head_W) == 3872, "cfg.head_W");
+static_assert(offsetof(HybridS2S3Config, preds) == 3968, "cfg.preds");
+static_assert(offsetof(HybridS2S3Config, timing_mask) == 4352, "cfg.timing_mask");
+static_assert(sizeof(HybridS2S3Config) == 4616, "HybridS2S3Config layout");
 #endif
 #endif

@@ -382,6 +382,14 @@ int  ssla_s2s3_drain_n_multi(const HybridS2S3Config* cfg,
                              HybridS2S3OutputSlot* const* outs,
                              unsigned long long* const* batch_clks,
                              void* stream);
+/* Fills the weight and head pointers of cfg->layers[block][0..3] (layers
+ * 4-7) and cfg->head_* with this engine's device weights, which are laid out
+ * as the reference's GPU kernels read them (qvgIn (9, IN, 3*OUT), goW
+ * (9, OUT, OUT) and input_proj (IN, OUT) row-major, the 2-layer head with BN
+ * folded, (IN, OUT) row-major) -- the buffers orin/orin/weights_ssla.py:24-88
+ * and orin/orin/hybrid_common.py:76-111 build for a HybridS2S3Config.  The
+ * pointers stay valid while the engine lives.  block: 0..15. */
+int  ssla_engine_fill_s2s3_config(SslaEngine* eng, HybridS2S3Config* cfg, int block);
 /* Two-ring form; replaces k_ssla_s2s3_celled_drain_n
  * (orin/kernels/ssla_s2_s3_head_celled.cuh:914-1095). */
 int  ssla_s2s3_drain_n(const HybridS2S3Config* cfg,

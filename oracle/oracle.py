@@ -82,6 +82,7 @@ class Oracle:
         lib.or_model_free.argtypes = [C.c_void_p]
         lib.or_run_events.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int] + [C.c_void_p] * 5
         lib.or_run_s2_records.argtypes = [C.c_void_p, C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] + [C.c_void_p] * 3
+        lib.or_head_raw.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
         lib.or_expf.restype = C.c_float
         lib.or_expf.argtypes = [C.c_float]
         lib.or_sigmoidf.restype = C.c_float
@@ -208,6 +209,13 @@ class Oracle:
 
     def expf(self, x: float) -> float:
         return self.lib.or_expf(x)
+
+    def head_raw(self, feat: np.ndarray) -> np.ndarray:
+        """Raw head outputs [reg 4, obj, cls...] of one 96-float stage-3 feature."""
+        f = _f32(feat).reshape(96)
+        out = np.zeros(5 + self.ncls, np.float32)
+        self.lib.or_head_raw(self.model, _ptr(f), _ptr(out))
+        return out
 
 
 class RefPipeline:

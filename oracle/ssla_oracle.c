@@ -310,6 +310,14 @@ static void head_cell(const OrModel* m, int gx, int gy, const float* feat,
     for (int c = 0; c < m->ncls; ++c) raw[5 + c] = cls[c];
 }
 
+/* Raw head outputs [reg0..3, obj, cls...] of one stage-3 feature (the
+ * values the reference's GPU head writes, ssla_s2_s3_head_celled.cuh:
+ * 841-902), for tests of kernels that write raw predictions. */
+void or_head_raw(const OrModel* m, const float* feat, float* raw) {
+    float dec[32];
+    head_cell(m, 0, 0, feat, dec, raw);
+}
+
 /* src/ssla_kernels.cpp:276-286 reset + :969-989 prepopulate_head_zero. */
 void or_state_reset(const OrModel* m, OrState* s) {
     for (int l = 0; l < 8; ++l)

@@ -117,6 +117,9 @@ void or_run_s2_records(const OrModel* m, OrState* s, const int* x2,
                        const int* y2, const float* feat1, const int* owner,
                        int n, int* pass2, int* pass3, float* s3_feat);
 
+/* Raw head outputs [reg 4, obj, cls ncls] of one 96-float stage-3 feature. */
+void or_head_raw(const OrModel* m, const float* feat, float* raw);
+
 /* Math restatements exposed for tests. */
 float or_expf(float x);
 float or_sigmoidf(float x);

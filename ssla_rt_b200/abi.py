@@ -118,7 +118,7 @@ EXPORTED = (
     "ssla_expf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
     "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
     "ssla_engine_live_start", "ssla_engine_live_join", "ssla_engine_live_latency",
-    "ssla_engine_live_withhold_completion",
+    "ssla_engine_live_withhold_completion", "ssla_engine_fill_s2s3_config",
     "ssla_engine_set_owned", "ssla_write_oracle_dump", "ssla_engine_oracle_dump",
     "ssla_engine_strip_init", "ssla_engine_strip_recv_buffer", "ssla_engine_strip_connect",
     "ssla_engine_strip_drain", "ssla_strip_drain_lockstep", "ssla_engine_strip_status",

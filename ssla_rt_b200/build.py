@@ -43,7 +43,28 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps) or not os.path.exists(S01G_LIB)
 
 
+# The stage-2/3 ring consumer module (kernels/), prebuilt for sm_100a: the
+# same source the reference's runners NVRTC-compile, loadable by name.
+KERNELS = os.path.join(HERE, "kernels")
+CONSUMER_SRC = os.path.join(KERNELS, "ssla_s2_s3_head_celled.cuh")
+CONSUMER_HDR = os.path.join(KERNELS, "proto_layer_pair.cuh")
+CONSUMER_CUBIN = os.path.join(HERE, "ssla_s2s3_consumer.cubin")
+
+
+def build_consumer(force: bool = False, verbose: bool = False) -> str:
+    if (not force and os.path.exists(CONSUMER_CUBIN) and
+            os.path.getmtime(CONSUMER_CUBIN) >= max(os.path.getmtime(CONSUMER_SRC), os.path.getmtime(CONSUMER_HDR))):
+        return CONSUMER_CUBIN
+    cmd = [_nvcc(), "-x", "cu", "-cubin", "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+           "-lineinfo", f"-I{KERNELS}", CONSUMER_SRC, "-o", CONSUMER_CUBIN]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return CONSUMER_CUBIN
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    build_consumer(force=force, verbose=verbose)
     if not force and not _stale():
         return LIB
     cmd = [_nvcc(), *NVCC_FLAGS, f"-I{os.path.join(REPO, 'include')}", f"-I{CSRC}",

@@ -1615,6 +1615,38 @@ int ssla_engine_live_join(SslaEngine* eng, unsigned* status) {
     });
 }
 
+int ssla_engine_fill_s2s3_config(SslaEngine* eng, HybridS2S3Config* cfg, int block) {
+    if (!eng || !cfg || block < 0 || block >= SSLA_MAX_BLOCKS) {
+        ssla::g_last_error = "bad argument";
+        return SSLA_ERR_ARG;
+    }
+    const ssla::Engine& e = eng->e;
+    for (int li = 0; li < 4; ++li) {
+        const ssla::DevLayer& L = e.L[4 + li];
+        LayerWeightsS2S3& w = cfg->layers[block][li];
+        w.qvgIn = L.qvgT;
+        w.goW = L.goWT;
+        w.input_proj = L.ipT;
+        w.ln_gamma = L.gamma;
+        w.ln_beta = L.beta;
+    }
+    const ssla::DevHead& h = e.head;
+    cfg->head_W = nullptr;
+    cfg->head_b = nullptr;
+    cfg->head_cls_conv_W = h.cls_convT;
+    cfg->head_cls_conv_b = h.cls_conv_b;
+    cfg->head_cls_pred_W = h.cls_predT;
+    cfg->head_cls_pred_b = h.cls_pred_b;
+    cfg->head_reg_conv_W = h.reg_convT;
+    cfg->head_reg_conv_b = h.reg_conv_b;
+    cfg->head_reg_pred_W = h.reg_predT;
+    cfg->head_reg_pred_b = h.reg_pred_b;
+    cfg->head_obj_pred_W = h.obj_predT;
+    cfg->head_obj_pred_b = h.obj_pred_b;
+    cfg->head_out_dim = 5 + e.g.ncls;
+    return SSLA_OK;
+}
+
 int ssla_engine_live_withhold_completion(SslaEngine* eng, long long ring_index) {
     if (!eng || ring_index < -1) { ssla::g_last_error = "bad argument"; return SSLA_ERR_ARG; }
     return ssla::guarded([&] {

@@ -56,6 +56,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_live_start": (i, [vp, i, C.POINTER(abi.SslaLiveRing), C.c_uint, vp]),
         "ssla_engine_live_join": (i, [vp, C.POINTER(C.c_uint)]),
         "ssla_engine_live_withhold_completion": (i, [vp, C.c_longlong]),
+        "ssla_engine_fill_s2s3_config": (i, [vp, C.POINTER(abi.HybridS2S3Config), i]),
         "ssla_engine_live_latency": (i, [vp, i, vp, i, vp, vp, vp]),
         "ssla_engine_set_owned": (i, [vp, i, i, i, i, i, vp]),
         "ssla_engine_strip_init": (i, [vp, i, i, i, i, i, i]),
@@ -258,6 +259,11 @@ class SslaEngine:
         if check or rc != abi.SSLA_ERR_CUDA:
             _check(rc)
         return st.value
+
+    def fill_s2s3_config(self, cfg: "abi.HybridS2S3Config", block: int) -> None:
+        """Layer 4-7 and head weight pointers of ``cfg`` (block ``block``)
+        from this engine's device weights (the reference's GPU layout)."""
+        _check(self.lib.ssla_engine_fill_s2s3_config(self.h, C.byref(cfg), block))
 
     def live_withhold_completion(self, ring_index: int) -> None:
         """Test hook of the loop's timeout path: the next live loop withholds

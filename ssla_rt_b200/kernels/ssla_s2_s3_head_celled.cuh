@@ -1,0 +1,567 @@
+// B200 consumer of the reference's stage-2/3 ring records: the four kernels
+// the reference's runners load by name from this module --
+//   k_ssla_s2s3_celled_drain_n          (ssla_s2_s3_head_celled.cuh:914-925)
+//   k_ssla_s2s3_celled_drain_n_multi    (:1110-1115)
+//   k_ssla_s2s3_celled_persistent       (:1271-1283)
+//   k_ssla_s2s3_celled_persistent_multi (:1547-1556)
+// -- with the reference's parameter lists, launch shape (one block of
+// 288 threads per ring, dynamic shared memory sized by the caller,
+// orin/bench_s2_s3_head_celled.py:89-108) and buffer layouts
+// (HybridS2S3Config, HybridInputRec, HybridS2S3OutputSlot, GpuTimingSlot).
+// The runners NVRTC-compile this file with proto_layer_pair.cuh
+// (orin/orin/nvrtc_util.py:74-86); ssla_rt_b200/build.py also builds it
+// into a prebuilt sm_100a module (ssla_s2s3_consumer.cubin) that can be
+// loaded by name instead.
+//
+// What each block does per batch of <= 8 consecutive records of its ring
+// (ring order, the reference's BATCH):
+//   gate s2 (tdrop counter of the record's stage-2 cell) -> layers 4, 5 on
+//   the stage-2 grid -> pool -> gate s3 for records that passed gate 2 ->
+//   layers 6, 7 on the stage-3 grid -> (persistent kernels) the YOLOX head
+//   for records that own their cell and passed both gates -> output slots /
+//   predictions, versions, timing slots, tail and events_done.
+// A layer's second half runs state-only for records whose output is not
+// consumed (layer 5 without gate 2, layer 7 without gate 3), as the
+// reference does (:1684-1713).
+//
+// Work split inside a block (9 warps): warp w owns the grid cells with
+// (cy % 3) * 3 + (cx % 3) == w, so the 9 cells of one record's 3x3 patch
+// belong to 9 different warps and every cell has exactly one writer; each
+// warp walks the batch's records in ring order and applies, for each patch
+// cell it owns, the fused q/v/g matvec, the LRU update of the cell's hidden
+// state and the goW contribution of that patch position -- no atomics on
+// state.  One warp per record then sums the contributions in the
+// reference's patch order (8..0), adds the residual and applies LayerNorm.
+//
+// Arithmetic is the CPU oracle's (proto_layer_pair.cuh), so the outputs are
+// bit-identical to it, not merely within the reference's max|d| s3_feat
+// budget of 5.0.
+//
+// Differences from the reference kernels, all on paths the reference leaves
+// undefined:
+//   * records whose stage-2 coordinates lie outside the H2 x W2 grid enter
+//     no gate and no layer (the reference would index out of bounds): pass
+//     codes 0 (owner) / -1, s3_feat zero;
+//   * a persistent block leaves its polling loop after
+//     ssla_consumer_idle_ns (a module global, 30 s unless the host sets it
+//     through cuModuleGetGlobal) without a new record, ORing bit 1 into the
+//     module global ssla_consumer_status; every wait is bounded;
+//   * a launch whose block is not 288 threads does nothing but OR bit 2
+//     into ssla_consumer_status.
+#pragma once
+#include "proto_layer_pair.cuh"
+
+// ---- the reference's buffer layouts (byte for byte; the runners build them
+// with ctypes, orin/orin/hybrid_common.py:30-122) ----
+struct LayerWeightsS2S3 {
+    const float* qvgIn;        // [9][IN][3*OUT]
+    const float* goW;          // [9][OUT][OUT]  (input channel, output channel)
+    const float* input_proj;   // [IN][OUT] or null (IN == OUT)
+    const float* ln_gamma;
+    const float* ln_beta;
+};
+
+struct HybridStrip {
+    int owned_lo, owned_hi;          // stage-2 x owned range [lo, hi)
+    int s3_owned_lo, s3_owned_hi;
+    int owned_y_lo, owned_y_hi;      // stage-2 y owned range
+    int s3_owned_y_lo, s3_owned_y_hi;
+};
+
+struct GpuTimingSlot {
+    unsigned long long t_pop_clk;
+    unsigned long long t_done_clk;
+    unsigned int seq;
+    unsigned int owner;               // 1 iff the record produced a prediction
+    unsigned long long t_push_ns;
+    unsigned long long t_emit_ns;
+};
+
+constexpr int MAX_BLOCKS = 16;
+
+struct HybridS2S3Config {
+    int H2, W2;
+    int H3, W3;
+    int tdrop_window;
+    int head_out_dim;
+    int n_blocks;
+    int _pad_nblocks;
+    HybridStrip strip[MAX_BLOCKS];
+    LayerWeightsS2S3 layers[MAX_BLOCKS][4];
+    float* hidden[MAX_BLOCKS][4];
+    unsigned char* tdrop_s2[MAX_BLOCKS];
+    unsigned char* tdrop_s3[MAX_BLOCKS];
+    const float* head_W;             // legacy single linear head (96, 7), or null
+    const float* head_b;
+    const float* head_cls_conv_W;    // 2-layer YOLOX head, BN folded, (IN, OUT) row-major
+    const float* head_cls_conv_b;
+    const float* head_cls_pred_W;
+    const float* head_cls_pred_b;
+    const float* head_reg_conv_W;
+    const float* head_reg_conv_b;
+    const float* head_reg_pred_W;
+    const float* head_reg_pred_b;
+    const float* head_obj_pred_W;
+    const float* head_obj_pred_b;
+    float* preds[MAX_BLOCKS];        // [owned s3 cells][7]
+    unsigned int* version[MAX_BLOCKS];
+    GpuTimingSlot* timing[MAX_BLOCKS];
+    unsigned int timing_mask;
+    unsigned int _pad_timing;
+    unsigned long long* kernel_start_clk[MAX_BLOCKS];
+    unsigned long long* kernel_end_clk[MAX_BLOCKS];
+};
+
+struct HybridInputRec {
+    unsigned long long seq_done;      // slot + 1 once published
+    float t;
+    unsigned short x, y;              // stage-2 coordinates
+    float feat1[24];                  // stage-1 output
+    unsigned long long t_push_ns;
+    unsigned long long t_emit_ns;
+};
+
+struct HybridS2S3OutputSlot {
+    int pass2;
+    int pass3;
+    float s3_feat[96];
+};
+
+// (sizes only: NVRTC has no offsetof; the field offsets are those of
+// include/ssla_abi_types.h, which asserts them)
+static_assert(sizeof(HybridInputRec) == 128, "HybridInputRec layout");
+static_assert(sizeof(HybridS2S3OutputSlot) == 392, "HybridS2S3OutputSlot layout");
+static_assert(sizeof(GpuTimingSlot) == 40, "GpuTimingSlot layout");
+static_assert(sizeof(HybridStrip) == 32 && sizeof(LayerWeightsS2S3) == 40, "strip / layer layouts");
+static_assert(sizeof(HybridS2S3Config) == 4616, "HybridS2S3Config layout");
+
+// Idle bound of the persistent kernels and their status word (bit 1: a
+// block left after the idle bound; bit 2: a launch with a block size other
+// than 288 did nothing).
+__device__ unsigned long long ssla_consumer_idle_ns = 30ull * 1000ull * 1000ull * 1000ull;
+__device__ unsigned int ssla_consumer_status = 0u;
+
+namespace sslab {
+
+constexpr int kWarps = 9;              // one per patch-cell owner class
+constexpr int kThreads = kWarps * 32;
+constexpr int kBatch = 8;              // records per batch
+constexpr int C1 = 24, C2 = 48, C3 = 96;
+constexpr int kHeadOut = 7;            // [reg 4, obj, cls 2]
+constexpr int kL4Qvg = 9 * C1 * 3 * C2;   // floats of layer 4's qvg block
+
+struct BatchShared {
+    float x[kBatch][C3];               // current layer input of each record
+    float con[kBatch][9][C3];          // goW contributions by patch position
+    float qh[kWarps][C3];              // per warp: q * h of its current cell; head activations
+    float hy[kBatch][8];               // head outputs of each record
+    int x2[kBatch], y2[kBatch];        // stage-2 coordinates
+    int owner[kBatch];
+    unsigned in_mask, p2, p3;          // bit e: record e in the grid / passed gate 2 / gate 3
+    unsigned heads;                    // bit e: record e ran the head (owner, both gates)
+    unsigned long long t_push[kBatch], t_emit[kBatch];
+    unsigned long long t_pop;
+    int nb, cmd;
+};
+
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned dyn_smem_bytes() {
+    unsigned v;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(v));
+    return v;
+}
+
+// ---- one layer over the batch -------------------------------------------------------
+// enter: records whose patch cells this layer updates; used: records whose
+// output is consumed (q, goW, gather and LayerNorm); (cx, cy) of record e
+// is its cell on this layer's Hl x Wl grid.  wq: the layer's qvg block
+// (shared-memory copy or global).
+template <int IN, int OUT, bool IP>
+__device__ void run_layer(BatchShared& sh, const LayerWeightsS2S3& L, const float* __restrict__ wq, float* hidden,
+                          int Hl, int Wl, int nb, const int* cxs, const int* cys, unsigned enter, unsigned used,
+                          int shift) {
+    constexpr int J3 = 3 * OUT;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // ---- the patch cells this warp owns, record by record in ring order ----
+    for (int e = 0; e < nb; ++e) {
+        if (!((enter >> e) & 1u)) continue;
+        const bool use = (used >> e) & 1u;
+        const int ex = cxs[e] >> shift, ey = cys[e] >> shift;
+        for (int d = 0; d < 9; ++d) {
+            const int cx = ex + 1 - d % 3, cy = ey + 1 - d / 3;
+            if (cx < 0 || cx >= Wl || cy < 0 || cy >= Hl || (cy % 3) * 3 + (cx % 3) != w) continue;
+            float* h = hidden + (static_cast<long long>(cy) * Wl + cx) * OUT;
+            const float* W = wq + static_cast<long long>(d) * IN * J3;
+            for (int c = lane; c < OUT; c += 32) {
+                float q = 0.0f;
+                if (use) q = dot_col<IN>(W + c, J3, sh.x[e], 0.0f);
+                const float v = dot_col<IN>(W + OUT + c, J3, sh.x[e], 0.0f);
+                const float g = dot_col<IN>(W + 2 * OUT + c, J3, sh.x[e], 0.0f);
+                const float hn = __fmaf_rn(sigmoid_exact(g), h[c], v);   // rnn.h:80-91 lru_step
+                h[c] = hn;
+                if (use) sh.qh[w][c] = __fmul_rn(q, hn);
+            }
+            if (use) {
+                __syncwarp();
+                const float* G = L.goW + static_cast<long long>(d) * OUT * OUT;
+                for (int c = lane; c < OUT; c += 32) sh.con[e][d][c] = dot_col<OUT>(G + c, OUT, sh.qh[w], 0.0f);
+                __syncwarp();
+            }
+        }
+    }
+    __syncthreads();
+    // ---- gather + residual + LayerNorm: warp e for record e ----
+    if (w < nb && ((used >> w) & 1u)) {
+        const int e = w;
+        const int ex = cxs[e] >> shift, ey = cys[e] >> shift;
+        float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (lane < OUT / 4) {
+            float r[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int o = 4 * lane + j;
+                r[j] = IP ? dot_col<IN>(L.input_proj + o, OUT, sh.x[e], 0.0f) : sh.x[e][o];
+            }
+            for (int d = 8; d >= 0; --d) {              // the reference's patch order
+                const int cx = ex + 1 - d % 3, cy = ey + 1 - d / 3;
+                if (cx < 0 || cx >= Wl || cy < 0 || cy >= Hl) continue;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) y[j] = __fadd_rn(y[j], sh.con[e][d][4 * lane + j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) y[j] = __fadd_rn(y[j], r[j]);
+        }
+        layernorm_warp<OUT>(y, L.ln_gamma, L.ln_beta);
+        __syncwarp();                                   // the residual has read x[e]
+        if (lane < OUT / 4)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sh.x[e][4 * lane + j] = y[j];
+    }
+    __syncthreads();
+}
+
+// ---- the YOLOX head of one record (warp w), into sh.hy[e] ---------------------------
+// vendor/openeva/heads/async_yolox.h:203-254 with BN folded into the convs:
+// cls = Wcp . SiLU(Wcc . x + bcc) + bcp, reg / obj likewise from the reg conv;
+// outputs [reg 4, obj, cls 2] as the reference's GPU head writes them.
+__device__ void head_record(BatchShared& sh, const HybridS2S3Config& cfg, int e) {
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* x = sh.x[e];
+    float* act = sh.qh[w];
+    if (cfg.head_cls_conv_W != nullptr) {
+        for (int branch = 0; branch < 2; ++branch) {
+            const float* Wc = branch == 0 ? cfg.head_cls_conv_W : cfg.head_reg_conv_W;
+            const float* bc = branch == 0 ? cfg.head_cls_conv_b : cfg.head_reg_conv_b;
+            for (int o = lane; o < C3; o += 32) {
+                const float a = dot_col<C3>(Wc + o, C3, x, bc[o]);
+                act[o] = __fmul_rn(a, sigmoid_exact(a));            // SiLU
+            }
+            __syncwarp();
+            if (branch == 0) {
+                if (lane < 2) sh.hy[e][5 + lane] = dot_col<C3>(cfg.head_cls_pred_W + lane, 2, act, cfg.head_cls_pred_b[lane]);
+            } else {
+                if (lane < 4) sh.hy[e][lane] = dot_col<C3>(cfg.head_reg_pred_W + lane, 4, act, cfg.head_reg_pred_b[lane]);
+                if (lane == 4) sh.hy[e][4] = dot_col<C3>(cfg.head_obj_pred_W, 1, act, cfg.head_obj_pred_b[0]);
+            }
+            __syncwarp();
+        }
+    } else if (lane < kHeadOut) {
+        // legacy single linear head: preds = head_W . x, then + head_b
+        sh.hy[e][lane] = __fadd_rn(dot_col<C3>(cfg.head_W + lane, kHeadOut, x, 0.0f), cfg.head_b[lane]);
+    }
+}
+
+// ---- one batch of nb records at ring positions base .. base + nb - 1 ----------------
+// volatile_ring: the ring lives in host-visible memory a producer writes
+// while the kernel runs (loads bypass the caches).
+__device__ void run_batch(BatchShared& sh, const HybridS2S3Config& cfg, int blk, const HybridInputRec* ring,
+                          unsigned long long base, unsigned long long mask, int nb, const float* wq4,
+                          bool volatile_ring, bool head, HybridS2S3OutputSlot* out) {
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    const HybridStrip& st = cfg.strip[blk];
+    // ---- records -> shared memory ----
+    for (int k = tid; k < nb * C1; k += kThreads) {
+        const int e = k / C1, i = k % C1;
+        const float* src = &ring[(base + e) & mask].feat1[i];
+        sh.x[e][i] = volatile_ring ? __ldcv(src) : *src;
+    }
+    if (tid < nb) {
+        const HybridInputRec* r = &ring[(base + tid) & mask];
+        unsigned int xy;
+        unsigned long long tp, te;
+        if (volatile_ring) {
+            xy = __ldcv(reinterpret_cast<const unsigned int*>(&r->x));
+            tp = __ldcv(&r->t_push_ns);
+            te = __ldcv(&r->t_emit_ns);
+        } else {
+            xy = *reinterpret_cast<const unsigned int*>(&r->x);
+            tp = r->t_push_ns;
+            te = r->t_emit_ns;
+        }
+        const int x2 = static_cast<int>(xy & 0xFFFFu), y2 = static_cast<int>(xy >> 16);
+        sh.x2[tid] = x2;
+        sh.y2[tid] = y2;
+        sh.owner[tid] = (x2 >= st.owned_lo && x2 < st.owned_hi && y2 >= st.owned_y_lo && y2 < st.owned_y_hi) ? 1 : 0;
+        sh.t_push[tid] = tp;
+        sh.t_emit[tid] = te;
+    }
+    __syncthreads();
+    // ---- gate s2: the tdrop counter of each record's stage-2 cell, ring order ----
+    if (w == 0) {
+        const bool act = lane < nb && sh.x2[lane] < cfg.W2 && sh.y2[lane] < cfg.H2;
+        const int key = act ? sh.y2[lane] * cfg.W2 + sh.x2[lane] : 0;
+        const unsigned in = __ballot_sync(kFull, act);
+        const unsigned p2 = __ballot_sync(kFull, gate_lanes(cfg.tdrop_s2[blk], act, key, cfg.tdrop_window));
+        if (lane == 0) {
+            sh.in_mask = in;
+            sh.p2 = p2;
+        }
+    }
+    __syncthreads();
+    const unsigned in = sh.in_mask, p2 = sh.p2;
+    // ---- stage 2: layer 4 for every record, layer 5 state-only without gate 2 ----
+    run_layer<C1, C2, true>(sh, cfg.layers[blk][0], wq4, cfg.hidden[blk][0], cfg.H2, cfg.W2, nb, sh.x2, sh.y2, in,
+                            in, 0);
+    run_layer<C2, C2, false>(sh, cfg.layers[blk][1], cfg.layers[blk][1].qvgIn, cfg.hidden[blk][1], cfg.H2, cfg.W2,
+                             nb, sh.x2, sh.y2, in, p2, 0);
+    // (x[e] is overwritten only by layers whose output record e consumes,
+    // so a record without gate 2 keeps layer 4's output there)
+    // ---- gate s3 for records that passed gate 2, on the pooled cell ----
+    if (w == 0) {
+        const bool act = ((p2 >> lane) & 1u) && (sh.x2[lane] >> 1) < cfg.W3 && (sh.y2[lane] >> 1) < cfg.H3;
+        const int key = act ? (sh.y2[lane] >> 1) * cfg.W3 + (sh.x2[lane] >> 1) : 0;
+        const unsigned p3 = __ballot_sync(kFull, gate_lanes(cfg.tdrop_s3[blk], act, key, cfg.tdrop_window));
+        if (lane == 0) sh.p3 = p3;
+    }
+    __syncthreads();
+    const unsigned p3 = sh.p3;
+    // ---- stage 3: layer 6 for records past gate 2, layer 7 state-only without gate 3 ----
+    if (p2) {
+        run_layer<C2, C3, true>(sh, cfg.layers[blk][2], cfg.layers[blk][2].qvgIn, cfg.hidden[blk][2], cfg.H3,
+                                cfg.W3, nb, sh.x2, sh.y2, p2, p2, 1);
+        run_layer<C3, C3, false>(sh, cfg.layers[blk][3], cfg.layers[blk][3].qvgIn, cfg.hidden[blk][3], cfg.H3,
+                                 cfg.W3, nb, sh.x2, sh.y2, p2, p3, 1);
+    }
+    // ---- output slots (drain_n contract): codes, and the record's last layer output ----
+    if (out != nullptr) {
+        for (int k = tid; k < nb * C3; k += kThreads) {
+            const int e = k / C3, i = k % C3;
+            float v;
+            if ((p3 >> e) & 1u) v = sh.x[e][i];                    // layer 7 output
+            else if ((p2 >> e) & 1u) v = sh.x[e][i];               // layer 6 output
+            else if ((in >> e) & 1u) v = i < C2 ? sh.x[e][i] : 0.0f;   // layer 4 output
+            else v = 0.0f;
+            out[base + e].s3_feat[i] = v;
+        }
+        if (tid < nb) {
+            const int e = tid;
+            const int own = sh.owner[e];
+            const int c2 = (p2 >> e) & 1u, c3 = (p3 >> e) & 1u;
+            out[base + e].pass2 = own ? c2 : -1;
+            out[base + e].pass3 = own ? (c2 ? c3 : 0) : -1;
+        }
+    }
+    // ---- head: records that own their cell and passed both gates ----
+    unsigned heads = 0;
+    if (head && (cfg.head_cls_conv_W != nullptr || cfg.head_W != nullptr)) {
+        for (int e = 0; e < nb; ++e)
+            if (((p3 >> e) & 1u) && sh.owner[e]) heads |= 1u << e;
+        if (w < nb && ((heads >> w) & 1u)) head_record(sh, cfg, w);
+        __syncthreads();
+        // predictions in ring order (the last record of a cell wins), one
+        // version bump per write; cells outside the owned stage-3 range
+        // are not written (ssla_s2_s3_head_celled.cuh:887-901)
+        if (w == 0 && heads && cfg.preds[blk] != nullptr && cfg.version[blk] != nullptr) {
+            const int ow = st.s3_owned_hi - st.s3_owned_lo, oh = st.s3_owned_y_hi - st.s3_owned_y_lo;
+            for (int e = 0; e < nb; ++e) {
+                if (!((heads >> e) & 1u)) continue;
+                const int hx = (sh.x2[e] >> 1) - st.s3_owned_lo, hy = (sh.y2[e] >> 1) - st.s3_owned_y_lo;
+                if (hx < 0 || hx >= ow || hy < 0 || hy >= oh) continue;
+                const int cell = hy * ow + hx;
+                if (lane < kHeadOut) cfg.preds[blk][static_cast<long long>(cell) * kHeadOut + lane] = sh.hy[e][lane];
+                __syncwarp();
+                if (lane == 0) cfg.version[blk][cell] += 1u;
+                __syncwarp();
+            }
+        }
+    }
+    if (tid == 0) sh.heads = heads;
+    __syncthreads();
+}
+
+// ---- kernel bodies ------------------------------------------------------------------------
+// Layer 4's qvg block in dynamic shared memory when the launch provides
+// room for it (the reference's launch does), else read from global memory.
+__device__ const float* stage_l4(const HybridS2S3Config& cfg, int blk, float* dyn) {
+    if (dyn_smem_bytes() < static_cast<unsigned>(sizeof(float) * kL4Qvg)) return cfg.layers[blk][0].qvgIn;
+    const float* src = cfg.layers[blk][0].qvgIn;
+    for (int i = threadIdx.x; i < kL4Qvg; i += kThreads) dyn[i] = src[i];
+    __syncthreads();
+    return dyn;
+}
+
+__device__ bool launch_ok() {
+    if (blockDim.x == kThreads && blockDim.y == 1 && blockDim.z == 1) return true;
+    if (threadIdx.x == 0) atomicOr(&ssla_consumer_status, 2u);
+    return false;
+}
+
+__device__ void drain_body(const HybridS2S3Config& cfg, int blk, const HybridInputRec* ring, int n,
+                           HybridS2S3OutputSlot* out, unsigned long long* batch_clk, float* dyn) {
+    __shared__ BatchShared sh;
+    if (threadIdx.x == 0 && cfg.kernel_start_clk[blk] != nullptr) *cfg.kernel_start_clk[blk] = clock64();
+    if (n <= 0) return;
+    const float* wq4 = stage_l4(cfg, blk, dyn);
+    int bi = 0;
+    for (int b0 = 0; b0 < n; b0 += kBatch, ++bi) {
+        const int nb = n - b0 < kBatch ? n - b0 : kBatch;
+        unsigned long long t0 = 0;
+        if (threadIdx.x == 0 && batch_clk != nullptr) t0 = clock64();
+        run_batch(sh, cfg, blk, ring, static_cast<unsigned long long>(b0), ~0ull, nb, wq4, false, false, out);
+        if (threadIdx.x == 0 && batch_clk != nullptr) {
+            batch_clk[2 * bi] = t0;
+            batch_clk[2 * bi + 1] = clock64();
+        }
+    }
+}
+
+__device__ void persistent_body(const HybridS2S3Config& cfg, int blk, const HybridInputRec* ring,
+                                unsigned long long mask, unsigned long long* tail, const int* stop_flag,
+                                unsigned long long* events_done, unsigned spin_ns, float* dyn) {
+    __shared__ BatchShared sh;
+    const int tid = threadIdx.x;
+    if (tid == 0 && cfg.kernel_start_clk[blk] != nullptr) {
+        *cfg.kernel_start_clk[blk] = clock64();
+        __threadfence_system();
+    }
+    const float* wq4 = stage_l4(cfg, blk, dyn);
+    unsigned long long t_local = *reinterpret_cast<volatile unsigned long long*>(tail);
+    unsigned long long idle_since = gtime();
+    const unsigned long long idle_ns = *reinterpret_cast<volatile unsigned long long*>(&ssla_consumer_idle_ns);
+    for (;;) {
+        if (tid == 0) {
+            int cmd = 0, n = 0;
+            if (*reinterpret_cast<const volatile int*>(stop_flag) != 0) {
+                cmd = 1;
+            } else {
+                while (n < kBatch && ld_acquire_sys(&ring[(t_local + n) & mask].seq_done) == t_local + n + 1ull) ++n;
+                if (n > 0) {
+                    __threadfence_system();
+                    sh.t_pop = clock64();
+                    idle_since = gtime();
+                } else if (gtime() - idle_since > idle_ns) {
+                    cmd = 2;
+                } else if (spin_ns) {
+                    __nanosleep(spin_ns);
+                }
+            }
+            sh.cmd = cmd;
+            sh.nb = n;
+        }
+        __syncthreads();
+        const int cmd = sh.cmd, nb = sh.nb;
+        __syncthreads();                      // every thread has read cmd / nb
+        if (cmd != 0) {
+            if (tid == 0) {
+                if (cmd == 2) atomicOr(&ssla_consumer_status, 1u);
+                if (cfg.kernel_end_clk[blk] != nullptr) {
+                    *cfg.kernel_end_clk[blk] = clock64();
+                    __threadfence_system();
+                }
+            }
+            return;
+        }
+        if (nb == 0) continue;
+        run_batch(sh, cfg, blk, ring, t_local, mask, nb, wq4, true, true, nullptr);
+        if (tid == 0) {
+            if (cfg.timing[blk] != nullptr) {
+                const unsigned long long t_done = clock64();
+                const unsigned heads = sh.heads;
+                for (int e = 0; e < nb; ++e) {
+                    const unsigned long long seq = t_local + static_cast<unsigned long long>(e);
+                    GpuTimingSlot* ts = &cfg.timing[blk][static_cast<unsigned>(seq) & cfg.timing_mask];
+                    ts->t_pop_clk = sh.t_pop;
+                    ts->t_done_clk = t_done;
+                    ts->seq = static_cast<unsigned>(seq);
+                    ts->owner = (heads >> e) & 1u;
+                    ts->t_push_ns = sh.t_push[e];
+                    ts->t_emit_ns = sh.t_emit[e];
+                }
+            }
+            t_local += static_cast<unsigned long long>(nb);
+            __threadfence_system();
+            st_release_sys(tail, t_local);
+            st_release_sys(events_done, t_local);
+        } else {
+            t_local += static_cast<unsigned long long>(nb);
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace sslab
+
+// ---- the four entry points the runners load by name -------------------------------------
+
+extern "C" __global__ void __launch_bounds__(sslab::kThreads, 1)
+k_ssla_s2s3_celled_drain_n(const HybridS2S3Config* cfg_in, const HybridInputRec* ring0, const HybridInputRec* ring1,
+                           int n0, int n1, HybridS2S3OutputSlot* out0, HybridS2S3OutputSlot* out1,
+                           unsigned long long* batch_clk0, unsigned long long* batch_clk1) {
+    extern __shared__ __align__(16) float ssla_dyn_smem[];
+    if (blockIdx.x >= 2 || !sslab::launch_ok()) return;
+    const int blk = blockIdx.x;
+    sslab::drain_body(*cfg_in, blk, blk == 0 ? ring0 : ring1, blk == 0 ? n0 : n1, blk == 0 ? out0 : out1,
+                      blk == 0 ? batch_clk0 : batch_clk1, ssla_dyn_smem);
+}
+
+extern "C" __global__ void __launch_bounds__(sslab::kThreads, 1)
+k_ssla_s2s3_celled_drain_n_multi(const HybridS2S3Config* cfg_in, const HybridInputRec* const* rings, const int* ns,
+                                 HybridS2S3OutputSlot* const* outs, unsigned long long* const* batch_clks) {
+    extern __shared__ __align__(16) float ssla_dyn_smem[];
+    const HybridS2S3Config& cfg = *cfg_in;
+    if (static_cast<int>(blockIdx.x) >= cfg.n_blocks || !sslab::launch_ok()) return;
+    const int blk = blockIdx.x;
+    sslab::drain_body(cfg, blk, rings[blk], ns[blk], outs != nullptr ? outs[blk] : nullptr,
+                      batch_clks != nullptr ? batch_clks[blk] : nullptr, ssla_dyn_smem);
+}
+
+extern "C" __global__ void __launch_bounds__(sslab::kThreads, 1)
+k_ssla_s2s3_celled_persistent(const HybridS2S3Config* cfg_in, HybridInputRec* ring0, HybridInputRec* ring1,
+                              unsigned long long ring_mask, volatile unsigned long long* tail0,
+                              volatile unsigned long long* tail1, volatile int* stop_flag,
+                              volatile unsigned long long* events_done0, volatile unsigned long long* events_done1,
+                              unsigned int spin_ns) {
+    extern __shared__ __align__(16) float ssla_dyn_smem[];
+    if (blockIdx.x >= 2 || !sslab::launch_ok()) return;
+    const int blk = blockIdx.x;
+    sslab::persistent_body(*cfg_in, blk, blk == 0 ? ring0 : ring1, ring_mask,
+                           const_cast<unsigned long long*>(blk == 0 ? tail0 : tail1), const_cast<int*>(stop_flag),
+                           const_cast<unsigned long long*>(blk == 0 ? events_done0 : events_done1), spin_ns,
+                           ssla_dyn_smem);
+}
+
+extern "C" __global__ void __launch_bounds__(sslab::kThreads, 1)
+k_ssla_s2s3_celled_persistent_multi(const HybridS2S3Config* cfg_in, HybridInputRec* const* rings,
+                                    unsigned long long ring_mask, volatile unsigned long long** tails,
+                                    volatile int* stop_flag, volatile unsigned long long** events_dones,
+                                    unsigned int spin_ns) {
+    extern __shared__ __align__(16) float ssla_dyn_smem[];
+    const HybridS2S3Config& cfg = *cfg_in;
+    if (static_cast<int>(blockIdx.x) >= cfg.n_blocks || !sslab::launch_ok()) return;
+    const int blk = blockIdx.x;
+    sslab::persistent_body(cfg, blk, rings[blk], ring_mask, const_cast<unsigned long long*>(tails[blk]),
+                           const_cast<int*>(stop_flag), const_cast<unsigned long long*>(events_dones[blk]), spin_ns,
+                           ssla_dyn_smem);
+}

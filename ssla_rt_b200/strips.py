@@ -107,7 +107,9 @@ def exact_strip_parity(weights_dir: str, events: np.ndarray, rank: int, world: i
     single-sensor run: the flags of its owned events, the hidden state of its
     rows at every layer, its gate counters, predictions and versions.
     Returns {"ok", "events", "routed", "owned", "exchange_status",
-    "mismatch": [names]}; every rank must call it together."""
+    "mismatch": {name: {"rows": first differing rows (stage-grid rows
+    counted from the strip's first), "n": how many}}}; every rank must call
+    it together."""
     import torch
     from . import abi
     from .engine import SslaEngine
@@ -133,21 +135,22 @@ def exact_strip_parity(weights_dir: str, events: np.ndarray, rank: int, world: i
     ff = torch.zeros(max(1, len(events)), dtype=torch.uint8, device=dev)
     full.drain(torch.from_numpy(np.ascontiguousarray(events)).to(dev), [0, len(events)], flags=ff)
     torch.cuda.synchronize(dev)
-    bad = []
+    bad = {}
+
+    def cmp(name, a, b):
+        if not np.array_equal(a, b):
+            rows = np.nonzero((a != b).reshape(a.shape[0], -1).any(axis=1))[0]
+            bad[name] = {"rows": [int(r) for r in rows[:8]], "n": int(len(rows))}
+
     idx = np.nonzero(mask)[0]
-    if not np.array_equal(sflags.cpu().numpy()[:n][own], ff.cpu().numpy()[idx[own]]):
-        bad.append("flags")
+    cmp("flags", sflags.cpu().numpy()[:n][own], ff.cpu().numpy()[idx[own]])
     for l in range(8):
         s = l // 2
-        if not np.array_equal(_rows(eng.hidden(l), H, W, s, lo, hi), _rows(full.hidden(l), H, W, s, lo, hi)):
-            bad.append(f"hidden{l}")
+        cmp(f"hidden{l}", _rows(eng.hidden(l), H, W, s, lo, hi), _rows(full.hidden(l), H, W, s, lo, hi))
     for g, s in enumerate((1, 2, 2, 3)):
-        if not np.array_equal(_rows(eng.counters(g), H, W, s, lo, hi), _rows(full.counters(g), H, W, s, lo, hi)):
-            bad.append(f"counter{g}")
-    if not np.array_equal(_rows(eng.preds_dec(), H, W, 3, lo, hi), _rows(full.preds_dec(), H, W, 3, lo, hi)):
-        bad.append("preds")
-    if not np.array_equal(_rows(eng.version(), H, W, 3, lo, hi), _rows(full.version(), H, W, 3, lo, hi)):
-        bad.append("version")
+        cmp(f"counter{g}", _rows(eng.counters(g), H, W, s, lo, hi), _rows(full.counters(g), H, W, s, lo, hi))
+    cmp("preds", _rows(eng.preds_dec(), H, W, 3, lo, hi), _rows(full.preds_dec(), H, W, 3, lo, hi))
+    cmp("version", _rows(eng.version(), H, W, 3, lo, hi), _rows(full.version(), H, W, 3, lo, hi))
     barrier()                 # no rank closes its buffers while a neighbour may still read them
     eng.close()
     full.close()

@@ -65,7 +65,7 @@ def test_exact_strips_across_gpus(stub_dir, world):
             if p.is_alive():
                 p.kill()
     for r in range(world):
-        assert results[r]["ok"], (r, results[r])
+        assert results[r]["ok"], str(results)
         assert results[r]["owned"] > 0 and results[r]["exchange_status"] == 0
     assert sum(results[r]["owned"] for r in range(world)) == 200_000
     assert all(p.exitcode == 0 for p in procs)
