@@ -437,6 +437,10 @@ int  ssla_measure_fp32_peak(int device, double* tflops_out);
 /* Portable exp used by every sigmoid / SiLU / box decode of the engine
  * (the device code's exact twin), for tests on hosts without a GPU. */
 float ssla_expf_host(float x);
+/* The sigmoid every LRU gate and SiLU of the engine uses (the device code's
+ * exact twin): 1 / (1 + exp(-x)) with a degree-6 minimax exp on the clamped
+ * range it needs, within 2.3 ulp of the exact value. */
+float ssla_sigmoidf_host(float x);
 
 const char* ssla_last_error(void);
 const char* ssla_version(void);

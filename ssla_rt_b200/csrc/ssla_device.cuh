@@ -135,13 +135,40 @@ __host__ __device__ __forceinline__ float ssla_expf(float x) {
     return (p * ssla_pow2i(n1)) * ssla_pow2i(n2);
 }
 
-// vendor/openeva/prim/activation.h:17.  The reciprocal is IEEE round-to-
-// nearest on both sides (__frcp_rn on the device), i.e. exactly 1.0f / y.
+// vendor/openeva/prim/activation.h:17, 1 / (1 + exp(-x)), with an exp of
+// its own for the range the sigmoid needs: t = -x clamped to [-17, 88]
+// (for x >= 17 the result is exactly 1, as 1 + exp(-17) rounds to 1; for
+// x <= -88 it is 1 / (1 + e^88) < 6.1e-39 instead of a smaller value).
+// n = nearest integer to t * log2(e) (1.5 * 2^23 trick), r = t - n ln 2 by
+// Cody-Waite with ln 2 split into a 12-bit head and a float tail, exp(r)
+// by a degree-6 minimax polynomial on [-ln2/2, ln2/2] (Remez exchange,
+// coefficients rounded to float, 0.87 ulp), Horner with fused
+// multiply-adds, then one exact scaling by 2^n (n in [-25, 127]).  IEEE
+// basic operations only, identical on host and device; the reciprocal is
+// IEEE round-to-nearest (__frcp_rn on the device, exactly 1.0f / y).
+// Within 2.3 ulp of the exact sigmoid, as the general exp route was.
 __host__ __device__ __forceinline__ float ssla_sigmoidf(float x) {
+    if (x != x) return x;
+    const float t = fminf(fmaxf(-x, -17.0f), 88.0f);
+    const float big = fmaf(t, 1.44269502f, 12582912.0f);
+    const float n = big - 12582912.0f;
+    float r = fmaf(-n, 0.693115234375f, t);
+    r = fmaf(-n, 3.19461833e-05f, r);
+    float p = 1.38368458e-03f;
+    p = fmaf(p, r, 8.37481581e-03f);
+    p = fmaf(p, r, 4.16682251e-02f);
+    p = fmaf(p, r, 1.66664198e-01f);
+    p = fmaf(p, r, 4.99999911e-01f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
 #ifdef __CUDA_ARCH__
-    return __frcp_rn(1.0f + ssla_expf(-x));
+    const int ni = __float_as_int(big) - 0x4B400000;
+    return __frcp_rn(1.0f + p * ssla_pow2i(ni));
 #else
-    return 1.0f / (1.0f + ssla_expf(-x));
+    union { float f; int32_t i; } bb;
+    bb.f = big;
+    const int ni = bb.i - 0x4B400000;
+    return 1.0f / (1.0f + p * ssla_pow2i(ni));
 #endif
 }
 

@@ -583,11 +583,15 @@ struct Engine {
         int has[2] = {0, 0};
         DevBuf idx, cnt, recv[2], ctr;
         char* peer[2] = {nullptr, nullptr};     // the neighbour's receive buffer for my rows of side s
+        int peer_cap[2] = {0, 0};               // rows per parity of that buffer (the neighbour's cap)
         void* opened[2] = {nullptr, nullptr};   // IPC mappings to close
         unsigned long long seq = 0;
         unsigned* err = nullptr;                // host-mapped SSLA_STRIP_ERR_* bits
     } strip;
-    static constexpr size_t kStripHdr = 32;     // u64 sequence, u64 row count per parity, pad
+    // receive-buffer header: u64 sequence, u64 row count per parity, u64 the
+    // buffer's rows per parity (its owner's cap; senders size the parity
+    // regions and clamp their row counts with it)
+    static constexpr size_t kStripHdr = 32;
 
     size_t strip_recv_bytes() const { return kStripHdr + 2 * static_cast<size_t>(strip.cap) * 96 * sizeof(float); }
 
@@ -607,6 +611,8 @@ struct Engine {
             if (strip.has[sd]) {
                 strip.recv[sd].alloc(strip_recv_bytes());
                 SSLA_CK(cudaMemset(strip.recv[sd].p, 0, strip_recv_bytes()));
+                const unsigned long long rows = static_cast<unsigned long long>(cap);
+                SSLA_CK(cudaMemcpy(strip.recv[sd].as<char>() + 24, &rows, sizeof rows, cudaMemcpyHostToDevice));
             }
         if (!strip.err) SSLA_CK(cudaHostAlloc(&strip.err, sizeof(unsigned), cudaHostAllocMapped));
         *strip.err = 0;
@@ -640,6 +646,11 @@ struct Engine {
             if (!ptr) throw std::invalid_argument("strip_connect needs a device address or an IPC handle");
             strip.peer[side] = static_cast<char*>(ptr);
         }
+        // the neighbour's rows per parity, from its buffer's header
+        unsigned long long rows = 0;
+        SSLA_CK(cudaMemcpy(&rows, strip.peer[side] + 24, sizeof rows, cudaMemcpyDeviceToHost));
+        if (rows == 0 || rows > (1ull << 30)) throw std::invalid_argument("strip_connect: the peer buffer has no row capacity");
+        strip.peer_cap[side] = static_cast<int>(rows);
     }
 
     // Step j of a strip drain: 0 = front, band lists, layer 1; 1..5 = layer
@@ -673,11 +684,14 @@ struct Engine {
     void strip_xfer(int j, bool do_export, unsigned long long seq, bool wait, cudaStream_t st) {
         const int l = j + 1, k = (l + 1) / 2, C = chans(l / 2);
         const int parity = static_cast<int>(seq & 1u);
-        const size_t data_off = kStripHdr + static_cast<size_t>(parity) * strip.cap * 96 * sizeof(float);
         for (int sd = 0; sd < 2; ++sd) {
             if (!strip.has[sd]) continue;
+            // parity regions of the buffer written: the receiver's rows per
+            // parity (its cap), whether it is the neighbour's or this engine's
+            const int rows = do_export ? strip.peer_cap[sd] : strip.cap;
+            const size_t data_off = kStripHdr + static_cast<size_t>(parity) * rows * 96 * sizeof(float);
             StripXferArgs xa{};
-            xa.X = ws.X.as<float>(); xa.C = C; xa.cap = strip.cap; xa.parity = parity; xa.seq = seq;
+            xa.X = ws.X.as<float>(); xa.C = C; xa.cap = std::min(strip.cap, rows); xa.parity = parity; xa.seq = seq;
             xa.err = strip.err;
             const int q = (k - 1) * 4 + sd * 2 + (do_export ? 0 : 1);
             xa.idx = strip.idx.as<int>() + static_cast<size_t>(q) * strip.cap;
@@ -1358,6 +1372,7 @@ extern "C" {
 const char* ssla_last_error(void) { return ssla::g_last_error.c_str(); }
 const char* ssla_version(void) { return "ssla_b200 0.1.0 (sm_100a)"; }
 float ssla_expf_host(float x) { return ssla::ssla_expf(x); }
+float ssla_sigmoidf_host(float x) { return ssla::ssla_sigmoidf(x); }
 
 int ssla_engine_create(const char* weights_dir, const SslaEngineConfig* cfg, SslaEngine** out) {
     if (!weights_dir || !cfg || !out) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }

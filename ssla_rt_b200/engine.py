@@ -81,6 +81,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_phase_times": (i, [vp, vp, i, C.POINTER(C.c_int)]),
         "ssla_measure_fp32_peak": (i, [i, C.POINTER(C.c_double)]),
         "ssla_expf_host": (f, [f]),
+        "ssla_sigmoidf_host": (f, [f]),
         "ssla_last_error": (C.c_char_p, []),
         "ssla_version": (C.c_char_p, []),
     }

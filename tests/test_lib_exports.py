@@ -75,3 +75,34 @@ def test_noalloc_source_names_no_allocating_call():
                  "cudaMallocManaged", "cudaMallocPitch", "cudaMalloc3D", "cudaMallocArray", "cuMemAlloc",
                  "cuMemCreate", "malloc(", "new ", "std::vector", "torch"):
         assert name not in code, name
+
+
+def test_sigmoid_twin_is_bit_identical_to_oracle(oracle_mod):
+    lib = load_library()
+    olib = C.CDLL(oracle_mod.ORACLE_SO)
+    olib.or_sigmoidf.restype = C.c_float
+    olib.or_sigmoidf.argtypes = [C.c_float]
+    rng = np.random.default_rng(2)
+    xs = np.concatenate([rng.uniform(-120, 120, 20000), rng.normal(0, 4, 20000),
+                         [0.0, -0.0, 16.99, 17.0, 17.01, -87.9, -88.0, -88.1, 1e-30]]).astype(np.float32)
+    for x in xs:
+        a = np.float32(lib.ssla_sigmoidf_host(float(x)))
+        b = np.float32(olib.or_sigmoidf(float(x)))
+        assert a.view(np.uint32) == b.view(np.uint32), x
+
+
+def test_sigmoid_accuracy():
+    """Within 2.3 ulp of the exact sigmoid wherever the result is normal."""
+    lib = load_library()
+    rng = np.random.default_rng(3)
+    xs = np.concatenate([rng.uniform(-87, 30, 60000), rng.normal(0, 4, 60000),
+                         np.linspace(-17.5, 17.5, 20001)]).astype(np.float32)
+    worst = 0.0
+    for x in xs:
+        got = np.float32(lib.ssla_sigmoidf_host(float(x)))
+        ref = 1.0 / (1.0 + math.exp(-float(x)))
+        if ref < 1.2e-38:
+            continue
+        worst = max(worst, abs(float(got) - ref) / float(np.spacing(np.float32(ref))))
+    assert worst <= 2.3, worst
+    assert lib.ssla_sigmoidf_host(17.0) == 1.0 and lib.ssla_sigmoidf_host(40.0) == 1.0
