@@ -399,6 +399,49 @@ def consumer_sweep(weights_dir: str, device: int, reps: int = 3) -> dict:
                       f"{reps}, L2 flushed before each rep"}
 
 
+def head_modes(weights_dir: str, device: int, parts, reps: int = 5) -> dict:
+    """The head on the CUDA cores (exact, the default) against the head's two
+    1x1 convolutions on tcgen05 tensor cores (split TF32,
+    ssla_engine_set_head_mode): the head phase's mean CUDA-event time over
+    `reps` profiled config-1 drains in each mode, and the largest difference
+    of the decoded and raw predictions on the same drains (untimed)."""
+    import torch
+    from ssla_rt_b200 import abi
+    from ssla_rt_b200.engine import SslaEngine
+    dev = torch.device("cuda", device)
+    ev = np.ascontiguousarray(np.concatenate(parts))
+    span = float(ev[:, 0].max()) + 1.0
+    out = {}
+    preds = {}
+    for name, mode in (("exact", abi.HEAD_EXACT), ("tensor", abi.HEAD_TENSOR)):
+        eng = SslaEngine(weights_dir, n_partitions=len(parts), max_events=len(ev), layout=abi.LAYOUT_HYBRID,
+                         device=device, max_events_per_partition=max(len(p) for p in parts))
+        eng.set_head_mode(mode)
+        t = torch.from_numpy(ev).to(dev)
+        off = eng.offsets([len(p) for p in parts])
+        eng.drain(t, off)
+        eng.set_profiling(True)
+        ms = []
+        for _ in range(reps):
+            t[:, 0] += span
+            eng.drain(t, off)
+            ms += [m for nm, m, _ in eng.phase_times() if nm == "head"]
+        eng.set_profiling(False)
+        preds[name] = (eng.preds_dec_all(), np.stack([eng.preds_raw(p) for p in range(len(parts))]))
+        out[f"{name}_head_ms"] = sum(ms) / len(ms)
+        if mode == abi.HEAD_TENSOR:
+            out["tensor_status"] = eng.head_status()
+        eng.close()
+    d_dec = np.abs(preds["tensor"][0] - preds["exact"][0])
+    d_raw = np.abs(preds["tensor"][1] - preds["exact"][1])
+    out["max_abs_diff_dec"] = float(d_dec.max())
+    out["max_abs_diff_raw"] = float(d_raw.max())
+    out["max_rel_diff_raw"] = float((d_raw / (np.abs(preds["exact"][1]) + 1e-3)).max())
+    out["method"] = ("config-1 drains, state carried; head phase = CUDA events around k_head / k_head_tc; "
+                     "predictions after the same drains in each mode")
+    return out
+
+
 PARITY_TOL_STAGE = 1e-3          # stated per-stage fp32 tolerance against the reference build
 PARITY_S3_BUDGET = 5.0           # the reference's own P1 budget on max|d| s3_feat
 
@@ -1186,6 +1229,9 @@ def main() -> int:
     # ---- acceptance parity: config 0 against the reference build (rank 0) ----
     parity = None if (args.no_parity or rank != 0) else acceptance_parity(wdir, local)
 
+    # ---- the head on CUDA cores vs tensor cores (rank 0, untimed) ----
+    heads = None if (args.no_parity or rank != 0) else head_modes(wdir, local, parts)
+
     # ---- config 1's persistent-block sweep through the reference kernel ABI (rank 0) ----
     sweep = None if (args.no_sweep or rank != 0) else consumer_sweep(wdir, local)
 
@@ -1215,6 +1261,7 @@ def main() -> int:
             "stage_events": stage_events,
             "phase_ms": phases,
             "parity": parity,
+            "head_modes": heads,
             "sweep": sweep,
             "strips": strips_line,
         }

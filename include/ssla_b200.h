@@ -197,6 +197,22 @@ int  ssla_engine_live_start(SslaEngine* eng, int partition, const SslaLiveRing* 
  * bits.  Returns SSLA_ERR_CUDA if a wait inside the loop ran out. */
 int  ssla_engine_live_join(SslaEngine* eng, unsigned* status);
 
+/* Head selection of the engine's drains.  SSLA_HEAD_EXACT (the default):
+ * the YOLOX head on the CUDA cores in the reference's fmaf order, bit-exact
+ * with the CPU oracle.  SSLA_HEAD_TENSOR: its two 1x1 convolutions (cls_conv
+ * | reg_conv, 96 -> 192) as one tcgen05 tensor-core GEMM over the drain's head
+ * events in three TF32 terms (split TF32), the rest as before; predictions
+ * then equal the exact head's within fp32 rounding, not bit for bit.  Flags,
+ * hidden state and versions are unaffected.  The single-event step and the
+ * live loop always use the exact head.  Replaces the head of the reference's
+ * drains (vendor/openeva/heads/async_yolox.h:203-254,
+ * orin/kernels/ssla_s2_s3_head_celled.cuh:841-902). */
+enum { SSLA_HEAD_EXACT = 0, SSLA_HEAD_TENSOR = 1 };
+int  ssla_engine_set_head_mode(SslaEngine* eng, int mode);
+/* Status bits of the tensor-core head since the last call (bit 0: a wait
+ * for its MMAs ran out); synchronises the device, then clears them. */
+int  ssla_engine_head_status(SslaEngine* eng, unsigned* status);
+
 /* Test hook for the loop's timeout path, no reference counterpart: the next
  * live loop started on `eng` withholds the completion message of ring event
  * `ring_index` (-1: none) from its head CTA.  The head CTA's bounded wait

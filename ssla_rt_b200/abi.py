@@ -103,6 +103,7 @@ class SslaPhaseTime(C.Structure):
 
 SSLA_OK, SSLA_ERR_ARG, SSLA_ERR_CUDA, SSLA_ERR_LOAD, SSLA_ERR_CAPACITY, SSLA_ERR_NO_DEVICE = range(6)
 LAYOUT_DECOMP, LAYOUT_HYBRID = 0, 1
+HEAD_EXACT, HEAD_TENSOR = 0, 1
 F_VALID, F_R1, F_R2, F_R3, F_R4 = 1, 2, 4, 8, 16
 (STATE_HIDDEN, STATE_COUNTER, STATE_LAST_T, STATE_PREDS_DEC, STATE_PREDS_RAW,
  STATE_VERSION, STATE_STAGE_OUT, STATE_FLAGS) = range(8)
@@ -119,6 +120,7 @@ EXPORTED = (
     "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
     "ssla_engine_live_start", "ssla_engine_live_join", "ssla_engine_live_latency",
     "ssla_engine_live_withhold_completion", "ssla_engine_fill_s2s3_config",
+    "ssla_engine_set_head_mode", "ssla_engine_head_status",
     "ssla_engine_set_owned", "ssla_write_oracle_dump", "ssla_engine_oracle_dump",
     "ssla_engine_strip_init", "ssla_engine_strip_recv_buffer", "ssla_engine_strip_connect",
     "ssla_engine_strip_drain", "ssla_strip_drain_lockstep", "ssla_engine_strip_status",

@@ -20,7 +20,7 @@ LIB = os.path.join(HERE, "libssla_b200.so")
 # The same library under the reference's name, for callers that load the
 # s01g_* ABI as libstage01_to_gpu.so (orin/orin/hybrid_common.py S01gAPI).
 S01G_LIB = os.path.join(HERE, "libstage01_to_gpu.so")
-SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp", "ssla_noalloc.cu", "ssla_s01g.cpp", "ssla_step.cu", "ssla_live.cu", "ssla_dump.cpp", "ssla_strip.cu", "ssla_rings.cu", "ssla_replay.cpp"]
+SOURCES = ["ssla_kernels.cu", "ssla_engine.cu", "ssla_weights.cpp", "ssla_noalloc.cu", "ssla_s01g.cpp", "ssla_step.cu", "ssla_live.cu", "ssla_dump.cpp", "ssla_strip.cu", "ssla_rings.cu", "ssla_replay.cpp", "ssla_head_tc.cu"]
 HEADERS = ["ssla_device.cuh", "ssla_kernels.cuh", "ssla_weights.h", "ssla_cluster.cuh"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
               "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-shared",

@@ -53,6 +53,10 @@ struct DevHead {
     const float *cls_predT, *cls_pred_b;                            // [96][ncls]
     const float *reg_predT, *reg_pred_b;                            // [96][4]
     const float *obj_predT, *obj_pred_b;                            // [96][1]
+    // drains only: non-null selects the tensor-core head (k_head_tc), whose
+    // [cls_conv | reg_conv] rows [192][96] these are (TF32 hi terms, then lo)
+    const float* tc_w1;
+    unsigned* tc_err;                                               // its status bits (host-mapped)
 };
 
 // Per-partition state pointers (device memory).

@@ -368,8 +368,14 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         HeadArgs ha{};
         ha.g = g; ha.count = d_count; ha.E4 = w.E[4].as<StageEntry>(); ha.X = X;
         ha.head = *head; ha.head_dec = w.head_dec.as<float>(); ha.head_raw = w.head_raw.as<float>();
-        launch_head(st, ha, w.cap[4]);
-        check_launch("k_head");
+        ha.tc_w1 = head->tc_w1; ha.err = head->tc_err;
+        if (head->tc_w1) {
+            launch_head_tc(st, ha, w.cap[4]);
+            check_launch("k_head_tc");
+        } else {
+            launch_head(st, ha, w.cap[4]);
+            check_launch("k_head");
+        }
         prof.mark("head", 1, st);
     }
 }
@@ -393,6 +399,8 @@ struct Engine {
     DevBuf hbuf[10];
     DevLayer L[8]{};
     DevHead head{};
+    DevBuf head_tc;                         // tensor-core head operand (see DevHead::tc_w1)
+    unsigned* head_tc_err = nullptr;        // host-mapped status bits of k_head_tc
     // state
     DevBuf hidden[8], cnt[4], last_t, preds_dec, preds_raw, version, parts;
     std::vector<PartState> h_parts;
@@ -425,6 +433,7 @@ struct Engine {
         for (void* p : strip.opened)
             if (p) cudaIpcCloseMemHandle(p);
         if (strip.err) cudaFreeHost(strip.err);
+        if (head_tc_err) cudaFreeHost(head_tc_err);
         if (step_err) cudaFreeHost(step_err);
         if (live_err) cudaFreeHost(live_err);
         if (hpipe.st) cudaStreamSynchronize(hpipe.st);
@@ -505,7 +514,30 @@ struct Engine {
         for (int i = 0; i < 10; ++i) upload(hbuf[i], *hv[i]);
         head = DevHead{hbuf[0].as<float>(), hbuf[1].as<float>(), hbuf[2].as<float>(), hbuf[3].as<float>(),
                        hbuf[4].as<float>(), hbuf[5].as<float>(), hbuf[6].as<float>(), hbuf[7].as<float>(),
-                       hbuf[8].as<float>(), hbuf[9].as<float>()};
+                       hbuf[8].as<float>(), hbuf[9].as<float>(), nullptr, nullptr};
+        // the tensor-core head's operand: [cls_conv | reg_conv] as [192 out][96 in]
+        // rows, split into TF32 hi terms and TF32 lo terms (the remainder)
+        {
+            auto tf32 = [](float x) {
+                uint32_t u;
+                std::memcpy(&u, &x, 4);
+                if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+                float r;
+                std::memcpy(&r, &u, 4);
+                return r;
+            };
+            std::vector<float> w1(2 * 192 * 96);
+            for (int o = 0; o < 192; ++o)
+                for (int i = 0; i < 96; ++i) {
+                    const float w = o < 96 ? hh.cls_convT[i * 96 + o] : hh.reg_convT[i * 96 + (o - 96)];
+                    const float hi = tf32(w);
+                    w1[o * 96 + i] = hi;
+                    w1[192 * 96 + o * 96 + i] = tf32(w - hi);
+                }
+            upload(head_tc, w1);
+            SSLA_CK(cudaHostAlloc(&head_tc_err, sizeof(unsigned), cudaHostAllocMapped));
+            *head_tc_err = 0;
+        }
         // state
         for (int l = 0; l < 8; ++l) hidden[l].alloc(state_elems(SSLA_STATE_HIDDEN, l) * 4 * P);
         for (int gi = 0; gi < 4; ++gi) cnt[gi].alloc(state_elems(SSLA_STATE_COUNTER, gi) * P);
@@ -1660,6 +1692,31 @@ int ssla_engine_fill_s2s3_config(SslaEngine* eng, HybridS2S3Config* cfg, int blo
     cfg->head_obj_pred_b = h.obj_pred_b;
     cfg->head_out_dim = 5 + e.g.ncls;
     return SSLA_OK;
+}
+
+int ssla_engine_set_head_mode(SslaEngine* eng, int mode) {
+    if (!eng || (mode != SSLA_HEAD_EXACT && mode != SSLA_HEAD_TENSOR)) {
+        ssla::g_last_error = "bad argument";
+        return SSLA_ERR_ARG;
+    }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        SSLA_CK(cudaDeviceSynchronize());           // no drain in flight reads the head selection
+        ssla::Engine& e = eng->e;
+        e.head.tc_w1 = mode == SSLA_HEAD_TENSOR ? e.head_tc.as<float>() : nullptr;
+        e.head.tc_err = mode == SSLA_HEAD_TENSOR ? e.head_tc_err : nullptr;
+        return SSLA_OK;
+    });
+}
+
+int ssla_engine_head_status(SslaEngine* eng, unsigned* status) {
+    if (!eng || !status) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(eng->e.device);
+        SSLA_CK(cudaDeviceSynchronize());
+        *status = eng->e.head_tc_err ? __atomic_exchange_n(eng->e.head_tc_err, 0u, __ATOMIC_ACQ_REL) : 0u;
+        return SSLA_OK;
+    });
 }
 
 int ssla_engine_live_withhold_completion(SslaEngine* eng, long long ring_index) {

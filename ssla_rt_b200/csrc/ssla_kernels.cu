@@ -34,15 +34,6 @@ __device__ __forceinline__ unsigned lanemask_lt() {
 
 __device__ __forceinline__ int hi_lane(unsigned m) { return 31 - __clz(m); }
 
-// Programmatic dependent launch: a drain kernel is launched while the
-// previous one in the stream completes and waits here for it to complete
-// (and its memory to be visible) before touching anything it may write.
-// No kernel triggers its dependants early: CTAs of the next kernel waiting
-// on the SMs slowed the running one (measured), so the dependant is
-// released at completion and only the launch latency overlaps.  Without
-// the launch attribute the wait is a no-op.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_enter() { pdl_wait(); }
 
 // uint8 counter rule of tdrop_check_at (src/ssla_kernels.cpp:912-921) and
 // parallel_tdrop (ssla_s2_s3_head_celled.cuh:742-745): pass iff window <= 1
@@ -744,12 +735,20 @@ __global__ void __launch_bounds__(kNT) k_compact_scatter(CompactArgs a) {
 // (vendor/openeva/prim/rnn.h:80-91): h = sigmoid(g) * h + v (fmaf), and
 // q -> q * h for entries whose layer output is consumed.  Lanes own
 // channels; hidden state stays in registers for the whole chunk.
+// The CTA stages the tile list through shared memory in rounds of 512
+// entries, the next round's loads issued before the current round is
+// walked, so a warp's walk reads shared memory instead of waiting on an L2
+// round trip per 32 entries; hits are applied HP at a time with their rows'
+// loads issued ahead of the fmaf chain.
 // grid (P, tiles, 8), block 256.
 // ---------------------------------------------------------------------------
 template <int A, int OUT>
 __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
     pdl_enter();
     constexpr int CPL = (OUT + 31) / 32;
+    constexpr int HP = CPL <= 2 ? 8 : 4;                  // hits per round
+    constexpr int kChunk = 2 * kNT;                       // list entries per staged round
+    __shared__ int2 sl[kChunk];
     const int p = blockIdx.x, tile = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int s = a.stage;
@@ -757,13 +756,14 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
     const int cx = (tile % a.g.tx[s]) * kTile + (local % kTile);
     const int cy = (tile / a.g.tx[s]) * kTile + (local / kTile);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    if (cx >= Wl || cy >= Hl || cy < a.g.row_lo[s] || cy >= a.g.row_hi[s]) return;
-    float* hp = a.parts[p].hidden[a.layer] + (static_cast<size_t>(cy) * Wl + cx) * OUT;
+    const bool active = cx < Wl && cy < Hl && cy >= a.g.row_lo[s] && cy < a.g.row_hi[s];
+    if (!__syncthreads_or(active)) return;                // CTA-uniform
+    float* hp = a.parts[p].hidden[a.layer] + (static_cast<size_t>(active ? cy : 0) * Wl + (active ? cx : 0)) * OUT;
     float h[CPL];
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
         const int o = lane + 32 * c;
-        h[c] = (o < OUT) ? hp[o] : 0.0f;
+        h[c] = (active && o < OUT) ? hp[o] : 0.0f;
     }
     const int ntiles = a.g.tx[s] * a.g.ty[s];
     const int n_p = a.range[p + 1] - a.range[p];
@@ -773,59 +773,75 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
         const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
         const int cnt = a.tl_cnt[slot];
         const int2* lst = a.tl + slot * a.g.seg;
-        for (int j0 = 0; j0 < cnt; j0 += 32) {
-            const int j = j0 + lane;
-            int2 ent = make_int2(0, 0);
-            if (j < cnt) ent = lst[j];
-            const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
-            const int dx = cx - ex, dy = cy - ey;
-            bool hit;
-            if (A == 1) hit = (j < cnt) && dx == 0 && dy == 0;
-            else hit = (j < cnt) && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1;
-            const int delta = (A == 1) ? 0 : (1 - dy) * 3 + (1 - dx);    // ssla_kernels.cpp:375
-            int outf = 1;
-            if (a.second) {
-                if (s == 0) outf = (hit && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
-                else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
+        int2 pre0 = make_int2(0, 0), pre1 = make_int2(0, 0);
+        if (static_cast<int>(threadIdx.x) < cnt) pre0 = lst[threadIdx.x];
+        if (static_cast<int>(threadIdx.x) + kNT < cnt) pre1 = lst[threadIdx.x + kNT];
+        for (int c0 = 0; c0 < cnt; c0 += kChunk) {
+            __syncthreads();                              // the previous round is consumed
+            sl[threadIdx.x] = pre0;
+            sl[threadIdx.x + kNT] = pre1;
+            __syncthreads();
+            {                                             // next round's loads, in flight during the walk
+                const int i0 = c0 + kChunk + static_cast<int>(threadIdx.x);
+                pre0 = (i0 < cnt) ? lst[i0] : make_int2(0, 0);
+                pre1 = (i0 + kNT < cnt) ? lst[i0 + kNT] : make_int2(0, 0);
             }
-            const int pk = ent.x * A + delta;                     // (entry, delta) row
-            const int pkf = (pk << 1) | outf;
-            unsigned m = __ballot_sync(0xffffffffu, hit);
-            while (m) {
-                int row[4], of[4];
-                int nh = 0;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int src = m ? (__ffs(m) - 1) : 0;
-                    const int v = __shfl_sync(0xffffffffu, pkf, src);
-                    row[q] = v >> 1;
-                    of[q] = (m != 0u) ? (v & 1) : 0;
-                    nh += (m != 0u) ? 1 : 0;
-                    m &= (m - 1u);
+            if (!active) continue;
+            const int nch = min(kChunk, cnt - c0);
+            for (int j0 = 0; j0 < nch; j0 += 32) {
+                const int j = j0 + lane;
+                int2 ent = make_int2(0, 0);
+                if (j < nch) ent = sl[j];
+                const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
+                const int dx = cx - ex, dy = cy - ey;
+                bool hit;
+                if (A == 1) hit = (j < nch) && dx == 0 && dy == 0;
+                else hit = (j < nch) && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1;
+                const int delta = (A == 1) ? 0 : (1 - dy) * 3 + (1 - dx);    // ssla_kernels.cpp:375
+                int outf = 1;
+                if (a.second) {
+                    if (s == 0) outf = (hit && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
+                    else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
                 }
-                float qv[4][CPL], vv[4][CPL], av[4][CPL];
+                const int pk = ent.x * A + delta;                     // (entry, delta) row
+                const int pkf = (pk << 1) | outf;
+                unsigned m = __ballot_sync(0xffffffffu, hit);
+                while (m) {
+                    int row[HP], of[HP];
+                    int nh = 0;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
-#pragma unroll
-                    for (int c = 0; c < CPL; ++c) {
-                        const int o = lane + 32 * c;
-                        const bool ok = (q < nh) && (o < OUT);
-                        qv[q][c] = (ok && of[q]) ? r[o] : 0.0f;
-                        vv[q][c] = ok ? r[OUT + o] : 0.0f;
-                        av[q][c] = ok ? r[2 * OUT + o] : 0.0f;
+                    for (int q = 0; q < HP; ++q) {
+                        const int src = m ? (__ffs(m) - 1) : 0;
+                        const int v = __shfl_sync(0xffffffffu, pkf, src);
+                        row[q] = v >> 1;
+                        of[q] = (m != 0u) ? (v & 1) : 0;
+                        nh += (m != 0u) ? 1 : 0;
+                        m &= (m - 1u);
                     }
-                }
+                    float qv[HP][CPL], vv[HP][CPL], av[HP][CPL];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    if (q < nh) {
-                        float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
+                    for (int q = 0; q < HP; ++q) {
+                        const float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
 #pragma unroll
                         for (int c = 0; c < CPL; ++c) {
                             const int o = lane + 32 * c;
-                            if (o < OUT) {
-                                h[c] = fmaf(av[q][c], h[c], vv[q][c]);
-                                if (of[q]) r[o] = qv[q][c] * h[c];
+                            const bool ok = (q < nh) && (o < OUT);
+                            qv[q][c] = (ok && of[q]) ? r[o] : 0.0f;
+                            vv[q][c] = ok ? r[OUT + o] : 0.0f;
+                            av[q][c] = ok ? r[2 * OUT + o] : 0.0f;
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < HP; ++q) {
+                        if (q < nh) {
+                            float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
+#pragma unroll
+                            for (int c = 0; c < CPL; ++c) {
+                                const int o = lane + 32 * c;
+                                if (o < OUT) {
+                                    h[c] = fmaf(av[q][c], h[c], vv[q][c]);
+                                    if (of[q]) r[o] = qv[q][c] * h[c];
+                                }
                             }
                         }
                     }
@@ -833,10 +849,12 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
             }
         }
     }
+    if (active) {
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-        const int o = lane + 32 * c;
-        if (o < OUT) hp[o] = h[c];
+        for (int c = 0; c < CPL; ++c) {
+            const int o = lane + 32 * c;
+            if (o < OUT) hp[o] = h[c];
+        }
     }
 }
 
@@ -1882,23 +1900,6 @@ int grid_for(size_t n, int per_block, int cap = 148 * 16) {
 }
 }  // namespace
 
-// Launches a drain kernel with programmatic stream serialization: it may be
-// scheduled while the previous kernel of the stream drains, and waits for
-// it in pdl_enter / pdl_wait.  Errors surface through cudaGetLastError.
-template <typename... P, typename... A>
-void pdl_launch(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, kern, static_cast<P>(args)...);
-}
 
 void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
                  uint32_t* ev_xy, uint8_t* rflags) {

@@ -158,6 +158,8 @@ struct HeadArgs {
     DevHead head;
     float* head_dec;         // [cap4][5+ncls]
     float* head_raw;
+    const float* tc_w1;      // tensor-core head: [cls_conv | reg_conv] rows [192][96], TF32 hi terms then lo terms
+    unsigned* err;           // tensor-core head: bit 0 when a wait for its MMAs ran out (host-mapped, or null)
 };
 
 enum { COLS_ALL = 0, COLS_VG = 1, COLS_Q = 2, COLS_RES = 3 };
@@ -293,6 +295,34 @@ void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
                          uint32_t* ev_xy, uint8_t* rflags, float* feat);
 void launch_filter(cudaStream_t st, const FilterArgs& a);
+// Programmatic dependent launch: a drain kernel is launched while the
+// previous one in the stream completes and waits here for it to complete
+// (and its memory to be visible) before touching anything it may write.
+// No kernel triggers its dependants early: CTAs of the next kernel waiting
+// on the SMs slowed the running one (measured), so the dependant is
+// released at completion and only the launch latency overlaps.  Without
+// the launch attribute the wait is a no-op.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() { pdl_wait(); }
+
+// Launches a drain kernel with programmatic stream serialization: it may be
+// scheduled while the previous kernel of the stream drains, and waits for
+// it in pdl_enter / pdl_wait.  Errors surface through cudaGetLastError.
+template <typename... P, typename... A>
+void pdl_launch(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<P>(args)...);
+}
+
 cudaError_t launch_live(cudaStream_t st, const LiveArgs& a);
 int live_max_ncls();
 cudaError_t launch_step(cudaStream_t st, const StepArgs& a);
@@ -307,6 +337,8 @@ void launch_contrib(cudaStream_t st, int layer, const ContribArgs& a, long long 
 void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows);
 void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a);
 void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows);
+// The head's convolutions on tcgen05 tensor cores (split TF32, ssla_head_tc.cu).
+void launch_head_tc(cudaStream_t st, const HeadArgs& a, long long max_rows);
 // GEMM for next layer `layer` (its IN = K, OUT2, A2) with the given columns.
 void launch_gemm(cudaStream_t st, int layer, const GemmArgs& a, long long max_rows);
 int gemm_cols(int layer, int colmode);

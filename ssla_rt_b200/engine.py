@@ -57,6 +57,8 @@ def load_library() -> C.CDLL:
         "ssla_engine_live_join": (i, [vp, C.POINTER(C.c_uint)]),
         "ssla_engine_live_withhold_completion": (i, [vp, C.c_longlong]),
         "ssla_engine_fill_s2s3_config": (i, [vp, C.POINTER(abi.HybridS2S3Config), i]),
+        "ssla_engine_set_head_mode": (i, [vp, i]),
+        "ssla_engine_head_status": (i, [vp, C.POINTER(C.c_uint)]),
         "ssla_engine_live_latency": (i, [vp, i, vp, i, vp, vp, vp]),
         "ssla_engine_set_owned": (i, [vp, i, i, i, i, i, vp]),
         "ssla_engine_strip_init": (i, [vp, i, i, i, i, i, i]),
@@ -259,6 +261,17 @@ class SslaEngine:
         self._live_ring = None
         if check or rc != abi.SSLA_ERR_CUDA:
             _check(rc)
+        return st.value
+
+    def set_head_mode(self, mode: int) -> None:
+        """abi.HEAD_EXACT (CUDA cores, bit-exact) or abi.HEAD_TENSOR (the
+        head's convolutions on tcgen05 tensor cores, split TF32)."""
+        _check(self.lib.ssla_engine_set_head_mode(self.h, mode))
+
+    def head_status(self) -> int:
+        """Status bits of the tensor-core head since the last call (0: fine)."""
+        st = C.c_uint(0)
+        _check(self.lib.ssla_engine_head_status(self.h, C.byref(st)))
         return st.value
 
     def fill_s2s3_config(self, cfg: "abi.HybridS2S3Config", block: int) -> None:

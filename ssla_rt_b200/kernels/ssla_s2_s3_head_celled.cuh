@@ -24,14 +24,17 @@
 // consumed (layer 5 without gate 2, layer 7 without gate 3), as the
 // reference does (:1684-1713).
 //
-// Work split inside a block (9 warps): warp w owns the grid cells with
-// (cy % 3) * 3 + (cx % 3) == w, so the 9 cells of one record's 3x3 patch
-// belong to 9 different warps and every cell has exactly one writer; each
-// warp walks the batch's records in ring order and applies, for each patch
-// cell it owns, the fused q/v/g matvec, the LRU update of the cell's hidden
-// state and the goW contribution of that patch position -- no atomics on
-// state.  One warp per record then sums the contributions in the
-// reference's patch order (8..0), adds the residual and applies LayerNorm.
+// Work split inside a block (9 warps), per layer:
+//   * warp d computes patch position d's fused q/v/g matvec for every record
+//     of the batch, so each weight is read from memory once per batch, not
+//     once per record (the weights, 2.96 MB, stream from L2);
+//   * warp w owns the grid cells with (cy % 3) * 3 + (cx % 3) == w -- the 9
+//     cells of one record's 3x3 patch belong to 9 different warps, every
+//     cell has exactly one writer -- and applies their LRU updates in ring
+//     order: no atomics on state;
+//   * warp d forms position d's goW contributions, again one weight read per
+//     batch; warp e sums record e's contributions in the reference's patch
+//     order (8..0), adds the residual and applies LayerNorm.
 //
 // Arithmetic is the CPU oracle's (proto_layer_pair.cuh), so the outputs are
 // bit-identical to it, not merely within the reference's max|d| s3_feat
@@ -46,8 +49,9 @@
 //     ssla_consumer_idle_ns (a module global, 30 s unless the host sets it
 //     through cuModuleGetGlobal) without a new record, ORing bit 1 into the
 //     module global ssla_consumer_status; every wait is bounded;
-//   * a launch whose block is not 288 threads does nothing but OR bit 2
-//     into ssla_consumer_status.
+//   * a launch whose block is not 288 threads, or whose dynamic shared
+//     memory is below 82,944 bytes (the batch's q|v|g rows), does nothing
+//     but OR bit 2 into ssla_consumer_status.
 #pragma once
 #include "proto_layer_pair.cuh"
 
@@ -137,7 +141,7 @@ static_assert(sizeof(HybridS2S3Config) == 4616, "HybridS2S3Config layout");
 
 // Idle bound of the persistent kernels and their status word (bit 1: a
 // block left after the idle bound; bit 2: a launch with a block size other
-// than 288 did nothing).
+// than 288 or too little dynamic shared memory did nothing).
 __device__ unsigned long long ssla_consumer_idle_ns = 30ull * 1000ull * 1000ull * 1000ull;
 __device__ unsigned int ssla_consumer_status = 0u;
 
@@ -148,12 +152,11 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kBatch = 8;              // records per batch
 constexpr int C1 = 24, C2 = 48, C3 = 96;
 constexpr int kHeadOut = 7;            // [reg 4, obj, cls 2]
-constexpr int kL4Qvg = 9 * C1 * 3 * C2;   // floats of layer 4's qvg block
 
 struct BatchShared {
     float x[kBatch][C3];               // current layer input of each record
     float con[kBatch][9][C3];          // goW contributions by patch position
-    float qh[kWarps][C3];              // per warp: q * h of its current cell; head activations
+    float act[kWarps][C3];             // per warp: head activations
     float hy[kBatch][8];               // head outputs of each record
     int x2[kBatch], y2[kBatch];        // stage-2 coordinates
     int owner[kBatch];
@@ -185,47 +188,118 @@ __device__ __forceinline__ unsigned dyn_smem_bytes() {
 
 // ---- one layer over the batch -------------------------------------------------------
 // enter: records whose patch cells this layer updates; used: records whose
-// output is consumed (q, goW, gather and LayerNorm); (cx, cy) of record e
-// is its cell on this layer's Hl x Wl grid.  wq: the layer's qvg block
-// (shared-memory copy or global).
+// output is consumed (q, goW, gather and LayerNorm); (cx, cy) >> shift of
+// record e is its cell on this layer's Hl x Wl grid.  stg: the batch's
+// [record][position][q | v | g] rows (dynamic shared memory).
+//   A) warp d, patch position d: the fused q/v/g matvec of every record
+//      whose cell at d is in bounds -- each weight is read once per batch and
+//      applied to all of the batch's records (one fmaf chain over the input
+//      channels per record and column, in input order);
+//   B) warp w, the cells it owns: the LRU updates in ring order (h = a*h + v,
+//      a = sigmoid(g)); q * h replaces q in the staging row;
+//   C) warp d: the goW contributions of position d for the records whose
+//      output is used, again one weight read per batch;
+//   D) warp e: gather in the reference's patch order (8..0), residual,
+//      LayerNorm, into x[e].
 template <int IN, int OUT, bool IP>
-__device__ void run_layer(BatchShared& sh, const LayerWeightsS2S3& L, const float* __restrict__ wq, float* hidden,
-                          int Hl, int Wl, int nb, const int* cxs, const int* cys, unsigned enter, unsigned used,
-                          int shift) {
+__device__ void run_layer(BatchShared& sh, float* stg, const LayerWeightsS2S3& L, const float* __restrict__ wq,
+                          float* hidden, int Hl, int Wl, int nb, const int* cxs, const int* cys, unsigned enter,
+                          unsigned used, int shift) {
     constexpr int J3 = 3 * OUT;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // ---- the patch cells this warp owns, record by record in ring order ----
-    for (int e = 0; e < nb; ++e) {
-        if (!((enter >> e) & 1u)) continue;
-        const bool use = (used >> e) & 1u;
-        const int ex = cxs[e] >> shift, ey = cys[e] >> shift;
-        for (int d = 0; d < 9; ++d) {
-            const int cx = ex + 1 - d % 3, cy = ey + 1 - d / 3;
-            if (cx < 0 || cx >= Wl || cy < 0 || cy >= Hl || (cy % 3) * 3 + (cx % 3) != w) continue;
-            float* h = hidden + (static_cast<long long>(cy) * Wl + cx) * OUT;
+    auto cell_of = [&](int e, int d, int& cx, int& cy) {
+        cx = (cxs[e] >> shift) + 1 - d % 3;
+        cy = (cys[e] >> shift) + 1 - d / 3;
+        return cx >= 0 && cx < Wl && cy >= 0 && cy < Hl;
+    };
+    // ---- A: q | v | g rows of position d = w ----
+    {
+        const int d = w;
+        unsigned m = 0;
+        for (int e = 0; e < nb; ++e) {
+            int cx, cy;
+            if (((enter >> e) & 1u) && cell_of(e, d, cx, cy)) m |= 1u << e;
+        }
+        const unsigned mq = m & used;
+        if (m) {
             const float* W = wq + static_cast<long long>(d) * IN * J3;
             for (int c = lane; c < OUT; c += 32) {
-                float q = 0.0f;
-                if (use) q = dot_col<IN>(W + c, J3, sh.x[e], 0.0f);
-                const float v = dot_col<IN>(W + OUT + c, J3, sh.x[e], 0.0f);
-                const float g = dot_col<IN>(W + 2 * OUT + c, J3, sh.x[e], 0.0f);
-                const float hn = __fmaf_rn(sigmoid_exact(g), h[c], v);   // rnn.h:80-91 lru_step
-                h[c] = hn;
-                if (use) sh.qh[w][c] = __fmul_rn(q, hn);
-            }
-            if (use) {
-                __syncwarp();
-                const float* G = L.goW + static_cast<long long>(d) * OUT * OUT;
-                for (int c = lane; c < OUT; c += 32) sh.con[e][d][c] = dot_col<OUT>(G + c, OUT, sh.qh[w], 0.0f);
-                __syncwarp();
+                float aq[kBatch], av[kBatch], ag[kBatch];
+#pragma unroll
+                for (int e = 0; e < kBatch; ++e) aq[e] = av[e] = ag[e] = 0.0f;
+#pragma unroll 2
+                for (int i = 0; i < IN; ++i) {
+                    const float* row = W + i * J3;
+                    const float wqi = row[c], wvi = row[OUT + c], wgi = row[2 * OUT + c];
+#pragma unroll
+                    for (int e = 0; e < kBatch; ++e) {
+                        if (!((m >> e) & 1u)) continue;
+                        const float xi = sh.x[e][i];
+                        if ((mq >> e) & 1u) aq[e] = __fmaf_rn(wqi, xi, aq[e]);
+                        av[e] = __fmaf_rn(wvi, xi, av[e]);
+                        ag[e] = __fmaf_rn(wgi, xi, ag[e]);
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < kBatch; ++e) {
+                    if (!((m >> e) & 1u)) continue;
+                    float* r = stg + (e * 9 + d) * J3;
+                    r[c] = aq[e];
+                    r[OUT + c] = av[e];
+                    r[2 * OUT + c] = ag[e];
+                }
             }
         }
     }
     __syncthreads();
-    // ---- gather + residual + LayerNorm: warp e for record e ----
+    // ---- B: ordered cell updates by the cells' owner warps ----
+    for (int e = 0; e < nb; ++e) {
+        if (!((enter >> e) & 1u)) continue;
+        const bool use = (used >> e) & 1u;
+        for (int d = 0; d < 9; ++d) {
+            int cx, cy;
+            if (!cell_of(e, d, cx, cy) || (cy % 3) * 3 + (cx % 3) != w) continue;
+            float* h = hidden + (static_cast<long long>(cy) * Wl + cx) * OUT;
+            float* r = stg + (e * 9 + d) * J3;
+            for (int c = lane; c < OUT; c += 32) {
+                const float hn = __fmaf_rn(sigmoid_exact(r[2 * OUT + c]), h[c], r[OUT + c]);   // rnn.h:80-91
+                h[c] = hn;
+                if (use) r[c] = __fmul_rn(r[c], hn);
+            }
+        }
+    }
+    __syncthreads();
+    // ---- C: goW contributions of position d = w ----
+    {
+        const int d = w;
+        unsigned m = 0;
+        for (int e = 0; e < nb; ++e) {
+            int cx, cy;
+            if (((enter >> e) & 1u) && ((used >> e) & 1u) && cell_of(e, d, cx, cy)) m |= 1u << e;
+        }
+        if (m) {
+            const float* G = L.goW + static_cast<long long>(d) * OUT * OUT;
+            for (int c = lane; c < OUT; c += 32) {
+                float acc[kBatch];
+#pragma unroll
+                for (int e = 0; e < kBatch; ++e) acc[e] = 0.0f;
+#pragma unroll 2
+                for (int j = 0; j < OUT; ++j) {
+                    const float g = G[j * OUT + c];
+#pragma unroll
+                    for (int e = 0; e < kBatch; ++e)
+                        if ((m >> e) & 1u) acc[e] = __fmaf_rn(g, stg[(e * 9 + d) * J3 + j], acc[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < kBatch; ++e)
+                    if ((m >> e) & 1u) sh.con[e][d][c] = acc[e];
+            }
+        }
+    }
+    __syncthreads();
+    // ---- D: gather + residual + LayerNorm: warp e for record e ----
     if (w < nb && ((used >> w) & 1u)) {
         const int e = w;
-        const int ex = cxs[e] >> shift, ey = cys[e] >> shift;
         float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (lane < OUT / 4) {
             float r[4];
@@ -235,8 +309,8 @@ __device__ void run_layer(BatchShared& sh, const LayerWeightsS2S3& L, const floa
                 r[j] = IP ? dot_col<IN>(L.input_proj + o, OUT, sh.x[e], 0.0f) : sh.x[e][o];
             }
             for (int d = 8; d >= 0; --d) {              // the reference's patch order
-                const int cx = ex + 1 - d % 3, cy = ey + 1 - d / 3;
-                if (cx < 0 || cx >= Wl || cy < 0 || cy >= Hl) continue;
+                int cx, cy;
+                if (!cell_of(e, d, cx, cy)) continue;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) y[j] = __fadd_rn(y[j], sh.con[e][d][4 * lane + j]);
             }
@@ -259,7 +333,7 @@ __device__ void run_layer(BatchShared& sh, const LayerWeightsS2S3& L, const floa
 __device__ void head_record(BatchShared& sh, const HybridS2S3Config& cfg, int e) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* x = sh.x[e];
-    float* act = sh.qh[w];
+    float* act = sh.act[w];
     if (cfg.head_cls_conv_W != nullptr) {
         for (int branch = 0; branch < 2; ++branch) {
             const float* Wc = branch == 0 ? cfg.head_cls_conv_W : cfg.head_reg_conv_W;
@@ -287,7 +361,7 @@ __device__ void head_record(BatchShared& sh, const HybridS2S3Config& cfg, int e)
 // volatile_ring: the ring lives in host-visible memory a producer writes
 // while the kernel runs (loads bypass the caches).
 __device__ void run_batch(BatchShared& sh, const HybridS2S3Config& cfg, int blk, const HybridInputRec* ring,
-                          unsigned long long base, unsigned long long mask, int nb, const float* wq4,
+                          unsigned long long base, unsigned long long mask, int nb, float* stg,
                           bool volatile_ring, bool head, HybridS2S3OutputSlot* out) {
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const HybridStrip& st = cfg.strip[blk];
@@ -332,10 +406,10 @@ __device__ void run_batch(BatchShared& sh, const HybridS2S3Config& cfg, int blk,
     __syncthreads();
     const unsigned in = sh.in_mask, p2 = sh.p2;
     // ---- stage 2: layer 4 for every record, layer 5 state-only without gate 2 ----
-    run_layer<C1, C2, true>(sh, cfg.layers[blk][0], wq4, cfg.hidden[blk][0], cfg.H2, cfg.W2, nb, sh.x2, sh.y2, in,
-                            in, 0);
-    run_layer<C2, C2, false>(sh, cfg.layers[blk][1], cfg.layers[blk][1].qvgIn, cfg.hidden[blk][1], cfg.H2, cfg.W2,
-                             nb, sh.x2, sh.y2, in, p2, 0);
+    run_layer<C1, C2, true>(sh, stg, cfg.layers[blk][0], cfg.layers[blk][0].qvgIn, cfg.hidden[blk][0], cfg.H2,
+                            cfg.W2, nb, sh.x2, sh.y2, in, in, 0);
+    run_layer<C2, C2, false>(sh, stg, cfg.layers[blk][1], cfg.layers[blk][1].qvgIn, cfg.hidden[blk][1], cfg.H2,
+                             cfg.W2, nb, sh.x2, sh.y2, in, p2, 0);
     // (x[e] is overwritten only by layers whose output record e consumes,
     // so a record without gate 2 keeps layer 4's output there)
     // ---- gate s3 for records that passed gate 2, on the pooled cell ----
@@ -349,9 +423,9 @@ __device__ void run_batch(BatchShared& sh, const HybridS2S3Config& cfg, int blk,
     const unsigned p3 = sh.p3;
     // ---- stage 3: layer 6 for records past gate 2, layer 7 state-only without gate 3 ----
     if (p2) {
-        run_layer<C2, C3, true>(sh, cfg.layers[blk][2], cfg.layers[blk][2].qvgIn, cfg.hidden[blk][2], cfg.H3,
+        run_layer<C2, C3, true>(sh, stg, cfg.layers[blk][2], cfg.layers[blk][2].qvgIn, cfg.hidden[blk][2], cfg.H3,
                                 cfg.W3, nb, sh.x2, sh.y2, p2, p2, 1);
-        run_layer<C3, C3, false>(sh, cfg.layers[blk][3], cfg.layers[blk][3].qvgIn, cfg.hidden[blk][3], cfg.H3,
+        run_layer<C3, C3, false>(sh, stg, cfg.layers[blk][3], cfg.layers[blk][3].qvgIn, cfg.hidden[blk][3], cfg.H3,
                                  cfg.W3, nb, sh.x2, sh.y2, p2, p3, 1);
     }
     // ---- output slots (drain_n contract): codes, and the record's last layer output ----
@@ -402,18 +476,12 @@ __device__ void run_batch(BatchShared& sh, const HybridS2S3Config& cfg, int blk,
 }
 
 // ---- kernel bodies ------------------------------------------------------------------------
-// Layer 4's qvg block in dynamic shared memory when the launch provides
-// room for it (the reference's launch does), else read from global memory.
-__device__ const float* stage_l4(const HybridS2S3Config& cfg, int blk, float* dyn) {
-    if (dyn_smem_bytes() < static_cast<unsigned>(sizeof(float) * kL4Qvg)) return cfg.layers[blk][0].qvgIn;
-    const float* src = cfg.layers[blk][0].qvgIn;
-    for (int i = threadIdx.x; i < kL4Qvg; i += kThreads) dyn[i] = src[i];
-    __syncthreads();
-    return dyn;
-}
+constexpr unsigned kStageBytes = sizeof(float) * kBatch * 9 * 3 * C3;   // q|v|g rows of a batch
 
+// The launch shape every kernel needs: 288 threads, and dynamic shared
+// memory for the batch's q|v|g rows (the reference's launch passes more).
 __device__ bool launch_ok() {
-    if (blockDim.x == kThreads && blockDim.y == 1 && blockDim.z == 1) return true;
+    if (blockDim.x == kThreads && blockDim.y == 1 && blockDim.z == 1 && dyn_smem_bytes() >= kStageBytes) return true;
     if (threadIdx.x == 0) atomicOr(&ssla_consumer_status, 2u);
     return false;
 }
@@ -423,13 +491,12 @@ __device__ void drain_body(const HybridS2S3Config& cfg, int blk, const HybridInp
     __shared__ BatchShared sh;
     if (threadIdx.x == 0 && cfg.kernel_start_clk[blk] != nullptr) *cfg.kernel_start_clk[blk] = clock64();
     if (n <= 0) return;
-    const float* wq4 = stage_l4(cfg, blk, dyn);
     int bi = 0;
     for (int b0 = 0; b0 < n; b0 += kBatch, ++bi) {
         const int nb = n - b0 < kBatch ? n - b0 : kBatch;
         unsigned long long t0 = 0;
         if (threadIdx.x == 0 && batch_clk != nullptr) t0 = clock64();
-        run_batch(sh, cfg, blk, ring, static_cast<unsigned long long>(b0), ~0ull, nb, wq4, false, false, out);
+        run_batch(sh, cfg, blk, ring, static_cast<unsigned long long>(b0), ~0ull, nb, dyn, false, false, out);
         if (threadIdx.x == 0 && batch_clk != nullptr) {
             batch_clk[2 * bi] = t0;
             batch_clk[2 * bi + 1] = clock64();
@@ -446,7 +513,6 @@ __device__ void persistent_body(const HybridS2S3Config& cfg, int blk, const Hybr
         *cfg.kernel_start_clk[blk] = clock64();
         __threadfence_system();
     }
-    const float* wq4 = stage_l4(cfg, blk, dyn);
     unsigned long long t_local = *reinterpret_cast<volatile unsigned long long*>(tail);
     unsigned long long idle_since = gtime();
     const unsigned long long idle_ns = *reinterpret_cast<volatile unsigned long long*>(&ssla_consumer_idle_ns);
@@ -484,7 +550,7 @@ __device__ void persistent_body(const HybridS2S3Config& cfg, int blk, const Hybr
             return;
         }
         if (nb == 0) continue;
-        run_batch(sh, cfg, blk, ring, t_local, mask, nb, wq4, true, true, nullptr);
+        run_batch(sh, cfg, blk, ring, t_local, mask, nb, dyn, true, true, nullptr);
         if (tid == 0) {
             if (cfg.timing[blk] != nullptr) {
                 const unsigned long long t_done = clock64();
