@@ -450,6 +450,14 @@ int  ssla_engine_phase_times(SslaEngine* eng, SslaPhaseTime* out, int max_n, int
  * loop over every SM (the denominator of the engine's roofline). */
 int  ssla_measure_fp32_peak(int device, double* tflops_out);
 
+/* Self-test of the device reciprocal inside every sigmoid (hardware
+ * approximation + one Newton-Raphson step): compares it on `device` with
+ * IEEE round-to-nearest 1/y for every float y in [1, 2^126), the range of
+ * the sigmoid's denominator.  *mismatches = 0 means the device sigmoid and
+ * ssla_sigmoidf_host (which divides) agree bit for bit; *first_bad (may be
+ * null) receives the lowest mismatching bit pattern, 0xFFFFFFFF if none. */
+int  ssla_selftest_reciprocal(int device, unsigned long long* mismatches, unsigned* first_bad);
+
 /* Portable exp used by every sigmoid / SiLU / box decode of the engine
  * (the device code's exact twin), for tests on hosts without a GPU. */
 float ssla_expf_host(float x);

@@ -61,16 +61,17 @@ float or_expf(float x) {
 /* activation.h:17  sigmoid(x) = 1 / (1 + exp(-x)) */
 /* Sigmoid, vendor/openeva/prim/activation.h:17: 1 / (1 + exp(-x)) with an
  * exp of its own for the range the sigmoid needs.  t = -x is clamped to
- * [-17, 88] (for x >= 17 the result is exactly 1, as 1 + exp(-17) rounds to
- * 1; for x <= -88 it is 1 / (1 + e^88) < 6.1e-39); n and r as in or_expf
+ * [-17, 87] (for x >= 17 the result is exactly 1, as 1 + exp(-17) rounds to
+ * 1; for x <= -87 it is 1 / (1 + e^87) ~ 1.6e-38, the smallest normal
+ * result); n and r as in or_expf
  * (with the product-sum for n fused); exp(r) by a degree-6 minimax
  * polynomial on [-ln2/2, ln2/2] (Remez exchange, coefficients rounded to
  * float, 0.87 ulp on the interval) by Horner with fmaf; one exact scaling by
- * 2^n, n in [-25, 127].  Within 2.3 ulp of the exact sigmoid, as
- * 1 / (1 + or_expf(-x)) is. */
+ * 2^n, n in [-25, 126]; IEEE division.  Within 2.3 ulp of the exact
+ * sigmoid for x >= -87, as 1 / (1 + or_expf(-x)) is. */
 float or_sigmoidf(float x) {
     if (x != x) return x;
-    const float t = fminf(fmaxf(-x, -17.0f), 88.0f);
+    const float t = fminf(fmaxf(-x, -17.0f), 87.0f);
     union { float f; int32_t i; } big;
     big.f = fmaf(t, 1.44269502f, 12582912.0f);
     const float n = big.f - 12582912.0f;

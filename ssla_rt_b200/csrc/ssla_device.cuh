@@ -139,21 +139,36 @@ __host__ __device__ __forceinline__ float ssla_expf(float x) {
     return (p * ssla_pow2i(n1)) * ssla_pow2i(n2);
 }
 
+// 1 / y rounded to nearest for y in [1, 2^126): the hardware approximation
+// (rcp.approx, within an ulp) refined by one Newton-Raphson step with fused
+// multiply-adds, e = 1 - y q exactly, q' = q + q e (P. Markstein, "Computation
+// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990).  Equal to IEEE round-to-nearest division for every
+// float in that range (checked exhaustively, ssla_selftest_reciprocal), with
+// no branch, so the sigmoids of a thread interleave.
+__device__ __forceinline__ float ssla_rcp_rn(float y) {
+    float q;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(q) : "f"(y));
+    return fmaf(q, fmaf(-y, q, 1.0f), q);
+}
+
 // vendor/openeva/prim/activation.h:17, 1 / (1 + exp(-x)), with an exp of
-// its own for the range the sigmoid needs: t = -x clamped to [-17, 88]
+// its own for the range the sigmoid needs: t = -x clamped to [-17, 87]
 // (for x >= 17 the result is exactly 1, as 1 + exp(-17) rounds to 1; for
-// x <= -88 it is 1 / (1 + e^88) < 6.1e-39 instead of a smaller value).
+// x <= -87 it is 1 / (1 + e^87) ~ 1.6e-38, the smallest normal result,
+// instead of a smaller value).
 // n = nearest integer to t * log2(e) (1.5 * 2^23 trick), r = t - n ln 2 by
 // Cody-Waite with ln 2 split into a 12-bit head and a float tail, exp(r)
 // by a degree-6 minimax polynomial on [-ln2/2, ln2/2] (Remez exchange,
 // coefficients rounded to float, 0.87 ulp), Horner with fused
-// multiply-adds, then one exact scaling by 2^n (n in [-25, 127]).  IEEE
-// basic operations only, identical on host and device; the reciprocal is
-// IEEE round-to-nearest (__frcp_rn on the device, exactly 1.0f / y).
-// Within 2.3 ulp of the exact sigmoid, as the general exp route was.
+// multiply-adds, then one exact scaling by 2^n (n in [-25, 126]).  IEEE
+// basic operations only, identical on host and device; the reciprocal of
+// 1 + e^t (in [1, 2^126)) is rounded to nearest (ssla_rcp_rn on the device,
+// exactly 1.0f / y on the host).  Within 2.3 ulp of the exact sigmoid for
+// x >= -87, as the general exp route was.
 __host__ __device__ __forceinline__ float ssla_sigmoidf(float x) {
     if (x != x) return x;
-    const float t = fminf(fmaxf(-x, -17.0f), 88.0f);
+    const float t = fminf(fmaxf(-x, -17.0f), 87.0f);
     const float big = fmaf(t, 1.44269502f, 12582912.0f);
     const float n = big - 12582912.0f;
     float r = fmaf(-n, 0.693115234375f, t);
@@ -167,7 +182,7 @@ __host__ __device__ __forceinline__ float ssla_sigmoidf(float x) {
     p = fmaf(p, r, 1.0f);
 #ifdef __CUDA_ARCH__
     const int ni = __float_as_int(big) - 0x4B400000;
-    return __frcp_rn(1.0f + p * ssla_pow2i(ni));
+    return ssla_rcp_rn(1.0f + p * ssla_pow2i(ni));
 #else
     union { float f; int32_t i; } bb;
     bb.f = big;

@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <stdexcept>
 
 #include "ssla_abi_types.h"
 
@@ -2138,7 +2139,41 @@ __global__ void __launch_bounds__(512) k_ffma_peak(const float* __restrict__ ab,
     for (int k = 0; k < 8; ++k) s += r[k];
     if (s == 123456.789f) sink[threadIdx.x] = s;
 }
+// ssla_rcp_rn against the IEEE round-to-nearest reciprocal for the float bit
+// patterns [lo, hi): mismatches counted, the first (lowest seen) recorded.
+__global__ void __launch_bounds__(256) k_rcp_check(uint32_t lo, uint32_t hi, unsigned long long* bad,
+                                                   unsigned* first) {
+    unsigned long long n = 0;
+    for (uint64_t u = lo + static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < hi;
+         u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float y = __uint_as_float(static_cast<uint32_t>(u));
+        if (__float_as_uint(ssla_rcp_rn(y)) != __float_as_uint(__frcp_rn(y))) {
+            ++n;
+            atomicMin(first, static_cast<unsigned>(u));
+        }
+    }
+    if (n) atomicAdd(bad, n);
+}
 }  // namespace
+
+unsigned long long check_reciprocal(unsigned* first_bad) {
+    unsigned long long* d = nullptr;
+    if (cudaMalloc(&d, 16) != cudaSuccess) throw std::runtime_error("cudaMalloc failed");
+    unsigned long long init[2] = {0, 0xFFFFFFFFull};
+    cudaMemcpy(d, init, sizeof init, cudaMemcpyHostToDevice);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // every float in [1, 2^126): the reciprocals the sigmoid takes
+    k_rcp_check<<<sms * 8, 256>>>(0x3F800000u, 0x7E800000u, d, reinterpret_cast<unsigned*>(d + 1));
+    const cudaError_t err = cudaDeviceSynchronize();
+    unsigned long long out[2] = {0, 0};
+    cudaMemcpy(out, d, sizeof out, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (err != cudaSuccess) throw std::runtime_error(cudaGetErrorString(err));
+    if (first_bad) *first_bad = static_cast<unsigned>(out[1]);
+    return out[0];
+}
 
 double measure_ffma_peak() {
     int dev = 0, sms = 0;

@@ -353,5 +353,8 @@ void launch_fill_clk(cudaStream_t st, int P, const int* rec_off, const unsigned 
 void launch_stamp(cudaStream_t st, unsigned long long* dst);
 // Measured FP32 FMA throughput of the current device, TFLOP/s.
 double measure_ffma_peak();
+// Mismatches of ssla_rcp_rn against IEEE round-to-nearest over every float
+// in [1, 2^126) (the first one's bit pattern in *first_bad, 0xFFFFFFFF if none).
+unsigned long long check_reciprocal(unsigned* first_bad);
 
 }  // namespace ssla

@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
-from typing import Optional, Sequence
+from typing import Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -82,6 +82,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_set_profiling": (i, [vp, i]),
         "ssla_engine_phase_times": (i, [vp, vp, i, C.POINTER(C.c_int)]),
         "ssla_measure_fp32_peak": (i, [i, C.POINTER(C.c_double)]),
+        "ssla_selftest_reciprocal": (i, [i, C.POINTER(C.c_ulonglong), C.POINTER(C.c_uint)]),
         "ssla_expf_host": (f, [f]),
         "ssla_sigmoidf_host": (f, [f]),
         "ssla_last_error": (C.c_char_p, []),
@@ -414,6 +415,15 @@ def measure_fp32_peak(device: int = 0) -> float:
     v = C.c_double()
     _check(load_library().ssla_measure_fp32_peak(device, C.byref(v)))
     return v.value
+
+
+def selftest_reciprocal(device: int = 0) -> Tuple[int, int]:
+    """(mismatches, first mismatching bit pattern) of the device sigmoid's
+    reciprocal against IEEE round-to-nearest over every float in [1, 2^126)."""
+    n = C.c_ulonglong()
+    first = C.c_uint()
+    _check(load_library().ssla_selftest_reciprocal(device, C.byref(n), C.byref(first)))
+    return n.value, first.value
 
 
 def drain_n_multi(cfg: abi.HybridS2S3Config, rings: Sequence[int], ns: Sequence[int],

@@ -61,16 +61,25 @@ __device__ __forceinline__ float exp_portable(float x) {
     return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(n2));
 }
 
+// 1 / y rounded to nearest for y in [1, 2^126): rcp.approx refined by one
+// Newton-Raphson step with fused multiply-adds (P. Markstein, IBM J. Res.
+// Dev. 34(1), 1990), equal to IEEE division on that whole range.
+__device__ __forceinline__ float rcp_rn(float y) {
+    float q;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(q) : "f"(y));
+    return __fmaf_rn(q, __fmaf_rn(-y, q, 1.0f), q);
+}
+
 // vendor/openeva/prim/activation.h:17, 1 / (1 + exp(-x)), with an exp of
 // its own for the range the sigmoid needs -- the engine's and the oracle's
-// sigmoid, operation for operation: t = -x clamped to [-17, 88]; n and the
+// sigmoid, operation for operation: t = -x clamped to [-17, 87]; n and the
 // Cody-Waite reduction as in exp_portable (the product-sum for n fused);
 // exp(r) by a degree-6 minimax polynomial on [-ln2/2, ln2/2] (Remez
 // exchange, coefficients rounded to float) by Horner; one exact scaling by
-// 2^n; an IEEE round-to-nearest reciprocal.
+// 2^n; the round-to-nearest reciprocal above.
 __device__ __forceinline__ float sigmoid_exact(float x) {
     if (x != x) return x;
-    const float t = fminf(fmaxf(-x, -17.0f), 88.0f);
+    const float t = fminf(fmaxf(-x, -17.0f), 87.0f);
     const float big = __fmaf_rn(t, 1.44269502f, 12582912.0f);
     const float n = __fsub_rn(big, 12582912.0f);
     float r = __fmaf_rn(-n, 0.693115234375f, t);
@@ -82,7 +91,7 @@ __device__ __forceinline__ float sigmoid_exact(float x) {
     p = __fmaf_rn(p, r, 4.99999911e-01f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    return __frcp_rn(__fadd_rn(1.0f, __fmul_rn(p, pow2i(__float_as_int(big) - 0x4B400000))));
+    return rcp_rn(__fadd_rn(1.0f, __fmul_rn(p, pow2i(__float_as_int(big) - 0x4B400000))));
 }
 
 // fmaf chain of one output column over N inputs, in input order
