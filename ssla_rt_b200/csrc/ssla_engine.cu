@@ -1171,7 +1171,9 @@ struct Engine {
         ga.n_gates = (s_last >= 3) ? 4 : 2;
         launch_gates(st, ga);
         check_launch("k_gates");
-        prof.mark("gates", 1, st);
+        launch_flag_s0(st, fa);                    // layer-1 output flags into the stage-0 lists
+        check_launch("k_flag_s0");
+        prof.mark("gates", 2, st);
         // stage lists
         CompactArgs ca{};
         ca.g = g; ca.s_first = 0; ca.tiles_per_part = ws.tiles_per_part; ca.ev_off = ws.ev_off.as<int>();

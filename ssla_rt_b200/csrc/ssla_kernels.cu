@@ -239,6 +239,34 @@ __global__ void __launch_bounds__(kNT) k_filter_tiles(FilterArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// k_flag_s0: after the gates, sets bit 31 of every stage-0 tile-list entry
+// whose event reaches stage 1 (its layer-1 output is consumed), so the
+// layer-1 scan reads the flag with the entry instead of loading the event's
+// flag byte behind it.  k_filter leaves the bit clear at stage 0.  One warp
+// per (partition, tile, segment) slot, grid-stride.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kNT) k_flag_s0(FilterArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int ntiles = a.g.tx[0] * a.g.ty[0];
+    const long long per_p = static_cast<long long>(ntiles) * a.g.nseg[0];
+    const long long slots = per_p * a.g.P;
+    const long long wstride = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+    for (long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < slots; w += wstride) {
+        const int p = static_cast<int>(w / per_p);
+        const int seg = static_cast<int>(w % a.g.nseg[0]);
+        const int n_p = a.range[p + 1] - a.range[p];
+        if (seg >= (n_p + a.g.seg - 1) / a.g.seg) continue;        // segment not written this drain
+        const int cnt = a.tl_cnt[w];
+        int2* lst = a.tl + w * a.g.seg;
+        for (int j = lane; j < cnt; j += 32) {
+            const int2 e = lst[j];
+            if (a.rflags[e.x] & F_R1) lst[j].y = e.y | static_cast<int>(0x80000000u);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // k_gates: one 4-warp CTA per (partition, s3 block).
 //   Phase 1 (warp 0): walks the block's own events in stream order (the
 //     stage-0 tile list of the block, two windows in flight) and computes
@@ -930,8 +958,8 @@ struct ScanGroupShape {
     static constexpr int DS = IN * J2 + ((IN * J2) % 32 == 16 ? 4 : ((IN * J2) % 32 == 0 ? 4 : 0));
     static constexpr int QR = ((2 * OUT / 4) % 2 == 0) ? 2 * OUT + 4 : 2 * OUT;   // [a | v] row
     static constexpr int QCAP = 160;                    // < 32 pending + 32 events x 4 cells
-    static constexpr int R = (4 * OUT + 31) / 32;       // (cell, channel) pairs per lane
-    static constexpr size_t per_warp = sizeof(float) * 32 * QR + (sizeof(int) + 1) * QCAP;
+    static constexpr int G4 = OUT / 4;                  // 4-channel slices of a cell (update lanes per cell)
+    static constexpr size_t per_warp = sizeof(float) * 32 * QR + (sizeof(int) + 1) * QCAP + 32;
     static constexpr size_t smem = sizeof(float) * 9 * DS + WPC * per_warp;
     static_assert(IN % 4 == 0 && OUT % 4 == 0 && DS % 4 == 0, "shape");
 };
@@ -939,13 +967,14 @@ struct ScanGroupShape {
 template <int IN, int OUT, int WPC>
 __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanFusedArgs a) {
     using Sh = ScanGroupShape<IN, OUT, WPC>;
-    constexpr int J2 = Sh::J2, DS = Sh::DS, QR = Sh::QR, QCAP = Sh::QCAP, R = Sh::R;
+    constexpr int J2 = Sh::J2, DS = Sh::DS, QR = Sh::QR, QCAP = Sh::QCAP, G4 = Sh::G4;
     extern __shared__ __align__(16) float dsm[];
     float* Ws = dsm;                                              // [9][DS]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* Qs = Ws + 9 * DS + warp * (Sh::per_warp / sizeof(float));   // [32][QR]
     int* qk = reinterpret_cast<int*>(Qs + 32 * QR);                    // [QCAP] entry
     unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<6
+    unsigned char* perm = qm + QCAP;                                    // [32] batch lane -> slot
     // the weights are constant: staged before the wait
     for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
         const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
@@ -984,26 +1013,40 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
         }
         if (gx0 >= Wl || gy0 >= Hl || gy0 + (ncell > 1 ? 1 : 0) < a.g.row_lo[s] || gy0 >= a.g.row_hi[s]) continue;
         float* const hid = a.parts[p].hidden[a.layer];
-        float h[R];
-        int hoff[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int pair = r * 32 + lane;
-            const int c = pair / OUT, ch = pair % OUT;
-            const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
-            const bool ok = pair < ncell * OUT && cx < Wl && cy < Hl;
-            hoff[r] = ok ? (cy * Wl + cx) * OUT + ch : -1;
-            h[r] = ok ? hid[hoff[r]] : 0.0f;
-        }
+        // update role: lane = (cell cc of the group, 4-channel slice g)
+        const int cc = lane / G4, g4 = lane % G4;
+        const int ux = gx0 + (cc & 1), uy = gy0 + (cc >> 1);
+        const bool uown = lane < 4 * G4 && cc < ncell && ux < Wl && uy < Hl;
+        float* const hp = hid + (static_cast<size_t>(uown ? uy : 0) * Wl + (uown ? ux : 0)) * OUT + 4 * g4;
+        float4 h4 = uown ? *reinterpret_cast<const float4*>(hp) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int np = 0;                                   // queued slots (warp-uniform)
         // Runs B, C, D on the first nb (1..32) queued slots.
         auto batch = [&](int nb) {
+            // cell and output masks over the slots (bit = slot)
             const bool valid = lane < nb;
-            const int sl = valid ? lane : 0;
-            const int k = qk[sl];
-            const int m = qm[sl];
-            const int d = m & 15, cell = (m >> 4) & 3;
-            const bool out = valid && ((m >> 6) & 1);
+            const int m0 = qm[valid ? lane : 0];
+            unsigned cm[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) cm[c] = __ballot_sync(0xffffffffu, valid && ((m0 >> 4) & 3) == c);
+            const unsigned om = __ballot_sync(0xffffffffu, valid && ((m0 >> 6) & 1));
+            // B runs the slots sorted by delta (counting sort, one ballot per
+            // delta), so the lanes of a weight read mostly share one row
+            {
+                const int d0 = valid ? (m0 & 15) : 9;
+                const unsigned lt = lanemask_lt();
+                int pos = 0, before = 0;
+#pragma unroll
+                for (int dd = 0; dd <= 9; ++dd) {
+                    const unsigned mk = __ballot_sync(0xffffffffu, d0 == dd);
+                    if (d0 == dd) pos = before + __popc(mk & lt);
+                    before += __popc(mk);
+                }
+                perm[pos] = static_cast<unsigned char>(lane);
+                __syncwarp();
+            }
+            const int sl = perm[lane];
+            const int k = qk[valid ? sl : 0];
+            const int d = qm[valid ? sl : 0] & 15;
             float x[IN];
 #pragma unroll
             for (int i4 = 0; i4 < IN / 4; ++i4) {
@@ -1011,7 +1054,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                 x[4 * i4] = t.x; x[4 * i4 + 1] = t.y; x[4 * i4 + 2] = t.z; x[4 * i4 + 3] = t.w;
             }
             const float* wr = Ws + d * DS;
-            float* qr = Qs + lane * QR;
+            float* qr = Qs + sl * QR;
             float2 acc[OUT / 2];
             // B: a = sigmoid(g) -> [0, OUT), v -> [OUT, 2*OUT); paired
             // output channels per packed FMA (each component an fmaf)
@@ -1040,82 +1083,94 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                     *reinterpret_cast<float4*>(qr + col + 4 * j4) =
                         make_float4(acc[2 * j4].x, acc[2 * j4].y, acc[2 * j4 + 1].x, acc[2 * j4 + 1].y);
             }
-            unsigned cm[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) cm[c] = __ballot_sync(0xffffffffu, valid && cell == c);
-            const unsigned om = __ballot_sync(0xffffffffu, out);
             __syncwarp();
-            // C: ordered updates per (cell, channel)
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                if (hoff[r] < 0) continue;
-                const int pair = r * 32 + lane;
-                const int c = pair / OUT, ch = pair % OUT;
-                unsigned mk = (c == 0) ? cm[0] : (c == 1) ? cm[1] : (c == 2) ? cm[2] : cm[3];
-                float hc = h[r];
-                // four hits per round: their a, v loads are issued before the
-                // chain of fmafs, so one shared-memory latency covers four
+            // C: ordered updates, lane = (cell, 4 channels); four hits per
+            // round, their rows' loads issued ahead of the fmaf chain
+            {
+                unsigned mk = uown ? ((cc == 0) ? cm[0] : (cc == 1) ? cm[1] : (cc == 2) ? cm[2] : cm[3]) : 0u;
+                float2 hlo = make_float2(h4.x, h4.y), hhi = make_float2(h4.z, h4.w);
                 while (mk) {
                     int s4[4];
                     bool on[4];
-                    float av[4], vv[4];
+                    float4 av[4], vv[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         on[q] = mk != 0u;
                         s4[q] = on[q] ? __ffs(mk) - 1 : 0;
                         mk &= mk - 1u;
-                        const float* q2 = Qs + s4[q] * QR;
-                        av[q] = q2[ch];
-                        vv[q] = q2[OUT + ch];
+                        const float* q2 = Qs + s4[q] * QR + 4 * g4;
+                        av[q] = *reinterpret_cast<const float4*>(q2);
+                        vv[q] = *reinterpret_cast<const float4*>(q2 + OUT);
                     }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         if (!on[q]) break;
-                        hc = fmaf(av[q], hc, vv[q]);
+                        // h = a * h + v per channel (each component one fmaf)
+                        hlo = __ffma2_rn(make_float2(av[q].x, av[q].y), hlo, make_float2(vv[q].x, vv[q].y));
+                        hhi = __ffma2_rn(make_float2(av[q].z, av[q].w), hhi, make_float2(vv[q].z, vv[q].w));
                         if ((om >> s4[q]) & 1u)
-                            QH[(static_cast<size_t>(qk[s4[q]]) * 9 + (qm[s4[q]] & 15)) * OUT + ch] = hc;
+                            *reinterpret_cast<float4*>(QH + (static_cast<size_t>(qk[s4[q]]) * 9 + (qm[s4[q]] & 15)) * OUT +
+                                                       4 * g4) = make_float4(hlo.x, hlo.y, hhi.x, hhi.y);
                     }
                 }
-                h[r] = hc;
+                h4 = make_float4(hlo.x, hlo.y, hhi.x, hhi.y);
             }
             __syncwarp();
         };
+        // The tile list arrives as segments; their counts are read 32 at a
+        // time (lane i: segment wbase + i) and each 32-entry block's load is
+        // issued one block ahead of its walk.
         const int n_p = a.range[p + 1] - a.range[p];
         const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[s]);
-        for (int seg = 0; seg < nseg; ++seg) {
-            const size_t lslot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s] + seg;
-            const int cnt = a.tl_cnt[lslot];
-            const int2* lst = a.tl + lslot * a.g.seg;
-            for (int j0 = 0; j0 < cnt; j0 += 32) {
-                const int j = j0 + lane;
-                int2 ent = make_int2(0, 0);
-                if (j < cnt) ent = lst[j];
-                const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
-                unsigned cmask = 0;
-                if (j < cnt) {
+        const size_t slot0 = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[s];
+        int wbase = -32, wcnt = 0;
+        auto seg_cnt = [&](int sg) -> int {         // warp-uniform, non-decreasing sg
+            if (sg >= nseg) return 0;
+            if (sg >= wbase + 32) {
+                wbase = sg & ~31;
+                wcnt = (wbase + lane < nseg) ? a.tl_cnt[slot0 + wbase + lane] : 0;
+            }
+            return __shfl_sync(0xffffffffu, wcnt, sg - wbase);
+        };
+        auto load_block = [&](int sg, int j0, int cnt) -> int2 {
+            return (sg < nseg && j0 + lane < cnt) ? a.tl[(slot0 + sg) * a.g.seg + j0 + lane] : make_int2(0, 0);
+        };
+        int cs = 0, cj = 0, ccnt = seg_cnt(0);
+        while (cs < nseg && ccnt == 0) ccnt = seg_cnt(++cs);
+        int2 cur = load_block(cs, 0, ccnt);
+        while (cs < nseg) {
+            int ns = cs, nj = cj + 32, ncnt = ccnt;
+            if (nj >= ccnt) {
+                ns = cs + 1;
+                nj = 0;
+                ncnt = seg_cnt(ns);
+            }
+            const int2 nxt = load_block(ns, nj, ncnt);       // in flight during this block's walk
+            const int j = cj + lane;
+            const int2 ent = cur;
+            const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
+            unsigned cmask = 0;
+            if (j < ccnt) {
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
-                        const int dx = cx - ex, dy = cy - ey;
-                        if (c < ncell && cx < Wl && cy < Hl && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1)
-                            cmask |= 1u << c;
-                    }
+                for (int c = 0; c < 4; ++c) {
+                    const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
+                    const int dx = cx - ex, dy = cy - ey;
+                    if (c < ncell && cx < Wl && cy < Hl && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1)
+                        cmask |= 1u << c;
                 }
-                // output flag of a hit (the stage-0 flag byte is read for hits only)
-                int outf = 1;
-                if (a.second) {
-                    if (s == 0) outf = (cmask && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
-                    else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
-                }
-                // queue positions: exclusive prefix of the hit counts (0..4)
-                // from one ballot per bit
-                const int nc = __popc(cmask);
-                const unsigned v0 = __ballot_sync(0xffffffffu, nc & 1);
-                const unsigned v1 = __ballot_sync(0xffffffffu, nc & 2);
-                const unsigned v2 = __ballot_sync(0xffffffffu, nc & 4);
-                const unsigned lt = lanemask_lt();
-                const int tot = __popc(v0) + 2 * __popc(v1) + 4 * __popc(v2);
-                if (tot == 0) continue;
+            }
+            // output flag of a hit: bit 31 of the entry (set for stage-0 lists
+            // by k_flag_s0 after the gates, by k_filter for later stages)
+            const int outf = a.second ? static_cast<int>(static_cast<uint32_t>(ent.y) >> 31) : 1;
+            // queue positions: exclusive prefix of the hit counts (0..4)
+            // from one ballot per bit
+            const int nc = __popc(cmask);
+            const unsigned v0 = __ballot_sync(0xffffffffu, nc & 1);
+            const unsigned v1 = __ballot_sync(0xffffffffu, nc & 2);
+            const unsigned v2 = __ballot_sync(0xffffffffu, nc & 4);
+            const unsigned lt = lanemask_lt();
+            const int tot = __popc(v0) + 2 * __popc(v1) + 4 * __popc(v2);
+            if (tot != 0) {
                 int pos = np + __popc(v0 & lt) + 2 * __popc(v1 & lt) + 4 * __popc(v2 & lt);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -1142,11 +1197,18 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                     }
                 }
             }
+            cs = ns;
+            cj = nj;
+            ccnt = ncnt;
+            cur = nxt;
+            while (cs < nseg && cj >= ccnt) {               // empty segments
+                ccnt = seg_cnt(++cs);
+                cj = 0;
+                cur = load_block(cs, 0, ccnt);
+            }
         }
         if (np > 0) batch(np);
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-            if (hoff[r] >= 0) hid[hoff[r]] = h[r];
+        if (uown) *reinterpret_cast<float4*>(hp) = h4;
     }
 }
 
@@ -2037,6 +2099,12 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
         case 2: go(k_scan_group<12, 24, 16>, ScanGroupShape<12, 24, 16>{}); break;
         default: go(k_scan_group<24, 24, 16>, ScanGroupShape<24, 24, 16>{}); break;
     }
+}
+
+void launch_flag_s0(cudaStream_t st, const FilterArgs& a) {
+    const long long slots = static_cast<long long>(a.g.P) * a.g.tx[0] * a.g.ty[0] * a.g.nseg[0];
+    const long long blocks = std::max(1LL, std::min((slots + (kNT / 32) - 1) / (kNT / 32), 148LL * 16));
+    pdl_launch(k_flag_s0, dim3(static_cast<unsigned>(blocks)), dim3(kNT), 0, st, a);
 }
 
 void launch_hot_tiles(cudaStream_t st, const HotArgs& a) {

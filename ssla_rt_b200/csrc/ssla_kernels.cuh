@@ -295,6 +295,8 @@ void launch_prep(cudaStream_t st, const float4* ev, int n, int W0, int H0,
 void launch_prep_records(cudaStream_t st, const void* rec, int n, StageEntry* E2,
                          uint32_t* ev_xy, uint8_t* rflags, float* feat);
 void launch_filter(cudaStream_t st, const FilterArgs& a);
+// Marks the stage-0 tile-list entries whose event reaches stage 1 (after the gates).
+void launch_flag_s0(cudaStream_t st, const FilterArgs& a);
 // Programmatic dependent launch: a drain kernel is launched while the
 // previous one in the stream completes and waits here for it to complete
 // (and its memory to be visible) before touching anything it may write.
