@@ -772,16 +772,18 @@ __global__ void __launch_bounds__(kNT) k_compact_scatter(CompactArgs a) {
 // grid (P, tiles, 8), block 256.
 // ---------------------------------------------------------------------------
 template <int A, int OUT>
-__global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
+__global__ void __launch_bounds__(kNT, 2) k_scan(ScanArgs a) {
     pdl_enter();
     constexpr int CPL = (OUT + 31) / 32;
-    constexpr int HP = CPL <= 2 ? 8 : 4;                  // hits per round
+    constexpr int HP = 4;                                 // hits per batch (two batches in flight)
     constexpr int kChunk = 2 * kNT;                       // list entries per staged round
     __shared__ int2 sl[kChunk];
+    __shared__ int hq_all[kNT / 32][kChunk];              // per warp: its cell's hits of a round
     const int p = blockIdx.x, tile = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int s = a.stage;
     const int local = blockIdx.z * (kNT / 32) + warp;     // 0..63 in the tile
+    int* const hq = hq_all[warp];
     const int cx = (tile % a.g.tx[s]) * kTile + (local % kTile);
     const int cy = (tile / a.g.tx[s]) * kTile + (local / kTile);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
@@ -817,6 +819,8 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
             }
             if (!active) continue;
             const int nch = min(kChunk, cnt - c0);
+            // 1) the cell's hits of this round, in list order: (row << 1) | output flag
+            int nq = 0;
             for (int j0 = 0; j0 < nch; j0 += 32) {
                 const int j = j0 + lane;
                 int2 ent = make_int2(0, 0);
@@ -832,50 +836,59 @@ __global__ void __launch_bounds__(kNT) k_scan(ScanArgs a) {
                     if (s == 0) outf = (hit && (a.rflags[ent.x] & F_R1)) ? 1 : 0;
                     else outf = (static_cast<uint32_t>(ent.y) >> 31) & 1;
                 }
-                const int pk = ent.x * A + delta;                     // (entry, delta) row
-                const int pkf = (pk << 1) | outf;
-                unsigned m = __ballot_sync(0xffffffffu, hit);
-                while (m) {
-                    int row[HP], of[HP];
-                    int nh = 0;
+                const unsigned m = __ballot_sync(0xffffffffu, hit);
+                if (hit) hq[nq + __popc(m & lanemask_lt())] = ((ent.x * A + delta) << 1) | outf;
+                nq += __popc(m);
+            }
+            __syncwarp();
+            // 2) applied HP at a time; the next batch's rows load while this
+            //    batch's fmaf chain runs
+            float qv[2][HP][CPL], vv[2][HP][CPL], av[2][HP][CPL];
+            int row[2][HP], of[2][HP];
+            auto fetch = [&](int buf, int b0) {
 #pragma unroll
-                    for (int q = 0; q < HP; ++q) {
-                        const int src = m ? (__ffs(m) - 1) : 0;
-                        const int v = __shfl_sync(0xffffffffu, pkf, src);
-                        row[q] = v >> 1;
-                        of[q] = (m != 0u) ? (v & 1) : 0;
-                        nh += (m != 0u) ? 1 : 0;
-                        m &= (m - 1u);
+                for (int q = 0; q < HP; ++q) {
+                    const bool on = b0 + q < nq;
+                    const int v = on ? hq[b0 + q] : 0;
+                    row[buf][q] = v >> 1;
+                    of[buf][q] = on ? (v & 1) : 0;
+                    const float* r = S + static_cast<size_t>(row[buf][q]) * (3 * OUT);
+#pragma unroll
+                    for (int c = 0; c < CPL; ++c) {
+                        const int o = lane + 32 * c;
+                        const bool ok = on && (o < OUT);
+                        qv[buf][q][c] = (ok && of[buf][q]) ? r[o] : 0.0f;
+                        vv[buf][q][c] = ok ? r[OUT + o] : 0.0f;
+                        av[buf][q][c] = ok ? r[2 * OUT + o] : 0.0f;
                     }
-                    float qv[HP][CPL], vv[HP][CPL], av[HP][CPL];
+                }
+            };
+            auto apply = [&](int buf, int b0) {
 #pragma unroll
-                    for (int q = 0; q < HP; ++q) {
-                        const float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
+                for (int q = 0; q < HP; ++q) {
+                    if (b0 + q < nq) {
+                        float* r = S + static_cast<size_t>(row[buf][q]) * (3 * OUT);
 #pragma unroll
                         for (int c = 0; c < CPL; ++c) {
                             const int o = lane + 32 * c;
-                            const bool ok = (q < nh) && (o < OUT);
-                            qv[q][c] = (ok && of[q]) ? r[o] : 0.0f;
-                            vv[q][c] = ok ? r[OUT + o] : 0.0f;
-                            av[q][c] = ok ? r[2 * OUT + o] : 0.0f;
-                        }
-                    }
-#pragma unroll
-                    for (int q = 0; q < HP; ++q) {
-                        if (q < nh) {
-                            float* r = S + static_cast<size_t>(row[q]) * (3 * OUT);
-#pragma unroll
-                            for (int c = 0; c < CPL; ++c) {
-                                const int o = lane + 32 * c;
-                                if (o < OUT) {
-                                    h[c] = fmaf(av[q][c], h[c], vv[q][c]);
-                                    if (of[q]) r[o] = qv[q][c] * h[c];
-                                }
+                            if (o < OUT) {
+                                h[c] = fmaf(av[buf][q][c], h[c], vv[buf][q][c]);
+                                if (of[buf][q]) r[o] = qv[buf][q][c] * h[c];
                             }
                         }
                     }
                 }
+            };
+            if (nq > 0) fetch(0, 0);
+            for (int b0 = 0; b0 < nq; b0 += 2 * HP) {
+                if (b0 + HP < nq) fetch(1, b0 + HP);
+                apply(0, b0);
+                if (b0 + HP < nq) {
+                    if (b0 + 2 * HP < nq) fetch(0, b0 + 2 * HP);
+                    apply(1, b0 + HP);
+                }
             }
+            __syncwarp();
         }
     }
     if (active) {
