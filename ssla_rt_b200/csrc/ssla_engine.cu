@@ -171,6 +171,7 @@ struct Workspace {
     DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps, work;
     DevBuf hot[2], hot_flag[2];    // hot tiles of stages 0-1 (k_hot_tiles)
     bool hot_on[2] = {false, false};   // this drain splits hot tiles of stage s
+    int gpt[2] = {16, 16};             // group items per tile of the stage-s scans
     DevBuf stage_out[4];
 
     void plan(Geo& g, int P_, int mpe_, int n_max_, int s_first_, bool record) {
@@ -282,10 +283,12 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
         int qstride;
         if (s < 2) {
             if (l == 1 || l == 2) {
-                // split hot tiles only when the 2x2-group items of the rows
+                // split hot tiles only when the cell-group items of the rows
                 // this engine scans are fewer than the kernel's resident warps
                 const int ty_lo = g.row_lo[s] / kTile, ty_hi = (g.row_hi[s] + kTile - 1) / kTile;
-                const long long groups = static_cast<long long>(g.P) * g.tx[s] * std::max(0, ty_hi - ty_lo) * 16;
+                const long long tiles = static_cast<long long>(g.P) * g.tx[s] * std::max(0, ty_hi - ty_lo);
+                w.gpt[s] = scan_fused_groups_per_tile(l, tiles);
+                const long long groups = tiles * w.gpt[s];
                 w.hot_on[s] = groups < scan_fused_resident_warps(l);
                 if (w.hot_on[s]) {
                     HotArgs ha{};
@@ -303,6 +306,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>(); fa.work = w.work.as<int>() + l;
             fa.hot = w.hot_on[s] ? w.hot[s].as<int>() : nullptr;
             fa.hot_flag = w.hot_on[s] ? w.hot_flag[s].as<uint8_t>() : nullptr;
+            fa.gpt = (l == 1) ? w.gpt[s] : 16;
             launch_scan_fused(st, l, fa);
             check_launch("k_scan_fused");
             prof.mark(kScan[l], 1, st);

@@ -946,7 +946,8 @@ __global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
 // k_scan_group: per-cell LRU scan of a small layer (layers 1-3: IN, OUT <= 24,
 // the 9 x IN x 3*OUT qvg weights fit in shared memory) fused with that
 // layer's qvg matvec (matvec_ct<IN,3*OUT>, linear.h:80-90).
-// Work item = (partition, 8x8 tile, 2x2 cell group), taken by one warp from
+// Work item = (partition, 8x8 tile, GX x GY cell group: 4x2 for layer 1,
+// 2x2 for layers 2-3), taken by one warp from
 // an atomic counter; warps never wait on one another.  When the group items
 // are fewer than the resident warps (one clustered stream, a strip of a
 // large sensor), tiles whose lists exceed kHotTileEntries are listed by
@@ -964,29 +965,34 @@ __global__ void __launch_bounds__(1024) k_hot_tiles(HotArgs a) {
 // One owner per cell, no atomics on state; results equal the per-event
 // reference (fmaf order over input channels, sigmoid, fmaf update).
 // ---------------------------------------------------------------------------
-template <int IN, int OUT, int WPC>
+template <int IN, int OUT, int WPC, int GX, int GY>
 struct ScanGroupShape {
     static constexpr int NT = 32 * WPC;
+    static constexpr int NCELL = GX * GY;               // cells of a group item
+    static constexpr int GPT = (kTile / GX) * (kTile / GY);   // group items per tile
+    static constexpr int HMAX = (GX < 3 ? GX : 3) * (GY < 3 ? GY : 3);   // hits of one entry at most
     static constexpr int J2 = 3 * OUT;
     static constexpr int DS = IN * J2 + ((IN * J2) % 32 == 16 ? 4 : ((IN * J2) % 32 == 0 ? 4 : 0));
     static constexpr int QR = ((2 * OUT / 4) % 2 == 0) ? 2 * OUT + 4 : 2 * OUT;   // [a | v] row
-    static constexpr int QCAP = 160;                    // < 32 pending + 32 events x 4 cells
+    static constexpr int QCAP = 32 + 32 * HMAX;         // < 32 pending + 32 entries x HMAX hits
     static constexpr int G4 = OUT / 4;                  // 4-channel slices of a cell (update lanes per cell)
     static constexpr size_t per_warp = sizeof(float) * 32 * QR + (sizeof(int) + 1) * QCAP + 32;
     static constexpr size_t smem = sizeof(float) * 9 * DS + WPC * per_warp;
-    static_assert(IN % 4 == 0 && OUT % 4 == 0 && DS % 4 == 0, "shape");
+    static_assert(IN % 4 == 0 && OUT % 4 == 0 && DS % 4 == 0 && NCELL <= 8 && NCELL * G4 <= 32 &&
+                  kTile % GX == 0 && kTile % GY == 0 && (32 * QR + QCAP + QCAP / 4 + 8) % 4 == 0, "shape");
 };
 
-template <int IN, int OUT, int WPC>
+template <int IN, int OUT, int WPC, int GX, int GY>
 __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanFusedArgs a) {
-    using Sh = ScanGroupShape<IN, OUT, WPC>;
+    using Sh = ScanGroupShape<IN, OUT, WPC, GX, GY>;
     constexpr int J2 = Sh::J2, DS = Sh::DS, QR = Sh::QR, QCAP = Sh::QCAP, G4 = Sh::G4;
+    constexpr int NCELL = Sh::NCELL, GPT = Sh::GPT;
     extern __shared__ __align__(16) float dsm[];
     float* Ws = dsm;                                              // [9][DS]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* Qs = Ws + 9 * DS + warp * (Sh::per_warp / sizeof(float));   // [32][QR]
     int* qk = reinterpret_cast<int*>(Qs + 32 * QR);                    // [QCAP] entry
-    unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<6
+    unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<7
     unsigned char* perm = qm + QCAP;                                    // [32] batch lane -> slot
     // the weights are constant: staged before the wait
     for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
@@ -998,7 +1004,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
     const int s = a.stage;
     const int Wl = a.g.W[s], Hl = a.g.H[s];
     const int ntiles = a.g.tx[s] * a.g.ty[s];
-    const int n_groups = a.g.P * ntiles * 16;
+    const int n_groups = a.g.P * ntiles * GPT;
     const int n_items = n_groups + (a.hot ? a.hot[0] * 64 : 0);
     float* const QH = a.QH;
     for (;;) {
@@ -1008,13 +1014,13 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
         if (item >= n_items) break;
         int p, tile, gx0, gy0, ncell;
         if (item < n_groups) {
-            const int grp = item & 15;
-            tile = (item >> 4) % ntiles;
-            p = (item >> 4) / ntiles;
+            const int grp = item % GPT;
+            tile = (item / GPT) % ntiles;
+            p = (item / GPT) / ntiles;
             if (a.hot_flag && a.hot_flag[p * ntiles + tile]) continue;      // scanned cell by cell
-            gx0 = (tile % a.g.tx[s]) * kTile + (grp & 3) * 2;
-            gy0 = (tile / a.g.tx[s]) * kTile + (grp >> 2) * 2;
-            ncell = 4;
+            gx0 = (tile % a.g.tx[s]) * kTile + (grp % (kTile / GX)) * GX;
+            gy0 = (tile / a.g.tx[s]) * kTile + (grp / (kTile / GX)) * GY;
+            ncell = NCELL;
         } else {
             const int h = (item - n_groups) >> 6, cell = (item - n_groups) & 63;
             const int pt = a.hot[1 + h];
@@ -1024,12 +1030,17 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             gy0 = (tile / a.g.tx[s]) * kTile + (cell >> 3);
             ncell = 1;
         }
-        if (gx0 >= Wl || gy0 >= Hl || gy0 + (ncell > 1 ? 1 : 0) < a.g.row_lo[s] || gy0 >= a.g.row_hi[s]) continue;
+        if (gx0 >= Wl || gy0 >= Hl || gy0 + (ncell > 1 ? GY - 1 : 0) < a.g.row_lo[s] || gy0 >= a.g.row_hi[s]) continue;
         float* const hid = a.parts[p].hidden[a.layer];
         // update role: lane = (cell cc of the group, 4-channel slice g)
         const int cc = lane / G4, g4 = lane % G4;
-        const int ux = gx0 + (cc & 1), uy = gy0 + (cc >> 1);
-        const bool uown = lane < 4 * G4 && cc < ncell && ux < Wl && uy < Hl;
+        const int ux = gx0 + cc % GX, uy = gy0 + cc / GX;
+        const bool uown = lane < NCELL * G4 && cc < ncell && ux < Wl && uy < Hl;
+        // the group's cells inside the grid (bit c: cell (c % GX, c / GX))
+        unsigned vmask = 0;
+#pragma unroll
+        for (int c = 0; c < NCELL; ++c)
+            if (c < ncell && gx0 + c % GX < Wl && gy0 + c / GX < Hl) vmask |= 1u << c;
         float* const hp = hid + (static_cast<size_t>(uown ? uy : 0) * Wl + (uown ? ux : 0)) * OUT + 4 * g4;
         float4 h4 = uown ? *reinterpret_cast<const float4*>(hp) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int np = 0;                                   // queued slots (warp-uniform)
@@ -1038,10 +1049,13 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             // cell and output masks over the slots (bit = slot)
             const bool valid = lane < nb;
             const int m0 = qm[valid ? lane : 0];
-            unsigned cm[4];
+            unsigned mk_own = 0;                  // this lane's update cell: its slots
 #pragma unroll
-            for (int c = 0; c < 4; ++c) cm[c] = __ballot_sync(0xffffffffu, valid && ((m0 >> 4) & 3) == c);
-            const unsigned om = __ballot_sync(0xffffffffu, valid && ((m0 >> 6) & 1));
+            for (int c = 0; c < NCELL; ++c) {
+                const unsigned b = __ballot_sync(0xffffffffu, valid && ((m0 >> 4) & 7) == c);
+                if (cc == c) mk_own = b;
+            }
+            const unsigned om = __ballot_sync(0xffffffffu, valid && ((m0 >> 7) & 1));
             // B runs the slots sorted by delta (counting sort, one ballot per
             // delta), so the lanes of a weight read mostly share one row
             {
@@ -1100,7 +1114,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             // C: ordered updates, lane = (cell, 4 channels); four hits per
             // round, their rows' loads issued ahead of the fmaf chain
             {
-                unsigned mk = uown ? ((cc == 0) ? cm[0] : (cc == 1) ? cm[1] : (cc == 2) ? cm[2] : cm[3]) : 0u;
+                unsigned mk = uown ? mk_own : 0u;
                 float2 hlo = make_float2(h4.x, h4.y), hhi = make_float2(h4.z, h4.w);
                 while (mk) {
                     int s4[4];
@@ -1162,15 +1176,19 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             const int j = cj + lane;
             const int2 ent = cur;
             const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
+            // cells of the group inside the entry's 3x3 patch: cell (i, j)
+            // is hit iff i in [rx - 2, rx] and j in [ry - 2, ry], with (rx, ry)
+            // the entry's position relative to the group's corner (-1, -1)
+            const int rx = ex - gx0 + 1, ry = ey - gy0 + 1;
             unsigned cmask = 0;
-            if (j < ccnt) {
+            if (j < ccnt && rx >= 0 && rx <= GX + 1 && ry >= 0 && ry <= GY + 1) {
+                const int xl = max(rx - 2, 0), xh = min(rx, GX - 1);
+                const int yl = max(ry - 2, 0), yh = min(ry, GY - 1);
+                const unsigned xm = (xh >= xl) ? (((2u << xh) - 1u) & ~((1u << xl) - 1u)) : 0u;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
-                    const int dx = cx - ex, dy = cy - ey;
-                    if (c < ncell && cx < Wl && cy < Hl && dx >= -1 && dx <= 1 && dy >= -1 && dy <= 1)
-                        cmask |= 1u << c;
-                }
+                for (int jy = 0; jy < GY; ++jy)
+                    if (jy >= yl && jy <= yh) cmask |= xm << (jy * GX);
+                cmask &= vmask;
             }
             // output flag of a hit: bit 31 of the entry (set for stage-0 lists
             // by k_flag_s0 after the gates, by k_filter for later stages)
@@ -1186,12 +1204,11 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             if (tot != 0) {
                 int pos = np + __popc(v0 & lt) + 2 * __popc(v1 & lt) + 4 * __popc(v2 & lt);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < NCELL; ++c) {
                     if ((cmask >> c) & 1u) {
-                        const int cx = gx0 + (c & 1), cy = gy0 + (c >> 1);
-                        const int d = (1 - (cy - ey)) * 3 + (1 - (cx - ex));
+                        const int d = (ry - c / GX) * 3 + (rx - c % GX);      // (1 - dy) * 3 + (1 - dx)
                         qk[pos] = ent.x;
-                        qm[pos] = static_cast<unsigned char>(d | (c << 4) | (outf << 6));
+                        qm[pos] = static_cast<unsigned char>(d | (c << 4) | (outf << 7));
                         ++pos;
                     }
                 }
@@ -2092,10 +2109,18 @@ int scan_fused_grid(K kern, Sh) {
 
 int scan_fused_resident_warps(int layer) {
     switch (layer) {
-        case 1: return scan_fused_grid(k_scan_group<12, 12, 8>, ScanGroupShape<12, 12, 8>{}) * 8;
-        case 2: return scan_fused_grid(k_scan_group<12, 24, 16>, ScanGroupShape<12, 24, 16>{}) * 16;
-        default: return scan_fused_grid(k_scan_group<24, 24, 16>, ScanGroupShape<24, 24, 16>{}) * 16;
+        case 1: return scan_fused_grid(k_scan_group<12, 12, 8, 2, 2>, ScanGroupShape<12, 12, 8, 2, 2>{}) * 8;
+        case 2: return scan_fused_grid(k_scan_group<12, 24, 16, 2, 2>, ScanGroupShape<12, 24, 16, 2, 2>{}) * 16;
+        default: return scan_fused_grid(k_scan_group<24, 24, 16, 2, 2>, ScanGroupShape<24, 24, 16, 2, 2>{}) * 16;
     }
+}
+
+int scan_fused_groups_per_tile(int layer, long long tile_count) {
+    // layer 1 takes 4x2 groups (half the list walks of 2x2) when that still
+    // leaves two items per resident warp, 2x2 groups otherwise
+    if (layer == 1 && tile_count * ScanGroupShape<12, 12, 8, 4, 2>::GPT >= 2LL * scan_fused_resident_warps(1))
+        return ScanGroupShape<12, 12, 8, 4, 2>::GPT;
+    return ScanGroupShape<12, 24, 16, 2, 2>::GPT;
 }
 
 void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
@@ -2108,9 +2133,12 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
         pdl_launch(kern, std::min(grid, need), Sh::NT, Sh::smem, st, a);
     };
     switch (layer) {
-        case 1: go(k_scan_group<12, 12, 8>, ScanGroupShape<12, 12, 8>{}); break;
-        case 2: go(k_scan_group<12, 24, 16>, ScanGroupShape<12, 24, 16>{}); break;
-        default: go(k_scan_group<24, 24, 16>, ScanGroupShape<24, 24, 16>{}); break;
+        case 1:
+            if (a.gpt == ScanGroupShape<12, 12, 8, 4, 2>::GPT) go(k_scan_group<12, 12, 8, 4, 2>, ScanGroupShape<12, 12, 8, 4, 2>{});
+            else go(k_scan_group<12, 12, 8, 2, 2>, ScanGroupShape<12, 12, 8, 2, 2>{});
+            break;
+        case 2: go(k_scan_group<12, 24, 16, 2, 2>, ScanGroupShape<12, 24, 16, 2, 2>{}); break;
+        default: go(k_scan_group<24, 24, 16, 2, 2>, ScanGroupShape<24, 24, 16, 2, 2>{}); break;
     }
 }
 

@@ -87,6 +87,7 @@ struct ScanFusedArgs {
     int* work;               // work-item counter of this launch, zero on entry
     const int* hot;          // hot tiles of the stage: [0] count, [1..] (p * ntiles + tile); null: none
     const uint8_t* hot_flag; // [P * ntiles] 1 = the tile is scanned cell by cell; null: none
+    int gpt;                 // group items per tile (scan_fused_groups_per_tile)
 };
 
 // When a stage-0/1 scan has fewer 2x2-group work items than resident warps,
@@ -107,6 +108,9 @@ struct HotArgs {
 void launch_hot_tiles(cudaStream_t st, const HotArgs& a);
 // Warps of the stage-0/1 scan kernel of `layer` resident on the device.
 int scan_fused_resident_warps(int layer);
+// Group work items per 8x8 tile of a stage-0/1 scan layer over tile_count
+// (partition, tile) pairs; the launch takes it in ScanFusedArgs::gpt.
+int scan_fused_groups_per_tile(int layer, long long tile_count);
 
 struct ContribArgs {
     Geo g;
