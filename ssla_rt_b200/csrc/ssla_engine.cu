@@ -306,7 +306,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
             fa.X = X; fa.W = L[l].qvgT; fa.QH = w.QH.as<float>(); fa.work = w.work.as<int>() + l;
             fa.hot = w.hot_on[s] ? w.hot[s].as<int>() : nullptr;
             fa.hot_flag = w.hot_on[s] ? w.hot_flag[s].as<uint8_t>() : nullptr;
-            fa.gpt = (l == 1) ? w.gpt[s] : 16;
+            fa.gpt = w.gpt[s];
             launch_scan_fused(st, l, fa);
             check_launch("k_scan_fused");
             prof.mark(kScan[l], 1, st);

@@ -2116,10 +2116,17 @@ int scan_fused_resident_warps(int layer) {
 }
 
 int scan_fused_groups_per_tile(int layer, long long tile_count) {
-    // layer 1 takes 4x2 groups (half the list walks of 2x2) when that still
-    // leaves two items per resident warp, 2x2 groups otherwise
-    if (layer == 1 && tile_count * ScanGroupShape<12, 12, 8, 4, 2>::GPT >= 2LL * scan_fused_resident_warps(1))
-        return ScanGroupShape<12, 12, 8, 4, 2>::GPT;
+    const long long warps = scan_fused_resident_warps(layer);
+    if (layer == 1) {
+        // 4x2 groups (half the list walks of 2x2) when that still leaves
+        // two items per resident warp
+        if (tile_count * ScanGroupShape<12, 12, 8, 4, 2>::GPT >= 2 * warps) return ScanGroupShape<12, 12, 8, 4, 2>::GPT;
+        return ScanGroupShape<12, 12, 8, 2, 2>::GPT;
+    }
+    // layers 2-3: 2x1 groups where 2x2 groups would leave between one and
+    // two items per resident warp (a second item for few warps: the tail)
+    const long long g22 = tile_count * ScanGroupShape<12, 24, 16, 2, 2>::GPT;
+    if (g22 >= warps && g22 < 2 * warps) return ScanGroupShape<12, 24, 16, 2, 1>::GPT;
     return ScanGroupShape<12, 24, 16, 2, 2>::GPT;
 }
 
@@ -2137,8 +2144,14 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
             if (a.gpt == ScanGroupShape<12, 12, 8, 4, 2>::GPT) go(k_scan_group<12, 12, 8, 4, 2>, ScanGroupShape<12, 12, 8, 4, 2>{});
             else go(k_scan_group<12, 12, 8, 2, 2>, ScanGroupShape<12, 12, 8, 2, 2>{});
             break;
-        case 2: go(k_scan_group<12, 24, 16, 2, 2>, ScanGroupShape<12, 24, 16, 2, 2>{}); break;
-        default: go(k_scan_group<24, 24, 16, 2, 2>, ScanGroupShape<24, 24, 16, 2, 2>{}); break;
+        case 2:
+            if (a.gpt == ScanGroupShape<12, 24, 16, 2, 1>::GPT) go(k_scan_group<12, 24, 16, 2, 1>, ScanGroupShape<12, 24, 16, 2, 1>{});
+            else go(k_scan_group<12, 24, 16, 2, 2>, ScanGroupShape<12, 24, 16, 2, 2>{});
+            break;
+        default:
+            if (a.gpt == ScanGroupShape<24, 24, 16, 2, 1>::GPT) go(k_scan_group<24, 24, 16, 2, 1>, ScanGroupShape<24, 24, 16, 2, 1>{});
+            else go(k_scan_group<24, 24, 16, 2, 2>, ScanGroupShape<24, 24, 16, 2, 2>{});
+            break;
     }
 }
 
