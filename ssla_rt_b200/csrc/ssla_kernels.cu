@@ -976,10 +976,11 @@ struct ScanGroupShape {
     static constexpr int QR = ((2 * OUT / 4) % 2 == 0) ? 2 * OUT + 4 : 2 * OUT;   // [a | v] row
     static constexpr int QCAP = 32 + 32 * HMAX;         // < 32 pending + 32 entries x HMAX hits
     static constexpr int G4 = OUT / 4;                  // 4-channel slices of a cell (update lanes per cell)
-    static constexpr size_t per_warp = sizeof(float) * 32 * QR + (sizeof(int) + 1) * QCAP + 32;
+    static constexpr size_t per_warp = sizeof(float) * 32 * QR + (sizeof(int) + 1) * QCAP + 32 + sizeof(int2) * 64;
     static constexpr size_t smem = sizeof(float) * 9 * DS + WPC * per_warp;
     static_assert(IN % 4 == 0 && OUT % 4 == 0 && DS % 4 == 0 && NCELL <= 8 && NCELL * G4 <= 32 &&
-                  kTile % GX == 0 && kTile % GY == 0 && (32 * QR + QCAP + QCAP / 4 + 8) % 4 == 0, "shape");
+                  kTile % GX == 0 && kTile % GY == 0 && (32 * QR + QCAP + QCAP / 4 + 8 + 128) % 4 == 0 &&
+                  (QCAP + 32) % 8 == 0, "shape");
 };
 
 template <int IN, int OUT, int WPC, int GX, int GY>
@@ -994,6 +995,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
     int* qk = reinterpret_cast<int*>(Qs + 32 * QR);                    // [QCAP] entry
     unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<7
     unsigned char* perm = qm + QCAP;                                    // [32] batch lane -> slot
+    int2* rbuf = reinterpret_cast<int2*>(perm + 32);                    // [64] relevant list entries
     // the weights are constant: staged before the wait
     for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
         const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
@@ -1162,26 +1164,18 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
         auto load_block = [&](int sg, int j0, int cnt) -> int2 {
             return (sg < nseg && j0 + lane < cnt) ? a.tl[(slot0 + sg) * a.g.seg + j0 + lane] : make_int2(0, 0);
         };
-        int cs = 0, cj = 0, ccnt = seg_cnt(0);
-        while (cs < nseg && ccnt == 0) ccnt = seg_cnt(++cs);
-        int2 cur = load_block(cs, 0, ccnt);
-        while (cs < nseg) {
-            int ns = cs, nj = cj + 32, ncnt = ccnt;
-            if (nj >= ccnt) {
-                ns = cs + 1;
-                nj = 0;
-                ncnt = seg_cnt(ns);
-            }
-            const int2 nxt = load_block(ns, nj, ncnt);       // in flight during this block's walk
-            const int j = cj + lane;
-            const int2 ent = cur;
+        // Hits of up to 32 relevant entries (rbuf[0, nrel)) into the slot queue,
+        // batches of 32 slots run as the queue fills.
+        auto queue_hits = [&](int nrel) {
+            const bool on = lane < nrel;
+            const int2 ent = on ? rbuf[lane] : make_int2(0, 0);
             const int ex = ent.y & 0xFFFF, ey = (ent.y >> 16) & 0x7FFF;
             // cells of the group inside the entry's 3x3 patch: cell (i, j)
             // is hit iff i in [rx - 2, rx] and j in [ry - 2, ry], with (rx, ry)
             // the entry's position relative to the group's corner (-1, -1)
             const int rx = ex - gx0 + 1, ry = ey - gy0 + 1;
             unsigned cmask = 0;
-            if (j < ccnt && rx >= 0 && rx <= GX + 1 && ry >= 0 && ry <= GY + 1) {
+            if (on) {
                 const int xl = max(rx - 2, 0), xh = min(rx, GX - 1);
                 const int yl = max(ry - 2, 0), yh = min(ry, GY - 1);
                 const unsigned xm = (xh >= xl) ? (((2u << xh) - 1u) & ~((1u << xl) - 1u)) : 0u;
@@ -1193,7 +1187,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             // output flag of a hit: bit 31 of the entry (set for stage-0 lists
             // by k_flag_s0 after the gates, by k_filter for later stages)
             const int outf = a.second ? static_cast<int>(static_cast<uint32_t>(ent.y) >> 31) : 1;
-            // queue positions: exclusive prefix of the hit counts (0..4)
+            // queue positions: exclusive prefix of the hit counts (0..6)
             // from one ballot per bit
             const int nc = __popc(cmask);
             const unsigned v0 = __ballot_sync(0xffffffffu, nc & 1);
@@ -1201,30 +1195,60 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
             const unsigned v2 = __ballot_sync(0xffffffffu, nc & 4);
             const unsigned lt = lanemask_lt();
             const int tot = __popc(v0) + 2 * __popc(v1) + 4 * __popc(v2);
-            if (tot != 0) {
-                int pos = np + __popc(v0 & lt) + 2 * __popc(v1 & lt) + 4 * __popc(v2 & lt);
+            if (tot == 0) return;
+            int pos = np + __popc(v0 & lt) + 2 * __popc(v1 & lt) + 4 * __popc(v2 & lt);
 #pragma unroll
-                for (int c = 0; c < NCELL; ++c) {
-                    if ((cmask >> c) & 1u) {
-                        const int d = (ry - c / GX) * 3 + (rx - c % GX);      // (1 - dy) * 3 + (1 - dx)
-                        qk[pos] = ent.x;
-                        qm[pos] = static_cast<unsigned char>(d | (c << 4) | (outf << 7));
-                        ++pos;
-                    }
+            for (int c = 0; c < NCELL; ++c) {
+                if ((cmask >> c) & 1u) {
+                    const int d = (ry - c / GX) * 3 + (rx - c % GX);      // (1 - dy) * 3 + (1 - dx)
+                    qk[pos] = ent.x;
+                    qm[pos] = static_cast<unsigned char>(d | (c << 4) | (outf << 7));
+                    ++pos;
                 }
-                np += tot;
-                __syncwarp();
-                while (np >= 32) {
-                    batch(32);
-                    np -= 32;
-                    // move the remaining queued slots to the front
-                    for (int b = 0; b < np; b += 32) {
-                        int kk = 0, mm = 0;
-                        if (b + lane < np) { kk = qk[32 + b + lane]; mm = qm[32 + b + lane]; }
-                        __syncwarp();
-                        if (b + lane < np) { qk[b + lane] = kk; qm[b + lane] = static_cast<unsigned char>(mm); }
-                        __syncwarp();
-                    }
+            }
+            np += tot;
+            __syncwarp();
+            while (np >= 32) {
+                batch(32);
+                np -= 32;
+                // move the remaining queued slots to the front
+                for (int b = 0; b < np; b += 32) {
+                    int kk = 0, mm = 0;
+                    if (b + lane < np) { kk = qk[32 + b + lane]; mm = qm[32 + b + lane]; }
+                    __syncwarp();
+                    if (b + lane < np) { qk[b + lane] = kk; qm[b + lane] = static_cast<unsigned char>(mm); }
+                    __syncwarp();
+                }
+            }
+        };
+        // The walk keeps only the entries whose patch touches the group (a
+        // few compares per entry), 32 at a time for the hit analysis.
+        int nrel = 0;
+        int cs = 0, cj = 0, ccnt = seg_cnt(0);
+        while (cs < nseg && ccnt == 0) ccnt = seg_cnt(++cs);
+        int2 cur = load_block(cs, 0, ccnt);
+        while (cs < nseg) {
+            int ns = cs, nj = cj + 32, ncnt = ccnt;
+            if (nj >= ccnt) {
+                ns = cs + 1;
+                nj = 0;
+                ncnt = seg_cnt(ns);
+            }
+            const int2 nxt = load_block(ns, nj, ncnt);       // in flight during this block's walk
+            {
+                const int ex = cur.y & 0xFFFF, ey = (cur.y >> 16) & 0x7FFF;
+                const int rx = ex - gx0 + 1, ry = ey - gy0 + 1;
+                const bool rel = cj + lane < ccnt && rx >= 0 && rx <= GX + 1 && ry >= 0 && ry <= GY + 1;
+                const unsigned m = __ballot_sync(0xffffffffu, rel);
+                if (rel) rbuf[nrel + __popc(m & lanemask_lt())] = cur;
+                nrel += __popc(m);
+                if (nrel >= 32) {
+                    __syncwarp();
+                    queue_hits(32);
+                    nrel -= 32;
+                    const int2 t = (lane < nrel) ? rbuf[32 + lane] : make_int2(0, 0);
+                    __syncwarp();
+                    if (lane < nrel) rbuf[lane] = t;
                 }
             }
             cs = ns;
@@ -1236,6 +1260,10 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                 cj = 0;
                 cur = load_block(cs, 0, ccnt);
             }
+        }
+        if (nrel > 0) {
+            __syncwarp();
+            queue_hits(nrel);
         }
         if (np > 0) batch(np);
         if (uown) *reinterpret_cast<float4*>(hp) = h4;
