@@ -363,7 +363,10 @@ int  ssla_engine_strip_connect(SslaEngine* eng, int side, void* peer_dev_ptr, co
 /* One drain of the strip's events (device rows, stream order) with the
  * exchanges; waits for the neighbours' rows on the device (bounded), so
  * each neighbour must drain the chunk with the same global event range on
- * its own GPU concurrently.  Asynchronous on `stream`. */
+ * its own GPU concurrently.  The events must lie in rows [lo - band_rows,
+ * hi + band_rows) (the routing of ssla_rt_b200/strips.py); the tile lists
+ * of a strip engine cover only those rows, so an event outside them is not
+ * processed.  Asynchronous on `stream`. */
 int  ssla_engine_strip_drain(SslaEngine* eng, const float* events_dev, int n, uint8_t* flags_dev,
                              void* stream);
 /* The same for k strips sharing one GPU and one stream: the engines' steps

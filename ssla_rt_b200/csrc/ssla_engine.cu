@@ -211,6 +211,7 @@ struct Workspace {
             const size_t slots = static_cast<size_t>(P) * g.tx[s] * g.ty[s] * g.nseg[s];
             tl[s].alloc(slots * g.seg * sizeof(int2));
             tl_cnt[s].alloc(slots * sizeof(int));
+            SSLA_CK(cudaMemset(tl_cnt[s].p, 0, slots * sizeof(int)));   // tiles no filter launch covers
             if (s < 2) {
                 const size_t nt = static_cast<size_t>(P) * g.tx[s] * g.ty[s];
                 hot[s].alloc(sizeof(int) * (nt + 1));
@@ -654,6 +655,9 @@ struct Engine {
         *strip.err = 0;
         strip.seq = 0;
         set_owned(0, 0, g.W[2], lo >> 2, hi >> 2, nullptr);
+        // the filters now cover only the strip's tile rows: no list outside them may keep old counts
+        for (int s = 0; s < 4; ++s)
+            if (ws.tl_cnt[s].p) SSLA_CK(cudaMemset(ws.tl_cnt[s].p, 0, ws.tl_cnt[s].n));
         // scans update the rows owned events read: own rows and one beyond each side
         for (int s = 0; s < 4; ++s) {
             g.row_lo[s] = std::max(0, (lo >> s) - 1);
@@ -1163,6 +1167,10 @@ struct Engine {
         FilterArgs fa{};
         fa.g = g; fa.stage = 0; fa.ev_xy = ws.ev_xy.as<uint32_t>(); fa.rflags = ws.rflags.as<uint8_t>();
         fa.range = ws.ev_off.as<int>(); fa.tl = ws.tl[0].as<int2>(); fa.tl_cnt = ws.tl_cnt[0].as<int>();
+        if (strip.on) {                            // a strip's events: its rows and the bands
+            fa.ev_row_lo = std::max(0, strip.lo - strip.band);
+            fa.ev_row_hi = std::min(g.H[0], strip.hi + strip.band);
+        }
         launch_filter(st, fa);
         check_launch("k_filter s0");
         prof.mark("filter_s0", 1, st);
@@ -1193,6 +1201,8 @@ struct Engine {
             f.g = g; f.stage = s; f.E = ws.E[s].as<StageEntry>(); f.rflags = ws.rflags.as<uint8_t>();
             f.range = ws.off[s].as<int>(); f.tl = ws.tl[s].as<int2>(); f.tl_cnt = ws.tl_cnt[s].as<int>();
             f.out_bit = static_cast<uint8_t>(F_R1 << s);
+            f.ev_row_lo = fa.ev_row_lo;
+            f.ev_row_hi = fa.ev_row_hi;
             launch_filter(st, f);
             check_launch("k_filter");
         }

@@ -105,7 +105,7 @@ __global__ void k_prep_records(const HybridInputRec* __restrict__ rec, int n,
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
     pdl_enter();
-    const int p = blockIdx.x, trow = blockIdx.y, seg = blockIdx.z;
+    const int p = blockIdx.x, trow = a.trow0 + blockIdx.y, seg = blockIdx.z;
     const int s = a.stage;
     const int tx = a.g.tx[s];
     const int ntiles = tx * a.g.ty[s];
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kNT) k_filter(FilterArgs a) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_filter_tiles(FilterArgs a) {
     pdl_enter();
-    const int p = blockIdx.x, tile = blockIdx.y, seg = blockIdx.z;
+    const int p = blockIdx.x, tile = a.trow0 * a.g.tx[a.stage] + blockIdx.y, seg = blockIdx.z;
     const int s = a.stage;
     const int ntiles = a.g.tx[s] * a.g.ty[s];
     const int lo = a.range[p], hi = a.range[p + 1];
@@ -2066,12 +2066,25 @@ void launch_records(cudaStream_t st, int n_cap, const int* count2, const StageEn
                                                      static_cast<HybridInputRec*>(rec));
 }
 
-void launch_filter(cudaStream_t st, const FilterArgs& a) {
+void launch_filter(cudaStream_t st, const FilterArgs& a0) {
+    FilterArgs a = a0;
     const int s = a.stage;
+    // tile rows whose lists can hold entries: a tile row t lists stage-s rows
+    // [8t - 1, 8t + 8]; without a row window, all of them.  Tiles outside
+    // keep count 0 (the counts are zeroed when allocated and when the window
+    // is set).
+    int t_lo = 0, t_hi = a.g.ty[s];
+    if (a.ev_row_hi > a.ev_row_lo) {
+        const int lo_s = a.ev_row_lo >> s, hi_s = ((a.ev_row_hi - 1) >> s) + 1;
+        t_lo = std::max(0, (lo_s - kTile) / kTile);
+        t_hi = std::min(a.g.ty[s], hi_s / kTile + 1);
+    }
+    if (t_hi <= t_lo) return;
+    a.trow0 = t_lo;
     if (s == 0)
-        pdl_launch(k_filter, dim3(a.g.P, a.g.ty[0], a.g.nseg[0]), kNT, 0, st, a);
+        pdl_launch(k_filter, dim3(a.g.P, t_hi - t_lo, a.g.nseg[0]), kNT, 0, st, a);
     else
-        pdl_launch(k_filter_tiles, dim3(a.g.P, a.g.tx[s] * a.g.ty[s], a.g.nseg[s]), kNT, 0, st, a);
+        pdl_launch(k_filter_tiles, dim3(a.g.P, a.g.tx[s] * (t_hi - t_lo), a.g.nseg[s]), kNT, 0, st, a);
 }
 
 void launch_gates(cudaStream_t st, const GateArgs& a) {

@@ -17,6 +17,8 @@ struct FilterArgs {
     int2* tl;                // tile lists
     int* tl_cnt;             // entries per (partition, tile, segment)
     uint8_t out_bit;         // reach bit meaning "second-layer output needed"
+    int ev_row_lo, ev_row_hi;  // stage-0 pixel rows holding the drain's events (hi <= lo: all)
+    int trow0;               // first tile row of the launch (set by launch_filter)
 };
 
 struct GateArgs {
