@@ -1254,7 +1254,8 @@ def main() -> int:
                     "d2h_bytes_per_step": int(d2h),
                     "method": "ssla_engine_drain_host_async per step: pinned host events copied in on the "
                               "engine's copy stream (overlapping the previous step), flags and all decoded "
-                              "predictions copied back; host wall time of the K steps, max over ranks"},
+                              "predictions written back into pinned host buffers by a kernel chained to the drain; "
+                              "host wall time of the K steps, max over ranks"},
             "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
             "latency_us": latency,
             "algorithmic_mac_per_event": tot_macs / N_EVENTS,

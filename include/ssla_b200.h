@@ -124,10 +124,12 @@ int  ssla_engine_drain_host(SslaEngine* eng, const float* events_host,
 /* Pipelined form of ssla_engine_drain_host for pinned host buffers: the
  * copy of the events runs on an engine-owned copy stream into one of two
  * device buffers, so it overlaps the previous drain on `stream`.  The drain
- * waits for it, then copies the flags (flags_host, may be NULL) and every
+ * waits for it, then the flags (flags_host, may be NULL) and every
  * partition's decoded predictions (preds_host, n_partitions x cells x
- * (5+ncls) floats, may be NULL) back on `stream`.  Returns without
- * waiting: the host buffers belong to the call until `stream` passes it.
+ * (5+ncls) floats, may be NULL) go back on `stream`: written by a kernel
+ * chained to the drain where the buffer is pinned (page-locked, device-
+ * mapped), copied where it is pageable.  Returns without waiting: the host
+ * buffers belong to the call until `stream` passes it.
  * The shard threads of the reference overlap their ring pushes with the
  * GPU drain the same way (src/lib_stage01_to_gpu.cpp:157-311). */
 int  ssla_engine_drain_host_async(SslaEngine* eng, const float* events_host,

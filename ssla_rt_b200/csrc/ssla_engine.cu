@@ -855,6 +855,19 @@ struct Engine {
                "; 1 weights, 2 layer input, 4 contributions, 8 event message, 16 completion)";
     }
 
+    // Device alias of a pinned, device-mapped host pointer (page-locked
+    // memory with unified addressing), or null for any other pointer.
+    template <typename T>
+    static T* mapped_alias(T* host) {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, host) != cudaSuccess) {
+            cudaGetLastError();                    // pageable memory: clear the sticky query error
+            return nullptr;
+        }
+        if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+        return static_cast<T*>(at.devicePointer);
+    }
+
     // ---- pipelined host drains: copy-in on a copy stream, double-buffered ----
     struct HostPipe {
         cudaStream_t st = nullptr;
@@ -865,9 +878,10 @@ struct Engine {
 
     // Events from pinned host memory: the copy of this drain's events runs on
     // the engine's copy stream, into the device buffer the drain before last
-    // used, while earlier drains may still run on `st`; the drain waits for
-    // its copy, then its flags and all partitions' decoded predictions are
-    // copied back to flags_host / preds_host (either may be null) on `st`.
+    // used (after that drain's results were copied out), while the previous
+    // drain runs on `st`; the drain waits for its copy, then its flags and
+    // all partitions' decoded predictions are copied back to flags_host /
+    // preds_host (either may be null) on `st`.
     // Returns without waiting; the host buffers belong to the call until
     // `st` has passed it.
     void drain_host_async(const float* ev_host, const int* off, uint8_t* flags_host, float* preds_host,
@@ -892,11 +906,25 @@ struct Engine {
         SSLA_CK(cudaEventRecord(hpipe.copied[k], hpipe.st));
         SSLA_CK(cudaStreamWaitEvent(st, hpipe.copied[k], 0));
         drain(hpipe.ev[k].as<float>(), off, nullptr, st);
-        SSLA_CK(cudaEventRecord(hpipe.consumed[k], st));
-        if (flags_host && n > 0)
+        // Results: pinned outputs are written by a kernel chained to the
+        // drain (no copy-engine round trip on the drain stream); pageable
+        // ones are copied.
+        uint8_t* fdev = (flags_host && n > 0) ? mapped_alias(flags_host) : nullptr;
+        float* pdev = preds_host ? mapped_alias(preds_host) : nullptr;
+        if (fdev || pdev) {
+            launch_results_to_host(st, ws.rflags.as<uint8_t>(), n, fdev, preds_dec.as<float>(),
+                                   static_cast<int>(preds_dec.n / sizeof(float)), pdev);
+            check_launch("k_results_to_host");
+        }
+        if (flags_host && n > 0 && !fdev)
             SSLA_CK(cudaMemcpyAsync(flags_host, ws.rflags.p, n, cudaMemcpyDeviceToHost, st));
-        if (preds_host)
+        if (preds_host && !pdev)
             SSLA_CK(cudaMemcpyAsync(preds_host, preds_dec.p, preds_dec.n, cudaMemcpyDeviceToHost, st));
+        // The copy-in of the drain after next (same buffer) starts once this
+        // drain's results are out: issued earlier it would take the copy
+        // engine while the results wait behind it, and it still has the
+        // whole next drain to finish.
+        SSLA_CK(cudaEventRecord(hpipe.consumed[k], st));
     }
 
     // ---- ring drains (ssla_rings.cu): one pinned ring per partition ----

@@ -2286,6 +2286,40 @@ void launch_fill_clk(cudaStream_t st, int P, const int* rec_off, const unsigned 
 void launch_stamp(cudaStream_t st, unsigned long long* dst) { k_stamp<<<1, 1, 0, st>>>(dst); }
 
 namespace {
+// Drain results into mapped pinned host memory (zero-copy writes over the
+// host link), 16 bytes per store where both sides are 16-byte aligned.
+__global__ void __launch_bounds__(kNT) k_results_to_host(const uint8_t* __restrict__ flags, int n_flags,
+                                                         uint8_t* flags_host, const float* __restrict__ preds,
+                                                         int n_preds, float* preds_host) {
+    pdl_enter();
+    const int stride = gridDim.x * blockDim.x;
+    const int t0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (flags_host) {
+        const bool vec = ((reinterpret_cast<uintptr_t>(flags_host) | reinterpret_cast<uintptr_t>(flags)) & 15) == 0;
+        const int n16 = vec ? n_flags / 16 : 0;
+        for (int i = t0; i < n16; i += stride)
+            reinterpret_cast<uint4*>(flags_host)[i] = reinterpret_cast<const uint4*>(flags)[i];
+        for (int i = n16 * 16 + t0; i < n_flags; i += stride) flags_host[i] = flags[i];
+    }
+    if (preds_host) {
+        const bool vec = ((reinterpret_cast<uintptr_t>(preds_host) | reinterpret_cast<uintptr_t>(preds)) & 15) == 0;
+        const int n4 = vec ? n_preds / 4 : 0;
+        for (int i = t0; i < n4; i += stride)
+            reinterpret_cast<float4*>(preds_host)[i] = reinterpret_cast<const float4*>(preds)[i];
+        for (int i = n4 * 4 + t0; i < n_preds; i += stride) preds_host[i] = preds[i];
+    }
+}
+}  // namespace
+
+void launch_results_to_host(cudaStream_t st, const uint8_t* flags, int n_flags, uint8_t* flags_host,
+                            const float* preds, int n_preds, float* preds_host) {
+    const int bytes = (flags_host ? n_flags : 0) + (preds_host ? n_preds * 4 : 0);
+    const int blocks = std::max(1, std::min(148, (bytes / 16 + kNT - 1) / kNT));
+    pdl_launch(k_results_to_host, dim3(blocks), dim3(kNT), 0, st, flags, n_flags, flags_host, preds, n_preds,
+               preds_host);
+}
+
+namespace {
 // 8 independent FFMA chains per thread; a and b come from memory so nothing
 // folds, the result is stored only under a never-true runtime condition.
 __global__ void __launch_bounds__(512) k_ffma_peak(const float* __restrict__ ab, int iters, float* sink) {

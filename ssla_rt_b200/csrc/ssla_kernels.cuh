@@ -359,6 +359,11 @@ void launch_write_slots(cudaStream_t st, int n, int P, const int* rec_off, const
 void launch_fill_clk(cudaStream_t st, int P, const int* rec_off, const unsigned long long* stamps,
                      unsigned long long* const* clks);
 void launch_stamp(cudaStream_t st, unsigned long long* dst);
+// Copies a drain's flags and decoded predictions into mapped pinned host
+// memory from a kernel (either destination may be null): host pointers as
+// their device aliases (cudaHostGetDevicePointer).
+void launch_results_to_host(cudaStream_t st, const uint8_t* flags, int n_flags, uint8_t* flags_host,
+                            const float* preds, int n_preds, float* preds_host);
 // Measured FP32 FMA throughput of the current device, TFLOP/s.
 double measure_ffma_peak();
 // Mismatches of ssla_rcp_rn against IEEE round-to-nearest over every float

@@ -193,11 +193,13 @@ def test_config1_full_size(oracle_mod, stub_dir):
     assert_engine_equals_oracle(eng, oracles, second, abi.LAYOUT_HYBRID)
 
 
-def test_pipelined_host_drains_match_sync(stub_dir):
+@pytest.mark.parametrize("outputs", ["pinned", "pageable"])
+def test_pipelined_host_drains_match_sync(stub_dir, outputs):
     """ssla_engine_drain_host_async (copies on the engine's copy stream,
-    two device buffers in turn, results copied back on the caller's stream)
-    gives, drain for drain, the flags, predictions and state of the
-    synchronous host path, with several drains in flight."""
+    two device buffers in turn; results written into pinned outputs by a
+    kernel chained to the drain, or copied back into pageable ones) gives,
+    drain for drain, the flags, predictions and state of the synchronous
+    host path, with several drains in flight."""
     d = stub_dir(64, 80, 1, 4)
     parts = E.split_partitions(E.config_events(1, n=40_000, seed=31), 4)
     base = np.ascontiguousarray(np.concatenate(parts))
@@ -212,9 +214,9 @@ def test_pipelined_host_drains_match_sync(stub_dir):
     ins = [torch.from_numpy(base.copy()).pin_memory() for _ in range(steps)]
     for k in range(steps):
         ins[k][:, 0] += span * k
-    flags = [torch.zeros(n, dtype=torch.uint8).pin_memory() for _ in range(steps)]
-    preds = [torch.zeros(tuple(sync.preds_dec_all().shape), dtype=torch.float32).pin_memory()
-             for _ in range(steps)]
+    pin = (lambda t: t.pin_memory()) if outputs == "pinned" else (lambda t: t)
+    flags = [pin(torch.zeros(n, dtype=torch.uint8)) for _ in range(steps)]
+    preds = [pin(torch.zeros(tuple(sync.preds_dec_all().shape), dtype=torch.float32)) for _ in range(steps)]
     stream = torch.cuda.current_stream()
     for k in range(steps):
         pipe.drain_host_async(ins[k], off, flags[k], preds[k], stream=stream)
