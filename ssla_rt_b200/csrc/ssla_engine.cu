@@ -1143,9 +1143,18 @@ struct Engine {
     }
 
     // Uploads the partition offsets into ws.ev_off through the next pinned
-    // slot (waits only if that slot's previous copy has not run yet).
+    // slot (waits only if that slot's previous copy has not run yet).  The
+    // same offsets as the last upload on the same stream are already there
+    // (ws.ev_off has no other writer), so the copy is skipped.
+    std::vector<int> off_last;
+    cudaStream_t off_last_st = nullptr;
     void upload_offsets(const int* off, cudaStream_t st) {
         const int P = g.P;
+        if (st == off_last_st && static_cast<int>(off_last.size()) == P + 1 &&
+            std::equal(off_last.begin(), off_last.end(), off))
+            return;
+        off_last.assign(off, off + P + 1);
+        off_last_st = st;
         const int slot = off_slot;
         off_slot = (off_slot + 1) % kOffSlots;
         SSLA_CK(cudaEventSynchronize(off_done[slot]));
