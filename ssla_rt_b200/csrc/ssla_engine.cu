@@ -273,7 +273,7 @@ void run_layers(cudaStream_t st, const Geo& g, Workspace& w, const PartState* d_
     float* R_first = w.R_A.as<float>();        // residual rows of first layers
     float* R_second = w.R_B.as<float>();       // residual rows of second layers
     const int l0 = (w.s_first == 0) ? 1 : 4;
-    if (l0 < 4 && l_begin <= l0) SSLA_CK(cudaMemsetAsync(w.work.p, 0, sizeof(int) * 8, st));
+    // the layer-1..3 work counters were zeroed by k_flag_s0 in the drain's front
     for (int l = std::max(l0, l_begin); l < l_end; ++l) {
         const int s = l / 2, half = l % 2;
         const int* range = (s == 0) ? w.ev_off.as<int>() : w.off[s].as<int>();
@@ -1220,6 +1220,7 @@ struct Engine {
         ga.n_gates = (s_last >= 3) ? 4 : 2;
         launch_gates(st, ga);
         check_launch("k_gates");
+        fa.zero_work = ws.work.as<int>();
         launch_flag_s0(st, fa);                    // layer-1 output flags into the stage-0 lists
         check_launch("k_flag_s0");
         prof.mark("gates", 2, st);

@@ -243,10 +243,13 @@ __global__ void __launch_bounds__(kNT) k_filter_tiles(FilterArgs a) {
 // whose event reaches stage 1 (its layer-1 output is consumed), so the
 // layer-1 scan reads the flag with the entry instead of loading the event's
 // flag byte behind it.  k_filter leaves the bit clear at stage 0.  One warp
-// per (partition, tile, segment) slot, grid-stride.
+// per (partition, tile, segment) slot, grid-stride.  Also zeroes the
+// stage-0/1 scans' work counters (no memset node in the launch chain).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kNT) k_flag_s0(FilterArgs a) {
     pdl_enter();
+    // the drain's layer-1..3 scans take work items from these counters
+    if (a.zero_work && blockIdx.x == 0 && threadIdx.x < 8) a.zero_work[threadIdx.x] = 0;
     const int lane = threadIdx.x & 31;
     const int ntiles = a.g.tx[0] * a.g.ty[0];
     const long long per_p = static_cast<long long>(ntiles) * a.g.nseg[0];

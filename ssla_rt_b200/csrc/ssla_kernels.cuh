@@ -19,6 +19,7 @@ struct FilterArgs {
     uint8_t out_bit;         // reach bit meaning "second-layer output needed"
     int ev_row_lo, ev_row_hi;  // stage-0 pixel rows holding the drain's events (hi <= lo: all)
     int trow0;               // first tile row of the launch (set by launch_filter)
+    int* zero_work;          // k_flag_s0: the stage-0/1 scans' 8 work counters, zeroed (may be null)
 };
 
 struct GateArgs {
