@@ -33,7 +33,7 @@ constexpr int kTile = 8;            // tile side (cells) of tile lists
 constexpr int kMaxTileCols = 64;    // tiles per row (stage-0 width <= 512)
 constexpr int kMaxParts = 1024;
 constexpr uint32_t kInvalidXY = 0xFFFFFFFFu;
-constexpr int kCompactTile = 4096;  // events per compaction tile
+constexpr int kCompactTile = 4096;  // events per compaction tile at most (512 at least)
 
 enum : uint8_t { F_VALID = 1, F_R1 = 2, F_R2 = 4, F_R3 = 8, F_R4 = 16, F_FOREIGN = 32 };
 enum { LAYOUT_DECOMP = 0, LAYOUT_HYBRID = 1 };

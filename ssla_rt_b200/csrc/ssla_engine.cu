@@ -165,7 +165,7 @@ void make_geo(Geo& g, int H, int W, int P, int layout, int window, int ncls) {
 // records and residuals, sized from proven upper bounds of the events that
 // can reach each stage.
 struct Workspace {
-    int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, n_active = 0;
+    int P = 0, mpe = 0, n_max = 0, s_first = 0, tiles_per_part = 1, ctile = kCompactTile, n_active = 0;
     long long cap_part[5] = {0}, cap[5] = {0};
     DevBuf ev, ev_off, ev_xy, rflags, E[5], off[5], count, tilecnt, tilebase;
     DevBuf tl[4], tl_cnt[4], S_A, S_B, QH, R_A, R_B, X, C, head_dec, head_raw, slot_feat, stamps, work;
@@ -193,7 +193,11 @@ struct Workspace {
         for (int s = 0; s < 4; ++s)
             g.nseg[s] = s < s_first ? 0 : static_cast<int>((cap_part[s] + g.seg - 1) / g.seg);
         for (int s = 0; s < 5; ++s) g.cap[s] = static_cast<int>(s < s_first ? 0 : cap[s]);
-        tiles_per_part = static_cast<int>((mpe + kCompactTile - 1) / kCompactTile);
+        // compaction tiles: about four per SM over the chunk (one CTA walks a
+        // tile in order, so few large tiles leave SMs idle), 512..4096 events
+        ctile = static_cast<int>(std::min<long long>(
+            kCompactTile, std::max<long long>(512, ((static_cast<long long>(P) * mpe / 592 + 255) / 256) * 256)));
+        tiles_per_part = static_cast<int>((mpe + ctile - 1) / ctile);
         if (tiles_per_part < 1) tiles_per_part = 1;
 
         ev.alloc(static_cast<size_t>(n_max) * sizeof(float4));
@@ -1226,7 +1230,7 @@ struct Engine {
         prof.mark("gates", 2, st);
         // stage lists
         CompactArgs ca{};
-        ca.g = g; ca.s_first = 0; ca.tiles_per_part = ws.tiles_per_part; ca.ev_off = ws.ev_off.as<int>();
+        ca.g = g; ca.s_first = 0; ca.tiles_per_part = ws.tiles_per_part; ca.ctile = ws.ctile; ca.ev_off = ws.ev_off.as<int>();
         ca.rflags = ws.rflags.as<uint8_t>(); ca.ev_xy = ws.ev_xy.as<uint32_t>();
         ca.tilecnt = ws.tilecnt.as<int>(); ca.tilebase = ws.tilebase.as<int>();
         for (int s = 0; s <= 4; ++s) { ca.E[s] = ws.E[s].as<StageEntry>(); ca.off[s] = ws.off[s].as<int>(); }
@@ -1367,7 +1371,7 @@ struct DrainN {
         launch_gates_s2(st, ga);
         check_launch("k_gates_s2");
         CompactArgs ca{};
-        ca.g = g; ca.s_first = 2; ca.tiles_per_part = w.tiles_per_part; ca.ev_off = w.ev_off.as<int>();
+        ca.g = g; ca.s_first = 2; ca.tiles_per_part = w.tiles_per_part; ca.ctile = w.ctile; ca.ev_off = w.ev_off.as<int>();
         ca.rflags = w.rflags.as<uint8_t>(); ca.ev_xy = w.ev_xy.as<uint32_t>();
         ca.tilecnt = w.tilecnt.as<int>(); ca.tilebase = w.tilebase.as<int>();
         for (int s = 0; s <= 4; ++s) { ca.E[s] = w.E[s].as<StageEntry>(); ca.off[s] = w.off[s].as<int>(); }

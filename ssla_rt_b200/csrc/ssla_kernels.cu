@@ -634,8 +634,8 @@ __global__ void __launch_bounds__(32) k_gates_s2(Gate2Args a) {
 __global__ void __launch_bounds__(kNT) k_compact_count(CompactArgs a) {
     pdl_enter();
     const int p = blockIdx.x, t = blockIdx.y;
-    const int lo = a.ev_off[p] + t * kCompactTile;
-    const int hi = min(a.ev_off[p + 1], lo + kCompactTile);
+    const int lo = a.ev_off[p] + t * a.ctile;
+    const int hi = min(a.ev_off[p + 1], lo + a.ctile);
     int c[4] = {0, 0, 0, 0};
     for (int i = lo + static_cast<int>(threadIdx.x); i < hi; i += kNT) {
         const uint8_t f = a.rflags[i];
@@ -711,8 +711,8 @@ __global__ void __launch_bounds__(kNT) k_compact_scan(CompactArgs a) {
 __global__ void __launch_bounds__(kNT) k_compact_scatter(CompactArgs a) {
     pdl_enter();
     const int p = blockIdx.x, t = blockIdx.y;
-    const int lo = a.ev_off[p] + t * kCompactTile;
-    const int hi = min(a.ev_off[p + 1], lo + kCompactTile);
+    const int lo = a.ev_off[p] + t * a.ctile;
+    const int hi = min(a.ev_off[p + 1], lo + a.ctile);
     if (lo >= hi) return;
     __shared__ int wtot[kNT / 32][4];
     __shared__ int run[4];

@@ -51,6 +51,7 @@ struct CompactArgs {
     Geo g;
     int s_first;             // lists s_first+1 .. 4 are built
     int tiles_per_part;
+    int ctile;               // events per compaction tile
     const int* ev_off;       // [P+1]
     const uint8_t* rflags;
     const uint32_t* ev_xy;
