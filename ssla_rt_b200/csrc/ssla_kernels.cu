@@ -398,6 +398,9 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
     };
     int2 ent1 = make_int2(0, 0), ent2 = make_int2(0, 0);
     bool val1 = false, val2 = false, have1 = false, have2 = false, own1 = false;
+    __shared__ int2 o_ent[64];               // own entries staged for the next gate windows
+    __shared__ float4 o_ev[64];
+    int o_n = 0;
     float4 ev1 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (warp == 0) {
         next_entries(ent1, val1, have1);
@@ -410,16 +413,42 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
         // ---- phase 1: gates and previous timestamps, buffer the own events
         if (warp == 0) {
             int n = 0;
-            while (have1 && n <= kGateBuf - 32) {
-                const int2 ent = ent1;
-                const float4 e = ev1;
-                const bool own = own1;
-                // advance the pipeline: window w+1 <- w+2 (event load issued), w+2 <- next
-                ent1 = ent2; val1 = val2; have1 = have2;
-                own1 = have1 && is_own(ent1, val1);
-                ev1 = own1 ? a.ev[ent1.x] : make_float4(0.f, 0.f, 0.f, 0.f);
-                if (have1) next_entries(ent2, val2, have2);
-                else have2 = false;
+            while ((have1 || o_n > 0) && n <= kGateBuf - 32) {
+                // stage the block's own entries (and their events, loaded a
+                // window ahead) until a full window of them is ready: the
+                // list's halo entries never reach the ordered gate window
+                while (o_n < 32 && have1) {
+                    const int2 ce = ent1;
+                    const float4 cv = ev1;
+                    const bool co = own1;
+                    // advance the pipeline: window w+1 <- w+2 (event load issued), w+2 <- next
+                    ent1 = ent2; val1 = val2; have1 = have2;
+                    own1 = have1 && is_own(ent1, val1);
+                    ev1 = own1 ? a.ev[ent1.x] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (have1) next_entries(ent2, val2, have2);
+                    else have2 = false;
+                    const unsigned cm = __ballot_sync(0xffffffffu, co);
+                    if (co) {
+                        const int pos = o_n + __popc(cm & lanemask_lt());
+                        o_ent[pos] = ce;
+                        o_ev[pos] = cv;
+                    }
+                    o_n += __popc(cm);
+                }
+                __syncwarp();
+                const int nw = min(o_n, 32);
+                const bool own = lane < nw;
+                const int2 ent = own ? o_ent[lane] : make_int2(0, 0);
+                const float4 e = own ? o_ev[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+                {   // the rest of the staged entries to the front
+                    const bool mv = lane < o_n - nw;
+                    const int2 te = mv ? o_ent[nw + lane] : make_int2(0, 0);
+                    const float4 tv = mv ? o_ev[nw + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    __syncwarp();
+                    if (mv) { o_ent[lane] = te; o_ev[lane] = tv; }
+                    __syncwarp();
+                    o_n -= nw;
+                }
                 const unsigned om = __ballot_sync(0xffffffffu, own);
                 if (om == 0u) continue;
                 const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
@@ -473,7 +502,7 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                 }
                 n += __popc(om);
             }
-            if (lane == 0) { b_n = n; b_done = have1 ? 0 : 1; }
+            if (lane == 0) { b_n = n; b_done = (have1 || o_n > 0) ? 0 : 1; }
             // per-pixel list offsets of this buffer
             int c_lo = pc[2 * lane], c_hi = pc[2 * lane + 1];
             int incl = c_lo + c_hi;
