@@ -366,67 +366,97 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
     const int tile = by * a.g.tx[0] + bx;     // s0 tiles are the s3 blocks
     const int n_p = a.ev_off[p + 1] - a.ev_off[p];
     const int nseg = min((n_p + a.g.seg - 1) / a.g.seg, a.g.nseg[0]);
-    // Phase-1 window pipeline (warp 0): the entries of window w+2 and the
-    // events of window w+1 are loaded while window w is processed.
-    int seg = 0, j0 = 0, cnt = -1;
-    const int2* lst = nullptr;
-    auto next_entries = [&](int2& ent, bool& valid, bool& have) {
-        have = false;
-        valid = false;
-        ent = make_int2(0, 0);
-        while (seg < nseg) {
-            if (cnt < 0) {
-                const size_t slot = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0] + seg;
-                cnt = a.tl0_cnt[slot];
-                lst = a.tl0 + slot * a.g.seg;
-                j0 = 0;
-            }
-            if (j0 < cnt) {
-                const int j = j0 + lane;
-                if (j < cnt) { ent = lst[j]; valid = true; }
-                j0 += 32;
-                have = true;
-                return;
-            }
-            ++seg;
-            cnt = -1;
-        }
-    };
-    auto is_own = [&](int2 ent, bool valid) {
-        const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
-        return valid && (x0 >> 3) == bx && (y0 >> 3) == by;
-    };
-    int2 ent1 = make_int2(0, 0), ent2 = make_int2(0, 0);
-    bool val1 = false, val2 = false, have1 = false, have2 = false, own1 = false;
+    // Phase 1 reads the block's tile list in chunks of kGateChunk entries,
+    // loaded by the whole CTA together with the events of the block's own
+    // entries (one round trip for the entries, one for the events); warp 0
+    // stages the own entries and runs the ordered gate windows from shared
+    // memory.  The list arrives as segments; their counts are read
+    // kGateChunk at a time and each chunk entry finds its segment by binary
+    // search over their prefix.
+    constexpr int kGateChunk = kGateNT;
+    __shared__ int2 ch_ent[kGateChunk];
+    __shared__ float4 ch_ev[kGateChunk];
+    __shared__ int sw_pre[kGateChunk + 1];   // exclusive prefix of the window's segment counts
+    __shared__ int sw_wsum[kGateNT / 32];
+    __shared__ int ch_n, ch_pos, ph1_act;
     __shared__ int2 o_ent[64];               // own entries staged for the next gate windows
     __shared__ float4 o_ev[64];
-    int o_n = 0;
-    float4 ev1 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (warp == 0) {
-        next_entries(ent1, val1, have1);
-        own1 = is_own(ent1, val1);
-        if (own1) ev1 = a.ev[ent1.x];
-        next_entries(ent2, val2, have2);
-    }
+    const size_t slot0 = (static_cast<size_t>(p) * ntiles + tile) * a.g.nseg[0];
+    int sw0 = -kGateChunk, sw_tot = 0, gp = 0;   // CTA-uniform walk state
+    bool list_done = false;
+    auto is_own = [&](int2 ent) {
+        const int x0 = ent.y & 0xFFFF, y0 = (ent.y >> 16) & 0x7FFF;
+        return (x0 >> 3) == bx && (y0 >> 3) == by;
+    };
+    // all threads: the next chunk into ch_ent / ch_ev (ch_n = 0 once the list is done)
+    auto load_chunk = [&]() {
+        while (!list_done && gp >= sw_tot) {
+            sw0 += kGateChunk;
+            if (sw0 >= nseg) {
+                list_done = true;
+                break;
+            }
+            const int sg = sw0 + tid;
+            int v = (sg < nseg) ? a.tl0_cnt[slot0 + sg] : 0;
+            const int c = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += y;
+            }
+            if (lane == 31) sw_wsum[warp] = v;
+            __syncthreads();
+            int wo = 0, tot = 0;
+#pragma unroll
+            for (int w = 0; w < kGateNT / 32; ++w) {
+                wo += (w < warp) ? sw_wsum[w] : 0;
+                tot += sw_wsum[w];
+            }
+            sw_pre[tid] = wo + v - c;
+            if (tid == 0) sw_pre[kGateChunk] = tot;
+            __syncthreads();
+            sw_tot = tot;
+            gp = 0;
+        }
+        const int nld = list_done ? 0 : min(kGateChunk, sw_tot - gp);
+        if (tid < nld) {
+            const int q = gp + tid;
+            int lo = 0, hi = kGateChunk;          // sw_pre[lo] <= q < sw_pre[hi]
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (sw_pre[mid] <= q) lo = mid;
+                else hi = mid;
+            }
+            const int2 ent = a.tl0[(slot0 + sw0 + lo) * a.g.seg + (q - sw_pre[lo])];
+            ch_ent[tid] = ent;
+            ch_ev[tid] = is_own(ent) ? a.ev[ent.x] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        gp += nld;
+        if (tid == 0) {
+            ch_n = nld;
+            ch_pos = 0;
+        }
+        __syncthreads();
+    };
+    int o_n = 0;                             // warp 0: staged own entries
+    enum { kNeedChunk = 0, kBufFull = 1, kListDone = 2 };
+    load_chunk();
 
     for (;;) {
         // ---- phase 1: gates and previous timestamps, buffer the own events
-        if (warp == 0) {
-            int n = 0;
-            while ((have1 || o_n > 0) && n <= kGateBuf - 32) {
-                // stage the block's own entries (and their events, loaded a
-                // window ahead) until a full window of them is ready: the
-                // list's halo entries never reach the ordered gate window
-                while (o_n < 32 && have1) {
-                    const int2 ce = ent1;
-                    const float4 cv = ev1;
-                    const bool co = own1;
-                    // advance the pipeline: window w+1 <- w+2 (event load issued), w+2 <- next
-                    ent1 = ent2; val1 = val2; have1 = have2;
-                    own1 = have1 && is_own(ent1, val1);
-                    ev1 = own1 ? a.ev[ent1.x] : make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (have1) next_entries(ent2, val2, have2);
-                    else have2 = false;
+        int nb = 0;                          // warp 0: events buffered for phase 2
+        int act = kListDone;
+        for (;;) {
+          if (warp == 0) {
+            int cp = ch_pos;
+            const int cn = ch_n;
+            for (;;) {
+                // stage the chunk's own entries until a full window is ready
+                while (o_n < 32 && cp < cn) {
+                    const int j = cp + lane;
+                    const int2 ce = (j < cn) ? ch_ent[j] : make_int2(0, 0);
+                    const bool co = j < cn && is_own(ce);
+                    const float4 cv = co ? ch_ev[j] : make_float4(0.f, 0.f, 0.f, 0.f);
                     const unsigned cm = __ballot_sync(0xffffffffu, co);
                     if (co) {
                         const int pos = o_n + __popc(cm & lanemask_lt());
@@ -434,8 +464,12 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                         o_ev[pos] = cv;
                     }
                     o_n += __popc(cm);
+                    cp += 32;
                 }
                 __syncwarp();
+                if (nb > kGateBuf - 32) { act = kBufFull; break; }
+                if (o_n < 32 && cp >= cn && !list_done) { act = kNeedChunk; break; }
+                if (o_n == 0) { act = kListDone; break; }
                 const int nw = min(o_n, 32);
                 const bool own = lane < nw;
                 const int2 ent = own ? o_ent[lane] : make_int2(0, 0);
@@ -491,7 +525,7 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                     if (in3) f |= F_R3;
                     if (in3 && pass3) f |= F_R4;
                     a.rflags[k] = f;
-                    const int pos = n + __popc(om & lanemask_lt());
+                    const int pos = nb + __popc(om & lanemask_lt());
                     b_k[pos] = k;
                     b_pix[pos] = static_cast<unsigned char>(pix);
                     b_rank[pos] = static_cast<unsigned char>(rank);
@@ -500,9 +534,20 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
                     b_p[pos] = e.w;
                     b_pass0[pos] = pass0 ? 1 : 0;
                 }
-                n += __popc(om);
+                nb += __popc(om);
             }
-            if (lane == 0) { b_n = n; b_done = (have1 || o_n > 0) ? 0 : 1; }
+            if (lane == 0) { ch_pos = cp; ph1_act = act; }
+          }
+          __syncthreads();
+          act = ph1_act;
+          if (act == kNeedChunk) {
+              load_chunk();
+              continue;
+          }
+          break;
+        }
+        if (warp == 0) {
+            if (lane == 0) { b_n = nb; b_done = (act == kListDone) ? 1 : 0; }
             // per-pixel list offsets of this buffer
             int c_lo = pc[2 * lane], c_hi = pc[2 * lane + 1];
             int incl = c_lo + c_hi;
