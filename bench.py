@@ -32,6 +32,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -155,6 +156,18 @@ class ClockSampler:
                  "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+
+    def wait_ready(self, timeout_s: float = 10.0) -> None:
+        """Returns once nvidia-smi has written its first sample (its start-up
+        can take over a second with several GPUs), or after timeout_s."""
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < timeout_s:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    return
+            except OSError:
+                return
+            time.sleep(0.05)
 
     def stop(self, device_index: int) -> dict:
         if self.proc is None:
@@ -580,7 +593,8 @@ STRIP_BAND = 16                  # exact mode: band rows (2 stage-3 rows)
 STRIP_PARITY_EVENTS = 200_000    # prefix of the stream checked against one sensor
 
 
-def strips_measure(args, rank: int, world: int, local: int, steps: int, warmup: int) -> dict:
+def strips_measure(args, rank: int, world: int, local: int, steps: int, warmup: int,
+                   min_timed_s: float = 0.0) -> dict:
     """Strong scaling of config 3: the one 10M-event stream split into `world`
     horizontal strips (ssla_rt_b200/strips.py), one per rank, drained in
     stream order.  value = the stream's events / the slowest rank's device
@@ -666,13 +680,25 @@ def strips_measure(args, rank: int, world: int, local: int, steps: int, warmup: 
             elif c1 > c0:
                 eng.drain(ev[c0:c1], [0, c1 - c0], stream=stream)
 
-    for _ in range(warmup):
+    for i in range(warmup):
         ev[:, 0] += span
+        if i == warmup - 1:
+            wa = torch.cuda.Event(enable_timing=True)
+            wb = torch.cuda.Event(enable_timing=True)
+            wa.record(stream)
         one_pass()
+    if warmup > 0:
+        wb.record(stream)
     torch.cuda.synchronize(dev)
+    if min_timed_s > 0.0 and warmup > 0:
+        # enough passes that the clock samples fall inside the timed region
+        # (the same count on every rank: each pass has a barrier)
+        need = int(math.ceil(min_timed_s * 1e3 / max(wa.elapsed_time(wb), 1e-3)))
+        steps = int(max_over_ranks(float(min(max(steps, need), 400))))
     clocks = ClockSampler()
     clocks.start()
-    time.sleep(0.3)
+    clocks.wait_ready()
+    time.sleep(0.2)
     launches = 0
     total_ms = 0.0
     barrier()
@@ -1238,7 +1264,7 @@ def main() -> int:
     # ---- config 3 in N strips (the north star's strong-scaling target) ----
     strips_line = None
     if not args.no_strips:
-        strips_line = strips_measure(args, rank, world, local, max(2, min(args.steps, 5)), 3)
+        strips_line = strips_measure(args, rank, world, local, max(2, min(args.steps, 5)), 3, min_timed_s=0.6)
 
     line = None
     if rank == 0:
