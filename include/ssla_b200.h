@@ -463,6 +463,14 @@ int  ssla_measure_fp32_peak(int device, double* tflops_out);
  * null) receives the lowest mismatching bit pattern, 0xFFFFFFFF if none. */
 int  ssla_selftest_reciprocal(int device, unsigned long long* mismatches, unsigned* first_bad);
 
+/* Self-test of the packed sigmoid the stage-0/1 scans and the stage-2/3
+ * GEMM epilogue use (two sigmoids per call with paired FP32 operations):
+ * compares it on `device`, bit for bit, with two calls of the scalar device
+ * sigmoid for every float x (pairs (x, -x)).  *mismatches = 0 means the
+ * packed form changes no result; *first_bad (may be null) receives the
+ * lowest mismatching bit pattern of the first component, 0xFFFFFFFF if none. */
+int  ssla_selftest_sigmoid_pair(int device, unsigned long long* mismatches, unsigned* first_bad);
+
 /* Portable exp used by every sigmoid / SiLU / box decode of the engine
  * (the device code's exact twin), for tests on hosts without a GPU. */
 float ssla_expf_host(float x);

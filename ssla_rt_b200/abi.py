@@ -116,6 +116,7 @@ EXPORTED = (
     "ssla_engine_read_state", "ssla_engine_write_state", "ssla_engine_state_ptr",
     "ssla_engine_info", "ssla_s2s3_drain_n_multi", "ssla_s2s3_drain_n",
     "ssla_engine_set_profiling", "ssla_engine_phase_times", "ssla_measure_fp32_peak", "ssla_selftest_reciprocal",
+    "ssla_selftest_sigmoid_pair",
     "ssla_expf_host", "ssla_sigmoidf_host", "ssla_last_error", "ssla_version", "ssla_s2s3_gate_codes_noalloc",
     "ssla_engine_drain_records", "ssla_engine_step", "ssla_engine_step_latency",
     "ssla_engine_live_start", "ssla_engine_live_join", "ssla_engine_live_latency",

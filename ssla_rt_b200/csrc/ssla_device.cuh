@@ -191,4 +191,43 @@ __host__ __device__ __forceinline__ float ssla_sigmoidf(float x) {
 #endif
 }
 
+#ifdef __CUDACC__
+// Two ssla_sigmoidf evaluations with packed FP32 operations: every component
+// of __ffma2_rn / __fadd2_rn / __fmul2_rn is one IEEE fmaf / fadd / fmul
+// rounded to nearest, the operations of ssla_sigmoidf in the same order, so
+// the results are bit-identical to two scalar calls (checked over every
+// float pair component by ssla_selftest_sigmoid_pair).  fmaf(-n, c, r) is
+// written fmaf(n, -c, r), the same product.  The scale 2^n comes from the
+// bits of big = 1.5 * 2^23 + n, which are 0x4B400000 + n: shifted left by
+// 23 the constant part leaves 32 bits, so (bits << 23) + (127 << 23) is
+// (n + 127) << 23 modulo 2^32, one integer multiply-add per component.
+__device__ __forceinline__ float2 ssla_sigmoidf2(float2 x) {
+    const float2 t = make_float2(fminf(fmaxf(-x.x, -17.0f), 87.0f), fminf(fmaxf(-x.y, -17.0f), 87.0f));
+    const float2 big = __ffma2_rn(t, make_float2(1.44269502f, 1.44269502f),
+                                  make_float2(12582912.0f, 12582912.0f));
+    const float2 n = __fadd2_rn(big, make_float2(-12582912.0f, -12582912.0f));
+    float2 r = __ffma2_rn(n, make_float2(-0.693115234375f, -0.693115234375f), t);
+    r = __ffma2_rn(n, make_float2(-3.19461833e-05f, -3.19461833e-05f), r);
+    float2 p = __ffma2_rn(make_float2(1.38368458e-03f, 1.38368458e-03f), r,
+                          make_float2(8.37481581e-03f, 8.37481581e-03f));
+    p = __ffma2_rn(p, r, make_float2(4.16682251e-02f, 4.16682251e-02f));
+    p = __ffma2_rn(p, r, make_float2(1.66664198e-01f, 1.66664198e-01f));
+    p = __ffma2_rn(p, r, make_float2(4.99999911e-01f, 4.99999911e-01f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    const float2 s = make_float2(__uint_as_float((__float_as_uint(big.x) << 23) + 0x3F800000u),
+                                 __uint_as_float((__float_as_uint(big.y) << 23) + 0x3F800000u));
+    const float2 y = __fadd2_rn(make_float2(1.0f, 1.0f), __fmul2_rn(p, s));
+    float qx, qy;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(qx) : "f"(y.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(qy) : "f"(y.y));
+    const float2 q = make_float2(qx, qy);
+    const float2 e = __ffma2_rn(make_float2(-y.x, -y.y), q, make_float2(1.0f, 1.0f));
+    float2 out = __ffma2_rn(q, e, q);
+    if (x.x != x.x) out.x = x.x;
+    if (x.y != x.y) out.y = x.y;
+    return out;
+}
+#endif
+
 }  // namespace ssla

@@ -1985,6 +1985,15 @@ int ssla_selftest_reciprocal(int device, unsigned long long* mismatches, unsigne
     });
 }
 
+int ssla_selftest_sigmoid_pair(int device, unsigned long long* mismatches, unsigned* first_bad) {
+    if (!mismatches) { ssla::g_last_error = "null argument"; return SSLA_ERR_ARG; }
+    return ssla::guarded([&] {
+        ssla::DeviceGuard dg(device);
+        *mismatches = ssla::check_sigmoid_pair(first_bad);
+        return SSLA_OK;
+    });
+}
+
 int ssla_s2s3_drain_n_multi(const HybridS2S3Config* cfg, const HybridInputRec* const* rings, const int* ns,
                             HybridS2S3OutputSlot* const* outs, unsigned long long* const* batch_clks,
                             void* stream) {

@@ -1181,7 +1181,7 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
                 if (part == 2) {
 #pragma unroll
                     for (int j = 0; j < OUT / 2; ++j)
-                        acc[j] = make_float2(ssla_sigmoidf(acc[j].x), ssla_sigmoidf(acc[j].y));
+                        acc[j] = ssla_sigmoidf2(acc[j]);
                 }
                 const int col = (part == 2) ? 0 : OUT;
 #pragma unroll
@@ -1922,8 +1922,9 @@ __global__ void __launch_bounds__(kNT) k_gemm(GemmArgs a) {
                     *reinterpret_cast<float4*>(a.R + static_cast<size_t>(xr) * OUT2 + col) = v;
                 } else {
                     if (part == 2) {
-                        v.x = ssla_sigmoidf(v.x); v.y = ssla_sigmoidf(v.y);
-                        v.z = ssla_sigmoidf(v.z); v.w = ssla_sigmoidf(v.w);
+                        const float2 s01 = ssla_sigmoidf2(make_float2(v.x, v.y));
+                        const float2 s23 = ssla_sigmoidf2(make_float2(v.z, v.w));
+                        v = make_float4(s01.x, s01.y, s23.x, s23.y);
                     }
                     *reinterpret_cast<float4*>(a.S + static_cast<size_t>(xr) * srow_stride + jcol) = v;
                 }
@@ -2428,7 +2429,45 @@ __global__ void __launch_bounds__(256) k_rcp_check(uint32_t lo, uint32_t hi, uns
     }
     if (n) atomicAdd(bad, n);
 }
+// ssla_sigmoidf2 against two ssla_sigmoidf calls: every float bit pattern u
+// in [lo, hi) as the first component, u ^ 0x80000000 (the same magnitude,
+// other sign) as the second; results compared bit for bit.
+__global__ void __launch_bounds__(256) k_sigmoid2_check(uint32_t lo, uint32_t hi, unsigned long long* bad,
+                                                        unsigned* first) {
+    unsigned long long n = 0;
+    for (uint64_t u = lo + static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < hi;
+         u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t b0 = static_cast<uint32_t>(u), b1 = b0 ^ 0x80000000u;
+        const float2 x = make_float2(__uint_as_float(b0), __uint_as_float(b1));
+        const float2 s = ssla_sigmoidf2(x);
+        if (__float_as_uint(s.x) != __float_as_uint(ssla_sigmoidf(x.x)) ||
+            __float_as_uint(s.y) != __float_as_uint(ssla_sigmoidf(x.y))) {
+            ++n;
+            atomicMin(first, b0);
+        }
+    }
+    if (n) atomicAdd(bad, n);
+}
 }  // namespace
+
+unsigned long long check_sigmoid_pair(unsigned* first_bad) {
+    unsigned long long* d = nullptr;
+    if (cudaMalloc(&d, 16) != cudaSuccess) throw std::runtime_error("cudaMalloc failed");
+    unsigned long long init[2] = {0, 0xFFFFFFFFull};
+    cudaMemcpy(d, init, sizeof init, cudaMemcpyHostToDevice);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // the 2^31 positive patterns, each paired with its negative twin
+    k_sigmoid2_check<<<sms * 8, 256>>>(0x00000000u, 0x80000000u, d, reinterpret_cast<unsigned*>(d + 1));
+    const cudaError_t err = cudaDeviceSynchronize();
+    unsigned long long out[2] = {0, 0};
+    cudaMemcpy(out, d, sizeof out, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (err != cudaSuccess) throw std::runtime_error(cudaGetErrorString(err));
+    if (first_bad) *first_bad = static_cast<unsigned>(out[1]);
+    return out[0];
+}
 
 unsigned long long check_reciprocal(unsigned* first_bad) {
     unsigned long long* d = nullptr;

@@ -371,5 +371,8 @@ double measure_ffma_peak();
 // Mismatches of ssla_rcp_rn against IEEE round-to-nearest over every float
 // in [1, 2^126) (the first one's bit pattern in *first_bad, 0xFFFFFFFF if none).
 unsigned long long check_reciprocal(unsigned* first_bad);
+// ssla_sigmoidf2 against two ssla_sigmoidf over every float (first component
+// u in [0, 2^31), second u ^ 2^31); mismatches and the first one's u.
+unsigned long long check_sigmoid_pair(unsigned* first_bad);
 
 }  // namespace ssla

@@ -83,6 +83,7 @@ def load_library() -> C.CDLL:
         "ssla_engine_phase_times": (i, [vp, vp, i, C.POINTER(C.c_int)]),
         "ssla_measure_fp32_peak": (i, [i, C.POINTER(C.c_double)]),
         "ssla_selftest_reciprocal": (i, [i, C.POINTER(C.c_ulonglong), C.POINTER(C.c_uint)]),
+        "ssla_selftest_sigmoid_pair": (i, [i, C.POINTER(C.c_ulonglong), C.POINTER(C.c_uint)]),
         "ssla_expf_host": (f, [f]),
         "ssla_sigmoidf_host": (f, [f]),
         "ssla_last_error": (C.c_char_p, []),
@@ -423,6 +424,15 @@ def selftest_reciprocal(device: int = 0) -> Tuple[int, int]:
     n = C.c_ulonglong()
     first = C.c_uint()
     _check(load_library().ssla_selftest_reciprocal(device, C.byref(n), C.byref(first)))
+    return n.value, first.value
+
+
+def selftest_sigmoid_pair(device: int = 0) -> Tuple[int, int]:
+    """(mismatches, first mismatching bit pattern) of the packed device
+    sigmoid against two scalar device sigmoids over every float."""
+    n = C.c_ulonglong()
+    first = C.c_uint()
+    _check(load_library().ssla_selftest_sigmoid_pair(device, C.byref(n), C.byref(first)))
     return n.value, first.value
 
 
