@@ -1557,7 +1557,7 @@ struct LnShape {
 };
 
 template <int A, int OUT>
-__global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 128)) k_ln(LnArgs a) {
+__global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 80)) k_ln(LnArgs a) {
     pdl_enter();
     using Sh = LnShape<OUT>;
     constexpr int EV = Sh::EV, NT = Sh::NT, PPT = Sh::PPT;
@@ -1637,9 +1637,11 @@ __global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 
         if (tid < EV && ev_ok[tid]) {
             const float* y = ybuf + tid * ST;
             double sum = 0.0;
+#pragma unroll 4
             for (int o = 0; o < OUT; ++o) sum += static_cast<double>(y[o]);
             const double mean = sum / static_cast<double>(OUT);
             double var = 0.0;
+#pragma unroll 4
             for (int o = 0; o < OUT; ++o) {
                 const double dd = static_cast<double>(y[o]) - mean;
                 var += dd * dd;
