@@ -1704,15 +1704,59 @@ __global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 
 // the cls (ncls), reg (4) and obj (1) predictions, then the box decode.
 // 32 events per batch; X holds the features in E_4 row order.
 // ---------------------------------------------------------------------------
+// Dynamic shared memory of k_head for `cols` = 5 + ncls outputs: the two 1x1
+// convolutions' weights [96][96] each, the prediction weights [96][cols]
+// (reg 0..3, obj 4, cls 5..), the batch's features [96][kMB], activations
+// [192][kMB] and results [kMB][cols].
+size_t head_smem_bytes(int cols) {
+    return sizeof(float) * (2 * 96 * 96 + static_cast<size_t>(96) * cols + 96 * kMB + 192 * kMB +
+                            static_cast<size_t>(kMB) * cols);
+}
+
+// The weights are constant: staged in shared memory before the wait for the
+// previous kernel, so every fmaf chain reads them at shared-memory latency.
 __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
-    pdl_enter();
-    __shared__ __align__(16) float x_s[96 * kMB];
-    __shared__ __align__(16) float act_s[192 * kMB];
-    __shared__ float res_s[kMB][24];
+    extern __shared__ __align__(16) float hsm[];
+    const int ncls = a.g.ncls, cols = 5 + ncls;
+    float* const w_cls = hsm;                    // [96][96] cls_convT
+    float* const w_reg = w_cls + 96 * 96;        // [96][96] reg_convT
+    float* const x_s = w_reg + 96 * 96;          // [96][kMB]
+    float* const act_s = x_s + 96 * kMB;         // [192][kMB]
+    float* const w_pred = act_s + 192 * kMB;     // [96][cols]
+    float* const res_s = w_pred + 96 * cols;     // [kMB][cols]
     __shared__ int valid_s[kMB], cx_s[kMB], cy_s[kMB];
     const int tid = threadIdx.x;
+    {
+        const float* const src[2] = {a.head.cls_convT, a.head.reg_convT};
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            float* const dst = hsm + m * 96 * 96;
+            if ((reinterpret_cast<uintptr_t>(src[m]) & 15u) == 0) {
+                constexpr int N4 = 96 * 96 / 4, PT = (N4 + kNT - 1) / kNT;
+                float4 v[PT];
+#pragma unroll
+                for (int q = 0; q < PT; ++q) {
+                    const int t = tid + q * kNT;
+                    if (t < N4) v[q] = __ldg(reinterpret_cast<const float4*>(src[m]) + t);
+                }
+#pragma unroll
+                for (int q = 0; q < PT; ++q) {
+                    const int t = tid + q * kNT;
+                    if (t < N4) reinterpret_cast<float4*>(dst)[t] = v[q];
+                }
+            } else {
+                for (int t = tid; t < 96 * 96; t += kNT) dst[t] = __ldg(src[m] + t);
+            }
+        }
+        for (int t = tid; t < 96 * cols; t += kNT) {
+            const int i = t / cols, r = t % cols;
+            w_pred[t] = (r < 4) ? __ldg(a.head.reg_predT + i * 4 + r)
+                      : (r == 4) ? __ldg(a.head.obj_predT + i)
+                                 : __ldg(a.head.cls_predT + i * ncls + (r - 5));
+        }
+    }
+    pdl_wait();
     const int n = min(a.count[4], a.g.cap[4]);
-    const int ncls = a.g.ncls, cols = 5 + ncls;
     for (int batch = blockIdx.x; batch * kMB < n; batch += gridDim.x) {
         __syncthreads();
         if (tid < kMB) {
@@ -1731,14 +1775,14 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
         for (int item = tid; item < 192 * kGroups; item += kNT) {
             const int j = item % 192, g = item / 192;
             const int jo = j % 96;
-            const float* Wt = (j < 96) ? a.head.cls_convT : a.head.reg_convT;
+            const float* Wt = (j < 96) ? w_cls : w_reg;
             const float bias = __ldg(((j < 96) ? a.head.cls_conv_b : a.head.reg_conv_b) + jo);
             float acc[kEPT];
 #pragma unroll
             for (int b = 0; b < kEPT; ++b) acc[b] = bias;
 #pragma unroll 4
             for (int i = 0; i < 96; ++i) {
-                const float wv = __ldg(Wt + i * 96 + jo);
+                const float wv = Wt[i * 96 + jo];
                 const float4 x0 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT);
                 const float4 x1 = *reinterpret_cast<const float4*>(x_s + i * kMB + g * kEPT + 4);
                 acc[0] = fmaf(wv, x0.x, acc[0]); acc[1] = fmaf(wv, x0.y, acc[1]);
@@ -1754,29 +1798,21 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
         for (int item = tid; item < kMB * cols; item += kNT) {
             const int b = item % kMB, r = item / kMB;
             if (!valid_s[b]) continue;
-            float acc;
-            if (r < 4) {
-                acc = __ldg(a.head.reg_pred_b + r);
-                for (int i = 0; i < 96; ++i)
-                    acc = fmaf(__ldg(a.head.reg_predT + i * 4 + r), act_s[(96 + i) * kMB + b], acc);
-            } else if (r == 4) {
-                acc = __ldg(a.head.obj_pred_b);
-                for (int i = 0; i < 96; ++i)
-                    acc = fmaf(__ldg(a.head.obj_predT + i), act_s[(96 + i) * kMB + b], acc);
-            } else {
-                const int c = r - 5;
-                acc = __ldg(a.head.cls_pred_b + c);
-                for (int i = 0; i < 96; ++i)
-                    acc = fmaf(__ldg(a.head.cls_predT + i * ncls + c), act_s[i * kMB + b], acc);
-            }
-            res_s[b][r] = acc;
+            // reg (0..3) and obj (4) read the reg branch, cls (5..) the cls branch
+            const float* act = act_s + (r < 5 ? 96 * kMB : 0) + b;
+            float acc = (r < 4) ? __ldg(a.head.reg_pred_b + r)
+                      : (r == 4) ? __ldg(a.head.obj_pred_b)
+                                 : __ldg(a.head.cls_pred_b + (r - 5));
+#pragma unroll 8
+            for (int i = 0; i < 96; ++i) acc = fmaf(w_pred[i * cols + r], act[i * kMB], acc);
+            res_s[b * cols + r] = acc;
         }
         __syncthreads();
         for (int item = tid; item < kMB * cols; item += kNT) {
             const int b = item % kMB, r = item / kMB;
             if (!valid_s[b]) continue;
             const int row = batch * kMB + b;
-            const float v = res_s[b][r];
+            const float v = res_s[b * cols + r];
             float d;
             if (r == 0) d = (v + static_cast<float>(cx_s[b])) * static_cast<float>(a.g.stride_w);
             else if (r == 1) d = (v + static_cast<float>(cy_s[b])) * static_cast<float>(a.g.stride_h);
@@ -2231,8 +2267,8 @@ int scan_fused_grid(K kern, Sh) {
 int scan_fused_resident_warps(int layer) {
     switch (layer) {
         case 1: return scan_fused_grid(k_scan_group<12, 12, 8, 2, 2>, ScanGroupShape<12, 12, 8, 2, 2>{}) * 8;
-        case 2: return scan_fused_grid(k_scan_group<12, 24, 16, 2, 2>, ScanGroupShape<12, 24, 16, 2, 2>{}) * 16;
-        default: return scan_fused_grid(k_scan_group<24, 24, 16, 2, 2>, ScanGroupShape<24, 24, 16, 2, 2>{}) * 16;
+        case 2: return scan_fused_grid(k_scan_group<12, 24, 20, 2, 2>, ScanGroupShape<12, 24, 20, 2, 2>{}) * 20;
+        default: return scan_fused_grid(k_scan_group<24, 24, 20, 2, 2>, ScanGroupShape<24, 24, 20, 2, 2>{}) * 20;
     }
 }
 
@@ -2246,9 +2282,9 @@ int scan_fused_groups_per_tile(int layer, long long tile_count) {
     }
     // layers 2-3: 2x1 groups where 2x2 groups would leave between one and
     // two items per resident warp (a second item for few warps: the tail)
-    const long long g22 = tile_count * ScanGroupShape<12, 24, 16, 2, 2>::GPT;
-    if (g22 >= warps && g22 < 2 * warps) return ScanGroupShape<12, 24, 16, 2, 1>::GPT;
-    return ScanGroupShape<12, 24, 16, 2, 2>::GPT;
+    const long long g22 = tile_count * ScanGroupShape<12, 24, 20, 2, 2>::GPT;
+    if (g22 >= warps && g22 < 2 * warps) return ScanGroupShape<12, 24, 20, 2, 1>::GPT;
+    return ScanGroupShape<12, 24, 20, 2, 2>::GPT;
 }
 
 void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
@@ -2266,12 +2302,12 @@ void launch_scan_fused(cudaStream_t st, int layer, const ScanFusedArgs& a) {
             else go(k_scan_group<12, 12, 8, 2, 2>, ScanGroupShape<12, 12, 8, 2, 2>{});
             break;
         case 2:
-            if (a.gpt == ScanGroupShape<12, 24, 16, 2, 1>::GPT) go(k_scan_group<12, 24, 16, 2, 1>, ScanGroupShape<12, 24, 16, 2, 1>{});
-            else go(k_scan_group<12, 24, 16, 2, 2>, ScanGroupShape<12, 24, 16, 2, 2>{});
+            if (a.gpt == ScanGroupShape<12, 24, 20, 2, 1>::GPT) go(k_scan_group<12, 24, 20, 2, 1>, ScanGroupShape<12, 24, 20, 2, 1>{});
+            else go(k_scan_group<12, 24, 20, 2, 2>, ScanGroupShape<12, 24, 20, 2, 2>{});
             break;
         default:
-            if (a.gpt == ScanGroupShape<24, 24, 16, 2, 1>::GPT) go(k_scan_group<24, 24, 16, 2, 1>, ScanGroupShape<24, 24, 16, 2, 1>{});
-            else go(k_scan_group<24, 24, 16, 2, 2>, ScanGroupShape<24, 24, 16, 2, 2>{});
+            if (a.gpt == ScanGroupShape<24, 24, 20, 2, 1>::GPT) go(k_scan_group<24, 24, 20, 2, 1>, ScanGroupShape<24, 24, 20, 2, 1>{});
+            else go(k_scan_group<24, 24, 20, 2, 2>, ScanGroupShape<24, 24, 20, 2, 2>{});
             break;
     }
 }
@@ -2303,7 +2339,9 @@ void launch_ln(cudaStream_t st, int layer, const LnArgs& a, long long max_rows) 
 
 void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows) {
     const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + kMB - 1) / kMB, 148LL * 8)));
-    pdl_launch(k_head, grid, kNT, 0, st, a);
+    const size_t smem = head_smem_bytes(5 + a.g.ncls);
+    cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    pdl_launch(k_head, grid, kNT, smem, st, a);
 }
 
 int gemm_cols(int layer, int colmode) {
