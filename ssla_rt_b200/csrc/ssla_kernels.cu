@@ -1715,7 +1715,10 @@ size_t head_smem_bytes(int cols) {
 
 // The weights are constant: staged in shared memory before the wait for the
 // previous kernel, so every fmaf chain reads them at shared-memory latency.
-__global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
+// kHeadNT threads: one per (convolution output, group of kEPT events) of a
+// batch, so each thread runs one 96-step chain group per batch.
+constexpr int kHeadNT = 192 * kGroups;
+__global__ void __launch_bounds__(kHeadNT) k_head(HeadArgs a) {
     extern __shared__ __align__(16) float hsm[];
     const int ncls = a.g.ncls, cols = 5 + ncls;
     float* const w_cls = hsm;                    // [96][96] cls_convT
@@ -1732,23 +1735,23 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
         for (int m = 0; m < 2; ++m) {
             float* const dst = hsm + m * 96 * 96;
             if ((reinterpret_cast<uintptr_t>(src[m]) & 15u) == 0) {
-                constexpr int N4 = 96 * 96 / 4, PT = (N4 + kNT - 1) / kNT;
+                constexpr int N4 = 96 * 96 / 4, PT = (N4 + kHeadNT - 1) / kHeadNT;
                 float4 v[PT];
 #pragma unroll
                 for (int q = 0; q < PT; ++q) {
-                    const int t = tid + q * kNT;
+                    const int t = tid + q * kHeadNT;
                     if (t < N4) v[q] = __ldg(reinterpret_cast<const float4*>(src[m]) + t);
                 }
 #pragma unroll
                 for (int q = 0; q < PT; ++q) {
-                    const int t = tid + q * kNT;
+                    const int t = tid + q * kHeadNT;
                     if (t < N4) reinterpret_cast<float4*>(dst)[t] = v[q];
                 }
             } else {
-                for (int t = tid; t < 96 * 96; t += kNT) dst[t] = __ldg(src[m] + t);
+                for (int t = tid; t < 96 * 96; t += kHeadNT) dst[t] = __ldg(src[m] + t);
             }
         }
-        for (int t = tid; t < 96 * cols; t += kNT) {
+        for (int t = tid; t < 96 * cols; t += kHeadNT) {
             const int i = t / cols, r = t % cols;
             w_pred[t] = (r < 4) ? __ldg(a.head.reg_predT + i * 4 + r)
                       : (r == 4) ? __ldg(a.head.obj_predT + i)
@@ -1766,13 +1769,13 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
             cx_s[tid] = static_cast<int>(xy0 & 0xFFFFu) >> 3;
             cy_s[tid] = static_cast<int>(xy0 >> 16) >> 3;
         }
-        for (int t = tid; t < 96 * kMB; t += kNT) {
+        for (int t = tid; t < 96 * kMB; t += kHeadNT) {
             const int i = t % 96, b = t / 96;
             const int r = batch * kMB + b;
             x_s[i * kMB + b] = (r < n) ? a.X[static_cast<size_t>(r) * 96 + i] : 0.0f;
         }
         __syncthreads();
-        for (int item = tid; item < 192 * kGroups; item += kNT) {
+        for (int item = tid; item < 192 * kGroups; item += kHeadNT) {
             const int j = item % 192, g = item / 192;
             const int jo = j % 96;
             const float* Wt = (j < 96) ? w_cls : w_reg;
@@ -1795,7 +1798,7 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
                 act_s[j * kMB + g * kEPT + b] = acc[b] * ssla_sigmoidf(acc[b]);
         }
         __syncthreads();
-        for (int item = tid; item < kMB * cols; item += kNT) {
+        for (int item = tid; item < kMB * cols; item += kHeadNT) {
             const int b = item % kMB, r = item / kMB;
             if (!valid_s[b]) continue;
             // reg (0..3) and obj (4) read the reg branch, cls (5..) the cls branch
@@ -1808,7 +1811,7 @@ __global__ void __launch_bounds__(kNT) k_head(HeadArgs a) {
             res_s[b * cols + r] = acc;
         }
         __syncthreads();
-        for (int item = tid; item < kMB * cols; item += kNT) {
+        for (int item = tid; item < kMB * cols; item += kHeadNT) {
             const int b = item % kMB, r = item / kMB;
             if (!valid_s[b]) continue;
             const int row = batch * kMB + b;
@@ -2341,7 +2344,7 @@ void launch_head(cudaStream_t st, const HeadArgs& a, long long max_rows) {
     const int grid = static_cast<int>(std::max(1LL, std::min((max_rows + kMB - 1) / kMB, 148LL * 8)));
     const size_t smem = head_smem_bytes(5 + a.g.ncls);
     cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    pdl_launch(k_head, grid, kNT, smem, st, a);
+    pdl_launch(k_head, grid, kHeadNT, smem, st, a);
 }
 
 int gemm_cols(int layer, int colmode) {
