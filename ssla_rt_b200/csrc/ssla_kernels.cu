@@ -294,13 +294,14 @@ constexpr int kGateBuf = 256;
 constexpr int kGateNT = 128;
 
 __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
-    pdl_enter();
     const int p = blockIdx.x, blk = blockIdx.y;
     const int W3 = a.g.W[3];
     const int bx = blk % W3, by = blk / W3;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const PartState ps = a.parts[p];
     const bool hyb = a.g.layout == LAYOUT_HYBRID;
+    // 16-byte stores of the layer-0 rows when both output arrays allow them
+    const bool v16 = ((reinterpret_cast<uintptr_t>(a.X1) | reinterpret_cast<uintptr_t>(a.Rcopy)) & 15u) == 0;
     __shared__ double lt[64];
     __shared__ int c0[16], c1[4], c2[4], c3[1];
     __shared__ unsigned char passtab[256];
@@ -316,26 +317,57 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
     __shared__ unsigned char pl[kGateBuf];
     __shared__ int b_n, b_done;
     const int W0 = a.g.W[0], W1 = a.g.W[1], W2 = a.g.W[2];
-    for (int i = tid; i < 72; i += kGateNT) w0[i] = a.L0.qvgT[i];
-    for (int i = tid; i < 24; i += kGateNT) w0[72 + i] = a.L0.ipT[i];
-    for (int i = tid; i < 144; i += kGateNT) w0[96 + i] = a.L0.goWT[i];
-    if (tid < 12) { w0[240 + tid] = a.L0.gamma[tid]; w0[252 + tid] = a.L0.beta[tid]; }
+    // The layer-0 weights are constant: loaded before the wait for the
+    // previous kernel.  Every load of the set-up is issued before any store,
+    // so the set-up costs one round trip, not one per array.
+    {
+        constexpr int NW = (264 + kGateNT - 1) / kGateNT;
+        float wv[NW];
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+            const int t = tid + q * kGateNT;
+            wv[q] = (t < 72) ? a.L0.qvgT[t] : (t < 96) ? a.L0.ipT[t - 72] : (t < 240) ? a.L0.goWT[t - 96]
+                  : (t < 252) ? a.L0.gamma[t - 240] : (t < 264) ? a.L0.beta[t - 252] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+            const int t = tid + q * kGateNT;
+            if (t < 264) w0[t] = wv[q];
+        }
+    }
     for (int i = tid; i < 256; i += kGateNT) passtab[i] = gate_pass(i, a.g.window) ? 1 : 0;
-    for (int i = tid; i < 64 * 12; i += kGateNT) {
-        const int px = i / 12, c = i % 12;
-        h0[i] = ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c];
-    }
-    for (int i = tid; i < 64; i += kGateNT) {
-        lt[i] = ps.last_t[(by * 8 + i / 8) * W0 + bx * 8 + (i % 8)];
-        pc[i] = 0;
-    }
-    if (tid < 16) c0[tid] = ps.cnt[0][(by * 4 + tid / 4) * W1 + bx * 4 + (tid % 4)];
-    if (tid < 4) c1[tid] = ps.cnt[1][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
-    if (hyb) {
-        if (tid < 4) c2[tid] = ps.cnt[2][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
-        if (tid == 0) c3[0] = ps.cnt[3][by * W3 + bx];
-    } else if (tid == 0) {
-        c2[0] = ps.cnt[2][by * W3 + bx];
+    pdl_enter();
+    {
+        constexpr int NH = 64 * 12 / kGateNT;
+        static_assert(64 * 12 % kGateNT == 0 && kGateNT >= 64, "gate set-up shape");
+        float hv[NH];
+#pragma unroll
+        for (int q = 0; q < NH; ++q) {
+            const int i = tid + q * kGateNT, px = i / 12, c = i % 12;
+            hv[q] = ps.hidden[0][(static_cast<size_t>(by * 8 + px / 8) * W0 + bx * 8 + (px % 8)) * 12 + c];
+        }
+        double ltv = 0.0;
+        if (tid < 64) ltv = ps.last_t[(by * 8 + tid / 8) * W0 + bx * 8 + (tid % 8)];
+        int cv0 = 0, cv1 = 0, cv2 = 0, cv3 = 0;
+        if (tid < 16) cv0 = ps.cnt[0][(by * 4 + tid / 4) * W1 + bx * 4 + (tid % 4)];
+        if (tid < 4) cv1 = ps.cnt[1][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
+        if (hyb) {
+            if (tid < 4) cv2 = ps.cnt[2][(by * 2 + tid / 2) * W2 + bx * 2 + (tid % 2)];
+            if (tid == 0) cv3 = ps.cnt[3][by * W3 + bx];
+        } else if (tid == 0) {
+            cv2 = ps.cnt[2][by * W3 + bx];
+        }
+#pragma unroll
+        for (int q = 0; q < NH; ++q) h0[tid + q * kGateNT] = hv[q];
+        if (tid < 64) { lt[tid] = ltv; pc[tid] = 0; }
+        if (tid < 16) c0[tid] = cv0;
+        if (tid < 4) c1[tid] = cv1;
+        if (hyb) {
+            if (tid < 4) c2[tid] = cv2;
+            if (tid == 0) c3[0] = cv3;
+        } else if (tid == 0) {
+            c2[0] = cv2;
+        }
     }
     __syncthreads();
 
@@ -625,13 +657,28 @@ __global__ void __launch_bounds__(kGateNT, 5) k_gates(GateArgs a) {
             const int k = b_k[i];
             float* xo = a.X1 + static_cast<size_t>(k) * 12;
             float* rc = (b_pass0[i] && a.Rcopy) ? a.Rcopy + static_cast<size_t>(k) * 12 : nullptr;
+            float xv[12];
 #pragma unroll
             for (int o = 0; o < 12; ++o) {
                 const double t = (static_cast<double>(y[o]) - mean) * inv;
-                const float xv = static_cast<float>(t * static_cast<double>(w0[240 + o]) +
-                                                    static_cast<double>(w0[252 + o]));
-                xo[o] = xv;
-                if (rc) rc[o] = xv;
+                xv[o] = static_cast<float>(t * static_cast<double>(w0[240 + o]) +
+                                           static_cast<double>(w0[252 + o]));
+            }
+            // one event's row per thread: three 16-byte stores instead of
+            // twelve scalar ones (each warp store touches 32 rows)
+            if (v16) {
+#pragma unroll
+                for (int o = 0; o < 12; o += 4) {
+                    const float4 v = make_float4(xv[o], xv[o + 1], xv[o + 2], xv[o + 3]);
+                    *reinterpret_cast<float4*>(xo + o) = v;
+                    if (rc) *reinterpret_cast<float4*>(rc + o) = v;
+                }
+            } else {
+#pragma unroll
+                for (int o = 0; o < 12; ++o) {
+                    xo[o] = xv[o];
+                    if (rc) rc[o] = xv[o];
+                }
             }
         }
         __syncthreads();
