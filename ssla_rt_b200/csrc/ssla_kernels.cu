@@ -1120,10 +1120,24 @@ __global__ void __launch_bounds__(32 * WPC, WPC == 8 ? 3 : 1) k_scan_group(ScanF
     unsigned char* qm = reinterpret_cast<unsigned char*>(qk + QCAP);    // [QCAP] delta | cell<<4 | out<<7
     unsigned char* perm = qm + QCAP;                                    // [32] batch lane -> slot
     int2* rbuf = reinterpret_cast<int2*>(perm + 32);                    // [64] relevant list entries
-    // the weights are constant: staged before the wait
-    for (int t = threadIdx.x; t < 9 * IN * J2 / 4; t += blockDim.x) {
-        const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
-        *reinterpret_cast<float4*>(Ws + d * DS + 4 * r) = __ldg(reinterpret_cast<const float4*>(a.W) + t);
+    // the weights are constant: staged before the wait, every load issued
+    // before the stores (one round trip)
+    {
+        constexpr int N4 = 9 * IN * J2 / 4, PT = (N4 + Sh::NT - 1) / Sh::NT;
+        float4 v[PT];
+#pragma unroll
+        for (int q = 0; q < PT; ++q) {
+            const int t = threadIdx.x + q * Sh::NT;
+            if (t < N4) v[q] = __ldg(reinterpret_cast<const float4*>(a.W) + t);
+        }
+#pragma unroll
+        for (int q = 0; q < PT; ++q) {
+            const int t = threadIdx.x + q * Sh::NT;
+            if (t < N4) {
+                const int d = t / (IN * J2 / 4), r = t % (IN * J2 / 4);
+                *reinterpret_cast<float4*>(Ws + d * DS + 4 * r) = v[q];
+            }
+        }
     }
     pdl_wait();
     __syncthreads();
@@ -1605,23 +1619,41 @@ struct LnShape {
 
 template <int A, int OUT>
 __global__ void __launch_bounds__(LnShape<OUT>::NT, 65536 / (LnShape<OUT>::NT * 80)) k_ln(LnArgs a) {
-    pdl_enter();
     using Sh = LnShape<OUT>;
     constexpr int EV = Sh::EV, NT = Sh::NT, PPT = Sh::PPT;
     constexpr int ST = OUT + 1;                  // conflict-free lane-per-event rows
     constexpr int IPN = (A == 9 && OUT <= 48) ? OUT * 2 * OUT : 1;
     __shared__ float ybuf[EV * ST];
-    __shared__ float ipw[IPN];
+    __shared__ __align__(16) float ipw[IPN];
     __shared__ double mean_s[EV], inv_s[EV];
     __shared__ int ev_r[EV], ev_sr[EV], ev_e[EV], ev_cx[EV], ev_cy[EV];
     __shared__ unsigned char ev_ok[EV], ev_cp[EV];
     const int tid = threadIdx.x;
+    // the next stage's input_proj weights are constant: staged before the
+    // wait for the previous kernel, every load issued before the stores
+    const bool ipn = (IPN > 1) && a.ipT_next != nullptr;
+    if (ipn) {
+        if ((reinterpret_cast<uintptr_t>(a.ipT_next) & 15u) == 0) {
+            constexpr int N4 = IPN / 4, PT = N4 > 0 ? (N4 + NT - 1) / NT : 1;
+            float4 v[PT];
+#pragma unroll
+            for (int q = 0; q < PT; ++q) {
+                const int t = tid + q * NT;
+                if (t < N4) v[q] = __ldg(reinterpret_cast<const float4*>(a.ipT_next) + t);
+            }
+#pragma unroll
+            for (int q = 0; q < PT; ++q) {
+                const int t = tid + q * NT;
+                if (t < N4) reinterpret_cast<float4*>(ipw)[t] = v[q];
+            }
+        } else {
+            for (int t = tid; t < IPN; t += NT) ipw[t] = __ldg(a.ipT_next + t);
+        }
+    }
+    pdl_wait();
     const int s = a.stage;
     const int n_list = (a.list == 0) ? a.n_static : min(a.count[a.list], a.g.cap[a.list]);
     const int Wl = a.g.W[s], Hl = a.g.H[s];
-    const bool ipn = (IPN > 1) && a.ipT_next != nullptr;
-    if (ipn)
-        for (int t = tid; t < IPN; t += NT) ipw[t] = __ldg(a.ipT_next + t);
     for (int r0 = blockIdx.x * EV; r0 < n_list; r0 += gridDim.x * EV) {
         __syncthreads();
         if (tid < EV) {
