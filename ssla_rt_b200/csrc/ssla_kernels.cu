@@ -1459,7 +1459,11 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
         const int d = (A - 1) - unit % A, tile = unit / A;
         const int dy = 1 - d / 3, dx = 1 - d % 3;
         __syncthreads();
-        for (int t = tid; t < BM; t += kNT) {
+        // unrolled over a thread's rows so their list and flag loads overlap
+#pragma unroll
+        for (int q = 0; q < (BM + kNT - 1) / kNT; ++q) {
+            const int t = tid + q * kNT;
+            if (t >= BM) break;
             const int r = tile * BM + t;
             int srow = -1;
             if (r < n_list) {
@@ -1515,19 +1519,41 @@ __global__ void __launch_bounds__(kNT) k_contrib(ContribArgs a) {
             }
         }
         if constexpr (QIN > 0) {
-            for (int t = tid; t < QIN * OUT; t += kNT) {
-                const int i = t / OUT, c = t % OUT;
-                Wqs[t] = __ldg(a.Wq + (static_cast<size_t>(d) * QIN + i) * (3 * OUT) + c);
+            // q weights of delta and the tile's input rows: all of a
+            // thread's loads issued before its stores (one round trip)
+            constexpr int NWQ = (QIN * OUT + kNT - 1) / kNT;
+            constexpr int NXQ = (BM * (QIN / 4) + kNT - 1) / kNT;
+            float wq[NWQ];
+            float4 xq[NXQ];
+#pragma unroll
+            for (int q = 0; q < NWQ; ++q) {
+                const int t = tid + q * kNT;
+                if (t < QIN * OUT)
+                    wq[q] = __ldg(a.Wq + (static_cast<size_t>(d) * QIN + t / OUT) * (3 * OUT) + t % OUT);
             }
-            for (int t = tid; t < BM * (QIN / 4); t += kNT) {
+#pragma unroll
+            for (int q = 0; q < NXQ; ++q) {
+                const int t = tid + q * kNT;
                 const int r = t % BM, k4 = t / BM;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (srow_s[r] >= 0)
-                    v = __ldg(reinterpret_cast<const float4*>(a.Xq + static_cast<size_t>(srow_s[r]) * QIN) + k4);
-                Xs[(4 * k4 + 0) * BMP + r] = v.x;
-                Xs[(4 * k4 + 1) * BMP + r] = v.y;
-                Xs[(4 * k4 + 2) * BMP + r] = v.z;
-                Xs[(4 * k4 + 3) * BMP + r] = v.w;
+                xq[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t < BM * (QIN / 4) && srow_s[r] >= 0)
+                    xq[q] = __ldg(reinterpret_cast<const float4*>(a.Xq + static_cast<size_t>(srow_s[r]) * QIN) + k4);
+            }
+#pragma unroll
+            for (int q = 0; q < NWQ; ++q) {
+                const int t = tid + q * kNT;
+                if (t < QIN * OUT) Wqs[t] = wq[q];
+            }
+#pragma unroll
+            for (int q = 0; q < NXQ; ++q) {
+                const int t = tid + q * kNT;
+                if (t < BM * (QIN / 4)) {
+                    const int r = t % BM, k4 = t / BM;
+                    Xs[(4 * k4 + 0) * BMP + r] = xq[q].x;
+                    Xs[(4 * k4 + 1) * BMP + r] = xq[q].y;
+                    Xs[(4 * k4 + 2) * BMP + r] = xq[q].z;
+                    Xs[(4 * k4 + 3) * BMP + r] = xq[q].w;
+                }
             }
             __syncthreads();
             float qa[8][3];
